@@ -1,0 +1,403 @@
+"""Benchmark of the ternary GEMV hot path (one JSON line on rank 0).
+
+Workload (per-layer shape set at batch 1): a step is
+one pass over a 64-layer model's ternary matmuls at batch 1. Every layer holds
+its own resident weights of the seven config-1 shapes (q 5120->6144, k/v
+5120->1024, o 6144->5120, gate/up 5120->17408, down 17408->5120; 5.8 GB in
+all, 46x the 126 MB L2, so every step streams its weights from HBM and no L2
+flush is needed) and runs the reference decoder's matmul call sequence
+(src/cuda/gpu_decoder.cu:411-416, :437-450): quantise -> gemv[q,k,v] ->
+quantise -> gemv+add[o] -> quantise -> gemv swiglu[gate,up] -> quantise ->
+gemv+add[down]. Weights, scales and activations are seeded synthetic data with
+the configuration's distributions (no checkpoint exists here).
+
+value  = algorithmic HBM bytes of all launches / device time (GB/s), inputs resident.
+e2e    = same metric through the same C-ABI calls with the step's activation
+         inputs copied from pinned host memory and its outputs copied back,
+         inside the timed region.
+With --gpus N > 1 (torchrun), every matrix is N-sharded by rows across the
+ranks (whole 16-row groups) and each GEMV's output is all-gathered over NCCL;
+the total work is fixed, so scaling is "strong".
+
+--impl reference times the reference's own CPU GEMV (oracle/_ref, built from
+the reference sources; its emulator loop on all host threads) on a bounded
+sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "bonsai-ternary-fast_b200")
+sys.path.insert(0, PKG)
+
+import synth  # noqa: E402
+
+N_LAYERS = 64
+METRIC = "ternary GEMV HBM GB/s, batch 1 (config-1 layer shape set, 64-layer step)"
+UNIT = "GB/s"
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Polls NVML for SM clock and throttle reasons while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - clocks are reported, not required
+            self.nv, self.err = None, str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.001)
+
+    def start(self):
+        if self.nv:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._thr:
+            self._thr.join()
+
+    def report(self):
+        if not self.nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "")}
+        busy = [s for s in self.samples]
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(busy)}
+
+
+# ------------------------------------------------------------------ CPU reference arm
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_reference(threads: int, reps: int = 3):
+    """Times the reference's CPU GEMV (emulator loop, src/emu_decoder.cpp:143-165, compiled
+    from the reference sources into oracle/_ref) on ONE layer of the workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    kind = "reference" if oracle.Reference.available() else "port"
+    R = oracle.Reference() if kind == "reference" else None
+    O = oracle.Oracle()
+    mats = {}
+    for name, K, N in synth.LAYER_SHAPES:
+        src = synth.ternary_ptq(N, K, seed=0)
+        mats[name] = (R.repack_rows(src, N, K) if R else O.repack_t2(src, N, K)) + (K, N)
+    acts = {K: (R or O).q8_rows(synth.activations(1, K, seed=2)) for K in (5120, 6144, 17408)}
+
+    def one_layer():
+        for name, (codes, scales, K, N) in mats.items():
+            q, d, s = acts[K]
+            if R:
+                R.gemv(codes, scales, K, q, d, s, threads=threads)
+            else:
+                O.gemv(codes, scales, K, q, d, s, threads=threads)
+
+    one_layer()  # warm caches / thread pool
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one_layer()
+    dt = (time.perf_counter() - t0) / reps
+    layer_bytes = sum(synth.gemv_bytes(N, K) for _, K, N in synth.LAYER_SHAPES)
+    return {"value": layer_bytes / dt / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"one of {N_LAYERS} layers (7 config-1 GEMVs, M=1), {reps} timed passes, "
+                      f"{dt * 1e3:.1f} ms per layer"}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = host_threads()
+    cb = cpu_reference(threads, reps=max(1, min(args.steps, 5)))
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int8 x ternary",
+            "data": "synthetic", "config": {"workload": "config1 layer set, batch 1, CPU emulator GEMV"},
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}, "vs_baseline": None}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+class Model:
+    """64 layers of resident panel weights (this rank's row shard of each matrix)."""
+
+    def __init__(self, btf, torch, dev, rank, world):
+        self.shapes = {name: (K, N) for name, K, N in synth.LAYER_SHAPES}
+        self.rows = {}
+        for name, (K, N) in self.shapes.items():
+            per = N // world
+            assert per % 16 == 0, (name, N, world)
+            self.rows[name] = (rank * per, per)
+        self.layers = []
+        src = {}
+        for name, (K, N) in self.shapes.items():
+            r0, n = self.rows[name]
+            full = synth.ternary_ptq(N, K, seed=0)
+            src[name] = torch.from_numpy(np.ascontiguousarray(full[r0:r0 + n])).to(dev)
+        for _ in range(N_LAYERS):
+            layer = {}
+            for name, (K, N) in self.shapes.items():
+                layer[name] = btf.repack_panels(src[name], self.rows[name][1], K)
+            self.layers.append(layer)
+        torch.cuda.synchronize()
+        del src
+
+
+def gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import btf_b200 as btf
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    btf.kernels_init(local)
+    model = Model(btf, torch, dev, rank, world)
+    sh = model.shapes
+
+    # activations and outputs (full width on every rank; each rank writes its row slice)
+    xs = {k: torch.from_numpy(synth.activations(1, k, seed=2 + i)).to(dev)
+          for i, k in enumerate((5120, 6144, 17408))}
+    x_in = {"attn": xs[5120], "o": xs[6144], "ffn": xs[5120].clone(), "down": xs[17408]}
+    acts = {k: btf.Q8Act.empty(1, sh_k, dev) for k, sh_k in (("attn", 5120), ("o", 6144), ("ffn", 5120),
+                                                              ("down", 17408))}
+    full_out = {n: torch.zeros((1, N), device=dev) for n, (K, N) in sh.items() if n != "up"}
+    loc_out = {n: torch.zeros((1, model.rows[n][1]), device=dev) for n in full_out}
+
+    stream = torch.cuda.Stream(device=dev)
+
+    def gather(name):
+        if world > 1:
+            dist.all_gather_into_tensor(full_out[name].view(-1), loc_out[name].view(-1))
+
+    # per-kernel timing events around the launches of the last layer of a step
+    kinds = ("quant", "qkv", "o", "gateup", "down")
+    evs = {k: (torch.cuda.Event(enable_timing=True, external=True),
+               torch.cuda.Event(enable_timing=True, external=True)) for k in kinds}
+
+    def layer(L, timed=False):
+        def t0(k):
+            if timed:
+                evs[k][0].record(stream)
+
+        def t1(k):
+            if timed:
+                evs[k][1].record(stream)
+
+        t0("quant")
+        btf.quant_q8(x_in["attn"], acts["attn"], stream=stream)
+        t1("quant")
+        t0("qkv")
+        btf.launch_gemv([(L["q"], loc_out["q"], loc_out["q"].shape[1]), (L["k"], loc_out["k"], loc_out["k"].shape[1]),
+                         (L["v"], loc_out["v"], loc_out["v"].shape[1])], 5120, 1, acts["attn"], btf.STORE, stream)
+        t1("qkv")
+        for n in ("q", "k", "v"):
+            gather(n)
+        btf.quant_q8(x_in["o"], acts["o"], stream=stream)
+        t0("o")
+        btf.launch_gemv([(L["o"], loc_out["o"], loc_out["o"].shape[1])], 6144, 1, acts["o"], btf.ADD, stream)
+        t1("o")
+        gather("o")
+        btf.quant_q8(x_in["ffn"], acts["ffn"], stream=stream)
+        t0("gateup")
+        btf.launch_gemv([(L["gate"], loc_out["gate"], loc_out["gate"].shape[1]), (L["up"], None, 0)], 5120, 1,
+                        acts["ffn"], btf.SWIGLU, stream)
+        t1("gateup")
+        gather("gate")
+        btf.quant_q8(x_in["down"], acts["down"], stream=stream)
+        t0("down")
+        btf.launch_gemv([(L["down"], loc_out["down"], loc_out["down"].shape[1])], 17408, 1, acts["down"], btf.ADD,
+                        stream)
+        t1("down")
+        gather("down")
+
+    def step():
+        for i, L in enumerate(model.layers):
+            layer(L, timed=(i == len(model.layers) - 1))
+
+    # e2e variant: inputs from pinned host memory in, outputs back, every step
+    h_in = {k: v.cpu().pin_memory() for k, v in x_in.items()}
+    h_out = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in full_out.items()}
+
+    def step_e2e():
+        for k in x_in:
+            x_in[k].copy_(h_in[k], non_blocking=True)
+        step()
+        for k in full_out:
+            h_out[k].copy_(full_out[k] if world > 1 else loc_out[k], non_blocking=True)
+
+    h2d = sum(v.numel() * 4 for v in h_in.values())
+    d2h = sum(v.numel() * 4 for v in h_out.values())
+
+    # capture both variants as CUDA graphs (the reference replays its decode step as one graph)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+            step_e2e()
+    torch.cuda.synchronize()
+    g_dev, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_dev, stream=stream):
+        step()
+    with torch.cuda.graph(g_e2e, stream=stream):
+        step_e2e()
+    torch.cuda.synchronize()
+
+    def timed(graph, K, W):
+        for _ in range(W):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(K):
+                graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        torch.cuda.synchronize()
+        return ms
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v for v in vis.split(",") if v.strip()]
+    nvml_index = int(ids[local]) if local < len(ids) and ids[local].strip().isdigit() else local
+    clocks = ClockSampler(nvml_index)
+    clocks.start()
+    ms_dev = timed(g_dev, args.steps, args.warmup)
+    clocks.stop()
+    kern_ms = {k: evs[k][0].elapsed_time(evs[k][1]) for k in kinds}
+    ms_e2e = timed(g_e2e, args.steps, args.warmup)
+
+    # algorithmic bytes (whole job: every matrix counted once)
+    per_layer = {
+        "qkv": sum(synth.gemv_bytes(sh[n][1], sh[n][0]) for n in ("q", "k", "v")) - 2 * 5120 * 5 // 4,
+        "o": synth.gemv_bytes(sh["o"][1], sh["o"][0], add=True),
+        "gateup": 2 * synth.gemv_bytes(sh["gate"][1], 5120) - 5120 * 5 // 4 - sh["gate"][1] * 4,
+        "down": synth.gemv_bytes(sh["down"][1], sh["down"][0], add=True),
+        "quant": 4 * 5120 + 5120 * 5 // 4,
+    }
+    quant_all = sum(4 * k + k * 5 // 4 for k in (5120, 6144, 5120, 17408))
+    layer_bytes = per_layer["qkv"] + per_layer["o"] + per_layer["gateup"] + per_layer["down"] + quant_all
+    step_bytes = layer_bytes * N_LAYERS
+    value = step_bytes * args.steps / (ms_dev * 1e-3) / 1e9
+    e2e = step_bytes * args.steps / (ms_e2e * 1e-3) / 1e9
+
+    peak, peak_kind = measured_peaks()
+    # dominant kernel: the gate/up swiglu GEMV (52 % of the step's bytes); on this rank's shard
+    dom_bytes = per_layer["gateup"] / world
+    dom_ach = dom_bytes / (kern_ms["gateup"] * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic_gateup_swiglu.txt")
+    if os.path.exists(tpath):
+        for line in open(tpath):
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = int(line.split(":")[1].strip()) // world
+    kernels = {k: {"us": kern_ms[k] * 1e3, "GB/s": (per_layer[k] / world) / (kern_ms[k] * 1e-3) / 1e9}
+               for k in kinds}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_dev / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x ternary (dp4a), fp32 accumulate",
+            "data": "synthetic (seeded ternary weights, fp16 block-128 scales, N(0,1) activations)",
+            "config": {"workload": "config1 per-layer shape set, batch 1, x64 layers per step",
+                       "shapes": [f"{n}:{K}->{N}" for n, K, N in synth.LAYER_SHAPES],
+                       "layers": N_LAYERS, "bytes_per_step": step_bytes,
+                       "l2": "inputs larger than L2: 5.8 GB of distinct resident weights per step",
+                       "parallelism": f"N-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "graph": "one CUDA graph per step"},
+            "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
+                         "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,8,SWIGLU> gate+up",
+                         "peak_source": peak_kind},
+            "kernels": kernels,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * N_LAYERS * 8,
+            "clocks": clocks.report(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference(host_threads())
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del g_dev, g_e2e
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

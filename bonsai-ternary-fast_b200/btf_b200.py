@@ -1,0 +1,242 @@
+"""Python host mirror of the btf_b200 C ABI (include/btf_b200.h).
+
+This module is the Python face of the B200 ternary GEMV/GEMM library. It
+mirrors the reference's launcher interface, ``btf::cuda`` in
+src/cuda/kernels.cuh:17-56 (kernels_init, gemv_max_nb, launch_repack,
+launch_gemv with GemvSeg / Q8Act / GemvMode), with the same argument meaning
+and the same error behaviour: a bad argument or a failed launch raises
+``RuntimeError`` (the reference throws ``std::runtime_error``).
+
+Device memory is held in torch tensors (torch is only the allocator and the
+stream source here); every kernel runs from ``libbtf_b200.so``, built in-tree
+by ``make -C bonsai-ternary-fast_b200``. There is no CPU fallback: if the
+library is missing, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libbtf_b200.so")
+
+STORE, ADD, SWIGLU = 0, 1, 2  # GemvMode values (src/cuda/kernels.cuh:53)
+PANEL_ROWS, PANEL_COLS, PANEL_BYTES = 16, 1024, 4352
+
+# Every symbol include/btf_b200.h declares; tests check the library exports them.
+EXPORTS = (
+    "btf_status_string", "btf_last_error", "btf_version", "btf_init", "btf_gemv_max_nb",
+    "btf_panel_bytes", "btf_t2_codes_bytes", "btf_t2_scales_bytes",
+    "btf_repack_panels", "btf_repack_panels_host", "btf_repack_t2", "btf_t2_to_panels", "btf_panels_to_t2",
+    "btf_quant_q8", "btf_gemv", "btf_gemv_idot",
+)
+
+
+class GemvSeg(ctypes.Structure):
+    """btf_gemv_seg: one matrix of a multi-segment GEMV (GemvSeg, kernels.cuh:46-52)."""
+
+    _fields_ = [("panels", ctypes.c_void_p), ("N", ctypes.c_int), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int)]
+
+
+class Q8ActC(ctypes.Structure):
+    """btf_q8act: Q8_0 activations (Q8Act, kernels.cuh:27-31)."""
+
+    _fields_ = [("q", ctypes.c_void_p), ("d", ctypes.c_void_p), ("s", ctypes.c_void_p)]
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libbtf_b200.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` (no CPU fallback exists)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    sig = {
+        "btf_status_string": (ctypes.c_char_p, [i32]),
+        "btf_last_error": (ctypes.c_char_p, []),
+        "btf_version": (ctypes.c_char_p, []),
+        "btf_init": (i32, [i32]),
+        "btf_gemv_max_nb": (i32, [i32]),
+        "btf_panel_bytes": (i64, [i64, i64]),
+        "btf_t2_codes_bytes": (i64, [i64, i64]),
+        "btf_t2_scales_bytes": (i64, [i64, i64]),
+        "btf_repack_panels": (i32, [vp, i64, i64, vp, vp]),
+        "btf_repack_panels_host": (i32, [vp, i64, i64, vp, i32]),
+        "btf_repack_t2": (i32, [vp, i64, vp, vp, vp]),
+        "btf_t2_to_panels": (i32, [vp, vp, i64, i64, vp, vp]),
+        "btf_panels_to_t2": (i32, [vp, i64, i64, vp, vp, vp]),
+        "btf_quant_q8": (i32, [vp, i32, i32, i32, Q8ActC, vp]),
+        "btf_gemv": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
+        "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(status: int, what: str) -> None:
+    """Raises RuntimeError for a nonzero status, like the reference's check()."""
+    if status != 0:
+        L = lib()
+        raise RuntimeError(f"{what}: {L.btf_status_string(status).decode()}: {L.btf_last_error().decode()}")
+
+
+# ---------------------------------------------------------------- torch glue
+def _torch():
+    import torch  # imported lazily: the CPU-only paths do not need it
+
+    return torch
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        return _torch().cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+_initialised = set()
+
+
+def kernels_init(device: int = 0) -> None:
+    """Per-device set-up (btf_init); kernels_init in src/cuda/kernels.cuh:17."""
+    check(lib().btf_init(device), "btf_init")
+    _initialised.add(device)
+
+
+def ensure_init(device: int) -> None:
+    if device not in _initialised:
+        kernels_init(device)
+
+
+def gemv_max_nb(K: int) -> int:
+    """gemv_max_nb (kernels.cuh:20): activation rows per GEMV pass for width K."""
+    return lib().btf_gemv_max_nb(K)
+
+
+def panel_bytes(N: int, K: int) -> int:
+    return lib().btf_panel_bytes(N, K)
+
+
+def t2_codes_bytes(N: int, K: int) -> int:
+    return lib().btf_t2_codes_bytes(N, K)
+
+
+def t2_scales_bytes(N: int, K: int) -> int:
+    return lib().btf_t2_scales_bytes(N, K)
+
+
+@dataclass
+class Q8Act:
+    """Q8_0 activations on the device: q int8 [M][K], d fp32 [M][K/32], s int32 [M][K/32]."""
+
+    q: object
+    d: object
+    s: object
+
+    def c(self) -> Q8ActC:
+        return Q8ActC(_ptr(self.q), _ptr(self.d), _ptr(self.s))
+
+    @staticmethod
+    def empty(M: int, K: int, device) -> "Q8Act":
+        torch = _torch()
+        return Q8Act(
+            torch.empty((M, K), dtype=torch.int8, device=device),
+            torch.empty((M, K // 32), dtype=torch.float32, device=device),
+            torch.empty((M, K // 32), dtype=torch.int32, device=device),
+        )
+
+
+@dataclass
+class PanelMatrix:
+    """A ternary [N][K] matrix resident on the device in the panel layout."""
+
+    panels: object  # uint8 tensor of panel_bytes(N, K)
+    N: int
+    K: int
+
+
+def repack_panels(ptq_src, N: int, K: int, out=None, stream=None) -> PanelMatrix:
+    """PTQ1_0 blocks (uint8 tensor, device or pinned-mapped) -> panel layout on the device.
+
+    Replaces launch_repack (kernels.cuh:24) for the B200 resident layout."""
+    torch = _torch()
+    dev = ptq_src.device if ptq_src.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    ensure_init(dev.index)
+    if out is None:
+        out = torch.empty(panel_bytes(N, K), dtype=torch.uint8, device=dev)
+    check(lib().btf_repack_panels(_ptr(ptq_src), N, K, _ptr(out), _stream(stream)), "btf_repack_panels")
+    return PanelMatrix(out, N, K)
+
+
+def repack_panels_host(ptq_src_np, N: int, K: int, threads: int = 0):
+    """Host twin of repack_panels (numpy in, numpy out); btf::repack_rows/repack, src/repack.cpp:16-45."""
+    import numpy as np
+
+    src = np.ascontiguousarray(ptq_src_np, dtype=np.uint8)
+    out = np.empty(panel_bytes(N, K), dtype=np.uint8)
+    check(lib().btf_repack_panels_host(src.ctypes.data, N, K, out.ctypes.data, threads), "btf_repack_panels_host")
+    return out
+
+
+def launch_repack(src, nblocks: int, codes, scales, stream=None) -> None:
+    """launch_repack (kernels.cuh:24): PTQ1_0 -> reference T2 codes/scales."""
+    check(lib().btf_repack_t2(_ptr(src), nblocks, _ptr(codes), _ptr(scales), _stream(stream)), "btf_repack_t2")
+
+
+def t2_to_panels(codes, scales, N: int, K: int, out=None, stream=None) -> PanelMatrix:
+    torch = _torch()
+    if out is None:
+        out = torch.empty(panel_bytes(N, K), dtype=torch.uint8, device=codes.device)
+    check(lib().btf_t2_to_panels(_ptr(codes), _ptr(scales), N, K, _ptr(out), _stream(stream)), "btf_t2_to_panels")
+    return PanelMatrix(out, N, K)
+
+
+def panels_to_t2(pm: PanelMatrix, stream=None):
+    torch = _torch()
+    codes = torch.empty(t2_codes_bytes(pm.N, pm.K), dtype=torch.uint8, device=pm.panels.device)
+    scales = torch.empty(t2_scales_bytes(pm.N, pm.K) // 2, dtype=torch.int16, device=pm.panels.device)
+    check(lib().btf_panels_to_t2(_ptr(pm.panels), pm.N, pm.K, _ptr(codes), _ptr(scales), _stream(stream)),
+          "btf_panels_to_t2")
+    return codes, scales
+
+
+def quant_q8(x, act: Optional[Q8Act] = None, stream=None) -> Q8Act:
+    """Q8_0 of fp32 rows x [M][K] (the quantising part of launch_prep, kernels.cuh:42-43)."""
+    M, K = x.shape
+    ensure_init(x.device.index)
+    if act is None:
+        act = Q8Act.empty(M, K, x.device)
+    check(lib().btf_quant_q8(_ptr(x), x.stride(0), M, K, act.c(), _stream(stream)), "btf_quant_q8")
+    return act
+
+
+def launch_gemv(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int = STORE, stream=None) -> None:
+    """launch_gemv (kernels.cuh:56). segs: (PanelMatrix, y tensor or None, ldy) per segment."""
+    arr = (GemvSeg * len(segs))()
+    for i, (pm, y, ldy) in enumerate(segs):
+        arr[i] = GemvSeg(_ptr(pm.panels), pm.N, _ptr(y), ldy)
+    check(lib().btf_gemv(arr, len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemv")
+
+
+def gemv_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):
+    """Exact int32 trit dots idot[M][N][K/32] through the GEMV's decode path."""
+    torch = _torch()
+    out = torch.empty((M, pm.N, pm.K // 32), dtype=torch.int32, device=pm.panels.device)
+    check(lib().btf_gemv_idot(_ptr(pm.panels), pm.N, pm.K, M, act.c(), _ptr(out), _stream(stream)), "btf_gemv_idot")
+    return out

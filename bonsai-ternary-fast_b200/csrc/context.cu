@@ -1,0 +1,106 @@
+// Library state: error reporting, per-device initialisation, layout sizes.
+#include <cstdarg>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace btf {
+
+namespace {
+thread_local std::string g_last_error;
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+}  // namespace
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(BTF_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+const DeviceInfo* current_device() {
+  int dev = -1;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices || !g_dev[dev].ready) {
+    fail(BTF_ERR_STATE, "btf_init(%d) has not been called for the current device", dev);
+    return nullptr;
+  }
+  return &g_dev[dev];
+}
+
+// Kernel attribute set-up lives beside each kernel; btf_init calls these.
+int gemv_setup(const DeviceInfo& d);
+int gemm_setup(const DeviceInfo& d);
+
+}  // namespace btf
+
+using namespace btf;
+
+extern "C" {
+
+const char* btf_status_string(int status) {
+  switch (status) {
+    case BTF_OK: return "ok";
+    case BTF_ERR_ARG: return "invalid argument";
+    case BTF_ERR_CUDA: return "CUDA error";
+    case BTF_ERR_UNSUPPORTED: return "unsupported";
+    case BTF_ERR_TIMEOUT: return "device wait timed out";
+    case BTF_ERR_STATE: return "not initialised";
+    default: return "unknown status";
+  }
+}
+
+const char* btf_last_error(void) { return g_last_error.c_str(); }
+
+const char* btf_version(void) { return "btf_b200 0.1 (sm_100a)"; }
+
+int btf_init(int device) {
+  if (device < 0 || device >= kMaxDevices) return fail(BTF_ERR_ARG, "btf_init: device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DeviceInfo d;
+  int major = 0, minor = 0;
+  int st = BTF_OK;
+  if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&d.optin_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device)) !=
+          cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&d.l2_bytes, cudaDevAttrL2CacheSize, device)) != cudaSuccess) {
+    st = cuda_fail(e, "cudaDeviceGetAttribute");
+  } else if (major != 10 || minor != 0) {
+    st = fail(BTF_ERR_UNSUPPORTED, "btf_b200 is built for sm_100a (B200); device %d is sm_%d%d", device, major, minor);
+  } else if ((st = gemv_setup(d)) == BTF_OK && (st = gemm_setup(d)) == BTF_OK) {
+    d.ready = true;
+    g_dev[device] = d;
+  }
+  cudaSetDevice(prev);
+  return st;
+}
+
+int64_t btf_panel_bytes(int64_t N, int64_t K) {
+  if (N < 0 || K < 0) return 0;
+  return groups_of(N) * slices_of(K) * (int64_t)kPanelBytes;
+}
+int64_t btf_t2_codes_bytes(int64_t N, int64_t K) { return N * (K / 4); }
+int64_t btf_t2_scales_bytes(int64_t N, int64_t K) { return N * (K / 128) * 2; }
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+// Q8_0 activation quantiser, bit-exact to the reference's host rule
+// q8_block_host (include/btf/packed.hpp:117-134): per 32-column block
+//   amax = max |x|, d = fp16_rne(amax / 127) kept as fp32,
+//   id = amax != 0 ? 127 / amax : 0, q = round_half_even(x * id), s = sum(q).
+// IEEE division and multiplication only (no fast-math), as in the quantising
+// tail of the reference's prep_kernel (src/cuda/kernels.cu:185-201).
+#include "common.cuh"
+
+namespace btf {
+namespace {
+
+constexpr int kQThreads = 256;
+constexpr int kQWarps = kQThreads / 32;
+
+__global__ void __launch_bounds__(kQThreads)
+    quant_q8_kernel(const float* __restrict__ x, int ldx, int K, int8_t* __restrict__ q, float* __restrict__ d,
+                    int32_t* __restrict__ s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nsub = K / 32;
+  const int sb = blockIdx.x * kQWarps + warp;
+  const int m = blockIdx.y;
+  if (sb >= nsub) return;
+  const float v = x[(size_t)m * ldx + sb * 32 + lane];
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  // The host rule updates amax with (amax > a ? amax : a) from +0, so a block
+  // of zeros ends with the last element's zero, sign included.
+  const float last = __shfl_sync(0xffffffffu, v, 31);
+  const float amax_signed = amax == 0.0f ? last : amax;
+  const float dq = __half2float(__float2half_rn(__fdiv_rn(amax_signed, 127.0f)));
+  const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  const int qv = __float2int_rn(__fmul_rn(v, id));
+  q[(size_t)m * K + sb * 32 + lane] = (int8_t)qv;
+  int sum = qv;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) {
+    d[(size_t)m * nsub + sb] = dq;
+    s[(size_t)m * nsub + sb] = sum;
+  }
+}
+
+}  // namespace
+}  // namespace btf
+
+using namespace btf;
+
+extern "C" int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act, void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (K <= 0 || K % 32 || ldx < K)
+    return fail(BTF_ERR_ARG, "btf_quant_q8: need K a positive multiple of 32 and ldx >= K (K=%d ldx=%d)", K, ldx);
+  if (!x || !act.q || !act.d || !act.s) return fail(BTF_ERR_ARG, "btf_quant_q8: null pointer");
+  if (!current_device()) return BTF_ERR_STATE;
+  const dim3 grid((K / 32 + kQWarps - 1) / kQWarps, M);
+  if (grid.y > 65535) return fail(BTF_ERR_ARG, "btf_quant_q8: M=%d exceeds 65535", M);
+  quant_q8_kernel<<<grid, kQThreads, 0, (cudaStream_t)stream>>>(x, ldx, K, act.q, act.d, act.s);
+  return launch_status("quant_q8_kernel");
+}

@@ -1,0 +1,130 @@
+/*
+ * btf_b200 — B200-native (sm_100a) ternary GEMV/GEMM hot path, C ABI.
+ *
+ * Drop-in boundary for bonsai-ternary-fast's CUDA matmul path. Each entry
+ * point names the reference interface it replaces (paths relative to the
+ * reference project root). Conventions:
+ *   - every pointer is a DEVICE pointer unless its name ends in _host;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - launches are asynchronous, allocate nothing and never synchronise, so
+ *     they are legal inside CUDA graph capture (like src/cuda/kernels.cuh:3-7);
+ *   - every function returns a status code (BTF_OK = 0) instead of throwing;
+ *     btf_last_error() gives a one-line message for the calling thread.
+ *
+ * Resident weight layout ("panels", replaces T2 of include/btf/packed.hpp:6-14):
+ *   a [N][K] ternary matrix is cut into row groups of 16 rows and column
+ *   slices of 1024 columns (32 sub-blocks of 32 = 8 PTQ1_0 blocks of 128).
+ *   Panel (g, j) is 4352 contiguous bytes at ((g * S) + j) * 4352, S = ceil(K/1024):
+ *     bytes [0, 4096):    codes of row r (0..15), sub-block l (0..31) at r*256 + l*8,
+ *                         two little-endian T2 words (2-bit code = trit + 1; word w
+ *                         holds column 32l + 16w + 4k + j at bit 8j + 2k);
+ *     bytes [4096, 4352): fp16 block scales, block b (0..7) of row r at 4096 + b*32 + r*2.
+ *   Rows >= N and columns >= K are padding (code 1 = trit 0, scale 0).
+ *   Total size: btf_panel_bytes(N, K).
+ */
+#ifndef BTF_B200_H
+#define BTF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes */
+#define BTF_OK 0
+#define BTF_ERR_ARG 1         /* bad shape, pointer, alignment or mode */
+#define BTF_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define BTF_ERR_UNSUPPORTED 3 /* valid request the library does not serve (e.g. K too wide) */
+#define BTF_ERR_TIMEOUT 4     /* a bounded device-side wait gave up */
+#define BTF_ERR_STATE 5       /* library not initialised for this device */
+
+/* GEMV output modes. Same values as GemvMode in src/cuda/kernels.cuh:53. */
+#define BTF_STORE 0  /* y  = W x */
+#define BTF_ADD 1    /* y += W x */
+#define BTF_SWIGLU 2 /* y  = silu(W_gate x) * (W_up x); segs[0] = gate, segs[1] = up */
+
+/* Layout constants. */
+#define BTF_PANEL_ROWS 16
+#define BTF_PANEL_COLS 1024
+#define BTF_PANEL_BYTES 4352
+
+/* One matrix of a multi-segment GEMV. Mirrors GemvSeg (src/cuda/kernels.cuh:46-52)
+ * with the T2 codes/scales pair replaced by one panel buffer. */
+typedef struct btf_gemv_seg {
+  const void* panels; /* btf_panel_bytes(N, K) bytes, 16-byte aligned */
+  int N;              /* output rows */
+  float* y;           /* [M][ldy]; unused for segs[1] of BTF_SWIGLU */
+  int ldy;
+} btf_gemv_seg;
+
+/* Q8_0 activations of M rows of width K. Mirrors Q8Act (src/cuda/kernels.cuh:27-31). */
+typedef struct btf_q8act {
+  int8_t* q;  /* [M][K], 16-byte aligned */
+  float* d;   /* [M][K/32] fp16-valued block scales */
+  int32_t* s; /* [M][K/32] sum of q per block */
+} btf_q8act;
+
+/* ---- library / device state */
+const char* btf_status_string(int status);
+/* Last error message of the calling thread ("" if none). */
+const char* btf_last_error(void);
+/* Library version string. */
+const char* btf_version(void);
+
+/* Per-device set-up: shared-memory opt-ins and device limits. Call once per
+ * device, outside stream capture, before any launch on that device.
+ * Replaces btf::cuda::kernels_init (src/cuda/kernels.cuh:17, kernels.cu:718-729). */
+int btf_init(int device);
+
+/* Largest activation batch one GEMV launch keeps per pass for width K; M above
+ * it is processed in passes. Replaces gemv_max_nb (src/cuda/kernels.cuh:20). */
+int btf_gemv_max_nb(int K);
+
+/* ---- layout sizes */
+/* Bytes of the panel layout of an [N][K] matrix (K % 128 == 0). */
+int64_t btf_panel_bytes(int64_t N, int64_t K);
+/* Reference T2 sizes, include/btf/fast.hpp:45-46. */
+int64_t btf_t2_codes_bytes(int64_t N, int64_t K);
+int64_t btf_t2_scales_bytes(int64_t N, int64_t K);
+
+/* ---- repack (load time)
+ * PTQ1_0 (28-byte blocks, [N][K/128] in row order, 4-byte aligned; the source
+ * may be mapped host memory) -> panel layout. Replaces launch_repack
+ * (src/cuda/kernels.cuh:24, kernels.cu:737-743) for the B200 layout. */
+int btf_repack_panels(const void* ptq_src, int64_t N, int64_t K, void* panels, void* stream);
+/* Host twin of btf_repack_panels: same bytes, computed on the CPU.
+ * Replaces btf::repack_rows / btf::repack (src/repack.cpp:16-45). */
+int btf_repack_panels_host(const void* ptq_src_host, int64_t N, int64_t K, void* panels_host, int threads);
+/* PTQ1_0 -> reference T2 codes [nblocks][32 B] + fp16 scales [nblocks], exactly
+ * launch_repack's output (src/cuda/kernels.cuh:24), for callers that keep T2. */
+int btf_repack_t2(const void* ptq_src, int64_t nblocks, uint8_t* codes, uint16_t* scales, void* stream);
+/* Resident T2 (codes [N][K/4], scales [N][K/128]) -> panel layout. */
+int btf_t2_to_panels(const uint8_t* codes, const uint16_t* scales, int64_t N, int64_t K, void* panels,
+                     void* stream);
+/* Panel layout -> T2 (inverse, for tests and for callers that read T2 back). */
+int btf_panels_to_t2(const void* panels, int64_t N, int64_t K, uint8_t* codes, uint16_t* scales, void* stream);
+
+/* ---- Q8 activation quantiser
+ * x [M][ldx] fp32 -> Q8_0 (bit-exact to q8_block_host, include/btf/packed.hpp:117-134).
+ * The quantising part of launch_prep (src/cuda/kernels.cuh:42-43, kernels.cu:185-201)
+ * for a raw input (no norm, no Hadamard transform). K % 32 == 0. */
+int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act, void* stream);
+
+/* ---- ternary GEMV (batch M, CUDA cores: dp4a on the 2-bit codes)
+ * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
+ * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
+ * segments (gate, up) with the same N. K % 128 == 0. */
+int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
+
+/* Debug/parity entry point: the exact int32 trit dot of every (m, row,
+ * sub-block), idot[M][N][K/32] = code_dot - sum(q) — the integers the GEMV
+ * scales (src/emu_decoder.cpp:154-157). Same decode path as btf_gemv. */
+int btf_gemv_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BTF_B200_H */

@@ -1,0 +1,89 @@
+// C++17 mirror of the reference's launcher interface (src/cuda/kernels.cuh:13-56
+// of bonsai-ternary-fast), implemented over the btf_b200 C ABI. Call sites
+// written against btf::cuda (e.g. src/cuda/gpu_decoder.cu:396-450) compile
+// unchanged; errors throw std::runtime_error like the reference's launchers.
+//
+// Differences a maintainer must know:
+//   - GemvSeg::codes points at the PANEL buffer of the matrix (include/btf_b200.h)
+//     and GemvSeg::scales must be nullptr: the scales live inside the panels;
+//   - launch_repack keeps the reference's T2 output; launch_repack_panels is the
+//     loader for the B200 layout and needs N and K;
+//   - launch_prep serves the raw-input case (no norm, no Hadamard transform).
+#pragma once
+#include <cuda_runtime_api.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "btf_b200.h"
+
+namespace btf {
+namespace cuda {
+
+inline void throw_if(int status, const char* what) {
+  if (status != BTF_OK)
+    throw std::runtime_error(std::string(what) + ": " + btf_status_string(status) + ": " + btf_last_error());
+}
+
+// kernels.cuh:17
+inline void kernels_init(int device) { throw_if(btf_init(device), "kernels_init"); }
+
+// kernels.cuh:20
+inline int gemv_max_nb(int K) { return btf_gemv_max_nb(K); }
+
+// kernels.cuh:24 (T2 output, unchanged semantics)
+inline void launch_repack(const uint8_t* src, int64_t nblocks, uint8_t* codes, uint16_t* scales, cudaStream_t st) {
+  throw_if(btf_repack_t2(src, nblocks, codes, scales, st), "launch_repack");
+}
+
+// B200 resident layout: PTQ1_0 rows -> panels (size btf_panel_bytes(N, K)).
+inline void launch_repack_panels(const uint8_t* src, int64_t N, int64_t K, uint8_t* panels, cudaStream_t st) {
+  throw_if(btf_repack_panels(src, N, K, panels, st), "launch_repack_panels");
+}
+
+// kernels.cuh:27-31
+struct Q8Act {
+  int8_t* q = nullptr;  // [M][K]
+  float* d = nullptr;   // [M][K/32]
+  int* s = nullptr;     // [M][K/32]
+};
+
+// kernels.cuh:34-38
+struct Hx {
+  int block = 0;
+  int perm_hd = 0, perm_nk = 0, perm_rep = 0;
+  const float* signs = nullptr;
+};
+
+// kernels.cuh:42-43 — raw-input quantisation only.
+inline void launch_prep(const float* x, int ldx, int M, int n, const float* normw, float /*eps*/, const Hx& hx,
+                        float* xn_out, int /*ldxn*/, const Q8Act& a, cudaStream_t st) {
+  if (normw || hx.block || hx.signs || hx.perm_rep > 1 || xn_out)
+    throw std::runtime_error("launch_prep: only the raw-input Q8 quantisation is implemented");
+  throw_if(btf_quant_q8(x, ldx, M, n, btf_q8act{a.q, a.d, a.s}, st), "launch_prep");
+}
+
+// kernels.cuh:46-53
+struct GemvSeg {
+  const uint8_t* codes = nullptr;    // panel buffer
+  const uint16_t* scales = nullptr;  // must be nullptr (scales are in the panels)
+  int N = 0;
+  float* y = nullptr;
+  int ldy = 0;
+};
+enum GemvMode { kStore = BTF_STORE, kAdd = BTF_ADD, kSwiglu = BTF_SWIGLU };
+
+// kernels.cuh:56
+inline void launch_gemv(const GemvSeg* segs, int nseg, int K, int M, const Q8Act& a, GemvMode mode, cudaStream_t st) {
+  if (nseg < 1 || nseg > 3) throw std::runtime_error("gemv: 1..3 segments");
+  btf_gemv_seg s[3];
+  for (int i = 0; i < nseg; ++i) {
+    if (segs[i].scales) throw std::runtime_error("gemv: GemvSeg::scales must be nullptr with the panel layout");
+    s[i] = btf_gemv_seg{segs[i].codes, segs[i].N, segs[i].y, segs[i].ldy};
+  }
+  throw_if(btf_gemv(s, nseg, K, M, btf_q8act{a.q, a.d, a.s}, (int)mode, st), "launch_gemv");
+}
+
+}  // namespace cuda
+}  // namespace btf

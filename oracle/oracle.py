@@ -1,0 +1,255 @@
+"""numpy wrappers over the CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+Two libraries, built by oracle/Makefile:
+  * ``_build/liboracle.so`` — oracle.c, the plain-C restatement of the
+    reference path (always present once built; travels to GPU hosts);
+  * ``_ref/libbtf_ref.so`` — the reference's own sources compiled in place,
+    plus ref_shim.cpp (present where the reference tree was available at build
+    time; the built file also travels).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline /
+``--impl reference`` legs may import this module, and only as the checker or
+the timed CPU baseline.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libbtf_ref.so")
+
+_vp, _i32, _i64, _u16, _u32, _f32 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_uint16,
+                                     ctypes.c_uint32, ctypes.c_float)
+
+
+def build(quiet: bool = True) -> None:
+    """Runs oracle/Makefile (the reference part only if the reference tree exists)."""
+    subprocess.run(["make", "-C", HERE], check=True,
+                   stdout=subprocess.DEVNULL if quiet else None, stderr=None)
+
+
+def _p(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data
+
+
+class Oracle:
+    """oracle.c: the C restatement."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        sig = {
+            "orc_f32_to_f16": (_u16, [_f32]),
+            "orc_f16_to_f32": (_f32, [_u16]),
+            "orc_ptq_trit": (_i32, [_vp, _i32]),
+            "orc_ptq_encode": (None, [_vp, _vp, _i64, _vp]),
+            "orc_ptq_quant_row": (None, [_vp, _vp, _i64]),
+            "orc_repack_t2": (None, [_vp, _i64, _i64, _vp, _vp]),
+            "orc_t2_code": (_i32, [_vp, _i64]),
+            "orc_q8_block": (_i32, [_vp, _vp, _vp]),
+            "orc_q8_rows": (None, [_vp, _i64, _i32, _i32, _vp, _vp, _vp]),
+            "orc_round_q8_0": (None, [_vp, _i64, _vp]),
+            "orc_sub_dot": (_i32, [_u32, _u32, _vp]),
+            "orc_idot": (None, [_vp, _i64, _i64, _vp, _vp, _i32, _vp]),
+            "orc_gemv": (None, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i32, _i32]),
+            "orc_gemv_swiglu": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i32]),
+            "orc_gemv_f64": (None, [_vp, _vp, _i64, _i64, _vp, _vp, _i32, _vp]),
+        }
+        for n, (r, a) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = r, a
+        self.L = L
+
+    # -- PTQ1_0
+    def ptq_encode(self, trits: np.ndarray, scales: np.ndarray) -> np.ndarray:
+        t = np.ascontiguousarray(trits, dtype=np.int8)
+        s = np.ascontiguousarray(scales, dtype=np.uint16)
+        N, K = t.shape
+        out = np.empty((N, K // 128 * 28), dtype=np.uint8)
+        self.L.orc_ptq_encode(_p(t), _p(s), N * (K // 128), _p(out))
+        return out
+
+    def ptq_quant_rows(self, w: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        N, K = w.shape
+        out = np.empty((N, K // 128 * 28), dtype=np.uint8)
+        for r in range(N):
+            self.L.orc_ptq_quant_row(w[r].ctypes.data, out[r].ctypes.data, K)
+        return out
+
+    def ptq_trits(self, src: np.ndarray, K: int) -> np.ndarray:
+        """All trits of a PTQ1_0 [N][K/128*28] array, by the digit rule."""
+        N = src.shape[0]
+        blk = np.ascontiguousarray(src, dtype=np.uint8).reshape(N * (K // 128), 28)
+        out = np.empty((N * (K // 128), 128), dtype=np.int8)
+        for b in range(blk.shape[0]):
+            p = blk[b].ctypes.data
+            out[b] = [self.L.orc_ptq_trit(p, e) for e in range(128)]
+        return out.reshape(N, K)
+
+    # -- T2
+    def repack_t2(self, src: np.ndarray, N: int, K: int):
+        src = np.ascontiguousarray(src, dtype=np.uint8)
+        codes = np.empty((N, K // 4), dtype=np.uint8)
+        scales = np.empty((N, K // 128), dtype=np.uint16)
+        self.L.orc_repack_t2(_p(src), N, K, _p(codes), _p(scales))
+        return codes, scales
+
+    # -- Q8
+    def q8_rows(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        M, K = x.shape
+        q = np.empty((M, K), dtype=np.int8)
+        d = np.empty((M, K // 32), dtype=np.float32)
+        s = np.empty((M, K // 32), dtype=np.int32)
+        self.L.orc_q8_rows(_p(x), K, M, K, _p(q), _p(d), _p(s))
+        return q, d, s
+
+    def round_q8_0(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        self.L.orc_round_q8_0(_p(x), x.size, _p(out))
+        return out
+
+    # -- dots and GEMV
+    def idot(self, codes, K: int, q, s) -> np.ndarray:
+        N = codes.shape[0]
+        M = q.shape[0]
+        out = np.empty((M, N, K // 32), dtype=np.int32)
+        self.L.orc_idot(_p(np.ascontiguousarray(codes)), N, K, _p(np.ascontiguousarray(q)),
+                        _p(np.ascontiguousarray(s)), M, _p(out))
+        return out
+
+    def gemv(self, codes, scales, K: int, q, d, s, y: Optional[np.ndarray] = None, add: bool = False,
+             threads: int = 1) -> np.ndarray:
+        N = codes.shape[0]
+        M = q.shape[0]
+        if y is None:
+            y = np.zeros((M, N), dtype=np.float32)
+        self.L.orc_gemv(_p(codes), _p(scales), N, K, _p(q), _p(d), _p(s), M, _p(y), y.shape[1], 1 if add else 0,
+                        threads)
+        return y
+
+    def gemv_swiglu(self, gate, up, K: int, q, d, s, threads: int = 1) -> np.ndarray:
+        (gc, gs), (uc, us) = gate, up
+        N = gc.shape[0]
+        M = q.shape[0]
+        y = np.zeros((M, N), dtype=np.float32)
+        self.L.orc_gemv_swiglu(_p(gc), _p(gs), _p(uc), _p(us), N, K, _p(q), _p(d), _p(s), M, _p(y), N, threads)
+        return y
+
+    def gemv_f64(self, codes, scales, K: int, q, d) -> np.ndarray:
+        N = codes.shape[0]
+        M = q.shape[0]
+        y = np.zeros((M, N), dtype=np.float64)
+        self.L.orc_gemv_f64(_p(codes), _p(scales), N, K, _p(q), _p(d), M, _p(y))
+        return y
+
+
+class Reference:
+    """libbtf_ref.so: the reference's own compiled code (see ref_shim.cpp)."""
+
+    def __init__(self, path: str = REF_SO):
+        L = ctypes.CDLL(path)
+        sig = {
+            "ref_f32_to_f16": (_u16, [_f32]),
+            "ref_f16_to_f32": (_f32, [_u16]),
+            "ref_ptq_quant_row": (None, [_vp, _vp, _i64]),
+            "ref_ptq_trit": (_i32, [_vp, _i32]),
+            "ref_repack_rows": (None, [_vp, _i64, _i64, _vp, _vp]),
+            "ref_packed_code": (_i32, [_vp, _i64]),
+            "ref_q8_block": (_i32, [_vp, _vp, _vp]),
+            "ref_round_q8_0": (None, [_vp, _i64, _vp]),
+            "ref_sub_dot": (_i32, [_u32, _u32, _vp]),
+            "ref_pool_create": (_vp, [_i32]),
+            "ref_pool_destroy": (None, [_vp]),
+            "ref_pool_size": (_i32, [_vp]),
+            "ref_gemv": (None, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i32]),
+            "ref_matvec_raw": (None, [_vp, _vp, _i64, _i64, _vp, _vp]),
+        }
+        for n, (r, a) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = r, a
+        self.L = L
+        self._pool = None
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_SO)
+
+    def pool(self, threads: int):
+        if self._pool is None or self.L.ref_pool_size(self._pool) != threads:
+            if self._pool is not None:
+                self.L.ref_pool_destroy(self._pool)
+            self._pool = self.L.ref_pool_create(threads)
+        return self._pool
+
+    def ptq_quant_rows(self, w: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        N, K = w.shape
+        out = np.empty((N, K // 128 * 28), dtype=np.uint8)
+        for r in range(N):
+            self.L.ref_ptq_quant_row(w[r].ctypes.data, out[r].ctypes.data, K)
+        return out
+
+    def repack_rows(self, src: np.ndarray, N: int, K: int):
+        src = np.ascontiguousarray(src, dtype=np.uint8)
+        codes = np.empty((N, K // 4), dtype=np.uint8)
+        scales = np.empty((N, K // 128), dtype=np.uint16)
+        self.L.ref_repack_rows(_p(src), N, K, _p(codes), _p(scales))
+        return codes, scales
+
+    def q8_rows(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        M, K = x.shape
+        q = np.empty((M, K), dtype=np.int8)
+        d = np.empty((M, K // 32), dtype=np.float32)
+        s = np.empty((M, K // 32), dtype=np.int32)
+        for m in range(M):
+            for b in range(K // 32):
+                s[m, b] = self.L.ref_q8_block(x[m, b * 32:].ctypes.data, q[m, b * 32:].ctypes.data,
+                                              d[m, b:].ctypes.data)
+        return q, d, s
+
+    def round_q8_0(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        self.L.ref_round_q8_0(_p(x), x.size, _p(out))
+        return out
+
+    def gemv(self, codes, scales, K: int, q, d, s, y: Optional[np.ndarray] = None, add: bool = False,
+             threads: int = 1) -> np.ndarray:
+        N = codes.shape[0]
+        M = q.shape[0]
+        if y is None:
+            y = np.zeros((M, N), dtype=np.float32)
+        pool = self.pool(threads) if threads > 1 else None
+        self.L.ref_gemv(pool, _p(codes), _p(scales), N, K, _p(q), _p(d), _p(s), M, _p(y), y.shape[1],
+                        1 if add else 0)
+        return y
+
+    def matvec_raw(self, src: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+        y = np.zeros(N, dtype=np.float32)
+        self.L.ref_matvec_raw(None, _p(np.ascontiguousarray(src)), N, K, _p(np.ascontiguousarray(x, np.float32)),
+                              _p(y))
+        return y
+
+
+def panel_decode(panels: np.ndarray, N: int, K: int):
+    """Independent numpy reader of the panel layout (include/btf_b200.h) -> T2 codes [N][K/4], scales [N][K/128].
+
+    Written from the layout description, not from the library, so a test that
+    compares it with the reference T2 checks the library's layout end to end."""
+    S = (K + 1023) // 1024
+    G = (N + 15) // 16
+    p = np.asarray(panels, dtype=np.uint8).reshape(G, S, 4352)
+    codes = p[:, :, :4096].reshape(G, S, 16, 256).transpose(0, 2, 1, 3).reshape(G * 16, S * 256)
+    sc = p[:, :, 4096:].copy().view(np.uint16).reshape(G, S, 8, 16).transpose(0, 3, 1, 2).reshape(G * 16, S * 8)
+    return np.ascontiguousarray(codes[:N, :K // 4]), np.ascontiguousarray(sc[:N, :K // 128])

@@ -1,0 +1,99 @@
+// C entry points over the REFERENCE's own compiled sources — TEST INFRASTRUCTURE ONLY.
+//
+// oracle/Makefile compiles this file together with the reference's sources
+// (src/repack.cpp and ref/bonsai-decoder/src/{types,cpu_ops,gguf,model,
+// mapped_file}.cpp, read in place from the reference tree) into
+// oracle/_ref/libbtf_ref.so. Nothing here re-implements reference math except
+// ref_gemv, whose 20-line loop is the body of the private member
+// EmuDecoder::gemv (src/emu_decoder.cpp:143-165) restated around the public
+// helpers it calls (btf::sub_dot_host, bd::fp16_to_f32, bd::ThreadPool),
+// because that member is not reachable from outside its translation unit.
+//
+// Used by tests/ to pin oracle/oracle.c, and by bench.py's CPU baseline /
+// `--impl reference` arm as the reference's own CPU GEMV.
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "bd/cpu_ops.hpp"
+#include "bd/gguf.hpp"
+#include "bd/types.hpp"
+#include "btf/fast.hpp"
+#include "btf/packed.hpp"
+
+#define REF_API extern "C" __attribute__((visibility("default")))
+
+REF_API uint16_t ref_f32_to_f16(float f) { return bd::f32_to_fp16(f); }
+REF_API float ref_f16_to_f32(uint16_t h) { return bd::fp16_to_f32(h); }
+
+// bd::quant_row(PTQ1_0) — ref/bonsai-decoder/src/types.cpp:289-320
+REF_API void ref_ptq_quant_row(const float* x, uint8_t* out, int64_t k) { bd::quant_row(bd::T_PTQ1_0, x, out, k); }
+
+// bd::ptq1_0_trit — ref/bonsai-decoder/include/bd/types.hpp:70-78
+REF_API int ref_ptq_trit(const uint8_t* blk, int e) { return bd::ptq1_0_trit(blk, e); }
+
+// btf::repack_rows — src/repack.cpp:16-27
+REF_API void ref_repack_rows(const uint8_t* src, int64_t rows, int64_t K, uint8_t* codes, uint16_t* scales) {
+  btf::repack_rows(src, rows, K, codes, scales);
+}
+
+// btf::packed_code — include/btf/packed.hpp:94-98
+REF_API int ref_packed_code(const uint8_t* row_codes, int64_t e) { return btf::packed_code(row_codes, e); }
+
+// btf::q8_block_host — include/btf/packed.hpp:117-134
+REF_API int ref_q8_block(const float* x, int8_t* q, float* d) { return btf::q8_block_host(x, q, d); }
+
+// bd::round_q8_0 — ref/bonsai-decoder/src/cpu_ops.cpp:189-197
+REF_API void ref_round_q8_0(const float* x, int64_t n, float* out) { bd::round_q8_0(x, n, out); }
+
+// btf::sub_dot_host — include/btf/packed.hpp:108-113
+REF_API int ref_sub_dot(uint32_t w0, uint32_t w1, const uint32_t* aw) { return btf::sub_dot_host(w0, w1, aw); }
+
+// bd::ThreadPool — ref/bonsai-decoder/src/cpu_ops.cpp:19-73
+REF_API void* ref_pool_create(int threads) { return new bd::ThreadPool(threads); }
+REF_API void ref_pool_destroy(void* p) { delete static_cast<bd::ThreadPool*>(p); }
+REF_API int ref_pool_size(void* p) { return static_cast<bd::ThreadPool*>(p)->size(); }
+
+// The emulator GEMV, src/emu_decoder.cpp:143-165, on T2 codes/scales.
+// add != 0: y += W x, else y = W x. pool may be null (one thread).
+REF_API void ref_gemv(void* pool, const uint8_t* codes, const uint16_t* scales, int64_t N, int64_t K,
+                      const int8_t* q, const float* d, const int32_t* s, int M, float* y, int64_t ldy, int add) {
+  const int64_t nsub = K / 32;
+  auto run = [&](int64_t b, int64_t e) {
+    for (int64_t r = b; r < e; ++r) {
+      const uint8_t* cr = codes + r * (K / 4);
+      const uint16_t* sr = scales + r * (K / 128);
+      for (int m = 0; m < M; ++m) {
+        const uint32_t* aw = reinterpret_cast<const uint32_t*>(q + (size_t)m * K);
+        float acc = 0.f;
+        for (int64_t sb = 0; sb < nsub; ++sb) {
+          uint32_t w0, w1;
+          std::memcpy(&w0, cr + sb * 8, 4);
+          std::memcpy(&w1, cr + sb * 8 + 4, 4);
+          const int idot = btf::sub_dot_host(w0, w1, aw + sb * 8) - s[(size_t)m * nsub + sb];
+          acc += bd::fp16_to_f32(sr[sb / 4]) * d[(size_t)m * nsub + sb] * (float)idot;
+        }
+        float& out = y[(size_t)m * ldy + r];
+        out = add ? out + acc : acc;
+      }
+    }
+  };
+  if (pool)
+    static_cast<bd::ThreadPool*>(pool)->parallel_for(N, run);
+  else
+    run(0, N);
+}
+
+// bd::matvec_raw(ggml_act = true) on a raw PTQ1_0 [N][K] tensor —
+// ref/bonsai-decoder/src/cpu_ops.cpp:199-243, the second oracle of
+// tests/test_packed.cpp:63-87.
+REF_API void ref_matvec_raw(void* pool, const uint8_t* src, int64_t N, int64_t K, const float* x, float* y) {
+  bd::GgufTensor t;
+  t.name = "w";
+  t.ne = {K, N};
+  t.type = bd::T_PTQ1_0;
+  t.data = src;
+  bd::ThreadPool one(1);
+  bd::ThreadPool& p = pool ? *static_cast<bd::ThreadPool*>(pool) : one;
+  bd::matvec_raw(p, t, x, y, true);
+}

@@ -1,0 +1,13 @@
+// Compile-only check: a reference-style call site (src/cuda/gpu_decoder.cu:396-416
+// of bonsai-ternary-fast) written against btf::cuda builds with include/btf_b200.hpp.
+#include "btf_b200.hpp"
+
+void ffn_call_site(const uint8_t* gate, const uint8_t* up, const uint8_t* down, float* G, float* x, int E, int F,
+                   int M, btf::cuda::Q8Act act, cudaStream_t st) {
+  namespace c = btf::cuda;
+  const c::GemvSeg gu[2] = {{gate, nullptr, F, G, F}, {up, nullptr, F, nullptr, 0}};
+  c::launch_gemv(gu, 2, E, M, act, c::kSwiglu, st);
+  c::launch_prep(G, F, M, F, nullptr, 1e-6f, c::Hx{}, nullptr, 0, act, st);
+  const c::GemvSeg d{down, nullptr, E, x, E};
+  c::launch_gemv(&d, 1, F, M, act, c::kAdd, st);
+}

@@ -1,0 +1,81 @@
+"""CPU tests of the product library's host side: exports, layout sizes, the
+host repack twin, argument checking. No kernel is launched here."""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, PKG
+
+
+def _declared_symbols():
+    hdr = open(os.path.join(ROOT, "include", "btf_b200.h")).read()
+    return sorted(set(re.findall(r"\b(btf_[a-z0-9_]+)\s*\(", hdr)))
+
+
+def test_library_exports_every_declared_symbol(btf):
+    names = _declared_symbols()
+    assert len(names) >= 15
+    L = btf.lib()
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert set(btf.EXPORTS) == set(names)
+    out = subprocess.run(["nm", "-D", "--defined-only", btf.LIB_PATH], capture_output=True, text=True).stdout
+    for n in names:
+        assert re.search(rf"\bT {n}$", out, re.M), n
+
+
+def test_layout_sizes(btf):
+    assert btf.panel_bytes(17408, 5120) == 17408 * 5120 // 4 + 17408 * 40 * 2  # no padding at the config-0 shape
+    assert btf.panel_bytes(37, 1024) == 3 * 1 * 4352
+    assert btf.panel_bytes(16, 1152) == 1 * 2 * 4352
+    assert btf.t2_codes_bytes(37, 1024) == 37 * 256
+    assert btf.t2_scales_bytes(37, 1024) == 37 * 8 * 2
+    assert btf.gemv_max_nb(5120) == 8 and btf.gemv_max_nb(100) == 0
+
+
+@pytest.mark.parametrize("N,K", [(37, 1024), (41, 1152), (16, 128), (1, 5120), (33, 3072)])
+def test_host_repack_matches_reference_t2(btf, orc, N, K):
+    import oracle
+    import synth
+
+    src = synth.ternary_ptq(N, K, seed=N + K)
+    pan = btf.repack_panels_host(src, N, K, threads=3)
+    assert pan.size == btf.panel_bytes(N, K)
+    codes, scales = oracle.panel_decode(pan, N, K)
+    c_ref, s_ref = orc.repack_t2(src, N, K)
+    assert np.array_equal(codes, c_ref) and np.array_equal(scales, s_ref)
+    # padding: rows >= N and columns >= K hold code 1 (trit 0) and scale 0
+    G, S = (N + 15) // 16, (K + 1023) // 1024
+    p = pan.reshape(G, S, 4352)
+    full_c = p[:, :, :4096].reshape(G, S, 16, 256).transpose(0, 2, 1, 3).reshape(G * 16, S * 256)
+    full_s = p[:, :, 4096:].copy().view(np.uint16).reshape(G, S, 8, 16).transpose(0, 3, 1, 2).reshape(G * 16, S * 8)
+    assert np.all(full_c[N:] == 0x55) and np.all(full_c[:, K // 4:] == 0x55)
+    assert np.all(full_s[N:] == 0) and np.all(full_s[:, K // 128:] == 0)
+
+
+def test_host_repack_rejects_bad_shape(btf):
+    src = np.zeros(28, dtype=np.uint8)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        btf.repack_panels_host(src, 1, 100)
+
+
+def test_init_without_gpu_reports_error(btf):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    rc = btf.lib().btf_init(0)
+    assert rc != 0
+    assert btf.lib().btf_last_error().decode()
+
+
+def test_cpp_shim_header_compiles():
+    # the C++17 mirror of the reference launchers (include/btf_b200.hpp) must
+    # compile as a drop-in for src/cuda/kernels.cuh call sites
+    src = os.path.join(ROOT, "tests", "shim_compile.cpp")
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
+                        "-I", "/usr/local/cuda/include", src], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
