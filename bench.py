@@ -223,11 +223,13 @@ def gpu_arm(args):
             dist.all_gather_into_tensor(full_out[name].view(-1), loc_out[name].view(-1))
 
     # per-kernel timing events around the launches of the last layer of a step
-    kinds = ("quant", "qkv", "o", "gateup", "down")
+    kinds = ("qkv", "o", "gateup", "down")
     evs = {k: (torch.cuda.Event(enable_timing=True, external=True),
                torch.cuda.Event(enable_timing=True, external=True)) for k in kinds}
 
-    def layer(L, timed=False):
+    def layer(L, timed=False, fused=True):
+        # fused: quantisation inside each GEMV (btf_gemv_f32, 4 launches per layer);
+        # otherwise the drop-in pair launch_prep -> launch_gemv (8 launches per layer)
         def t0(k):
             if timed:
                 evs[k][0].record(stream)
@@ -236,36 +238,37 @@ def gpu_arm(args):
             if timed:
                 evs[k][1].record(stream)
 
-        t0("quant")
-        btf.quant_q8(x_in["attn"], acts["attn"], stream=stream)
-        t1("quant")
+        def gemv(segs, K, xk, mode):
+            if fused:
+                btf.launch_gemv_f32(segs, K, 1, x_in[xk], mode, stream)
+            else:
+                btf.quant_q8(x_in[xk], acts[xk], stream=stream)
+                btf.launch_gemv(segs, K, 1, acts[xk], mode, stream)
+
+        def seg(n):
+            return (L[n], loc_out[n], loc_out[n].shape[1])
+
         t0("qkv")
-        btf.launch_gemv([(L["q"], loc_out["q"], loc_out["q"].shape[1]), (L["k"], loc_out["k"], loc_out["k"].shape[1]),
-                         (L["v"], loc_out["v"], loc_out["v"].shape[1])], 5120, 1, acts["attn"], btf.STORE, stream)
+        gemv([seg("q"), seg("k"), seg("v")], 5120, "attn", btf.STORE)
         t1("qkv")
         for n in ("q", "k", "v"):
             gather(n)
-        btf.quant_q8(x_in["o"], acts["o"], stream=stream)
         t0("o")
-        btf.launch_gemv([(L["o"], loc_out["o"], loc_out["o"].shape[1])], 6144, 1, acts["o"], btf.ADD, stream)
+        gemv([seg("o")], 6144, "o", btf.ADD)
         t1("o")
         gather("o")
-        btf.quant_q8(x_in["ffn"], acts["ffn"], stream=stream)
         t0("gateup")
-        btf.launch_gemv([(L["gate"], loc_out["gate"], loc_out["gate"].shape[1]), (L["up"], None, 0)], 5120, 1,
-                        acts["ffn"], btf.SWIGLU, stream)
+        gemv([seg("gate"), (L["up"], None, 0)], 5120, "ffn", btf.SWIGLU)
         t1("gateup")
         gather("gate")
-        btf.quant_q8(x_in["down"], acts["down"], stream=stream)
         t0("down")
-        btf.launch_gemv([(L["down"], loc_out["down"], loc_out["down"].shape[1])], 17408, 1, acts["down"], btf.ADD,
-                        stream)
+        gemv([seg("down")], 17408, "down", btf.ADD)
         t1("down")
         gather("down")
 
-    def step():
+    def step(fused=True):
         for i, L in enumerate(model.layers):
-            layer(L, timed=(i == len(model.layers) - 1))
+            layer(L, timed=(i == len(model.layers) - 1) and fused, fused=fused)
 
     # e2e variant: inputs from pinned host memory in, outputs back, every step
     h_in = {k: v.cpu().pin_memory() for k, v in x_in.items()}
@@ -285,13 +288,16 @@ def gpu_arm(args):
     with torch.cuda.stream(stream):
         for _ in range(2):
             step()
+            step(fused=False)
             step_e2e()
     torch.cuda.synchronize()
-    g_dev, g_e2e = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    g_dev, g_e2e, g_unf = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_dev, stream=stream):
         step()
     with torch.cuda.graph(g_e2e, stream=stream):
         step_e2e()
+    with torch.cuda.graph(g_unf, stream=stream):
+        step(fused=False)
     torch.cuda.synchronize()
 
     def timed(graph, K, W):
@@ -326,6 +332,8 @@ def gpu_arm(args):
     clocks.stop()
     kern_ms = {k: evs[k][0].elapsed_time(evs[k][1]) for k in kinds}
     ms_e2e = timed(g_e2e, args.steps, args.warmup)
+    ms_unf = timed(g_unf, args.steps, args.warmup)
+    dev_err = btf.device_error()
 
     # algorithmic bytes (whole job: every matrix counted once)
     per_layer = {
@@ -333,13 +341,17 @@ def gpu_arm(args):
         "o": synth.gemv_bytes(sh["o"][1], sh["o"][0], add=True),
         "gateup": 2 * synth.gemv_bytes(sh["gate"][1], 5120) - 5120 * 5 // 4 - sh["gate"][1] * 4,
         "down": synth.gemv_bytes(sh["down"][1], sh["down"][0], add=True),
-        "quant": 4 * 5120 + 5120 * 5 // 4,
     }
-    quant_all = sum(4 * k + k * 5 // 4 for k in (5120, 6144, 5120, 17408))
-    layer_bytes = per_layer["qkv"] + per_layer["o"] + per_layer["gateup"] + per_layer["down"] + quant_all
+    # fused quantisation reads x (fp32) instead of the Q8 copy: +2.75 B per input element
+    per_layer["qkv"] += 5120 * 11 // 4
+    per_layer["o"] += 6144 * 11 // 4
+    per_layer["gateup"] += 5120 * 11 // 4
+    per_layer["down"] += 17408 * 11 // 4
+    layer_bytes = per_layer["qkv"] + per_layer["o"] + per_layer["gateup"] + per_layer["down"]
     step_bytes = layer_bytes * N_LAYERS
     value = step_bytes * args.steps / (ms_dev * 1e-3) / 1e9
     e2e = step_bytes * args.steps / (ms_e2e * 1e-3) / 1e9
+    unfused = step_bytes * args.steps / (ms_unf * 1e-3) / 1e9
 
     peak, peak_kind = measured_peaks()
     # dominant kernel: the gate/up swiglu GEMV (52 % of the step's bytes); on this rank's shard
@@ -365,13 +377,17 @@ def gpu_arm(args):
                        "layers": N_LAYERS, "bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2: 5.8 GB of distinct resident weights per step",
                        "parallelism": f"N-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-                       "graph": "one CUDA graph per step"},
+                       "graph": "one CUDA graph per step, programmatic dependent launch between kernels",
+                       "quantisation": "fused into each GEMV (btf_gemv_f32)"},
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
-                         "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,8,SWIGLU> gate+up",
+                         "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,SWIGLU,fused> gate+up",
                          "peak_source": peak_kind},
             "kernels": kernels,
+            "unfused_drop_in_path": {"value": unfused, "unit": UNIT, "note": "launch_prep + launch_gemv pairs, "
+                                     "8 launches per layer (same bytes counted)"},
+            "device_error_word": dev_err,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * N_LAYERS * 8,
+            "gpu_launches": args.steps * N_LAYERS * 4,
             "clocks": clocks.report(),
         }
         if world == 1 and not args.no_cpu_baseline:

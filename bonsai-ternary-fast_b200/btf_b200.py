@@ -23,14 +23,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libbtf_b200.so")
 
 STORE, ADD, SWIGLU = 0, 1, 2  # GemvMode values (src/cuda/kernels.cuh:53)
-PANEL_ROWS, PANEL_COLS, PANEL_BYTES = 16, 1024, 4352
+PANEL_ROWS, PANEL_COLS, PANEL_BYTES = 8, 1024, 2176
 
 # Every symbol include/btf_b200.h declares; tests check the library exports them.
 EXPORTS = (
     "btf_status_string", "btf_last_error", "btf_version", "btf_init", "btf_gemv_max_nb",
     "btf_panel_bytes", "btf_t2_codes_bytes", "btf_t2_scales_bytes",
     "btf_repack_panels", "btf_repack_panels_host", "btf_repack_t2", "btf_t2_to_panels", "btf_panels_to_t2",
-    "btf_quant_q8", "btf_gemv", "btf_gemv_idot",
+    "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot",
 )
 
 
@@ -74,6 +74,8 @@ def lib() -> ctypes.CDLL:
         "btf_panels_to_t2": (i32, [vp, i64, i64, vp, vp, vp]),
         "btf_quant_q8": (i32, [vp, i32, i32, i32, Q8ActC, vp]),
         "btf_gemv": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
+        "btf_gemv_f32": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
+        "btf_device_error": (i32, [i32]),
         "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
     }
     for name, (res, args) in sig.items():
@@ -228,10 +230,25 @@ def quant_q8(x, act: Optional[Q8Act] = None, stream=None) -> Q8Act:
 
 def launch_gemv(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int = STORE, stream=None) -> None:
     """launch_gemv (kernels.cuh:56). segs: (PanelMatrix, y tensor or None, ldy) per segment."""
+    check(lib().btf_gemv(_segs(segs), len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemv")
+
+
+def _segs(segs):
     arr = (GemvSeg * len(segs))()
     for i, (pm, y, ldy) in enumerate(segs):
         arr[i] = GemvSeg(_ptr(pm.panels), pm.N, _ptr(y), ldy)
-    check(lib().btf_gemv(arr, len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemv")
+    return arr
+
+
+def launch_gemv_f32(segs: Sequence[tuple], K: int, M: int, x, mode: int = STORE, stream=None) -> None:
+    """Fused quantise + GEMV from fp32 activations x [M][>=K] (btf_gemv_f32)."""
+    check(lib().btf_gemv_f32(_segs(segs), len(segs), K, M, _ptr(x), x.stride(0), mode, _stream(stream)),
+          "btf_gemv_f32")
+
+
+def device_error(clear: bool = False) -> int:
+    """Device error word (nonzero after a bounded device-side wait timed out)."""
+    return lib().btf_device_error(1 if clear else 0)
 
 
 def gemv_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):

@@ -30,6 +30,7 @@ struct DeviceInfo {
   int optin_smem = 0;   // max dynamic shared memory per block (opt-in)
   int smem_per_sm = 0;
   int l2_bytes = 0;
+  int* err_word = nullptr;  // device address of the error word (bounded-wait time-outs)
 };
 // State of the current device, or nullptr (and a recorded error) if btf_init
 // was not called for it.
@@ -38,8 +39,8 @@ const DeviceInfo* current_device();
 // ------------------------------------------------------------------ layout
 constexpr int kRows = BTF_PANEL_ROWS;         // rows per row group
 constexpr int kCols = BTF_PANEL_COLS;         // columns per slice
-constexpr int kPanelBytes = BTF_PANEL_BYTES;  // 16 * 256 code bytes + 16 * 8 * 2 scale bytes
-constexpr int kCodeBytes = 4096;              // code part of a panel
+constexpr int kPanelBytes = BTF_PANEL_BYTES;  // 8 * 256 code bytes + 8 * 8 * 2 scale bytes
+constexpr int kCodeBytes = 2048;              // code part of a panel
 constexpr int kSubPerSlice = 32;              // 32-column sub-blocks per slice
 constexpr int kBlocksPerSlice = 8;            // 128-column scale blocks per slice
 
@@ -48,7 +49,7 @@ __host__ __device__ inline int64_t slices_of(int64_t K) { return (K + kCols - 1)
 __host__ __device__ inline int64_t panel_offset(int64_t g, int64_t j, int64_t S) { return (g * S + j) * kPanelBytes; }
 // Byte offset inside a panel of row r's codes for sub-block l, and of row r's scale for block b.
 __host__ __device__ inline int code_offset(int r, int l) { return r * 256 + l * 8; }
-__host__ __device__ inline int scale_offset(int r, int b) { return kCodeBytes + b * 32 + r * 2; }
+__host__ __device__ inline int scale_offset(int r, int b) { return kCodeBytes + b * 16 + r * 2; }
 
 // Byte of a 32-bit T2 code word filled with code 1 (trit 0) in every field.
 constexpr uint32_t kPadWord = 0x55555555u;
@@ -91,6 +92,104 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+}  // namespace btf
+
+namespace btf {
+
+// ------------------------------------------------------------------ Q8 (one 32-block per warp)
+// Quantises the 32 values of a block held one per lane, bit-exact to the host
+// rule q8_block_host (include/btf/packed.hpp:117-134 of the reference):
+// amax = max |x| (a block of zeros keeps the last element's sign, as the host's
+// sequential (amax > a ? amax : a) update does), d = fp16_rne(amax / 127),
+// id = amax != 0 ? 127 / amax : 0, q = round_half_even(x * id), s = sum(q).
+// Returns q of this lane; d and s are valid in every lane.
+__device__ __forceinline__ int q8_warp(float v, float& dq, int& sum) {
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float last = __shfl_sync(0xffffffffu, v, 31);
+  const float amax_signed = amax == 0.0f ? last : amax;
+  dq = __half2float(__float2half_rn(__fdiv_rn(amax_signed, 127.0f)));
+  const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  const int qv = __float2int_rn(__fmul_rn(v, id));
+  sum = qv;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  return qv;
+}
+
+// ------------------------------------------------------------------ async copies, barriers, PDL
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// 1-D bulk copy global -> shared (TMA unit), completion counted on `bar`.
+// dst, src and bytes must be multiples of 16. No multicast.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for phase `parity` of `bar` for at most `limit_ns`; false on time-out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue now / wait until the previous kernel's memory is visible.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Device-side error word (time-outs of bounded waits); read by btf_device_error().
+constexpr int kErrWaitTimeout = 1;
+
+// Launches kern<<<grid, block, smem, st>>> with programmatic stream
+// serialisation enabled, so it may overlap the tail of the previous kernel.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace btf

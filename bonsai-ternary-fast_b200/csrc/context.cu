@@ -42,8 +42,8 @@ const DeviceInfo* current_device() {
 }
 
 // Kernel attribute set-up lives beside each kernel; btf_init calls these.
-int gemv_setup(const DeviceInfo& d);
-int gemm_setup(const DeviceInfo& d);
+int gemv_setup(DeviceInfo& d);
+int gemm_setup(DeviceInfo& d);
 
 }  // namespace btf
 

@@ -5,22 +5,32 @@
 // activation row m:
 //   y[m][r] {=, +=} sum_s  (fp16 scale[r][s/4] * d[m][s]) * idot[m][r][s],
 //   idot = sum over the 32 columns of sub-block s of trit * q  (exact int32),
-// with the swiglu epilogue silu(gate) * up.
+// with the swiglu epilogue silu(gate) * up (kernels.cu:318-320).
 //
-// Work decomposition (B200 design, not the reference's):
-//   - one warp owns a tile of RW output rows (inside one 16-row group) and
-//     walks every 1024-column slice of those rows; lane l always handles
-//     sub-block l of the slice, so its activation words for the slice are
-//     loaded once and reused for all RW rows;
-//   - the codes of the RW rows are 8-byte streaming loads (L1 bypass), the
-//     RW fp16 scales of a lane one vector load (they sit contiguous in the
-//     panel), and the next slice's codes/scales are loaded before the current
-//     slice is computed, so two slices per warp are in flight;
+// B200 design (not the reference's):
+//   - persistent grid (one or two CTAs per SM); each CTA owns a contiguous,
+//     balanced range of "units" (one 8-row group of a segment, all K; for
+//     swiglu the gate and up groups of the same rows), so every SM streams
+//     the same number of bytes;
+//   - each of the 8 warps is its own producer: lane 0 keeps a ring of DEPTH
+//     panels (2176 B, 8 rows x 1024 columns + scales; swiglu: gate + up)
+//     filled by 1-D TMA bulk copies (cp.async.bulk, no multicast) on an
+//     mbarrier per slot; waits are bounded and report a device error word;
+//   - programmatic dependent launch: the weight copies of the first DEPTH
+//     panels are issued before griddepcontrol.wait, i.e. while the previous
+//     kernel in the stream (quantiser or GEMV) is still finishing; the
+//     activation is read only after the wait;
+//   - the activation (Q8, or fp32 quantised in the prologue with the same
+//     bit-exact rule as btf_quant_q8) sits in shared memory, split so that the
+//     lane loads are bank-conflict free; lane l always handles sub-block l of
+//     a slice, so its activation is loaded once per panel and reused for all
+//     8 (16) rows;
 //   - per (row, sub-block) the code dot uses four unshifted code masks
 //     (code * 4^k per byte) with unsigned x signed dp4a, one accumulator per
-//     k, recombined by exact arithmetic shifts; the -sum(q) correction and the
-//     int->float conversion are folded into one biased add (see kMagicInt).
+//     k, recombined by exact arithmetic shifts; -sum(q) and the int->float
+//     conversion are folded into one biased add (kMagicInt).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -30,18 +40,29 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSeg = 3;
+constexpr int kMaxNb = 4;                 // activation rows per pass
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per bounded wait
+constexpr size_t kSmemTarget = 110 * 1024;        // two CTAs per SM when it fits
 
 struct GemvParams {
-  const uint8_t* pan[kMaxSeg];
-  float* y[kMaxSeg];
-  int n[kMaxSeg];
-  int ldy[kMaxSeg];
-  int t1, t2, ttotal;  // cumulative warp-tile counts of the segments
+  const uint8_t* pan0;
+  const uint8_t* pan1;
+  const uint8_t* pan2;
+  float* y0;
+  float* y1;
+  float* y2;
+  int n0, n1, n2;
+  int ld0, ld1, ld2;
+  int u1, u2, utotal;  // cumulative unit (8-row group) counts of the segments
   int K, S, nsub;
-  int m0, nb;  // activation rows m0 .. m0 + nb - 1 (nb <= NB)
-  const int8_t* q;
+  int m0, nb;          // activation rows m0 .. m0 + nb - 1 (nb <= NB)
+  const int8_t* q;     // Q8 input (FUSE == false)
   const float* d;
   const int32_t* s;
+  const float* x;      // fp32 input (FUSE == true)
+  int ldx;
+  int depth;           // ring slots per warp
+  int* err;
 };
 
 // Biased trit dot of one (row, sub-block): returns kMagicInt + idot, where
@@ -61,140 +82,193 @@ __device__ __forceinline__ int sub_dot_biased(uint32_t w0, uint32_t w1, const ui
   return c0 + (c1 >> 2) + (c2 >> 4) + (c3 >> 6);
 }
 
-// RWO fp16 scales (RWO consecutive rows, one block) as RWO/2 half2 words.
-template <int RWO>
-__device__ __forceinline__ void load_scales(const uint8_t* p, uint32_t (&h)[(RWO + 1) / 2]) {
-  if constexpr (RWO == 16) {
-    const uint4 a = ld_stream_v4(p), b = ld_stream_v4(p + 16);
-    h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w;
-    h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
-  } else if constexpr (RWO == 8) {
-    const uint4 a = ld_stream_v4(p);
-    h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w;
-  } else if constexpr (RWO == 4) {
-    const uint2 a = ld_stream_v2(p);
-    h[0] = a.x; h[1] = a.y;
-  } else {
-    static_assert(RWO == 2, "RWO must be 2, 4, 8 or 16");
-    h[0] = *reinterpret_cast<const uint32_t*>(p);
-  }
-}
-
 __device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu))); }
 __device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 >> 16))); }
-
-template <int RWO>
-__device__ __forceinline__ float scale_of(const uint32_t (&h)[(RWO + 1) / 2], int i) {
-  return (i & 1) ? half_hi(h[i >> 1]) : half_lo(h[i >> 1]);
-}
-
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
-// NB: activation rows per pass; RW: rows loaded per warp tile; MODE: BTF_STORE / BTF_ADD / BTF_SWIGLU.
-// For swiglu a tile is RW/2 gate rows plus the same RW/2 rows of up.
-template <int NB, int RW, int MODE>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
+// Shared-memory layout (bytes), identical on host and device.
+struct SmemPlan {
+  int stage, ring, bars, act, total;
+  __host__ __device__ SmemPlan(int mode, int nb, int S, int depth) {
+    stage = (mode == BTF_SWIGLU ? 2 : 1) * kPanelBytes;
+    ring = kWarps * depth * stage;
+    bars = kWarps * depth * 8;
+    act = nb * S * kSubPerSlice * 40;  // qa 16 B + qb 16 B + d 4 B + magic_s 4 B per sub-block
+    total = ring + bars + act;
+  }
+};
+
+template <int NB, int MODE, bool FUSE>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
-  constexpr int RWO = kSwi ? RW / 2 : RW;  // output rows per tile
-  static_assert(kRows % RWO == 0, "a tile must sit inside one row group");
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (t >= p.ttotal) return;
-  const int seg = kSwi ? 0 : (t >= p.t1) + (t >= p.t2);
-  const int lt = t - (seg == 0 ? 0 : seg == 1 ? p.t1 : p.t2);
-  const int row0 = lt * RWO;
-  const int g = row0 / kRows, r_in = row0 % kRows;
-  // select by value: indexing the kernel-parameter arrays with a run-time
-  // index would copy them to local memory
-  const uint8_t* base_a = seg == 0 ? p.pan[0] : seg == 1 ? p.pan[1] : p.pan[2];
-  const uint8_t* base_b = kSwi ? p.pan[1] : base_a;
-  const int n_seg = seg == 0 ? p.n[0] : seg == 1 ? p.n[1] : p.n[2];
-  const int ldy_seg = seg == 0 ? p.ldy[0] : seg == 1 ? p.ldy[1] : p.ldy[2];
-  float* y_seg = seg == 0 ? p.y[0] : seg == 1 ? p.y[1] : p.y[2];
-  const int64_t S = p.S;
-  const int64_t gbase = (int64_t)g * S * kPanelBytes;
+  constexpr int R = kSwi ? 2 * kRows : kRows;  // rows computed per panel (gate + up for swiglu)
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = p.S, depth = p.depth;
+  const int nsp = S * kSubPerSlice;  // sub-blocks incl. padding to whole slices
+  const SmemPlan plan(MODE, NB, S, depth);
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.ring);
+  uint4* qa_s = reinterpret_cast<uint4*>(smem + plan.ring + plan.bars);
+  uint4* qb_s = qa_s + NB * nsp;
+  float* d_s = reinterpret_cast<float*>(qb_s + NB * nsp);
+  int* ms_s = reinterpret_cast<int*>(d_s + NB * nsp);
 
-  float acc[RW][NB];
-#pragma unroll
-  for (int i = 0; i < RW; ++i)
-#pragma unroll
-    for (int m = 0; m < NB; ++m) acc[i][m] = 0.0f;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u_begin = (int)((int64_t)blockIdx.x * p.utotal / gridDim.x);
+  const int u_end = (int)((int64_t)(blockIdx.x + 1) * p.utotal / gridDim.x);
+  const int first = u_begin + warp;
+  const int n_units = first < u_end ? (u_end - first + kWarps - 1) / kWarps : 0;
+  const int n_panels = n_units * S;
+  const uint32_t my_bars = smem_u32(bars + warp * depth);
+  const uint32_t my_ring = smem_u32(ring + warp * depth * plan.stage);
 
-  // prefetch registers: codes of the RW rows and the scales, for one slice
-  uint2 cur[RW];
-  uint32_t sca[(RWO + 1) / 2], scb[(RWO + 1) / 2];
-  auto load_slice = [&](int64_t j, uint2 (&c)[RW], uint32_t (&sa)[(RWO + 1) / 2], uint32_t (&sb)[(RWO + 1) / 2]) {
-    const uint8_t* pa = base_a + gbase + j * kPanelBytes;
-    const uint8_t* pb = base_b + gbase + j * kPanelBytes;
-#pragma unroll
-    for (int i = 0; i < RW; ++i) {
-      const uint8_t* pp = (kSwi && i >= RWO) ? pb : pa;
-      const int r = r_in + (kSwi ? (i % RWO) : i);
-      c[i] = ld_stream_v2(pp + code_offset(r, lane));
-    }
-    load_scales<RWO>(pa + scale_offset(r_in, lane >> 2), sa);
-    if constexpr (kSwi) load_scales<RWO>(pb + scale_offset(r_in, lane >> 2), sb);
+  // unit -> (segment, row group)
+  auto locate = [&](int u, int& seg, int& g) {
+    seg = kSwi ? 0 : (u >= p.u1) + (u >= p.u2);
+    g = u - (seg == 0 ? 0 : seg == 1 ? p.u1 : p.u2);
   };
-  load_slice(0, cur, sca, scb);
+  auto issue = [&](int k) {  // lane 0: start the copies of this warp's k-th panel
+    const int ui = k / S, j = k - ui * S;
+    int seg, g;
+    locate(first + ui * kWarps, seg, g);
+    const uint8_t* base = seg == 0 ? p.pan0 : seg == 1 ? p.pan1 : p.pan2;
+    const int64_t off = ((int64_t)g * S + j) * kPanelBytes;
+    const int slot = k % depth;
+    const uint32_t bar = my_bars + slot * 8, dst = my_ring + slot * plan.stage;
+    mbar_expect_tx(bar, plan.stage);
+    bulk_g2s(dst, base + off, kPanelBytes, bar);
+    if (kSwi) bulk_g2s(dst + kPanelBytes, p.pan1 + off, kPanelBytes, bar);
+  };
 
-  for (int64_t j = 0; j < S; ++j) {
-    uint2 nxt[RW];
-    uint32_t nsa[(RWO + 1) / 2], nsb[(RWO + 1) / 2];
-    if (j + 1 < S) load_slice(j + 1, nxt, nsa, nsb);
+  if (lane == 0) {
+    for (int i = 0; i < depth; ++i) mbar_init(my_bars + i * 8, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  pdl_launch_dependents();
+  // weights never depend on the previous kernel: start streaming them now
+  if (lane == 0)
+    for (int k = 0; k < depth && k < n_panels; ++k) issue(k);
+  pdl_wait();
 
-    const int sbk = (int)j * kSubPerSlice + lane;
-    const bool valid = sbk < p.nsub;
-#pragma unroll
-    for (int m = 0; m < NB; ++m) {
-      uint4 qa = make_uint4(0, 0, 0, 0), qb = qa;
-      float dm = 0.0f;
-      int magic_s = kMagicInt;
-      if (valid && m < p.nb) {
-        const int64_t row = p.m0 + m;
-        const int8_t* qp = p.q + row * p.K + (int64_t)sbk * 32;
-        qa = ld_nc_v4(qp);
-        qb = ld_nc_v4(qp + 16);
-        dm = p.d[row * p.nsub + sbk];
-        magic_s = kMagicInt - p.s[row * p.nsub + sbk];
+  // ---- activation -> shared memory (padded to whole slices with q = 0)
+  if constexpr (FUSE) {
+    for (int b = warp; b < NB * nsp; b += kWarps) {
+      const int m = b / nsp, sb = b - m * nsp;
+      int qv = 0, sum = 0;
+      float dq = 0.0f;
+      if (m < p.nb && sb < p.nsub) {
+        const float v = p.x[(int64_t)(p.m0 + m) * p.ldx + sb * 32 + lane];
+        qv = q8_warp(v, dq, sum);
       }
-#pragma unroll
-      for (int i = 0; i < RW; ++i) {
-        const float sc = (kSwi && i >= RWO) ? scale_of<RWO>(scb, i - RWO) : scale_of<RWO>(sca, i);
-        const int biased = sub_dot_biased(cur[i].x, cur[i].y, qa, qb, magic_s);
-        const float fi = __int_as_float(biased) - kMagicFloat;
-        acc[i][m] = fmaf(sc * dm, fi, acc[i][m]);
+      // lanes 0..15 -> qa bytes, 16..31 -> qb bytes
+      uint8_t* dstq = reinterpret_cast<uint8_t*>(lane < 16 ? qa_s : qb_s) + ((int64_t)m * nsp + sb) * 16 + (lane & 15);
+      *dstq = (uint8_t)(int8_t)qv;
+      if (lane == 0) {
+        d_s[m * nsp + sb] = dq;
+        ms_s[m * nsp + sb] = kMagicInt - sum;
       }
     }
-    if (j + 1 < S) {
-#pragma unroll
-      for (int i = 0; i < RW; ++i) cur[i] = nxt[i];
-#pragma unroll
-      for (int i = 0; i < (RWO + 1) / 2; ++i) {
-        sca[i] = nsa[i];
-        scb[i] = nsb[i];
+  } else {
+    for (int i = threadIdx.x; i < NB * nsp; i += kThreads) {
+      const int m = i / nsp, sb = i - m * nsp;
+      uint4 a = make_uint4(0, 0, 0, 0), b = a;
+      float dv = 0.0f;
+      int sv = 0;
+      if (m < p.nb && sb < p.nsub) {
+        const int64_t row = p.m0 + m;
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + row * p.K + (int64_t)sb * 32);
+        a = src[0];
+        b = src[1];
+        dv = p.d[row * p.nsub + sb];
+        sv = p.s[row * p.nsub + sb];
       }
+      qa_s[i] = a;
+      qb_s[i] = b;
+      d_s[i] = dv;
+      ms_s[i] = kMagicInt - sv;
     }
   }
+  __syncthreads();
 
-  // reduce over the 32 lanes; lane i then owns output row row0 + i
+  float acc[R][NB];
 #pragma unroll
-  for (int m = 0; m < NB; ++m) {
-    float mine = 0.0f, mine_up = 0.0f;
+  for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int i = 0; i < RW; ++i) {
-      const float v = warp_sum(acc[i][m]);
-      if (kSwi && i >= RWO) {
-        if (lane == i - RWO) mine_up = v;
-      } else if (lane == i) {
-        mine = v;
+    for (int m = 0; m < NB; ++m) acc[r][m] = 0.0f;
+
+  for (int k = 0; k < n_panels; ++k) {
+    const int slot = k % depth;
+    const uint32_t bar = my_bars + slot * 8;
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, (uint32_t)((k / depth) & 1), kWaitLimitNs));
+    if (!ok) {
+      // report, let copies already in flight land (bounded), and leave
+      if (lane == 0) {
+        atomicCAS(p.err, 0, kErrWaitTimeout);
+        for (int kk = k + 1; kk < n_panels && kk < k + depth; ++kk)
+          mbar_wait_bounded(my_bars + (kk % depth) * 8, (uint32_t)((kk / depth) & 1), kWaitLimitNs / 10);
+      }
+      __syncwarp();
+      return;
+    }
+    const int j = k % S;
+    const uint8_t* stage = ring + (warp * depth + slot) * plan.stage;
+    // scales of this lane's block (lane / 4) for the 8 rows, fp16
+    uint4 sc[kSwi ? 2 : 1];
+    sc[0] = *reinterpret_cast<const uint4*>(stage + kCodeBytes + (lane >> 2) * 16);
+    if constexpr (kSwi) sc[1] = *reinterpret_cast<const uint4*>(stage + kPanelBytes + kCodeBytes + (lane >> 2) * 16);
+    uint2 w[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      w[r] = *reinterpret_cast<const uint2*>(stage + (r / kRows) * kPanelBytes + code_offset(r % kRows, lane));
+#pragma unroll
+    for (int m = 0; m < NB; ++m) {
+      const int ai = m * nsp + j * kSubPerSlice + lane;
+      const uint4 qa = qa_s[ai], qb = qb_s[ai];
+      const float dm = d_s[ai];
+      const int ms = ms_s[ai];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint4 s4 = sc[r / kRows];
+        const int rr = r % kRows;
+        const uint32_t h2 = rr < 2 ? s4.x : rr < 4 ? s4.y : rr < 6 ? s4.z : s4.w;
+        const float scale = (rr & 1) ? half_hi(h2) : half_lo(h2);
+        const int biased = sub_dot_biased(w[r].x, w[r].y, qa, qb, ms);
+        acc[r][m] = fmaf(scale * dm, __int_as_float(biased) - kMagicFloat, acc[r][m]);
       }
     }
-    const int row = row0 + lane;
-    if (lane < RWO && row < n_seg && m < p.nb) {
-      float* yp = y_seg + (int64_t)(p.m0 + m) * ldy_seg + row;
-      if constexpr (MODE == BTF_STORE) *yp = mine;
-      else if constexpr (MODE == BTF_ADD) *yp += mine;
-      else *yp = silu(mine) * mine_up;
+    __syncwarp();
+    if (lane == 0 && k + depth < n_panels) {
+      fence_proxy_async_smem();  // our generic-proxy reads of the slot precede the next async write
+      issue(k + depth);
+    }
+    if (j == S - 1) {  // unit done: reduce over lanes, lane i stores row i
+      int seg, g;
+      locate(first + (k / S) * kWarps, seg, g);
+      const int n = seg == 0 ? p.n0 : seg == 1 ? p.n1 : p.n2;
+      const int ldy = seg == 0 ? p.ld0 : seg == 1 ? p.ld1 : p.ld2;
+      float* y = seg == 0 ? p.y0 : seg == 1 ? p.y1 : p.y2;
+#pragma unroll
+      for (int m = 0; m < NB; ++m) {
+        float mine = 0.0f, mine_up = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float v = warp_sum(acc[r][m]);
+          if (r < kRows) {
+            if (lane == r) mine = v;
+          } else if (lane == r - kRows) {
+            mine_up = v;
+          }
+          acc[r][m] = 0.0f;
+        }
+        const int row = g * kRows + lane;
+        if (lane < kRows && row < n && m < p.nb) {
+          float* yp = y + (int64_t)(p.m0 + m) * ldy + row;
+          if constexpr (MODE == BTF_STORE) *yp = mine;
+          else if constexpr (MODE == BTF_ADD) *yp += mine;
+          else *yp = silu(mine) * mine_up;
+        }
+      }
     }
   }
 }
@@ -221,26 +295,139 @@ __global__ void __launch_bounds__(256)
 
 using KernelFn = void (*)(const GemvParams);
 
-template <int MODE>
+template <int MODE, bool FUSE>
 KernelFn pick(int NB) {
   switch (NB) {
-    case 1: return gemv_kernel<1, 8, MODE>;
-    case 2: return gemv_kernel<2, 8, MODE>;
-    case 4: return gemv_kernel<4, 4, MODE>;
-    default: return gemv_kernel<8, 4, MODE>;
+    case 1: return gemv_kernel<1, MODE, FUSE>;
+    case 2: return gemv_kernel<2, MODE, FUSE>;
+    default: return gemv_kernel<4, MODE, FUSE>;
   }
 }
-// Output rows per warp tile for a given (NB, mode); must match pick().
-int rows_per_tile(int NB, int mode) {
-  const int rw = NB <= 2 ? 8 : 4;
-  return mode == BTF_SWIGLU ? rw / 2 : rw;
+KernelFn pick(int NB, int mode, bool fuse) {
+  if (fuse) return mode == BTF_STORE ? pick<BTF_STORE, true>(NB) : mode == BTF_ADD ? pick<BTF_ADD, true>(NB) : pick<BTF_SWIGLU, true>(NB);
+  return mode == BTF_STORE ? pick<BTF_STORE, false>(NB) : mode == BTF_ADD ? pick<BTF_ADD, false>(NB) : pick<BTF_SWIGLU, false>(NB);
 }
 
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
 
+int check_segs(const char* fn, const btf_gemv_seg* segs, int nseg, int K, int mode) {
+  if (!segs || nseg < 1 || nseg > kMaxSeg) return fail(BTF_ERR_ARG, "%s: 1..3 segments (got %d)", fn, nseg);
+  if (mode != BTF_STORE && mode != BTF_ADD && mode != BTF_SWIGLU) return fail(BTF_ERR_ARG, "%s: bad mode %d", fn, mode);
+  if (mode == BTF_SWIGLU && (nseg != 2 || segs[0].N != segs[1].N))
+    return fail(BTF_ERR_ARG, "%s: swiglu needs gate+up segments with the same N", fn);
+  if (K <= 0 || K % 128) return fail(BTF_ERR_ARG, "%s: K must be a positive multiple of 128 (K=%d)", fn, K);
+  for (int i = 0; i < nseg; ++i) {
+    if (!segs[i].panels || !aligned(segs[i].panels, 16) || segs[i].N <= 0)
+      return fail(BTF_ERR_ARG, "%s: segment %d has a null/misaligned panel buffer or N <= 0", fn, i);
+    const bool needs_y = !(mode == BTF_SWIGLU && i == 1);
+    if (needs_y && (!segs[i].y || segs[i].ldy < segs[i].N))
+      return fail(BTF_ERR_ARG, "%s: segment %d needs y and ldy >= N", fn, i);
+  }
+  return BTF_OK;
+}
+
+// CTAs of `fn` that fit on one SM with `smem` bytes of dynamic shared memory
+// (registers and shared memory), cached: the grid is persistent, so it must
+// not exceed what is co-resident.
+int resident_ctas(KernelFn fn, int smem) {
+  struct Entry { KernelFn fn; int smem; int n; };
+  static Entry cache[64];
+  static int used = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].smem == smem) return cache[i].n;
+  int n = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) != cudaSuccess || n < 1) n = 1;
+  n = std::min(n, 2);
+  if (used < 64) cache[used++] = Entry{fn, smem, n};
+  return n;
+}
+
+// Launches the GEMV over M rows in passes of at most kMaxNb activation rows.
+int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* act, const float* x, int ldx,
+             int mode, cudaStream_t st) {
+  const DeviceInfo* dev = current_device();
+  if (!dev) return BTF_ERR_STATE;
+  GemvParams p{};
+  const uint8_t* pans[kMaxSeg] = {nullptr, nullptr, nullptr};
+  float* ys[kMaxSeg] = {nullptr, nullptr, nullptr};
+  int ns[kMaxSeg] = {0, 0, 0}, lds[kMaxSeg] = {0, 0, 0}, units[kMaxSeg] = {0, 0, 0};
+  for (int i = 0; i < nseg; ++i) {
+    pans[i] = static_cast<const uint8_t*>(segs[i].panels);
+    ys[i] = segs[i].y;
+    ns[i] = segs[i].N;
+    lds[i] = segs[i].ldy;
+    units[i] = (int)groups_of(segs[i].N);
+  }
+  if (mode == BTF_SWIGLU) units[1] = 0;  // a swiglu unit covers the gate and up groups together
+  p.pan0 = pans[0]; p.pan1 = pans[1]; p.pan2 = pans[2];
+  p.y0 = ys[0]; p.y1 = ys[1]; p.y2 = ys[2];
+  p.n0 = ns[0]; p.n1 = ns[1]; p.n2 = ns[2];
+  p.ld0 = lds[0]; p.ld1 = lds[1]; p.ld2 = lds[2];
+  p.u1 = units[0];
+  p.u2 = units[0] + units[1];
+  p.utotal = units[0] + units[1] + units[2];
+  p.K = K;
+  p.S = (int)slices_of(K);
+  p.nsub = K / 32;
+  if (act) {
+    p.q = act->q;
+    p.d = act->d;
+    p.s = act->s;
+  }
+  p.x = x;
+  p.ldx = ldx;
+  p.err = dev->err_word;
+  for (int m0 = 0; m0 < M; m0 += kMaxNb) {
+    const int nb = std::min(kMaxNb, M - m0);
+    const int NB = nb <= 1 ? 1 : nb <= 2 ? 2 : 4;
+    // ring depth: fill ~kSmemTarget, at least 2 slots
+    const SmemPlan base(mode, NB, p.S, 0);
+    const int per_slot = kWarps * (base.stage + 8);
+    int depth = (int)((kSmemTarget - (size_t)base.act) / per_slot);
+    depth = std::max(2, std::min(depth, 6));
+    const SmemPlan plan(mode, NB, p.S, depth);
+    if (plan.total > dev->optin_smem)
+      return fail(BTF_ERR_UNSUPPORTED, "btf_gemv: K=%d with %d activation rows needs %d B of shared memory (max %d)",
+                  K, NB, plan.total, dev->optin_smem);
+    p.depth = depth;
+    p.m0 = m0;
+    p.nb = nb;
+    const KernelFn fn = pick(NB, mode, x != nullptr);
+    const int per_sm = resident_ctas(fn, plan.total);
+    const int grid = std::max(1, std::min(p.utotal, dev->sm_count * per_sm));
+    const cudaError_t e = launch_pdl(fn, dim3(grid), dim3(kThreads), (size_t)plan.total, st, p);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv_kernel launch");
+    if (int rc = launch_status("gemv_kernel")) return rc;
+  }
+  return BTF_OK;
+}
+
+template <int MODE, bool FUSE>
+cudaError_t set_attrs(int smem) {
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(gemv_kernel<1, MODE, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+  if ((e = cudaFuncSetAttribute(gemv_kernel<2, MODE, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
+  return cudaFuncSetAttribute(gemv_kernel<4, MODE, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 }  // namespace
 
-int gemv_setup(const DeviceInfo&) { return BTF_OK; }
+// One error word per device (module-scope device variable, no allocation).
+__device__ int g_device_error;
+
+int gemv_setup(DeviceInfo& d) {
+  cudaError_t e;
+  void* ew = nullptr;
+  if ((e = cudaGetSymbolAddress(&ew, g_device_error)) != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+  d.err_word = static_cast<int*>(ew);
+  if ((e = set_attrs<BTF_STORE, false>(d.optin_smem)) || (e = set_attrs<BTF_ADD, false>(d.optin_smem)) ||
+      (e = set_attrs<BTF_SWIGLU, false>(d.optin_smem)) || (e = set_attrs<BTF_STORE, true>(d.optin_smem)) ||
+      (e = set_attrs<BTF_ADD, true>(d.optin_smem)) || (e = set_attrs<BTF_SWIGLU, true>(d.optin_smem)))
+    return cuda_fail(e, "cudaFuncSetAttribute(gemv_kernel)");
+  return BTF_OK;
+}
 
 }  // namespace btf
 
@@ -248,60 +435,35 @@ using namespace btf;
 
 extern "C" {
 
-int btf_gemv_max_nb(int K) { return (K > 0 && K % 128 == 0) ? 8 : 0; }
+int btf_gemv_max_nb(int K) { return (K > 0 && K % 128 == 0) ? kMaxNb : 0; }
 
 int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream) {
   if (M <= 0) return BTF_OK;
-  if (!segs || nseg < 1 || nseg > kMaxSeg) return fail(BTF_ERR_ARG, "btf_gemv: 1..3 segments (got %d)", nseg);
-  if (mode != BTF_STORE && mode != BTF_ADD && mode != BTF_SWIGLU) return fail(BTF_ERR_ARG, "btf_gemv: bad mode %d", mode);
-  if (mode == BTF_SWIGLU && (nseg != 2 || segs[0].N != segs[1].N))
-    return fail(BTF_ERR_ARG, "btf_gemv: swiglu needs gate+up segments with the same N");
-  if (K <= 0 || K % 128) return fail(BTF_ERR_ARG, "btf_gemv: K must be a positive multiple of 128 (K=%d)", K);
+  if (int rc = check_segs("btf_gemv", segs, nseg, K, mode)) return rc;
   if (!act.q || !act.d || !act.s || !aligned(act.q, 16) || !aligned(act.d, 4) || !aligned(act.s, 4))
     return fail(BTF_ERR_ARG, "btf_gemv: activation pointers null or misaligned (q needs 16 B)");
-  for (int i = 0; i < nseg; ++i) {
-    if (!segs[i].panels || !aligned(segs[i].panels, 16) || segs[i].N <= 0)
-      return fail(BTF_ERR_ARG, "btf_gemv: segment %d has a null/misaligned panel buffer or N <= 0", i);
-    const bool needs_y = !(mode == BTF_SWIGLU && i == 1);
-    if (needs_y && (!segs[i].y || segs[i].ldy < segs[i].N))
-      return fail(BTF_ERR_ARG, "btf_gemv: segment %d needs y and ldy >= N", i);
-  }
-  const DeviceInfo* dev = current_device();
-  if (!dev) return BTF_ERR_STATE;
+  return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream);
+}
 
-  GemvParams p{};
-  for (int i = 0; i < nseg; ++i) {
-    p.pan[i] = static_cast<const uint8_t*>(segs[i].panels);
-    p.y[i] = segs[i].y;
-    p.n[i] = segs[i].N;
-    p.ldy[i] = segs[i].ldy;
+int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* x, int ldx, int mode, void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (int rc = check_segs("btf_gemv_f32", segs, nseg, K, mode)) return rc;
+  if (!x || ldx < K || !aligned(x, 4)) return fail(BTF_ERR_ARG, "btf_gemv_f32: x null/misaligned or ldx < K");
+  return run_gemv(segs, nseg, K, M, nullptr, x, ldx, mode, (cudaStream_t)stream);
+}
+
+int btf_device_error(int clear) {
+  const DeviceInfo* dev = current_device();
+  if (!dev) return -1;
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, dev->err_word, sizeof v, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_device_error"), -1;
+  if (clear && v) {
+    const int z = 0;
+    if ((e = cudaMemcpy(dev->err_word, &z, sizeof z, cudaMemcpyHostToDevice)) != cudaSuccess)
+      return cuda_fail(e, "btf_device_error"), -1;
   }
-  p.K = K;
-  p.S = (int)slices_of(K);
-  p.nsub = K / 32;
-  p.q = act.q;
-  p.d = act.d;
-  p.s = act.s;
-  const cudaStream_t st = (cudaStream_t)stream;
-  constexpr int kMaxNb = 8;
-  for (int m0 = 0; m0 < M; m0 += kMaxNb) {
-    const int nb = std::min(kMaxNb, M - m0);
-    const int NB = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8;
-    const int rwo = rows_per_tile(NB, mode);
-    int tiles[kMaxSeg] = {0, 0, 0};
-    const int used = mode == BTF_SWIGLU ? 1 : nseg;
-    for (int i = 0; i < used; ++i) tiles[i] = (segs[i].N + rwo - 1) / rwo;
-    p.t1 = tiles[0];
-    p.t2 = tiles[0] + tiles[1];
-    p.ttotal = tiles[0] + tiles[1] + tiles[2];
-    p.m0 = m0;
-    p.nb = nb;
-    const KernelFn fn = mode == BTF_STORE ? pick<BTF_STORE>(NB) : mode == BTF_ADD ? pick<BTF_ADD>(NB) : pick<BTF_SWIGLU>(NB);
-    const int grid = (p.ttotal + kWarps - 1) / kWarps;
-    fn<<<grid, kThreads, 0, st>>>(p);
-    if (int rc = launch_status("gemv_kernel")) return rc;
-  }
-  return BTF_OK;
+  return v;
 }
 
 int btf_gemv_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream) {

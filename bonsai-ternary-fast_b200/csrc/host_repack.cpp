@@ -40,7 +40,7 @@ void repack_groups(const uint8_t* src, int64_t N, int64_t K, uint8_t* panels, in
         }
         uint8_t* pan = panels + (g * S + b / 8) * kPanelH;
         std::memcpy(pan + r * 256 + (b % 8) * 32, w, 32);
-        std::memcpy(pan + 4096 + (b % 8) * 32 + r * 2, &scale, 2);
+        std::memcpy(pan + 2048 + (b % 8) * 16 + r * 2, &scale, 2);
       }
     }
 }

@@ -27,7 +27,7 @@ __device__ __forceinline__ void load_block(const uint8_t* src, int64_t blk, Src7
   scale = (uint16_t)(s.v[6] >> 16);
 }
 
-// Grid covers the padded domain: G*16 rows x S*8 blocks; out-of-range blocks
+// Grid covers the padded domain: G*8 rows x S*8 blocks; out-of-range blocks
 // are written as padding (code 1 everywhere, scale 0).
 __global__ void __launch_bounds__(kThreads)
     repack_panels_kernel(const uint8_t* __restrict__ src, int64_t N, int64_t K, uint8_t* __restrict__ panels) {

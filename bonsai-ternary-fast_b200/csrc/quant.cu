@@ -19,22 +19,14 @@ __global__ void __launch_bounds__(kQThreads)
   const int nsub = K / 32;
   const int sb = blockIdx.x * kQWarps + warp;
   const int m = blockIdx.y;
+  pdl_launch_dependents();
+  pdl_wait();
   if (sb >= nsub) return;
   const float v = x[(size_t)m * ldx + sb * 32 + lane];
-  float amax = fabsf(v);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  // The host rule updates amax with (amax > a ? amax : a) from +0, so a block
-  // of zeros ends with the last element's zero, sign included.
-  const float last = __shfl_sync(0xffffffffu, v, 31);
-  const float amax_signed = amax == 0.0f ? last : amax;
-  const float dq = __half2float(__float2half_rn(__fdiv_rn(amax_signed, 127.0f)));
-  const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-  const int qv = __float2int_rn(__fmul_rn(v, id));
+  float dq;
+  int sum;
+  const int qv = q8_warp(v, dq, sum);
   q[(size_t)m * K + sb * 32 + lane] = (int8_t)qv;
-  int sum = qv;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) {
     d[(size_t)m * nsub + sb] = dq;
     s[(size_t)m * nsub + sb] = sum;
@@ -54,6 +46,7 @@ extern "C" int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act
   if (!current_device()) return BTF_ERR_STATE;
   const dim3 grid((K / 32 + kQWarps - 1) / kQWarps, M);
   if (grid.y > 65535) return fail(BTF_ERR_ARG, "btf_quant_q8: M=%d exceeds 65535", M);
-  quant_q8_kernel<<<grid, kQThreads, 0, (cudaStream_t)stream>>>(x, ldx, K, act.q, act.d, act.s);
-  return launch_status("quant_q8_kernel");
+  const cudaError_t e = launch_pdl(quant_q8_kernel, grid, dim3(kQThreads), 0, (cudaStream_t)stream, x, ldx, K,
+                                   act.q, act.d, act.s);
+  return e == cudaSuccess ? launch_status("quant_q8_kernel") : cuda_fail(e, "quant_q8_kernel launch");
 }

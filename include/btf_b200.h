@@ -12,13 +12,15 @@
  *     btf_last_error() gives a one-line message for the calling thread.
  *
  * Resident weight layout ("panels", replaces T2 of include/btf/packed.hpp:6-14):
- *   a [N][K] ternary matrix is cut into row groups of 16 rows and column
+ *   a [N][K] ternary matrix is cut into row groups of 8 rows and column
  *   slices of 1024 columns (32 sub-blocks of 32 = 8 PTQ1_0 blocks of 128).
- *   Panel (g, j) is 4352 contiguous bytes at ((g * S) + j) * 4352, S = ceil(K/1024):
- *     bytes [0, 4096):    codes of row r (0..15), sub-block l (0..31) at r*256 + l*8,
+ *   Panel (g, j) is 2176 contiguous bytes at ((g * S) + j) * 2176, S = ceil(K/1024):
+ *     bytes [0, 2048):    codes of row r (0..7), sub-block l (0..31) at r*256 + l*8,
  *                         two little-endian T2 words (2-bit code = trit + 1; word w
  *                         holds column 32l + 16w + 4k + j at bit 8j + 2k);
- *     bytes [4096, 4352): fp16 block scales, block b (0..7) of row r at 4096 + b*32 + r*2.
+ *     bytes [2048, 2176): fp16 block scales, block b (0..7) of row r at 2048 + b*16 + r*2.
+ *   A row group's S panels are contiguous, so one 1-D bulk copy per panel streams
+ *   8 rows x 1024 columns with their scales.
  *   Rows >= N and columns >= K are padding (code 1 = trit 0, scale 0).
  *   Total size: btf_panel_bytes(N, K).
  */
@@ -46,9 +48,9 @@ extern "C" {
 #define BTF_SWIGLU 2 /* y  = silu(W_gate x) * (W_up x); segs[0] = gate, segs[1] = up */
 
 /* Layout constants. */
-#define BTF_PANEL_ROWS 16
+#define BTF_PANEL_ROWS 8
 #define BTF_PANEL_COLS 1024
-#define BTF_PANEL_BYTES 4352
+#define BTF_PANEL_BYTES 2176
 
 /* One matrix of a multi-segment GEMV. Mirrors GemvSeg (src/cuda/kernels.cuh:46-52)
  * with the T2 codes/scales pair replaced by one panel buffer. */
@@ -117,6 +119,16 @@ int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act, void* str
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
  * segments (gate, up) with the same N. K % 128 == 0. */
 int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
+
+/* Fused form: the activation is given as fp32 x [M][ldx] and quantised to Q8_0
+ * inside the GEMV (same bit-exact rule as btf_quant_q8), saving the separate
+ * quantiser launch of launch_prep + launch_gemv. */
+int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* x, int ldx, int mode, void* stream);
+
+/* Device error word of the current device: nonzero after a bounded device-side
+ * wait gave up (the kernel then returned early instead of hanging). Synchronous;
+ * not for use inside stream capture. clear != 0 resets it. Returns -1 on failure. */
+int btf_device_error(int clear);
 
 /* Debug/parity entry point: the exact int32 trit dot of every (m, row,
  * sub-block), idot[M][N][K/32] = code_dot - sum(q) — the integers the GEMV

@@ -248,8 +248,8 @@ def panel_decode(panels: np.ndarray, N: int, K: int):
     Written from the layout description, not from the library, so a test that
     compares it with the reference T2 checks the library's layout end to end."""
     S = (K + 1023) // 1024
-    G = (N + 15) // 16
-    p = np.asarray(panels, dtype=np.uint8).reshape(G, S, 4352)
-    codes = p[:, :, :4096].reshape(G, S, 16, 256).transpose(0, 2, 1, 3).reshape(G * 16, S * 256)
-    sc = p[:, :, 4096:].copy().view(np.uint16).reshape(G, S, 8, 16).transpose(0, 3, 1, 2).reshape(G * 16, S * 8)
+    G = (N + 7) // 8
+    p = np.asarray(panels, dtype=np.uint8).reshape(G, S, 2176)
+    codes = p[:, :, :2048].reshape(G, S, 8, 256).transpose(0, 2, 1, 3).reshape(G * 8, S * 256)
+    sc = p[:, :, 2048:].copy().view(np.uint16).reshape(G, S, 8, 8).transpose(0, 3, 1, 2).reshape(G * 8, S * 8)
     return np.ascontiguousarray(codes[:N, :K // 4]), np.ascontiguousarray(sc[:N, :K // 128])

@@ -126,10 +126,36 @@ def test_config1_shapes_quantised_end_to_end(cuda, btf, orc, name, K, N):
         assert rel_rms(g, y64) <= TOL, name
     # integer partials of the first rows are exact
     rows = slice(0, 48)
-    small = Mat.__new__(Mat)
-    small.N, small.K = 48, K
     idot_gpu = btf.gemv_idot(mat.pm, 1, act).cpu().numpy()[:, rows]
     assert np.array_equal(idot_gpu, orc.idot(mat.codes[rows], K, q, s))
+
+
+@pytest.mark.parametrize("K,M,mode", [(5120, 1, 0), (6144, 2, 1), (17408, 1, 0), (1152, 3, 2), (5120, 4, 2),
+                                      (2048, 9, 1)])
+def test_fused_quantise_gemv_equals_two_step(cuda, btf, orc, K, M, mode):
+    # btf_gemv_f32 quantises inside the GEMV with the same bit-exact rule:
+    # its output must equal quantiser + GEMV bit for bit, and match the oracle
+    import torch
+
+    x = _dev(synth.activations(M, K, seed=K + M), cuda)
+    a = Mat(btf, orc, 45, K, seed=K, device=cuda)
+    b = Mat(btf, orc, 45, K, seed=K + 1, device=cuda)
+    segs2 = [(a.pm, None, 0), (b.pm, None, 0)]
+    y1 = torch.randn((M, 45), device=cuda)
+    y2 = y1.clone()
+    if mode == btf.SWIGLU:
+        segs_a, segs_b = [(a.pm, y1, 45), segs2[1]], [(a.pm, y2, 45), segs2[1]]
+    else:
+        segs_a, segs_b = [(a.pm, y1, 45)], [(a.pm, y2, 45)]
+    act = btf.quant_q8(x)
+    btf.launch_gemv(segs_a, K, M, act, mode)
+    btf.launch_gemv_f32(segs_b, K, M, x, mode)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    q, d, s = orc.q8_rows(x.cpu().numpy())
+    if mode == btf.STORE:
+        assert rel_rms(y2.cpu().numpy(), orc.gemv(a.codes, a.scales, K, q, d, s)) <= TOL
+    assert btf.device_error() == 0
 
 
 def test_gemv_in_cuda_graph_matches_eager(cuda, btf, orc):

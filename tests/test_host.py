@@ -29,11 +29,11 @@ def test_library_exports_every_declared_symbol(btf):
 
 def test_layout_sizes(btf):
     assert btf.panel_bytes(17408, 5120) == 17408 * 5120 // 4 + 17408 * 40 * 2  # no padding at the config-0 shape
-    assert btf.panel_bytes(37, 1024) == 3 * 1 * 4352
-    assert btf.panel_bytes(16, 1152) == 1 * 2 * 4352
+    assert btf.panel_bytes(37, 1024) == 5 * 1 * 2176
+    assert btf.panel_bytes(16, 1152) == 2 * 2 * 2176
     assert btf.t2_codes_bytes(37, 1024) == 37 * 256
     assert btf.t2_scales_bytes(37, 1024) == 37 * 8 * 2
-    assert btf.gemv_max_nb(5120) == 8 and btf.gemv_max_nb(100) == 0
+    assert btf.gemv_max_nb(5120) == 4 and btf.gemv_max_nb(100) == 0
 
 
 @pytest.mark.parametrize("N,K", [(37, 1024), (41, 1152), (16, 128), (1, 5120), (33, 3072)])
@@ -48,10 +48,10 @@ def test_host_repack_matches_reference_t2(btf, orc, N, K):
     c_ref, s_ref = orc.repack_t2(src, N, K)
     assert np.array_equal(codes, c_ref) and np.array_equal(scales, s_ref)
     # padding: rows >= N and columns >= K hold code 1 (trit 0) and scale 0
-    G, S = (N + 15) // 16, (K + 1023) // 1024
-    p = pan.reshape(G, S, 4352)
-    full_c = p[:, :, :4096].reshape(G, S, 16, 256).transpose(0, 2, 1, 3).reshape(G * 16, S * 256)
-    full_s = p[:, :, 4096:].copy().view(np.uint16).reshape(G, S, 8, 16).transpose(0, 3, 1, 2).reshape(G * 16, S * 8)
+    G, S = (N + 7) // 8, (K + 1023) // 1024
+    p = pan.reshape(G, S, 2176)
+    full_c = p[:, :, :2048].reshape(G, S, 8, 256).transpose(0, 2, 1, 3).reshape(G * 8, S * 256)
+    full_s = p[:, :, 2048:].copy().view(np.uint16).reshape(G, S, 8, 8).transpose(0, 3, 1, 2).reshape(G * 8, S * 8)
     assert np.all(full_c[N:] == 0x55) and np.all(full_c[:, K // 4:] == 0x55)
     assert np.all(full_s[N:] == 0) and np.all(full_s[:, K // 128:] == 0)
 

@@ -31,15 +31,27 @@ def test_repack_panels_device_matches_host_twin(cuda, btf, orc, N, K):
 
 
 def test_repack_from_mapped_host_memory(cuda, btf):
+    # the reference's test_repack reads the PTQ1_0 source from mapped host
+    # memory (cudaHostAlloc(cudaHostAllocMapped) + cudaHostGetDevicePointer,
+    # tests/test_gpu_kernels.cpp:78-83); do the same through the runtime
+    import ctypes
+
     import torch
 
+    rt = ctypes.CDLL("libcudart.so.12")
     N, K = 41, 1024
     src = synth.ternary_ptq(N, K, seed=3)
-    pinned = torch.from_numpy(src).pin_memory()  # page-locked: the device reads it over the bus
-    out = torch.empty(btf.panel_bytes(N, K), dtype=torch.uint8, device=cuda)
-    btf.check(btf.lib().btf_repack_panels(pinned.data_ptr(), N, K, out.data_ptr(), None), "repack")
-    torch.cuda.synchronize()
-    assert np.array_equal(out.cpu().numpy(), btf.repack_panels_host(src, N, K))
+    hptr, dptr = ctypes.c_void_p(), ctypes.c_void_p()
+    assert rt.cudaHostAlloc(ctypes.byref(hptr), ctypes.c_size_t(src.nbytes), ctypes.c_uint(2)) == 0  # Mapped
+    try:
+        ctypes.memmove(hptr, src.ctypes.data, src.nbytes)
+        assert rt.cudaHostGetDevicePointer(ctypes.byref(dptr), hptr, ctypes.c_uint(0)) == 0
+        out = torch.empty(btf.panel_bytes(N, K), dtype=torch.uint8, device=cuda)
+        btf.check(btf.lib().btf_repack_panels(dptr.value, N, K, out.data_ptr(), None), "repack")
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), btf.repack_panels_host(src, N, K))
+    finally:
+        rt.cudaFreeHost(hptr)
 
 
 def test_repack_t2_and_roundtrip(cuda, btf, orc):
@@ -69,7 +81,7 @@ def test_quant_q8_bit_exact(cuda, btf, orc, M, K):
         x[-1, 128:160] = -0.0
         x[-1, 192:224] = 0.0
         x[-1, 223] = -0.0
-        x[0, 160:192] = 1e-38  # subnormal-range amax
+        x[0, 160:192] = 1e-30  # tiny amax (127/amax still finite)
     act = btf.quant_q8(_dev(x, cuda))
     q, d, s = orc.q8_rows(x)
     assert np.array_equal(act.q.cpu().numpy(), q)
