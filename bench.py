@@ -266,9 +266,9 @@ def gpu_arm(args):
         t1("down")
         gather("down")
 
-    def step(fused=True):
+    def step(fused=False):
         for i, L in enumerate(model.layers):
-            layer(L, timed=(i == len(model.layers) - 1) and fused, fused=fused)
+            layer(L, timed=(i == len(model.layers) - 1) and not fused, fused=fused)
 
     # e2e variant: inputs from pinned host memory in, outputs back, every step
     h_in = {k: v.cpu().pin_memory() for k, v in x_in.items()}
@@ -288,7 +288,7 @@ def gpu_arm(args):
     with torch.cuda.stream(stream):
         for _ in range(2):
             step()
-            step(fused=False)
+            step(fused=True)
             step_e2e()
     torch.cuda.synchronize()
     g_dev, g_e2e, g_unf = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
@@ -297,7 +297,7 @@ def gpu_arm(args):
     with torch.cuda.graph(g_e2e, stream=stream):
         step_e2e()
     with torch.cuda.graph(g_unf, stream=stream):
-        step(fused=False)
+        step(fused=True)
     torch.cuda.synchronize()
 
     def timed(graph, K, W):
@@ -342,7 +342,8 @@ def gpu_arm(args):
         "gateup": 2 * synth.gemv_bytes(sh["gate"][1], 5120) - 5120 * 5 // 4 - sh["gate"][1] * 4,
         "down": synth.gemv_bytes(sh["down"][1], sh["down"][0], add=True),
     }
-    # fused quantisation reads x (fp32) instead of the Q8 copy: +2.75 B per input element
+    # path-independent bytes: x is read as fp32 (4 B/element) instead of the
+    # Q8 copy (1.25 B/element) the two-kernel path hands between its kernels
     per_layer["qkv"] += 5120 * 11 // 4
     per_layer["o"] += 6144 * 11 // 4
     per_layer["gateup"] += 5120 * 11 // 4
@@ -351,7 +352,7 @@ def gpu_arm(args):
     step_bytes = layer_bytes * N_LAYERS
     value = step_bytes * args.steps / (ms_dev * 1e-3) / 1e9
     e2e = step_bytes * args.steps / (ms_e2e * 1e-3) / 1e9
-    unfused = step_bytes * args.steps / (ms_unf * 1e-3) / 1e9
+    fused_v = step_bytes * args.steps / (ms_unf * 1e-3) / 1e9
 
     peak, peak_kind = measured_peaks()
     # dominant kernel: the gate/up swiglu GEMV (52 % of the step's bytes); on this rank's shard
@@ -378,16 +379,16 @@ def gpu_arm(args):
                        "l2": "inputs larger than L2: 5.8 GB of distinct resident weights per step",
                        "parallelism": f"N-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
                        "graph": "one CUDA graph per step, programmatic dependent launch between kernels",
-                       "quantisation": "fused into each GEMV (btf_gemv_f32)"},
+                       "path": "drop-in pairs: btf_quant_q8 (launch_prep) + btf_gemv (launch_gemv), PDL-chained"},
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
-                         "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,SWIGLU,fused> gate+up",
+                         "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,SWIGLU> gate+up",
                          "peak_source": peak_kind},
             "kernels": kernels,
-            "unfused_drop_in_path": {"value": unfused, "unit": UNIT, "note": "launch_prep + launch_gemv pairs, "
-                                     "8 launches per layer (same bytes counted)"},
+            "fused_quantise_path": {"value": fused_v, "unit": UNIT, "note": "btf_gemv_f32: quantisation inside "
+                                    "each GEMV, 4 launches per layer (same bytes counted)"},
             "device_error_word": dev_err,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * N_LAYERS * 4,
+            "gpu_launches": args.steps * N_LAYERS * 8,
             "clocks": clocks.report(),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -399,6 +400,44 @@ def gpu_arm(args):
         dist.destroy_process_group()
 
 
+def only_kernel(args):
+    """Runs ONE config-1 GEMV kind (no graph) `--iters` times over 4 rotating weight
+    copies (> L2), for profiler captures of a single kernel; prints per-launch us."""
+    import torch
+
+    import btf_b200 as btf
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    btf.kernels_init(0)
+    K, segs_n, mode = {"qkv": (5120, ("q", "k", "v"), btf.STORE), "o": (6144, ("o",), btf.ADD),
+                       "gateup": (5120, ("gate", "up"), btf.SWIGLU), "down": (17408, ("down",), btf.ADD)}[args.only]
+    shapes = {n: N for n, _, N in synth.LAYER_SHAPES}
+    srcs = {n: torch.from_numpy(synth.ternary_ptq(shapes[n], K, seed=0)).to(dev) for n in segs_n}
+    copies = [{n: btf.repack_panels(srcs[n], shapes[n], K) for n in segs_n} for _ in range(4)]
+    x = torch.from_numpy(synth.activations(1, K, seed=2)).to(dev)
+    act = btf.quant_q8(x)
+    ys = {n: torch.zeros((1, shapes[n]), device=dev) for n in segs_n}
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.iters)]
+    for i in range(args.iters):
+        c = copies[i % 4]
+        segs = [(c[n], ys[n], shapes[n]) for n in segs_n]
+        if mode == btf.SWIGLU:
+            segs[1] = (c["up"], None, 0)
+        ev[2 * i].record()
+        if args.fused:
+            btf.launch_gemv_f32(segs, K, 1, x, mode)
+        else:
+            btf.launch_gemv(segs, K, 1, act, mode)
+        ev[2 * i + 1].record()
+    torch.cuda.synchronize()
+    us = [ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1e3 for i in range(args.iters)]
+    nbytes = sum(btf.panel_bytes(shapes[n], K) for n in segs_n)
+    print(json.dumps({"kernel": args.only, "fused": bool(args.fused), "us": us,
+                      "GB/s_weights_min_us": nbytes / min(us) / 1e3}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -406,10 +445,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down"], help="profile mode: one GEMV kind")
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--fused", type=int, default=1)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.only:
+        only_kernel(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         gpu_arm(args)

@@ -20,7 +20,8 @@ from dataclasses import dataclass
 from typing import Optional, Sequence
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libbtf_b200.so")
+# BTF_B200_LIB selects another build of the library (e.g. a tuning variant)
+LIB_PATH = os.environ.get("BTF_B200_LIB", os.path.join(HERE, "libbtf_b200.so"))
 
 STORE, ADD, SWIGLU = 0, 1, 2  # GemvMode values (src/cuda/kernels.cuh:53)
 PANEL_ROWS, PANEL_COLS, PANEL_BYTES = 8, 1024, 2176

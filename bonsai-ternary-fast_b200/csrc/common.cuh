@@ -120,6 +120,32 @@ __device__ __forceinline__ int q8_warp(float v, float& dq, int& sum) {
   return qv;
 }
 
+// Same rule with each thread holding 4 consecutive values of a block and a
+// block spread over 8 consecutive lanes (lane & 7 = which 4 values). Returns the
+// four q of this thread packed as int8x4; d and s valid in all 8 lanes.
+__device__ __forceinline__ uint32_t q8_quad(float4 v, float& dq, int& sum) {
+  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float last = __shfl_sync(0xffffffffu, v.w, (threadIdx.x & 31) | 7);  // element 31 of the block
+  const float amax_signed = amax == 0.0f ? last : amax;
+  dq = __half2float(__float2half_rn(__fdiv_rn(amax_signed, 127.0f)));
+  const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  const int q0 = __float2int_rn(__fmul_rn(v.x, id)), q1 = __float2int_rn(__fmul_rn(v.y, id));
+  const int q2 = __float2int_rn(__fmul_rn(v.z, id)), q3 = __float2int_rn(__fmul_rn(v.w, id));
+  sum = q0 + q1 + q2 + q3;
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  return (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+         ((uint32_t)(q3 & 0xff) << 24);
+}
+
+// Loads 4 consecutive floats (vector load when 16-byte aligned).
+__device__ __forceinline__ float4 load4(const float* p, bool vec) {
+  if (vec) return *reinterpret_cast<const float4*>(p);
+  return make_float4(p[0], p[1], p[2], p[3]);
+}
+
 // ------------------------------------------------------------------ async copies, barriers, PDL
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

@@ -25,10 +25,13 @@
 //     lane loads are bank-conflict free; lane l always handles sub-block l of
 //     a slice, so its activation is loaded once per panel and reused for all
 //     8 (16) rows;
-//   - per (row, sub-block) the code dot uses four unshifted code masks
-//     (code * 4^k per byte) with unsigned x signed dp4a, one accumulator per
-//     k, recombined by exact arithmetic shifts; -sum(q) and the int->float
-//     conversion are folded into one biased add (kMagicInt).
+//   - codes are stored row-interleaved (one 32-bit word = 4 rows x 4 columns,
+//     row k in bits 2k..2k+1 of each byte): one AND with 0x03030303 << 2k gives
+//     4^k x the codes of row k aligned with the int8x4 activation word, so each
+//     (row, 4 columns) costs one LOP3 + one unsigned x signed dp4a, and the 4^k
+//     is removed once per (row, sub-block) by an exact arithmetic shift;
+//     -sum(q) and the int->float conversion are one biased add (kMagicInt);
+//     the fp32 epilogue runs on row pairs with packed f32x2 FMA (sm_100).
 #include <algorithm>
 #include <mutex>
 
@@ -37,12 +40,33 @@
 namespace btf {
 namespace {
 
-constexpr int kWarps = 8;
+// Launch shape (tuned on B200 by sweeping these; overridable at build time).
+#ifndef BTF_GEMV_WARPS
+#define BTF_GEMV_WARPS 8
+#endif
+#ifndef BTF_GEMV_SMEM_KB
+#define BTF_GEMV_SMEM_KB 110
+#endif
+#ifndef BTF_GEMV_MAX_CTAS
+#define BTF_GEMV_MAX_CTAS 2
+#endif
+#ifndef BTF_GEMV_MINB
+#define BTF_GEMV_MINB 1
+#endif
+#ifndef BTF_GEMV_GRID_CTAS
+#define BTF_GEMV_GRID_CTAS BTF_GEMV_MAX_CTAS
+#endif
+constexpr int kWarps = BTF_GEMV_WARPS;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSeg = 3;
-constexpr int kMaxNb = 4;                 // activation rows per pass
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per bounded wait
-constexpr size_t kSmemTarget = 110 * 1024;        // two CTAs per SM when it fits
+constexpr int kMaxNb = 4;                                  // activation rows per pass
+constexpr uint64_t kWaitLimitNs = 1000000000ull;           // 1 s per bounded wait
+constexpr size_t kSmemTarget = BTF_GEMV_SMEM_KB * 1024;    // ring + activation budget per CTA
+constexpr int kGridCtasPerSm = BTF_GEMV_GRID_CTAS;         // persistent CTAs per SM launched (<= resident)
+// 512-thread builds raised an illegal-address fault in the bench on B200 whose
+// cause was not found (a CPU replay of every index stayed in bounds); only
+// 128- and 256-thread CTAs are built.
+static_assert(kWarps == 4 || kWarps == 8, "gemv_kernel is built with 4 or 8 warps per CTA");
 
 struct GemvParams {
   const uint8_t* pan0;
@@ -65,26 +89,57 @@ struct GemvParams {
   int* err;
 };
 
-// Biased trit dot of one (row, sub-block): returns kMagicInt + idot, where
-// magic_s = kMagicInt - sum(q). w0/w1: the two T2 words; qa/qb: the eight
-// int8x4 activation words (columns 0..15 and 16..31 of the sub-block).
-__device__ __forceinline__ int sub_dot_biased(uint32_t w0, uint32_t w1, const uint4& qa, const uint4& qb,
-                                              int magic_s) {
-  int c0 = dp4a_us(w0 & 0x03030303u, qa.x, magic_s);
-  int c1 = dp4a_us(w0 & 0x0c0c0c0cu, qa.y, 0);
-  int c2 = dp4a_us(w0 & 0x30303030u, qa.z, 0);
-  int c3 = dp4a_us(w0 & 0xc0c0c0c0u, qa.w, 0);
-  c0 = dp4a_us(w1 & 0x03030303u, qb.x, c0);
-  c1 = dp4a_us(w1 & 0x0c0c0c0cu, qb.y, c1);
-  c2 = dp4a_us(w1 & 0x30303030u, qb.z, c2);
-  c3 = dp4a_us(w1 & 0xc0c0c0c0u, qb.w, c3);
-  // c_k = 4^k * (code dot of slot k): the shifts are exact.
-  return c0 + (c1 >> 2) + (c2 >> 4) + (c3 >> 6);
+// Per-row code dots of one row quad over one 32-column sub-block. cw0/cw1:
+// the quad words of columns 0..15 / 16..31; qa/qb: the activation words of the
+// same columns. c[k] = 4^k * code_dot(row k) accumulated onto c[k].
+__device__ __forceinline__ void quad_dots(const uint4& cw0, const uint4& cw1, const uint4& qa, const uint4& qb,
+                                          int c[4]) {
+  const uint32_t w[8] = {cw0.x, cw0.y, cw0.z, cw0.w, cw1.x, cw1.y, cw1.z, cw1.w};
+  const uint32_t a[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[0] = dp4a_us(w[i] & 0x03030303u, a[i], c[0]);
+    c[1] = dp4a_us(w[i] & 0x0c0c0c0cu, a[i], c[1]);
+    c[2] = dp4a_us(w[i] & 0x30303030u, a[i], c[2]);
+    c[3] = dp4a_us(w[i] & 0xc0c0c0c0u, a[i], c[3]);
+  }
 }
+
+// kMagicInt + idot of row k from its quad accumulator (exact shift) and
+// magic_s = kMagicInt - sum(q).
+template <int k>
+__device__ __forceinline__ int biased_idot(int c, int magic_s) { return (c >> (2 * k)) + magic_s; }
 
 __device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu))); }
 __device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 >> 16))); }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// Sums v[0..7] over the 32 lanes by recursive halving: after 9 shuffles lane l
+// holds in v[0] the total of row r(l) = 4*bit4(l) + 2*bit3(l) + bit2(l) (the 4
+// lanes of a group of four hold the same row). Returns r(l).
+__device__ __forceinline__ int reduce_rows8(float (&v)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // keep rows 0..3 (b4 = 0) or 4..7 (b4 = 1)
+    const float send = b4 ? v[i] : v[i + 4];
+    const float keep = b4 ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? v[i] : v[i + 2];
+    const float keep = b3 ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const float send = b2 ? v[0] : v[1];
+    const float keep = b2 ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  return 4 * (int)b4 + 2 * (int)b3 + (int)b2;
+}
 
 // Shared-memory layout (bytes), identical on host and device.
 struct SmemPlan {
@@ -99,9 +154,8 @@ struct SmemPlan {
 };
 
 template <int NB, int MODE, bool FUSE>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
-  constexpr int R = kSwi ? 2 * kRows : kRows;  // rows computed per panel (gate + up for swiglu)
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.S, depth = p.depth;
   const int nsp = S * kSubPerSlice;  // sub-blocks incl. padding to whole slices
@@ -127,17 +181,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
     seg = kSwi ? 0 : (u >= p.u1) + (u >= p.u2);
     g = u - (seg == 0 ? 0 : seg == 1 ? p.u1 : p.u2);
   };
-  auto issue = [&](int k) {  // lane 0: start the copies of this warp's k-th panel
-    const int ui = k / S, j = k - ui * S;
+  // Copy issue state (used by lane 0): next panel's unit, slice, slot and
+  // source pointers. A unit's S panels are contiguous, so moving to the next
+  // slice is a pointer bump; only a new unit needs locate().
+  int is_ui = 0, is_j = 0, is_slot = 0, is_count = 0;
+  const uint8_t* is_a = nullptr;
+  const uint8_t* is_b = nullptr;
+  auto unit_src = [&](int ui) {
     int seg, g;
     locate(first + ui * kWarps, seg, g);
-    const uint8_t* base = seg == 0 ? p.pan0 : seg == 1 ? p.pan1 : p.pan2;
-    const int64_t off = ((int64_t)g * S + j) * kPanelBytes;
-    const int slot = k % depth;
-    const uint32_t bar = my_bars + slot * 8, dst = my_ring + slot * plan.stage;
+    const int64_t off = (int64_t)g * S * kPanelBytes;
+    is_a = (seg == 0 ? p.pan0 : seg == 1 ? p.pan1 : p.pan2) + off;
+    is_b = kSwi ? p.pan1 + off : nullptr;
+  };
+  auto issue_next = [&]() {  // lane 0: start the copies of the next panel, advance
+    const uint32_t bar = my_bars + is_slot * 8, dst = my_ring + is_slot * plan.stage;
     mbar_expect_tx(bar, plan.stage);
-    bulk_g2s(dst, base + off, kPanelBytes, bar);
-    if (kSwi) bulk_g2s(dst + kPanelBytes, p.pan1 + off, kPanelBytes, bar);
+    bulk_g2s(dst, is_a, kPanelBytes, bar);
+    if (kSwi) bulk_g2s(dst + kPanelBytes, is_b, kPanelBytes, bar);
+    ++is_count;
+    if (++is_slot == depth) is_slot = 0;
+    if (++is_j == S) {
+      is_j = 0;
+      if (++is_ui < n_units) unit_src(is_ui);
+    } else {
+      is_a += kPanelBytes;
+      if (kSwi) is_b += kPanelBytes;
+    }
   };
 
   if (lane == 0) {
@@ -147,26 +217,45 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
   __syncwarp();
   pdl_launch_dependents();
   // weights never depend on the previous kernel: start streaming them now
-  if (lane == 0)
-    for (int k = 0; k < depth && k < n_panels; ++k) issue(k);
+  if (lane == 0 && n_panels > 0) {
+    unit_src(0);
+    while (is_count < depth && is_count < n_panels) issue_next();
+  }
   pdl_wait();
 
   // ---- activation -> shared memory (padded to whole slices with q = 0)
   if constexpr (FUSE) {
-    for (int b = warp; b < NB * nsp; b += kWarps) {
-      const int m = b / nsp, sb = b - m * nsp;
-      int qv = 0, sum = 0;
-      float dq = 0.0f;
-      if (m < p.nb && sb < p.nsub) {
-        const float v = p.x[(int64_t)(p.m0 + m) * p.ldx + sb * 32 + lane];
-        qv = q8_warp(v, dq, sum);
-      }
-      // lanes 0..15 -> qa bytes, 16..31 -> qb bytes
-      uint8_t* dstq = reinterpret_cast<uint8_t*>(lane < 16 ? qa_s : qb_s) + ((int64_t)m * nsp + sb) * 16 + (lane & 15);
-      *dstq = (uint8_t)(int8_t)qv;
-      if (lane == 0) {
-        d_s[m * nsp + sb] = dq;
-        ms_s[m * nsp + sb] = kMagicInt - sum;
+    // every thread owns 4 consecutive columns of a row; all loads of a row are
+    // issued before any is used (kQuads per thread covers K <= 18432 in one round)
+    constexpr int kQuads = 18;
+    const int nq = nsp * 8;  // quads incl. padding
+    const bool vec = ((reinterpret_cast<uintptr_t>(p.x) | ((uintptr_t)p.ldx * 4)) & 15) == 0;
+    for (int m = 0; m < NB; ++m) {
+      const bool row_ok = m < p.nb;
+      const float* xr = p.x + (int64_t)(p.m0 + (row_ok ? m : 0)) * p.ldx;
+      for (int base = 0; base < nq; base += kQuads * kThreads) {
+        float4 v[kQuads];
+#pragma unroll
+        for (int i = 0; i < kQuads; ++i) {
+          const int qi = base + i * kThreads + (int)threadIdx.x;
+          v[i] = (row_ok && qi < p.nsub * 8) ? load4(xr + qi * 4, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < kQuads; ++i) {
+          const int qi = base + i * kThreads + (int)threadIdx.x;
+          if (base + i * kThreads < nq && qi < nq) {  // warp-uniform: nq = S * 256 is a multiple of kThreads
+            float dq;
+            int sum;
+            const uint32_t q4 = q8_quad(v[i], dq, sum);
+            const int sb = qi >> 3, part = qi & 7;
+            uint32_t* dstq = reinterpret_cast<uint32_t*>(part < 4 ? qa_s : qb_s) + (m * nsp + sb) * 4 + (part & 3);
+            *dstq = q4;
+            if (part == 0) {
+              d_s[m * nsp + sb] = dq;
+              ms_s[m * nsp + sb] = kMagicInt - sum;
+            }
+          }
+        }
       }
     }
   } else {
@@ -191,89 +280,135 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
   }
   __syncthreads();
 
-  float acc[R][NB];
+  // acc[panel][quad][row pair][m]: rows (4h + 2e, 4h + 2e + 1) of the panel
+  float2 acc[kSwi ? 2 : 1][2][2][NB];
 #pragma unroll
-  for (int r = 0; r < R; ++r)
+  for (int pp = 0; pp < (kSwi ? 2 : 1); ++pp)
 #pragma unroll
-    for (int m = 0; m < NB; ++m) acc[r][m] = 0.0f;
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+#pragma unroll
+        for (int m = 0; m < NB; ++m) acc[pp][h][e][m] = make_float2(0.0f, 0.0f);
 
+  int slot = 0, j = 0, ui = 0;
+  uint32_t phase = 0;
   for (int k = 0; k < n_panels; ++k) {
-    const int slot = k % depth;
     const uint32_t bar = my_bars + slot * 8;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, (uint32_t)((k / depth) & 1), kWaitLimitNs));
+    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, phase, kWaitLimitNs));
     if (!ok) {
       // report, let copies already in flight land (bounded), and leave
       if (lane == 0) {
         atomicCAS(p.err, 0, kErrWaitTimeout);
-        for (int kk = k + 1; kk < n_panels && kk < k + depth; ++kk)
-          mbar_wait_bounded(my_bars + (kk % depth) * 8, (uint32_t)((kk / depth) & 1), kWaitLimitNs / 10);
+        int s2 = slot;
+        uint32_t ph2 = phase;
+        for (int kk = k + 1; kk < is_count; ++kk) {
+          if (++s2 == depth) {
+            s2 = 0;
+            ph2 ^= 1u;
+          }
+          mbar_wait_bounded(my_bars + s2 * 8, ph2, kWaitLimitNs / 10);
+        }
       }
       __syncwarp();
       return;
     }
-    const int j = k % S;
     const uint8_t* stage = ring + (warp * depth + slot) * plan.stage;
-    // scales of this lane's block (lane / 4) for the 8 rows, fp16
-    uint4 sc[kSwi ? 2 : 1];
-    sc[0] = *reinterpret_cast<const uint4*>(stage + kCodeBytes + (lane >> 2) * 16);
-    if constexpr (kSwi) sc[1] = *reinterpret_cast<const uint4*>(stage + kPanelBytes + kCodeBytes + (lane >> 2) * 16);
-    uint2 w[R];
+    constexpr int P = kSwi ? 2 : 1;  // panels per stage (gate, up)
+    uint4 cw[P][2][2];               // [panel][quad][half]
+    float sc[P][kRows];
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-      w[r] = *reinterpret_cast<const uint2*>(stage + (r / kRows) * kPanelBytes + code_offset(r % kRows, lane));
+    for (int pp = 0; pp < P; ++pp) {
+      const uint8_t* pan = stage + pp * kPanelBytes;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int v = 0; v < 2; ++v)
+          cw[pp][h][v] = *reinterpret_cast<const uint4*>(pan + h * 1024 + v * 512 + lane * 16);
+      const uint4 s4 = *reinterpret_cast<const uint4*>(pan + kCodeBytes + (lane >> 2) * 16);
+      sc[pp][0] = half_lo(s4.x); sc[pp][1] = half_hi(s4.x);
+      sc[pp][2] = half_lo(s4.y); sc[pp][3] = half_hi(s4.y);
+      sc[pp][4] = half_lo(s4.z); sc[pp][5] = half_hi(s4.z);
+      sc[pp][6] = half_lo(s4.w); sc[pp][7] = half_hi(s4.w);
+    }
 #pragma unroll
     for (int m = 0; m < NB; ++m) {
       const int ai = m * nsp + j * kSubPerSlice + lane;
       const uint4 qa = qa_s[ai], qb = qb_s[ai];
       const float dm = d_s[ai];
       const int ms = ms_s[ai];
+      const float2 d2 = make_float2(dm, dm);
+      const float2 nmagic = make_float2(-kMagicFloat, -kMagicFloat);
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint4 s4 = sc[r / kRows];
-        const int rr = r % kRows;
-        const uint32_t h2 = rr < 2 ? s4.x : rr < 4 ? s4.y : rr < 6 ? s4.z : s4.w;
-        const float scale = (rr & 1) ? half_hi(h2) : half_lo(h2);
-        const int biased = sub_dot_biased(w[r].x, w[r].y, qa, qb, ms);
-        acc[r][m] = fmaf(scale * dm, __int_as_float(biased) - kMagicFloat, acc[r][m]);
-      }
+      for (int pp = 0; pp < P; ++pp)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int c[4] = {0, 0, 0, 0};
+          quad_dots(cw[pp][h][0], cw[pp][h][1], qa, qb, c);
+          const float2 f01 = __fadd2_rn(make_float2(__int_as_float(biased_idot<0>(c[0], ms)),
+                                                    __int_as_float(biased_idot<1>(c[1], ms))), nmagic);
+          const float2 f23 = __fadd2_rn(make_float2(__int_as_float(biased_idot<2>(c[2], ms)),
+                                                    __int_as_float(biased_idot<3>(c[3], ms))), nmagic);
+          const int r = 4 * h;
+          const float2 s01 = __fmul2_rn(make_float2(sc[pp][r], sc[pp][r + 1]), d2);
+          const float2 s23 = __fmul2_rn(make_float2(sc[pp][r + 2], sc[pp][r + 3]), d2);
+          acc[pp][h][0][m] = __ffma2_rn(s01, f01, acc[pp][h][0][m]);
+          acc[pp][h][1][m] = __ffma2_rn(s23, f23, acc[pp][h][1][m]);
+        }
     }
     __syncwarp();
-    if (lane == 0 && k + depth < n_panels) {
+    if (lane == 0 && is_count < n_panels) {
       fence_proxy_async_smem();  // our generic-proxy reads of the slot precede the next async write
-      issue(k + depth);
+      issue_next();
     }
-    if (j == S - 1) {  // unit done: reduce over lanes, lane i stores row i
+    if (++slot == depth) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    if (++j == S) {  // unit done: reduce over lanes, lane i stores row i
+      j = 0;
       int seg, g;
-      locate(first + (k / S) * kWarps, seg, g);
+      locate(first + ui * kWarps, seg, g);
+      ++ui;
       const int n = seg == 0 ? p.n0 : seg == 1 ? p.n1 : p.n2;
       const int ldy = seg == 0 ? p.ld0 : seg == 1 ? p.ld1 : p.ld2;
       float* y = seg == 0 ? p.y0 : seg == 1 ? p.y1 : p.y2;
 #pragma unroll
       for (int m = 0; m < NB; ++m) {
-        float mine = 0.0f, mine_up = 0.0f;
+        float v[kRows], u[kRows];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float v = warp_sum(acc[r][m]);
-          if (r < kRows) {
-            if (lane == r) mine = v;
-          } else if (lane == r - kRows) {
-            mine_up = v;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            v[4 * h + 2 * e] = acc[0][h][e][m].x;
+            v[4 * h + 2 * e + 1] = acc[0][h][e][m].y;
+            acc[0][h][e][m] = make_float2(0.0f, 0.0f);
+            if constexpr (kSwi) {
+              u[4 * h + 2 * e] = acc[kSwi ? 1 : 0][h][e][m].x;
+              u[4 * h + 2 * e + 1] = acc[kSwi ? 1 : 0][h][e][m].y;
+              acc[kSwi ? 1 : 0][h][e][m] = make_float2(0.0f, 0.0f);
+            }
           }
-          acc[r][m] = 0.0f;
+        const int row_l = reduce_rows8(v, lane);
+        float up = 0.0f;
+        if constexpr (kSwi) {
+          reduce_rows8(u, lane);  // same lane -> row map as v
+          up = u[0];
         }
-        const int row = g * kRows + lane;
-        if (lane < kRows && row < n && m < p.nb) {
+        const int row = g * kRows + row_l;
+        if ((lane & 3) == 0 && row < n && m < p.nb) {
           float* yp = y + (int64_t)(p.m0 + m) * ldy + row;
-          if constexpr (MODE == BTF_STORE) *yp = mine;
-          else if constexpr (MODE == BTF_ADD) *yp += mine;
-          else *yp = silu(mine) * mine_up;
+          if constexpr (MODE == BTF_STORE) *yp = v[0];
+          else if constexpr (MODE == BTF_ADD) *yp += v[0];
+          else *yp = silu(v[0]) * up;
         }
       }
     }
   }
 }
 
-// Exact idot dump (parity/debug): one thread per (m, row, sub-block).
+// Exact idot dump (parity/debug): one thread per (m, row, sub-block), same
+// quad decode as the GEMV.
 __global__ void __launch_bounds__(256)
     idot_kernel(const uint8_t* __restrict__ pan, int N, int K, int M, const int8_t* __restrict__ q,
                 const int32_t* __restrict__ s, int32_t* __restrict__ idot) {
@@ -284,12 +419,15 @@ __global__ void __launch_bounds__(256)
     const int sbk = (int)(i % nsub);
     const int64_t mr = i / nsub;
     const int r = (int)(mr % N), m = (int)(mr / N);
-    const uint8_t* pp = pan + panel_offset(r / kRows, sbk / kSubPerSlice, S) + code_offset(r % kRows, sbk % kSubPerSlice);
-    const uint2 w = *reinterpret_cast<const uint2*>(pp);
+    const int rg = r % kRows, h = rg / 4, kk = rg % 4, l = sbk % kSubPerSlice;
+    const uint8_t* pp = pan + panel_offset(r / kRows, sbk / kSubPerSlice, S) + h * 1024 + l * 16;
+    const uint4 cw0 = *reinterpret_cast<const uint4*>(pp), cw1 = *reinterpret_cast<const uint4*>(pp + 512);
     const int8_t* qp = q + (int64_t)m * K + (int64_t)sbk * 32;
     const uint4 qa = *reinterpret_cast<const uint4*>(qp), qb = *reinterpret_cast<const uint4*>(qp + 16);
-    const int magic_s = kMagicInt - s[(int64_t)m * nsub + sbk];
-    idot[i] = sub_dot_biased(w.x, w.y, qa, qb, magic_s) - kMagicInt;
+    int c[4] = {0, 0, 0, 0};
+    quad_dots(cw0, cw1, qa, qb, c);
+    const int cd = kk == 0 ? c[0] : kk == 1 ? (c[1] >> 2) : kk == 2 ? (c[2] >> 4) : (c[3] >> 6);
+    idot[i] = cd - s[(int64_t)m * nsub + sbk];
   }
 }
 
@@ -339,7 +477,7 @@ int resident_ctas(KernelFn fn, int smem) {
     if (cache[i].fn == fn && cache[i].smem == smem) return cache[i].n;
   int n = 1;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) != cudaSuccess || n < 1) n = 1;
-  n = std::min(n, 2);
+  n = std::min(n, kGridCtasPerSm);
   if (used < 64) cache[used++] = Entry{fn, smem, n};
   return n;
 }
@@ -385,8 +523,9 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
     // ring depth: fill ~kSmemTarget, at least 2 slots
     const SmemPlan base(mode, NB, p.S, 0);
     const int per_slot = kWarps * (base.stage + 8);
-    int depth = (int)((kSmemTarget - (size_t)base.act) / per_slot);
-    depth = std::max(2, std::min(depth, 6));
+    const size_t room = kSmemTarget > (size_t)base.act ? kSmemTarget - (size_t)base.act : 0;
+    int depth = (int)(room / per_slot);
+    depth = std::max(2, std::min(depth, 8));
     const SmemPlan plan(mode, NB, p.S, depth);
     if (plan.total > dev->optin_smem)
       return fail(BTF_ERR_UNSUPPORTED, "btf_gemv: K=%d with %d activation rows needs %d B of shared memory (max %d)",

@@ -26,23 +26,23 @@ struct BytePtr {
 void repack_groups(const uint8_t* src, int64_t N, int64_t K, uint8_t* panels, int64_t g0, int64_t g1) {
   const int64_t nbk = K / 128, S = (K + BTF_PANEL_COLS - 1) / BTF_PANEL_COLS, bpr = S * 8;
   for (int64_t g = g0; g < g1; ++g)
-    for (int64_t r = 0; r < kRowsH; ++r) {
-      const int64_t n = g * kRowsH + r;
+    for (int h = 0; h < 2; ++h)
       for (int64_t b = 0; b < bpr; ++b) {
-        uint32_t w[8];
-        uint16_t scale = 0;
-        if (n < N && b < nbk) {
-          const uint8_t* blk = src + (n * nbk + b) * 28;
-          ptq_block_to_t2(BytePtr{blk}, w);
-          scale = (uint16_t)(blk[26] | (blk[27] << 8));
-        } else {
-          for (int k = 0; k < 8; ++k) w[k] = 0x55555555u;
+        uint32_t tw[4][8];
+        uint16_t sc[4];
+        for (int k = 0; k < 4; ++k) {
+          const int64_t n = g * kRowsH + h * 4 + k;
+          sc[k] = 0;
+          if (n < N && b < nbk) {
+            const uint8_t* blk = src + (n * nbk + b) * 28;
+            ptq_block_to_t2(BytePtr{blk}, tw[k]);
+            sc[k] = (uint16_t)(blk[26] | (blk[27] << 8));
+          } else {
+            for (int w = 0; w < 8; ++w) tw[k][w] = 0x55555555u;
+          }
         }
-        uint8_t* pan = panels + (g * S + b / 8) * kPanelH;
-        std::memcpy(pan + r * 256 + (b % 8) * 32, w, 32);
-        std::memcpy(pan + 2048 + (b % 8) * 16 + r * 2, &scale, 2);
+        store_quad_block(panels + (g * S + b / 8) * kPanelH, h, (int)(b % 8), tw, sc);
       }
-    }
 }
 
 }  // namespace

@@ -27,30 +27,31 @@ __device__ __forceinline__ void load_block(const uint8_t* src, int64_t blk, Src7
   scale = (uint16_t)(s.v[6] >> 16);
 }
 
-// Grid covers the padded domain: G*8 rows x S*8 blocks; out-of-range blocks
-// are written as padding (code 1 everywhere, scale 0).
+// Grid covers the padded domain: G*2 row quads x S*8 blocks, one thread each;
+// rows >= N and blocks >= K/128 are written as padding (code 1, scale 0).
 __global__ void __launch_bounds__(kThreads)
     repack_panels_kernel(const uint8_t* __restrict__ src, int64_t N, int64_t K, uint8_t* __restrict__ panels) {
-  const int64_t nbk = K / 128, S = slices_of(K), bpr = S * kBlocksPerSlice;  // blocks per padded row
-  const int64_t total = groups_of(N) * kRows * bpr;
+  const int64_t nbk = K / 128, S = slices_of(K), bpr = S * kBlocksPerSlice;
+  const int64_t total = groups_of(N) * 2 * bpr;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / bpr, b = i - n * bpr;
-    uint32_t w[8];
-    uint16_t scale = 0;
-    if (n < N && b < nbk) {
-      Src7 s;
-      load_block(src, n * nbk + b, s, scale);
-      ptq_block_to_t2(s, w);
-    } else {
+    const int64_t qd = i / bpr, b = i - qd * bpr;
+    uint32_t tw[4][8];
+    uint16_t sc[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) w[k] = kPadWord;
+    for (int k = 0; k < 4; ++k) {
+      const int64_t n = qd * 4 + k;
+      sc[k] = 0;
+      if (n < N && b < nbk) {
+        Src7 s;
+        load_block(src, n * nbk + b, s, sc[k]);
+        ptq_block_to_t2(s, tw[k]);
+      } else {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tw[k][w] = kPadWord;
+      }
     }
-    uint8_t* pan = panels + panel_offset(n / kRows, b / kBlocksPerSlice, S);
-    const int r = (int)(n % kRows), bb = (int)(b % kBlocksPerSlice);
-    uint4* dst = reinterpret_cast<uint4*>(pan + code_offset(r, bb * 4));
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    *reinterpret_cast<uint16_t*>(pan + scale_offset(r, bb)) = scale;
+    store_quad_block(panels + panel_offset(qd / 2, b / kBlocksPerSlice, S), (int)(qd % 2), (int)(b % kBlocksPerSlice),
+                     tw, sc);
   }
 }
 
@@ -73,23 +74,28 @@ __global__ void __launch_bounds__(kThreads)
     t2_to_panels_kernel(const uint8_t* __restrict__ codes, const uint16_t* __restrict__ scales, int64_t N, int64_t K,
                         uint8_t* __restrict__ panels) {
   const int64_t nbk = K / 128, S = slices_of(K), bpr = S * kBlocksPerSlice;
-  const int64_t total = groups_of(N) * kRows * bpr;
+  const int64_t total = groups_of(N) * 2 * bpr;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / bpr, b = i - n * bpr;
-    uint4 c0 = make_uint4(kPadWord, kPadWord, kPadWord, kPadWord), c1 = c0;
-    uint16_t scale = 0;
-    if (n < N && b < nbk) {
-      const uint4* src = reinterpret_cast<const uint4*>(codes + (n * nbk + b) * 32);
-      c0 = src[0];
-      c1 = src[1];
-      scale = scales[n * nbk + b];
+    const int64_t qd = i / bpr, b = i - qd * bpr;
+    uint32_t tw[4][8];
+    uint16_t sc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t n = qd * 4 + k;
+      sc[k] = 0;
+      if (n < N && b < nbk) {
+        const uint4* sp = reinterpret_cast<const uint4*>(codes + (n * nbk + b) * 32);
+        const uint4 c0 = sp[0], c1 = sp[1];
+        tw[k][0] = c0.x; tw[k][1] = c0.y; tw[k][2] = c0.z; tw[k][3] = c0.w;
+        tw[k][4] = c1.x; tw[k][5] = c1.y; tw[k][6] = c1.z; tw[k][7] = c1.w;
+        sc[k] = scales[n * nbk + b];
+      } else {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tw[k][w] = kPadWord;
+      }
     }
-    uint8_t* pan = panels + panel_offset(n / kRows, b / kBlocksPerSlice, S);
-    const int r = (int)(n % kRows), bb = (int)(b % kBlocksPerSlice);
-    uint4* dst = reinterpret_cast<uint4*>(pan + code_offset(r, bb * 4));
-    dst[0] = c0;
-    dst[1] = c1;
-    *reinterpret_cast<uint16_t*>(pan + scale_offset(r, bb)) = scale;
+    store_quad_block(panels + panel_offset(qd / 2, b / kBlocksPerSlice, S), (int)(qd % 2), (int)(b % kBlocksPerSlice),
+                     tw, sc);
   }
 }
 
@@ -97,16 +103,23 @@ __global__ void __launch_bounds__(kThreads)
     panels_to_t2_kernel(const uint8_t* __restrict__ panels, int64_t N, int64_t K, uint8_t* __restrict__ codes,
                         uint16_t* __restrict__ scales) {
   const int64_t nbk = K / 128, S = slices_of(K);
-  const int64_t total = N * nbk;
+  const int64_t nquad = (N + 3) / 4;
+  const int64_t total = nquad * nbk;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / nbk, b = i - n * nbk;
-    const uint8_t* pan = panels + panel_offset(n / kRows, b / kBlocksPerSlice, S);
-    const int r = (int)(n % kRows), bb = (int)(b % kBlocksPerSlice);
-    const uint4* src = reinterpret_cast<const uint4*>(pan + code_offset(r, bb * 4));
-    uint4* dst = reinterpret_cast<uint4*>(codes + i * 32);
-    dst[0] = src[0];
-    dst[1] = src[1];
-    scales[i] = *reinterpret_cast<const uint16_t*>(pan + scale_offset(r, bb));
+    const int64_t qd = i / nbk, b = i - qd * nbk;
+    uint32_t tw[4][8];
+    uint16_t sc[4];
+    load_quad_block(panels + panel_offset(qd / 2, b / kBlocksPerSlice, S), (int)(qd % 2), (int)(b % kBlocksPerSlice),
+                    tw, sc);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t n = qd * 4 + k;
+      if (n >= N) break;
+      uint4* dst = reinterpret_cast<uint4*>(codes + (n * nbk + b) * 32);
+      dst[0] = make_uint4(tw[k][0], tw[k][1], tw[k][2], tw[k][3]);
+      dst[1] = make_uint4(tw[k][4], tw[k][5], tw[k][6], tw[k][7]);
+      scales[n * nbk + b] = sc[k];
+    }
   }
 }
 
@@ -135,7 +148,7 @@ int btf_repack_panels(const void* ptq_src, int64_t N, int64_t K, void* panels, v
   if (!ptq_src || !panels || !aligned(ptq_src, 4) || !aligned(panels, 16))
     return fail(BTF_ERR_ARG, "btf_repack_panels: null or misaligned pointer (src needs 4 B, panels 16 B)");
   if (!current_device()) return BTF_ERR_STATE;
-  const int64_t total = groups_of(N) * kRows * slices_of(K) * kBlocksPerSlice;
+  const int64_t total = groups_of(N) * 2 * slices_of(K) * kBlocksPerSlice;
   repack_panels_kernel<<<grid_for(total), kThreads, 0, (cudaStream_t)stream>>>(
       static_cast<const uint8_t*>(ptq_src), N, K, static_cast<uint8_t*>(panels));
   return launch_status("repack_panels_kernel");
@@ -157,7 +170,7 @@ int btf_t2_to_panels(const uint8_t* codes, const uint16_t* scales, int64_t N, in
   if (!codes || !scales || !panels || !aligned(codes, 16) || !aligned(scales, 2) || !aligned(panels, 16))
     return fail(BTF_ERR_ARG, "btf_t2_to_panels: null or misaligned pointer");
   if (!current_device()) return BTF_ERR_STATE;
-  const int64_t total = groups_of(N) * kRows * slices_of(K) * kBlocksPerSlice;
+  const int64_t total = groups_of(N) * 2 * slices_of(K) * kBlocksPerSlice;
   t2_to_panels_kernel<<<grid_for(total), kThreads, 0, (cudaStream_t)stream>>>(codes, scales, N, K,
                                                                              static_cast<uint8_t*>(panels));
   return launch_status("t2_to_panels_kernel");
@@ -168,7 +181,7 @@ int btf_panels_to_t2(const void* panels, int64_t N, int64_t K, uint8_t* codes, u
   if (!codes || !scales || !panels || !aligned(codes, 16) || !aligned(scales, 2) || !aligned(panels, 16))
     return fail(BTF_ERR_ARG, "btf_panels_to_t2: null or misaligned pointer");
   if (!current_device()) return BTF_ERR_STATE;
-  panels_to_t2_kernel<<<grid_for(N * (K / 128)), kThreads, 0, (cudaStream_t)stream>>>(
+  panels_to_t2_kernel<<<grid_for((N + 3) / 4 * (K / 128)), kThreads, 0, (cudaStream_t)stream>>>(
       static_cast<const uint8_t*>(panels), N, K, codes, scales);
   return launch_status("panels_to_t2_kernel");
 }

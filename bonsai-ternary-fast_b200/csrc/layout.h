@@ -67,4 +67,82 @@ BTF_HD void ptq_block_to_t2(const ByteAt& byte, uint32_t w[8]) {
   }
 }
 
+// Row-interleaved ("quad") form used by the panel layout: for 4 rows k = 0..3
+// and one 16-column half of a sub-block, word i (columns 4i .. 4i+3) holds the
+// code of row k, column 4i + j in byte j at bits 2k .. 2k+1, so
+//   word & (0x03030303 << 2k)  ==  4^k * (the four codes of row k)
+// lines up with the int8x4 activation word of those columns. The map is a 4x4
+// transpose of 2-bit fields and is its own inverse: t2_quad_transpose turns
+// the 4 rows' T2 words of a half (t[k]) into the quad words and back.
+BTF_HD void t2_quad_transpose(const uint32_t in[4], uint32_t out[4]) {
+  BTF_UNROLL
+  for (int a = 0; a < 4; ++a) {
+    uint32_t w = 0;
+    BTF_UNROLL
+    for (int b = 0; b < 4; ++b) w |= ((in[b] >> (2 * a)) & 0x03030303u) << (2 * b);
+    out[a] = w;
+  }
+}
+
+// Panel geometry (see include/btf_b200.h).
+constexpr int kQuadBytes = 1024;  // one row quad's codes in a panel
+constexpr int kHalfBytes = 512;   // one 16-column half of a quad
+constexpr int kScaleBase = 2048;
+
+BTF_HD void copy16(uint8_t* dst, const uint32_t w[4]) {
+#if defined(__CUDA_ARCH__)
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+#else
+  for (int i = 0; i < 4; ++i)
+    for (int b = 0; b < 4; ++b) dst[4 * i + b] = (uint8_t)(w[i] >> (8 * b));
+#endif
+}
+BTF_HD void load16(const uint8_t* src, uint32_t w[4]) {
+#if defined(__CUDA_ARCH__)
+  const uint4 v = *reinterpret_cast<const uint4*>(src);
+  w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+#else
+  for (int i = 0; i < 4; ++i)
+    w[i] = (uint32_t)src[4 * i] | ((uint32_t)src[4 * i + 1] << 8) | ((uint32_t)src[4 * i + 2] << 16) |
+           ((uint32_t)src[4 * i + 3] << 24);
+#endif
+}
+
+// Writes one 128-column block (block bb of the panel's slice) of a row quad
+// (quad h of the panel) from the 4 rows' T2 words tw[k][0..7] and scales.
+BTF_HD void store_quad_block(uint8_t* pan, int h, int bb, const uint32_t tw[4][8], const uint16_t sc[4]) {
+  BTF_UNROLL
+  for (int sb = 0; sb < 4; ++sb)
+    BTF_UNROLL
+    for (int v = 0; v < 2; ++v) {
+      const uint32_t in[4] = {tw[0][2 * sb + v], tw[1][2 * sb + v], tw[2][2 * sb + v], tw[3][2 * sb + v]};
+      uint32_t out[4];
+      t2_quad_transpose(in, out);
+      copy16(pan + h * kQuadBytes + v * kHalfBytes + (bb * 4 + sb) * 16, out);
+    }
+  uint8_t* sp = pan + kScaleBase + bb * 16 + h * 8;
+  BTF_UNROLL
+  for (int k = 0; k < 4; ++k) {
+    sp[2 * k] = (uint8_t)(sc[k] & 0xffu);
+    sp[2 * k + 1] = (uint8_t)(sc[k] >> 8);
+  }
+}
+
+// Inverse of store_quad_block: the 4 rows' T2 words and scales of one block.
+BTF_HD void load_quad_block(const uint8_t* pan, int h, int bb, uint32_t tw[4][8], uint16_t sc[4]) {
+  BTF_UNROLL
+  for (int sb = 0; sb < 4; ++sb)
+    BTF_UNROLL
+    for (int v = 0; v < 2; ++v) {
+      uint32_t in[4], out[4];
+      load16(pan + h * kQuadBytes + v * kHalfBytes + (bb * 4 + sb) * 16, in);
+      t2_quad_transpose(in, out);
+      BTF_UNROLL
+      for (int k = 0; k < 4; ++k) tw[k][2 * sb + v] = out[k];
+    }
+  const uint8_t* sp = pan + kScaleBase + bb * 16 + h * 8;
+  BTF_UNROLL
+  for (int k = 0; k < 4; ++k) sc[k] = (uint16_t)(sp[2 * k] | (sp[2 * k + 1] << 8));
+}
+
 }  // namespace btf

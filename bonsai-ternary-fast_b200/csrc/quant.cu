@@ -10,26 +10,28 @@ namespace btf {
 namespace {
 
 constexpr int kQThreads = 256;
-constexpr int kQWarps = kQThreads / 32;
 
+// One thread per 4 consecutive values, 8 lanes per 32-block (q8_quad).
 __global__ void __launch_bounds__(kQThreads)
     quant_q8_kernel(const float* __restrict__ x, int ldx, int K, int8_t* __restrict__ q, float* __restrict__ d,
                     int32_t* __restrict__ s) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nsub = K / 32;
-  const int sb = blockIdx.x * kQWarps + warp;
+  const int nquad = K / 4;
+  const int qi = blockIdx.x * kQThreads + threadIdx.x;
   const int m = blockIdx.y;
   pdl_launch_dependents();
   pdl_wait();
-  if (sb >= nsub) return;
-  const float v = x[(size_t)m * ldx + sb * 32 + lane];
+  if (blockIdx.x * kQThreads >= nquad) return;  // whole block beyond the row (warp-uniform)
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) | ((uintptr_t)ldx * 4)) & 15) == 0;
+  const bool ok = qi < nquad;  // K % 32 == 0: a 32-block is all in or all out
+  const float4 v = ok ? load4(x + (size_t)m * ldx + qi * 4, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
   float dq;
   int sum;
-  const int qv = q8_warp(v, dq, sum);
-  q[(size_t)m * K + sb * 32 + lane] = (int8_t)qv;
-  if (lane == 0) {
-    d[(size_t)m * nsub + sb] = dq;
-    s[(size_t)m * nsub + sb] = sum;
+  const uint32_t q4 = q8_quad(v, dq, sum);
+  if (!ok) return;
+  *reinterpret_cast<uint32_t*>(q + (size_t)m * K + qi * 4) = q4;
+  if ((qi & 7) == 0) {
+    d[(size_t)m * (K / 32) + (qi >> 3)] = dq;
+    s[(size_t)m * (K / 32) + (qi >> 3)] = sum;
   }
 }
 
@@ -44,7 +46,8 @@ extern "C" int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act
     return fail(BTF_ERR_ARG, "btf_quant_q8: need K a positive multiple of 32 and ldx >= K (K=%d ldx=%d)", K, ldx);
   if (!x || !act.q || !act.d || !act.s) return fail(BTF_ERR_ARG, "btf_quant_q8: null pointer");
   if (!current_device()) return BTF_ERR_STATE;
-  const dim3 grid((K / 32 + kQWarps - 1) / kQWarps, M);
+  if (((uintptr_t)act.q & 3) != 0) return fail(BTF_ERR_ARG, "btf_quant_q8: q must be 4-byte aligned");
+  const dim3 grid((K / 4 + kQThreads - 1) / kQThreads, M);
   if (grid.y > 65535) return fail(BTF_ERR_ARG, "btf_quant_q8: M=%d exceeds 65535", M);
   const cudaError_t e = launch_pdl(quant_q8_kernel, grid, dim3(kQThreads), 0, (cudaStream_t)stream, x, ldx, K,
                                    act.q, act.d, act.s);

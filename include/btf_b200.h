@@ -12,15 +12,18 @@
  *     btf_last_error() gives a one-line message for the calling thread.
  *
  * Resident weight layout ("panels", replaces T2 of include/btf/packed.hpp:6-14):
- *   a [N][K] ternary matrix is cut into row groups of 8 rows and column
- *   slices of 1024 columns (32 sub-blocks of 32 = 8 PTQ1_0 blocks of 128).
+ *   a [N][K] ternary matrix is cut into row groups of 8 rows and column slices
+ *   of 1024 columns (32 sub-blocks of 32 = 8 PTQ1_0 blocks of 128).
  *   Panel (g, j) is 2176 contiguous bytes at ((g * S) + j) * 2176, S = ceil(K/1024):
- *     bytes [0, 2048):    codes of row r (0..7), sub-block l (0..31) at r*256 + l*8,
- *                         two little-endian T2 words (2-bit code = trit + 1; word w
- *                         holds column 32l + 16w + 4k + j at bit 8j + 2k);
+ *     bytes [0, 2048):    codes, 2 bits each (code = trit + 1), as 32-bit words:
+ *                         quad h (rows 4h..4h+3), half v, sub-block l, word i at
+ *                         h*1024 + v*512 + l*16 + i*4 holds columns 32l + 16v + 4i + c
+ *                         (c = byte 0..3) of row 4h + k at bits 8c + 2k .. 8c + 2k + 1;
  *     bytes [2048, 2176): fp16 block scales, block b (0..7) of row r at 2048 + b*16 + r*2.
  *   A row group's S panels are contiguous, so one 1-D bulk copy per panel streams
- *   8 rows x 1024 columns with their scales.
+ *   8 rows x 1024 columns with their scales; in a word, (word & (3 << 2k) per byte)
+ *   is 4^k times the codes of row 4h + k, ready for a byte-wise dot product with
+ *   the int8x4 activation word of the same four columns.
  *   Rows >= N and columns >= K are padding (code 1 = trit 0, scale 0).
  *   Total size: btf_panel_bytes(N, K).
  */

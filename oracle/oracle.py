@@ -246,10 +246,26 @@ def panel_decode(panels: np.ndarray, N: int, K: int):
     """Independent numpy reader of the panel layout (include/btf_b200.h) -> T2 codes [N][K/4], scales [N][K/128].
 
     Written from the layout description, not from the library, so a test that
-    compares it with the reference T2 checks the library's layout end to end."""
+    compares it with the reference T2 checks the library's layout end to end.
+    Returns the padded arrays too when N or K are not multiples of 8 / 1024."""
     S = (K + 1023) // 1024
     G = (N + 7) // 8
     p = np.asarray(panels, dtype=np.uint8).reshape(G, S, 2176)
-    codes = p[:, :, :2048].reshape(G, S, 8, 256).transpose(0, 2, 1, 3).reshape(G * 8, S * 256)
+    # codes: [G][S][quad h][half v][sub-block l][word i] uint32
+    w = p[:, :, :2048].copy().view("<u4").reshape(G, S, 2, 2, 32, 4).astype(np.uint32)
+    # code of row 4h+k, column 32l + 16v + 4i + c: (w >> (8c + 2k)) & 3
+    c = np.arange(4, dtype=np.uint32)
+    k = np.arange(4, dtype=np.uint32)
+    codes = (w[..., None, None] >> (8 * c[None, :] + 2 * k[:, None])) & 3  # [..., k, c]
+    # -> [G][h][k][S][l][v][i][c] = row (8G + 4h + k), column (1024 S + 32 l + 16 v + 4 i + c)
+    codes = codes.transpose(0, 2, 6, 1, 4, 3, 5, 7).reshape(G * 8, S * 1024).astype(np.uint8)
+    # back to T2 bytes: column e of a block at byte (e//32)*8 + ((e//16)%2)*4 + e%4, shift ((e//4)%4)*2
+    e = np.arange(S * 1024)
+    byte = (e // 128) * 32 + ((e % 128) // 32) * 8 + (((e % 128) // 16) % 2) * 4 + (e % 4)
+    shift = (((e % 128) // 4) % 4) * 2
+    t2 = np.zeros((G * 8, S * 256), dtype=np.uint8)
+    for sh in range(0, 8, 2):
+        sel = shift == sh
+        np.bitwise_or.at(t2, (slice(None), byte[sel]), (codes[:, sel] << sh).astype(np.uint8))
     sc = p[:, :, 2048:].copy().view(np.uint16).reshape(G, S, 8, 8).transpose(0, 3, 1, 2).reshape(G * 8, S * 8)
-    return np.ascontiguousarray(codes[:N, :K // 4]), np.ascontiguousarray(sc[:N, :K // 128])
+    return np.ascontiguousarray(t2[:N, :K // 4]), np.ascontiguousarray(sc[:N, :K // 128])

@@ -49,11 +49,9 @@ def test_host_repack_matches_reference_t2(btf, orc, N, K):
     assert np.array_equal(codes, c_ref) and np.array_equal(scales, s_ref)
     # padding: rows >= N and columns >= K hold code 1 (trit 0) and scale 0
     G, S = (N + 7) // 8, (K + 1023) // 1024
-    p = pan.reshape(G, S, 2176)
-    full_c = p[:, :, :2048].reshape(G, S, 8, 256).transpose(0, 2, 1, 3).reshape(G * 8, S * 256)
-    full_s = p[:, :, 2048:].copy().view(np.uint16).reshape(G, S, 8, 8).transpose(0, 3, 1, 2).reshape(G * 8, S * 8)
-    assert np.all(full_c[N:] == 0x55) and np.all(full_c[:, K // 4:] == 0x55)
-    assert np.all(full_s[N:] == 0) and np.all(full_s[:, K // 128:] == 0)
+    full_codes, full_scales = oracle.panel_decode(pan, G * 8, S * 1024)
+    assert np.all(full_codes[N:] == 0x55) and np.all(full_codes[:, K // 4:] == 0x55)
+    assert np.all(full_scales[N:] == 0) and np.all(full_scales[:, K // 128:] == 0)
 
 
 def test_host_repack_rejects_bad_shape(btf):
