@@ -88,6 +88,8 @@ int btf_init(int device) {
     st = cuda_fail(e, "cudaDeviceGetAttribute");
   } else if (major != 10 || minor != 0) {
     st = fail(BTF_ERR_UNSUPPORTED, "btf_b200 is built for sm_100a (B200); device %d is sm_%d%d", device, major, minor);
+  } else if (g_dev[device].ready) {
+    st = BTF_OK;  // already initialised
   } else if ((st = gemv_setup(d)) == BTF_OK && (st = gemm_setup(d)) == BTF_OK) {
     d.ready = true;
     g_dev[device] = d;

@@ -85,7 +85,7 @@ struct GemvParams {
   const int32_t* s;
   const float* x;      // fp32 input (FUSE == true)
   int ldx;
-  int depth;           // ring slots per warp
+  int slots;           // ring slots of a CTA, shared by the warps that have work
   int* err;
 };
 
@@ -143,13 +143,14 @@ __device__ __forceinline__ int reduce_rows8(float (&v)[8], int lane) {
 
 // Shared-memory layout (bytes), identical on host and device.
 struct SmemPlan {
-  int stage, ring, bars, act, total;
-  __host__ __device__ SmemPlan(int mode, int nb, int S, int depth) {
+  int stage, ring, bars, act, pieces, total;
+  __host__ __device__ SmemPlan(int mode, int nb, int S, int slots) {
     stage = (mode == BTF_SWIGLU ? 2 : 1) * kPanelBytes;
-    ring = kWarps * depth * stage;
-    bars = kWarps * depth * 8;
+    ring = slots * stage;
+    bars = (slots * 8 + 15) / 16 * 16;  // keeps the uint4 activation arrays 16-byte aligned
     act = nb * S * kSubPerSlice * 40;  // qa 16 B + qb 16 B + d 4 B + magic_s 4 B per sub-block
-    total = ring + bars + act;
+    pieces = kWarps * kMaxNb * 16 * 4;  // per-warp partial row sums when units are split by slices
+    total = ring + bars + act + pieces;
   }
 };
 
@@ -157,22 +158,36 @@ template <int NB, int MODE, bool FUSE>
 __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int S = p.S, depth = p.depth;
+  const int S = p.S;
   const int nsp = S * kSubPerSlice;  // sub-blocks incl. padding to whole slices
-  const SmemPlan plan(MODE, NB, S, depth);
+  const SmemPlan plan(MODE, NB, S, p.slots);
   uint8_t* ring = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.ring);
   uint4* qa_s = reinterpret_cast<uint4*>(smem + plan.ring + plan.bars);
   uint4* qb_s = qa_s + NB * nsp;
   float* d_s = reinterpret_cast<float*>(qb_s + NB * nsp);
   int* ms_s = reinterpret_cast<int*>(d_s + NB * nsp);
+  float* pieces = reinterpret_cast<float*>(smem + plan.ring + plan.bars + plan.act);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int u_begin = (int)((int64_t)blockIdx.x * p.utotal / gridDim.x);
   const int u_end = (int)((int64_t)(blockIdx.x + 1) * p.utotal / gridDim.x);
-  const int first = u_begin + warp;
-  const int n_units = first < u_end ? (u_end - first + kWarps - 1) / kWarps : 0;
-  const int n_panels = n_units * S;
+  const int cta_units = u_end - u_begin;
+  // With fewer units than warps, each unit is cut into G slice ranges handled
+  // by G warps (partial sums combined in shared memory at the end); otherwise
+  // warp w takes units u_begin + w, u_begin + w + kWarps, ...
+  const int G = (cta_units > 0 && cta_units < kWarps) ? min(kWarps / cta_units, S) : 1;
+  const int part = warp % G;
+  const int first = u_begin + (G > 1 ? warp / G : warp);
+  const int stride = G > 1 ? cta_units : kWarps;  // unit step between a warp's units
+  const bool has_work = G > 1 ? warp < cta_units * G : first < u_end;
+  const int j_lo = G > 1 ? part * S / G : 0, j_hi = G > 1 ? (part + 1) * S / G : S;
+  const int n_units = !has_work ? 0 : G > 1 ? 1 : (u_end - first + kWarps - 1) / kWarps;
+  const int n_panels = n_units * (j_hi - j_lo);
+  // the ring is split among the warps that have work only, so a CTA with few
+  // (long) units keeps proportionally more of each warp's panels in flight
+  const int active = G > 1 ? cta_units * G : min(kWarps, cta_units);
+  const int depth = active > 0 ? p.slots / active : p.slots;
   const uint32_t my_bars = smem_u32(bars + warp * depth);
   const uint32_t my_ring = smem_u32(ring + warp * depth * plan.stage);
 
@@ -184,13 +199,13 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
   // Copy issue state (used by lane 0): next panel's unit, slice, slot and
   // source pointers. A unit's S panels are contiguous, so moving to the next
   // slice is a pointer bump; only a new unit needs locate().
-  int is_ui = 0, is_j = 0, is_slot = 0, is_count = 0;
+  int is_ui = 0, is_j = j_lo, is_slot = 0, is_count = 0;
   const uint8_t* is_a = nullptr;
   const uint8_t* is_b = nullptr;
   auto unit_src = [&](int ui) {
     int seg, g;
-    locate(first + ui * kWarps, seg, g);
-    const int64_t off = (int64_t)g * S * kPanelBytes;
+    locate(first + ui * stride, seg, g);
+    const int64_t off = ((int64_t)g * S + j_lo) * kPanelBytes;
     is_a = (seg == 0 ? p.pan0 : seg == 1 ? p.pan1 : p.pan2) + off;
     is_b = kSwi ? p.pan1 + off : nullptr;
   };
@@ -201,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
     if (kSwi) bulk_g2s(dst + kPanelBytes, is_b, kPanelBytes, bar);
     ++is_count;
     if (++is_slot == depth) is_slot = 0;
-    if (++is_j == S) {
-      is_j = 0;
+    if (++is_j == j_hi) {
+      is_j = j_lo;
       if (++is_ui < n_units) unit_src(is_ui);
     } else {
       is_a += kPanelBytes;
@@ -210,18 +225,27 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
     }
   };
 
-  if (lane == 0) {
+  if (lane == 0 && n_panels > 0) {
     for (int i = 0; i < depth; ++i) mbar_init(my_bars + i * 8, 1);
     fence_mbar_init();
   }
   __syncwarp();
   pdl_launch_dependents();
-  // weights never depend on the previous kernel: start streaming them now
+  // Weights never depend on the previous kernel: before waiting for it, start
+  // the copy of this warp's FIRST panel only. Every warp's first panel is thus
+  // ahead of everyone's later panels in the memory queues, so all warps can
+  // start computing early instead of some waiting behind a whole-ring burst.
   if (lane == 0 && n_panels > 0) {
     unit_src(0);
-    while (is_count < depth && is_count < n_panels) issue_next();
+    issue_next();
   }
   pdl_wait();
+  // The activation is read next (few KB, L2-resident); the rest of the ring is
+  // started once those loads are in flight.
+  auto start_ring = [&]() {
+    if (lane == 0)
+      while (is_count < depth && is_count < n_panels) issue_next();
+  };
 
   // ---- activation -> shared memory (padded to whole slices with q = 0)
   if constexpr (FUSE) {
@@ -258,24 +282,43 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
         }
       }
     }
+    start_ring();
   } else {
-    for (int i = threadIdx.x; i < NB * nsp; i += kThreads) {
-      const int m = i / nsp, sb = i - m * nsp;
-      uint4 a = make_uint4(0, 0, 0, 0), b = a;
-      float dv = 0.0f;
-      int sv = 0;
-      if (m < p.nb && sb < p.nsub) {
-        const int64_t row = p.m0 + m;
-        const uint4* src = reinterpret_cast<const uint4*>(p.q + row * p.K + (int64_t)sb * 32);
-        a = src[0];
-        b = src[1];
-        dv = p.d[row * p.nsub + sb];
-        sv = p.s[row * p.nsub + sb];
+    // chunks of kStageIters items per thread (one chunk covers K <= 17408 for NB = 1)
+    constexpr int kStageIters = (NB * 544 + kThreads - 1) / kThreads;
+    for (int base = 0; base < NB * nsp; base += kStageIters * kThreads) {
+      uint4 ra[kStageIters], rb[kStageIters];
+      float rd[kStageIters];
+      int rs[kStageIters];
+#pragma unroll
+      for (int it = 0; it < kStageIters; ++it) {
+        const int i = base + (int)threadIdx.x + it * kThreads;
+        ra[it] = rb[it] = make_uint4(0, 0, 0, 0);
+        rd[it] = 0.0f;
+        rs[it] = 0;
+        if (i < NB * nsp) {
+          const int m = i / nsp, sb = i - m * nsp;
+          if (m < p.nb && sb < p.nsub) {
+            const int64_t row = p.m0 + m;
+            const uint4* src = reinterpret_cast<const uint4*>(p.q + row * p.K + (int64_t)sb * 32);
+            ra[it] = src[0];
+            rb[it] = src[1];
+            rd[it] = p.d[row * p.nsub + sb];
+            rs[it] = p.s[row * p.nsub + sb];
+          }
+        }
       }
-      qa_s[i] = a;
-      qb_s[i] = b;
-      d_s[i] = dv;
-      ms_s[i] = kMagicInt - sv;
+      if (base == 0) start_ring();
+#pragma unroll
+      for (int it = 0; it < kStageIters; ++it) {
+        const int i = base + (int)threadIdx.x + it * kThreads;
+        if (i < NB * nsp) {
+          qa_s[i] = ra[it];
+          qb_s[i] = rb[it];
+          d_s[i] = rd[it];
+          ms_s[i] = kMagicInt - rs[it];
+        }
+      }
     }
   }
   __syncthreads();
@@ -291,8 +334,9 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
 #pragma unroll
         for (int m = 0; m < NB; ++m) acc[pp][h][e][m] = make_float2(0.0f, 0.0f);
 
-  int slot = 0, j = 0, ui = 0;
+  int slot = 0, j = j_lo, ui = 0;
   uint32_t phase = 0;
+  bool aborted = false;
   for (int k = 0; k < n_panels; ++k) {
     const uint32_t bar = my_bars + slot * 8;
     const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, phase, kWaitLimitNs));
@@ -311,14 +355,15 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
         }
       }
       __syncwarp();
-      return;
+      aborted = true;  // leave the loop but still reach the CTA barrier below
+      break;
     }
     const uint8_t* stage = ring + (warp * depth + slot) * plan.stage;
-    constexpr int P = kSwi ? 2 : 1;  // panels per stage (gate, up)
-    uint4 cw[P][2][2];               // [panel][quad][half]
-    float sc[P][kRows];
+    constexpr int kPan = kSwi ? 2 : 1;  // panels per stage (gate, up)
+    uint4 cw[kPan][2][2];               // [panel][quad][half]
+    float sc[kPan][kRows];
 #pragma unroll
-    for (int pp = 0; pp < P; ++pp) {
+    for (int pp = 0; pp < kPan; ++pp) {
       const uint8_t* pan = stage + pp * kPanelBytes;
 #pragma unroll
       for (int h = 0; h < 2; ++h)
@@ -340,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
       const float2 d2 = make_float2(dm, dm);
       const float2 nmagic = make_float2(-kMagicFloat, -kMagicFloat);
 #pragma unroll
-      for (int pp = 0; pp < P; ++pp)
+      for (int pp = 0; pp < kPan; ++pp)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           int c[4] = {0, 0, 0, 0};
@@ -365,10 +410,10 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
       slot = 0;
       phase ^= 1u;
     }
-    if (++j == S) {  // unit done: reduce over lanes, lane i stores row i
-      j = 0;
+    if (++j == j_hi) {  // this warp's part of the unit is done: reduce over lanes
+      j = j_lo;
       int seg, g;
-      locate(first + ui * kWarps, seg, g);
+      locate(first + ui * stride, seg, g);
       ++ui;
       const int n = seg == 0 ? p.n0 : seg == 1 ? p.n1 : p.n2;
       const int ldy = seg == 0 ? p.ld0 : seg == 1 ? p.ld1 : p.ld2;
@@ -395,12 +440,45 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
           reduce_rows8(u, lane);  // same lane -> row map as v
           up = u[0];
         }
-        const int row = g * kRows + row_l;
-        if ((lane & 3) == 0 && row < n && m < p.nb) {
+        if ((lane & 3) == 0) {
+          if (G > 1) {  // partial over slices [j_lo, j_hi): combined below
+            pieces[(warp * kMaxNb + m) * 16 + row_l] = v[0];
+            if constexpr (kSwi) pieces[(warp * kMaxNb + m) * 16 + kRows + row_l] = up;
+          } else {
+            const int row = g * kRows + row_l;
+            if (row < n && m < p.nb) {
+              float* yp = y + (int64_t)(p.m0 + m) * ldy + row;
+              if constexpr (MODE == BTF_STORE) *yp = v[0];
+              else if constexpr (MODE == BTF_ADD) *yp += v[0];
+              else *yp = silu(v[0]) * up;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  if (G > 1) {  // CTA-uniform: the G parts of each unit are summed in part order
+    __syncthreads();
+    if (has_work && part == 0 && !aborted) {
+      int seg, g;
+      locate(first, seg, g);
+      const int n = seg == 0 ? p.n0 : seg == 1 ? p.n1 : p.n2;
+      const int ldy = seg == 0 ? p.ld0 : seg == 1 ? p.ld1 : p.ld2;
+      float* y = seg == 0 ? p.y0 : seg == 1 ? p.y1 : p.y2;
+      const int r = lane & 7, m = lane >> 3;
+      if (m < NB) {
+        float sg = 0.0f, su = 0.0f;
+        for (int w = warp; w < warp + G; ++w) {
+          sg += pieces[(w * kMaxNb + m) * 16 + r];
+          if constexpr (kSwi) su += pieces[(w * kMaxNb + m) * 16 + kRows + r];
+        }
+        const int row = g * kRows + r;
+        if (row < n && m < p.nb) {
           float* yp = y + (int64_t)(p.m0 + m) * ldy + row;
-          if constexpr (MODE == BTF_STORE) *yp = v[0];
-          else if constexpr (MODE == BTF_ADD) *yp += v[0];
-          else *yp = silu(v[0]) * up;
+          if constexpr (MODE == BTF_STORE) *yp = sg;
+          else if constexpr (MODE == BTF_ADD) *yp += sg;
+          else *yp = silu(sg) * su;
         }
       }
     }
@@ -520,17 +598,15 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
   for (int m0 = 0; m0 < M; m0 += kMaxNb) {
     const int nb = std::min(kMaxNb, M - m0);
     const int NB = nb <= 1 ? 1 : nb <= 2 ? 2 : 4;
-    // ring depth: fill ~kSmemTarget, at least 2 slots
+    // ring slots: fill ~kSmemTarget, at least 2 per warp
     const SmemPlan base(mode, NB, p.S, 0);
-    const int per_slot = kWarps * (base.stage + 8);
     const size_t room = kSmemTarget > (size_t)base.act ? kSmemTarget - (size_t)base.act : 0;
-    int depth = (int)(room / per_slot);
-    depth = std::max(2, std::min(depth, 8));
-    const SmemPlan plan(mode, NB, p.S, depth);
-    if (plan.total > dev->optin_smem)
+    const int slots = std::max(2 * kWarps, std::min((int)(room / (base.stage + 8)), 64));
+    const SmemPlan plan(mode, NB, p.S, slots);
+    if (plan.total > dev->optin_smem - 1024)
       return fail(BTF_ERR_UNSUPPORTED, "btf_gemv: K=%d with %d activation rows needs %d B of shared memory (max %d)",
-                  K, NB, plan.total, dev->optin_smem);
-    p.depth = depth;
+                  K, NB, plan.total, dev->optin_smem - 1024);
+    p.slots = slots;
     p.m0 = m0;
     p.nb = nb;
     const KernelFn fn = pick(NB, mode, x != nullptr);
@@ -561,9 +637,11 @@ int gemv_setup(DeviceInfo& d) {
   void* ew = nullptr;
   if ((e = cudaGetSymbolAddress(&ew, g_device_error)) != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
   d.err_word = static_cast<int*>(ew);
-  if ((e = set_attrs<BTF_STORE, false>(d.optin_smem)) || (e = set_attrs<BTF_ADD, false>(d.optin_smem)) ||
-      (e = set_attrs<BTF_SWIGLU, false>(d.optin_smem)) || (e = set_attrs<BTF_STORE, true>(d.optin_smem)) ||
-      (e = set_attrs<BTF_ADD, true>(d.optin_smem)) || (e = set_attrs<BTF_SWIGLU, true>(d.optin_smem)))
+  // leave room for static shared memory (per-block limit = dynamic + static)
+  const int dyn = d.optin_smem - 1024;
+  if ((e = set_attrs<BTF_STORE, false>(dyn)) || (e = set_attrs<BTF_ADD, false>(dyn)) ||
+      (e = set_attrs<BTF_SWIGLU, false>(dyn)) || (e = set_attrs<BTF_STORE, true>(dyn)) ||
+      (e = set_attrs<BTF_ADD, true>(dyn)) || (e = set_attrs<BTF_SWIGLU, true>(dyn)))
     return cuda_fail(e, "cudaFuncSetAttribute(gemv_kernel)");
   return BTF_OK;
 }
