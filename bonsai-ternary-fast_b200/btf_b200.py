@@ -31,7 +31,7 @@ EXPORTS = (
     "btf_status_string", "btf_last_error", "btf_version", "btf_init", "btf_gemv_max_nb",
     "btf_panel_bytes", "btf_t2_codes_bytes", "btf_t2_scales_bytes",
     "btf_repack_panels", "btf_repack_panels_host", "btf_repack_t2", "btf_t2_to_panels", "btf_panels_to_t2",
-    "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot",
+    "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot", "btf_gemm",
 )
 
 
@@ -78,6 +78,7 @@ def lib() -> ctypes.CDLL:
         "btf_gemv_f32": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
         "btf_device_error": (i32, [i32]),
         "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
+        "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -245,6 +246,11 @@ def launch_gemv_f32(segs: Sequence[tuple], K: int, M: int, x, mode: int = STORE,
     """Fused quantise + GEMV from fp32 activations x [M][>=K] (btf_gemv_f32)."""
     check(lib().btf_gemv_f32(_segs(segs), len(segs), K, M, _ptr(x), x.stride(0), mode, _stream(stream)),
           "btf_gemv_f32")
+
+
+def launch_gemm(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int = STORE, stream=None) -> None:
+    """Prefill GEMM on the tcgen05 int8 tensor cores (btf_gemm), M >= 64; store / add modes."""
+    check(lib().btf_gemm(_segs(segs), len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemm")
 
 
 def device_error(clear: bool = False) -> int:

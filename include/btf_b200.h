@@ -133,6 +133,13 @@ int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* 
  * not for use inside stream capture. clear != 0 resets it. Returns -1 on failure. */
 int btf_device_error(int clear);
 
+/* ---- ternary GEMM for prefill batches (M >= 64): tcgen05 int8 tensor cores
+ * (kind::i8, one exact 32-deep MMA step per activation block, fp32 epilogue on
+ * the CUDA cores). Same result contract as btf_gemv for BTF_STORE / BTF_ADD; it
+ * replaces the repeated 8-row passes of launch_gemv (src/cuda/kernels.cu:805-821)
+ * for large M. q and d must be 16-byte aligned. */
+int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
+
 /* Debug/parity entry point: the exact int32 trit dot of every (m, row,
  * sub-block), idot[M][N][K/32] = code_dot - sum(q) — the integers the GEMV
  * scales (src/emu_decoder.cpp:154-157). Same decode path as btf_gemv. */

@@ -1,0 +1,88 @@
+"""GPU parity of the tcgen05 prefill GEMM (btf_gemm) against the oracle.
+
+The reference has no GEMM: prefill runs as repeated 8-row GEMV passes
+(src/cuda/kernels.cu:805-821), whose math the oracle restates
+(src/emu_decoder.cpp:143-165). The bar is the GEMV's: exact int32 partials
+(the MMA computes each 32-column idot exactly in int32) and fp32 outputs within
+rel-RMS 1e-5 of the oracle and of the double reference. Shapes cover partial M
+and N tiles, add mode, and the benchmark's prefill configurations (M = 64 and
+512 with K=5120 -> N=17408 and K=17408 -> N=5120), the latter checked on a
+subset of output rows so the CPU oracle stays quick.
+"""
+import numpy as np
+import pytest
+
+import synth
+from conftest import rel_rms
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def _dev(a, device):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def _case(btf, orc, cuda, M, K, N, seed, mode=0, rows=None):
+    import torch
+
+    src = synth.ternary_ptq(N, K, seed=seed)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    x = synth.activations(M, K, seed=seed + 1)
+    act = btf.quant_q8(_dev(x, cuda))
+    y0 = np.random.default_rng(seed).standard_normal((M, N)).astype(np.float32)
+    y = _dev(y0, cuda) if mode == btf.ADD else torch.full((M, N), 7.0, device=cuda)
+    btf.launch_gemm([(pm, y, N)], K, M, act, mode)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    got = y.cpu().numpy()
+    q, d, s = orc.q8_rows(x)
+    sel = slice(None) if rows is None else rows
+    codes, scales = orc.repack_t2(src[sel], src[sel].shape[0], K)
+    want = orc.gemv(codes, scales, K, q, d, s, threads=8)
+    want64 = orc.gemv_f64(codes, scales, K, q, d) if rows is None and N * K * M <= 64 * 5120 * 260 else None
+    g = got[:, sel]
+    if mode == btf.ADD:
+        want = want + y0[:, sel]
+        if want64 is not None:
+            want64 = want64 + y0[:, sel]
+    assert rel_rms(g, want) <= TOL, rel_rms(g, want)
+    if want64 is not None:
+        assert rel_rms(g, want64) <= TOL
+    return got
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 1024, 64), (128, 1024, 37), (130, 2048, 130), (64, 5120, 200),
+                                   (200, 1152, 72)])
+def test_gemm_matches_oracle(cuda, btf, orc, M, K, N):
+    _case(btf, orc, cuda, M, K, N, seed=M + K + N)
+
+
+def test_gemm_add_mode(cuda, btf, orc):
+    _case(btf, orc, cuda, 96, 1024, 80, seed=5, mode=btf.ADD)
+
+
+def test_gemm_equals_gemv_passes(cuda, btf, orc):
+    # same Q8 input through both paths: the GEMM and the 4-row GEMV passes agree
+    import torch
+
+    M, K, N = 64, 2048, 96
+    src = synth.ternary_ptq(N, K, seed=9)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    act = btf.quant_q8(_dev(synth.activations(M, K, seed=10), cuda))
+    y1 = torch.empty((M, N), device=cuda)
+    y2 = torch.empty((M, N), device=cuda)
+    btf.launch_gemm([(pm, y1, N)], K, M, act, btf.STORE)
+    btf.launch_gemv([(pm, y2, N)], K, M, act, btf.STORE)
+    torch.cuda.synchronize()
+    assert rel_rms(y1.cpu().numpy(), y2.cpu().numpy()) <= TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 5120, 17408), (512, 5120, 17408), (64, 17408, 5120), (512, 17408, 5120)])
+def test_gemm_prefill_configs(cuda, btf, orc, M, K, N):
+    # benchmark configuration 2 shapes; rows from the first, a middle and the last N tile
+    rows = np.r_[0:64, N // 2 - 32:N // 2 + 32, N - 64:N]
+    _case(btf, orc, cuda, M, K, N, seed=0, rows=rows)
