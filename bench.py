@@ -391,6 +391,8 @@ def gpu_arm(args):
             "gpu_launches": args.steps * N_LAYERS * 8,
             "clocks": clocks.report(),
         }
+        if world == 1:
+            line["prefill_gemm_config2"] = prefill_gemm(btf, torch, dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(host_threads())
         print(json.dumps(line), flush=True)
@@ -398,6 +400,45 @@ def gpu_arm(args):
         del g_dev, g_e2e
         dist.barrier()
         dist.destroy_process_group()
+
+
+PREFILL_SHAPES = ((64, 5120, 17408), (512, 5120, 17408), (64, 17408, 5120), (512, 17408, 5120))
+
+
+def prefill_gemm(btf, torch, dev, reps=10):
+    """Benchmark configuration 2: the tcgen05 prefill GEMM (btf_gemm) at M = 64 and 512
+    on both weight shapes, each launch over one of 4 rotating weight copies (> L2),
+    timed with CUDA events around a CUDA graph of `reps` launches."""
+    out = {}
+    for M, K, N in PREFILL_SHAPES:
+        src = torch.from_numpy(synth.ternary_ptq(N, K, seed=0)).to(dev)
+        mats = [btf.repack_panels(src, N, K) for _ in range(4)]
+        act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=2)).to(dev))
+        y = torch.empty((M, N), device=dev)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            for i in range(4):
+                btf.launch_gemm([(mats[i % 4], y, N)], K, M, act, btf.STORE, st)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(reps):
+                btf.launch_gemm([(mats[i % 4], y, N)], K, M, act, btf.STORE, st)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        with torch.cuda.stream(st):
+            g.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        ops = 2.0 * M * N * K
+        out[f"M{M}_K{K}_N{N}"] = {"us": us, "TOPS": ops / us / 1e6,
+                                  "frac_of_int8_spec_4500": ops / us / 1e6 / 4500.0,
+                                  "weight_GBps": btf.panel_bytes(N, K) / us / 1e3}
+        del g, mats, src
+    return out
 
 
 def only_kernel(args):
@@ -410,6 +451,17 @@ def only_kernel(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     btf.kernels_init(0)
+    if args.only == "gemm":  # one prefill GEMM: M=512, K=5120 -> N=17408
+        M, K, N = 512, 5120, 17408
+        src = torch.from_numpy(synth.ternary_ptq(N, K, seed=0)).to(dev)
+        mats = [btf.repack_panels(src, N, K) for _ in range(2)]
+        act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=2)).to(dev))
+        y = torch.empty((M, N), device=dev)
+        for i in range(args.iters):
+            btf.launch_gemm([(mats[i % 2], y, N)], K, M, act, btf.STORE)
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel": "gemm", "iters": args.iters, "device_error": btf.device_error()}))
+        return
     K, segs_n, mode = {"qkv": (5120, ("q", "k", "v"), btf.STORE), "o": (6144, ("o",), btf.ADD),
                        "gateup": (5120, ("gate", "up"), btf.SWIGLU), "down": (17408, ("down",), btf.ADD)}[args.only]
     shapes = {n: N for n, _, N in synth.LAYER_SHAPES}
@@ -445,7 +497,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down"], help="profile mode: one GEMV kind")
+    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm"], help="profile mode: one kernel kind")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--fused", type=int, default=1)
     args = ap.parse_args()

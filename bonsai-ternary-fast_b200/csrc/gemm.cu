@@ -18,8 +18,8 @@
 //   warps 2-5   expand the 2-bit codes of the chunk into int8 trits in the
 //               canonical K-major SW128 layout the MMA reads, and stage the
 //               chunk's activation scales d and fp32 weight scales;
-//   warps 6-13  epilogue: TMEM -> registers (tcgen05.ld 32x32b), per step
-//               T += d * idot, per 128-column block acc += scale * T.
+//   warps 6-21  epilogue: TMEM -> registers (tcgen05.ld 32x32b, 16 columns),
+//               per step T += d * idot, per 128-column block acc += scale * T.
 // Every wait is bounded; on a time-out the kernel records an error word, stops
 // issuing work, waits (bounded) for its MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -38,9 +38,11 @@ constexpr int kChunk = 128;          // K columns per pipeline chunk (one scale 
 constexpr int kStepsPerChunk = 4;    // 32-column MMA steps per chunk
 constexpr int kStagesA = 4;          // A / B / d stages (chunks)
 constexpr int kStagesP = 2;          // panel stages (slices of 1024 columns)
-constexpr int kDRegions = 4;         // TMEM accumulator regions (one per in-flight step)
-constexpr int kTmemCols = kDRegions * kTileN;  // 256
-constexpr int kThreads = 14 * 32;
+constexpr int kDRegions = 8;         // TMEM accumulator regions (one per in-flight step)
+constexpr int kTmemCols = kDRegions * kTileN;  // 512: all of TMEM
+constexpr int kEpiWarps = 16;        // 4 per SMSP: TMEM-load latency of one hides behind the others' math
+constexpr int kEpiCols = kTileN * 4 / kEpiWarps;  // columns per epilogue thread (16)
+constexpr int kThreads = (6 + kEpiWarps) * 32;
 constexpr int kExpWarp0 = 2, kEpiWarp0 = 6;
 constexpr uint64_t kGemmWaitNs = 1000000000ull;
 
@@ -51,7 +53,8 @@ constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStagesA * kABytes;          // 65536
 constexpr int kOffP = kOffB + kStagesA * kBBytes;          // 98304
 constexpr int kOffD = kOffP + kStagesP * kPBytes;          // 133120
-constexpr int kOffS = kOffD + kStagesA * kTileM * 4 * 4;   // d: [stage][128][4] floats
+constexpr int kDBytes = kTileM * 4 * 4;                    // d of one chunk: [128 rows][4 steps] fp32
+constexpr int kOffS = kOffD + kStagesA * kDBytes;          // d: [stage][128][4] floats (TMA)
 constexpr int kOffBar = kOffS + kStagesA * kTileN * 4;     // s: [stage][64] floats
 constexpr int kNumBars = 4 * kStagesA + 2 * kStagesP + 2 * kDRegions + 4;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
@@ -106,6 +109,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(addr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -120,7 +134,7 @@ __device__ __forceinline__ uint32_t codes_to_trits(uint32_t c) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base (SW128 atoms and TMA destinations)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -147,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(a_full(s), 1);
       mbar_init(ab_empty(s), 1);
       mbar_init(b_full(s), 4);
-      mbar_init(dsf_empty(s), 8);
+      mbar_init(dsf_empty(s), kEpiWarps);
     }
     for (int s = 0; s < kStagesP; ++s) {
       mbar_init(p_full(s), 1);
@@ -155,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int r = 0; r < kDRegions; ++r) {
       mbar_init(mma_done(r), 1);
-      mbar_init(d_free(r), 8);
+      mbar_init(d_free(r), kEpiWarps);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -200,9 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                      p.pan + ((int64_t)(g0 + gi) * p.S + j) * kPanelBytes, kPanelBytes, p_full(ps));
         }
         const int s = c % kStagesA;
-        if (c >= kStagesA && !wait(ab_empty(s), (uint32_t)((c / kStagesA - 1) & 1))) break;
-        mbar_expect_tx(a_full(s), kABytes);
+        if (c >= kStagesA) {
+          // the slot's A (MMA) and d (epilogue) must both have been consumed:
+          // this also keeps every a_full waiter within one phase of the barrier
+          const uint32_t ph = (uint32_t)((c / kStagesA - 1) & 1);
+          if (!wait(ab_empty(s), ph) || !wait(dsf_empty(s), ph)) break;
+        }
+        mbar_expect_tx(a_full(s), kABytes + kDBytes);
         tma_load_2d(sbase + kOffA + s * kABytes, &tmA, c * kChunk, m0, a_full(s));
+        tma_load_2d(sbase + kOffD + s * kDBytes, &tmD, c * kStepsPerChunk, m0, a_full(s));
         issued = c + 1;
       }
       if (*abort_flag) {
@@ -246,8 +266,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int e = threadIdx.x - kExpWarp0 * 32;  // 0..127
     const int G = (int)groups_of(p.N);
     const int g0 = n0 / kRows;
-    const int nsub = p.K / 32;
-    pdl_wait();  // d comes from the previous kernel
     for (int c = 0; c < nchunks; ++c) {
       const int j = c / 8, ps = j % kStagesP, b = c % 8, s = c % kStagesA;
       if (b == 0 && !wait(p_full(ps), (uint32_t)((j / kStagesP) & 1))) break;
@@ -283,11 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         reinterpret_cast<float*>(smem + kOffS)[s * kTileN + e] = sc;
       }
-      {  // activation scales of the chunk's 4 steps for row e
-        float4 dv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m0 + e < p.M) dv = *reinterpret_cast<const float4*>(p.d + (int64_t)(m0 + e) * nsub + c * 4);
-        reinterpret_cast<float4*>(smem + kOffD)[s * kTileM + e] = dv;
-      }
       fence_proxy_async_smem();  // generic writes of B -> visible to the tensor core (async proxy)
       __syncwarp();
       if (lane == 0) {
@@ -298,16 +311,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;                    // TMEM lane quarter this warp may access
-    const int wg = (warp - kEpiWarp0) >> 2;    // column half of the tile
+    const int cg = (warp - kEpiWarp0) >> 2;    // column group of the tile
     const int m = q * 32 + lane;               // tile row of this thread
-    float2 acc[16], tsum[16];
+    constexpr int H = kEpiCols / 2;
+    float2 acc[H], tsum[H];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = tsum[i] = make_float2(0.f, 0.f);
+    for (int i = 0; i < H; ++i) acc[i] = tsum[i] = make_float2(0.f, 0.f);
     const float2 nmagic = make_float2(-kMagicFloat, -kMagicFloat);
     bool ok = true;
     for (int c = 0; c < nchunks && ok; ++c) {
       const int s = c % kStagesA;
-      if (!wait(b_full(s), (uint32_t)((c / kStagesA) & 1))) break;
+      const uint32_t ph = (uint32_t)((c / kStagesA) & 1);
+      if (!wait(b_full(s), ph) || !wait(a_full(s), ph)) break;  // scales (expanders) and d (TMA with A)
       const float4 dv = reinterpret_cast<const float4*>(smem + kOffD)[s * kTileM + m];
       const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
@@ -318,14 +333,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        uint32_t dr[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + r * kTileN + wg * 32, dr);
+        uint32_t dr[kEpiCols];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + r * kTileN + cg * kEpiCols, dr);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(d_free(r));
         const float2 d2 = make_float2(dk[ks], dk[ks]);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < H; ++i) {
           const float2 f = __fadd2_rn(make_float2(__int_as_float((int)dr[2 * i] + kMagicInt),
                                                   __int_as_float((int)dr[2 * i + 1] + kMagicInt)),
                                       nmagic);
@@ -333,9 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      const float* sc = reinterpret_cast<const float*>(smem + kOffS) + s * kTileN + wg * 32;
+      const float* sc = reinterpret_cast<const float*>(smem + kOffS) + s * kTileN + cg * kEpiCols;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < H; ++i) {
         const float2 s2 = make_float2(sc[2 * i], sc[2 * i + 1]);
         acc[i] = __ffma2_rn(s2, tsum[i], acc[i]);
         tsum[i] = make_float2(0.f, 0.f);
@@ -345,10 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     pdl_wait();  // y may be read (BTF_ADD) and is written: the previous kernel must be done
     if (ok && !*abort_flag && m0 + m < p.M) {
-      float* yr = p.y + (int64_t)(m0 + m) * p.ldy + n0 + wg * 32;
+      float* yr = p.y + (int64_t)(m0 + m) * p.ldy + n0 + cg * kEpiCols;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int n = n0 + wg * 32 + 2 * i;
+      for (int i = 0; i < H; ++i) {
+        const int n = n0 + cg * kEpiCols + 2 * i;
         if (n < p.N) {
           if (p.mode == BTF_ADD) yr[2 * i] += acc[i].x;
           else yr[2 * i] = acc[i].x;
@@ -412,6 +427,15 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(BTF_ERR_ARG, "btf_gemm: tensor map encoding failed (%d)", (int)r);
+  // activation block scales: fp32 [M][K/32], box 4 steps x 128 rows, rows beyond M read as zero
+  CUtensorMap dmap;
+  const cuuint64_t ddims[2] = {(cuuint64_t)(K / 32), (cuuint64_t)M};
+  const cuuint64_t dstrides[1] = {(cuuint64_t)(K / 32) * 4};
+  const cuuint32_t dbox[2] = {(cuuint32_t)kStepsPerChunk, (cuuint32_t)kTileM};
+  const CUresult r2 = enc(&dmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(act.d), ddims, dstrides, dbox,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r2 != CUDA_SUCCESS) return fail(BTF_ERR_ARG, "btf_gemm: scale tensor map encoding failed (%d)", (int)r2);
   GemmParams p{};
   p.pan = static_cast<const uint8_t*>(seg.panels);
   p.N = seg.N;
@@ -424,7 +448,7 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
   p.mode = mode;
   p.err = dev->err_word;
   const dim3 grid((seg.N + kTileN - 1) / kTileN, (M + kTileM - 1) / kTileM);
-  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, map, p);
+  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, map, dmap, p);
   return e == cudaSuccess ? launch_status("gemm_kernel") : cuda_fail(e, "gemm_kernel launch");
 }
 
