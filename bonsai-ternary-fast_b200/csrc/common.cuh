@@ -188,14 +188,37 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Waits for phase `parity` of `bar` for at most `limit_ns`; false on time-out.
+#ifndef BTF_WAIT_HINT_NS
+#define BTF_WAIT_HINT_NS 0
+#endif
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps
+// until the phase completes or about `hint_ns` pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+#if BTF_WAIT_HINT_NS > 0
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"((uint32_t)BTF_WAIT_HINT_NS)
+      : "memory");
+  return ok != 0;
+#else
+  return mbar_try_wait(bar, parity);
+#endif
+}
+
+// Waits for phase `parity` of `bar` for at most about `limit_ns`; false on
+// time-out. The clock is read once per 8 tries so that a waiting warp issues
+// few instructions.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(bar, parity)) return true;
     if (globaltimer_ns() - t0 > limit_ns) return false;
   }
-  return true;
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start its

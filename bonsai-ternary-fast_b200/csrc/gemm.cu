@@ -36,8 +36,15 @@ constexpr int kTileM = 128;
 constexpr int kTileN = 64;
 constexpr int kChunk = 128;          // K columns per pipeline chunk (one scale block)
 constexpr int kStepsPerChunk = 4;    // 32-column MMA steps per chunk
-constexpr int kStagesA = 4;          // A / B / d stages (chunks)
-constexpr int kStagesP = 2;          // panel stages (slices of 1024 columns)
+#ifndef BTF_GEMM_STAGES
+#define BTF_GEMM_STAGES 8
+#endif
+#ifndef BTF_GEMM_RASTER_M
+#define BTF_GEMM_RASTER_M 1
+#endif
+constexpr int kStagesA = BTF_GEMM_STAGES;  // A / B stages (chunks): freed by the MMA alone
+constexpr int kStagesS = 8;          // weight-scale stages (freed by the epilogue)
+constexpr int kPrefetch = 4;         // chunks of weight codes the expanders hold in registers
 constexpr int kDRegions = 8;         // TMEM accumulator regions (one per in-flight step)
 constexpr int kTmemCols = kDRegions * kTileN;  // 512: all of TMEM
 constexpr int kEpiWarps = 16;        // 4 per SMSP: TMEM-load latency of one hides behind the others' math
@@ -48,17 +55,14 @@ constexpr uint64_t kGemmWaitNs = 1000000000ull;
 
 constexpr int kABytes = kTileM * kChunk;                  // 16 KB
 constexpr int kBBytes = kTileN * kChunk;                  // 8 KB
-constexpr int kPBytes = (kTileN / kRows) * kPanelBytes;   // 8 panels = 17408 B
 constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStagesA * kABytes;          // 65536
-constexpr int kOffP = kOffB + kStagesA * kBBytes;          // 98304
-constexpr int kOffD = kOffP + kStagesP * kPBytes;          // 133120
-constexpr int kDBytes = kTileM * 4 * 4;                    // d of one chunk: [128 rows][4 steps] fp32
-constexpr int kOffS = kOffD + kStagesA * kDBytes;          // d: [stage][128][4] floats (TMA)
-constexpr int kOffBar = kOffS + kStagesA * kTileN * 4;     // s: [stage][64] floats
-constexpr int kNumBars = 4 * kStagesA + 2 * kStagesP + 2 * kDRegions + 4;
+constexpr int kOffB = kOffA + kStagesA * kABytes;
+constexpr int kOffS = kOffB + kStagesA * kBBytes;          // s: [stage][64] fp32 weight scales
+constexpr int kOffBar = kOffS + kStagesS * kTileN * 4;
+constexpr int kNumBars = 3 * kStagesA + 2 * kStagesS + 2 * kDRegions + 4;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;      // + slack for 1024-B alignment
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 struct GemmParams {
   const uint8_t* pan;  // weight panels of an [N][K] matrix
@@ -96,21 +100,9 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// 32 lanes x 32 columns of 32-bit TMEM -> 32 registers per thread.
-__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(addr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-// 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread.
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+// 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread, without the
+// wait: the registers are valid only after tmem_wait16 on the same array.
+__device__ __forceinline__ void tmem_ld16_async(uint32_t addr, uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
       "%15}, [%16];"
@@ -118,7 +110,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(addr)
       : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// The wait names the destination registers as read-write operands, so the
+// compiler orders every use of them after it.
+__device__ __forceinline__ void tmem_wait16(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -133,26 +133,29 @@ __device__ __forceinline__ uint32_t codes_to_trits(uint32_t c) {
   return ((c | 0x80808080u) - 0x01010101u) ^ 0x80808080u;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base (SW128 atoms and TMA destinations)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#if BTF_GEMM_RASTER_M
+  // the M tiles of one N tile run side by side: they share its weight codes in L2
+  const int n0 = blockIdx.y * kTileN, m0 = blockIdx.x * kTileM;
+#else
   const int n0 = blockIdx.x * kTileN, m0 = blockIdx.y * kTileM;
+#endif
   const int nchunks = p.K / kChunk;
 
   const uint32_t bar0 = sbase + kOffBar;
   auto a_full = [&](int s) { return bar0 + (0 * kStagesA + s) * 8; };
   auto ab_empty = [&](int s) { return bar0 + (1 * kStagesA + s) * 8; };
   auto b_full = [&](int s) { return bar0 + (2 * kStagesA + s) * 8; };
-  auto dsf_empty = [&](int s) { return bar0 + (3 * kStagesA + s) * 8; };
-  auto p_full = [&](int s) { return bar0 + (4 * kStagesA + s) * 8; };
-  auto p_empty = [&](int s) { return bar0 + (4 * kStagesA + kStagesP + s) * 8; };
-  auto mma_done = [&](int r) { return bar0 + (4 * kStagesA + 2 * kStagesP + r) * 8; };
-  auto d_free = [&](int r) { return bar0 + (4 * kStagesA + 2 * kStagesP + kDRegions + r) * 8; };
-  const uint32_t final_bar = bar0 + (4 * kStagesA + 2 * kStagesP + 2 * kDRegions) * 8;
+  auto s_full = [&](int s) { return bar0 + (3 * kStagesA + s) * 8; };
+  auto s_empty = [&](int s) { return bar0 + (3 * kStagesA + kStagesS + s) * 8; };
+  auto mma_done = [&](int r) { return bar0 + (3 * kStagesA + 2 * kStagesS + r) * 8; };
+  auto d_free = [&](int r) { return bar0 + (3 * kStagesA + 2 * kStagesS + kDRegions + r) * 8; };
+  const uint32_t final_bar = bar0 + (3 * kStagesA + 2 * kStagesS + 2 * kDRegions) * 8;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
@@ -161,11 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(a_full(s), 1);
       mbar_init(ab_empty(s), 1);
       mbar_init(b_full(s), 4);
-      mbar_init(dsf_empty(s), kEpiWarps);
     }
-    for (int s = 0; s < kStagesP; ++s) {
-      mbar_init(p_full(s), 1);
-      mbar_init(p_empty(s), 4);
+    for (int s = 0; s < kStagesS; ++s) {
+      mbar_init(s_full(s), 4);
+      mbar_init(s_empty(s), kEpiWarps);
     }
     for (int r = 0; r < kDRegions; ++r) {
       mbar_init(mma_done(r), 1);
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {  // TMEM: 256 columns (4 regions x 64) for this CTA
+  if (warp == 1) {  // TMEM: all 512 columns (8 regions x 64) for this CTA
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"((uint32_t)kTmemCols)
                  : "memory");
@@ -199,40 +201,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const int G = (int)groups_of(p.N);
-      const int g0 = n0 / kRows;
       int issued = 0;
       pdl_wait();  // the activation tile is written by the previous kernel
       for (int c = 0; c < nchunks; ++c) {
-        if (c % 8 == 0) {  // a new slice: the 8 panels of this tile's row groups
-          const int j = c / 8, ps = j % kStagesP;
-          if (j >= kStagesP && !wait(p_empty(ps), (uint32_t)((j / kStagesP - 1) & 1))) break;
-          int ng = min(kTileN / kRows, G - g0);
-          mbar_expect_tx(p_full(ps), (uint32_t)(ng * kPanelBytes));
-          for (int gi = 0; gi < ng; ++gi)
-            bulk_g2s(sbase + kOffP + ps * kPBytes + gi * kPanelBytes,
-                     p.pan + ((int64_t)(g0 + gi) * p.S + j) * kPanelBytes, kPanelBytes, p_full(ps));
-        }
         const int s = c % kStagesA;
-        if (c >= kStagesA) {
-          // the slot's A (MMA) and d (epilogue) must both have been consumed:
-          // this also keeps every a_full waiter within one phase of the barrier
-          const uint32_t ph = (uint32_t)((c / kStagesA - 1) & 1);
-          if (!wait(ab_empty(s), ph) || !wait(dsf_empty(s), ph)) break;
-        }
-        mbar_expect_tx(a_full(s), kABytes + kDBytes);
+        if (c >= kStagesA && !wait(ab_empty(s), (uint32_t)((c / kStagesA - 1) & 1))) break;
+        mbar_expect_tx(a_full(s), kABytes);
         tma_load_2d(sbase + kOffA + s * kABytes, &tmA, c * kChunk, m0, a_full(s));
-        tma_load_2d(sbase + kOffD + s * kDBytes, &tmD, c * kStepsPerChunk, m0, a_full(s));
         issued = c + 1;
       }
-      if (*abort_flag) {
-        // leave no copy in flight into this CTA's shared memory (bounded)
+      if (*abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
         for (int c = max(0, issued - kStagesA); c < issued; ++c)
           mbar_wait_bounded(a_full(c % kStagesA), (uint32_t)((c / kStagesA) & 1), kGemmWaitNs / 10);
-        const int js = issued > 0 ? (issued - 1) / 8 : -1;
-        for (int j = max(0, js - kStagesP + 1); j <= js; ++j)
-          mbar_wait_bounded(p_full(j % kStagesP), (uint32_t)((j / kStagesP) & 1), kGemmWaitNs / 10);
-      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -263,23 +243,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kEpiWarp0) {
     // ------------------------------------------------------------ code expanders
+    // Thread e owns one row quad (4 rows) x 16 columns of every chunk: the
+    // 16-byte quad word at panel offset h*1024 + v*512 + (4b + t/2)*16 (b = chunk
+    // within its 1024-column slice). The words are read from global memory
+    // kPrefetch chunks ahead into registers; threads e < 64 also fetch the fp16
+    // block scale of tile row e.
     const int e = threadIdx.x - kExpWarp0 * 32;  // 0..127
     const int G = (int)groups_of(p.N);
     const int g0 = n0 / kRows;
-    for (int c = 0; c < nchunks; ++c) {
-      const int j = c / 8, ps = j % kStagesP, b = c % 8, s = c % kStagesA;
-      if (b == 0 && !wait(p_full(ps), (uint32_t)((j / kStagesP) & 1))) break;
-      if (c >= kStagesA) {
-        const uint32_t ph = (uint32_t)((c / kStagesA - 1) & 1);
-        if (!wait(ab_empty(s), ph) || !wait(dsf_empty(s), ph)) break;
-      }
-      const uint8_t* pan = smem + kOffP + ps * kPBytes;
-      // one row quad (4 rows) x 16 columns per thread
-      {
-        const int qd = e >> 3, t = e & 7;  // quad 0..15 of the tile, 16-column chunk 0..7
-        const int gi = qd >> 1, h = qd & 1, v = t & 1, l = b * 4 + (t >> 1);
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (g0 + gi < G) w = *reinterpret_cast<const uint4*>(pan + gi * kPanelBytes + h * 1024 + v * 512 + l * 16);
+    const int qd = e >> 3, t = e & 7;
+    const int gi = qd >> 1, h = qd & 1, v = t & 1;
+    const bool have_codes = g0 + gi < G;
+    const uint8_t* cbase = p.pan + (int64_t)(g0 + min(gi, G - 1 - g0)) * p.S * kPanelBytes + h * 1024 + v * 512 +
+                           (t >> 1) * 16;
+    const int sg = e >> 3, sr = e & 7;  // scale: row group and row of tile row e (e < 64)
+    const bool have_scale = e < kTileN && g0 + sg < G;
+    const uint8_t* sbase_g = p.pan + (int64_t)(g0 + min(sg, G - 1 - g0)) * p.S * kPanelBytes + kCodeBytes + sr * 2;
+    auto code_addr = [&](int c) { return cbase + (int64_t)(c >> 3) * kPanelBytes + (c & 7) * 64; };
+    auto scale_addr = [&](int c) { return sbase_g + (int64_t)(c >> 3) * kPanelBytes + (c & 7) * 16; };
+    uint4 wq[kPrefetch];
+    uint16_t sq[kPrefetch];
+#pragma unroll
+    for (int u = 0; u < kPrefetch; ++u) {
+      wq[u] = (have_codes && u < nchunks) ? ld_nc_v4(code_addr(u)) : make_uint4(0, 0, 0, 0);
+      sq[u] = (have_scale && u < nchunks) ? __ldg(reinterpret_cast<const unsigned short*>(scale_addr(u))) : 0;
+    }
+    bool ok = true;
+    for (int c0 = 0; c0 < nchunks && ok; c0 += kPrefetch) {
+#pragma unroll
+      for (int u = 0; u < kPrefetch; ++u) {
+        const int c = c0 + u;
+        if (c >= nchunks) break;
+        const int s = c % kStagesA, ss = c % kStagesS;
+        if (c >= kStagesA && !wait(ab_empty(s), (uint32_t)((c / kStagesA - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        if (c >= kStagesS && !wait(s_empty(ss), (uint32_t)((c / kStagesS - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        const uint4 w = wq[u];
+        const uint16_t hb = sq[u];
+        if (c + kPrefetch < nchunks) {
+          if (have_codes) wq[u] = ld_nc_v4(code_addr(c + kPrefetch));
+          if (have_scale) sq[u] = __ldg(reinterpret_cast<const unsigned short*>(scale_addr(c + kPrefetch)));
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int n = gi * 8 + h * 4 + k;  // row of the tile
@@ -291,21 +300,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int off = (n >> 3) * 1024 + (n & 7) * 128 + ((t ^ (n & 7)) << 4);
           *reinterpret_cast<uint4*>(smem + kOffB + s * kBBytes + off) = o;
         }
-      }
-      if (e < kTileN) {  // fp32 weight scale of row e for this 128-column block
-        const int gi = e >> 3, r = e & 7;
-        float sc = 0.0f;
-        if (g0 + gi < G) {
-          const uint16_t hb = *reinterpret_cast<const uint16_t*>(pan + gi * kPanelBytes + kCodeBytes + b * 16 + r * 2);
-          sc = __half2float(__ushort_as_half(hb));
+        if (e < kTileN)
+          reinterpret_cast<float*>(smem + kOffS)[ss * kTileN + e] = __half2float(__ushort_as_half(hb));
+        fence_proxy_async_smem();  // generic writes of B -> visible to the tensor core (async proxy)
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(b_full(s));
+          mbar_arrive(s_full(ss));
         }
-        reinterpret_cast<float*>(smem + kOffS)[s * kTileN + e] = sc;
-      }
-      fence_proxy_async_smem();  // generic writes of B -> visible to the tensor core (async proxy)
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(b_full(s));
-        if (b == 7 || c == nchunks - 1) mbar_arrive(p_empty(ps));
       }
     }
   } else {
@@ -318,13 +320,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < H; ++i) acc[i] = tsum[i] = make_float2(0.f, 0.f);
     const float2 nmagic = make_float2(-kMagicFloat, -kMagicFloat);
+    // activation scales of this row, [K/32] fp32, read from global memory one
+    // chunk ahead (rows beyond M read row M-1: their sums are never stored)
+    pdl_wait();  // d is written by the previous kernel; y is read (BTF_ADD) and written below
+    const float4* drow = reinterpret_cast<const float4*>(p.d + (int64_t)min(m0 + m, p.M - 1) * (p.K / 32));
+    float4 dnext = __ldg(drow);
+    auto step_math = [&](const uint32_t (&dr)[16], float dk) {
+      const float2 d2 = make_float2(dk, dk);
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        const float2 f = __fadd2_rn(
+            make_float2(__int_as_float((int)dr[2 * i] + kMagicInt), __int_as_float((int)dr[2 * i + 1] + kMagicInt)),
+            nmagic);
+        tsum[i] = __ffma2_rn(d2, f, tsum[i]);
+      }
+    };
     bool ok = true;
     for (int c = 0; c < nchunks && ok; ++c) {
-      const int s = c % kStagesA;
-      const uint32_t ph = (uint32_t)((c / kStagesA) & 1);
-      if (!wait(b_full(s), ph) || !wait(a_full(s), ph)) break;  // scales (expanders) and d (TMA with A)
-      const float4 dv = reinterpret_cast<const float4*>(smem + kOffD)[s * kTileM + m];
+      const int ss = c % kStagesS;
+      const float4 dv = dnext;
+      if (c + 1 < nchunks) dnext = __ldg(drow + c + 1);
       const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
+      uint32_t dr[2][kEpiCols];
+      // step ks: load its accumulator while the previous step's math runs
 #pragma unroll
       for (int ks = 0; ks < kStepsPerChunk; ++ks) {
         const int gks = c * kStepsPerChunk + ks, r = gks % kDRegions;
@@ -333,22 +351,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        uint32_t dr[kEpiCols];
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + r * kTileN + cg * kEpiCols, dr);
+        tmem_ld16_async(tmem_base + ((uint32_t)(q * 32) << 16) + r * kTileN + cg * kEpiCols, dr[ks & 1]);
+        if (ks > 0) step_math(dr[(ks - 1) & 1], dk[ks - 1]);
+        tmem_wait16(dr[ks & 1]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(d_free(r));
-        const float2 d2 = make_float2(dk[ks], dk[ks]);
-#pragma unroll
-        for (int i = 0; i < H; ++i) {
-          const float2 f = __fadd2_rn(make_float2(__int_as_float((int)dr[2 * i] + kMagicInt),
-                                                  __int_as_float((int)dr[2 * i + 1] + kMagicInt)),
-                                      nmagic);
-          tsum[i] = __ffma2_rn(d2, f, tsum[i]);
-        }
       }
       if (!ok) break;
-      const float* sc = reinterpret_cast<const float*>(smem + kOffS) + s * kTileN + cg * kEpiCols;
+      step_math(dr[(kStepsPerChunk - 1) & 1], dk[kStepsPerChunk - 1]);
+      if (!wait(s_full(ss), (uint32_t)((c / kStagesS) & 1))) break;
+      const float* sc = reinterpret_cast<const float*>(smem + kOffS) + ss * kTileN + cg * kEpiCols;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         const float2 s2 = make_float2(sc[2 * i], sc[2 * i + 1]);
@@ -356,9 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tsum[i] = make_float2(0.f, 0.f);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(dsf_empty(s));
+      if (lane == 0) mbar_arrive(s_empty(ss));
     }
-    pdl_wait();  // y may be read (BTF_ADD) and is written: the previous kernel must be done
     if (ok && !*abort_flag && m0 + m < p.M) {
       float* yr = p.y + (int64_t)(m0 + m) * p.ldy + n0 + cg * kEpiCols;
 #pragma unroll
@@ -427,15 +439,6 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(BTF_ERR_ARG, "btf_gemm: tensor map encoding failed (%d)", (int)r);
-  // activation block scales: fp32 [M][K/32], box 4 steps x 128 rows, rows beyond M read as zero
-  CUtensorMap dmap;
-  const cuuint64_t ddims[2] = {(cuuint64_t)(K / 32), (cuuint64_t)M};
-  const cuuint64_t dstrides[1] = {(cuuint64_t)(K / 32) * 4};
-  const cuuint32_t dbox[2] = {(cuuint32_t)kStepsPerChunk, (cuuint32_t)kTileM};
-  const CUresult r2 = enc(&dmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(act.d), ddims, dstrides, dbox,
-                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r2 != CUDA_SUCCESS) return fail(BTF_ERR_ARG, "btf_gemm: scale tensor map encoding failed (%d)", (int)r2);
   GemmParams p{};
   p.pan = static_cast<const uint8_t*>(seg.panels);
   p.N = seg.N;
@@ -447,8 +450,12 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
   p.d = act.d;
   p.mode = mode;
   p.err = dev->err_word;
+#if BTF_GEMM_RASTER_M
+  const dim3 grid((M + kTileM - 1) / kTileM, (seg.N + kTileN - 1) / kTileN);
+#else
   const dim3 grid((seg.N + kTileN - 1) / kTileN, (M + kTileM - 1) / kTileM);
-  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, map, dmap, p);
+#endif
+  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, map, p);
   return e == cudaSuccess ? launch_status("gemm_kernel") : cuda_fail(e, "gemm_kernel launch");
 }
 
