@@ -16,7 +16,7 @@ e2e    = same metric through the same C-ABI calls with the step's activation
          inputs copied from pinned host memory and its outputs copied back,
          inside the timed region.
 With --gpus N > 1 (torchrun), every matrix is N-sharded by rows across the
-ranks (whole 16-row groups) and each GEMV's output is all-gathered over NCCL;
+ranks (whole 8-row groups, shard.shard_rows) and each GEMV's output is all-gathered over NCCL;
 the total work is fixed, so scaling is "strong".
 
 --impl reference times the reference's own CPU GEMV (oracle/_ref, built from
@@ -167,22 +167,20 @@ class Model:
     """64 layers of resident panel weights (this rank's row shard of each matrix)."""
 
     def __init__(self, btf, torch, dev, rank, world):
+        import shard
+
         self.shapes = {name: (K, N) for name, K, N in synth.LAYER_SHAPES}
-        self.rows = {}
-        for name, (K, N) in self.shapes.items():
-            per = N // world
-            assert per % 16 == 0, (name, N, world)
-            self.rows[name] = (rank * per, per)
+        self.rows = {name: shard.shard_rows(N, world, rank) for name, (K, N) in self.shapes.items()}
         self.layers = []
         src = {}
         for name, (K, N) in self.shapes.items():
-            r0, n = self.rows[name]
+            r = self.rows[name]
             full = synth.ternary_ptq(N, K, seed=0)
-            src[name] = torch.from_numpy(np.ascontiguousarray(full[r0:r0 + n])).to(dev)
+            src[name] = torch.from_numpy(np.ascontiguousarray(full[r.r0:r.r0 + r.n])).to(dev)
         for _ in range(N_LAYERS):
             layer = {}
             for name, (K, N) in self.shapes.items():
-                layer[name] = btf.repack_panels(src[name], self.rows[name][1], K)
+                layer[name] = btf.repack_panels(src[name], self.rows[name].n, K)
             self.layers.append(layer)
         torch.cuda.synchronize()
         del src
@@ -193,6 +191,7 @@ def gpu_arm(args):
     import torch.distributed as dist
 
     import btf_b200 as btf
+    import shard
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -213,14 +212,14 @@ def gpu_arm(args):
     x_in = {"attn": xs[5120], "o": xs[6144], "ffn": xs[5120].clone(), "down": xs[17408]}
     acts = {k: btf.Q8Act.empty(1, sh_k, dev) for k, sh_k in (("attn", 5120), ("o", 6144), ("ffn", 5120),
                                                               ("down", 17408))}
-    full_out = {n: torch.zeros((1, N), device=dev) for n, (K, N) in sh.items() if n != "up"}
-    loc_out = {n: torch.zeros((1, model.rows[n][1]), device=dev) for n in full_out}
+    full_out = {n: torch.zeros((1, model.rows[n].per * world), device=dev) for n in sh if n != "up"}
+    loc_out = {n: torch.zeros((1, model.rows[n].per), device=dev) for n in full_out}
 
     stream = torch.cuda.Stream(device=dev)
 
     def gather(name):
         if world > 1:
-            dist.all_gather_into_tensor(full_out[name].view(-1), loc_out[name].view(-1))
+            shard.all_gather_rows(loc_out[name], full_out[name])
 
     # per-kernel timing events around the launches of the last layer of a step
     kinds = ("qkv", "o", "gateup", "down")
@@ -246,7 +245,7 @@ def gpu_arm(args):
                 btf.launch_gemv(segs, K, 1, acts[xk], mode, stream)
 
         def seg(n):
-            return (L[n], loc_out[n], loc_out[n].shape[1])
+            return (L[n], loc_out[n], model.rows[n].per)
 
         t0("qkv")
         gemv([seg("q"), seg("k"), seg("v")], 5120, "attn", btf.STORE)
@@ -499,7 +498,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm"], help="profile mode: one kernel kind")
     ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--fused", type=int, default=1)
+    ap.add_argument("--fused", type=int, default=0, help="--only: 1 = btf_gemv_f32 (quantise inside the GEMV)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

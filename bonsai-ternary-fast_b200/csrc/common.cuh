@@ -140,6 +140,32 @@ __device__ __forceinline__ uint32_t q8_quad(float4 v, float& dq, int& sum) {
          ((uint32_t)(q3 & 0xff) << 24);
 }
 
+// Same rule with one thread holding a whole 32-value block (v[k] = values
+// 4k..4k+3): the per-block division and fp16 rounding run once per block.
+// Returns the 32 q as int8 in qa (values 0..15) and qb (values 16..31).
+__device__ __forceinline__ void q8_block32(const float4 (&v)[8], uint4& qa, uint4& qb, float& dq, int& sum) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+  const float amax_signed = amax == 0.0f ? v[7].w : amax;  // element 31 of the block
+  dq = __half2float(__float2half_rn(__fdiv_rn(amax_signed, 127.0f)));
+  const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  uint32_t w[8];
+  int s = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int q0 = __float2int_rn(__fmul_rn(v[k].x, id)), q1 = __float2int_rn(__fmul_rn(v[k].y, id));
+    const int q2 = __float2int_rn(__fmul_rn(v[k].z, id)), q3 = __float2int_rn(__fmul_rn(v[k].w, id));
+    s += q0 + q1 + q2 + q3;
+    w[k] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+           ((uint32_t)(q3 & 0xff) << 24);
+  }
+  qa = make_uint4(w[0], w[1], w[2], w[3]);
+  qb = make_uint4(w[4], w[5], w[6], w[7]);
+  sum = s;
+}
+
 // Loads 4 consecutive floats (vector load when 16-byte aligned).
 __device__ __forceinline__ float4 load4(const float* p, bool vec) {
   if (vec) return *reinterpret_cast<const float4*>(p);
@@ -226,6 +252,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Thread-block clusters (distributed shared memory). The barriers are the
+// hardware cluster barrier: every thread of every CTA of the cluster executes
+// each arrive/wait pair exactly once, unconditionally.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_b32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // Device-side error word (time-outs of bounded waits); read by btf_device_error().
 constexpr int kErrWaitTimeout = 1;
 
@@ -243,6 +301,27 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// launch_pdl with a thread-block cluster of `cluster` CTAs along x (1 = none).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               int cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 

@@ -63,6 +63,30 @@ constexpr int kMaxNb = 4;                                  // activation rows pe
 constexpr uint64_t kWaitLimitNs = 1000000000ull;           // 1 s per bounded wait
 constexpr size_t kSmemTarget = BTF_GEMV_SMEM_KB * 1024;    // ring + activation budget per CTA
 constexpr int kGridCtasPerSm = BTF_GEMV_GRID_CTAS;         // persistent CTAs per SM launched (<= resident)
+#ifndef BTF_GEMV_BALANCED
+#define BTF_GEMV_BALANCED 1
+#endif
+constexpr bool kBalancedGrid = BTF_GEMV_BALANCED;
+
+#ifndef BTF_GEMV_FUSE_CLUSTER
+#define BTF_GEMV_FUSE_CLUSTER 4
+#endif
+// btf_gemv_f32: CTAs per cluster that share the quantisation of the activation
+// (each quantises 1/kFuseCluster of it into every CTA's shared memory)
+constexpr int kFuseCluster = BTF_GEMV_FUSE_CLUSTER;
+#ifndef BTF_GEMV_RING_AFTER_STAGE
+#define BTF_GEMV_RING_AFTER_STAGE 0
+#endif
+// cluster path: start the weight ring only once the activation is quantised
+constexpr bool kRingAfterStage = BTF_GEMV_RING_AFTER_STAGE;
+static_assert(kFuseCluster == 1 || kFuseCluster == 2 || kFuseCluster == 4 || kFuseCluster == 8, "cluster size");
+#ifndef BTF_GEMV_FUSE_QUAD
+#define BTF_GEMV_FUSE_QUAD 0
+#endif
+#ifndef BTF_GEMV_PREWAIT
+#define BTF_GEMV_PREWAIT 2
+#endif
+constexpr int kPrewaitPanels = BTF_GEMV_PREWAIT;           // panels per warp copied before griddepcontrol.wait
 // 512-thread builds raised an illegal-address fault in the bench on B200 whose
 // cause was not found (a CPU replay of every index stayed in bounds); only
 // 128- and 256-thread CTAs are built.
@@ -157,7 +181,9 @@ struct SmemPlan {
 template <int NB, int MODE, bool FUSE>
 __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
+  constexpr bool kCluster = FUSE && kFuseCluster > 1;
   extern __shared__ __align__(128) uint8_t smem[];
+  if constexpr (kCluster) cluster_arrive_relaxed();  // matched by the wait before the first remote store
   const int S = p.S;
   const int nsp = S * kSubPerSlice;  // sub-blocks incl. padding to whole slices
   const SmemPlan plan(MODE, NB, S, p.slots);
@@ -238,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
   if (lane == 0 && n_panels > 0) {
     unit_src(0);
     issue_next();
+    while (is_count < kPrewaitPanels && is_count < depth && is_count < n_panels) issue_next();
   }
   pdl_wait();
   // The activation is read next (few KB, L2-resident); the rest of the ring is
@@ -249,6 +276,72 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
 
   // ---- activation -> shared memory (padded to whole slices with q = 0)
   if constexpr (FUSE) {
+#if !BTF_GEMV_FUSE_QUAD
+    // one thread per (row, 32-column block): the per-block division and fp16
+    // rounding run once per block; the next round's loads are in flight while
+    // this round is quantised, and the weight ring starts behind the first loads
+    const bool vec = ((reinterpret_cast<uintptr_t>(p.x) | ((uintptr_t)p.ldx * 4)) & 15) == 0;
+    const int total = NB * nsp;  // (row, block) items incl. padding
+    auto load_blk = [&](int i, float4 (&v)[8]) {
+      const int m = i / nsp, b = i - m * nsp;
+      const bool ok = i < total && m < p.nb && b < p.nsub;
+      const float* src = p.x + (int64_t)(p.m0 + (ok ? m : 0)) * p.ldx + (ok ? b : 0) * 32;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = ok ? load4(src + 4 * k, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    float4 cur[8], nxt[8];
+    if constexpr (kCluster) {
+      // this CTA's share of the (row, block) items, written into the shared
+      // memory of every CTA of the cluster (same offsets: same launch, same plan)
+      const uint32_t rank = cluster_ctarank();
+      const int lo = (int)((int64_t)rank * total / kFuseCluster);
+      const int hi = (int)((int64_t)(rank + 1) * total / kFuseCluster);
+      const int i0 = lo + (int)threadIdx.x;
+      load_blk(i0 < hi ? i0 : total, cur);
+      if (!kRingAfterStage) start_ring();
+      __syncwarp();
+      cluster_wait_acquire();  // every CTA of the cluster is running: remote stores are safe
+      for (int i = i0; i < hi; i += kThreads) {
+        load_blk(i + kThreads < hi ? i + kThreads : total, nxt);
+        uint4 qa, qb;
+        float dq;
+        int sum;
+        q8_block32(cur, qa, qb, dq, sum);
+        const uint32_t aqa = smem_u32(qa_s + i), aqb = smem_u32(qb_s + i);
+        const uint32_t ad = smem_u32(d_s + i), ams = smem_u32(ms_s + i);
+#pragma unroll
+        for (int c = 0; c < kFuseCluster; ++c) {
+          st_cluster_v4(mapa_shared(aqa, c), qa);
+          st_cluster_v4(mapa_shared(aqb, c), qb);
+          st_cluster_b32(mapa_shared(ad, c), __float_as_uint(dq));
+          st_cluster_b32(mapa_shared(ams, c), (uint32_t)(kMagicInt - sum));
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+      }
+      __syncwarp();
+      cluster_arrive_release();  // publish this CTA's stores ...
+      if (kRingAfterStage) start_ring();
+      __syncwarp();
+      cluster_wait_acquire();    // ... and see everyone else's
+    } else {
+      load_blk(threadIdx.x, cur);
+      start_ring();
+      for (int i = threadIdx.x; i < total; i += kThreads) {
+        load_blk(i + kThreads, nxt);
+        uint4 qa, qb;
+        float dq;
+        int sum;
+        q8_block32(cur, qa, qb, dq, sum);
+        qa_s[i] = qa;
+        qb_s[i] = qb;
+        d_s[i] = dq;
+        ms_s[i] = kMagicInt - sum;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+      }
+    }
+#else
     // every thread owns 4 consecutive columns of a row; all loads of a row are
     // issued before any is used (kQuads per thread covers K <= 18432 in one round)
     constexpr int kQuads = 18;
@@ -283,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
       }
     }
     start_ring();
+#endif
   } else {
     // chunks of kStageIters items per thread (one chunk covers K <= 17408 for NB = 1)
     constexpr int kStageIters = (NB * 544 + kThreads - 1) / kThreads;
@@ -560,6 +654,36 @@ int resident_ctas(KernelFn fn, int smem) {
   return n;
 }
 
+// CTAs of `fn` resident at once when launched in clusters of `cluster` CTAs
+// (whole clusters only; capped at kGridCtasPerSm per SM), cached per (kernel, smem).
+int resident_cluster_ctas(KernelFn fn, int smem, int cluster, cudaStream_t st) {
+  struct Entry { KernelFn fn; int smem; int n; };
+  static Entry cache[64];
+  static int used = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].smem == smem) return cache[i].n;
+  const DeviceInfo* dev = current_device();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) != cudaSuccess) clusters = 0;
+  int n = std::min(clusters * cluster, dev ? dev->sm_count * kGridCtasPerSm : clusters * cluster);
+  if (used < 64) cache[used++] = Entry{fn, smem, n};
+  return n;
+}
+
 // Launches the GEMV over M rows in passes of at most kMaxNb activation rows.
 int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* act, const float* x, int ldx,
              int mode, cudaStream_t st) {
@@ -610,9 +734,16 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
     p.m0 = m0;
     p.nb = nb;
     const KernelFn fn = pick(NB, mode, x != nullptr);
-    const int per_sm = resident_ctas(fn, plan.total);
-    const int grid = std::max(1, std::min(p.utotal, dev->sm_count * per_sm));
-    const cudaError_t e = launch_pdl(fn, dim3(grid), dim3(kThreads), (size_t)plan.total, st, p);
+    const int cluster = x != nullptr ? kFuseCluster : 1;
+    const int resident = cluster > 1 ? resident_cluster_ctas(fn, plan.total, cluster, st)
+                                     : dev->sm_count * resident_ctas(fn, plan.total);
+    if (resident < cluster) return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_f32: no cluster of %d CTAs fits", cluster);
+    // every CTA gets ceil(utotal / resident CTAs) units, or fewer; whole clusters
+    const int cap = std::max(1, std::min(p.utotal, resident));
+    const int upc = (p.utotal + cap - 1) / cap;
+    int grid = kBalancedGrid ? (p.utotal + upc - 1) / upc : cap;
+    grid = std::min((grid + cluster - 1) / cluster * cluster, resident / cluster * cluster);
+    const cudaError_t e = launch_pdl_cluster(fn, dim3(grid), dim3(kThreads), (size_t)plan.total, st, cluster, p);
     if (e != cudaSuccess) return cuda_fail(e, "gemv_kernel launch");
     if (int rc = launch_status("gemv_kernel")) return rc;
   }
