@@ -212,14 +212,22 @@ def gpu_arm(args):
     x_in = {"attn": xs[5120], "o": xs[6144], "ffn": xs[5120].clone(), "down": xs[17408]}
     acts = {k: btf.Q8Act.empty(1, sh_k, dev) for k, sh_k in (("attn", 5120), ("o", 6144), ("ffn", 5120),
                                                               ("down", 17408))}
-    full_out = {n: torch.zeros((1, model.rows[n].per * world), device=dev) for n in sh if n != "up"}
-    loc_out = {n: torch.zeros((1, model.rows[n].per), device=dev) for n in full_out}
+    # full-width outputs; with N > 1 they live in a GatherArena: each rank's GEMV
+    # stores its rows into every rank's copy over NVLink (btf_gemv_gather)
+    outs = [n for n in sh if n != "up"]
+    arena = None
+    if world > 1:
+        arena = shard.GatherArena(btf, sum(4 * sh[n][1] + 256 for n in outs), world, rank, dev)
+        offs, full_out = {}, {}
+        for n in outs:
+            offs[n], full_out[n] = arena.buffer((1, sh[n][1]))
+        gdesc = {kind: arena.gather_desc([offs[n] + 4 * model.rows[n].r0 for n in names])
+                 for kind, names in (("qkv", ("q", "k", "v")), ("o", ("o",)), ("gateup", ("gate",)),
+                                     ("down", ("down",)))}
+    else:
+        full_out = {n: torch.zeros((1, sh[n][1]), device=dev) for n in outs}
 
     stream = torch.cuda.Stream(device=dev)
-
-    def gather(name):
-        if world > 1:
-            shard.all_gather_rows(loc_out[name], full_out[name])
 
     # per-kernel timing events around the launches of the last layer of a step
     kinds = ("qkv", "o", "gateup", "down")
@@ -237,33 +245,32 @@ def gpu_arm(args):
             if timed:
                 evs[k][1].record(stream)
 
-        def gemv(segs, K, xk, mode):
-            if fused:
+        def gemv(segs, K, xk, mode, kind):
+            if world > 1:  # drop-in pair with the all-gather in the GEMV epilogue
+                btf.quant_q8(x_in[xk], acts[xk], stream=stream)
+                btf.launch_gemv_gather(segs, K, 1, acts[xk], mode, gdesc[kind], stream)
+            elif fused:
                 btf.launch_gemv_f32(segs, K, 1, x_in[xk], mode, stream)
             else:
                 btf.quant_q8(x_in[xk], acts[xk], stream=stream)
                 btf.launch_gemv(segs, K, 1, acts[xk], mode, stream)
 
         def seg(n):
-            return (L[n], loc_out[n], model.rows[n].per)
+            r = model.rows[n]
+            return (L[n], full_out[n][:, r.r0:], sh[n][1])
 
         t0("qkv")
-        gemv([seg("q"), seg("k"), seg("v")], 5120, "attn", btf.STORE)
+        gemv([seg("q"), seg("k"), seg("v")], 5120, "attn", btf.STORE, "qkv")
         t1("qkv")
-        for n in ("q", "k", "v"):
-            gather(n)
         t0("o")
-        gemv([seg("o")], 6144, "o", btf.ADD)
+        gemv([seg("o")], 6144, "o", btf.ADD, "o")
         t1("o")
-        gather("o")
         t0("gateup")
-        gemv([seg("gate"), (L["up"], None, 0)], 5120, "ffn", btf.SWIGLU)
+        gemv([seg("gate"), (L["up"], None, 0)], 5120, "ffn", btf.SWIGLU, "gateup")
         t1("gateup")
-        gather("gate")
         t0("down")
-        gemv([seg("down")], 17408, "down", btf.ADD)
+        gemv([seg("down")], 17408, "down", btf.ADD, "down")
         t1("down")
-        gather("down")
 
     def step(fused=False):
         for i, L in enumerate(model.layers):
@@ -278,7 +285,7 @@ def gpu_arm(args):
             x_in[k].copy_(h_in[k], non_blocking=True)
         step()
         for k in full_out:
-            h_out[k].copy_(full_out[k] if world > 1 else loc_out[k], non_blocking=True)
+            h_out[k].copy_(full_out[k], non_blocking=True)
 
     h2d = sum(v.numel() * 4 for v in h_in.values())
     d2h = sum(v.numel() * 4 for v in h_out.values())
@@ -295,8 +302,9 @@ def gpu_arm(args):
         step()
     with torch.cuda.graph(g_e2e, stream=stream):
         step_e2e()
-    with torch.cuda.graph(g_unf, stream=stream):
-        step(fused=True)
+    if world == 1:  # with N > 1 the step always runs the gathering pairs
+        with torch.cuda.graph(g_unf, stream=stream):
+            step(fused=True)
     torch.cuda.synchronize()
 
     def timed(graph, K, W):
@@ -331,7 +339,7 @@ def gpu_arm(args):
     clocks.stop()
     kern_ms = {k: evs[k][0].elapsed_time(evs[k][1]) for k in kinds}
     ms_e2e = timed(g_e2e, args.steps, args.warmup)
-    ms_unf = timed(g_unf, args.steps, args.warmup)
+    ms_unf = timed(g_unf, args.steps, args.warmup) if world == 1 else None
     dev_err = btf.device_error()
 
     # algorithmic bytes (whole job: every matrix counted once)
@@ -351,7 +359,7 @@ def gpu_arm(args):
     step_bytes = layer_bytes * N_LAYERS
     value = step_bytes * args.steps / (ms_dev * 1e-3) / 1e9
     e2e = step_bytes * args.steps / (ms_e2e * 1e-3) / 1e9
-    fused_v = step_bytes * args.steps / (ms_unf * 1e-3) / 1e9
+    fused_v = step_bytes * args.steps / (ms_unf * 1e-3) / 1e9 if ms_unf else None
 
     peak, peak_kind = measured_peaks()
     # dominant kernel: the gate/up swiglu GEMV (52 % of the step's bytes); on this rank's shard
@@ -376,7 +384,9 @@ def gpu_arm(args):
                        "shapes": [f"{n}:{K}->{N}" for n, K, N in synth.LAYER_SHAPES],
                        "layers": N_LAYERS, "bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2: 5.8 GB of distinct resident weights per step",
-                       "parallelism": f"N-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "parallelism": f"N-shard x{world}" + (", all-gather fused into the GEMV epilogue (NVLink "
+                                                             "stores + arrival counters, no NCCL in the step)"
+                                                             if world > 1 else ""),
                        "graph": "one CUDA graph per step, programmatic dependent launch between kernels",
                        "path": "drop-in pairs: btf_quant_q8 (launch_prep) + btf_gemv (launch_gemv), PDL-chained"},
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
@@ -384,7 +394,8 @@ def gpu_arm(args):
                          "peak_source": peak_kind},
             "kernels": kernels,
             "fused_quantise_path": {"value": fused_v, "unit": UNIT, "note": "btf_gemv_f32: quantisation inside "
-                                    "each GEMV, 4 launches per layer (same bytes counted)"},
+                                    "each GEMV (4-CTA clusters), 4 launches per layer (same bytes counted)"}
+            if world == 1 else None,
             "device_error_word": dev_err,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * N_LAYERS * 8,
@@ -396,7 +407,10 @@ def gpu_arm(args):
             line["cpu_baseline"] = cpu_reference(host_threads())
         print(json.dumps(line), flush=True)
     if world > 1:
-        del g_dev, g_e2e
+        del g_dev, g_e2e, g_unf
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still stores into another's arena
+        arena.close()
         dist.barrier()
         dist.destroy_process_group()
 

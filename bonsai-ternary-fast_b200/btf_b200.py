@@ -32,6 +32,7 @@ EXPORTS = (
     "btf_panel_bytes", "btf_t2_codes_bytes", "btf_t2_scales_bytes",
     "btf_repack_panels", "btf_repack_panels_host", "btf_repack_t2", "btf_t2_to_panels", "btf_panels_to_t2",
     "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot", "btf_gemm",
+    "btf_gemv_gather", "btf_alloc", "btf_free", "btf_ipc_handle", "btf_ipc_open", "btf_ipc_close",
 )
 
 
@@ -48,6 +49,17 @@ class Q8ActC(ctypes.Structure):
 
 
 _lib: Optional[ctypes.CDLL] = None
+
+
+MAX_RANKS = 8
+
+
+class GatherC(ctypes.Structure):
+    """btf_gather (include/btf_b200.h): N-sharded launch with the all-gather in the epilogue."""
+
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("peer_y", (ctypes.c_void_p * MAX_RANKS) * 3), ("flags", ctypes.c_void_p * MAX_RANKS),
+                ("expect", ctypes.c_void_p), ("done", ctypes.c_void_p)]
 
 
 def lib() -> ctypes.CDLL:
@@ -79,6 +91,12 @@ def lib() -> ctypes.CDLL:
         "btf_device_error": (i32, [i32]),
         "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
         "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
+        "btf_gemv_gather": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, ctypes.POINTER(GatherC), vp]),
+        "btf_alloc": (i32, [ctypes.c_size_t, ctypes.POINTER(vp)]),
+        "btf_free": (i32, [vp]),
+        "btf_ipc_handle": (i32, [vp, ctypes.c_char_p]),
+        "btf_ipc_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]),
+        "btf_ipc_close": (i32, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -264,3 +282,37 @@ def gemv_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):
     out = torch.empty((M, pm.N, pm.K // 32), dtype=torch.int32, device=pm.panels.device)
     check(lib().btf_gemv_idot(_ptr(pm.panels), pm.N, pm.K, M, act.c(), _ptr(out), _stream(stream)), "btf_gemv_idot")
     return out
+
+
+def launch_gemv_gather(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int, gather: GatherC,
+                       stream=None) -> None:
+    """N-sharded launch_gemv whose epilogue all-gathers the outputs over NVLink (btf_gemv_gather)."""
+    check(lib().btf_gemv_gather(_segs(segs), len(segs), K, M, act.c(), mode, ctypes.byref(gather), _stream(stream)),
+          "btf_gemv_gather")
+
+
+def alloc(nbytes: int) -> int:
+    """cudaMalloc on the current device (a buffer whose IPC handle maps exactly it)."""
+    p = ctypes.c_void_p()
+    check(lib().btf_alloc(nbytes, ctypes.byref(p)), "btf_alloc")
+    return p.value
+
+
+def free(ptr: int) -> None:
+    check(lib().btf_free(ptr), "btf_free")
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    check(lib().btf_ipc_handle(ptr, buf), "btf_ipc_handle")
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    p = ctypes.c_void_p()
+    check(lib().btf_ipc_open(handle, ctypes.byref(p)), "btf_ipc_open")
+    return p.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().btf_ipc_close(ptr), "btf_ipc_close")

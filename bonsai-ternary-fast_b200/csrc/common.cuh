@@ -186,7 +186,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 }
 
 // 1-D bulk copy global -> shared (TMA unit), completion counted on `bar`.
-// dst, src and bytes must be multiples of 16. No multicast.
+// dst, src and bytes must be multiples of 16; the copy lands in this CTA only.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)

@@ -1,5 +1,6 @@
 // Library state: error reporting, per-device initialisation, layout sizes.
 #include <cstdarg>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -104,5 +105,44 @@ int64_t btf_panel_bytes(int64_t N, int64_t K) {
 }
 int64_t btf_t2_codes_bytes(int64_t N, int64_t K) { return N * (K / 4); }
 int64_t btf_t2_scales_bytes(int64_t N, int64_t K) { return N * (K / 128) * 2; }
+
+}  // extern "C"
+
+// ---- device buffers shared across processes (CUDA IPC)
+extern "C" {
+
+int btf_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(BTF_ERR_ARG, "btf_alloc: null out pointer or zero size");
+  const cudaError_t e = cudaMalloc(ptr, bytes);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_alloc");
+}
+
+int btf_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_free");
+}
+
+int btf_ipc_handle(void* ptr, void* handle64) {
+  if (!ptr || !handle64) return fail(BTF_ERR_ARG, "btf_ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_ipc_handle");
+  static_assert(sizeof h == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(handle64, &h, sizeof h);
+  return BTF_OK;
+}
+
+int btf_ipc_open(const void* handle64, void** ptr) {
+  if (!handle64 || !ptr) return fail(BTF_ERR_ARG, "btf_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof h);
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_ipc_open");
+}
+
+int btf_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_ipc_close");
+}
 
 }  // extern "C"

@@ -14,7 +14,7 @@
 //     the same number of bytes;
 //   - each of the 8 warps is its own producer: lane 0 keeps a ring of DEPTH
 //     panels (2176 B, 8 rows x 1024 columns + scales; swiglu: gate + up)
-//     filled by 1-D TMA bulk copies (cp.async.bulk, no multicast) on an
+//     filled by 1-D TMA bulk copies (cp.async.bulk, this CTA only) on an
 //     mbarrier per slot; waits are bounded and report a device error word;
 //   - programmatic dependent launch: the weight copies of the first DEPTH
 //     panels are issued before griddepcontrol.wait, i.e. while the previous
@@ -61,6 +61,8 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSeg = 3;
 constexpr int kMaxNb = 4;                                  // activation rows per pass
 constexpr uint64_t kWaitLimitNs = 1000000000ull;           // 1 s per bounded wait
+constexpr uint64_t kGatherWaitNs = 2000000000ull;          // 2 s for the other ranks' arrivals
+
 constexpr size_t kSmemTarget = BTF_GEMV_SMEM_KB * 1024;    // ring + activation budget per CTA
 constexpr int kGridCtasPerSm = BTF_GEMV_GRID_CTAS;         // persistent CTAs per SM launched (<= resident)
 #ifndef BTF_GEMV_BALANCED
@@ -111,6 +113,7 @@ struct GemvParams {
   int ldx;
   int slots;           // ring slots of a CTA, shared by the warps that have work
   int* err;
+  btf_gather gather;   // world == 0: plain launch; else the epilogue all-gathers over NVLink
 };
 
 // Per-row code dots of one row quad over one 32-column sub-block. cw0/cw1:
@@ -178,8 +181,41 @@ struct SmemPlan {
   }
 };
 
+// End of an N-sharded launch: once every CTA of this launch on this rank has
+// made its stores to all ranks visible system-wide, the last one adds 1 to every
+// rank's arrival counter and waits (bounded) until its own counter shows this
+// launch's arrivals from all ranks. Arrivals of a rank's next launch can only
+// come after that rank's wait for this one, so a cumulative count suffices.
+__device__ __noinline__ void gather_arrive(const btf_gather& g, int* err) {
+  // The CTA barrier orders every thread's output stores before thread 0's
+  // acq_rel count below, and the last CTA's release-adds to the other ranks
+  // (system scope) are ordered after all counts.
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  unsigned prev;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(g.done) : "memory");
+  if (prev != gridDim.x - 1) return;
+  *g.done = 0;  // the next launch's CTAs touch it only after this launch completes
+  // release.sys is cumulative: every CTA's stores, ordered before its acq_rel
+  // count and so before this thread, are visible to whoever acquires the add
+  for (int r = 0; r < g.world; ++r)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(g.flags[r]) : "memory");
+  const unsigned target = *g.expect + (unsigned)g.world;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.flags[g.rank]) : "memory");
+    if ((int)(v - target) >= 0) break;
+    if (globaltimer_ns() - t0 > kGatherWaitNs) {
+      atomicCAS(err, 0, kErrWaitTimeout);
+      break;
+    }
+  }
+  *g.expect = target;
+}
+
 template <int NB, int MODE, bool FUSE>
-__global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __grid_constant__ GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
   constexpr bool kCluster = FUSE && kFuseCluster > 1;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -221,6 +257,15 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
   auto locate = [&](int u, int& seg, int& g) {
     seg = kSwi ? 0 : (u >= p.u1) + (u >= p.u2);
     g = u - (seg == 0 ? 0 : seg == 1 ? p.u1 : p.u2);
+  };
+  // Output store: this rank's buffer, or (N-sharded launch) every rank's
+  // buffer over NVLink; the value is the same everywhere.
+  auto put = [&](int seg, float* y, int64_t idx, float val) {
+    if (p.gather.world == 0) {
+      y[idx] = val;
+    } else {
+      for (int r = 0; r < p.gather.world; ++r) p.gather.peer_y[seg][r][idx] = val;
+    }
   };
   // Copy issue state (used by lane 0): next panel's unit, slice, slot and
   // source pointers. A unit's S panels are contiguous, so moving to the next
@@ -541,10 +586,10 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
           } else {
             const int row = g * kRows + row_l;
             if (row < n && m < p.nb) {
-              float* yp = y + (int64_t)(p.m0 + m) * ldy + row;
-              if constexpr (MODE == BTF_STORE) *yp = v[0];
-              else if constexpr (MODE == BTF_ADD) *yp += v[0];
-              else *yp = silu(v[0]) * up;
+              const int64_t idx = (int64_t)(p.m0 + m) * ldy + row;
+              if constexpr (MODE == BTF_STORE) put(seg, y, idx, v[0]);
+              else if constexpr (MODE == BTF_ADD) put(seg, y, idx, y[idx] + v[0]);
+              else put(seg, y, idx, silu(v[0]) * up);
             }
           }
         }
@@ -569,14 +614,15 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const Gem
         }
         const int row = g * kRows + r;
         if (row < n && m < p.nb) {
-          float* yp = y + (int64_t)(p.m0 + m) * ldy + row;
-          if constexpr (MODE == BTF_STORE) *yp = sg;
-          else if constexpr (MODE == BTF_ADD) *yp += sg;
-          else *yp = silu(sg) * su;
+          const int64_t idx = (int64_t)(p.m0 + m) * ldy + row;
+          if constexpr (MODE == BTF_STORE) put(seg, y, idx, sg);
+          else if constexpr (MODE == BTF_ADD) put(seg, y, idx, y[idx] + sg);
+          else put(seg, y, idx, silu(sg) * su);
         }
       }
     }
   }
+  if (p.gather.world > 0) gather_arrive(p.gather, p.err);
 }
 
 // Exact idot dump (parity/debug): one thread per (m, row, sub-block), same
@@ -686,7 +732,7 @@ int resident_cluster_ctas(KernelFn fn, int smem, int cluster, cudaStream_t st) {
 
 // Launches the GEMV over M rows in passes of at most kMaxNb activation rows.
 int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* act, const float* x, int ldx,
-             int mode, cudaStream_t st) {
+             int mode, cudaStream_t st, const btf_gather* gather = nullptr) {
   const DeviceInfo* dev = current_device();
   if (!dev) return BTF_ERR_STATE;
   GemvParams p{};
@@ -719,6 +765,7 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
   p.x = x;
   p.ldx = ldx;
   p.err = dev->err_word;
+  if (gather) p.gather = *gather;
   for (int m0 = 0; m0 < M; m0 += kMaxNb) {
     const int nb = std::min(kMaxNb, M - m0);
     const int NB = nb <= 1 ? 1 : nb <= 2 ? 2 : 4;
@@ -791,6 +838,29 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
   if (!act.q || !act.d || !act.s || !aligned(act.q, 16) || !aligned(act.d, 4) || !aligned(act.s, 4))
     return fail(BTF_ERR_ARG, "btf_gemv: activation pointers null or misaligned (q needs 16 B)");
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream);
+}
+
+int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, const btf_gather* g,
+                    void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (int rc = check_segs("btf_gemv_gather", segs, nseg, K, mode)) return rc;
+  if (!act.q || !act.d || !act.s || !aligned(act.q, 16) || !aligned(act.d, 4) || !aligned(act.s, 4))
+    return fail(BTF_ERR_ARG, "btf_gemv_gather: activation pointers null or misaligned (q needs 16 B)");
+  if (!g || g->world < 2 || g->world > BTF_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+    return fail(BTF_ERR_ARG, "btf_gemv_gather: need 2 <= world <= %d and 0 <= rank < world", BTF_MAX_RANKS);
+  if (!g->expect || !g->done) return fail(BTF_ERR_ARG, "btf_gemv_gather: expect/done counters are null");
+  const int nout = mode == BTF_SWIGLU ? 1 : nseg;  // segments with an output
+  for (int r = 0; r < g->world; ++r) {
+    if (!g->flags[r]) return fail(BTF_ERR_ARG, "btf_gemv_gather: arrival counter of rank %d is null", r);
+    for (int s = 0; s < nout; ++s)
+      if (!g->peer_y[s][r]) return fail(BTF_ERR_ARG, "btf_gemv_gather: peer_y[%d][%d] is null", s, r);
+  }
+  for (int s = 0; s < nout; ++s)
+    if (g->peer_y[s][g->rank] != segs[s].y)
+      return fail(BTF_ERR_ARG, "btf_gemv_gather: peer_y[%d][rank] must be segs[%d].y", s, s);
+  if (M > kMaxNb)
+    return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_gather: M <= %d (one pass; one arrival per launch)", kMaxNb);
+  return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream, g);
 }
 
 int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* x, int ldx, int mode, void* stream) {

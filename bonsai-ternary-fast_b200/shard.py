@@ -94,3 +94,75 @@ def unpad(y_full, N: int):
 def local_widths(Ns: Sequence[int], world: int, align: int = 8):
     """Per-rank slice widths of several matrices."""
     return [shard_rows(N, world, 0, align).per for N in Ns]
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ view of raw device memory (for torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class GatherArena:
+    """Full-width output buffers of N-sharded GEMVs, shared by all ranks.
+
+    Each rank allocates one device buffer (btf_alloc): a 256-byte control block
+    (its arrival counter at +0, its consumed-arrivals counter at +4, its CTA
+    completion counter at +8) followed by the output buffers, laid out the same
+    on every rank. The buffers' IPC handles are exchanged over the default
+    process group, so each process can address every rank's buffer; a sharded
+    GEMV then stores each output value into all of them (btf_gemv_gather).
+    Collective: every rank constructs it with the same `nbytes`."""
+
+    CTL = 256
+
+    def __init__(self, btf, nbytes: int, world: int, rank: int, device):
+        import torch
+        import torch.distributed as dist
+
+        self.btf, self.world, self.rank, self.device = btf, world, rank, device
+        self.nbytes = (nbytes + 255) // 256 * 256
+        self.base = btf.alloc(self.CTL + self.nbytes)
+        torch.as_tensor(_DeviceArray(self.base, ((self.CTL + self.nbytes) // 4,), "<u4"), device=device).zero_()
+        torch.cuda.synchronize(device)
+        handles = [None] * world
+        dist.all_gather_object(handles, btf.ipc_handle(self.base))
+        self.bases = [self.base if r == rank else btf.ipc_open(handles[r]) for r in range(world)]
+        dist.barrier()
+        self._next = 0
+
+    def buffer(self, shape) -> tuple:
+        """Reserves a float32 buffer of `shape`; returns (offset, torch view of this rank's copy)."""
+        import torch
+
+        n = 1
+        for d in shape:
+            n *= d
+        off = self._next
+        self._next = (off + 4 * n + 255) // 256 * 256
+        if self._next > self.nbytes:
+            raise ValueError("GatherArena: out of space")
+        return off, torch.as_tensor(_DeviceArray(self.base + self.CTL + off, shape), device=self.device)
+
+    def gather_desc(self, seg_offsets_bytes):
+        """btf_gather for a launch whose segment s has its y (this rank's first
+        output row, i.e. the buffer offset plus 4 * row0 of this rank's shard) at
+        byte offset seg_offsets_bytes[s] within every rank's output area."""
+        g = self.btf.GatherC()
+        g.world, g.rank = self.world, self.rank
+        for s, off in enumerate(seg_offsets_bytes):
+            for r in range(self.world):
+                g.peer_y[s][r] = self.bases[r] + self.CTL + off
+        for r in range(self.world):
+            g.flags[r] = self.bases[r]
+        g.expect = self.base + 4
+        g.done = self.base + 8
+        return g
+
+    def close(self):
+        for r, b in enumerate(self.bases):
+            if r != self.rank:
+                self.btf.ipc_close(b)
+        self.btf.free(self.base)
+        self.bases = []

@@ -145,6 +145,44 @@ int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
  * scales (src/emu_decoder.cpp:154-157). Same decode path as btf_gemv. */
 int btf_gemv_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
 
+/* ---- N-sharded GEMV with the all-gather fused into the epilogue
+ * The reference is single-GPU (src/cuda/gpu_decoder.cu); this is the B200
+ * build's multi-GPU form of launch_gemv (src/cuda/kernels.cuh:56). Rank r of
+ * `world` holds rows [row0_r, row0_r + n_r) of every matrix and runs
+ * btf_gemv_gather on them with the SAME activation as every other rank. Every
+ * output value is stored into every rank's full output buffer over NVLink
+ * (peer pointers from CUDA IPC; plain stores). The last CTA of the launch on
+ * each rank then adds 1 to every rank's arrival counter (system scope) and
+ * waits, bounded, until its own counter shows all `world` ranks of this
+ * launch, so when the launch completes in stream order the gathered outputs
+ * are complete on this rank. Every rank must make the same sequence of
+ * btf_gemv_gather calls with one arrival counter. A wait that gives up sets the
+ * device error word (btf_device_error). */
+#define BTF_MAX_RANKS 8
+typedef struct btf_gather {
+  int world; /* ranks, 2..BTF_MAX_RANKS */
+  int rank;  /* this rank */
+  /* per segment s: where segs[s].y lies in each rank's output buffer, as mapped
+   * in this process; peer_y[s][rank] must equal segs[s].y */
+  float* peer_y[3][BTF_MAX_RANKS];
+  unsigned int* flags[BTF_MAX_RANKS]; /* each rank's arrival counter, as mapped here */
+  unsigned int* expect;               /* this rank's consumed-arrivals counter (device, starts at 0) */
+  unsigned int* done;                 /* this rank's CTA completion counter (device, starts at 0) */
+} btf_gather;
+int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, const btf_gather* g,
+                    void* stream);
+
+/* Device buffers shared across processes (one process per GPU) through CUDA IPC.
+ * btf_alloc/btf_free: cudaMalloc/cudaFree on the current device (the IPC
+ * handle of a cudaMalloc'd buffer maps exactly that buffer).
+ * btf_ipc_handle: 64-byte handle of a btf_alloc buffer (cudaIpcGetMemHandle).
+ * btf_ipc_open/btf_ipc_close: map / unmap another process's buffer. */
+int btf_alloc(size_t bytes, void** ptr);
+int btf_free(void* ptr);
+int btf_ipc_handle(void* ptr, void* handle64);
+int btf_ipc_open(const void* handle64, void** ptr);
+int btf_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif
