@@ -246,31 +246,28 @@ def gpu_arm(args):
                 evs[k][1].record(stream)
 
         def gemv(segs, K, xk, mode, kind):
+            # timed layer: the events bracket the GEMV launch alone (after its quantiser)
             if world > 1:  # drop-in pair with the all-gather in the GEMV epilogue
                 btf.quant_q8(x_in[xk], acts[xk], stream=stream)
+                t0(kind)
                 btf.launch_gemv_gather(segs, K, 1, acts[xk], mode, gdesc[kind], stream)
             elif fused:
+                t0(kind)
                 btf.launch_gemv_f32(segs, K, 1, x_in[xk], mode, stream)
             else:
                 btf.quant_q8(x_in[xk], acts[xk], stream=stream)
+                t0(kind)
                 btf.launch_gemv(segs, K, 1, acts[xk], mode, stream)
+            t1(kind)
 
         def seg(n):
             r = model.rows[n]
             return (L[n], full_out[n][:, r.r0:], sh[n][1])
 
-        t0("qkv")
         gemv([seg("q"), seg("k"), seg("v")], 5120, "attn", btf.STORE, "qkv")
-        t1("qkv")
-        t0("o")
         gemv([seg("o")], 6144, "o", btf.ADD, "o")
-        t1("o")
-        t0("gateup")
         gemv([seg("gate"), (L["up"], None, 0)], 5120, "ffn", btf.SWIGLU, "gateup")
-        t1("gateup")
-        t0("down")
         gemv([seg("down")], 17408, "down", btf.ADD, "down")
-        t1("down")
 
     def step(fused=False):
         for i, L in enumerate(model.layers):
@@ -361,9 +358,17 @@ def gpu_arm(args):
     e2e = step_bytes * args.steps / (ms_e2e * 1e-3) / 1e9
     fused_v = step_bytes * args.steps / (ms_unf * 1e-3) / 1e9 if ms_unf else None
 
+    # each GEMV launch's own algorithmic bytes (codes + fp16 scales + Q8 activation + fp32 y,
+    # y read too in add mode), for the per-kernel rates and the roofline
+    kernel_bytes = {
+        "qkv": sum(synth.gemv_bytes(sh[n][1], sh[n][0]) for n in ("q", "k", "v")) - 2 * 5120 * 5 // 4,
+        "o": synth.gemv_bytes(sh["o"][1], sh["o"][0], add=True),
+        "gateup": 2 * synth.gemv_bytes(sh["gate"][1], 5120) - 5120 * 5 // 4 - sh["gate"][1] * 4,
+        "down": synth.gemv_bytes(sh["down"][1], sh["down"][0], add=True),
+    }
     peak, peak_kind = measured_peaks()
     # dominant kernel: the gate/up swiglu GEMV (52 % of the step's bytes); on this rank's shard
-    dom_bytes = per_layer["gateup"] / world
+    dom_bytes = kernel_bytes["gateup"] / world
     dom_ach = dom_bytes / (kern_ms["gateup"] * 1e-3) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic_gateup_swiglu.txt")
@@ -371,7 +376,7 @@ def gpu_arm(args):
         for line in open(tpath):
             if line.startswith("dram_bytes_per_launch:"):
                 traffic = int(line.split(":")[1].strip()) // world
-    kernels = {k: {"us": kern_ms[k] * 1e3, "GB/s": (per_layer[k] / world) / (kern_ms[k] * 1e-3) / 1e9}
+    kernels = {k: {"us": kern_ms[k] * 1e3, "GB/s": (kernel_bytes[k] / world) / (kern_ms[k] * 1e-3) / 1e9}
                for k in kinds}
 
     if rank == 0:
@@ -391,6 +396,8 @@ def gpu_arm(args):
                        "path": "drop-in pairs: btf_quant_q8 (launch_prep) + btf_gemv (launch_gemv), PDL-chained"},
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
                          "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,SWIGLU> gate+up",
+                         "bytes_per_launch": dom_bytes, "launch_us": kern_ms["gateup"] * 1e3,
+                         "timing": "CUDA events around the GEMV launch of the last layer of each timed step",
                          "peak_source": peak_kind},
             "kernels": kernels,
             "fused_quantise_path": {"value": fused_v, "unit": UNIT, "note": "btf_gemv_f32: quantisation inside "
