@@ -19,7 +19,9 @@
 //               canonical K-major SW128 layout the MMA reads, and stage the
 //               chunk's activation scales d and fp32 weight scales;
 //   warps 6-21  epilogue: TMEM -> registers (tcgen05.ld 32x32b, 16 columns),
-//               per step T += d * idot, per 128-column block acc += scale * T.
+//               per step T += d * idot, per 128-column block acc += scale * T;
+//               MMA completion and TMEM release are signalled once per chunk
+//               (4 steps), with 2 chunks in flight in TMEM.
 // Every wait is bounded; on a time-out the kernel records an error word, stops
 // issuing work, waits (bounded) for its MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -46,6 +48,7 @@ constexpr int kStagesA = BTF_GEMM_STAGES;  // A / B stages (chunks): freed by th
 constexpr int kStagesS = 8;          // weight-scale stages (freed by the epilogue)
 constexpr int kPrefetch = 4;         // chunks of weight codes the expanders hold in registers
 constexpr int kDRegions = 8;         // TMEM accumulator regions (one per in-flight step)
+constexpr int kChunkSlots = kDRegions / kStepsPerChunk;  // chunks in flight in TMEM (2): one barrier pair each
 constexpr int kTmemCols = kDRegions * kTileN;  // 512: all of TMEM
 constexpr int kEpiWarps = 16;        // 4 per SMSP: TMEM-load latency of one hides behind the others' math
 constexpr int kEpiCols = kTileN * 4 / kEpiWarps;  // columns per epilogue thread (16)
@@ -59,7 +62,7 @@ constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStagesA * kABytes;
 constexpr int kOffS = kOffB + kStagesA * kBBytes;          // s: [stage][64] fp32 weight scales
 constexpr int kOffBar = kOffS + kStagesS * kTileN * 4;
-constexpr int kNumBars = 3 * kStagesA + 2 * kStagesS + 2 * kDRegions + 4;
+constexpr int kNumBars = 3 * kStagesA + 2 * kStagesS + 2 * kChunkSlots + 4;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;      // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -153,9 +156,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   auto b_full = [&](int s) { return bar0 + (2 * kStagesA + s) * 8; };
   auto s_full = [&](int s) { return bar0 + (3 * kStagesA + s) * 8; };
   auto s_empty = [&](int s) { return bar0 + (3 * kStagesA + kStagesS + s) * 8; };
-  auto mma_done = [&](int r) { return bar0 + (3 * kStagesA + 2 * kStagesS + r) * 8; };
-  auto d_free = [&](int r) { return bar0 + (3 * kStagesA + 2 * kStagesS + kDRegions + r) * 8; };
-  const uint32_t final_bar = bar0 + (3 * kStagesA + 2 * kStagesS + 2 * kDRegions) * 8;
+  // per chunk slot cs (TMEM regions 4cs .. 4cs+3): MMAs done / read out by the epilogue
+  auto mma_done = [&](int cs) { return bar0 + (3 * kStagesA + 2 * kStagesS + cs) * 8; };
+  auto d_free = [&](int cs) { return bar0 + (3 * kStagesA + 2 * kStagesS + kChunkSlots + cs) * 8; };
+  const uint32_t final_bar = bar0 + (3 * kStagesA + 2 * kStagesS + 2 * kChunkSlots) * 8;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       mbar_init(s_full(s), 4);
       mbar_init(s_empty(s), kEpiWarps);
     }
-    for (int r = 0; r < kDRegions; ++r) {
+    for (int r = 0; r < kChunkSlots; ++r) {
       mbar_init(mma_done(r), 1);
       mbar_init(d_free(r), kEpiWarps);
     }
@@ -221,22 +225,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int s = c % kStagesA;
         const uint32_t ph = (uint32_t)((c / kStagesA) & 1);
         if (!wait(a_full(s), ph) || !wait(b_full(s), ph)) break;
+        const int cs = c % kChunkSlots;
+        if (c >= kChunkSlots && !wait(d_free(cs), (uint32_t)((c / kChunkSlots - 1) & 1))) break;
         tc_fence_after();
-        bool ok = true;
+#pragma unroll
         for (int ks = 0; ks < kStepsPerChunk; ++ks) {
-          const int gks = c * kStepsPerChunk + ks, r = gks % kDRegions;
-          if (gks >= kDRegions && !wait(d_free(r), (uint32_t)((gks / kDRegions - 1) & 1))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
           const uint64_t ad = smem_desc_sw128(sbase + kOffA + s * kABytes + ks * 32);
           const uint64_t bd = smem_desc_sw128(sbase + kOffB + s * kBBytes + ks * 32);
-          mma_i8(tmem_base + r * kTileN, ad, bd, 0u);
-          mma_commit(mma_done(r));
+          mma_i8(tmem_base + (cs * kStepsPerChunk + ks) * kTileN, ad, bd, 0u);
         }
-        if (!ok) break;
-        mma_commit(ab_empty(s));  // A and B of this chunk are free once its MMAs finish
+        mma_commit(mma_done(cs));  // the chunk's 4 steps (commits track all prior MMAs)
+        mma_commit(ab_empty(s));   // A and B of this chunk are free once its MMAs finish
       }
       mma_commit(final_bar);  // completes when every MMA issued above has finished
       mbar_wait_bounded(final_bar, 0, kGemmWaitNs);
@@ -342,24 +341,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       if (c + 1 < nchunks) dnext = __ldg(drow + c + 1);
       const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
       uint32_t dr[2][kEpiCols];
-      // step ks: load its accumulator while the previous step's math runs
+      // one wait per chunk; step ks + 1 is loaded while step ks's math runs
+      const int cs = c % kChunkSlots;
+      if (!wait(mma_done(cs), (uint32_t)((c / kChunkSlots) & 1))) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + cs * kStepsPerChunk * kTileN + cg * kEpiCols;
+      tmem_ld16_async(taddr, dr[0]);
 #pragma unroll
       for (int ks = 0; ks < kStepsPerChunk; ++ks) {
-        const int gks = c * kStepsPerChunk + ks, r = gks % kDRegions;
-        if (!wait(mma_done(r), (uint32_t)((gks / kDRegions) & 1))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_ld16_async(tmem_base + ((uint32_t)(q * 32) << 16) + r * kTileN + cg * kEpiCols, dr[ks & 1]);
-        if (ks > 0) step_math(dr[(ks - 1) & 1], dk[ks - 1]);
         tmem_wait16(dr[ks & 1]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(d_free(r));
+        if (ks + 1 < kStepsPerChunk) tmem_ld16_async(taddr + (ks + 1) * kTileN, dr[(ks + 1) & 1]);
+        step_math(dr[ks & 1], dk[ks]);
       }
-      if (!ok) break;
-      step_math(dr[(kStepsPerChunk - 1) & 1], dk[kStepsPerChunk - 1]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(d_free(cs));
       if (!wait(s_full(ss), (uint32_t)((c / kStagesS) & 1))) break;
       const float* sc = reinterpret_cast<const float*>(smem + kOffS) + ss * kTileN + cg * kEpiCols;
 #pragma unroll
