@@ -217,13 +217,25 @@ def gpu_arm(args):
     outs = [n for n in sh if n != "up"]
     arena = None
     if world > 1:
-        arena = shard.GatherArena(btf, sum(4 * sh[n][1] + 256 for n in outs), world, rank, dev)
-        offs, full_out = {}, {}
-        for n in outs:
-            offs[n], full_out[n] = arena.buffer((1, sh[n][1]))
-        gdesc = {kind: arena.gather_desc([offs[n] + 4 * model.rows[n].r0 for n in names])
-                 for kind, names in (("qkv", ("q", "k", "v")), ("o", ("o",)), ("gateup", ("gate",)),
-                                     ("down", ("down",)))}
+        # tagged (value, tag) outputs: no counters or waits in the GEMV; one bounded
+        # tag check per layer (btf_gather_wait) over the layer's six outputs
+        # Per-layer output buffers (nothing is stored twice within a step) and one
+        # cross-rank barrier per step (no rank stores into the next step's
+        # buffers before every rank has checked this step's).
+        arena = shard.GatherArena(btf, N_LAYERS * sum(8 * sh[n][1] + 256 for n in outs), world, rank, dev)
+        offs = [{} for _ in range(N_LAYERS)]
+        lay_out = [{} for _ in range(N_LAYERS)]
+        for li in range(N_LAYERS):
+            for n in outs:
+                offs[li][n], lay_out[li][n] = arena.buffer((1, sh[n][1]), tagged=True)
+        full_out = lay_out[N_LAYERS - 1]
+        kind_names = (("qkv", ("q", "k", "v")), ("o", ("o",)), ("gateup", ("gate",)), ("down", ("down",)))
+        gdesc = [{kind: arena.gather_desc([offs[li][n] + 8 * model.rows[n].r0 for n in names], tagged=True,
+                                          site=4 * li + ki)
+                  for ki, (kind, names) in enumerate(kind_names)} for li in range(N_LAYERS)]
+        gwait = [[(arena.word_ptr(offs[li][n]), sh[n][1], 4 * li + ki) for ki, (kind, names) in enumerate(kind_names)
+                  for n in names] for li in range(N_LAYERS)]
+        gbar = arena.gather_desc([])
     else:
         full_out = {n: torch.zeros((1, sh[n][1]), device=dev) for n in outs}
 
@@ -234,7 +246,7 @@ def gpu_arm(args):
     evs = {k: (torch.cuda.Event(enable_timing=True, external=True),
                torch.cuda.Event(enable_timing=True, external=True)) for k in kinds}
 
-    def layer(L, timed=False, fused=True):
+    def layer(L, li, timed=False, fused=True):
         # fused: quantisation inside each GEMV (btf_gemv_f32, 4 launches per layer);
         # otherwise the drop-in pair launch_prep -> launch_gemv (8 launches per layer)
         def t0(k):
@@ -250,7 +262,7 @@ def gpu_arm(args):
             if world > 1:  # drop-in pair with the all-gather in the GEMV epilogue
                 btf.quant_q8(x_in[xk], acts[xk], stream=stream)
                 t0(kind)
-                btf.launch_gemv_gather(segs, K, 1, acts[xk], mode, gdesc[kind], stream)
+                btf.launch_gemv_gather(segs, K, 1, acts[xk], mode, gdesc[li][kind], stream)
             elif fused:
                 t0(kind)
                 btf.launch_gemv_f32(segs, K, 1, x_in[xk], mode, stream)
@@ -262,16 +274,22 @@ def gpu_arm(args):
 
         def seg(n):
             r = model.rows[n]
-            return (L[n], full_out[n][:, r.r0:], sh[n][1])
+            return (L[n], (lay_out[li] if world > 1 else full_out)[n][:, r.r0:], sh[n][1])
 
         gemv([seg("q"), seg("k"), seg("v")], 5120, "attn", btf.STORE, "qkv")
         gemv([seg("o")], 6144, "o", btf.ADD, "o")
         gemv([seg("gate"), (L["up"], None, 0)], 5120, "ffn", btf.SWIGLU, "gateup")
         gemv([seg("down")], 17408, "down", btf.ADD, "down")
+        if world > 1:  # every rank's rows of this layer's outputs have arrived
+            btf.gather_wait(gwait[li], arena.epoch_ptr, stream)
 
     def step(fused=False):
+        if world > 1:
+            btf.gather_epoch_advance(arena.epoch_ptr, stream)
         for i, L in enumerate(model.layers):
-            layer(L, timed=(i == len(model.layers) - 1) and not fused, fused=fused)
+            layer(L, i, timed=(i == len(model.layers) - 1) and not fused, fused=fused)
+        if world > 1:
+            btf.gather_barrier(gbar, stream)
 
     # e2e variant: inputs from pinned host memory in, outputs back, every step
     h_in = {k: v.cpu().pin_memory() for k, v in x_in.items()}
@@ -390,8 +408,8 @@ def gpu_arm(args):
                        "layers": N_LAYERS, "bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2: 5.8 GB of distinct resident weights per step",
                        "parallelism": f"N-shard x{world}" + (", all-gather fused into the GEMV epilogue (NVLink "
-                                                             "stores + arrival counters, no NCCL in the step)"
-                                                             if world > 1 else ""),
+                                                             "64-bit (value, tag) stores; one tag check per "
+                                                             "layer; no NCCL in the step)" if world > 1 else ""),
                        "graph": "one CUDA graph per step, programmatic dependent launch between kernels",
                        "path": "drop-in pairs: btf_quant_q8 (launch_prep) + btf_gemv (launch_gemv), PDL-chained"},
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",

@@ -33,6 +33,7 @@ EXPORTS = (
     "btf_repack_panels", "btf_repack_panels_host", "btf_repack_t2", "btf_t2_to_panels", "btf_panels_to_t2",
     "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot", "btf_gemm",
     "btf_gemv_gather", "btf_alloc", "btf_free", "btf_ipc_handle", "btf_ipc_open", "btf_ipc_close",
+    "btf_gather_epoch_advance", "btf_gather_wait", "btf_gather_barrier",
 )
 
 
@@ -59,7 +60,14 @@ class GatherC(ctypes.Structure):
 
     _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
                 ("peer_y", (ctypes.c_void_p * MAX_RANKS) * 3), ("flags", ctypes.c_void_p * MAX_RANKS),
-                ("expect", ctypes.c_void_p), ("done", ctypes.c_void_p)]
+                ("expect", ctypes.c_void_p), ("done", ctypes.c_void_p),
+                ("tagged", ctypes.c_int), ("site", ctypes.c_int), ("epoch", ctypes.c_void_p)]
+
+
+class TaggedBufC(ctypes.Structure):
+    """btf_tagged_buf: `words` 64-bit (value, tag) words at p, stored by the launch with `site`."""
+
+    _fields_ = [("p", ctypes.c_void_p), ("words", ctypes.c_int64), ("site", ctypes.c_int)]
 
 
 def lib() -> ctypes.CDLL:
@@ -97,6 +105,9 @@ def lib() -> ctypes.CDLL:
         "btf_ipc_handle": (i32, [vp, ctypes.c_char_p]),
         "btf_ipc_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]),
         "btf_ipc_close": (i32, [vp]),
+        "btf_gather_epoch_advance": (i32, [vp, vp]),
+        "btf_gather_wait": (i32, [ctypes.POINTER(TaggedBufC), i32, vp, vp]),
+        "btf_gather_barrier": (i32, [ctypes.POINTER(GatherC), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -316,3 +327,21 @@ def ipc_open(handle: bytes) -> int:
 
 def ipc_close(ptr: int) -> None:
     check(lib().btf_ipc_close(ptr), "btf_ipc_close")
+
+
+def gather_epoch_advance(epoch_ptr: int, stream=None) -> None:
+    """Starts a new tag epoch for tagged N-sharded launches (btf_gather_epoch_advance)."""
+    check(lib().btf_gather_epoch_advance(epoch_ptr, _stream(stream)), "btf_gather_epoch_advance")
+
+
+def gather_wait(bufs, epoch_ptr: int, stream=None) -> None:
+    """Waits (bounded, on the device) for the tags of tagged output buffers: bufs = [(ptr, words, site)]."""
+    arr = (TaggedBufC * len(bufs))()
+    for i, (ptr, words, site) in enumerate(bufs):
+        arr[i] = TaggedBufC(ptr, words, site)
+    check(lib().btf_gather_wait(arr, len(bufs), epoch_ptr, _stream(stream)), "btf_gather_wait")
+
+
+def gather_barrier(gather: GatherC, stream=None) -> None:
+    """Cross-rank barrier in stream order on the arrival counters (btf_gather_barrier)."""
+    check(lib().btf_gather_barrier(ctypes.byref(gather), _stream(stream)), "btf_gather_barrier")

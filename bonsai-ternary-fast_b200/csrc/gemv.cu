@@ -260,12 +260,21 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
   };
   // Output store: this rank's buffer, or (N-sharded launch) every rank's
   // buffer over NVLink; the value is the same everywhere.
+  // Tagged N-sharded launches store (value bits | tag << 32) as one 64-bit word
+  // (single-copy atomic), so a reader that sees the tag also sees the value.
+  unsigned tag = 0;  // set after griddepcontrol.wait (the epoch is advanced in stream order)
   auto put = [&](int seg, float* y, int64_t idx, float val) {
     if (p.gather.world == 0) {
       y[idx] = val;
+    } else if (p.gather.tagged) {
+      const unsigned long long w = (unsigned long long)__float_as_uint(val) | ((unsigned long long)tag << 32);
+      for (int r = 0; r < p.gather.world; ++r) reinterpret_cast<unsigned long long*>(p.gather.peer_y[seg][r])[idx] = w;
     } else {
       for (int r = 0; r < p.gather.world; ++r) p.gather.peer_y[seg][r][idx] = val;
     }
+  };
+  auto get = [&](const float* y, int64_t idx) -> float {  // current output (BTF_ADD)
+    return p.gather.tagged ? __uint_as_float(reinterpret_cast<const unsigned*>(y)[2 * idx]) : y[idx];
   };
   // Copy issue state (used by lane 0): next panel's unit, slice, slot and
   // source pointers. A unit's S panels are contiguous, so moving to the next
@@ -312,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
     while (is_count < kPrewaitPanels && is_count < depth && is_count < n_panels) issue_next();
   }
   pdl_wait();
+  if (p.gather.tagged) tag = *p.gather.epoch * 1024u + (unsigned)p.gather.site;
   // The activation is read next (few KB, L2-resident); the rest of the ring is
   // started once those loads are in flight.
   auto start_ring = [&]() {
@@ -588,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
             if (row < n && m < p.nb) {
               const int64_t idx = (int64_t)(p.m0 + m) * ldy + row;
               if constexpr (MODE == BTF_STORE) put(seg, y, idx, v[0]);
-              else if constexpr (MODE == BTF_ADD) put(seg, y, idx, y[idx] + v[0]);
+              else if constexpr (MODE == BTF_ADD) put(seg, y, idx, get(y, idx) + v[0]);
               else put(seg, y, idx, silu(v[0]) * up);
             }
           }
@@ -616,13 +626,64 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
         if (row < n && m < p.nb) {
           const int64_t idx = (int64_t)(p.m0 + m) * ldy + row;
           if constexpr (MODE == BTF_STORE) put(seg, y, idx, sg);
-          else if constexpr (MODE == BTF_ADD) put(seg, y, idx, y[idx] + sg);
+          else if constexpr (MODE == BTF_ADD) put(seg, y, idx, get(y, idx) + sg);
           else put(seg, y, idx, silu(sg) * su);
         }
       }
     }
   }
-  if (p.gather.world > 0) gather_arrive(p.gather, p.err);
+  if (p.gather.world > 0 && !p.gather.tagged) gather_arrive(p.gather, p.err);
+}
+
+// Cross-rank barrier (one thread): the release-adds / bounded acquire wait of
+// gather_arrive, on its own.
+__global__ void gather_barrier_kernel(const __grid_constant__ btf_gather g, int* err) {
+  for (int r = 0; r < g.world; ++r)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(g.flags[r]) : "memory");
+  const unsigned target = *g.expect + (unsigned)g.world;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.flags[g.rank]) : "memory");
+    if ((int)(v - target) >= 0) break;
+    if (globaltimer_ns() - t0 > kGatherWaitNs) {
+      atomicCAS(err, 0, kErrWaitTimeout);
+      break;
+    }
+  }
+  *g.expect = target;
+}
+
+// Tagged gather: a new epoch (one thread, in stream order).
+__global__ void gather_epoch_kernel(unsigned* epoch) { *epoch += 1u; }
+
+struct TaggedBufs {
+  btf_tagged_buf b[8];
+  int n;
+};
+// Tagged gather: every thread checks word i of every buffer (bounded spin on
+// the tag half with system-scope relaxed loads, so no stale L1 copy is read).
+__global__ void __launch_bounds__(1024) gather_wait_kernel(const __grid_constant__ TaggedBufs t, const unsigned* epoch,
+                                                           int* err) {
+  pdl_launch_dependents();
+  pdl_wait();  // this rank's own stores come from the previous kernel
+  const unsigned e = *epoch * 1024u;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t t0 = globaltimer_ns();
+  for (int bi = 0; bi < t.n; ++bi) {
+    if (i >= t.b[bi].words) continue;
+    const unsigned want = e + (unsigned)t.b[bi].site;
+    const unsigned* hi = reinterpret_cast<const unsigned*>(t.b[bi].p + i) + 1;
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(hi) : "memory");
+      if (v == want) break;
+      if (globaltimer_ns() - t0 > kGatherWaitNs) {
+        atomicCAS(err, 0, kErrWaitTimeout);
+        return;
+      }
+    }
+  }
 }
 
 // Exact idot dump (parity/debug): one thread per (m, row, sub-block), same
@@ -848,10 +909,15 @@ int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act 
     return fail(BTF_ERR_ARG, "btf_gemv_gather: activation pointers null or misaligned (q needs 16 B)");
   if (!g || g->world < 2 || g->world > BTF_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
     return fail(BTF_ERR_ARG, "btf_gemv_gather: need 2 <= world <= %d and 0 <= rank < world", BTF_MAX_RANKS);
-  if (!g->expect || !g->done) return fail(BTF_ERR_ARG, "btf_gemv_gather: expect/done counters are null");
+  if (g->tagged) {
+    if (!g->epoch || g->site < 0 || g->site >= 1024)
+      return fail(BTF_ERR_ARG, "btf_gemv_gather: tagged launch needs an epoch counter and 0 <= site < 1024");
+  } else if (!g->expect || !g->done) {
+    return fail(BTF_ERR_ARG, "btf_gemv_gather: expect/done counters are null");
+  }
   const int nout = mode == BTF_SWIGLU ? 1 : nseg;  // segments with an output
   for (int r = 0; r < g->world; ++r) {
-    if (!g->flags[r]) return fail(BTF_ERR_ARG, "btf_gemv_gather: arrival counter of rank %d is null", r);
+    if (!g->tagged && !g->flags[r]) return fail(BTF_ERR_ARG, "btf_gemv_gather: arrival counter of rank %d is null", r);
     for (int s = 0; s < nout; ++s)
       if (!g->peer_y[s][r]) return fail(BTF_ERR_ARG, "btf_gemv_gather: peer_y[%d][%d] is null", s, r);
   }
@@ -861,6 +927,43 @@ int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act 
   if (M > kMaxNb)
     return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_gather: M <= %d (one pass; one arrival per launch)", kMaxNb);
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream, g);
+}
+
+int btf_gather_epoch_advance(unsigned int* epoch, void* stream) {
+  if (!epoch) return fail(BTF_ERR_ARG, "btf_gather_epoch_advance: null epoch");
+  if (!current_device()) return BTF_ERR_STATE;
+  gather_epoch_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(epoch);
+  return launch_status("gather_epoch_kernel");
+}
+
+int btf_gather_barrier(const btf_gather* g, void* stream) {
+  if (!g || g->world < 2 || g->world > BTF_MAX_RANKS || g->rank < 0 || g->rank >= g->world || !g->expect)
+    return fail(BTF_ERR_ARG, "btf_gather_barrier: need 2 <= world <= %d, a rank and an expect counter", BTF_MAX_RANKS);
+  for (int r = 0; r < g->world; ++r)
+    if (!g->flags[r]) return fail(BTF_ERR_ARG, "btf_gather_barrier: arrival counter of rank %d is null", r);
+  const DeviceInfo* dev = current_device();
+  if (!dev) return BTF_ERR_STATE;
+  gather_barrier_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(*g, dev->err_word);
+  return launch_status("gather_barrier_kernel");
+}
+
+int btf_gather_wait(const btf_tagged_buf* bufs, int n, const unsigned int* epoch, void* stream) {
+  if (!bufs || n < 1 || n > 8 || !epoch) return fail(BTF_ERR_ARG, "btf_gather_wait: 1..8 buffers and an epoch");
+  const DeviceInfo* dev = current_device();
+  if (!dev) return BTF_ERR_STATE;
+  TaggedBufs t{};
+  int64_t most = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!bufs[i].p || bufs[i].words < 0 || bufs[i].site < 0 || bufs[i].site >= 1024 || !aligned(bufs[i].p, 8))
+      return fail(BTF_ERR_ARG, "btf_gather_wait: buffer %d is null, misaligned or has a bad site", i);
+    t.b[i] = bufs[i];
+    most = std::max(most, bufs[i].words);
+  }
+  t.n = n;
+  const int grid = (int)std::max<int64_t>(1, (most + 1023) / 1024);
+  const cudaError_t e = launch_pdl(gather_wait_kernel, dim3(grid), dim3(1024), 0, (cudaStream_t)stream, t, epoch,
+                                   dev->err_word);
+  return e == cudaSuccess ? launch_status("gather_wait_kernel") : cuda_fail(e, "gather_wait_kernel launch");
 }
 
 int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* x, int ldx, int mode, void* stream) {

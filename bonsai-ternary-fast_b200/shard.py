@@ -109,7 +109,8 @@ class GatherArena:
 
     Each rank allocates one device buffer (btf_alloc): a 256-byte control block
     (its arrival counter at +0, its consumed-arrivals counter at +4, its CTA
-    completion counter at +8) followed by the output buffers, laid out the same
+    completion counter at +8, its tag epoch at +12) followed by the output
+    buffers (float32, or 64-bit (value, tag) words for tagged launches), laid out the same
     on every rank. The buffers' IPC handles are exchanged over the default
     process group, so each process can address every rank's buffer; a sharded
     GEMV then stores each output value into all of them (btf_gemv_gather).
@@ -132,20 +133,36 @@ class GatherArena:
         dist.barrier()
         self._next = 0
 
-    def buffer(self, shape) -> tuple:
-        """Reserves a float32 buffer of `shape`; returns (offset, torch view of this rank's copy)."""
+    def buffer(self, shape, tagged: bool = False) -> tuple:
+        """Reserves an output buffer of `shape`: float32, or (tagged) 64-bit (value, tag) words
+        as int64. Returns (offset, torch view of this rank's copy)."""
         import torch
 
         n = 1
         for d in shape:
             n *= d
+        esz = 8 if tagged else 4
         off = self._next
-        self._next = (off + 4 * n + 255) // 256 * 256
+        self._next = (off + esz * n + 255) // 256 * 256
         if self._next > self.nbytes:
             raise ValueError("GatherArena: out of space")
-        return off, torch.as_tensor(_DeviceArray(self.base + self.CTL + off, shape), device=self.device)
+        return off, torch.as_tensor(_DeviceArray(self.base + self.CTL + off, shape, "<i8" if tagged else "<f4"),
+                                    device=self.device)
 
-    def gather_desc(self, seg_offsets_bytes):
+    @property
+    def epoch_ptr(self) -> int:
+        """This rank's tag epoch counter (control block +12)."""
+        return self.base + 12
+
+    def word_ptr(self, offset: int) -> int:
+        return self.base + self.CTL + offset
+
+    @staticmethod
+    def values(words):
+        """float32 values of a tagged int64 buffer (low halves)."""
+        return words.view(dtype=__import__("torch").float32)[..., ::2]
+
+    def gather_desc(self, seg_offsets_bytes, tagged: bool = False, site: int = 0):
         """btf_gather for a launch whose segment s has its y (this rank's first
         output row, i.e. the buffer offset plus 4 * row0 of this rank's shard) at
         byte offset seg_offsets_bytes[s] within every rank's output area."""
@@ -158,6 +175,7 @@ class GatherArena:
             g.flags[r] = self.bases[r]
         g.expect = self.base + 4
         g.done = self.base + 8
+        g.tagged, g.site, g.epoch = int(tagged), site, self.epoch_ptr
         return g
 
     def close(self):

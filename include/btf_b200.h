@@ -168,9 +168,38 @@ typedef struct btf_gather {
   unsigned int* flags[BTF_MAX_RANKS]; /* each rank's arrival counter, as mapped here */
   unsigned int* expect;               /* this rank's consumed-arrivals counter (device, starts at 0) */
   unsigned int* done;                 /* this rank's CTA completion counter (device, starts at 0) */
+  /* Tagged form (tagged != 0): the outputs are 64-bit words (fp32 value bits in
+   * the low half, tag in the high half) and no counter is used: every word is
+   * stored with one single-copy-atomic 64-bit store, so a reader that sees the
+   * expected tag in a word also sees that launch's value. tag = *epoch * 1024 +
+   * site (site < 1024, unique per launch within an epoch). Readers check tags
+   * with btf_gather_wait; btf_gather_epoch_advance starts a new epoch. */
+  int tagged;
+  int site;
+  const unsigned int* epoch; /* this rank's epoch counter (device) */
 } btf_gather;
 int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, const btf_gather* g,
                     void* stream);
+
+/* Tagged-gather helpers. One tagged output buffer to check: `words` 64-bit
+ * words at `p` that the launch with `site` stores. */
+typedef struct btf_tagged_buf {
+  const uint64_t* p;
+  int64_t words;
+  int site;
+} btf_tagged_buf;
+/* *epoch += 1 (one thread, in stream order): a new epoch for the next launches. */
+int btf_gather_epoch_advance(unsigned int* epoch, void* stream);
+/* Waits (bounded) until every word of bufs[0..n) carries the tag
+ * *epoch * 1024 + site of its buffer; on time-out sets the device error word.
+ * n <= 8. The launch returns once the outputs are all there. */
+int btf_gather_wait(const btf_tagged_buf* bufs, int n, const unsigned int* epoch, void* stream);
+/* Cross-rank barrier in stream order (one thread): adds 1 to every rank's
+ * arrival counter (g->flags, system scope) and waits, bounded, until this rank's
+ * counter shows all g->world ranks (g->expect tracks the count). With tagged
+ * launches it separates epochs: no rank starts storing into a buffer for the next
+ * epoch before every rank has finished checking the current one. */
+int btf_gather_barrier(const btf_gather* g, void* stream);
 
 /* Device buffers shared across processes (one process per GPU) through CUDA IPC.
  * btf_alloc/btf_free: cudaMalloc/cudaFree on the current device (the IPC

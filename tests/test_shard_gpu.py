@@ -3,8 +3,9 @@ runs only its row shard through the C ABI, the fp32 slices are all-gathered, and
 every rank's gathered output must match the unsharded oracle within rel-RMS
 1e-5 (the GEMV's own tolerance; a shard's CTA split differs from the
 unsharded launch's, so the fp32 summation order of a row may differ). Run
-twice: all-gather by NCCL after the GEMV, and fused into the GEMV epilogue
-(btf_gemv_gather: NVLink stores into every rank's buffer + arrival counters).
+three times: all-gather by NCCL after the GEMV; fused into the GEMV epilogue
+(btf_gemv_gather: NVLink stores into every rank's buffer + arrival counters);
+and the tagged form (64-bit (value, tag) words checked by btf_gather_wait).
 Skipped with fewer than 2 GPUs."""
 import os
 import socket
@@ -65,7 +66,7 @@ def _worker(rank, world, port, out_dir):
             np.save(os.path.join(out_dir, f"c{ci}_r{rank}.npy"), shard.unpad(y_full, N).cpu().numpy())
         dist.barrier()
         # the same cases with the all-gather fused into the GEMV epilogue (NVLink stores)
-        arena = shard.GatherArena(btf, sum(M * N * 4 + 256 for N, K, M, _ in CASES), world, rank, dev)
+        arena = shard.GatherArena(btf, sum(M * N * 12 + 512 for N, K, M, _ in CASES), world, rank, dev)
         for ci, (N, K, M, mode) in enumerate(CASES):
             src = synth.ternary_ptq(N, K, seed=10 + ci)
             act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=20 + ci)).to(dev))
@@ -85,6 +86,31 @@ def _worker(rank, world, port, out_dir):
             torch.cuda.synchronize()
             assert btf.device_error() == 0
             np.save(os.path.join(out_dir, f"g{ci}_r{rank}.npy"), y_full.cpu().numpy())
+        dist.barrier()
+        # tagged form: (value, tag) words, no counters; a bounded device wait checks the tags
+        btf.gather_epoch_advance(arena.epoch_ptr)
+        for ci, (N, K, M, mode) in enumerate(CASES):
+            src = synth.ternary_ptq(N, K, seed=10 + ci)
+            act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=20 + ci)).to(dev))
+            gate = shard.ShardedMatrix(btf, src, N, K, world, rank, dev)
+            up = shard.ShardedMatrix(btf, synth.ternary_ptq(N, K, seed=30 + ci), N, K, world, rank, dev) \
+                if mode == btf.SWIGLU else None
+            sh = gate.shard
+            off, words = arena.buffer((M, N), tagged=True)
+            y0 = torch.from_numpy(np.random.default_rng(ci).standard_normal((M, N)).astype(np.float32)).to(dev)
+            words.copy_(y0.view(torch.int32).to(torch.int64) & 0xFFFFFFFF)  # tag 0
+            torch.cuda.synchronize()
+            dist.barrier()
+            segs = [(gate.pm, words[:, sh.r0:], N)]
+            if up is not None:
+                segs.append((up.pm, None, 0))
+            btf.launch_gemv_gather(segs, K, M, act, mode,
+                                   arena.gather_desc([off + 8 * sh.r0], tagged=True, site=ci))
+            btf.gather_wait([(arena.word_ptr(off), M * N, ci)], arena.epoch_ptr)
+            btf.gather_barrier(arena.gather_desc([]))
+            torch.cuda.synchronize()
+            assert btf.device_error() == 0
+            np.save(os.path.join(out_dir, f"t{ci}_r{rank}.npy"), shard.GatherArena.values(words).cpu().numpy())
         dist.barrier()
         arena.close()
     finally:
@@ -115,3 +141,5 @@ def test_sharded_gemv_nccl_matches_oracle(orc, tmp_path):
             assert rel_rms(got, want) <= 1e-5, (ci, r, rel_rms(got, want))
             got = np.load(tmp_path / f"g{ci}_r{r}.npy")  # NVLink-gathered in the epilogue
             assert rel_rms(got, want) <= 1e-5, ("gather", ci, r, rel_rms(got, want))
+            got = np.load(tmp_path / f"t{ci}_r{r}.npy")  # tagged (value, tag) words
+            assert rel_rms(got, want) <= 1e-5, ("tagged", ci, r, rel_rms(got, want))
