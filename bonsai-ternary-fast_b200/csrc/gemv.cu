@@ -949,8 +949,6 @@ int btf_gather_barrier(const btf_gather* g, void* stream) {
 
 int btf_gather_wait(const btf_tagged_buf* bufs, int n, const unsigned int* epoch, void* stream) {
   if (!bufs || n < 1 || n > 8 || !epoch) return fail(BTF_ERR_ARG, "btf_gather_wait: 1..8 buffers and an epoch");
-  const DeviceInfo* dev = current_device();
-  if (!dev) return BTF_ERR_STATE;
   TaggedBufs t{};
   int64_t most = 0;
   for (int i = 0; i < n; ++i) {
@@ -960,6 +958,8 @@ int btf_gather_wait(const btf_tagged_buf* bufs, int n, const unsigned int* epoch
     most = std::max(most, bufs[i].words);
   }
   t.n = n;
+  const DeviceInfo* dev = current_device();
+  if (!dev) return BTF_ERR_STATE;
   const int grid = (int)std::max<int64_t>(1, (most + 1023) / 1024);
   const cudaError_t e = launch_pdl(gather_wait_kernel, dim3(grid), dim3(1024), 0, (cudaStream_t)stream, t, epoch,
                                    dev->err_word);

@@ -77,3 +77,38 @@ def test_cpp_shim_header_compiles():
     r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
                         "-I", "/usr/local/cuda/include", src], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def _seg(btf, ptr=16, N=8, y=64, ldy=8):
+    arr = (btf.GemvSeg * 1)()
+    arr[0] = btf.GemvSeg(ptr, N, y, ldy)
+    return arr
+
+
+def test_gather_entry_points_reject_bad_arguments(btf):
+    # argument checks run before any device access, so they are testable without a GPU
+    import ctypes
+
+    L = btf.lib()
+    act = btf.Q8ActC(256, 256, 256)
+    g = btf.GatherC()
+    g.world, g.rank = 1, 0  # world must be >= 2
+    rc = L.btf_gemv_gather(_seg(btf), 1, 1024, 1, act, btf.STORE, ctypes.byref(g), None)
+    assert rc == 1 and "world" in L.btf_last_error().decode()
+    g.world, g.rank = 2, 0
+    g.tagged, g.site = 1, 2000  # site >= 1024
+    rc = L.btf_gemv_gather(_seg(btf), 1, 1024, 1, act, btf.STORE, ctypes.byref(g), None)
+    assert rc == 1 and "site" in L.btf_last_error().decode()
+    g.site, g.epoch = 3, 4096
+    rc = L.btf_gemv_gather(_seg(btf), 1, 1024, 1, act, btf.STORE, ctypes.byref(g), None)
+    assert rc == 1 and "peer_y" in L.btf_last_error().decode()  # peer pointers not set
+    rc = L.btf_gemv_gather(_seg(btf), 1, 1000, 1, act, btf.STORE, ctypes.byref(g), None)
+    assert rc == 1 and "multiple of 128" in L.btf_last_error().decode()
+    bufs = (btf.TaggedBufC * 1)()
+    assert L.btf_gather_wait(bufs, 0, 4096, None) == 1
+    bufs[0] = btf.TaggedBufC(0, 10, 1)
+    assert L.btf_gather_wait(bufs, 1, 4096, None) == 1  # null buffer
+    assert L.btf_gather_epoch_advance(None, None) == 1
+    assert L.btf_gather_barrier(ctypes.byref(btf.GatherC()), None) == 1
+    assert L.btf_alloc(0, ctypes.byref(ctypes.c_void_p())) == 1
+    assert L.btf_ipc_handle(None, ctypes.create_string_buffer(64)) == 1
