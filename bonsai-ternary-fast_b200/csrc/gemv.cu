@@ -214,7 +214,9 @@ __device__ __noinline__ void gather_arrive(const btf_gather& g, int* err) {
   *g.expect = target;
 }
 
-template <int NB, int MODE, bool FUSE>
+// GATHER: 0 = plain launch; 1 = N-sharded, counted completion; 2 = N-sharded,
+// tagged (value, tag) words. Compile-time, so plain launches carry none of it.
+template <int NB, int MODE, bool FUSE, int GATHER>
 __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __grid_constant__ GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
   constexpr bool kCluster = FUSE && kFuseCluster > 1;
@@ -264,9 +266,9 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
   // (single-copy atomic), so a reader that sees the tag also sees the value.
   unsigned tag = 0;  // set after griddepcontrol.wait (the epoch is advanced in stream order)
   auto put = [&](int seg, float* y, int64_t idx, float val) {
-    if (p.gather.world == 0) {
+    if constexpr (GATHER == 0) {
       y[idx] = val;
-    } else if (p.gather.tagged) {
+    } else if constexpr (GATHER == 2) {
       const unsigned long long w = (unsigned long long)__float_as_uint(val) | ((unsigned long long)tag << 32);
       for (int r = 0; r < p.gather.world; ++r) reinterpret_cast<unsigned long long*>(p.gather.peer_y[seg][r])[idx] = w;
     } else {
@@ -274,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
     }
   };
   auto get = [&](const float* y, int64_t idx) -> float {  // current output (BTF_ADD)
-    return p.gather.tagged ? __uint_as_float(reinterpret_cast<const unsigned*>(y)[2 * idx]) : y[idx];
+    if constexpr (GATHER == 2) return __uint_as_float(reinterpret_cast<const unsigned*>(y)[2 * idx]);
+    else return y[idx];
   };
   // Copy issue state (used by lane 0): next panel's unit, slice, slot and
   // source pointers. A unit's S panels are contiguous, so moving to the next
@@ -321,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
     while (is_count < kPrewaitPanels && is_count < depth && is_count < n_panels) issue_next();
   }
   pdl_wait();
-  if (p.gather.tagged) tag = *p.gather.epoch * 1024u + (unsigned)p.gather.site;
+  if constexpr (GATHER == 2) tag = *p.gather.epoch * 1024u + (unsigned)p.gather.site;
   // The activation is read next (few KB, L2-resident); the rest of the ring is
   // started once those loads are in flight.
   auto start_ring = [&]() {
@@ -632,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
       }
     }
   }
-  if (p.gather.world > 0 && !p.gather.tagged) gather_arrive(p.gather, p.err);
+  if constexpr (GATHER == 1) gather_arrive(p.gather, p.err);
 }
 
 // Cross-rank barrier (one thread): the release-adds / bounded acquire wait of
@@ -712,17 +715,25 @@ __global__ void __launch_bounds__(256)
 
 using KernelFn = void (*)(const GemvParams);
 
-template <int MODE, bool FUSE>
+template <int MODE, bool FUSE, int GATHER>
 KernelFn pick(int NB) {
   switch (NB) {
-    case 1: return gemv_kernel<1, MODE, FUSE>;
-    case 2: return gemv_kernel<2, MODE, FUSE>;
-    default: return gemv_kernel<4, MODE, FUSE>;
+    case 1: return gemv_kernel<1, MODE, FUSE, GATHER>;
+    case 2: return gemv_kernel<2, MODE, FUSE, GATHER>;
+    default: return gemv_kernel<4, MODE, FUSE, GATHER>;
   }
 }
-KernelFn pick(int NB, int mode, bool fuse) {
-  if (fuse) return mode == BTF_STORE ? pick<BTF_STORE, true>(NB) : mode == BTF_ADD ? pick<BTF_ADD, true>(NB) : pick<BTF_SWIGLU, true>(NB);
-  return mode == BTF_STORE ? pick<BTF_STORE, false>(NB) : mode == BTF_ADD ? pick<BTF_ADD, false>(NB) : pick<BTF_SWIGLU, false>(NB);
+template <bool FUSE, int GATHER>
+KernelFn pick_mode(int NB, int mode) {
+  return mode == BTF_STORE ? pick<BTF_STORE, FUSE, GATHER>(NB)
+         : mode == BTF_ADD ? pick<BTF_ADD, FUSE, GATHER>(NB)
+                           : pick<BTF_SWIGLU, FUSE, GATHER>(NB);
+}
+// fused-quantise launches are never N-sharded
+KernelFn pick(int NB, int mode, bool fuse, int gather) {
+  if (fuse) return pick_mode<true, 0>(NB, mode);
+  return gather == 0 ? pick_mode<false, 0>(NB, mode) : gather == 1 ? pick_mode<false, 1>(NB, mode)
+                                                                   : pick_mode<false, 2>(NB, mode);
 }
 
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }
@@ -841,7 +852,7 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
     p.slots = slots;
     p.m0 = m0;
     p.nb = nb;
-    const KernelFn fn = pick(NB, mode, x != nullptr);
+    const KernelFn fn = pick(NB, mode, x != nullptr, !gather ? 0 : gather->tagged ? 2 : 1);
     const int cluster = x != nullptr ? kFuseCluster : 1;
     const int resident = cluster > 1 ? resident_cluster_ctas(fn, plan.total, cluster, st)
                                      : dev->sm_count * resident_ctas(fn, plan.total);
@@ -858,12 +869,22 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
   return BTF_OK;
 }
 
-template <int MODE, bool FUSE>
+template <int MODE, bool FUSE, int GATHER>
 cudaError_t set_attrs(int smem) {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(gemv_kernel<1, MODE, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
-  if ((e = cudaFuncSetAttribute(gemv_kernel<2, MODE, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem))) return e;
-  return cudaFuncSetAttribute(gemv_kernel<4, MODE, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if ((e = cudaFuncSetAttribute(gemv_kernel<1, MODE, FUSE, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem)))
+    return e;
+  if ((e = cudaFuncSetAttribute(gemv_kernel<2, MODE, FUSE, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem)))
+    return e;
+  return cudaFuncSetAttribute(gemv_kernel<4, MODE, FUSE, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+template <bool FUSE, int GATHER>
+cudaError_t set_attrs_all(int smem) {
+  cudaError_t e;
+  if ((e = set_attrs<BTF_STORE, FUSE, GATHER>(smem)) || (e = set_attrs<BTF_ADD, FUSE, GATHER>(smem))) return e;
+  return set_attrs<BTF_SWIGLU, FUSE, GATHER>(smem);
 }
 
 }  // namespace
@@ -878,9 +899,8 @@ int gemv_setup(DeviceInfo& d) {
   d.err_word = static_cast<int*>(ew);
   // leave room for static shared memory (per-block limit = dynamic + static)
   const int dyn = d.optin_smem - 1024;
-  if ((e = set_attrs<BTF_STORE, false>(dyn)) || (e = set_attrs<BTF_ADD, false>(dyn)) ||
-      (e = set_attrs<BTF_SWIGLU, false>(dyn)) || (e = set_attrs<BTF_STORE, true>(dyn)) ||
-      (e = set_attrs<BTF_ADD, true>(dyn)) || (e = set_attrs<BTF_SWIGLU, true>(dyn)))
+  if ((e = set_attrs_all<false, 0>(dyn)) || (e = set_attrs_all<false, 1>(dyn)) || (e = set_attrs_all<false, 2>(dyn)) ||
+      (e = set_attrs_all<true, 0>(dyn)))
     return cuda_fail(e, "cudaFuncSetAttribute(gemv_kernel)");
   return BTF_OK;
 }
