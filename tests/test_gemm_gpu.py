@@ -86,3 +86,29 @@ def test_gemm_prefill_configs(cuda, btf, orc, M, K, N):
     # benchmark configuration 2 shapes; rows from the first, a middle and the last N tile
     rows = np.r_[0:64, N // 2 - 32:N // 2 + 32, N - 64:N]
     _case(btf, orc, cuda, M, K, N, seed=0, rows=rows)
+
+
+def test_gemm_three_segments_qkv_shapes(cuda, btf, orc):
+    # q/k/v in one call (3 segments sharing K and the activation), prefill M=64
+    import torch
+
+    K, M = 5120, 64
+    Ns = (6144, 1024, 1024)
+    x = synth.activations(M, K, seed=41)
+    act = btf.quant_q8(_dev(x, cuda))
+    q, d, s = orc.q8_rows(x)
+    segs, srcs, ys = [], [], []
+    for i, N in enumerate(Ns):
+        src = synth.ternary_ptq(N, K, seed=42 + i)
+        y = torch.empty((M, N + 3), device=cuda)  # ldy > N
+        segs.append((btf.repack_panels(_dev(src, cuda), N, K), y, N + 3))
+        srcs.append(src)
+        ys.append(y)
+    btf.launch_gemm(segs, K, M, act, btf.STORE)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    for src, y, N in zip(srcs, ys, Ns):
+        rows = np.r_[0:32, N - 32:N]
+        codes, scales = orc.repack_t2(src[rows], len(rows), K)
+        want = orc.gemv(codes, scales, K, q, d, s, threads=8)
+        assert rel_rms(y.cpu().numpy()[:, :N][:, rows], want) <= TOL

@@ -194,3 +194,30 @@ def test_gemv_rejects_bad_arguments(cuda, btf):
         btf.launch_gemv([(pm, y, 16)], 1024, 1, act, btf.SWIGLU)
     with pytest.raises(RuntimeError, match="segments"):
         btf.launch_gemv([(pm, y, 16)] * 4, 1024, 1, act)
+
+
+@pytest.mark.parametrize("M", [1, 16])
+def test_lm_head_shape_row_subsets(cuda, btf, orc, M):
+    # BASELINE configuration 4's lm_head, 5120 -> 248320 (31040 row groups; M=16 runs as
+    # four 4-row passes), checked on rows from the first, a middle and the last row groups
+    import torch
+
+    N, K = synth.LM_HEAD[2], synth.LM_HEAD[1]
+    # random digit bytes are valid PTQ1_0 (every byte decodes to trits, types.hpp:70-78);
+    # bytes 26-27 of each block get a proper fp16 scale
+    rng = np.random.default_rng(5)
+    src = rng.integers(0, 256, size=(N, K // 128, 28), dtype=np.uint8)
+    src[:, :, 26:28] = synth.block_scales(N, K, seed=6).view(np.uint8).reshape(N, K // 128, 2)
+    src = src.reshape(N, K // 128 * 28)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    x = synth.activations(M, K, seed=6)
+    act = btf.quant_q8(_dev(x, cuda))
+    y = torch.empty((M, N), device=cuda)
+    btf.launch_gemv([(pm, y, N)], K, M, act, btf.STORE)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    rows = np.r_[0:64, N // 2 - 32:N // 2 + 32, N - 64:N]
+    codes, scales = orc.repack_t2(src[rows], len(rows), K)
+    q, d, s = orc.q8_rows(x)
+    want = orc.gemv(codes, scales, K, q, d, s, threads=8)
+    assert rel_rms(y.cpu().numpy()[:, rows], want) <= TOL
