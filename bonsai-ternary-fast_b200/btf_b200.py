@@ -33,7 +33,7 @@ EXPORTS = (
     "btf_repack_panels", "btf_repack_panels_host", "btf_repack_t2", "btf_t2_to_panels", "btf_panels_to_t2",
     "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot", "btf_gemm",
     "btf_gemv_gather", "btf_alloc", "btf_free", "btf_ipc_handle", "btf_ipc_open", "btf_ipc_close",
-    "btf_gather_epoch_advance", "btf_gather_wait", "btf_gather_barrier",
+    "btf_gather_epoch_advance", "btf_gather_wait", "btf_gather_barrier", "btf_prep",
 )
 
 
@@ -53,6 +53,13 @@ _lib: Optional[ctypes.CDLL] = None
 
 
 MAX_RANKS = 8
+
+
+class HxC(ctypes.Structure):
+    """btf_hx: input transform of a folded-Hadamard weight (kernels.cuh:34-38)."""
+
+    _fields_ = [("block", ctypes.c_int), ("perm_hd", ctypes.c_int), ("perm_nk", ctypes.c_int),
+                ("perm_rep", ctypes.c_int), ("signs", ctypes.c_void_p)]
 
 
 class GatherC(ctypes.Structure):
@@ -108,6 +115,7 @@ def lib() -> ctypes.CDLL:
         "btf_gather_epoch_advance": (i32, [vp, vp]),
         "btf_gather_wait": (i32, [ctypes.POINTER(TaggedBufC), i32, vp, vp]),
         "btf_gather_barrier": (i32, [ctypes.POINTER(GatherC), vp]),
+        "btf_prep": (i32, [vp, i32, i32, i32, vp, ctypes.c_float, HxC, vp, i32, Q8ActC, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -345,3 +353,17 @@ def gather_wait(bufs, epoch_ptr: int, stream=None) -> None:
 def gather_barrier(gather: GatherC, stream=None) -> None:
     """Cross-rank barrier in stream order on the arrival counters (btf_gather_barrier)."""
     check(lib().btf_gather_barrier(ctypes.byref(gather), _stream(stream)), "btf_gather_barrier")
+
+
+def prep(x, normw=None, eps: float = 1e-6, block: int = 0, perm=(0, 0, 0), signs=None, xn_out=None,
+         act: Optional[Q8Act] = None, stream=None) -> Q8Act:
+    """launch_prep (kernels.cuh:42-43): RMSNorm -> permutation -> signs -> Hadamard -> Q8_0 (btf_prep)."""
+    M, n = x.shape
+    ensure_init(x.device.index)
+    if act is None:
+        act = Q8Act.empty(M, n, x.device)
+    hx = HxC(block, perm[0], perm[1], perm[2], _ptr(signs))
+    ldxn = xn_out.stride(0) if xn_out is not None else 0
+    check(lib().btf_prep(_ptr(x), x.stride(0), M, n, _ptr(normw), eps, hx, _ptr(xn_out), ldxn, act.c(),
+                         _stream(stream)), "btf_prep")
+    return act

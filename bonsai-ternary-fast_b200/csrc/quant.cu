@@ -35,10 +35,151 @@ __global__ void __launch_bounds__(kQThreads)
   }
 }
 
+// ---------------------------------------------------------------- fused prep
+// RMSNorm -> permutation -> signs -> blockwise Walsh-Hadamard -> Q8_0, the
+// reference's launch_prep (src/cuda/kernels.cu:147-202, :745-774). Host forms:
+// bd::rmsnorm / bd::hadamard_input (ref/bonsai-decoder/src/cpu_ops.cpp:90-127)
+// and q8_block_host. One CTA per (span of S <= 1024 columns, row); the span is
+// the largest power of two <= 1024 dividing n, so Hadamard blocks never cross
+// CTAs. Every butterfly computes (a + b, a - b) in the host's stage order, and
+// the norm scale and the products are correctly rounded, so only the order of
+// the double sum of squares differs from the host.
+constexpr int kPrepThreads = 256;
+
+struct PrepParams {
+  const float* x;
+  int ldx, n, S;
+  const float* normw;
+  float eps;
+  int block, perm_hd, perm_nk, perm_rep;
+  const float* signs;
+  float* xn_out;
+  int ldxn;
+  int8_t* q;
+  float* d;
+  int32_t* s;
+};
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <bool NORM>
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constant__ PrepParams a) {
+  extern __shared__ float buf[];  // [S]
+  __shared__ double red[kPrepThreads / 32];
+  const int m = blockIdx.y, base = blockIdx.x * a.S;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* xr = a.x + (size_t)m * a.ldx;
+  pdl_launch_dependents();
+  pdl_wait();  // x is written by the previous kernel
+  float scale = 1.0f;
+  if constexpr (NORM) {
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < a.n; i += kPrepThreads) acc += (double)xr[i] * (double)xr[i];
+    acc = warp_sum_d(acc);
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < kPrepThreads / 32; ++w) tot += red[w];
+    const float mean = (float)(tot / (double)a.n);
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+  }
+  for (int o = threadIdx.x; o < a.S; o += kPrepThreads) {
+    const int og = base + o;
+    int src = og;
+    if (a.perm_rep > 1) {  // tiled [hd, nk, rep] -> grouped [hd, rep, nk]
+      const int dd = og % a.perm_hd, t = og / a.perm_hd;
+      const int r = t % a.perm_rep, k = t / a.perm_rep;
+      src = dd + a.perm_hd * (k + a.perm_nk * r);
+    }
+    float v = xr[src];
+    if constexpr (NORM) v = __fmul_rn(__fmul_rn(v, scale), a.normw[src]);
+    if (a.signs) v = __fmul_rn(v, a.signs[og]);
+    buf[o] = v;
+    if (a.xn_out) {
+      float u = xr[og];
+      if constexpr (NORM) u = __fmul_rn(__fmul_rn(u, scale), a.normw[og]);
+      a.xn_out[(size_t)m * a.ldxn + og] = u;
+    }
+  }
+  __syncthreads();
+  float hs = 1.0f;
+  if (a.block > 1) {
+    // stages len = 1 .. 16 inside each warp's 32 consecutive values (shuffles)
+    const int lim = min(a.block, 32);
+    for (int c = warp; c < a.S / 32; c += kPrepThreads / 32) {
+      float v = buf[c * 32 + lane];
+      for (int len = 1; len < lim; len <<= 1) {
+        const float p = __shfl_xor_sync(0xffffffffu, v, len);
+        v = (lane & len) ? __fsub_rn(p, v) : __fadd_rn(v, p);
+      }
+      buf[c * 32 + lane] = v;
+    }
+    __syncthreads();
+    // stages len = 32 .. block/2 in shared memory
+    for (int len = 32; len < a.block; len <<= 1) {
+      for (int pidx = threadIdx.x; pidx < (a.S >> 1); pidx += kPrepThreads) {
+        const int j = (pidx / len) * (len << 1) + (pidx % len);
+        const float x0 = buf[j], x1 = buf[j + len];
+        buf[j] = __fadd_rn(x0, x1);
+        buf[j + len] = __fsub_rn(x0, x1);
+      }
+      __syncthreads();
+    }
+    hs = __fdiv_rn(1.0f, __fsqrt_rn((float)a.block));
+  }
+  for (int g = warp; g < a.S / 32; g += kPrepThreads / 32) {
+    float v = buf[g * 32 + lane];
+    if (a.block > 1) v = __fmul_rn(v, hs);
+    float dq;
+    int sum;
+    const int qv = q8_warp(v, dq, sum);
+    const size_t col = (size_t)base + g * 32 + lane;
+    a.q[(size_t)m * a.n + col] = (int8_t)qv;
+    if (lane == 0) {
+      const size_t bi = (size_t)m * (a.n / 32) + (base / 32 + g);
+      a.d[bi] = dq;
+      a.s[bi] = sum;
+    }
+  }
+}
+
+int span_of(int n) {
+  int s = 1;
+  while (s < 1024 && n % (s * 2) == 0) s *= 2;
+  return s;
+}
+
 }  // namespace
 }  // namespace btf
 
 using namespace btf;
+
+extern "C" int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float eps, btf_hx hx,
+                        float* xn_out, int ldxn, btf_q8act act, void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (n <= 0 || n % 32 || ldx < n) return fail(BTF_ERR_ARG, "btf_prep: need n a positive multiple of 32 and ldx >= n");
+  if (!x || !act.q || !act.d || !act.s) return fail(BTF_ERR_ARG, "btf_prep: null pointer");
+  if (xn_out && ldxn < n) return fail(BTF_ERR_ARG, "btf_prep: ldxn < n");
+  if (M > 65535) return fail(BTF_ERR_ARG, "btf_prep: M=%d exceeds 65535", M);
+  const int S = span_of(n);
+  if (hx.block < 0 || (hx.block > 0 && ((hx.block & (hx.block - 1)) || S % hx.block)))
+    return fail(BTF_ERR_ARG, "btf_prep: hadamard block %d must be a power of two dividing the span %d", hx.block, S);
+  if (hx.perm_rep > 1 && (hx.perm_hd <= 0 || hx.perm_nk <= 0 || (int64_t)hx.perm_hd * hx.perm_nk * hx.perm_rep != n))
+    return fail(BTF_ERR_ARG, "btf_prep: permutation geometry hd*nk*rep must equal n");
+  if (!current_device()) return BTF_ERR_STATE;
+  PrepParams p{x, ldx, n, S, normw, eps, hx.block, hx.perm_hd, hx.perm_nk, hx.perm_rep, hx.signs, xn_out, ldxn,
+               act.q, act.d, act.s};
+  const dim3 grid(n / S, M);
+  const size_t smem = (size_t)S * sizeof(float);
+  const cudaError_t e = normw ? launch_pdl(prep_kernel<true>, grid, dim3(kPrepThreads), smem, (cudaStream_t)stream, p)
+                              : launch_pdl(prep_kernel<false>, grid, dim3(kPrepThreads), smem, (cudaStream_t)stream, p);
+  return e == cudaSuccess ? launch_status("prep_kernel") : cuda_fail(e, "prep_kernel launch");
+}
 
 extern "C" int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act, void* stream) {
   if (M <= 0) return BTF_OK;

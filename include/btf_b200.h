@@ -117,6 +117,23 @@ int btf_panels_to_t2(const void* panels, int64_t N, int64_t K, uint8_t* codes, u
  * for a raw input (no norm, no Hadamard transform). K % 32 == 0. */
 int btf_quant_q8(const float* x, int ldx, int M, int K, btf_q8act act, void* stream);
 
+/* Input transform of a folded-Hadamard weight. Mirrors Hx (src/cuda/kernels.cuh:34-38):
+ * block = 0: none; else blockwise Walsh-Hadamard of `block` (a power of two dividing
+ * the span, the largest power of two <= 1024 dividing n); perm_rep > 1: tiled
+ * [hd, nk, rep] -> grouped [hd, rep, nk] permutation first; signs: per-column +-1. */
+typedef struct btf_hx {
+  int block;
+  int perm_hd, perm_nk, perm_rep;
+  const float* signs; /* [n] or NULL */
+} btf_hx;
+
+/* ---- fused prep: RMSNorm (normw != NULL) -> permutation -> signs -> Hadamard
+ * -> Q8_0, plus the normalised rows in xn_out [M][ldxn] when non-NULL.
+ * Replaces launch_prep (src/cuda/kernels.cuh:42-43, kernels.cu:745-774). With
+ * normw == NULL and hx.block == 0 it is bit-exact to btf_quant_q8. */
+int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float eps, btf_hx hx, float* xn_out,
+             int ldxn, btf_q8act act, void* stream);
+
 /* ---- ternary GEMV (batch M, CUDA cores: dp4a on the 2-bit codes)
  * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two

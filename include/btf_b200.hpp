@@ -8,7 +8,7 @@
 //     and GemvSeg::scales must be nullptr: the scales live inside the panels;
 //   - launch_repack keeps the reference's T2 output; launch_repack_panels is the
 //     loader for the B200 layout and needs N and K;
-//   - launch_prep serves the raw-input case (no norm, no Hadamard transform).
+//   - launch_prep runs the whole prep (RMSNorm, permutation, signs, Hadamard, Q8).
 #pragma once
 #include <cuda_runtime_api.h>
 
@@ -56,12 +56,11 @@ struct Hx {
   const float* signs = nullptr;
 };
 
-// kernels.cuh:42-43 — raw-input quantisation only.
-inline void launch_prep(const float* x, int ldx, int M, int n, const float* normw, float /*eps*/, const Hx& hx,
-                        float* xn_out, int /*ldxn*/, const Q8Act& a, cudaStream_t st) {
-  if (normw || hx.block || hx.signs || hx.perm_rep > 1 || xn_out)
-    throw std::runtime_error("launch_prep: only the raw-input Q8 quantisation is implemented");
-  throw_if(btf_quant_q8(x, ldx, M, n, btf_q8act{a.q, a.d, a.s}, st), "launch_prep");
+// kernels.cuh:42-43 — RMSNorm -> permutation -> signs -> Hadamard -> Q8_0.
+inline void launch_prep(const float* x, int ldx, int M, int n, const float* normw, float eps, const Hx& hx,
+                        float* xn_out, int ldxn, const Q8Act& a, cudaStream_t st) {
+  const btf_hx h{hx.block, hx.perm_hd, hx.perm_nk, hx.perm_rep, hx.signs};
+  throw_if(btf_prep(x, ldx, M, n, normw, eps, h, xn_out, ldxn, btf_q8act{a.q, a.d, a.s}, st), "launch_prep");
 }
 
 // kernels.cuh:46-53

@@ -390,3 +390,78 @@ ORC_API void orc_gemv_f64(const uint8_t* codes, const uint16_t* scales, int64_t 
       y[(int64_t)m * N + r] = acc;
     }
 }
+
+/* ------------------------------------------------------------------ prep (norm, permutation, signs, WHT, Q8) */
+
+/* RMSNorm. Follows ref/bonsai-decoder/src/cpu_ops.cpp:121-127 (bd::rmsnorm):
+ * double sum of squares in index order, mean = (float)(sum / n),
+ * scale = 1 / sqrtf(mean + eps), y = x * scale * w (w = NULL: 1). */
+ORC_API void orc_rmsnorm(const float* x, const float* w, int64_t n, float eps, float* y) {
+  double sum = 0.0;
+  for (int64_t i = 0; i < n; ++i) sum += (double)x[i] * x[i];
+  const float mean = (float)(sum / (double)n);
+  const float scale = 1.0f / sqrtf(mean + eps);
+  for (int64_t i = 0; i < n; ++i) y[i] = x[i] * scale * (w ? w[i] : 1.0f);
+}
+
+/* In-place fast Walsh-Hadamard transform of n (power of two) values with the
+ * 1/sqrt(n) scale. Follows ref/bonsai-decoder/src/cpu_ops.cpp:76-88 (bd::fwht):
+ * stages len = 1, 2, 4, ...; butterfly (a, b) -> (a + b, a - b). */
+static void orc_fwht(float* x, int n) {
+  for (int len = 1; len < n; len <<= 1)
+    for (int i = 0; i < n; i += len << 1)
+      for (int j = i; j < i + len; ++j) {
+        const float a = x[j], b = x[j + len];
+        x[j] = a + b;
+        x[j + len] = a - b;
+      }
+  const float s = 1.0f / sqrtf((float)n);
+  for (int i = 0; i < n; ++i) x[i] *= s;
+}
+
+/* Input transform of a folded-Hadamard weight. Follows
+ * ref/bonsai-decoder/src/cpu_ops.cpp:90-111 (bd::hadamard_input): optional
+ * permutation out[d + hd*(r + rep*k)] = x[d + hd*(k + nk*r)] (perm_rep > 1),
+ * optional sign flip, then blockwise FWHT of size `block` (block == 0: copy). */
+ORC_API void orc_hadamard_input(int block, int perm_hd, int perm_nk, int perm_rep, const float* signs, const float* x,
+                                int64_t n, float* out) {
+  if (block <= 0) {
+    if (out != x) memcpy(out, x, (size_t)n * sizeof(float));
+    return;
+  }
+  if (perm_rep > 1) {
+    for (int k = 0; k < perm_nk; ++k)
+      for (int r = 0; r < perm_rep; ++r)
+        for (int d = 0; d < perm_hd; ++d)
+          out[d + (int64_t)perm_hd * (r + perm_rep * k)] = x[d + (int64_t)perm_hd * (k + perm_nk * r)];
+  } else if (out != x) {
+    memcpy(out, x, (size_t)n * sizeof(float));
+  }
+  if (signs)
+    for (int64_t i = 0; i < n; ++i) out[i] *= signs[i];
+  for (int64_t b = 0; b < n; b += block) orc_fwht(out + b, block);
+}
+
+/* The whole prep of M rows (the host form of launch_prep, as the reference's
+ * test_prep builds it, tests/test_gpu_kernels.cpp:117-127): RMSNorm (normw
+ * non-NULL), the input transform, Q8_0 per 32 (orc_q8_block). xn (optional)
+ * receives the normalised, untransformed rows. */
+ORC_API void orc_prep_rows(const float* x, int64_t ldx, int M, int n, const float* normw, float eps, int block,
+                           int perm_hd, int perm_nk, int perm_rep, const float* signs, float* xn, int8_t* q, float* d,
+                           int32_t* s) {
+  float* t = (float*)malloc((size_t)n * sizeof(float));
+  float* u = (float*)malloc((size_t)n * sizeof(float));
+  for (int m = 0; m < M; ++m) {
+    const float* xr = x + (int64_t)m * ldx;
+    if (normw)
+      orc_rmsnorm(xr, normw, n, eps, u);
+    else
+      memcpy(u, xr, (size_t)n * sizeof(float));
+    if (xn) memcpy(xn + (int64_t)m * n, u, (size_t)n * sizeof(float));
+    orc_hadamard_input(block, perm_hd, perm_nk, perm_rep, signs, u, n, t);
+    for (int b = 0; b < n / 32; ++b)
+      s[(int64_t)m * (n / 32) + b] = orc_q8_block(t + b * 32, q + (int64_t)m * n + b * 32, d + (int64_t)m * (n / 32) + b);
+  }
+  free(t);
+  free(u);
+}

@@ -61,6 +61,10 @@ class Oracle:
             "orc_gemv": (None, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i32, _i32]),
             "orc_gemv_swiglu": (None, [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i32]),
             "orc_gemv_f64": (None, [_vp, _vp, _i64, _i64, _vp, _vp, _i32, _vp]),
+            "orc_rmsnorm": (None, [_vp, _vp, _i64, _f32, _vp]),
+            "orc_hadamard_input": (None, [_i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
+            "orc_prep_rows": (None, [_vp, _i64, _i32, _i32, _vp, _f32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
+                                     _vp]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -153,6 +157,47 @@ class Oracle:
         return y
 
 
+def _as_f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _prep_methods(prefix):
+    """rmsnorm / hadamard_input wrappers shared by Oracle and Reference."""
+
+    def rmsnorm(self, x, w, eps):
+        x, w = _as_f32(x), _as_f32(w)
+        y = np.empty_like(x)
+        getattr(self.L, prefix + "rmsnorm")(_p(x), _p(w), x.size, eps, _p(y))
+        return y
+
+    def hadamard_input(self, x, block, perm=(0, 0, 0), signs=None):
+        x, sg = _as_f32(x), _as_f32(signs)
+        out = np.empty_like(x)
+        getattr(self.L, prefix + "hadamard_input")(block, perm[0], perm[1], perm[2], _p(sg), _p(x), x.size, _p(out))
+        return out
+
+    return rmsnorm, hadamard_input
+
+
+Oracle.rmsnorm, Oracle.hadamard_input = _prep_methods("orc_")
+
+
+def _oracle_prep_rows(self, x, normw=None, eps=1e-6, block=0, perm=(0, 0, 0), signs=None):
+    """Host prep of M rows (norm, transform, Q8): q, d, s and the normalised rows."""
+    x = _as_f32(x)
+    M, n = x.shape
+    q = np.empty((M, n), np.int8)
+    d = np.empty((M, n // 32), np.float32)
+    s = np.empty((M, n // 32), np.int32)
+    xn = np.empty((M, n), np.float32)
+    self.L.orc_prep_rows(_p(x), n, M, n, _p(_as_f32(normw)), eps, block, perm[0], perm[1], perm[2], _p(_as_f32(signs)),
+                         _p(xn), _p(q), _p(d), _p(s))
+    return q, d, s, xn
+
+
+Oracle.prep_rows = _oracle_prep_rows
+
+
 class Reference:
     """libbtf_ref.so: the reference's own compiled code (see ref_shim.cpp)."""
 
@@ -173,6 +218,8 @@ class Reference:
             "ref_pool_size": (_i32, [_vp]),
             "ref_gemv": (None, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i64, _i32]),
             "ref_matvec_raw": (None, [_vp, _vp, _i64, _i64, _vp, _vp]),
+            "ref_rmsnorm": (None, [_vp, _vp, _i64, _f32, _vp]),
+            "ref_hadamard_input": (None, [_i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -269,3 +316,6 @@ def panel_decode(panels: np.ndarray, N: int, K: int):
         np.bitwise_or.at(t2, (slice(None), byte[sel]), (codes[:, sel] << sh).astype(np.uint8))
     sc = p[:, :, 2048:].copy().view(np.uint16).reshape(G, S, 8, 8).transpose(0, 3, 1, 2).reshape(G * 8, S * 8)
     return np.ascontiguousarray(t2[:N, :K // 4]), np.ascontiguousarray(sc[:N, :K // 128])
+
+
+Reference.rmsnorm, Reference.hadamard_input = _prep_methods("ref_")

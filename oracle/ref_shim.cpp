@@ -97,3 +97,23 @@ REF_API void ref_matvec_raw(void* pool, const uint8_t* src, int64_t N, int64_t K
   bd::ThreadPool& p = pool ? *static_cast<bd::ThreadPool*>(pool) : one;
   bd::matvec_raw(p, t, x, y, true);
 }
+
+// bd::rmsnorm — ref/bonsai-decoder/src/cpu_ops.cpp:121-127
+REF_API void ref_rmsnorm(const float* x, const float* w, int64_t n, float eps, float* y) { bd::rmsnorm(x, w, n, eps, y); }
+
+// bd::hadamard_input — ref/bonsai-decoder/src/cpu_ops.cpp:90-111
+REF_API void ref_hadamard_input(int block, int perm_hd, int perm_nk, int perm_rep, const float* signs, const float* x,
+                                int64_t n, float* out) {
+  bd::HadamardXform hx;
+  hx.active = block > 0;
+  hx.block = block;
+  std::vector<float> sg;
+  if (signs) {
+    sg.assign(signs, signs + n);
+    hx.signs = &sg;
+  }
+  hx.perm_hd = perm_hd;
+  hx.perm_nk = perm_nk;
+  hx.perm_rep = perm_rep;
+  bd::hadamard_input(hx, x, n, out);
+}

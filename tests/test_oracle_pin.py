@@ -137,3 +137,21 @@ def test_idot_is_code_dot_minus_sum(orc, ref):
     for sb in range(K // 32):
         cd = ref.L.ref_sub_dot(int(cw[2 * sb]), int(cw[2 * sb + 1]), aw[sb * 8:].ctypes.data)
         assert cd - s[0, sb] == idot[0, 0, sb]
+
+
+@pytest.mark.parametrize("n,block,perm,signs", [(1024, 64, False, True), (5120, 1024, False, True),
+                                                (2048, 128, True, True), (256, 0, False, False),
+                                                (17408, 1024, False, True), (64, 32, True, False)])
+def test_prep_transform_matches_reference(orc, ref, n, block, perm, signs):
+    # bd::rmsnorm and bd::hadamard_input (cpu_ops.cpp:90-127) against the restatement,
+    # bit for bit, on the shapes of the reference's test_prep (test_gpu_kernels.cpp:557-561)
+    rng = np.random.default_rng(n + block)
+    x = (rng.standard_normal(n) * 3).astype(np.float32)
+    w = rng.standard_normal(n).astype(np.float32)
+    assert np.array_equal(orc.rmsnorm(x, w, 1e-6).view(np.uint32), ref.rmsnorm(x, w, 1e-6).view(np.uint32))
+    assert np.array_equal(orc.rmsnorm(x, None, 1e-6).view(np.uint32), ref.rmsnorm(x, None, 1e-6).view(np.uint32))
+    sg = np.where(rng.random(n) < 0.5, -1.0, 1.0).astype(np.float32) if signs else None
+    pm = (32, n // 64, 2) if perm else (0, 0, 0)
+    a = orc.hadamard_input(x, block, pm, sg)
+    b = ref.hadamard_input(x, block, pm, sg)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
