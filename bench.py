@@ -423,7 +423,9 @@ def gpu_arm(args):
             if world == 1 else None,
             "device_error_word": dev_err,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * N_LAYERS * 8,
+            # per step: 4 x (quantiser + GEMV) per layer; with N > 1 also one tag check per
+            # layer, the epoch advance and the cross-rank barrier
+            "gpu_launches": args.steps * (N_LAYERS * 8 + (N_LAYERS + 2 if world > 1 else 0)),
             "clocks": clocks.report(),
         }
         if world == 1:
