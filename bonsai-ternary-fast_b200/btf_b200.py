@@ -34,6 +34,8 @@ EXPORTS = (
     "btf_quant_q8", "btf_gemv", "btf_gemv_f32", "btf_device_error", "btf_gemv_idot", "btf_gemm",
     "btf_gemv_gather", "btf_alloc", "btf_free", "btf_ipc_handle", "btf_ipc_open", "btf_ipc_close",
     "btf_gather_epoch_advance", "btf_gather_wait", "btf_gather_barrier", "btf_prep",
+    "btf_gguf_open", "btf_gguf_close", "btf_gguf_tensor_count", "btf_gguf_find", "btf_gguf_tensor",
+    "btf_gguf_load_panels",
 )
 
 
@@ -60,6 +62,13 @@ class HxC(ctypes.Structure):
 
     _fields_ = [("block", ctypes.c_int), ("perm_hd", ctypes.c_int), ("perm_nk", ctypes.c_int),
                 ("perm_rep", ctypes.c_int), ("signs", ctypes.c_void_p)]
+
+
+class GgufTensorC(ctypes.Structure):
+    """btf_gguf_tensor: one tensor of an open GGUF file."""
+
+    _fields_ = [("name", ctypes.c_char_p), ("n_dims", ctypes.c_int), ("ne", ctypes.c_int64 * 4),
+                ("type", ctypes.c_uint32), ("data", ctypes.c_void_p), ("bytes", ctypes.c_uint64)]
 
 
 class GatherC(ctypes.Structure):
@@ -116,6 +125,12 @@ def lib() -> ctypes.CDLL:
         "btf_gather_wait": (i32, [ctypes.POINTER(TaggedBufC), i32, vp, vp]),
         "btf_gather_barrier": (i32, [ctypes.POINTER(GatherC), vp]),
         "btf_prep": (i32, [vp, i32, i32, i32, vp, ctypes.c_float, HxC, vp, i32, Q8ActC, vp]),
+        "btf_gguf_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]),
+        "btf_gguf_close": (i32, [vp]),
+        "btf_gguf_tensor_count": (i64, [vp]),
+        "btf_gguf_find": (i64, [vp, ctypes.c_char_p]),
+        "btf_gguf_tensor": (i32, [vp, i64, ctypes.POINTER(GgufTensorC)]),
+        "btf_gguf_load_panels": (i32, [vp, i64, vp, i64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -367,3 +382,58 @@ def prep(x, normw=None, eps: float = 1e-6, block: int = 0, perm=(0, 0, 0), signs
     check(lib().btf_prep(_ptr(x), x.stride(0), M, n, _ptr(normw), eps, hx, _ptr(xn_out), ldxn, act.c(),
                          _stream(stream)), "btf_prep")
     return act
+
+
+PTQ1_0 = 143
+
+
+class GgufFile:
+    """An open GGUF file (btf_gguf_*): tensor table and PTQ1_0 -> panel loading."""
+
+    def __init__(self, path: str):
+        h = ctypes.c_void_p()
+        check(lib().btf_gguf_open(path.encode(), ctypes.byref(h)), "btf_gguf_open")
+        self.h = h.value
+
+    def close(self) -> None:
+        if self.h:
+            lib().btf_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __len__(self) -> int:
+        return int(lib().btf_gguf_tensor_count(self.h))
+
+    def find(self, name: str) -> int:
+        return int(lib().btf_gguf_find(self.h, name.encode()))
+
+    def tensor(self, index: int) -> dict:
+        t = GgufTensorC()
+        check(lib().btf_gguf_tensor(self.h, index, ctypes.byref(t)), "btf_gguf_tensor")
+        return {"name": t.name.decode(), "ne": list(t.ne)[:t.n_dims], "type": t.type, "data": t.data,
+                "bytes": int(t.bytes)}
+
+    def data(self, index: int):
+        """The tensor's bytes as a read-only numpy view of the mapping."""
+        import numpy as np
+
+        t = self.tensor(index)
+        buf = (ctypes.c_uint8 * t["bytes"]).from_address(t["data"])
+        return np.frombuffer(buf, dtype=np.uint8)
+
+    def load_panels(self, index: int, staging_bytes: int = 8 << 20, stream=None) -> PanelMatrix:
+        """A 2-D PTQ1_0 tensor -> resident panels on the current device."""
+        torch = _torch()
+        t = self.tensor(index)
+        K, N = t["ne"][0], t["ne"][1]
+        dev = torch.device("cuda", torch.cuda.current_device())
+        ensure_init(dev.index)
+        out = torch.empty(panel_bytes(N, K), dtype=torch.uint8, device=dev)
+        check(lib().btf_gguf_load_panels(self.h, index, _ptr(out), staging_bytes, _stream(stream)),
+              "btf_gguf_load_panels")
+        return PanelMatrix(out, N, K)

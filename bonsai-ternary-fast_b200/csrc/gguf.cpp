@@ -1,0 +1,296 @@
+// GGUF (v2/v3) tensor access and the load path for PTQ1_0 weights: file ->
+// mmap -> pinned staging -> GPU repack into the panel layout. The reference's
+// load path is bd::Gguf (ref/bonsai-decoder/src/gguf.cpp) + GpuDecoder::upload_mat
+// (src/cuda/gpu_decoder.cu:284-300); this reader is written from the public GGUF
+// layout:
+//   u32 magic "GGUF", u32 version, u64 tensor_count, u64 kv_count,
+//   kv_count x { string key, u32 value type, value },
+//   tensor_count x { string name, u32 n_dims, u64 ne[n_dims], u32 type, u64 offset },
+//   data section at the header end rounded up to general.alignment (default 32);
+//   strings are u64 length + bytes; arrays are u32 element type + u64 count + elements.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "btf_b200.h"
+
+namespace btf {
+int fail(int status, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+}  // namespace btf
+
+namespace {
+
+constexpr uint32_t kGgufMagic = 0x46554747u;  // "GGUF"
+constexpr uint32_t kTypePtq1_0 = 143;
+
+struct Tensor {
+  std::string name;
+  int n_dims = 0;
+  int64_t ne[4] = {1, 1, 1, 1};
+  uint32_t type = 0;
+  uint64_t offset = 0;
+  uint64_t bytes = 0;
+};
+
+struct File {
+  int fd = -1;
+  const uint8_t* map = nullptr;
+  size_t size = 0;
+  uint32_t version = 0;
+  uint64_t alignment = 32;
+  uint64_t data_start = 0;
+  std::vector<Tensor> tensors;
+  ~File() {
+    if (map) munmap(const_cast<uint8_t*>(map), size);
+    if (fd >= 0) close(fd);
+  }
+};
+
+// Bounds-checked little-endian reader over the mapped header.
+struct Reader {
+  const uint8_t* p;
+  size_t n, pos = 0;
+  bool ok = true;
+  bool need(size_t k) {
+    if (!ok || k > n - pos) ok = false;
+    return ok;
+  }
+  template <class T>
+  T get() {
+    T v{};
+    if (need(sizeof(T))) {
+      std::memcpy(&v, p + pos, sizeof(T));
+      pos += sizeof(T);
+    }
+    return v;
+  }
+  std::string str() {
+    const uint64_t len = get<uint64_t>();
+    if (!ok || !need(len)) return {};
+    std::string s(reinterpret_cast<const char*>(p + pos), len);
+    pos += len;
+    return s;
+  }
+  void skip(uint64_t k) {
+    if (need(k)) pos += k;
+  }
+};
+
+// Bytes of one scalar of a metadata value type (0 for strings and arrays).
+size_t scalar_bytes(uint32_t t) {
+  switch (t) {
+    case 0: case 1: case 7: return 1;   // u8, i8, bool
+    case 2: case 3: return 2;           // u16, i16
+    case 4: case 5: case 6: return 4;   // u32, i32, f32
+    case 10: case 11: case 12: return 8;  // u64, i64, f64
+    default: return 0;
+  }
+}
+
+// Skips one metadata value; returns its integer value when it is an integer
+// scalar (for general.alignment), else -1.
+int64_t skip_value(Reader& r, uint32_t type, int depth = 0) {
+  if (type == 8) {  // string
+    r.str();
+    return -1;
+  }
+  if (type == 9) {  // array
+    if (depth > 0) {
+      r.ok = false;  // nested arrays are not part of the format this reader accepts
+      return -1;
+    }
+    const uint32_t et = r.get<uint32_t>();
+    const uint64_t count = r.get<uint64_t>();
+    const size_t eb = scalar_bytes(et);
+    if (et == 8) {
+      for (uint64_t i = 0; i < count && r.ok; ++i) r.str();
+    } else if (eb) {
+      if (count > (r.n - r.pos) / eb) r.ok = false;
+      else r.skip(count * eb);
+    } else {
+      r.ok = false;
+    }
+    return -1;
+  }
+  const size_t b = scalar_bytes(type);
+  if (!b) {
+    r.ok = false;
+    return -1;
+  }
+  int64_t v = 0;
+  if (b == 4 && (type == 4 || type == 5)) v = type == 4 ? (int64_t)r.get<uint32_t>() : r.get<int32_t>();
+  else if (b == 8 && (type == 10 || type == 11)) v = type == 10 ? (int64_t)r.get<uint64_t>() : r.get<int64_t>();
+  else {
+    r.skip(b);
+    return -1;
+  }
+  return v;
+}
+
+// Data bytes of a tensor for the types this library reads; 0 if unknown.
+uint64_t tensor_bytes(uint32_t type, int64_t n_elem, int64_t ne0) {
+  switch (type) {
+    case 0: return (uint64_t)n_elem * 4;                                   // f32
+    case 1: case 30: return (uint64_t)n_elem * 2;                          // f16, bf16
+    case 8: return ne0 % 32 ? 0 : (uint64_t)(n_elem / 32) * 34;           // q8_0
+    case kTypePtq1_0: return ne0 % 128 ? 0 : (uint64_t)(n_elem / 128) * 28;
+    default: return 0;
+  }
+}
+
+int parse(File& f) {
+  Reader r{f.map, f.size};
+  if (r.get<uint32_t>() != kGgufMagic) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: not a GGUF file");
+  f.version = r.get<uint32_t>();
+  if (f.version < 2 || f.version > 3) return btf::fail(BTF_ERR_UNSUPPORTED, "btf_gguf_open: GGUF version %u", f.version);
+  const uint64_t n_tensors = r.get<uint64_t>(), n_kv = r.get<uint64_t>();
+  if (!r.ok || n_tensors > (1u << 24) || n_kv > (1u << 24)) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: bad header");
+  for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
+    const std::string key = r.str();
+    const uint32_t type = r.get<uint32_t>();
+    const int64_t v = skip_value(r, type);
+    if (r.ok && key == "general.alignment" && v > 0) f.alignment = (uint64_t)v;
+  }
+  f.tensors.resize(n_tensors);
+  for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
+    Tensor& t = f.tensors[i];
+    t.name = r.str();
+    const uint32_t nd = r.get<uint32_t>();
+    if (nd < 1 || nd > 4) {
+      r.ok = false;
+      break;
+    }
+    t.n_dims = (int)nd;
+    int64_t n_elem = 1;
+    for (uint32_t d = 0; d < nd; ++d) {
+      t.ne[d] = (int64_t)r.get<uint64_t>();
+      if (t.ne[d] <= 0 || t.ne[d] > (int64_t(1) << 40) || n_elem > (int64_t(1) << 50) / t.ne[d]) r.ok = false;
+      else n_elem *= t.ne[d];
+    }
+    t.type = r.get<uint32_t>();
+    t.offset = r.get<uint64_t>();
+    t.bytes = tensor_bytes(t.type, n_elem, t.ne[0]);
+  }
+  if (!r.ok) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: truncated or malformed header");
+  if (f.alignment == 0 || (f.alignment & (f.alignment - 1))) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: bad alignment");
+  f.data_start = (r.pos + f.alignment - 1) / f.alignment * f.alignment;
+  for (const Tensor& t : f.tensors)
+    if (f.data_start > f.size || t.offset > f.size - f.data_start || t.bytes > f.size - f.data_start - t.offset)
+      return btf::fail(BTF_ERR_ARG, "btf_gguf_open: tensor %s lies beyond the file", t.name.c_str());
+  return BTF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int btf_gguf_open(const char* path, void** handle) {
+  if (!path || !handle) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: null argument");
+  *handle = nullptr;
+  File* f = new File;
+  f->fd = open(path, O_RDONLY);
+  struct stat st;
+  if (f->fd < 0 || fstat(f->fd, &st) != 0 || st.st_size < 24) {
+    delete f;
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_open: cannot open %s", path);
+  }
+  f->size = (size_t)st.st_size;
+  void* m = mmap(nullptr, f->size, PROT_READ, MAP_PRIVATE, f->fd, 0);
+  if (m == MAP_FAILED) {
+    delete f;
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_open: mmap failed for %s", path);
+  }
+  f->map = static_cast<const uint8_t*>(m);
+  if (int rc = parse(*f)) {
+    delete f;
+    return rc;
+  }
+  *handle = f;
+  return BTF_OK;
+}
+
+int btf_gguf_close(void* handle) {
+  delete static_cast<File*>(handle);
+  return BTF_OK;
+}
+
+int64_t btf_gguf_tensor_count(const void* handle) {
+  return handle ? (int64_t) static_cast<const File*>(handle)->tensors.size() : -1;
+}
+
+int64_t btf_gguf_find(const void* handle, const char* name) {
+  if (!handle || !name) return -1;
+  const File* f = static_cast<const File*>(handle);
+  for (size_t i = 0; i < f->tensors.size(); ++i)
+    if (f->tensors[i].name == name) return (int64_t)i;
+  return -1;
+}
+
+int btf_gguf_tensor(const void* handle, int64_t index, btf_gguf_tensor_info* out) {
+  const File* f = static_cast<const File*>(handle);
+  if (!f || !out || index < 0 || index >= (int64_t)f->tensors.size())
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_tensor: bad handle or index");
+  const Tensor& t = f->tensors[(size_t)index];
+  out->name = t.name.c_str();
+  out->n_dims = t.n_dims;
+  for (int d = 0; d < 4; ++d) out->ne[d] = t.ne[d];
+  out->type = t.type;
+  out->data = f->map + f->data_start + t.offset;
+  out->bytes = t.bytes;
+  return BTF_OK;
+}
+
+int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_t staging_bytes, void* stream) {
+  const File* f = static_cast<const File*>(handle);
+  if (!f || !panels || index < 0 || index >= (int64_t)f->tensors.size())
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_load_panels: bad handle, index or panel buffer");
+  const Tensor& t = f->tensors[(size_t)index];
+  if (t.type != kTypePtq1_0 || t.n_dims != 2)
+    return btf::fail(BTF_ERR_UNSUPPORTED, "btf_gguf_load_panels: %s is not a 2-D PTQ1_0 tensor", t.name.c_str());
+  const int64_t K = t.ne[0], N = t.ne[1];
+  const int64_t row_bytes = K / 128 * 28, S = (K + 1023) / 1024;
+  // whole 8-row groups per chunk, so every chunk starts a panel row group
+  const int64_t rows_per = std::max<int64_t>(8, staging_bytes / row_bytes / 8 * 8);
+  const size_t stage = (size_t)(rows_per * row_bytes);
+  const uint8_t* src = f->map + f->data_start + t.offset;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // two pinned staging buffers, read by the repack kernel over the bus (mapped)
+  void* buf[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  int rc = BTF_OK;
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+    e = cudaHostAlloc(&buf[i], stage, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) rc = btf::cuda_fail(e, "btf_gguf_load_panels: staging");
+  int slot = 0;
+  for (int64_t r0 = 0; r0 < N && rc == BTF_OK; r0 += rows_per, slot ^= 1) {
+    const int64_t rows = std::min(rows_per, N - r0);
+    if ((e = cudaEventSynchronize(ev[slot])) != cudaSuccess) {  // this buffer's previous repack is done
+      rc = btf::cuda_fail(e, "btf_gguf_load_panels: staging wait");
+      break;
+    }
+    std::memcpy(buf[slot], src + r0 * row_bytes, (size_t)(rows * row_bytes));
+    uint8_t* dst = static_cast<uint8_t*>(panels) + (r0 / 8) * S * BTF_PANEL_BYTES;
+    if ((rc = btf_repack_panels(buf[slot], rows, K, dst, stream)) != BTF_OK) break;
+    if ((e = cudaEventRecord(ev[slot], st)) != cudaSuccess) rc = btf::cuda_fail(e, "btf_gguf_load_panels: record");
+  }
+  if ((e = cudaStreamSynchronize(st)) != cudaSuccess && rc == BTF_OK) rc = btf::cuda_fail(e, "btf_gguf_load_panels");
+  for (int i = 0; i < 2; ++i) {
+    if (ev[i]) cudaEventDestroy(ev[i]);
+    if (buf[i]) cudaFreeHost(buf[i]);
+  }
+  return rc;
+}
+
+}  // extern "C"

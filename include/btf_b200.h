@@ -229,6 +229,30 @@ int btf_ipc_handle(void* ptr, void* handle64);
 int btf_ipc_open(const void* handle64, void** ptr);
 int btf_ipc_close(void* ptr);
 
+/* ---- load path: GGUF (v2/v3) -> resident panels
+ * Replaces bd::Gguf + GpuDecoder::upload_mat (ref/bonsai-decoder/src/gguf.cpp,
+ * src/cuda/gpu_decoder.cu:284-300). The file is mmapped read-only; tensor data
+ * is reached without copying. Load-time functions: they may allocate and
+ * synchronise (not for use inside stream capture). */
+typedef struct btf_gguf_tensor_info {
+  const char* name;  /* valid until btf_gguf_close */
+  int n_dims;
+  int64_t ne[4];     /* ggml order: ne[0] is the contiguous (row) dimension */
+  uint32_t type;     /* ggml type id (PTQ1_0 = 143) */
+  const void* data;  /* host pointer into the mapping */
+  uint64_t bytes;    /* data bytes for f32/f16/bf16/q8_0/PTQ1_0, else 0 */
+} btf_gguf_tensor_info;
+int btf_gguf_open(const char* path, void** handle);
+int btf_gguf_close(void* handle);
+int64_t btf_gguf_tensor_count(const void* handle);
+int64_t btf_gguf_find(const void* handle, const char* name); /* index, or -1 */
+int btf_gguf_tensor(const void* handle, int64_t index, btf_gguf_tensor_info* out);
+/* A 2-D PTQ1_0 tensor [ne1 rows][ne0 columns] -> panels (btf_panel_bytes(ne1, ne0)
+ * bytes on the device): whole 8-row groups are staged through two pinned
+ * buffers of about staging_bytes and repacked on the GPU as they arrive.
+ * Returns after the panels are complete. */
+int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_t staging_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

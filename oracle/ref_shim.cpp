@@ -12,6 +12,7 @@
 // Used by tests/ to pin oracle/oracle.c, and by bench.py's CPU baseline /
 // `--impl reference` arm as the reference's own CPU GEMV.
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <vector>
 
@@ -116,4 +117,33 @@ REF_API void ref_hadamard_input(int block, int perm_hd, int perm_nk, int perm_re
   hx.perm_nk = perm_nk;
   hx.perm_rep = perm_rep;
   bd::hadamard_input(hx, x, n, out);
+}
+
+// bd::GgufWriter — ref/bonsai-decoder/include/bd/gguf.hpp:88-114: writes a GGUF
+// file with a few metadata entries of several kinds and the given 2-D tensors
+// (ne0 = row length, ne1 = rows). Used to make test fixtures.
+REF_API int ref_gguf_write(const char* path, int n, const char** names, const int64_t* ne0, const int64_t* ne1,
+                           const uint32_t* types, const uint8_t** data, const uint64_t* bytes, uint32_t alignment) {
+  bd::GgufWriter w;
+  w.kv_str("general.architecture", "bonsai-test");
+  w.kv_u32("test.u32", 7u);
+  w.kv_arr_f32("test.floats", {1.5f, -2.0f, 3.25f});
+  w.kv_arr_str("test.strings", {"alpha", "beta"});
+  w.kv_bool("test.flag", true);
+  for (int i = 0; i < n; ++i)
+    w.tensor(names[i], {ne0[i], ne1[i]}, types[i], std::vector<uint8_t>(data[i], data[i] + bytes[i]));
+  const std::vector<uint8_t> img = w.finish(alignment);
+  FILE* f = std::fopen(path, "wb");
+  if (!f) return 1;
+  const size_t wr = std::fwrite(img.data(), 1, img.size(), f);
+  std::fclose(f);
+  return wr == img.size() ? 0 : 2;
+}
+
+// bd::Gguf::open — the reference's reader, for cross-checking where a tensor's
+// data starts in the file.
+REF_API int64_t ref_gguf_tensor_offset(const char* path, const char* name) {
+  auto g = bd::Gguf::open(path);
+  const bd::GgufTensor* t = g->tensor(name);
+  return t ? (int64_t)(g->data_offset + t->offset) : -1;  // byte offset of the tensor data in the file
 }

@@ -1,0 +1,73 @@
+"""GGUF load path (btf_gguf_*): the library's own reader against a file written
+by the reference's GGUF writer (tests/golden/tiny_ptq.gguf, made by
+tests/golden/make_gguf.py with bd::GgufWriter), malformed-file rejection, and
+(-m gpu) PTQ1_0 -> panels on the device equal to the host repack twin."""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+META = json.load(open(os.path.join(GOLDEN, "MANIFEST_GGUF.json")))
+PATH = os.path.join(GOLDEN, META["file"])
+
+
+def test_fixture_checksum():
+    assert hashlib.sha256(open(PATH, "rb").read()).hexdigest() == META["sha256"]
+
+
+def test_reader_tensor_table_and_data(btf):
+    with btf.GgufFile(PATH) as g:
+        assert len(g) == len(META["tensors"])
+        for i, t in enumerate(META["tensors"]):
+            assert g.find(t["name"]) == i
+            info = g.tensor(i)
+            assert info["name"] == t["name"] and info["ne"] == [t["ne0"], t["ne1"]] and info["type"] == t["type"]
+            assert info["bytes"] == t["bytes"]
+            assert hashlib.sha256(g.data(i).tobytes()).hexdigest() == t["sha256"]
+        assert g.find("no.such.tensor") == -1
+
+
+def test_ptq_tensor_repacks_like_reference(btf, orc):
+    import oracle
+    import synth
+
+    with btf.GgufFile(PATH) as g:
+        for t in META["tensors"]:
+            if t["type"] != btf.PTQ1_0:
+                continue
+            K, N = t["ne0"], t["ne1"]
+            src = g.data(g.find(t["name"])).reshape(N, K // 128 * 28)
+            assert np.array_equal(src, synth.ternary_ptq(N, K, seed=t["seed"]))
+            codes, scales = oracle.panel_decode(btf.repack_panels_host(src, N, K), N, K)[:2]
+            c_ref, s_ref = orc.repack_t2(src, N, K)
+            assert np.array_equal(codes, c_ref) and np.array_equal(scales, s_ref)
+
+
+def test_reader_rejects_malformed_files(btf, tmp_path):
+    data = open(PATH, "rb").read()
+    cases = {"missing": None, "truncated": data[:300], "magic": b"GGUX" + data[4:],
+             "version": data[:4] + (9).to_bytes(4, "little") + data[8:],
+             "tensor_beyond": data[:len(data) - 4096]}
+    for name, blob in cases.items():
+        p = tmp_path / f"{name}.gguf"
+        if blob is not None:
+            p.write_bytes(blob)
+        with pytest.raises(RuntimeError):
+            btf.GgufFile(str(p))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("staging", [1 << 20, 8 * 288])  # one chunk; one 8-row group per chunk
+def test_load_panels_on_device_equals_host_twin(cuda, btf, staging):
+    with btf.GgufFile(PATH) as g:
+        for t in META["tensors"]:
+            if t["type"] != btf.PTQ1_0:
+                continue
+            i = g.find(t["name"])
+            pm = g.load_panels(i, staging_bytes=staging)
+            host = btf.repack_panels_host(g.data(i).reshape(t["ne1"], -1), t["ne1"], t["ne0"])
+            assert np.array_equal(pm.panels.cpu().numpy(), host)
