@@ -82,9 +82,6 @@ constexpr int kFuseCluster = BTF_GEMV_FUSE_CLUSTER;
 // cluster path: start the weight ring only once the activation is quantised
 constexpr bool kRingAfterStage = BTF_GEMV_RING_AFTER_STAGE;
 static_assert(kFuseCluster == 1 || kFuseCluster == 2 || kFuseCluster == 4 || kFuseCluster == 8, "cluster size");
-#ifndef BTF_GEMV_FUSE_QUAD
-#define BTF_GEMV_FUSE_QUAD 0
-#endif
 #ifndef BTF_GEMV_PREWAIT
 #define BTF_GEMV_PREWAIT 2
 #endif
@@ -334,7 +331,6 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
 
   // ---- activation -> shared memory (padded to whole slices with q = 0)
   if constexpr (FUSE) {
-#if !BTF_GEMV_FUSE_QUAD
     // one thread per (row, 32-column block): the per-block division and fp16
     // rounding run once per block; the next round's loads are in flight while
     // this round is quantised, and the weight ring starts behind the first loads
@@ -399,42 +395,6 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
         for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
       }
     }
-#else
-    // every thread owns 4 consecutive columns of a row; all loads of a row are
-    // issued before any is used (kQuads per thread covers K <= 18432 in one round)
-    constexpr int kQuads = 18;
-    const int nq = nsp * 8;  // quads incl. padding
-    const bool vec = ((reinterpret_cast<uintptr_t>(p.x) | ((uintptr_t)p.ldx * 4)) & 15) == 0;
-    for (int m = 0; m < NB; ++m) {
-      const bool row_ok = m < p.nb;
-      const float* xr = p.x + (int64_t)(p.m0 + (row_ok ? m : 0)) * p.ldx;
-      for (int base = 0; base < nq; base += kQuads * kThreads) {
-        float4 v[kQuads];
-#pragma unroll
-        for (int i = 0; i < kQuads; ++i) {
-          const int qi = base + i * kThreads + (int)threadIdx.x;
-          v[i] = (row_ok && qi < p.nsub * 8) ? load4(xr + qi * 4, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int i = 0; i < kQuads; ++i) {
-          const int qi = base + i * kThreads + (int)threadIdx.x;
-          if (base + i * kThreads < nq && qi < nq) {  // warp-uniform: nq = S * 256 is a multiple of kThreads
-            float dq;
-            int sum;
-            const uint32_t q4 = q8_quad(v[i], dq, sum);
-            const int sb = qi >> 3, part = qi & 7;
-            uint32_t* dstq = reinterpret_cast<uint32_t*>(part < 4 ? qa_s : qb_s) + (m * nsp + sb) * 4 + (part & 3);
-            *dstq = q4;
-            if (part == 0) {
-              d_s[m * nsp + sb] = dq;
-              ms_s[m * nsp + sb] = kMagicInt - sum;
-            }
-          }
-        }
-      }
-    }
-    start_ring();
-#endif
   } else {
     // chunks of kStageIters items per thread (one chunk covers K <= 17408 for NB = 1)
     constexpr int kStageIters = (NB * 544 + kThreads - 1) / kThreads;
