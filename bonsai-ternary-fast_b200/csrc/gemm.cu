@@ -10,18 +10,29 @@
 // tcgen05.mma.kind::i8 (M=128, N=64, K=32) per 32-column step, each into its
 // own TMEM region, and the CUDA-core epilogue does the fp32 work.
 //
+// Epilogue arithmetic: one packed FMA and one packed add per element per step.
+// Before each data MMA a bias MMA of two constant tiles (2 x 64 over 32 columns)
+// sets the region to 4096, so the region ends as P = idot + 4096 in [0, 8192].
+// P's bits read as an fp32 value are the denormal P * 2^-149, and
+//   fma(d * 2^110, P * 2^-149, -d * 2^-27) = RN(d * idot) * 2^-39
+// exactly: the FMA's product is exact, d * 2^110 and d * 2^-27 are exact powers
+// of two times d, and the one rounding of a normal result commutes with the
+// 2^-39. The 2^39 returns in the weight scale (scale * 2^39, exact), so no
+// integer-to-float conversion runs. Q8 scales are fp16 values (0 or 2^-24 ..
+// 65504, or inf), so every finite d takes this path; |d| >= 2^18, inf and NaN
+// take a conversion path instead.
+//
 // One CTA computes a 128 x 64 output tile; warp roles:
 //   warp 0      producer: TMA (tensor map, 128B swizzle) of the int8
-//               activation tile [128 rows][128 cols] per 128-column chunk, and
-//               1-D bulk copies of the weight panels (8 rows x 1024 cols each);
+//               activation tile [128 rows][128 cols] per 128-column chunk;
 //   warp 1      MMA issuer (one thread) + TMEM owner (alloc / dealloc);
-//   warps 2-5   expand the 2-bit codes of the chunk into int8 trits in the
+//   warps 2-3   expand the 2-bit codes of the chunk into int8 trits in the
 //               canonical K-major SW128 layout the MMA reads, and stage the
-//               chunk's activation scales d and fp32 weight scales;
-//   warps 6-21  epilogue: TMEM -> registers (tcgen05.ld 32x32b, 16 columns),
-//               per step T += d * idot, per 128-column block acc += scale * T;
-//               MMA completion and TMEM release are signalled once per chunk
-//               (4 steps), with 2 chunks in flight in TMEM.
+//               chunk's fp32 weight scales;
+//   warps 4-19  epilogue: TMEM -> registers (tcgen05.ld 32x32b, 16 columns),
+//               per step T += RN(d * idot), per 128-column block
+//               acc += scale * T. TMEM holds 4 groups of 2 steps; a group is
+//               released as soon as its registers are loaded, before the math.
 // Every wait is bounded; on a time-out the kernel records an error word, stops
 // issuing work, waits (bounded) for its MMAs, frees TMEM and returns.
 #include <cuda.h>
@@ -39,40 +50,61 @@ constexpr int kTileN = 64;
 constexpr int kChunk = 128;          // K columns per pipeline chunk (one scale block)
 constexpr int kStepsPerChunk = 4;    // 32-column MMA steps per chunk
 #ifndef BTF_GEMM_STAGES
-#define BTF_GEMM_STAGES 8
+#define BTF_GEMM_STAGES 7
 #endif
 #ifndef BTF_GEMM_RASTER_M
 #define BTF_GEMM_RASTER_M 1
 #endif
-constexpr int kStagesA = BTF_GEMM_STAGES;  // A / B stages (chunks): freed by the MMA alone
-constexpr int kStagesS = 8;          // weight-scale stages (freed by the epilogue)
-constexpr int kPrefetch = 4;         // chunks of weight codes the expanders hold in registers
+constexpr int kStagesA = BTF_GEMM_STAGES;  // input stages (chunks), all filled by TMA
+constexpr int kStagesS = 8;          // fp32 weight-scale stages (written by the expanders, freed by the epilogue)
 constexpr int kDRegions = 8;         // TMEM accumulator regions (one per in-flight step)
-constexpr int kChunkSlots = kDRegions / kStepsPerChunk;  // chunks in flight in TMEM (2): one barrier pair each
+constexpr int kStepsPerGroup = 2;    // steps per TMEM group (one mma_done / d_free barrier pair)
+constexpr int kGroupsPerChunk = kStepsPerChunk / kStepsPerGroup;
+constexpr int kGroupSlots = kDRegions / kStepsPerGroup;  // groups in flight in TMEM (4)
 constexpr int kTmemCols = kDRegions * kTileN;  // 512: all of TMEM
 constexpr int kEpiWarps = 16;        // 4 per SMSP: TMEM-load latency of one hides behind the others' math
 constexpr int kEpiCols = kTileN * 4 / kEpiWarps;  // columns per epilogue thread (16)
-constexpr int kThreads = (6 + kEpiWarps) * 32;
-constexpr int kExpWarp0 = 2, kEpiWarp0 = 6;
+constexpr int kExpWarps = 2;         // code expanders (64 threads: 2 row quads x 16 columns each)
+constexpr int kExpWarp0 = 2, kEpiWarp0 = kExpWarp0 + kExpWarps;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 20 warps: 5 per SMSP leaves 96 registers a thread
+// bias MMA: every region starts at sum over 32 columns of kBiasA * kBiasB
+constexpr int kBiasA = 2, kBiasB = 64, kBias = 32 * kBiasA * kBiasB;  // 4096 >= 32 * 128
+static_assert(kBias == 4096, "the bias is a power of two");
 constexpr uint64_t kGemmWaitNs = 1000000000ull;
 
+// One input stage s holds chunk c (c % kStagesA == s), all brought by the producer's TMA:
+//   A    [128 rows][128 cols] int8 activations (128B swizzle)
+//   C    raw 2-bit codes of the tile's 8 row groups: [group][quad h][half v][64 B]
+//   R    raw fp16 weight scales: [group][row][1] (16 B per group)
+//   D    activation block scales d: [128 rows][4] fp32
+// and B[s], the int8 trits the expanders write from C[s].
 constexpr int kABytes = kTileM * kChunk;                  // 16 KB
 constexpr int kBBytes = kTileN * kChunk;                  // 8 KB
+constexpr int kCBytes = kTileN * kChunk / 4;              // 2 KB
+constexpr int kRBytes = kTileN * 2;                       // 128 B
+constexpr int kDBytes = kTileM * kStepsPerChunk * 4;      // 2 KB
+constexpr int kStageTx = kABytes + kCBytes + kRBytes + kDBytes;
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStagesA * kABytes;
-constexpr int kOffS = kOffB + kStagesA * kBBytes;          // s: [stage][64] fp32 weight scales
-constexpr int kOffBar = kOffS + kStagesS * kTileN * 4;
-constexpr int kNumBars = 3 * kStagesA + 2 * kStagesS + 2 * kChunkSlots + 4;
+constexpr int kOffC = kOffB + kStagesA * kBBytes;
+constexpr int kOffD = kOffC + kStagesA * kCBytes;
+constexpr int kOffR = kOffD + kStagesA * kDBytes;
+constexpr int kOffS = kOffR + kStagesA * kRBytes;          // s: [stage][64] fp32 weight scales * 2^39
+constexpr int kOffBiasA = (kOffS + kStagesS * kTileN * 4 + 1023) / 1024 * 1024;  // [128][128] bytes of kBiasA
+constexpr int kOffBiasB = kOffBiasA + kABytes;            // [64][128] bytes of kBiasB
+constexpr int kOffBar = kOffBiasB + kBBytes;
+constexpr int kNumBars = 3 * kStagesA + 2 * kStagesS + 2 * kGroupSlots + 4;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;      // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+constexpr int kStgLd = kTileN + 4;  // output staging row (floats): conflict-free float4 writes
+static_assert(kTileM * kStgLd * 4 <= kStagesA * kABytes, "output staging fits the A ring");
+static_assert(kOffC % 128 == 0 && kOffD % 128 == 0 && kOffR % 128 == 0, "TMA destinations");
 
 struct GemmParams {
-  const uint8_t* pan;  // weight panels of an [N][K] matrix
-  int N, M, K, S;
+  int N, M, K;
   float* y;
   int ldy;
-  const float* d;      // activation block scales [M][K/32]
   int mode;            // BTF_STORE / BTF_ADD
   int* err;
 };
@@ -114,14 +146,40 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t addr, uint32_t (&v)[16]
       : "r"(addr)
       : "memory");
 }
-// The wait names the destination registers as read-write operands, so the
-// compiler orders every use of them after it.
+// Waits for this thread's tcgen05.ld (two x16 loads). The wait names the
+// destination registers as read-write operands, so the compiler orders every
+// use of them after it.
+__device__ __forceinline__ void tmem_wait16x2(uint32_t (&v)[16], uint32_t (&w)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+                 "+r"(w[0]), "+r"(w[1]), "+r"(w[2]), "+r"(w[3]), "+r"(w[4]), "+r"(w[5]), "+r"(w[6]), "+r"(w[7]),
+                 "+r"(w[8]), "+r"(w[9]), "+r"(w[10]), "+r"(w[11]), "+r"(w[12]), "+r"(w[13]), "+r"(w[14]), "+r"(w[15])
+               :
+               : "memory");
+}
+// Waits for this thread's tcgen05.ld (one x16 load); same contract.
 __device__ __forceinline__ void tmem_wait16(uint32_t (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
                  "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
                :
                : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w, int v,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v), "r"(bar)
+      : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -136,7 +194,12 @@ __device__ __forceinline__ uint32_t codes_to_trits(uint32_t c) {
   return ((c | 0x80808080u) - 0x01010101u) ^ 0x80808080u;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmA, const GemmParams p) {
+// Tensor maps: tmA the int8 activation [M][K]; tmC the panel codes as a 5-D
+// tensor {512 B of a quad half, half v, quad h, slice, group}; tmR the panel
+// scales {16 B of a block, slice, group}; tmD the activation scales [M][K/32].
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmC,
+                const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base (SW128 atoms and TMA destinations)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -156,30 +219,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   auto b_full = [&](int s) { return bar0 + (2 * kStagesA + s) * 8; };
   auto s_full = [&](int s) { return bar0 + (3 * kStagesA + s) * 8; };
   auto s_empty = [&](int s) { return bar0 + (3 * kStagesA + kStagesS + s) * 8; };
-  // per chunk slot cs (TMEM regions 4cs .. 4cs+3): MMAs done / read out by the epilogue
-  auto mma_done = [&](int cs) { return bar0 + (3 * kStagesA + 2 * kStagesS + cs) * 8; };
-  auto d_free = [&](int cs) { return bar0 + (3 * kStagesA + 2 * kStagesS + kChunkSlots + cs) * 8; };
-  const uint32_t final_bar = bar0 + (3 * kStagesA + 2 * kStagesS + 2 * kChunkSlots) * 8;
+  // per group slot gs (TMEM regions 2gs, 2gs+1): MMAs done / loaded by the epilogue
+  auto mma_done = [&](int gs) { return bar0 + (3 * kStagesA + 2 * kStagesS + gs) * 8; };
+  auto d_free = [&](int gs) { return bar0 + (3 * kStagesA + 2 * kStagesS + kGroupSlots + gs) * 8; };
+  const uint32_t final_bar = bar0 + (3 * kStagesA + 2 * kStagesS + 2 * kGroupSlots) * 8;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesA; ++s) {
       mbar_init(a_full(s), 1);
-      mbar_init(ab_empty(s), 1);
-      mbar_init(b_full(s), 4);
+      mbar_init(ab_empty(s), 1 + kEpiWarps);  // the MMA's commit + every epilogue warp (done with D[s])
+      mbar_init(b_full(s), kExpWarps);
     }
     for (int s = 0; s < kStagesS; ++s) {
-      mbar_init(s_full(s), 4);
+      mbar_init(s_full(s), kExpWarps);
       mbar_init(s_empty(s), kEpiWarps);
     }
-    for (int r = 0; r < kChunkSlots; ++r) {
+    for (int r = 0; r < kGroupSlots; ++r) {
       mbar_init(mma_done(r), 1);
       mbar_init(d_free(r), kEpiWarps);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  {  // the bias MMA's constant operand tiles (every byte equal, so any layout reads the same values)
+    const uint32_t va = 0x01010101u * kBiasA, vb = 0x01010101u * kBiasB;
+    for (int i = threadIdx.x; i < (kABytes + kBBytes) / 16; i += kThreads) {
+      const uint32_t v = i < kABytes / 16 ? va : vb;
+      reinterpret_cast<uint4*>(smem + kOffBiasA)[i] = make_uint4(v, v, v, v);
+    }
+    fence_proxy_async_smem();  // generic writes -> visible to the tensor core (async proxy)
   }
   if (warp == 1) {  // TMEM: all 512 columns (8 regions x 64) for this CTA
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -193,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const uint32_t tmem_base = *tmem_slot;
 
   auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (mbar_wait_bounded(bar, parity, kGemmWaitNs)) return true;
     atomicCAS(p.err, 0, kErrWaitTimeout);
@@ -206,12 +278,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int issued = 0;
-      pdl_wait();  // the activation tile is written by the previous kernel
+      const int g0 = n0 / kRows;
+      pdl_wait();  // the activation and its scales are written by the previous kernel
       for (int c = 0; c < nchunks; ++c) {
         const int s = c % kStagesA;
         if (c >= kStagesA && !wait(ab_empty(s), (uint32_t)((c / kStagesA - 1) & 1))) break;
-        mbar_expect_tx(a_full(s), kABytes);
-        tma_load_2d(sbase + kOffA + s * kABytes, &tmA, c * kChunk, m0, a_full(s));
+        const uint32_t bar = a_full(s);
+        mbar_expect_tx(bar, kStageTx);
+        tma_load_2d(sbase + kOffA + s * kABytes, &tmA, c * kChunk, m0, bar);
+        tma_load_5d(sbase + kOffC + s * kCBytes, &tmC, (c & 7) * 64, 0, 0, c >> 3, g0, bar);
+        tma_load_3d(sbase + kOffR + s * kRBytes, &tmR, (c & 7) * 16, c >> 3, g0, bar);
+        tma_load_2d(sbase + kOffD + s * kDBytes, &tmD, c * kStepsPerChunk, m0, bar);
         issued = c + 1;
       }
       if (*abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
@@ -225,72 +302,54 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int s = c % kStagesA;
         const uint32_t ph = (uint32_t)((c / kStagesA) & 1);
         if (!wait(a_full(s), ph) || !wait(b_full(s), ph)) break;
-        const int cs = c % kChunkSlots;
-        if (c >= kChunkSlots && !wait(d_free(cs), (uint32_t)((c / kChunkSlots - 1) & 1))) break;
-        tc_fence_after();
+        const uint64_t bias_ad = smem_desc_sw128(sbase + kOffBiasA), bias_bd = smem_desc_sw128(sbase + kOffBiasB);
+        bool go = true;
 #pragma unroll
-        for (int ks = 0; ks < kStepsPerChunk; ++ks) {
-          const uint64_t ad = smem_desc_sw128(sbase + kOffA + s * kABytes + ks * 32);
-          const uint64_t bd = smem_desc_sw128(sbase + kOffB + s * kBBytes + ks * 32);
-          mma_i8(tmem_base + (cs * kStepsPerChunk + ks) * kTileN, ad, bd, 0u);
+        for (int j = 0; j < kGroupsPerChunk; ++j) {
+          const int g = c * kGroupsPerChunk + j, gs = g % kGroupSlots;
+          if (g >= kGroupSlots && !wait(d_free(gs), (uint32_t)((g / kGroupSlots - 1) & 1))) {
+            go = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k2 = 0; k2 < kStepsPerGroup; ++k2) {
+            const int ks = j * kStepsPerGroup + k2;
+            const uint32_t dt = tmem_base + (gs * kStepsPerGroup + k2) * kTileN;
+            mma_i8(dt, bias_ad, bias_bd, 0u);  // region = kBias
+            mma_i8(dt, smem_desc_sw128(sbase + kOffA + s * kABytes + ks * 32),
+                   smem_desc_sw128(sbase + kOffB + s * kBBytes + ks * 32), 1u);  // += idot
+          }
+          mma_commit(mma_done(gs));  // the group's 2 steps (commits track all prior MMAs)
         }
-        mma_commit(mma_done(cs));  // the chunk's 4 steps (commits track all prior MMAs)
-        mma_commit(ab_empty(s));   // A and B of this chunk are free once its MMAs finish
+        if (!go) break;
+        mma_commit(ab_empty(s));  // A and B of this chunk are free once its MMAs finish
       }
       mma_commit(final_bar);  // completes when every MMA issued above has finished
       mbar_wait_bounded(final_bar, 0, kGemmWaitNs);
     }
   } else if (warp < kEpiWarp0) {
     // ------------------------------------------------------------ code expanders
-    // Thread e owns one row quad (4 rows) x 16 columns of every chunk: the
-    // 16-byte quad word at panel offset h*1024 + v*512 + (4b + t/2)*16 (b = chunk
-    // within its 1024-column slice). The words are read from global memory
-    // kPrefetch chunks ahead into registers; threads e < 64 also fetch the fp16
-    // block scale of tile row e.
-    const int e = threadIdx.x - kExpWarp0 * 32;  // 0..127
-    const int G = (int)groups_of(p.N);
-    const int g0 = n0 / kRows;
-    const int qd = e >> 3, t = e & 7;
-    const int gi = qd >> 1, h = qd & 1, v = t & 1;
-    const bool have_codes = g0 + gi < G;
-    const uint8_t* cbase = p.pan + (int64_t)(g0 + min(gi, G - 1 - g0)) * p.S * kPanelBytes + h * 1024 + v * 512 +
-                           (t >> 1) * 16;
-    const int sg = e >> 3, sr = e & 7;  // scale: row group and row of tile row e (e < 64)
-    const bool have_scale = e < kTileN && g0 + sg < G;
-    const uint8_t* sbase_g = p.pan + (int64_t)(g0 + min(sg, G - 1 - g0)) * p.S * kPanelBytes + kCodeBytes + sr * 2;
-    auto code_addr = [&](int c) { return cbase + (int64_t)(c >> 3) * kPanelBytes + (c & 7) * 64; };
-    auto scale_addr = [&](int c) { return sbase_g + (int64_t)(c >> 3) * kPanelBytes + (c & 7) * 16; };
-    uint4 wq[kPrefetch];
-    uint16_t sq[kPrefetch];
-#pragma unroll
-    for (int u = 0; u < kPrefetch; ++u) {
-      wq[u] = (have_codes && u < nchunks) ? ld_nc_v4(code_addr(u)) : make_uint4(0, 0, 0, 0);
-      sq[u] = (have_scale && u < nchunks) ? __ldg(reinterpret_cast<const unsigned short*>(scale_addr(u))) : 0;
-    }
+    // Thread e expands two row quads (quad h of row groups gi and gi + 4) x 16
+    // columns (sub-block t/2, half t&1) of every chunk: the 16-byte quad words
+    // at C[s] + group*256 + h*128 + (t&1)*64 + (t/2)*16, into int8 trits of the
+    // K-major SW128 B tile. It also converts the fp16 scale of tile row e.
+    const int e = threadIdx.x - kExpWarp0 * 32;  // 0..63
+    const int t = e & 7, h = (e >> 3) & 1, gi = e >> 4;
+    const int coff = gi * 256 + h * 128 + (t & 1) * 64 + (t >> 1) * 16;
     bool ok = true;
-    for (int c0 = 0; c0 < nchunks && ok; c0 += kPrefetch) {
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int s = c % kStagesA, ss = c % kStagesS;
+      // a_full(s) for chunk c implies the MMAs of chunk c - kStagesA (which read B[s]) are done
+      if (!wait(a_full(s), (uint32_t)((c / kStagesA) & 1))) break;
+      if (c >= kStagesS && !wait(s_empty(ss), (uint32_t)((c / kStagesS - 1) & 1))) break;
+      const uint8_t* cs = smem + kOffC + s * kCBytes;
 #pragma unroll
-      for (int u = 0; u < kPrefetch; ++u) {
-        const int c = c0 + u;
-        if (c >= nchunks) break;
-        const int s = c % kStagesA, ss = c % kStagesS;
-        if (c >= kStagesA && !wait(ab_empty(s), (uint32_t)((c / kStagesA - 1) & 1))) {
-          ok = false;
-          break;
-        }
-        if (c >= kStagesS && !wait(s_empty(ss), (uint32_t)((c / kStagesS - 1) & 1))) {
-          ok = false;
-          break;
-        }
-        const uint4 w = wq[u];
-        const uint16_t hb = sq[u];
-        if (c + kPrefetch < nchunks) {
-          if (have_codes) wq[u] = ld_nc_v4(code_addr(c + kPrefetch));
-          if (have_scale) sq[u] = __ldg(reinterpret_cast<const unsigned short*>(scale_addr(c + kPrefetch)));
-        }
+      for (int r = 0; r < 2; ++r) {
+        const uint4 w = *reinterpret_cast<const uint4*>(cs + coff + r * 4 * 256);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const int n = gi * 8 + h * 4 + k;  // row of the tile
+          const int n = (gi + 4 * r) * 8 + h * 4 + k;  // row of the tile
           uint4 o;
           o.x = codes_to_trits((w.x >> (2 * k)) & 0x03030303u);
           o.y = codes_to_trits((w.y >> (2 * k)) & 0x03030303u);
@@ -299,14 +358,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           const int off = (n >> 3) * 1024 + (n & 7) * 128 + ((t ^ (n & 7)) << 4);
           *reinterpret_cast<uint4*>(smem + kOffB + s * kBBytes + off) = o;
         }
-        if (e < kTileN)
-          reinterpret_cast<float*>(smem + kOffS)[ss * kTileN + e] = __half2float(__ushort_as_half(hb));
-        fence_proxy_async_smem();  // generic writes of B -> visible to the tensor core (async proxy)
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(b_full(s));
-          mbar_arrive(s_full(ss));
-        }
+      }
+      const uint16_t hb = *reinterpret_cast<const uint16_t*>(smem + kOffR + s * kRBytes + e * 2);
+      reinterpret_cast<float*>(smem + kOffS)[ss * kTileN + e] = __half2float(__ushort_as_half(hb)) * 0x1p39f;
+      fence_proxy_async_smem();  // generic writes of B -> visible to the tensor core (async proxy)
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(b_full(s));
+        mbar_arrive(s_full(ss));
       }
     }
   } else {
@@ -314,71 +373,120 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int q = warp & 3;                    // TMEM lane quarter this warp may access
     const int cg = (warp - kEpiWarp0) >> 2;    // column group of the tile
     const int m = q * 32 + lane;               // tile row of this thread
+    // a warp whose 32 rows all lie beyond M keeps the barrier protocol but skips the loads and math
+    const bool rows_live = m0 + q * 32 < p.M;
+    int nchunks_live = nchunks;
     constexpr int H = kEpiCols / 2;
     float2 acc[H], tsum[H];
 #pragma unroll
     for (int i = 0; i < H; ++i) acc[i] = tsum[i] = make_float2(0.f, 0.f);
-    const float2 nmagic = make_float2(-kMagicFloat, -kMagicFloat);
-    // activation scales of this row, [K/32] fp32, read from global memory one
-    // chunk ahead (rows beyond M read row M-1: their sums are never stored)
-    pdl_wait();  // d is written by the previous kernel; y is read (BTF_ADD) and written below
-    const float4* drow = reinterpret_cast<const float4*>(p.d + (int64_t)min(m0 + m, p.M - 1) * (p.K / 32));
-    float4 dnext = __ldg(drow);
-    auto step_math = [&](const uint32_t (&dr)[16], float dk) {
-      const float2 d2 = make_float2(dk, dk);
+    pdl_wait();  // y is read (BTF_ADD) and written below
+    // T (= tsum) gets RN(d * idot) * 2^-39 for one 32-column step; `first` starts a new 128-column block
+    auto step_math = [&](const uint32_t (&dr)[16], float dk, bool first) {
+      if (fabsf(dk) < 0x1p18f) {
+        const float2 a2 = make_float2(dk * 0x1p110f, dk * 0x1p110f);
+        const float2 c2 = make_float2(dk * -0x1p-27f, dk * -0x1p-27f);  // -kBias * 2^-149 * d * 2^110
 #pragma unroll
-      for (int i = 0; i < H; ++i) {
-        const float2 f = __fadd2_rn(
-            make_float2(__int_as_float((int)dr[2 * i] + kMagicInt), __int_as_float((int)dr[2 * i + 1] + kMagicInt)),
-            nmagic);
-        tsum[i] = __ffma2_rn(d2, f, tsum[i]);
+        for (int i = 0; i < H; ++i) {
+          const float2 r = __ffma2_rn(a2, make_float2(__uint_as_float(dr[2 * i]), __uint_as_float(dr[2 * i + 1])), c2);
+          tsum[i] = first ? r : __fadd2_rn(tsum[i], r);
+        }
+      } else {  // |d| >= 2^18, inf or NaN: d * 2^110 would overflow; convert the integers instead
+        const float ds = dk * 0x1p-39f;
+#pragma unroll
+        for (int i = 0; i < H; ++i) {
+          const float2 r = make_float2(ds * (float)((int)dr[2 * i] - kBias), ds * (float)((int)dr[2 * i + 1] - kBias));
+          tsum[i] = first ? r : __fadd2_rn(tsum[i], r);
+        }
       }
     };
     bool ok = true;
-    for (int c = 0; c < nchunks && ok; ++c) {
-      const int ss = c % kStagesS;
-      const float4 dv = dnext;
-      if (c + 1 < nchunks) dnext = __ldg(drow + c + 1);
-      const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
-      uint32_t dr[2][kEpiCols];
-      // one wait per chunk; step ks + 1 is loaded while step ks's math runs
-      const int cs = c % kChunkSlots;
-      if (!wait(mma_done(cs), (uint32_t)((c / kChunkSlots) & 1))) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + cs * kStepsPerChunk * kTileN + cg * kEpiCols;
-      tmem_ld16_async(taddr, dr[0]);
-#pragma unroll
-      for (int ks = 0; ks < kStepsPerChunk; ++ks) {
-        tmem_wait16(dr[ks & 1]);
-        if (ks + 1 < kStepsPerChunk) tmem_ld16_async(taddr + (ks + 1) * kTileN, dr[(ks + 1) & 1]);
-        step_math(dr[ks & 1], dk[ks]);
+    if (!rows_live) {
+      // every row of this warp lies beyond M: only the barrier protocol. Each
+      // arrival follows the wait on the same use of the slot, which keeps it in
+      // that use's phase.
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int s = c % kStagesA;
+        ok = wait(a_full(s), (uint32_t)((c / kStagesA) & 1));
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(ab_empty(s));
+        for (int j = 0; j < kGroupsPerChunk && ok; ++j) {
+          const int g = c * kGroupsPerChunk + j, gs = g % kGroupSlots;
+          ok = wait(mma_done(gs), (uint32_t)((g / kGroupSlots) & 1));
+          __syncwarp();
+          if (ok && lane == 0) mbar_arrive(d_free(gs));
+        }
+        const int ss = c % kStagesS;
+        ok = ok && wait(s_full(ss), (uint32_t)((c / kStagesS) & 1));
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(s_empty(ss));
       }
-      tc_fence_before();
+      nchunks_live = 0;
+    }
+    for (int c = 0; c < nchunks_live && ok; ++c) {
+      const int ss = c % kStagesS, s = c % kStagesA;
+      // this row's 4 activation scales from D[s]; the stage is released right after
+      if (!wait(a_full(s), (uint32_t)((c / kStagesA) & 1))) break;
+      const float4 dv = *reinterpret_cast<const float4*>(smem + kOffD + s * kDBytes + m * 16);
       __syncwarp();
-      if (lane == 0) mbar_arrive(d_free(cs));
-      if (!wait(s_full(ss), (uint32_t)((c / kStagesS) & 1))) break;
+      if (lane == 0) mbar_arrive(ab_empty(s));
+      const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+      for (int j = 0; j < kGroupsPerChunk; ++j) {
+        const int g = c * kGroupsPerChunk + j, gs = g % kGroupSlots;
+        if (!wait(mma_done(gs), (uint32_t)((g / kGroupSlots) & 1))) {
+          ok = false;
+          break;
+        }
+        // both steps' loads in flight behind one wait; the group's regions are
+        // released as soon as they are in registers, before the math
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + gs * kStepsPerGroup * kTileN + cg * kEpiCols;
+        tc_fence_after();
+        uint32_t dr0[kEpiCols], dr1[kEpiCols];
+        tmem_ld16_async(taddr, dr0);
+        tmem_ld16_async(taddr + kTileN, dr1);
+        tmem_wait16x2(dr0, dr1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_free(gs));  // the group's regions may be overwritten now
+        step_math(dr0, dk[j * kStepsPerGroup], j == 0);
+        step_math(dr1, dk[j * kStepsPerGroup + 1], false);
+      }
+      if (!ok || !wait(s_full(ss), (uint32_t)((c / kStagesS) & 1))) break;
       const float* sc = reinterpret_cast<const float*>(smem + kOffS) + ss * kTileN + cg * kEpiCols;
 #pragma unroll
       for (int i = 0; i < H; ++i) {
         const float2 s2 = make_float2(sc[2 * i], sc[2 * i + 1]);
         acc[i] = __ffma2_rn(s2, tsum[i], acc[i]);
-        tsum[i] = make_float2(0.f, 0.f);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty(ss));
     }
-    if (ok && !*abort_flag && m0 + m < p.M) {
-      float* yr = p.y + (int64_t)(m0 + m) * p.ldy + n0 + cg * kEpiCols;
+    // The tile goes out through shared memory as whole rows. The A ring is idle
+    // here: this warp has seen every chunk's TMA land and every MMA complete.
+    float* stg = reinterpret_cast<float*>(smem + kOffA);  // [128][kStgLd]
+    if (rows_live) {
+      float4* dst = reinterpret_cast<float4*>(stg + m * kStgLd + cg * kEpiCols);
 #pragma unroll
-      for (int i = 0; i < H; ++i) {
-        const int n = n0 + cg * kEpiCols + 2 * i;
-        if (n < p.N) {
-          if (p.mode == BTF_ADD) yr[2 * i] += acc[i].x;
-          else yr[2 * i] = acc[i].x;
-        }
-        if (n + 1 < p.N) {
-          if (p.mode == BTF_ADD) yr[2 * i + 1] += acc[i].y;
-          else yr[2 * i + 1] = acc[i].y;
+      for (int i = 0; i < H / 2; ++i) dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+    }
+    // every epilogue warp reaches this barrier once (its chunk loop always ends)
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+    if (!*abort_flag) {
+      const int we = warp - kEpiWarp0;
+#pragma unroll 1
+      for (int rr = 0; rr < kTileM / kEpiWarps; ++rr) {
+        const int r = we * (kTileM / kEpiWarps) + rr;
+        if (m0 + r >= p.M) break;
+        float* yr = p.y + (int64_t)(m0 + r) * p.ldy + n0;
+#pragma unroll
+        for (int h2 = 0; h2 < kTileN / 32; ++h2) {
+          const int col = h2 * 32 + lane;
+          if (n0 + col < p.N) {
+            const float v = stg[r * kStgLd + col];
+            if (p.mode == BTF_ADD) yr[col] += v;
+            else yr[col] = v;
+          }
         }
       }
     }
@@ -424,26 +532,58 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
   if (!dev) return BTF_ERR_STATE;
   const EncodeFn enc = encode_fn();
   if (!enc) return fail(BTF_ERR_CUDA, "btf_gemm: cuTensorMapEncodeTiled unavailable");
-  // activation tile map: int8 [M][K], box 128 columns x 128 rows, 128B swizzle,
-  // rows beyond M read as zero
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  const cuuint64_t strides[1] = {(cuuint64_t)K};
-  const cuuint32_t box[2] = {(cuuint32_t)kChunk, (cuuint32_t)kTileM};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(act.q), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(BTF_ERR_ARG, "btf_gemm: tensor map encoding failed (%d)", (int)r);
+  auto encode = [&](CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+                    const char* what) -> int {
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = enc(map, type, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? BTF_OK : fail(BTF_ERR_ARG, "btf_gemm: %s tensor map encoding failed (%d)", what, (int)r);
+  };
+  const int64_t S = slices_of(K), G = groups_of(seg.N);
+  const uint8_t* pan = static_cast<const uint8_t*>(seg.panels);
+  CUtensorMap mA, mC, mR, mD;
+  {  // activation: int8 [M][K], box 128 columns x 128 rows, 128B swizzle; rows beyond M read as zero
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunk, (cuuint32_t)kTileM};
+    if (int rc = encode(&mA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act.q, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, "activation"))
+      return rc;
+  }
+  {  // panel codes {x: 512 B of a quad half (8 blocks x 64 B), half v (stride 512), quad h (1024), slice, group};
+     // box: one block (64 B) x 2 halves x 2 quads x 1 slice x 8 groups; groups beyond G read as zero
+    const cuuint64_t dims[5] = {512, 2, 2, (cuuint64_t)S, (cuuint64_t)G};
+    const cuuint64_t strides[4] = {512, 1024, (cuuint64_t)kPanelBytes,
+                                   (cuuint64_t)(S * kPanelBytes)};
+    const cuuint32_t box[5] = {64, 2, 2, 1, (cuuint32_t)(kTileN / kRows)};
+    if (int rc = encode(&mC, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, pan, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        "panel code"))
+      return rc;
+  }
+  {  // panel scales {x: 128 B (8 blocks x 8 rows fp16), slice, group}; box: one block (16 B) x 1 x 8 groups
+    const cuuint64_t dims[3] = {128, (cuuint64_t)S, (cuuint64_t)G};
+    const cuuint64_t strides[2] = {(cuuint64_t)kPanelBytes, (cuuint64_t)(S * kPanelBytes)};
+    const cuuint32_t box[3] = {16, 1, (cuuint32_t)(kTileN / kRows)};
+    if (int rc = encode(&mR, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, pan + kCodeBytes, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, "panel scale"))
+      return rc;
+  }
+  {  // activation block scales: fp32 [M][K/32], box 4 blocks (one chunk) x 128 rows
+    const cuuint64_t dims[2] = {(cuuint64_t)(K / 32), (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)(K / 32) * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)kStepsPerChunk, (cuuint32_t)kTileM};
+    if (int rc = encode(&mD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, act.d, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, "activation scale"))
+      return rc;
+  }
   GemmParams p{};
-  p.pan = static_cast<const uint8_t*>(seg.panels);
   p.N = seg.N;
   p.M = M;
   p.K = K;
-  p.S = (int)slices_of(K);
   p.y = seg.y;
   p.ldy = seg.ldy;
-  p.d = act.d;
   p.mode = mode;
   p.err = dev->err_word;
 #if BTF_GEMM_RASTER_M
@@ -451,7 +591,7 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
 #else
   const dim3 grid((seg.N + kTileN - 1) / kTileN, (M + kTileM - 1) / kTileM);
 #endif
-  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, map, p);
+  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, mA, mC, mR, mD, p);
   return e == cudaSuccess ? launch_status("gemm_kernel") : cuda_fail(e, "gemm_kernel launch");
 }
 

@@ -112,3 +112,33 @@ def test_gemm_three_segments_qkv_shapes(cuda, btf, orc):
         codes, scales = orc.repack_t2(src[rows], len(rows), K)
         want = orc.gemv(codes, scales, K, q, d, s, threads=8)
         assert rel_rms(y.cpu().numpy()[:, :N][:, rows], want) <= TOL
+
+
+def test_gemm_extreme_activation_scales(cuda, btf, orc):
+    # rows whose Q8 scale d = fp16(amax/127) is near the fp16 maximum, a
+    # subnormal fp16 value, or zero, beside ordinary rows; each row is checked
+    # on its own since the rows differ by 12 orders of magnitude
+    import torch
+
+    M, K, N = 96, 2048, 136
+    src = synth.ternary_ptq(N, K, seed=61)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    x = synth.activations(M, K, seed=62)
+    x[3] *= np.float32(2e6)
+    x[5] *= np.float32(1e-5)
+    x[7] = 0.0
+    x[70, 256:512] *= np.float32(2e6)  # two 128-column blocks of row 70
+    act = btf.quant_q8(_dev(x, cuda))
+    y = torch.full((M, N), 7.0, device=cuda)
+    btf.launch_gemm([(pm, y, N)], K, M, act, btf.STORE)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    got = y.cpu().numpy()
+    q, d, s = orc.q8_rows(x)
+    assert 2.0 ** 14 < d[3].max() < 65504 and 0 < d[5].max() < 2.0 ** -14
+    codes, scales = orc.repack_t2(src, N, K)
+    want = orc.gemv(codes, scales, K, q, d, s, threads=8)
+    assert np.all(got[7] == 0.0)
+    for r in range(M):
+        if r != 7:
+            assert rel_rms(got[r], want[r]) <= TOL, (r, rel_rms(got[r], want[r]))
