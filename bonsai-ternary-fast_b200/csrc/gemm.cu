@@ -11,9 +11,10 @@
 // own TMEM region, and the CUDA-core epilogue does the fp32 work.
 //
 // Epilogue arithmetic: one packed FMA and one packed add per element per step.
-// Before each data MMA a bias MMA of two constant tiles (2 x 64 over 32 columns)
-// sets the region to 4096, so the region ends as P = idot + 4096 in [0, 8192].
-// P's bits read as an fp32 value are the denormal P * 2^-149, and
+// A bias MMA of two constant tiles (2 x 64 over 32 columns, N = 256: a chunk's
+// 4 regions at once) sets the regions to 4096 before the data MMAs accumulate,
+// so each region ends as P = idot + 4096 in [0, 8192]. P's bits read as an
+// fp32 value are the denormal P * 2^-149, and
 //   fma(d * 2^110, P * 2^-149, -d * 2^-27) = RN(d * idot) * 2^-39
 // exactly: the FMA's product is exact, d * 2^110 and d * 2^-27 are exact powers
 // of two times d, and the one rounding of a normal result commutes with the
@@ -22,19 +23,23 @@
 // 65504, or inf), so every finite d takes this path; |d| >= 2^18, inf and NaN
 // take a conversion path instead.
 //
-// One CTA computes a 128 x 64 output tile; warp roles:
-//   warp 0      producer: TMA (tensor map, 128B swizzle) of the int8
-//               activation tile [128 rows][128 cols] per 128-column chunk;
-//   warp 1      MMA issuer (one thread) + TMEM owner (alloc / dealloc);
-//   warps 2-3   expand the 2-bit codes of the chunk into int8 trits in the
-//               canonical K-major SW128 layout the MMA reads, and stage the
-//               chunk's fp32 weight scales;
-//   warps 4-19  epilogue: TMEM -> registers (tcgen05.ld 32x32b, 16 columns),
-//               per step T += RN(d * idot), per 128-column block
-//               acc += scale * T. TMEM holds 4 groups of 2 steps; a group is
-//               released as soon as its registers are loaded, before the math.
+// One CTA computes a 128 x 64 output tile, one 128-column chunk of K at a time:
+//   warp 0      producer (one thread): per chunk, TMA of the int8 activation
+//               tile (128B swizzle), the tile's raw 2-bit codes and fp16
+//               scales (one box each) into input stage s, and of the
+//               activation scales d into scale stage ss;
+//   warp 1      MMA issuer (one thread) + TMEM owner: per chunk one bias MMA
+//               and 4 data MMAs into one of 2 TMEM chunk slots (4 x 64 columns);
+//   warps 2-3   expanders: raw codes -> int8 trits in the canonical K-major
+//               SW128 layout the MMA reads; fp16 scales -> fp32 (x 2^39);
+//   warps 4-19  epilogue: tcgen05.ld (32x32b, 16 columns) of step k+1 in
+//               flight during the math of step k, per step T += RN(d * idot),
+//               per chunk acc += scale * T; a chunk slot is released as soon as
+//               its last step is in registers. The output tile leaves through
+//               shared memory as whole rows.
+// Per chunk the epilogue makes 2 waits (scales, MMA results) and 2 arrivals.
 // Every wait is bounded; on a time-out the kernel records an error word, stops
-// issuing work, waits (bounded) for its MMAs, frees TMEM and returns.
+// issuing work, waits (bounded) for its copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
 
 #include <algorithm>
@@ -55,14 +60,11 @@ constexpr int kStepsPerChunk = 4;    // 32-column MMA steps per chunk
 #ifndef BTF_GEMM_RASTER_M
 #define BTF_GEMM_RASTER_M 1
 #endif
-constexpr int kStagesA = BTF_GEMM_STAGES;  // input stages (chunks), all filled by TMA
-constexpr int kStagesS = 8;          // fp32 weight-scale stages (written by the expanders, freed by the epilogue)
-constexpr int kDRegions = 8;         // TMEM accumulator regions (one per in-flight step)
-constexpr int kStepsPerGroup = 2;    // steps per TMEM group (one mma_done / d_free barrier pair)
-constexpr int kGroupsPerChunk = kStepsPerChunk / kStepsPerGroup;
-constexpr int kGroupSlots = kDRegions / kStepsPerGroup;  // groups in flight in TMEM (4)
-constexpr int kTmemCols = kDRegions * kTileN;  // 512: all of TMEM
-constexpr int kEpiWarps = 16;        // 4 per SMSP: TMEM-load latency of one hides behind the others' math
+constexpr int kStagesA = BTF_GEMM_STAGES;  // input stages: A, codes, raw scales (TMA) and B (expanders)
+constexpr int kStagesS = 8;          // scale stages: d (TMA) and fp32 weight scales (expanders)
+constexpr int kChunkSlots = 2;       // chunks in flight in TMEM
+constexpr int kTmemCols = kChunkSlots * kStepsPerChunk * kTileN;  // 512: all of TMEM
+constexpr int kEpiWarps = 16;        // 4 per SMSP
 constexpr int kEpiCols = kTileN * 4 / kEpiWarps;  // columns per epilogue thread (16)
 constexpr int kExpWarps = 2;         // code expanders (64 threads: 2 row quads x 16 columns each)
 constexpr int kExpWarp0 = 2, kEpiWarp0 = kExpWarp0 + kExpWarps;
@@ -72,34 +74,42 @@ constexpr int kBiasA = 2, kBiasB = 64, kBias = 32 * kBiasA * kBiasB;  // 4096 >=
 static_assert(kBias == 4096, "the bias is a power of two");
 constexpr uint64_t kGemmWaitNs = 1000000000ull;
 
-// One input stage s holds chunk c (c % kStagesA == s), all brought by the producer's TMA:
-//   A    [128 rows][128 cols] int8 activations (128B swizzle)
-//   C    raw 2-bit codes of the tile's 8 row groups: [group][quad h][half v][64 B]
-//   R    raw fp16 weight scales: [group][row][1] (16 B per group)
-//   D    activation block scales d: [128 rows][4] fp32
-// and B[s], the int8 trits the expanders write from C[s].
+// Input stage s (chunk c, c % kStagesA == s):
+//   A  [128 rows][128 cols] int8 activations (128B swizzle)
+//   B  [64 rows][128 cols] int8 trits (128B swizzle), written by the expanders
+//   C  raw 2-bit codes of the tile's 8 row groups: [group][quad h][half v][64 B]
+//   R  raw fp16 weight scales: [group][row] (16 B per group)
+// Scale stage ss (c % kStagesS == ss):
+//   D  activation block scales d: [128 rows][4] fp32
+//   W  fp32 weight scales x 2^39: [64]
 constexpr int kABytes = kTileM * kChunk;                  // 16 KB
 constexpr int kBBytes = kTileN * kChunk;                  // 8 KB
 constexpr int kCBytes = kTileN * kChunk / 4;              // 2 KB
 constexpr int kRBytes = kTileN * 2;                       // 128 B
 constexpr int kDBytes = kTileM * kStepsPerChunk * 4;      // 2 KB
-constexpr int kStageTx = kABytes + kCBytes + kRBytes + kDBytes;
+constexpr int kWBytes = kTileN * 4;                       // 256 B
+constexpr int kStageTxA = kABytes + kCBytes + kRBytes;
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStagesA * kABytes;
 constexpr int kOffC = kOffB + kStagesA * kBBytes;
-constexpr int kOffD = kOffC + kStagesA * kCBytes;
-constexpr int kOffR = kOffD + kStagesA * kDBytes;
-constexpr int kOffS = kOffR + kStagesA * kRBytes;          // s: [stage][64] fp32 weight scales * 2^39
-constexpr int kOffBiasA = (kOffS + kStagesS * kTileN * 4 + 1023) / 1024 * 1024;  // [128][128] bytes of kBiasA
-constexpr int kOffBiasB = kOffBiasA + kABytes;            // [64][128] bytes of kBiasB
-constexpr int kOffBar = kOffBiasB + kBBytes;
-constexpr int kNumBars = 3 * kStagesA + 2 * kStagesS + 2 * kGroupSlots + 4;
-constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffTmemSlot + 16 + 1024;      // + slack for 1024-B alignment
+constexpr int kOffR = kOffC + kStagesA * kCBytes;
+constexpr int kOffD = kOffR + kStagesA * kRBytes;
+constexpr int kOffW = kOffD + kStagesS * kDBytes;
+// bias operands: K-major, no swizzle, 8-row x 16-byte core matrices (LBO 128 B
+// along K, SBO 256 B along M/N); every byte equal, so any core-matrix order
+// reads the same values
+constexpr int kBiasN = kStepsPerChunk * kTileN;            // 256: one bias MMA covers a chunk's 4 regions
+constexpr int kBiasABytes = kTileM * 32, kBiasBBytes = kBiasN * 32;  // 4 KB, 8 KB
+constexpr int kOffBiasA = (kOffW + kStagesS * kWBytes + 1023) / 1024 * 1024;
+constexpr int kOffBiasB = kOffBiasA + kBiasABytes;
+constexpr int kOffBar = kOffBiasB + kBiasBBytes;
+constexpr int kNumBars = 3 * kStagesA + 3 * kStagesS + 2 * kChunkSlots + 1;
+constexpr int kOffFlags = kOffBar + kNumBars * 8;         // TMEM base (4 B), abort flag (4 B)
+constexpr int kSmemBytes = kOffFlags + 16 + 1024;         // + slack for 1024-B alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kOffC % 128 == 0 && kOffR % 128 == 0 && kOffD % 128 == 0 && kOffW % 128 == 0, "TMA destinations");
 constexpr int kStgLd = kTileN + 4;  // output staging row (floats): conflict-free float4 writes
 static_assert(kTileM * kStgLd * 4 <= kStagesA * kABytes, "output staging fits the A ring");
-static_assert(kOffC % 128 == 0 && kOffD % 128 == 0 && kOffR % 128 == 0, "TMA destinations");
 
 struct GemmParams {
   int N, M, K;
@@ -116,15 +126,26 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3fffu) | ((uint64_t)1u << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
-// kind::i8 instruction descriptor: D s32, A s8, B s8, both K-major, M = 128, N = 64.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileN >> 3) << 17) |
-                            ((uint32_t)(kTileM >> 4) << 24);
+// K-major, no swizzle: start >> 4, LBO = 128 B (core matrices along K), SBO =
+// 256 B (core matrices along M/N), descriptor version 1, layout type 0.
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3fffu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+         ((uint64_t)1u << 46);
+}
+// kind::i8 instruction descriptor: D s32, A s8, B s8, both K-major, M = 128, N = n.
+constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+}
+constexpr uint32_t kIdesc = idesc_i8(kTileN);
+constexpr uint32_t kIdescBias = idesc_i8(kBiasN);
+static_assert(kBiasN <= 256 && kBiasN % 16 == 0, "M=128 MMA: N a multiple of 16 up to 256");
 
+template <uint32_t IDESC>
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u)
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate), "r"(0u)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -214,29 +235,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nchunks = p.K / kChunk;
 
   const uint32_t bar0 = sbase + kOffBar;
-  auto a_full = [&](int s) { return bar0 + (0 * kStagesA + s) * 8; };
-  auto ab_empty = [&](int s) { return bar0 + (1 * kStagesA + s) * 8; };
-  auto b_full = [&](int s) { return bar0 + (2 * kStagesA + s) * 8; };
-  auto s_full = [&](int s) { return bar0 + (3 * kStagesA + s) * 8; };
-  auto s_empty = [&](int s) { return bar0 + (3 * kStagesA + kStagesS + s) * 8; };
-  // per group slot gs (TMEM regions 2gs, 2gs+1): MMAs done / loaded by the epilogue
-  auto mma_done = [&](int gs) { return bar0 + (3 * kStagesA + 2 * kStagesS + gs) * 8; };
-  auto d_free = [&](int gs) { return bar0 + (3 * kStagesA + 2 * kStagesS + kGroupSlots + gs) * 8; };
-  const uint32_t final_bar = bar0 + (3 * kStagesA + 2 * kStagesS + 2 * kGroupSlots) * 8;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
+  auto a_full = [&](int s) { return bar0 + (0 * kStagesA + s) * 8; };    // TMA: A, C, R of stage s
+  auto ab_empty = [&](int s) { return bar0 + (1 * kStagesA + s) * 8; };  // MMA commit: stage s read
+  auto b_full = [&](int s) { return bar0 + (2 * kStagesA + s) * 8; };    // expanders: B[s] written
+  auto d_full = [&](int s) { return bar0 + (3 * kStagesA + s) * 8; };    // TMA: D of scale stage s
+  auto s_full = [&](int s) { return bar0 + (3 * kStagesA + kStagesS + s) * 8; };      // expanders: W (and D) ready
+  auto s_empty = [&](int s) { return bar0 + (3 * kStagesA + 2 * kStagesS + s) * 8; };  // epilogue: stage read
+  auto mma_done = [&](int cs) { return bar0 + (3 * kStagesA + 3 * kStagesS + cs) * 8; };
+  auto d_free = [&](int cs) { return bar0 + (3 * kStagesA + 3 * kStagesS + kChunkSlots + cs) * 8; };
+  const uint32_t final_bar = bar0 + (3 * kStagesA + 3 * kStagesS + 2 * kChunkSlots) * 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffFlags);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffFlags + 8);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesA; ++s) {
       mbar_init(a_full(s), 1);
-      mbar_init(ab_empty(s), 1 + kEpiWarps);  // the MMA's commit + every epilogue warp (done with D[s])
+      mbar_init(ab_empty(s), 1);
       mbar_init(b_full(s), kExpWarps);
     }
     for (int s = 0; s < kStagesS; ++s) {
+      mbar_init(d_full(s), 1);
       mbar_init(s_full(s), kExpWarps);
       mbar_init(s_empty(s), kEpiWarps);
     }
-    for (int r = 0; r < kGroupSlots; ++r) {
+    for (int r = 0; r < kChunkSlots; ++r) {
       mbar_init(mma_done(r), 1);
       mbar_init(d_free(r), kEpiWarps);
     }
@@ -244,15 +266,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  {  // the bias MMA's constant operand tiles (every byte equal, so any layout reads the same values)
+  {  // the bias MMA's constant operand tiles
     const uint32_t va = 0x01010101u * kBiasA, vb = 0x01010101u * kBiasB;
-    for (int i = threadIdx.x; i < (kABytes + kBBytes) / 16; i += kThreads) {
-      const uint32_t v = i < kABytes / 16 ? va : vb;
+    for (int i = threadIdx.x; i < (kBiasABytes + kBiasBBytes) / 16; i += kThreads) {
+      const uint32_t v = i < kBiasABytes / 16 ? va : vb;
       reinterpret_cast<uint4*>(smem + kOffBiasA)[i] = make_uint4(v, v, v, v);
     }
     fence_proxy_async_smem();  // generic writes -> visible to the tensor core (async proxy)
   }
-  if (warp == 1) {  // TMEM: all 512 columns (8 regions x 64) for this CTA
+  if (warp == 1) {  // TMEM: all 512 columns (2 chunk slots x 4 regions x 64) for this CTA
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"((uint32_t)kTmemCols)
                  : "memory");
@@ -263,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // bounded wait; false (and the abort flag set) on a time-out or after another role's time-out
   auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
@@ -280,50 +303,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       const int g0 = n0 / kRows;
       pdl_wait();  // the activation and its scales are written by the previous kernel
+      // stage indices and fill parities as counters (kStagesA need not be a power of 2)
+      int s = 0, ss = 0;
+      uint32_t ph = 0, phs = 0;
       for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kStagesA;
-        if (c >= kStagesA && !wait(ab_empty(s), (uint32_t)((c / kStagesA - 1) & 1))) break;
-        const uint32_t bar = a_full(s);
-        mbar_expect_tx(bar, kStageTx);
-        tma_load_2d(sbase + kOffA + s * kABytes, &tmA, c * kChunk, m0, bar);
-        tma_load_5d(sbase + kOffC + s * kCBytes, &tmC, (c & 7) * 64, 0, 0, c >> 3, g0, bar);
-        tma_load_3d(sbase + kOffR + s * kRBytes, &tmR, (c & 7) * 16, c >> 3, g0, bar);
-        tma_load_2d(sbase + kOffD + s * kDBytes, &tmD, c * kStepsPerChunk, m0, bar);
+        if (c >= kStagesA && !wait(ab_empty(s), ph ^ 1u)) break;
+        mbar_expect_tx(a_full(s), kStageTxA);
+        tma_load_2d(sbase + kOffA + s * kABytes, &tmA, c * kChunk, m0, a_full(s));
+        tma_load_5d(sbase + kOffC + s * kCBytes, &tmC, (c & 7) * 64, 0, 0, c >> 3, g0, a_full(s));
+        tma_load_3d(sbase + kOffR + s * kRBytes, &tmR, (c & 7) * 16, c >> 3, g0, a_full(s));
+        if (c >= kStagesS && !wait(s_empty(ss), phs ^ 1u)) {
+          issued = -(c + 1);  // stage s of chunk c is in flight, its scale stage is not
+          break;
+        }
+        mbar_expect_tx(d_full(ss), kDBytes);
+        tma_load_2d(sbase + kOffD + ss * kDBytes, &tmD, c * kStepsPerChunk, m0, d_full(ss));
         issued = c + 1;
+        if (++s == kStagesA) s = 0, ph ^= 1u;
+        if (++ss == kStagesS) ss = 0, phs ^= 1u;
       }
-      if (*abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
-        for (int c = max(0, issued - kStagesA); c < issued; ++c)
+      if (*abort_flag) {  // leave no copy in flight into this CTA's shared memory (bounded)
+        const int na = issued < 0 ? -issued : issued, nd = issued < 0 ? -issued - 1 : issued;
+        for (int c = max(0, na - kStagesA); c < na; ++c)
           mbar_wait_bounded(a_full(c % kStagesA), (uint32_t)((c / kStagesA) & 1), kGemmWaitNs / 10);
+        for (int c = max(0, nd - kStagesS); c < nd; ++c)
+          mbar_wait_bounded(d_full(c % kStagesS), (uint32_t)((c / kStagesS) & 1), kGemmWaitNs / 10);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      // descriptors: the start-address field (address >> 4, 14 bits) takes the
+      // byte offsets >> 4 by plain addition (shared memory < 256 KB)
+      const uint64_t bias_ad = smem_desc_noswz(sbase + kOffBiasA), bias_bd = smem_desc_noswz(sbase + kOffBiasB);
+      const uint64_t a_desc0 = smem_desc_sw128(sbase + kOffA), b_desc0 = smem_desc_sw128(sbase + kOffB);
+      int s = 0;
+      uint32_t ph = 0;
       for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kStagesA;
-        const uint32_t ph = (uint32_t)((c / kStagesA) & 1);
         if (!wait(a_full(s), ph) || !wait(b_full(s), ph)) break;
-        const uint64_t bias_ad = smem_desc_sw128(sbase + kOffBiasA), bias_bd = smem_desc_sw128(sbase + kOffBiasB);
-        bool go = true;
+        const int cs = c & (kChunkSlots - 1);
+        if (c >= kChunkSlots && !wait(d_free(cs), (uint32_t)(((c / kChunkSlots) - 1) & 1))) break;
+        tc_fence_after();
+        const uint32_t dt = tmem_base + cs * kStepsPerChunk * kTileN;
+        mma_i8<kIdescBias>(dt, bias_ad, bias_bd, 0u);  // the chunk's 4 regions = kBias
+        const uint64_t ad = a_desc0 + (uint64_t)((s * kABytes) >> 4), bd = b_desc0 + (uint64_t)((s * kBBytes) >> 4);
 #pragma unroll
-        for (int j = 0; j < kGroupsPerChunk; ++j) {
-          const int g = c * kGroupsPerChunk + j, gs = g % kGroupSlots;
-          if (g >= kGroupSlots && !wait(d_free(gs), (uint32_t)((g / kGroupSlots - 1) & 1))) {
-            go = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int k2 = 0; k2 < kStepsPerGroup; ++k2) {
-            const int ks = j * kStepsPerGroup + k2;
-            const uint32_t dt = tmem_base + (gs * kStepsPerGroup + k2) * kTileN;
-            mma_i8(dt, bias_ad, bias_bd, 0u);  // region = kBias
-            mma_i8(dt, smem_desc_sw128(sbase + kOffA + s * kABytes + ks * 32),
-                   smem_desc_sw128(sbase + kOffB + s * kBBytes + ks * 32), 1u);  // += idot
-          }
-          mma_commit(mma_done(gs));  // the group's 2 steps (commits track all prior MMAs)
-        }
-        if (!go) break;
-        mma_commit(ab_empty(s));  // A and B of this chunk are free once its MMAs finish
+        for (int ks = 0; ks < kStepsPerChunk; ++ks)
+          mma_i8<kIdesc>(dt + ks * kTileN, ad + (ks * 32 >> 4), bd + (ks * 32 >> 4), 1u);  // += idot
+        mma_commit(mma_done(cs));  // the chunk's MMAs (commits track all prior MMAs)
+        mma_commit(ab_empty(s));   // A and B of this chunk are free once its MMAs finish
+        if (++s == kStagesA) s = 0, ph ^= 1u;
       }
       mma_commit(final_bar);  // completes when every MMA issued above has finished
       mbar_wait_bounded(final_bar, 0, kGemmWaitNs);
@@ -337,12 +366,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int e = threadIdx.x - kExpWarp0 * 32;  // 0..63
     const int t = e & 7, h = (e >> 3) & 1, gi = e >> 4;
     const int coff = gi * 256 + h * 128 + (t & 1) * 64 + (t >> 1) * 16;
-    bool ok = true;
-    for (int c = 0; c < nchunks && ok; ++c) {
-      const int s = c % kStagesA, ss = c % kStagesS;
+    int s = 0, ss = 0;
+    uint32_t ph = 0, phs = 0;
+    for (int c = 0; c < nchunks; ++c) {
       // a_full(s) for chunk c implies the MMAs of chunk c - kStagesA (which read B[s]) are done
-      if (!wait(a_full(s), (uint32_t)((c / kStagesA) & 1))) break;
-      if (c >= kStagesS && !wait(s_empty(ss), (uint32_t)((c / kStagesS - 1) & 1))) break;
+      if (!wait(a_full(s), ph)) break;
       const uint8_t* cs = smem + kOffC + s * kCBytes;
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
@@ -359,14 +387,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(smem + kOffB + s * kBBytes + off) = o;
         }
       }
-      const uint16_t hb = *reinterpret_cast<const uint16_t*>(smem + kOffR + s * kRBytes + e * 2);
-      reinterpret_cast<float*>(smem + kOffS)[ss * kTileN + e] = __half2float(__ushort_as_half(hb)) * 0x1p39f;
       fence_proxy_async_smem();  // generic writes of B -> visible to the tensor core (async proxy)
+      const uint16_t hb = *reinterpret_cast<const uint16_t*>(smem + kOffR + s * kRBytes + e * 2);
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(b_full(s));
-        mbar_arrive(s_full(ss));
-      }
+      if (lane == 0) mbar_arrive(b_full(s));
+      // scale stage: W after the epilogue has released the stage, forwarded once D has landed
+      if (c >= kStagesS && !wait(s_empty(ss), phs ^ 1u)) break;
+      reinterpret_cast<float*>(smem + kOffW + ss * kWBytes)[e] = __half2float(__ushort_as_half(hb)) * 0x1p39f;
+      if (!wait(d_full(ss), phs)) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_full(ss));
+      if (++s == kStagesA) s = 0, ph ^= 1u;
+      if (++ss == kStagesS) ss = 0, phs ^= 1u;
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -375,7 +407,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int m = q * 32 + lane;               // tile row of this thread
     // a warp whose 32 rows all lie beyond M keeps the barrier protocol but skips the loads and math
     const bool rows_live = m0 + q * 32 < p.M;
-    int nchunks_live = nchunks;
     constexpr int H = kEpiCols / 2;
     float2 acc[H], tsum[H];
 #pragma unroll
@@ -403,67 +434,76 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     if (!rows_live) {
       // every row of this warp lies beyond M: only the barrier protocol. Each
-      // arrival follows the wait on the same use of the slot, which keeps it in
-      // that use's phase.
+      // arrival follows the wait on the same use of the barrier's stage or
+      // slot, which keeps it in that use's phase.
+      int ss = 0;
+      uint32_t phs = 0;
       for (int c = 0; c < nchunks && ok; ++c) {
-        const int s = c % kStagesA;
-        ok = wait(a_full(s), (uint32_t)((c / kStagesA) & 1));
+        const int cs = c & (kChunkSlots - 1);
+        ok = wait(s_full(ss), phs) && wait(mma_done(cs), (uint32_t)((c / kChunkSlots) & 1));
         __syncwarp();
-        if (ok && lane == 0) mbar_arrive(ab_empty(s));
-        for (int j = 0; j < kGroupsPerChunk && ok; ++j) {
-          const int g = c * kGroupsPerChunk + j, gs = g % kGroupSlots;
-          ok = wait(mma_done(gs), (uint32_t)((g / kGroupSlots) & 1));
-          __syncwarp();
-          if (ok && lane == 0) mbar_arrive(d_free(gs));
+        if (ok && lane == 0) {
+          mbar_arrive(d_free(cs));
+          mbar_arrive(s_empty(ss));
         }
-        const int ss = c % kStagesS;
-        ok = ok && wait(s_full(ss), (uint32_t)((c / kStagesS) & 1));
-        __syncwarp();
-        if (ok && lane == 0) mbar_arrive(s_empty(ss));
+        if (++ss == kStagesS) ss = 0, phs ^= 1u;
       }
-      nchunks_live = 0;
-    }
-    for (int c = 0; c < nchunks_live && ok; ++c) {
-      const int ss = c % kStagesS, s = c % kStagesA;
-      // this row's 4 activation scales from D[s]; the stage is released right after
-      if (!wait(a_full(s), (uint32_t)((c / kStagesA) & 1))) break;
-      const float4 dv = *reinterpret_cast<const float4*>(smem + kOffD + s * kDBytes + m * 16);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ab_empty(s));
-      const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
-#pragma unroll
-      for (int j = 0; j < kGroupsPerChunk; ++j) {
-        const int g = c * kGroupsPerChunk + j, gs = g % kGroupSlots;
-        if (!wait(mma_done(gs), (uint32_t)((g / kGroupSlots) & 1))) {
-          ok = false;
-          break;
-        }
-        // both steps' loads in flight behind one wait; the group's regions are
-        // released as soon as they are in registers, before the math
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + gs * kStepsPerGroup * kTileN + cg * kEpiCols;
+    } else if (nchunks > 0) {
+      const uint32_t tlane = tmem_base + ((uint32_t)(q * 32) << 16) + cg * kEpiCols;
+      uint32_t buf[2][kEpiCols];
+      int ss = 0;
+      uint32_t phs = 0;
+      // prologue: chunk 0's scales and the load of its first step
+      ok = wait(s_full(0), 0) && wait(mma_done(0), 0);
+      float4 dv = ok ? *reinterpret_cast<const float4*>(smem + kOffD + m * 16) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok) {
         tc_fence_after();
-        uint32_t dr0[kEpiCols], dr1[kEpiCols];
-        tmem_ld16_async(taddr, dr0);
-        tmem_ld16_async(taddr + kTileN, dr1);
-        tmem_wait16x2(dr0, dr1);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(d_free(gs));  // the group's regions may be overwritten now
-        step_math(dr0, dk[j * kStepsPerGroup], j == 0);
-        step_math(dr1, dk[j * kStepsPerGroup + 1], false);
+        tmem_ld16_async(tlane, buf[0]);
       }
-      if (!ok || !wait(s_full(ss), (uint32_t)((c / kStagesS) & 1))) break;
-      const float* sc = reinterpret_cast<const float*>(smem + kOffS) + ss * kTileN + cg * kEpiCols;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int cs = c & (kChunkSlots - 1);
+        const float dk[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-      for (int i = 0; i < H; ++i) {
-        const float2 s2 = make_float2(sc[2 * i], sc[2 * i + 1]);
-        acc[i] = __ffma2_rn(s2, tsum[i], acc[i]);
+        for (int ks = 0; ks < kStepsPerChunk; ++ks) {
+          tmem_wait16(buf[ks & 1]);  // step ks of chunk c
+          if (ks + 1 < kStepsPerChunk) {
+            tmem_ld16_async(tlane + (cs * kStepsPerChunk + ks + 1) * kTileN, buf[(ks + 1) & 1]);
+          } else {
+            // the chunk is in registers: release its slot, start the next chunk's first load
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_free(cs));
+            if (c + 1 < nchunks) {
+              const int cn = c + 1, csn = cn & (kChunkSlots - 1);
+              if (!wait(mma_done(csn), (uint32_t)((cn / kChunkSlots) & 1))) ok = false;
+              if (ok) {
+                tc_fence_after();
+                tmem_ld16_async(tlane + csn * kStepsPerChunk * kTileN, buf[0]);
+              }
+            }
+          }
+          step_math(buf[ks & 1], dk[ks], ks == 0);
+        }
+        // weight scales of the chunk's 128-column block; then the stage is free
+        const float* sc = reinterpret_cast<const float*>(smem + kOffW + ss * kWBytes) + cg * kEpiCols;
+#pragma unroll
+        for (int i = 0; i < H; ++i) {
+          const float2 s2 = make_float2(sc[2 * i], sc[2 * i + 1]);
+          acc[i] = __ffma2_rn(s2, tsum[i], acc[i]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty(ss));
+        if (++ss == kStagesS) ss = 0, phs ^= 1u;
+        if (ok && c + 1 < nchunks) {
+          if (!wait(s_full(ss), phs)) ok = false;
+          else dv = *reinterpret_cast<const float4*>(smem + kOffD + ss * kDBytes + m * 16);
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(ss));
+      if (!ok) tmem_wait16(buf[0]);  // no load left in flight
     }
     // The tile goes out through shared memory as whole rows. The A ring is idle
-    // here: this warp has seen every chunk's TMA land and every MMA complete.
+    // here: this warp has seen every chunk's MMAs complete, and they consumed
+    // every chunk's TMA.
     float* stg = reinterpret_cast<float*>(smem + kOffA);  // [128][kStgLd]
     if (rows_live) {
       float4* dst = reinterpret_cast<float4*>(stg + m * kStgLd + cg * kEpiCols);
