@@ -35,7 +35,8 @@ EXPORTS = (
     "btf_gemv_gather", "btf_alloc", "btf_free", "btf_ipc_handle", "btf_ipc_open", "btf_ipc_close",
     "btf_gather_epoch_advance", "btf_gather_wait", "btf_gather_barrier", "btf_prep",
     "btf_gguf_open", "btf_gguf_close", "btf_gguf_tensor_count", "btf_gguf_find", "btf_gguf_tensor",
-    "btf_gguf_load_panels",
+    "btf_gguf_load_panels", "btf_decoder_open", "btf_decoder_synthetic", "btf_decoder_step", "btf_decoder_run",
+    "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info",
 )
 
 
@@ -86,6 +87,25 @@ class TaggedBufC(ctypes.Structure):
     _fields_ = [("p", ctypes.c_void_p), ("words", ctypes.c_int64), ("site", ctypes.c_int)]
 
 
+class DecoderOptsC(ctypes.Structure):
+    _fields_ = [("n_ctx", ctypes.c_int), ("round_q_f16", ctypes.c_int), ("attn_splits", ctypes.c_int),
+                ("cuda_graph", ctypes.c_int)]
+
+
+DIM_FIELDS = ("n_layer", "n_embd", "n_ff", "n_vocab", "n_head", "n_head_kv", "head_dim", "n_rot", "d_state",
+              "n_group", "dt_rank", "d_inner", "conv_kernel", "hadamard_block")
+
+
+class DecoderDimsC(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_int) for f in DIM_FIELDS] + [("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+
+class DecoderInfoC(ctypes.Structure):
+    _fields_ = [("dims", DecoderDimsC), ("pos", ctypes.c_int), ("stream", ctypes.c_void_p),
+                ("weight_bytes", ctypes.c_uint64), ("state_bytes", ctypes.c_uint64),
+                ("kv_bytes_per_token", ctypes.c_uint64), ("logits", ctypes.c_void_p)]
+
+
 def lib() -> ctypes.CDLL:
     """Loads libbtf_b200.so (raises if it was not built)."""
     global _lib
@@ -131,6 +151,14 @@ def lib() -> ctypes.CDLL:
         "btf_gguf_find": (i64, [vp, ctypes.c_char_p]),
         "btf_gguf_tensor": (i32, [vp, i64, ctypes.POINTER(GgufTensorC)]),
         "btf_gguf_load_panels": (i32, [vp, i64, vp, i64, vp]),
+        "btf_decoder_open": (i32, [ctypes.c_char_p, ctypes.POINTER(DecoderOptsC), ctypes.POINTER(vp)]),
+        "btf_decoder_synthetic": (i32, [ctypes.POINTER(DecoderDimsC), ctypes.c_uint64, ctypes.POINTER(DecoderOptsC),
+                                        ctypes.POINTER(vp)]),
+        "btf_decoder_step": (i32, [vp, ctypes.c_int32, vp, ctypes.POINTER(ctypes.c_int32)]),
+        "btf_decoder_run": (i32, [vp, i32]),
+        "btf_decoder_reset": (i32, [vp]),
+        "btf_decoder_close": (i32, [vp]),
+        "btf_decoder_get_info": (i32, [vp, ctypes.POINTER(DecoderInfoC)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -437,3 +465,62 @@ class GgufFile:
         check(lib().btf_gguf_load_panels(self.h, index, _ptr(out), staging_bytes, _stream(stream)),
               "btf_gguf_load_panels")
         return PanelMatrix(out, N, K)
+
+
+class Decoder:
+    """The batch-1 qwen35 decode step (btf_decoder_*): from a GGUF file or from
+    seeded synthetic weights of a given geometry (a dict of DIM_FIELDS plus
+    rope_base / rms_eps)."""
+
+    def __init__(self, path: Optional[str] = None, dims: Optional[dict] = None, seed: int = 1, n_ctx: int = 4096,
+                 round_q_f16: bool = True, attn_splits: int = 16, cuda_graph: bool = True, device: int = 0):
+        torch = _torch()
+        torch.cuda.set_device(device)
+        ensure_init(device)
+        o = DecoderOptsC(n_ctx, int(round_q_f16), attn_splits, int(cuda_graph))
+        h = ctypes.c_void_p()
+        if path is not None:
+            check(lib().btf_decoder_open(path.encode(), ctypes.byref(o), ctypes.byref(h)), "btf_decoder_open")
+        else:
+            d = DecoderDimsC(*[int(dims.get(f, 0)) for f in DIM_FIELDS], float(dims.get("rope_base", 1e4)),
+                             float(dims.get("rms_eps", 1e-6)))
+            check(lib().btf_decoder_synthetic(ctypes.byref(d), seed, ctypes.byref(o), ctypes.byref(h)),
+                  "btf_decoder_synthetic")
+        self.h = h.value
+
+    def close(self) -> None:
+        if self.h:
+            lib().btf_decoder_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def info(self) -> dict:
+        i = DecoderInfoC()
+        check(lib().btf_decoder_get_info(self.h, ctypes.byref(i)), "btf_decoder_get_info")
+        r = {f: getattr(i.dims, f) for f in DIM_FIELDS}
+        r.update(rope_base=i.dims.rope_base, rms_eps=i.dims.rms_eps, pos=i.pos, stream=i.stream,
+                 weight_bytes=int(i.weight_bytes), state_bytes=int(i.state_bytes),
+                 kv_bytes_per_token=int(i.kv_bytes_per_token), logits=i.logits)
+        return r
+
+    def step(self, token: int, logits: bool = False):
+        """One token -> (greedy next token, logits as a numpy array or None)."""
+        import numpy as np
+
+        out = np.empty(self.info()["n_vocab"], dtype=np.float32) if logits else None
+        nxt = ctypes.c_int32()
+        check(lib().btf_decoder_step(self.h, token, out.ctypes.data if logits else None, ctypes.byref(nxt)),
+              "btf_decoder_step")
+        return nxt.value, out
+
+    def run(self, steps: int) -> None:
+        """`steps` greedy steps on the device (asynchronous on the decoder's stream)."""
+        check(lib().btf_decoder_run(self.h, steps), "btf_decoder_run")
+
+    def reset(self) -> None:
+        check(lib().btf_decoder_reset(self.h), "btf_decoder_reset")

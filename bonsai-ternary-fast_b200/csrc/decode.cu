@@ -1,0 +1,538 @@
+// Kernels of the batch-1 decode step other than the matmuls (the ternary
+// GEMVs and the fused prep live in gemv.cu and quant.cu).
+//
+// Each kernel restates one piece of the reference's CPU emulator of its CUDA
+// decode step (src/emu_decoder.cpp of bonsai-ternary-fast), which is the
+// oracle the decoder is tested against:
+//   embed_kernel      packed token_embd row -> inverse transform   (:175-183)
+//   ab_gates_kernel   alpha / beta dots, softplus, sigmoid          (:235-249)
+//   conv_silu_kernel  causal conv (K taps) + SiLU, state shift      (:251-264)
+//   gdn_kernel        gated delta rule + gated RMSNorm per v-head   (:266-298)
+//   attn_prep_kernel  q/k RMSNorm, partial RoPE, fp16 KV write      (:307-338)
+//   attn_split_kernel / attn_combine_kernel
+//                     softmax attention over the fp16 KV cache in
+//                     key splits, then the sigmoid gate             (:339-372)
+//   argmax kernels    greedy token, lowest index on ties            (:214-217)
+// The decode position lives in device memory, so one captured graph serves
+// every token.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cfloat>
+
+#include "common.cuh"
+#include "decode.h"
+
+namespace btf {
+namespace {
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+// bd::softplus (cpu_ops.cpp:136): threshold 20
+__device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+// bd::f32_to_bf16 (types.cpp:64-70) then back: round to nearest even on the bits
+__device__ __forceinline__ float round_bf16(float f) {
+  uint32_t x = __float_as_uint(f);
+  if ((x & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(((x >> 16) | 0x40u) << 16);
+  x += 0x7fffu + ((x >> 16) & 1u);
+  return __uint_as_float((x >> 16) << 16);
+}
+
+// Block-wide sum of one double per thread (blockDim.x a multiple of 32, <= 1024).
+__device__ double block_sum(double v, double* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  double s = 0.0;
+  for (int i = 0; i < nw; ++i) s += red[i];
+  return s;
+}
+
+// bd::rmsnorm (cpu_ops.cpp:116-122): double sum of squares, float mean,
+// 1/sqrt(mean + eps) in float.
+__device__ __forceinline__ float rms_scale(double sumsq, int n, float eps) {
+  const float mean = (float)(sumsq / n);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// ------------------------------------------------------------------ embed
+// One CTA per transform block of `blk` columns (blk threads; blk = 0: no
+// transform, 256 columns per CTA). Row r of the panel matrix: group r/8, quad
+// (r%8)/4, bit pair 2*(r%4) of byte (c%4) of word (c%16)/4 of the 16-column half.
+__global__ void embed_kernel(const uint8_t* __restrict__ pan, int V, int E, int S, const int32_t* __restrict__ tok,
+                             int blk, const float* __restrict__ signs, float* __restrict__ x) {
+  extern __shared__ float sh[];
+  const int n = blk ? blk : blockDim.x;
+  const int e = blockIdx.x * n + threadIdx.x;
+  const int r = min(max(*tok, 0), V - 1);  // the host validates tokens; the clamp keeps reads in bounds
+  const int g = r >> 3, rr = r & 7, h = rr >> 2, k = rr & 3;
+  float v = 0.f;
+  if (e < E) {
+    const int j = e >> 10, c = e & 1023, bb = c >> 7, sb = (c >> 5) & 3, hv = (c >> 4) & 1;
+    const uint8_t* p = pan + ((int64_t)g * S + j) * kPanelBytes;
+    const uint8_t byte = p[h * 1024 + hv * 512 + (bb * 4 + sb) * 16 + ((c >> 2) & 3) * 4 + (c & 3)];
+    const int code = (byte >> (2 * k)) & 3;
+    const uint16_t sc = *reinterpret_cast<const uint16_t*>(p + kCodeBytes + bb * 16 + rr * 2);
+    v = __fmul_rn((float)(code - 1), __half2float(__ushort_as_half(sc)));
+  }
+  if (!blk) {
+    if (e < E) x[e] = v;
+    return;
+  }
+  // bd::hadamard_inverse (cpu_ops.cpp:109-114): fwht of the block, * 1/sqrt(blk), then signs
+  sh[threadIdx.x] = v;
+  __syncthreads();
+  for (int len = 1; len < n; len <<= 1) {
+    const int i = threadIdx.x;
+    float a = 0.f, b = 0.f;
+    const bool lo = !(i & len);
+    if (lo) {
+      a = sh[i];
+      b = sh[i + len];
+    }
+    __syncthreads();
+    if (lo) {
+      sh[i] = __fadd_rn(a, b);
+      sh[i + len] = __fsub_rn(a, b);
+    }
+    __syncthreads();
+  }
+  if (e < E) {
+    float o = __fmul_rn(sh[threadIdx.x], __fdiv_rn(1.0f, __fsqrt_rn((float)n)));
+    if (signs) o = __fmul_rn(o, signs[e]);
+    x[e] = o;
+  }
+}
+
+// ------------------------------------------------------------------ alpha / beta
+// CTA per v-head h: beta[h] = sigmoid(bw[h] . x), g[h] = softplus(aw[h] . x + dt[h]) * a[h],
+// x = xn rounded to bf16 when the alpha/beta weights are bf16.
+__global__ void ab_gates_kernel(const float* __restrict__ xn, int E, const float* __restrict__ aw,
+                                const float* __restrict__ bw, const float* __restrict__ dt,
+                                const float* __restrict__ a, int bf16_in, float* __restrict__ beta,
+                                float* __restrict__ g) {
+  __shared__ double red[32];
+  const int h = blockIdx.x;
+  double sa = 0.0, sb = 0.0;
+  for (int i = threadIdx.x; i < E; i += blockDim.x) {
+    const float xv = bf16_in ? round_bf16(xn[i]) : xn[i];
+    sa += (double)__fmul_rn(aw[(int64_t)h * E + i], xv);
+    sb += (double)__fmul_rn(bw[(int64_t)h * E + i], xv);
+  }
+  sa = block_sum(sa, red);
+  sb = block_sum(sb, red);
+  if (threadIdx.x == 0) {
+    beta[h] = sigmoidf_((float)sb);
+    g[h] = __fmul_rn(softplus(__fadd_rn((float)sa, dt[h])), a[h]);
+  }
+}
+
+// ------------------------------------------------------------------ conv + silu
+// Channel c: s = sum_{i<K-1} state[i][c] w[c][i] + x[c] w[c][K-1] (that order),
+// out = silu(s); the state shifts by one and takes x[c].
+__global__ void conv_silu_kernel(const float* __restrict__ x, float* __restrict__ state, const float* __restrict__ w,
+                                 int C, int K, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float s = 0.f;
+  for (int i = 0; i < K - 1; ++i) s = __fadd_rn(s, __fmul_rn(state[(int64_t)i * C + c], w[(int64_t)c * K + i]));
+  const float xin = x[c];
+  s = __fadd_rn(s, __fmul_rn(xin, w[(int64_t)c * K + K - 1]));
+  for (int i = 0; i + 1 < K - 1; ++i) state[(int64_t)i * C + c] = state[(int64_t)(i + 1) * C + c];
+  state[(int64_t)(K - 2) * C + c] = xin;
+  out[c] = silu(s);
+}
+
+// ------------------------------------------------------------------ gated delta rule
+// CTA per v-head h, kTpc threads per state column j (DV columns of DK floats;
+// state[h][j][i], DK a multiple of 16 up to 128). q, k: l2-normalised rows kh = h % NK of the conv output.
+constexpr int kTpc = 4;
+__global__ void gdn_kernel(const float* __restrict__ cv, const float* __restrict__ z, const float* __restrict__ beta,
+                           const float* __restrict__ gg, float* __restrict__ state, const float* __restrict__ nw,
+                           int NK, int DK, int DV, int QK, float eps, float* __restrict__ o) {
+  extern __shared__ float sm[];  // q[DK], k[DK], out[DV]
+  __shared__ double red[32];
+  float* q = sm;
+  float* k = sm + DK;
+  float* ov = sm + 2 * DK;
+  const int h = blockIdx.x, kh = h % NK, tid = threadIdx.x;
+  // bd::l2norm (cpu_ops.cpp:124-129): x / max(sqrt(sum x^2), eps), sum in double
+  const float* qs = cv + (int64_t)kh * DK;
+  const float* ks = cv + QK + (int64_t)kh * DK;
+  double sq = 0.0, sk = 0.0;
+  for (int i = tid; i < DK; i += blockDim.x) {
+    sq += (double)qs[i] * qs[i];
+    sk += (double)ks[i] * ks[i];
+  }
+  sq = block_sum(sq, red);
+  sk = block_sum(sk, red);
+  const float iq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), eps));
+  const float ik = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), eps));
+  for (int i = tid; i < DK; i += blockDim.x) {
+    q[i] = __fmul_rn(qs[i], iq);
+    k[i] = __fmul_rn(ks[i], ik);
+  }
+  __syncthreads();
+  const float decay = expf(gg[h]), bt = beta[h];
+  const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)DK));
+  // thread (j, part) holds floats i = 16 t + 4 part + {0..3} of column j (DK <= 128)
+  const int j = tid / kTpc, part = tid % kTpc;
+  const int nt = DK / (4 * kTpc);
+  float4* col = reinterpret_cast<float4*>(state + ((int64_t)h * DV + j) * DK) + part;
+  const float4* k4 = reinterpret_cast<const float4*>(k) + part;
+  const float4* q4 = reinterpret_cast<const float4*>(q) + part;
+  const float vj = cv[2 * QK + (int64_t)h * DV + j];
+  float4 st[8];
+  float kv = 0.f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    if (t < nt) {
+      const float4 c = col[t * kTpc], kk = k4[t * kTpc];
+      st[t] = make_float4(__fmul_rn(c.x, decay), __fmul_rn(c.y, decay), __fmul_rn(c.z, decay), __fmul_rn(c.w, decay));
+      kv = __fadd_rn(kv, __fmul_rn(st[t].x, kk.x));
+      kv = __fadd_rn(kv, __fmul_rn(st[t].y, kk.y));
+      kv = __fadd_rn(kv, __fmul_rn(st[t].z, kk.z));
+      kv = __fadd_rn(kv, __fmul_rn(st[t].w, kk.w));
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < kTpc; off <<= 1) kv += __shfl_xor_sync(0xffffffffu, kv, off);
+  const float dl = __fmul_rn(__fsub_rn(vj, kv), bt);
+  float acc = 0.f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    if (t < nt) {
+      const float4 kk = k4[t * kTpc], qq = q4[t * kTpc];
+      float4 c = st[t];
+      c.x = __fadd_rn(c.x, __fmul_rn(kk.x, dl));
+      c.y = __fadd_rn(c.y, __fmul_rn(kk.y, dl));
+      c.z = __fadd_rn(c.z, __fmul_rn(kk.z, dl));
+      c.w = __fadd_rn(c.w, __fmul_rn(kk.w, dl));
+      col[t * kTpc] = c;
+      acc = __fadd_rn(acc, __fmul_rn(c.x, qq.x));
+      acc = __fadd_rn(acc, __fmul_rn(c.y, qq.y));
+      acc = __fadd_rn(acc, __fmul_rn(c.z, qq.z));
+      acc = __fadd_rn(acc, __fmul_rn(c.w, qq.w));
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < kTpc; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  const float oj = __fmul_rn(acc, qscale);
+  if (part == 0) ov[j] = oj;
+  __syncthreads();
+  // bd::rmsnorm over the head's DV outputs with ssm_norm, then * silu(z)
+  double ss = 0.0;
+  for (int i = tid; i < DV; i += blockDim.x) ss += (double)ov[i] * ov[i];
+  ss = block_sum(ss, red);
+  const float sc = rms_scale(ss, DV, eps);
+  for (int i = tid; i < DV; i += blockDim.x) {
+    const float y = __fmul_rn(__fmul_rn(ov[i], sc), nw[i]);
+    o[(int64_t)h * DV + i] = __fmul_rn(y, silu(z[(int64_t)h * DV + i]));
+  }
+}
+
+// ------------------------------------------------------------------ attention prep
+// CTA per head: blockIdx.x < H are q heads (rows h*2D .. of qf), the rest k
+// heads. D threads. RMSNorm with q_norm / k_norm, then RoPE on the first R
+// dims at position *pos: theta_0 = pos, theta_{i+1} = theta_i * base^(-2/R)
+// (in float, as the emulator), pairs (i, i + R/2). q is rounded to fp16 when
+// round_q; k and v go to the fp16 cache row pos.
+__global__ void attn_prep_kernel(const float* __restrict__ qf, const float* __restrict__ kin,
+                                 const float* __restrict__ vin, const float* __restrict__ qn,
+                                 const float* __restrict__ kn, int H, int HK, int D, int R, float theta_scale,
+                                 float eps, const int32_t* __restrict__ pos_p, int round_q, float* __restrict__ qout,
+                                 __half* __restrict__ kc, __half* __restrict__ vc) {
+  extern __shared__ float hv[];
+  __shared__ double red[32];
+  const int b = blockIdx.x, i = threadIdx.x;
+  const bool isq = b < H;
+  const int hh = isq ? b : b - H;
+  const float* src = isq ? qf + (int64_t)hh * 2 * D : kin + (int64_t)hh * D;
+  const float* w = isq ? qn : kn;
+  const float xv = i < D ? src[i] : 0.f;
+  double ss = block_sum(i < D ? (double)xv * xv : 0.0, red);
+  const float sc = rms_scale(ss, D, eps);
+  if (i < D) hv[i] = __fmul_rn(__fmul_rn(xv, sc), w[i]);
+  __syncthreads();
+  const int p = *pos_p;
+  float outv = i < D ? hv[i] : 0.f;
+  if (i < R) {
+    const int ic = i < R / 2 ? i : i - R / 2;
+    float theta = (float)p;
+    for (int t = 0; t < ic; ++t) theta = __fmul_rn(theta, theta_scale);
+    const float c = cosf(theta), s = sinf(theta);
+    const float x0 = hv[ic], x1 = hv[ic + R / 2];
+    outv = i < R / 2 ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)) : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  }
+  if (i >= D) return;
+  const int64_t kvw = (int64_t)HK * D;
+  if (isq) {
+    qout[(int64_t)hh * D + i] = round_q ? __half2float(__float2half_rn(outv)) : outv;
+  } else {
+    kc[(int64_t)p * kvw + (int64_t)hh * D + i] = __float2half_rn(outv);
+    vc[(int64_t)p * kvw + (int64_t)hh * D + i] = __float2half_rn(vin[(int64_t)hh * D + i]);
+  }
+}
+
+// ------------------------------------------------------------------ attention
+// Grid (H, splits): split s covers keys [s*chunk, min((s+1)*chunk, pos+1)).
+// Each of the 4 warps walks every 4th key: lane-sliced dot q.k (D/32 dims per
+// lane), then an online softmax with its running max / sum and V accumulator.
+// The CTA merges its warps and writes (max, sum, acc[D]) for the split.
+constexpr int kAttnWarps = 4;
+__global__ void attn_split_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                                  const __half* __restrict__ vc, int H, int HK, int D, int chunk, float scale,
+                                  const int32_t* __restrict__ pos_p, float* __restrict__ part) {
+  extern __shared__ float sm[];  // q[D], then per warp: m, l, acc[D]
+  const int h = blockIdx.x, sp = blockIdx.y, lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int g = h / (H / HK), T = *pos_p + 1;
+  const int t0 = sp * chunk, t1 = min(t0 + chunk, T);
+  float* qs = sm;
+  float* wm = sm + D + wp * (D + 2);
+  for (int i = threadIdx.x; i < D; i += blockDim.x) qs[i] = q[(int64_t)h * D + i];
+  __syncthreads();
+  const int per = D / 32;
+  float m = -INFINITY, l = 0.f;
+  float acc[8];  // D <= 256
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+  const int64_t kvw = (int64_t)HK * D;
+  for (int t = t0 + wp; t < t1; t += kAttnWarps) {
+    const __half* kt = kc + (int64_t)t * kvw + (int64_t)g * D;
+    float dd = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < per) dd = fmaf(qs[lane * per + r], __half2float(kt[lane * per + r]), dd);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) dd += __shfl_xor_sync(0xffffffffu, dd, o);
+    const float s = dd * scale;
+    const float mn = fmaxf(m, s);
+    const float cf = expf(m - mn), pf = expf(s - mn);
+    l = l * cf + pf;
+    const __half* vt = vc + (int64_t)t * kvw + (int64_t)g * D;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < per) acc[r] = fmaf(pf, __half2float(vt[lane * per + r]), acc[r] * cf);
+    m = mn;
+  }
+  if (lane == 0) {
+    wm[0] = m;
+    wm[1] = l;
+  }
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+    if (r < per) wm[2 + lane * per + r] = acc[r];
+  __syncthreads();
+  // merge the warps
+  float* out = part + ((int64_t)h * gridDim.y + sp) * (D + 2);
+  float M = -INFINITY;
+  for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm[D + w * (D + 2)]);
+  for (int i = threadIdx.x; i < D + 2; i += blockDim.x) {
+    float v = 0.f;
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float* ww = sm + D + w * (D + 2);
+      const float f = ww[0] == -INFINITY ? 0.f : expf(ww[0] - M);
+      if (i == 1) v += ww[1] * f;
+      else if (i >= 2) v += ww[i] * f;
+    }
+    out[i] = i == 0 ? M : v;
+  }
+}
+
+// CTA per head: o = (sum_s acc_s e^{m_s - M}) / (sum_s l_s e^{m_s - M}) * sigmoid(gate).
+__global__ void attn_combine_kernel(const float* __restrict__ part, int splits, int D, const float* __restrict__ qf,
+                                    float* __restrict__ o) {
+  const int h = blockIdx.x;
+  const float* ph = part + (int64_t)h * splits * (D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ph[(int64_t)s * (D + 2)]);
+  float L = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float ms = ph[(int64_t)s * (D + 2)];
+    if (ms != -INFINITY) L += ph[(int64_t)s * (D + 2) + 1] * expf(ms - M);
+  }
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float a = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float ms = ph[(int64_t)s * (D + 2)];
+      if (ms != -INFINITY) a += ph[(int64_t)s * (D + 2) + 2 + i] * expf(ms - M);
+    }
+    const float gate = qf[(int64_t)h * 2 * D + D + i];
+    o[(int64_t)h * D + i] = a / L * sigmoidf_(gate);
+  }
+}
+
+// ------------------------------------------------------------------ argmax
+// Stage 1: CTA b takes a contiguous range; (value, index) with the lowest
+// index among equal maxima. NaN counts as -inf (the emulator's
+// `lg[i] > lg[best]` never picks a NaN), so all-NaN logits give index 0.
+__device__ __forceinline__ void better(float& v, int& i, float v2, int i2) {
+  if (i2 < 0) return;
+  if (v2 != v2) v2 = -INFINITY;
+  if (i < 0 || v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+__global__ void argmax1_kernel(const float* __restrict__ x, int n, float* __restrict__ pv, int* __restrict__ pi) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int per = (n + gridDim.x - 1) / gridDim.x, b0 = blockIdx.x * per, b1 = min(n, b0 + per);
+  float v = -INFINITY;
+  int idx = -1;
+  for (int i = b0 + threadIdx.x; i < b1; i += blockDim.x) better(v, idx, x[i], i);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) better(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = v;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(v, idx, sv[w], si[w]);
+    pv[blockIdx.x] = v;
+    pi[blockIdx.x] = idx;
+  }
+}
+// Stage 2: one warp; writes the token, and the next step's input token and
+// position (pos += 1) when those pointers are given.
+__global__ void argmax2_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int parts,
+                               int32_t* __restrict__ out, int32_t* __restrict__ tok_next, int32_t* __restrict__ pos) {
+  float v = -INFINITY;
+  int idx = -1;
+  for (int i = threadIdx.x; i < parts; i += 32) better(v, idx, pv[i], pi[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) better(v, idx, __shfl_xor_sync(0xffffffffu, v, o), __shfl_xor_sync(0xffffffffu, idx, o));
+  if (threadIdx.x == 0) {
+    const int t = idx < 0 ? 0 : idx;
+    *out = t;
+    if (tok_next) *tok_next = t;
+    if (pos) *pos += 1;
+  }
+}
+
+// Fills a panel buffer with seeded valid codes (0..2) and fp16 scales
+// |N(0,1)| * scale_mul; padding rows / columns get code 1 and scale 0.
+__device__ __forceinline__ uint32_t mix32(uint64_t x) {
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdull;
+  x ^= x >> 33;
+  x *= 0xc4ceb9fe1a85ec53ull;
+  x ^= x >> 33;
+  return (uint32_t)x;
+}
+__global__ void fill_panels_kernel(uint8_t* __restrict__ pan, int64_t npanels, int N, int K, int S, uint64_t seed,
+                                   float scale_mul) {
+  const int64_t nb = npanels * kPanelBytes;
+  for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pidx = b / kPanelBytes;
+    const int off = (int)(b % kPanelBytes);
+    const int g = (int)(pidx / S), j = (int)(pidx % S);
+    if (off < kCodeBytes) {
+      // byte: 4 rows (bit pairs) of one column
+      const int h = off >> 10, c = j * 1024 + ((off >> 4) & 31) / 4 * 128 + ((off >> 4) & 3) * 32 +
+                                   ((off >> 9) & 1) * 16 + ((off >> 2) & 3) * 4 + (off & 3);
+      uint32_t rnd = mix32(seed * 0x9e3779b97f4a7c15ull + (uint64_t)b);
+      uint8_t byte = 0;
+      for (int k = 0; k < 4; ++k) {
+        const int row = g * 8 + h * 4 + k;
+        int code = 1;
+        if (row < N && c < K) {
+          code = (int)((rnd & 0xffff) % 3u);
+          rnd >>= 8;
+          rnd ^= mix32((uint64_t)b * 4 + k + seed);
+        }
+        byte |= (uint8_t)(code << (2 * k));
+      }
+      pan[b] = byte;
+    } else {
+      const int so = off - kCodeBytes, bb = so >> 4, rr = (so >> 1) & 7;
+      const int row = g * 8 + rr, col = j * 1024 + bb * 128;
+      if (so & 1) continue;  // the even byte writes both bytes of the fp16
+      float v = 0.f;
+      if (row < N && col < K) {
+        const uint32_t a = mix32(seed ^ (0xabcdef12ull + (uint64_t)b)), c2 = mix32(seed + 77 + (uint64_t)b * 3);
+        const float u1 = ((a >> 8) + 1) * (1.0f / 16777217.0f), u2 = (c2 >> 8) * (1.0f / 16777216.0f);
+        v = fabsf(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2)) * scale_mul;
+      }
+      const uint16_t hb = __half_as_ushort(__float2half_rn(v));
+      pan[b] = (uint8_t)(hb & 0xff);
+      pan[b + 1] = (uint8_t)(hb >> 8);
+    }
+  }
+}
+
+// Seeded floats: base + uniform(-spread, spread).
+__global__ void fill_uniform_kernel(float* __restrict__ x, int64_t n, uint64_t seed, float base, float spread) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t a = mix32(seed * 0x9e3779b97f4a7c15ull + (uint64_t)i);
+    x[i] = base + spread * (2.0f * ((a >> 8) * (1.0f / 16777216.0f)) - 1.0f);
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_embed(const uint8_t* pan, int V, int E, const int32_t* tok, int blk, const float* signs, float* x,
+                         cudaStream_t st) {
+  const int n = blk ? blk : 256;
+  embed_kernel<<<(E + n - 1) / n, n, blk ? blk * sizeof(float) : 0, st>>>(pan, V, E, (int)slices_of(E), tok, blk,
+                                                                          signs, x);
+  return cudaGetLastError();
+}
+cudaError_t launch_ab_gates(const float* xn, int E, const float* aw, const float* bw, const float* dt, const float* a,
+                            int bf16_in, int NV, float* beta, float* g, cudaStream_t st) {
+  ab_gates_kernel<<<NV, 256, 0, st>>>(xn, E, aw, bw, dt, a, bf16_in, beta, g);
+  return cudaGetLastError();
+}
+cudaError_t launch_conv_silu(const float* x, float* state, const float* w, int C, int K, float* out, cudaStream_t st) {
+  conv_silu_kernel<<<(C + 255) / 256, 256, 0, st>>>(x, state, w, C, K, out);
+  return cudaGetLastError();
+}
+cudaError_t launch_gdn(const float* cv, const float* z, const float* beta, const float* g, float* state,
+                       const float* norm_w, int NV, int NK, int DK, int DV, int QK, float eps, float* o,
+                       cudaStream_t st) {
+  gdn_kernel<<<NV, DV * kTpc, (2 * DK + DV) * sizeof(float), st>>>(cv, z, beta, g, state, norm_w, NK, DK, DV, QK, eps,
+                                                                    o);
+  return cudaGetLastError();
+}
+cudaError_t launch_attn_prep(const float* qf, const float* k, const float* v, const float* qn, const float* kn, int H,
+                             int HK, int D, int R, float theta_scale, float eps, const int32_t* pos, int round_q,
+                             float* qout, void* kc, void* vc, cudaStream_t st) {
+  const int threads = (D + 31) / 32 * 32;
+  attn_prep_kernel<<<H + HK, threads, D * sizeof(float), st>>>(qf, k, v, qn, kn, H, HK, D, R, theta_scale, eps, pos,
+                                                                round_q, qout, static_cast<__half*>(kc),
+                                                                static_cast<__half*>(vc));
+  return cudaGetLastError();
+}
+cudaError_t launch_attention(const float* q, const void* kc, const void* vc, const float* qf, int H, int HK, int D,
+                             int n_ctx, int splits, const int32_t* pos, float* part, float* o, cudaStream_t st) {
+  const int chunk = (n_ctx + splits - 1) / splits;
+  const float scale = 1.0f / sqrtf((float)D);
+  attn_split_kernel<<<dim3(H, splits), kAttnWarps * 32, (D + kAttnWarps * (D + 2)) * sizeof(float), st>>>(
+      q, static_cast<const __half*>(kc), static_cast<const __half*>(vc), H, HK, D, chunk, scale, pos, part);
+  if (cudaError_t e = cudaGetLastError()) return e;
+  attn_combine_kernel<<<H, 128, 0, st>>>(part, splits, D, qf, o);
+  return cudaGetLastError();
+}
+cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, int32_t* out, int32_t* tok_next,
+                          int32_t* pos, cudaStream_t st) {
+  argmax1_kernel<<<parts, 256, 0, st>>>(x, n, pv, pi);
+  if (cudaError_t e = cudaGetLastError()) return e;
+  argmax2_kernel<<<1, 32, 0, st>>>(pv, pi, parts, out, tok_next, pos);
+  return cudaGetLastError();
+}
+cudaError_t launch_fill_panels(uint8_t* pan, int N, int K, uint64_t seed, float scale_mul, cudaStream_t st) {
+  const int64_t np = groups_of(N) * slices_of(K);
+  fill_panels_kernel<<<1184, 256, 0, st>>>(pan, np, N, K, (int)slices_of(K), seed, scale_mul);
+  return cudaGetLastError();
+}
+cudaError_t launch_fill_uniform(float* x, int64_t n, uint64_t seed, float base, float spread, cudaStream_t st) {
+  fill_uniform_kernel<<<592, 256, 0, st>>>(x, n, seed, base, spread);
+  return cudaGetLastError();
+}
+
+}  // namespace btf

@@ -1,0 +1,41 @@
+// Launchers of the non-matmul decode-step kernels (csrc/decode.cu). Internal:
+// the decoder (csrc/decoder.cu) calls them; the C ABI exposes the decoder.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace btf {
+
+// x[E] = inverse transform of row *tok of a panel matrix [V][E] (blk = 0: none).
+cudaError_t launch_embed(const uint8_t* panels, int V, int E, const int32_t* tok, int blk, const float* signs,
+                         float* x, cudaStream_t st);
+// beta[h] = sigmoid(bw[h] . x), g[h] = softplus(aw[h] . x + dt[h]) * a[h] for h < NV.
+cudaError_t launch_ab_gates(const float* xn, int E, const float* aw, const float* bw, const float* dt, const float* a,
+                            int bf16_in, int NV, float* beta, float* g, cudaStream_t st);
+// out[C] = silu(causal conv of x with the K-tap state); state [(K-1)][C] advances.
+cudaError_t launch_conv_silu(const float* x, float* state, const float* w, int C, int K, float* out, cudaStream_t st);
+// Gated delta rule of NV v-heads on the conv output cv, state [NV][DV][DK], then
+// RMSNorm(norm_w) * silu(z) -> o[NV * DV].
+cudaError_t launch_gdn(const float* cv, const float* z, const float* beta, const float* g, float* state,
+                       const float* norm_w, int NV, int NK, int DK, int DV, int QK, float eps, float* o,
+                       cudaStream_t st);
+// q/k RMSNorm + RoPE at *pos; q -> qout[H*D] (fp16-rounded when round_q), k and v
+// -> fp16 caches [n_ctx][HK*D] row *pos.
+cudaError_t launch_attn_prep(const float* qf, const float* k, const float* v, const float* qn, const float* kn, int H,
+                             int HK, int D, int R, float theta_scale, float eps, const int32_t* pos, int round_q,
+                             float* qout, void* kc, void* vc, cudaStream_t st);
+// Softmax attention of H q-heads over keys 0..*pos of the fp16 caches, in
+// `splits` key ranges (part: [H][splits][D + 2] floats), times sigmoid(gate) -> o[H*D].
+cudaError_t launch_attention(const float* q, const void* kc, const void* vc, const float* qf, int H, int HK, int D,
+                             int n_ctx, int splits, const int32_t* pos, float* part, float* o, cudaStream_t st);
+// Greedy argmax of x[n] (lowest index on ties) -> *out; also *tok_next = token and
+// *pos += 1 when those are non-null. pv/pi: `parts` partials.
+cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, int32_t* out, int32_t* tok_next,
+                          int32_t* pos, cudaStream_t st);
+// Seeded synthetic weights: a panel matrix [N][K] of codes 0..2 with fp16
+// scales |N(0,1)| * scale_mul, and uniform floats base +- spread.
+cudaError_t launch_fill_panels(uint8_t* panels, int N, int K, uint64_t seed, float scale_mul, cudaStream_t st);
+cudaError_t launch_fill_uniform(float* x, int64_t n, uint64_t seed, float base, float spread, cudaStream_t st);
+
+}  // namespace btf

@@ -1,0 +1,717 @@
+// Batch-1 decode step of the qwen35 hybrid decoder (gated delta net + gated
+// full attention) on the library's kernels, as one CUDA graph.
+//
+// Mirrors GpuDecoder (src/cuda/gpu_decoder.cu of bonsai-ternary-fast:
+// forward_chunk :401-450, enqueue_step / capture :461-486) and computes what the
+// reference's CPU emulator computes (src/emu_decoder.cpp:167-220, gdn :222-303,
+// attn :305-375): per layer a fused prep (RMSNorm -> Hadamard transform -> Q8)
+// feeding the ternary GEMVs, the mixer (delta rule or attention), the FFN with
+// SwiGLU, then the output norm, lm_head and a greedy argmax. The model binding
+// restates bd::Model::bind (ref/bonsai-decoder/src/model.cpp:68-205) over the
+// library's own GGUF reader. Weights stay resident; the position and the next
+// input token live in device memory, so the captured graph replays for every
+// token. Batch 1 only: a prompt is fed one token per step.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "btf_b200.h"
+#include "common.cuh"
+#include "decode.h"
+#include "gguf_meta.h"
+
+namespace btf {
+namespace {
+
+constexpr uint32_t kF32 = 0, kF16 = 1, kBF16 = 30, kPTQ = 143;
+
+struct Mat {
+  uint8_t* pan = nullptr;
+  int N = 0, K = 0;
+  btf_hx hx{0, 0, 0, 0, nullptr};
+};
+
+struct Layer {
+  bool rec = false;
+  float *attn_norm = nullptr, *post_norm = nullptr;
+  Mat gate, up, down;
+  // gated delta net
+  Mat qkv, zg, out;
+  float *alpha_w = nullptr, *beta_w = nullptr, *ssm_a = nullptr, *ssm_dt = nullptr, *conv_w = nullptr,
+        *ssm_norm = nullptr;
+  int ab_bf16 = 0;
+  float *conv_state = nullptr, *ssm_state = nullptr;
+  // attention
+  Mat wq, wk, wv, wo;
+  float *q_norm = nullptr, *k_norm = nullptr;
+  __half *kc = nullptr, *vc = nullptr;
+};
+
+struct Decoder {
+  int device = 0;
+  cudaStream_t st = nullptr;
+  btf_decoder_dims d{};
+  btf_decoder_opts o{};
+  int C = 0, DK = 0, DV = 0, NK = 0, NV = 0, QK = 0, DI = 0, Kmax = 0;
+  float theta_scale = 0.f;
+  std::vector<Layer> L;
+  Mat embd, output;
+  float* out_norm = nullptr;
+  int inv_block = 0;
+  float* inv_signs = nullptr;
+  std::vector<void*> allocs;
+  // step buffers
+  float *x = nullptr, *xn = nullptr, *bA = nullptr, *bB = nullptr, *bC = nullptr, *bO = nullptr, *bQ = nullptr,
+        *bG = nullptr, *beta = nullptr, *gg = nullptr, *logits = nullptr, *part = nullptr, *amax_v = nullptr;
+  int* amax_i = nullptr;
+  int8_t* aq = nullptr;
+  float* ad = nullptr;
+  int32_t* as = nullptr;
+  int32_t *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr;
+  int32_t* h_io = nullptr;  // pinned: [0] token in, [1] token out
+  int pos = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t weight_bytes = 0, state_bytes = 0, kv_bytes_per_token = 0;
+  static constexpr int kArgmaxParts = 148;
+
+  ~Decoder() {
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (st) cudaStreamSynchronize(st);
+    for (void* p : allocs) cudaFree(p);
+    if (h_io) cudaFreeHost(h_io);
+    if (st) cudaStreamDestroy(st);
+  }
+  template <class T>
+  T* alloc(size_t n, int* rc) {
+    void* p = nullptr;
+    if (*rc) return nullptr;
+    const cudaError_t e = cudaMalloc(&p, n * sizeof(T) > 0 ? n * sizeof(T) : 16);
+    if (e != cudaSuccess) {
+      *rc = cuda_fail(e, "btf_decoder: cudaMalloc");
+      return nullptr;
+    }
+    allocs.push_back(p);
+    return static_cast<T*>(p);
+  }
+};
+
+// ---------------------------------------------------------------- buffers
+int make_buffers(Decoder& D) {
+  int rc = BTF_OK;
+  const btf_decoder_dims& d = D.d;
+  const int E = d.n_embd, F = d.n_ff, H = d.n_head, HK = d.n_head_kv, HD = d.head_dim;
+  int n_gdn = 0, n_attn = 0;
+  for (auto& l : D.L) (l.rec ? n_gdn : n_attn)++;
+  const int wa = std::max(n_gdn ? D.C : 0, n_attn ? 2 * H * HD : 0);
+  const int wb = std::max(n_gdn ? D.DI : 0, n_attn ? HK * HD : 0);
+  const int wc = std::max(n_gdn ? D.C : 0, n_attn ? HK * HD : 0);
+  const int wo = std::max(n_gdn ? D.DI : 0, n_attn ? H * HD : 0);
+  D.Kmax = std::max({E, F, wo});
+  D.x = D.alloc<float>(E, &rc);
+  D.xn = D.alloc<float>(E, &rc);
+  D.bA = D.alloc<float>(wa, &rc);
+  D.bB = D.alloc<float>(wb, &rc);
+  D.bC = D.alloc<float>(wc, &rc);
+  D.bO = D.alloc<float>(wo, &rc);
+  D.bQ = D.alloc<float>(std::max(1, H * HD), &rc);
+  D.bG = D.alloc<float>(F, &rc);
+  D.beta = D.alloc<float>(std::max(1, D.NV), &rc);
+  D.gg = D.alloc<float>(std::max(1, D.NV), &rc);
+  D.logits = D.alloc<float>(d.n_vocab, &rc);
+  D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
+  D.amax_v = D.alloc<float>(Decoder::kArgmaxParts, &rc);
+  D.amax_i = D.alloc<int>(Decoder::kArgmaxParts, &rc);
+  D.aq = D.alloc<int8_t>(D.Kmax, &rc);
+  D.ad = D.alloc<float>(D.Kmax / 32, &rc);
+  D.as = D.alloc<int32_t>(D.Kmax / 32, &rc);
+  D.d_tok = D.alloc<int32_t>(4, &rc);
+  if (rc) return rc;
+  D.d_pos = D.d_tok + 1;
+  D.d_next = D.d_tok + 2;
+  for (Layer& l : D.L) {
+    if (l.rec) {
+      l.conv_state = D.alloc<float>((size_t)(d.conv_kernel - 1) * D.C, &rc);
+      l.ssm_state = D.alloc<float>((size_t)D.NV * D.DV * D.DK, &rc);
+      D.state_bytes += 2 * ((uint64_t)(d.conv_kernel - 1) * D.C + (uint64_t)D.NV * D.DV * D.DK) * 4;
+    } else {
+      l.kc = D.alloc<__half>((size_t)D.o.n_ctx * HK * HD, &rc);
+      l.vc = D.alloc<__half>((size_t)D.o.n_ctx * HK * HD, &rc);
+      D.kv_bytes_per_token += 2ull * HK * HD * 2;
+    }
+  }
+  if (rc) return rc;
+  const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&D.h_io), 4 * sizeof(int32_t), cudaHostAllocDefault);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder: pinned io");
+}
+
+int reset_state(Decoder& D) {
+  cudaError_t e = cudaSuccess;
+  for (Layer& l : D.L) {
+    if (l.rec) {
+      if (e == cudaSuccess)
+        e = cudaMemsetAsync(l.conv_state, 0, (size_t)(D.d.conv_kernel - 1) * D.C * sizeof(float), D.st);
+      if (e == cudaSuccess) e = cudaMemsetAsync(l.ssm_state, 0, (size_t)D.NV * D.DV * D.DK * sizeof(float), D.st);
+    }
+  }
+  if (e == cudaSuccess) e = cudaMemsetAsync(D.d_tok, 0, 4 * sizeof(int32_t), D.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(D.st);
+  D.pos = 0;
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_reset");
+}
+
+// ---------------------------------------------------------------- one step
+int gemv(Decoder& D, std::initializer_list<btf_gemv_seg> segs, int K, int mode) {
+  const btf_q8act act{D.aq, D.ad, D.as};
+  return btf_gemv(segs.begin(), (int)segs.size(), K, 1, act, mode, D.st);
+}
+int prep(Decoder& D, const float* x, int n, const float* normw, const btf_hx& hx, float* xn) {
+  const btf_q8act act{D.aq, D.ad, D.as};
+  return btf_prep(x, n, 1, n, normw, D.d.rms_eps, hx, xn, n, act, D.st);
+}
+#define BTF_TRY(call)                   \
+  do {                                  \
+    const int rc_ = (call);             \
+    if (rc_) return rc_;                \
+  } while (0)
+#define BTF_TRYC(call)                                                        \
+  do {                                                                        \
+    const cudaError_t e_ = (call);                                            \
+    if (e_ != cudaSuccess) return cuda_fail(e_, "btf_decoder: step kernel"); \
+  } while (0)
+
+// Enqueues one decode step for the token at d_tok: logits, the greedy token
+// into d_next and d_tok, and pos + 1.
+int enqueue_step(Decoder& D) {
+  const btf_decoder_dims& d = D.d;
+  const int E = d.n_embd, F = d.n_ff, H = d.n_head, HK = d.n_head_kv, HD = d.head_dim;
+  BTF_TRYC(launch_embed(D.embd.pan, d.n_vocab, E, D.d_tok, D.inv_block, D.inv_signs, D.x, D.st));
+  for (Layer& l : D.L) {
+    if (l.rec) {
+      BTF_TRY(prep(D, D.x, E, l.attn_norm, l.qkv.hx, D.xn));
+      BTF_TRY(gemv(D, {{l.qkv.pan, l.qkv.N, D.bA, l.qkv.N}, {l.zg.pan, l.zg.N, D.bB, l.zg.N}}, E,
+                   BTF_STORE));
+      BTF_TRYC(launch_ab_gates(D.xn, E, l.alpha_w, l.beta_w, l.ssm_dt, l.ssm_a, l.ab_bf16, D.NV, D.beta, D.gg, D.st));
+      BTF_TRYC(launch_conv_silu(D.bA, l.conv_state, l.conv_w, D.C, d.conv_kernel, D.bC, D.st));
+      BTF_TRYC(launch_gdn(D.bC, D.bB, D.beta, D.gg, l.ssm_state, l.ssm_norm, D.NV, D.NK, D.DK, D.DV, D.QK, d.rms_eps,
+                          D.bO, D.st));
+      BTF_TRY(prep(D, D.bO, D.DI, nullptr, l.out.hx, nullptr));
+      BTF_TRY(gemv(D, {{l.out.pan, E, D.x, E}}, D.DI, BTF_ADD));
+    } else {
+      BTF_TRY(prep(D, D.x, E, l.attn_norm, l.wq.hx, nullptr));
+      BTF_TRY(gemv(D,
+                   {{l.wq.pan, l.wq.N, D.bA, l.wq.N},
+                    {l.wk.pan, l.wk.N, D.bB, l.wk.N},
+                    {l.wv.pan, l.wv.N, D.bC, l.wv.N}},
+                   E, BTF_STORE));
+      BTF_TRYC(launch_attn_prep(D.bA, D.bB, D.bC, l.q_norm, l.k_norm, H, HK, HD, d.n_rot, D.theta_scale, d.rms_eps,
+                                D.d_pos, D.o.round_q_f16, D.bQ, l.kc, l.vc, D.st));
+      BTF_TRYC(launch_attention(D.bQ, l.kc, l.vc, D.bA, H, HK, HD, D.o.n_ctx, D.o.attn_splits, D.d_pos, D.part, D.bO,
+                                D.st));
+      BTF_TRY(prep(D, D.bO, H * HD, nullptr, l.wo.hx, nullptr));
+      BTF_TRY(gemv(D, {{l.wo.pan, E, D.x, E}}, H * HD, BTF_ADD));
+    }
+    BTF_TRY(prep(D, D.x, E, l.post_norm, l.gate.hx, nullptr));
+    BTF_TRY(gemv(D, {{l.gate.pan, F, D.bG, F}, {l.up.pan, F, nullptr, 0}}, E, BTF_SWIGLU));
+    BTF_TRY(prep(D, D.bG, F, nullptr, l.down.hx, nullptr));
+    BTF_TRY(gemv(D, {{l.down.pan, E, D.x, E}}, F, BTF_ADD));
+  }
+  BTF_TRY(prep(D, D.x, E, D.out_norm, D.output.hx, nullptr));
+  BTF_TRY(gemv(D, {{D.output.pan, d.n_vocab, D.logits, d.n_vocab}}, E, BTF_STORE));
+  BTF_TRYC(launch_argmax(D.logits, d.n_vocab, D.amax_v, D.amax_i, Decoder::kArgmaxParts, D.d_next, D.d_tok, D.d_pos,
+                         D.st));
+  return BTF_OK;
+}
+
+int capture(Decoder& D) {
+  cudaError_t e = cudaStreamBeginCapture(D.st, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder: begin capture");
+  const int rc = enqueue_step(D);
+  cudaGraph_t g = nullptr;
+  e = cudaStreamEndCapture(D.st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder: end capture");
+  D.graph = g;
+  e = cudaGraphInstantiate(&D.exec, g, 0);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder: graph instantiate");
+}
+
+// Runs one step (graph replay or eager) on D.st, no host synchronisation.
+int run_step(Decoder& D) {
+  if (D.pos >= D.o.n_ctx) return fail(BTF_ERR_ARG, "btf_decoder: context full (n_ctx %d)", D.o.n_ctx);
+  if (D.o.cuda_graph) {
+    if (!D.exec) BTF_TRY(capture(D));
+    const cudaError_t e = cudaGraphLaunch(D.exec, D.st);
+    if (e != cudaSuccess) return cuda_fail(e, "btf_decoder: graph launch");
+  } else {
+    BTF_TRY(enqueue_step(D));
+  }
+  D.pos += 1;
+  return BTF_OK;
+}
+
+// ---------------------------------------------------------------- weights
+int upload_f32(Decoder& D, const void* src, uint32_t type, int64_t n, float** out) {
+  int rc = BTF_OK;
+  float* p = D.alloc<float>(n, &rc);
+  if (rc) return rc;
+  std::vector<float> h(n);
+  const uint16_t* s16 = static_cast<const uint16_t*>(src);
+  if (type == kF32) {
+    std::memcpy(h.data(), src, n * 4);
+  } else if (type == kBF16) {
+    for (int64_t i = 0; i < n; ++i) {
+      const uint32_t b = (uint32_t)s16[i] << 16;
+      std::memcpy(&h[i], &b, 4);
+    }
+  } else if (type == kF16) {
+    for (int64_t i = 0; i < n; ++i) h[i] = __half2float(__ushort_as_half(s16[i]));
+  } else {
+    return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: vector tensor of type %u", type);
+  }
+  const cudaError_t e = cudaMemcpy(p, h.data(), n * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder: upload");
+  *out = p;
+  return BTF_OK;
+}
+
+struct Binder {
+  Decoder& D;
+  void* g;
+  std::set<std::string> folded;
+  std::map<int, float*> signs;  // device sign vectors by width
+  int block = 0;
+  bool explicit_signs = false, v_grouped = false;
+
+  const gguf::Value* kv(const std::string& k) { return gguf::meta(g, k); }
+  int64_t geti(const std::string& k, int64_t def, bool* missing = nullptr) {
+    const gguf::Value* v = kv(k);
+    if (!v || v->type == 8 || v->type == 9) {
+      if (missing) *missing = true;
+      return def;
+    }
+    return v->i;
+  }
+  double getf(const std::string& k, double def) {
+    const gguf::Value* v = kv(k);
+    return (!v || v->type == 8 || v->type == 9) ? def : v->f;
+  }
+  std::string gets(const std::string& k) {
+    const gguf::Value* v = kv(k);
+    return v && v->type == 8 ? v->s : std::string();
+  }
+  bool tensor(const std::string& name, btf_gguf_tensor_info* t, int64_t* idx = nullptr) {
+    const int64_t i = btf_gguf_find(g, name.c_str());
+    if (i < 0) return false;
+    if (idx) *idx = i;
+    return btf_gguf_tensor(g, i, t) == BTF_OK;
+  }
+  // A PTQ1_0 matrix [out][in] -> panels, with its input transform (model.cpp:29-58).
+  int mat(const std::string& name, Mat* m) {
+    btf_gguf_tensor_info t;
+    int64_t idx = -1;
+    if (!tensor(name, &t, &idx)) return fail(BTF_ERR_ARG, "btf_decoder: missing tensor %s", name.c_str());
+    if (t.type != kPTQ || t.n_dims != 2) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: %s is not a 2-D PTQ1_0 matrix", name.c_str());
+    m->K = (int)t.ne[0];
+    m->N = (int)t.ne[1];
+    int rc = BTF_OK;
+    m->pan = D.alloc<uint8_t>(btf_panel_bytes(m->N, m->K), &rc);
+    if (rc) return rc;
+    BTF_TRY(btf_gguf_load_panels(g, idx, m->pan, 64 << 20, D.st));
+    D.weight_bytes += btf_panel_bytes(m->N, m->K);
+    if (folded.count(name)) {
+      if (m->K % block) return fail(BTF_ERR_ARG, "btf_decoder: %s width not a multiple of the hadamard block", name.c_str());
+      m->hx.block = block;
+      if (explicit_signs) {
+        auto it = signs.find(m->K);
+        if (it == signs.end()) return fail(BTF_ERR_ARG, "btf_decoder: no sign vector for width %d (%s)", m->K, name.c_str());
+        m->hx.signs = it->second;
+      }
+      if (v_grouped && name.find(".ssm_out.") != std::string::npos) {
+        const int nv = D.NV, nk = D.NK;
+        if (nk <= 0 || nv <= 0 || nv % nk || m->K % nv) return fail(BTF_ERR_ARG, "btf_decoder: bad GDN head geometry");
+        m->hx.perm_hd = m->K / nv;
+        m->hx.perm_nk = nk;
+        m->hx.perm_rep = nv / nk;
+      }
+    }
+    return BTF_OK;
+  }
+  int vec(const std::string& name, float** out, int64_t expect, uint32_t* type = nullptr) {
+    btf_gguf_tensor_info t;
+    if (!tensor(name, &t)) return fail(BTF_ERR_ARG, "btf_decoder: missing tensor %s", name.c_str());
+    int64_t n = 1;
+    for (int i = 0; i < t.n_dims; ++i) n *= t.ne[i];
+    if (expect >= 0 && n != expect) return fail(BTF_ERR_ARG, "btf_decoder: %s has %lld elements, expected %lld", name.c_str(), (long long)n, (long long)expect);
+    if (type) *type = t.type;
+    D.weight_bytes += n * 4;
+    return upload_f32(D, t.data, t.type, n, out);
+  }
+
+  int bind() {
+    if (gets("general.architecture") != "qwen35")
+      return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: architecture '%s' (this decoder implements qwen35)",
+                  gets("general.architecture").c_str());
+    const std::string p = "qwen35.";
+    bool miss = false;
+    btf_decoder_dims& d = D.d;
+    d.n_layer = (int)geti(p + "block_count", 0, &miss);
+    d.n_embd = (int)geti(p + "embedding_length", 0, &miss);
+    d.n_ff = (int)geti(p + "feed_forward_length", 0, &miss);
+    d.n_head = (int)geti(p + "attention.head_count", 0, &miss);
+    d.n_head_kv = (int)geti(p + "attention.head_count_kv", 0, &miss);
+    d.head_dim = (int)geti(p + "attention.key_length", d.n_head ? d.n_embd / d.n_head : 0);
+    if (geti(p + "attention.value_length", d.head_dim) != d.head_dim)
+      return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: key_length != value_length");
+    d.n_rot = (int)geti(p + "rope.dimension_count", d.head_dim);
+    d.rope_base = (float)getf(p + "rope.freq_base", 10000.0);
+    if (getf(p + "rope.scaling.factor", 1.0) != 1.0) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: rope scaling");
+    d.rms_eps = (float)getf(p + "attention.layer_norm_rms_epsilon", 1e-6);
+    d.conv_kernel = (int)geti(p + "ssm.conv_kernel", 0, &miss);
+    d.d_state = (int)geti(p + "ssm.state_size", 0, &miss);
+    d.n_group = (int)geti(p + "ssm.group_count", 0, &miss);
+    d.dt_rank = (int)geti(p + "ssm.time_step_rank", 0, &miss);
+    const int d_inner = (int)geti(p + "ssm.inner_size", 0, &miss);
+    d.d_inner = d_inner;
+    const int interval = (int)geti(p + "full_attention_interval", 4);
+    d.n_layer -= (int)geti(p + "nextn_predict_layers", 0);
+    if (miss) return fail(BTF_ERR_ARG, "btf_decoder: missing qwen35 hyperparameters");
+    if (d.n_head_kv <= 0 || d.n_head % d.n_head_kv || d.n_group <= 0 || d.dt_rank % d.n_group || d.n_rot > d.head_dim ||
+        d.n_rot % 2 || interval <= 0)
+      return fail(BTF_ERR_ARG, "btf_decoder: inconsistent qwen35 hyperparameters");
+    D.DK = d.d_state;
+    if (d_inner % d.dt_rank) return fail(BTF_ERR_ARG, "btf_decoder: ssm.inner_size %% time_step_rank");
+    D.DV = d_inner / d.dt_rank;
+    D.NK = d.n_group;
+    D.NV = d.dt_rank;
+    D.QK = d.d_state * d.n_group;
+    D.DI = d_inner;
+    D.C = 2 * D.QK + d_inner;
+    // prism Hadamard metadata (model.cpp:100-156)
+    const int version = (int)geti("prism.hadamard.version", 0);
+    const bool tied = geti("prism.hadamard.tied_output", 0) != 0;
+    std::set<std::string> inverse;
+    if (version) {
+      if ((version != 1 && version != 2) || ((version == 2) != tied))
+        return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: prism.hadamard.version %d", version);
+      block = (int)geti("prism.hadamard.block_size", 0);
+      if (block <= 0 || (block & (block - 1)) || block > 1024) return fail(BTF_ERR_ARG, "btf_decoder: bad hadamard block");
+      d.hadamard_block = block;
+      if (gets("prism.hadamard.transform") != "normalized-sylvester-walsh-hadamard" ||
+          gets("prism.hadamard.axis") != "input-last-dimension")
+        return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: hadamard transform / axis");
+      const std::string mode = gets("prism.hadamard.sign_mode");
+      if (mode != "identity" && mode != "explicit") return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: sign mode %s", mode.c_str());
+      explicit_signs = mode == "explicit";
+      const gguf::Value* wn = kv("prism.hadamard.weight_names");
+      if (!wn || wn->as.empty()) return fail(BTF_ERR_ARG, "btf_decoder: prism.hadamard.weight_names missing");
+      folded.insert(wn->as.begin(), wn->as.end());
+      if (explicit_signs) {
+        const gguf::Value* sw = kv("prism.hadamard.sign_widths");
+        const gguf::Value* sv = kv("prism.hadamard.sign_values");
+        if (!sw || !sv || sw->ai.empty()) return fail(BTF_ERR_ARG, "btf_decoder: explicit sign mode without sign arrays");
+        size_t off = 0;
+        for (int64_t width : sw->ai) {
+          if (width <= 0 || width % block || off + width > sv->ai.size() || signs.count((int)width))
+            return fail(BTF_ERR_ARG, "btf_decoder: bad sign width");
+          std::vector<float> h(width);
+          for (int64_t i = 0; i < width; ++i) {
+            const int64_t v = sv->ai[off + i];
+            if (v != 1 && v != -1) return fail(BTF_ERR_ARG, "btf_decoder: sign values must be +-1");
+            h[i] = (float)v;
+          }
+          int rc = BTF_OK;
+          float* dv = D.alloc<float>(width, &rc);
+          if (rc) return rc;
+          if (cudaMemcpy(dv, h.data(), width * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(BTF_ERR_CUDA, "btf_decoder: sign upload");
+          signs[(int)width] = dv;
+          off += width;
+        }
+        if (off != sv->ai.size()) return fail(BTF_ERR_ARG, "btf_decoder: sign_values length");
+      }
+      v_grouped = geti("prism.hadamard.gdn_v_grouped", 0) != 0;
+      if (const gguf::Value* inv = kv("prism.hadamard.inverse_weight_names")) {
+        for (auto& s : inv->as) {
+          if (s != "token_embd.weight") return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: inverse table %s", s.c_str());
+          inverse.insert(s);
+        }
+      }
+      if (tied) folded.insert("token_embd.weight");
+    }
+    // embedding (never transformed on lookup), output norm, lm_head
+    const bool embd_folded = folded.count("token_embd.weight") != 0;
+    folded.erase("token_embd.weight");
+    BTF_TRY(mat("token_embd.weight", &D.embd));
+    D.weight_bytes -= btf_panel_bytes(D.embd.N, D.embd.K);  // one row per step is read, counted below
+    D.weight_bytes += (uint64_t)D.embd.K / 4 + (uint64_t)D.embd.K / 64;
+    d.n_vocab = D.embd.N;
+    if (D.embd.K != d.n_embd) return fail(BTF_ERR_ARG, "btf_decoder: token_embd width");
+    if (inverse.count("token_embd.weight")) {
+      D.inv_block = block;
+      if (explicit_signs) {
+        auto it = signs.find(d.n_embd);
+        if (it == signs.end()) return fail(BTF_ERR_ARG, "btf_decoder: no sign vector for the embedding width");
+        D.inv_signs = it->second;
+      }
+    }
+    BTF_TRY(vec("output_norm.weight", &D.out_norm, d.n_embd));
+    btf_gguf_tensor_info t;
+    if (tensor("output.weight", &t)) {
+      BTF_TRY(mat("output.weight", &D.output));
+    } else {
+      if (embd_folded) folded.insert("token_embd.weight");
+      BTF_TRY(mat("token_embd.weight", &D.output));
+    }
+    D.L.resize(d.n_layer);
+    for (int il = 0; il < d.n_layer; ++il) {
+      const std::string b = "blk." + std::to_string(il) + ".";
+      Layer& l = D.L[il];
+      l.rec = ((il + 1) % interval) != 0;
+      BTF_TRY(vec(b + "attn_norm.weight", &l.attn_norm, d.n_embd));
+      BTF_TRY(vec(b + "post_attention_norm.weight", &l.post_norm, d.n_embd));
+      BTF_TRY(mat(b + "ffn_gate.weight", &l.gate));
+      BTF_TRY(mat(b + "ffn_up.weight", &l.up));
+      BTF_TRY(mat(b + "ffn_down.weight", &l.down));
+      if (l.rec) {
+        BTF_TRY(mat(b + "attn_qkv.weight", &l.qkv));
+        BTF_TRY(mat(b + "attn_gate.weight", &l.zg));
+        uint32_t at = 0;
+        BTF_TRY(vec(b + "ssm_alpha.weight", &l.alpha_w, (int64_t)D.NV * d.n_embd, &at));
+        BTF_TRY(vec(b + "ssm_beta.weight", &l.beta_w, (int64_t)D.NV * d.n_embd));
+        l.ab_bf16 = at == kBF16;
+        BTF_TRY(vec(b + "ssm_a", &l.ssm_a, D.NV));
+        BTF_TRY(vec(b + "ssm_dt.bias", &l.ssm_dt, D.NV));
+        BTF_TRY(vec(b + "ssm_conv1d.weight", &l.conv_w, (int64_t)d.conv_kernel * D.C));
+        BTF_TRY(vec(b + "ssm_norm.weight", &l.ssm_norm, D.DV));
+        BTF_TRY(mat(b + "ssm_out.weight", &l.out));
+        if (l.qkv.N != D.C || l.zg.N != D.DI || l.out.K != D.DI)
+          return fail(BTF_ERR_ARG, "btf_decoder: %sGDN matrix shapes", b.c_str());
+      } else {
+        BTF_TRY(mat(b + "attn_q.weight", &l.wq));
+        BTF_TRY(mat(b + "attn_k.weight", &l.wk));
+        BTF_TRY(mat(b + "attn_v.weight", &l.wv));
+        BTF_TRY(mat(b + "attn_output.weight", &l.wo));
+        BTF_TRY(vec(b + "attn_q_norm.weight", &l.q_norm, d.head_dim));
+        BTF_TRY(vec(b + "attn_k_norm.weight", &l.k_norm, d.head_dim));
+        if (l.wq.N != 2 * d.head_dim * d.n_head || l.wk.N != d.head_dim * d.n_head_kv ||
+            l.wo.K != d.head_dim * d.n_head)
+          return fail(BTF_ERR_ARG, "btf_decoder: %sattention matrix shapes", b.c_str());
+      }
+    }
+    return BTF_OK;
+  }
+};
+
+// Geometry the kernels support.
+int check_dims(const Decoder& D) {
+  const btf_decoder_dims& d = D.d;
+  if (d.n_embd % 128 || d.n_ff % 128 || D.DI % 128 || (d.n_head * d.head_dim) % 128)
+    return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: matmul widths must be multiples of 128");
+  if (d.head_dim % 32 || d.head_dim > 256) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: head_dim must be 32..256, a multiple of 32");
+  if (D.DK % 16 || D.DK > 128 || D.DV * 4 > 1024 || D.DV % 8)
+    return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: GDN head sizes (k <= 128, multiple of 16; v <= 256, multiple of 8)");
+  if (d.conv_kernel < 2) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: conv_kernel < 2");
+  if (D.o.n_ctx < 1 || D.o.attn_splits < 1 || D.o.attn_splits > 256)
+    return fail(BTF_ERR_ARG, "btf_decoder: n_ctx >= 1 and 1 <= attn_splits <= 256");
+  return BTF_OK;
+}
+
+int finish_open(Decoder& D) {
+  BTF_TRY(check_dims(D));
+  D.theta_scale = std::pow(D.d.rope_base, -2.0f / (float)D.d.n_rot);
+  BTF_TRY(make_buffers(D));
+  return reset_state(D);
+}
+
+btf_decoder_opts defaults(const btf_decoder_opts* o) {
+  btf_decoder_opts r{4096, 1, 16, 1};
+  if (o) r = *o;
+  return r;
+}
+
+}  // namespace
+}  // namespace btf
+
+using namespace btf;
+
+extern "C" {
+
+int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void** handle) {
+  if (!gguf_path || !handle) return fail(BTF_ERR_ARG, "btf_decoder_open: null argument");
+  *handle = nullptr;
+  auto D = std::make_unique<Decoder>();
+  D->o = defaults(opts);
+  if (cudaGetDevice(&D->device) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_open: no device");
+  if (int rc = btf_init(D->device)) return rc;
+  if (cudaStreamCreateWithFlags(&D->st, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(BTF_ERR_CUDA, "btf_decoder_open: stream");
+  void* g = nullptr;
+  BTF_TRY(btf_gguf_open(gguf_path, &g));
+  Binder b{*D, g};
+  const int rc = b.bind();
+  btf_gguf_close(g);
+  if (rc) return rc;
+  BTF_TRY(finish_open(*D));
+  *handle = D.release();
+  return BTF_OK;
+}
+
+int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, void** handle) {
+  if (!dims || !handle) return fail(BTF_ERR_ARG, "btf_decoder_synthetic: null argument");
+  *handle = nullptr;
+  auto D = std::make_unique<Decoder>();
+  Decoder& R = *D;
+  R.o = defaults(opts);
+  R.d = *dims;
+  const btf_decoder_dims& d = R.d;
+  if (d.n_layer <= 0 || d.n_head_kv <= 0 || d.n_head % d.n_head_kv || d.n_group <= 0 || d.dt_rank % d.n_group ||
+      d.n_rot > d.head_dim || d.n_rot % 2 || d.n_vocab <= 0)
+    return fail(BTF_ERR_ARG, "btf_decoder_synthetic: inconsistent dims");
+  if (d.hadamard_block < 0 || (d.hadamard_block & (d.hadamard_block - 1)) || d.hadamard_block > 1024)
+    return fail(BTF_ERR_ARG, "btf_decoder_synthetic: hadamard_block 0 or a power of two <= 1024");
+  if (cudaGetDevice(&R.device) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: no device");
+  if (int rc = btf_init(R.device)) return rc;
+  if (cudaStreamCreateWithFlags(&R.st, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: stream");
+  if (R.d.d_inner == 0) R.d.d_inner = d.dt_rank * d.d_state;
+  if (d.d_inner % d.dt_rank) return fail(BTF_ERR_ARG, "btf_decoder_synthetic: d_inner %% dt_rank");
+  R.DK = d.d_state;
+  R.NK = d.n_group;
+  R.NV = d.dt_rank;
+  R.DV = d.d_inner / d.dt_rank;
+  R.DI = d.d_inner;
+  R.QK = d.d_state * d.n_group;
+  R.C = 2 * R.QK + R.DI;
+  BTF_TRY(check_dims(R));
+  if (d.hadamard_block && (d.n_embd % d.hadamard_block || d.n_ff % d.hadamard_block || R.DI % d.hadamard_block ||
+                           (d.n_head * d.head_dim) % d.hadamard_block))
+    return fail(BTF_ERR_ARG, "btf_decoder_synthetic: matmul widths must be multiples of hadamard_block");
+  int rc = BTF_OK;
+  uint64_t s = seed * 1000003ull;
+  const int blk = d.hadamard_block;
+  auto mat = [&](Mat* m, int N, int K, bool ssm_out) -> int {
+    m->N = N;
+    m->K = K;
+    m->pan = R.alloc<uint8_t>(btf_panel_bytes(N, K), &rc);
+    if (rc) return rc;
+    R.weight_bytes += btf_panel_bytes(N, K);
+    if (blk) {
+      m->hx.block = blk;
+      if (ssm_out) {
+        m->hx.perm_hd = K / R.NV;
+        m->hx.perm_nk = R.NK;
+        m->hx.perm_rep = R.NV / R.NK;
+      }
+    }
+    const cudaError_t e = launch_fill_panels(m->pan, N, K, ++s, 1.0f / std::sqrt((float)K), R.st);
+    return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_synthetic: fill");
+  };
+  auto vec = [&](float** p, int64_t n, float base, float spread) -> int {
+    *p = R.alloc<float>(n, &rc);
+    if (rc) return rc;
+    R.weight_bytes += n * 4;
+    const cudaError_t e = launch_fill_uniform(*p, n, ++s, base, spread, R.st);
+    return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_synthetic: fill");
+  };
+  const int E = d.n_embd, F = d.n_ff, H = d.n_head, HK = d.n_head_kv, HD = d.head_dim;
+  BTF_TRY(mat(&R.embd, d.n_vocab, E, false));
+  R.embd.hx = btf_hx{0, 0, 0, 0, nullptr};
+  R.weight_bytes -= btf_panel_bytes(d.n_vocab, E);
+  R.weight_bytes += (uint64_t)E / 4 + (uint64_t)E / 64;
+  R.inv_block = blk;
+  BTF_TRY(vec(&R.out_norm, E, 1.0f, 0.3f));
+  BTF_TRY(mat(&R.output, d.n_vocab, E, false));
+  R.L.resize(d.n_layer);
+  for (int il = 0; il < d.n_layer; ++il) {
+    Layer& l = R.L[il];
+    l.rec = ((il + 1) % 4) != 0;
+    BTF_TRY(vec(&l.attn_norm, E, 1.0f, 0.3f));
+    BTF_TRY(vec(&l.post_norm, E, 0.8f, 0.3f));
+    BTF_TRY(mat(&l.gate, F, E, false));
+    BTF_TRY(mat(&l.up, F, E, false));
+    BTF_TRY(mat(&l.down, E, F, false));
+    if (l.rec) {
+      BTF_TRY(mat(&l.qkv, R.C, E, false));
+      BTF_TRY(mat(&l.zg, R.DI, E, false));
+      BTF_TRY(vec(&l.alpha_w, (int64_t)R.NV * E, 0.f, 1.0f / std::sqrt((float)E)));
+      BTF_TRY(vec(&l.beta_w, (int64_t)R.NV * E, 0.f, 1.0f / std::sqrt((float)E)));
+      BTF_TRY(vec(&l.ssm_a, R.NV, -0.1f, 0.09f));
+      BTF_TRY(vec(&l.ssm_dt, R.NV, 0.f, 4.0f));
+      BTF_TRY(vec(&l.conv_w, (int64_t)d.conv_kernel * R.C, 0.f, 0.6f));
+      BTF_TRY(vec(&l.ssm_norm, R.DV, 0.85f, 0.3f));
+      BTF_TRY(mat(&l.out, E, R.DI, true));
+    } else {
+      BTF_TRY(mat(&l.wq, 2 * H * HD, E, false));
+      BTF_TRY(mat(&l.wk, HK * HD, E, false));
+      BTF_TRY(mat(&l.wv, HK * HD, E, false));
+      BTF_TRY(mat(&l.wo, E, H * HD, false));
+      BTF_TRY(vec(&l.q_norm, HD, 1.2f, 0.3f));
+      BTF_TRY(vec(&l.k_norm, HD, 1.2f, 0.3f));
+    }
+  }
+  if (cudaStreamSynchronize(R.st) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: fill");
+  BTF_TRY(finish_open(R));
+  *handle = D.release();
+  return BTF_OK;
+}
+
+int btf_decoder_step(void* handle, int32_t token, float* logits, int32_t* next) {
+  if (!handle) return fail(BTF_ERR_ARG, "btf_decoder_step: null handle");
+  Decoder& D = *static_cast<Decoder*>(handle);
+  if (token < 0 || token >= D.d.n_vocab) return fail(BTF_ERR_ARG, "btf_decoder_step: token %d out of range", token);
+  D.h_io[0] = token;
+  cudaError_t e = cudaMemcpyAsync(D.d_tok, D.h_io, sizeof(int32_t), cudaMemcpyHostToDevice, D.st);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_step: token");
+  BTF_TRY(run_step(D));
+  e = cudaMemcpyAsync(D.h_io + 1, D.d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, D.st);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpyAsync(logits, D.logits, (size_t)D.d.n_vocab * sizeof(float), cudaMemcpyDeviceToHost, D.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(D.st);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_step");
+  if (next) *next = D.h_io[1];
+  return BTF_OK;
+}
+
+int btf_decoder_run(void* handle, int steps) {
+  if (!handle || steps < 0) return fail(BTF_ERR_ARG, "btf_decoder_run: bad argument");
+  Decoder& D = *static_cast<Decoder*>(handle);
+  for (int i = 0; i < steps; ++i) BTF_TRY(run_step(D));
+  return BTF_OK;
+}
+
+int btf_decoder_reset(void* handle) {
+  if (!handle) return fail(BTF_ERR_ARG, "btf_decoder_reset: null handle");
+  return reset_state(*static_cast<Decoder*>(handle));
+}
+
+int btf_decoder_close(void* handle) {
+  delete static_cast<Decoder*>(handle);
+  return BTF_OK;
+}
+
+int btf_decoder_get_info(void* handle, btf_decoder_info* out) {
+  if (!handle || !out) return fail(BTF_ERR_ARG, "btf_decoder_get_info: null argument");
+  const Decoder& D = *static_cast<const Decoder*>(handle);
+  out->dims = D.d;
+  out->pos = D.pos;
+  out->stream = D.st;
+  out->weight_bytes = D.weight_bytes;
+  out->state_bytes = D.state_bytes;
+  out->kv_bytes_per_token = D.kv_bytes_per_token;
+  out->logits = D.logits;
+  return BTF_OK;
+}
+
+}  // extern "C"

@@ -17,10 +17,12 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <map>
 #include <string>
 #include <vector>
 
 #include "btf_b200.h"
+#include "gguf_meta.h"
 
 namespace btf {
 int fail(int status, const char* fmt, ...);
@@ -42,6 +44,7 @@ struct Tensor {
 };
 
 struct File {
+  std::map<std::string, btf::gguf::Value> kv;
   int fd = -1;
   const uint8_t* map = nullptr;
   size_t size = 0;
@@ -96,42 +99,53 @@ size_t scalar_bytes(uint32_t t) {
   }
 }
 
-// Skips one metadata value; returns its integer value when it is an integer
-// scalar (for general.alignment), else -1.
-int64_t skip_value(Reader& r, uint32_t type, int depth = 0) {
-  if (type == 8) {  // string
-    r.str();
-    return -1;
+// Reads one scalar of metadata type t (u8, i8, u16, i16, u32, i32, f32, bool,
+// u64, i64, f64) into the integer or the float slot of v.
+void read_scalar(Reader& r, uint32_t t, int64_t& i, double& f) {
+  switch (t) {
+    case 0: i = r.get<uint8_t>(); break;
+    case 1: i = r.get<int8_t>(); break;
+    case 2: i = r.get<uint16_t>(); break;
+    case 3: i = r.get<int16_t>(); break;
+    case 4: i = r.get<uint32_t>(); break;
+    case 5: i = r.get<int32_t>(); break;
+    case 6: f = r.get<float>(); break;
+    case 7: i = r.get<uint8_t>() != 0; break;
+    case 10: i = (int64_t)r.get<uint64_t>(); break;
+    case 11: i = r.get<int64_t>(); break;
+    case 12: f = r.get<double>(); break;
+    default: r.ok = false;
   }
-  if (type == 9) {  // array
-    if (depth > 0) {
-      r.ok = false;  // nested arrays are not part of the format this reader accepts
-      return -1;
-    }
+  if (t != 6 && t != 12) f = (double)i;
+  else i = (int64_t)f;
+}
+
+// Reads one metadata value (scalars, strings and one level of arrays).
+btf::gguf::Value read_value(Reader& r, uint32_t type) {
+  btf::gguf::Value v;
+  v.type = type;
+  if (type == 8) {  // string
+    v.s = r.str();
+  } else if (type == 9) {  // array
     const uint32_t et = r.get<uint32_t>();
     const uint64_t count = r.get<uint64_t>();
-    const size_t eb = scalar_bytes(et);
+    v.elem_type = et;
     if (et == 8) {
-      for (uint64_t i = 0; i < count && r.ok; ++i) r.str();
-    } else if (eb) {
-      if (count > (r.n - r.pos) / eb) r.ok = false;
-      else r.skip(count * eb);
+      if (count > r.n - r.pos) r.ok = false;  // every string takes at least its 8-byte length
+      for (uint64_t i = 0; i < count && r.ok; ++i) v.as.push_back(r.str());
+    } else if (const size_t eb = scalar_bytes(et)) {
+      if (count > (r.n - r.pos) / eb) {
+        r.ok = false;
+      } else {
+        v.ai.resize(count);
+        v.af.resize(count);
+        for (uint64_t i = 0; i < count && r.ok; ++i) read_scalar(r, et, v.ai[i], v.af[i]);
+      }
     } else {
-      r.ok = false;
+      r.ok = false;  // nested arrays are not part of the format this reader accepts
     }
-    return -1;
-  }
-  const size_t b = scalar_bytes(type);
-  if (!b) {
-    r.ok = false;
-    return -1;
-  }
-  int64_t v = 0;
-  if (b == 4 && (type == 4 || type == 5)) v = type == 4 ? (int64_t)r.get<uint32_t>() : r.get<int32_t>();
-  else if (b == 8 && (type == 10 || type == 11)) v = type == 10 ? (int64_t)r.get<uint64_t>() : r.get<int64_t>();
-  else {
-    r.skip(b);
-    return -1;
+  } else {
+    read_scalar(r, type, v.i, v.f);
   }
   return v;
 }
@@ -157,8 +171,9 @@ int parse(File& f) {
   for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
     const std::string key = r.str();
     const uint32_t type = r.get<uint32_t>();
-    const int64_t v = skip_value(r, type);
-    if (r.ok && key == "general.alignment" && v > 0) f.alignment = (uint64_t)v;
+    btf::gguf::Value v = read_value(r, type);
+    if (r.ok && key == "general.alignment" && type != 8 && type != 9 && v.i > 0) f.alignment = (uint64_t)v.i;
+    if (r.ok) f.kv[key] = std::move(v);
   }
   f.tensors.resize(n_tensors);
   for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
@@ -190,6 +205,17 @@ int parse(File& f) {
 }
 
 }  // namespace
+
+namespace btf {
+namespace gguf {
+const Value* meta(const void* handle, const std::string& key) {
+  if (!handle) return nullptr;
+  const File& f = *static_cast<const File*>(handle);
+  const auto it = f.kv.find(key);
+  return it == f.kv.end() ? nullptr : &it->second;
+}
+}  // namespace gguf
+}  // namespace btf
 
 extern "C" {
 

@@ -253,6 +253,47 @@ int btf_gguf_tensor(const void* handle, int64_t index, btf_gguf_tensor_info* out
  * Returns after the panels are complete. */
 int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_t staging_bytes, void* stream);
 
+/* ---- batch-1 decode step of the qwen35 hybrid decoder (gated delta net + gated
+ * full attention) as one CUDA graph: the decode path the ternary GEMV serves.
+ * Replaces GpuDecoder / make_gpu_decoder (src/cuda/gpu_decoder.cu:401-486,
+ * include/btf/fast.hpp:71-101) for one token per step. The model comes from a
+ * qwen35 GGUF (PTQ1_0 matrices, prism Hadamard fold, ref/bonsai-decoder/src/
+ * model.cpp:68-205) or from seeded synthetic weights of a given geometry. */
+typedef struct btf_decoder_opts {
+  int n_ctx;       /* KV cache capacity in tokens (FastOptions::n_ctx) */
+  int round_q_f16; /* round q to fp16 before q.k (FastOptions::round_q_f16) */
+  int attn_splits; /* key ranges of the attention (FastOptions::attn_splits), 1..256 */
+  int cuda_graph;  /* capture one step as a graph and replay it (FastOptions::cuda_graph) */
+} btf_decoder_opts;  /* NULL options: {4096, 1, 16, 1} */
+
+typedef struct btf_decoder_dims { /* bd::HParams (ref/bonsai-decoder/include/bd/model.hpp:18-35) */
+  int n_layer, n_embd, n_ff, n_vocab, n_head, n_head_kv, head_dim, n_rot;
+  int d_state, n_group, dt_rank, d_inner, conv_kernel;
+  int hadamard_block; /* 0: no transform (synthetic) */
+  float rope_base, rms_eps;
+} btf_decoder_dims;
+
+typedef struct btf_decoder_info {
+  btf_decoder_dims dims;
+  int pos;                     /* tokens decoded since the last reset */
+  void* stream;                /* the decoder's CUDA stream */
+  uint64_t weight_bytes;       /* resident weights one step reads (one embedding row) */
+  uint64_t state_bytes;        /* recurrent state read + written per step */
+  uint64_t kv_bytes_per_token; /* KV cache bytes read per step per cached token */
+  const float* logits;         /* device [n_vocab] of the last step */
+} btf_decoder_info;
+
+int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void** handle);
+/* d_inner = 0: dt_rank * d_state. Every layer il with (il + 1) % 4 != 0 is recurrent. */
+int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, void** handle);
+/* One step for `token`: the greedy next token into *next; logits (host, n_vocab) when non-NULL. Synchronous. */
+int btf_decoder_step(void* handle, int32_t token, float* logits, int32_t* next);
+/* `steps` steps, each fed the previous step's greedy token on the device; asynchronous on the decoder's stream. */
+int btf_decoder_run(void* handle, int steps);
+int btf_decoder_reset(void* handle);
+int btf_decoder_close(void* handle);
+int btf_decoder_get_info(void* handle, btf_decoder_info* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -220,6 +220,12 @@ class Reference:
             "ref_matvec_raw": (None, [_vp, _vp, _i64, _i64, _vp, _vp]),
             "ref_rmsnorm": (None, [_vp, _vp, _i64, _f32, _vp]),
             "ref_hadamard_input": (None, [_i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
+            "ref_synth_write": (_i32, [ctypes.c_char_p, _i32, ctypes.c_uint64, _vp]),
+            "ref_emu_open": (_vp, [ctypes.c_char_p, _i32, _i32, _i32]),
+            "ref_emu_step": (_i32, [_vp, ctypes.c_int32, _vp]),
+            "ref_emu_reset": (None, [_vp]),
+            "ref_emu_close": (None, [_vp]),
+            "ref_emu_hparams": (None, [_vp, _vp]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -319,3 +325,52 @@ def panel_decode(panels: np.ndarray, N: int, K: int):
 
 
 Reference.rmsnorm, Reference.hadamard_input = _prep_methods("ref_")
+
+
+# bd::SynthOptions defaults (ref/bonsai-decoder/include/bd/synth.hpp:17-30), in
+# the order ref_synth_write takes them.
+SYNTH_DEFAULTS = dict(n_embd=128, n_ff=256, n_head=4, n_head_kv=2, head_dim=32, n_rot=16, d_state=32, n_group=2,
+                      dt_rank=4, hadamard_block=64, hadamard=1, explicit_signs=1, gdn_v_grouped=1, small_mat_type=30)
+
+
+def synth_model(ref: "Reference", path: str, n_layer: int = 8, seed: int = 1, **over) -> None:
+    """Writes the reference's synthetic qwen35 GGUF (bd::make_synth_qwen35)."""
+    import numpy as np
+
+    o = dict(SYNTH_DEFAULTS, **over)
+    geom = np.array([o[k] for k in SYNTH_DEFAULTS], dtype=np.int32)
+    if ref.L.ref_synth_write(path.encode(), n_layer, seed, geom.ctypes.data) != 0:
+        raise RuntimeError("ref_synth_write failed")
+
+
+class Emulator:
+    """The reference's CPU emulator of its CUDA decode step (btf::make_emu_decoder)."""
+
+    HP = ("n_layer", "n_embd", "n_ff", "n_vocab", "n_head", "n_head_kv", "head_dim", "n_rot", "d_state", "n_group",
+          "dt_rank", "d_inner", "conv_kernel")
+
+    def __init__(self, ref: "Reference", path: str, n_ctx: int = 64, round_q_f16: bool = True, threads: int = 8):
+        import numpy as np
+
+        self.ref = ref
+        self.h = ref.L.ref_emu_open(path.encode(), n_ctx, int(round_q_f16), threads)
+        if not self.h:
+            raise RuntimeError("ref_emu_open failed")
+        hp = np.zeros(13, dtype=np.int32)
+        ref.L.ref_emu_hparams(self.h, hp.ctypes.data)
+        self.hp = dict(zip(self.HP, (int(v) for v in hp)))
+
+    def step(self, token: int):
+        import numpy as np
+
+        lg = np.empty(self.hp["n_vocab"], dtype=np.float32)
+        nxt = self.ref.L.ref_emu_step(self.h, token, lg.ctypes.data)
+        return nxt, lg
+
+    def reset(self) -> None:
+        self.ref.L.ref_emu_reset(self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.ref.L.ref_emu_close(self.h)
+            self.h = None

@@ -21,6 +21,7 @@
 #include "bd/types.hpp"
 #include "btf/fast.hpp"
 #include "btf/packed.hpp"
+#include <memory>
 
 #define REF_API extern "C" __attribute__((visibility("default")))
 
@@ -146,4 +147,67 @@ REF_API int64_t ref_gguf_tensor_offset(const char* path, const char* name) {
   auto g = bd::Gguf::open(path);
   const bd::GgufTensor* t = g->tensor(name);
   return t ? (int64_t)(g->data_offset + t->offset) : -1;  // byte offset of the tensor data in the file
+}
+
+// ---------------------------------------------------------------- whole decoder
+// bd::make_synth_qwen35 (ref/bonsai-decoder/src/synth.cpp:50-177): writes the
+// reference's synthetic qwen35 GGUF (every layer type, prism Hadamard fold,
+// PTQ1_0 matrices, BF16 alpha/beta) to `path`. geom (may be null) overrides
+// {n_embd, n_ff, n_head, n_head_kv, head_dim, n_rot, d_state, n_group, dt_rank,
+// hadamard_block, hadamard, explicit_signs, gdn_v_grouped, small_mat_type}.
+#include "bd/synth.hpp"
+#include "bd/model.hpp"
+
+REF_API int ref_synth_write(const char* path, int n_layer, uint64_t seed, const int* geom) {
+  bd::SynthOptions o;
+  o.n_layer = n_layer;
+  o.seed = seed;
+  if (geom) {
+    o.n_embd = geom[0]; o.n_ff = geom[1]; o.n_head = geom[2]; o.n_head_kv = geom[3]; o.head_dim = geom[4];
+    o.n_rot = geom[5]; o.d_state = geom[6]; o.n_group = geom[7]; o.dt_rank = geom[8]; o.hadamard_block = geom[9];
+    o.hadamard = geom[10] != 0; o.explicit_signs = geom[11] != 0; o.gdn_v_grouped = geom[12] != 0;
+    o.small_mat_type = (uint32_t)geom[13];
+  }
+  const std::vector<uint8_t> img = bd::make_synth_qwen35(o);
+  FILE* f = std::fopen(path, "wb");
+  if (!f) return 1;
+  const size_t wr = std::fwrite(img.data(), 1, img.size(), f);
+  std::fclose(f);
+  return wr == img.size() ? 0 : 2;
+}
+
+// btf::make_emu_decoder (src/emu_decoder.cpp:377-379): the reference's CPU
+// emulator of its CUDA decode step, over a model file.
+struct RefEmu {
+  std::unique_ptr<bd::Model> model;
+  std::unique_ptr<btf::FastDecoder> dec;
+};
+REF_API void* ref_emu_open(const char* path, int n_ctx, int round_q_f16, int threads) {
+  try {
+    auto* e = new RefEmu;
+    e->model = bd::Model::load(path);
+    btf::FastOptions o;
+    o.n_ctx = n_ctx;
+    o.round_q_f16 = round_q_f16 != 0;
+    o.threads = threads;
+    o.max_batch = 1;
+    e->dec = btf::make_emu_decoder(*e->model, o);
+    return e;
+  } catch (const std::exception& ex) {
+    std::fprintf(stderr, "ref_emu_open: %s\n", ex.what());
+    return nullptr;
+  }
+}
+// One decode step: returns the greedy next token; logits (n_vocab floats) may be null.
+REF_API int ref_emu_step(void* h, int32_t token, float* logits) {
+  return static_cast<RefEmu*>(h)->dec->step(token, logits);
+}
+REF_API void ref_emu_reset(void* h) { static_cast<RefEmu*>(h)->dec->reset(); }
+REF_API void ref_emu_close(void* h) { delete static_cast<RefEmu*>(h); }
+// {n_layer, n_embd, n_ff, n_vocab, n_head, n_head_kv, head_dim, n_rot, d_state, n_group, dt_rank, d_inner, conv_kernel}
+REF_API void ref_emu_hparams(void* h, int* out) {
+  const bd::HParams& p = static_cast<RefEmu*>(h)->model->hp;
+  const int v[13] = {p.n_layer, p.n_embd, p.n_ff, p.n_vocab, p.n_head, p.n_head_kv, p.head_dim,
+                     p.n_rot, p.d_state, p.n_group, p.dt_rank, p.d_inner, p.conv_kernel};
+  std::memcpy(out, v, sizeof v);
 }

@@ -1,0 +1,113 @@
+"""GPU parity of the batch-1 decode step (btf_decoder_*) against the reference's
+CPU emulator of its CUDA decode step, on the reference's synthetic models.
+
+Mirrors tests/test_gpu_decoder.cpp of the reference (the emulator half):
+for each synthetic configuration (tests/test_common.hpp:17-47) the prompt and
+24 greedy tokens run through both; per step the logits agree with the
+emulator's to rel-RMS <= 2e-2 (kAbsTol, :12), the greedy tokens agree on at
+least 23 of 24 steps, graph replay == eager launches bit-exact, and reset +
+the same prompt reproduces the last prompt token's prediction.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_rms
+
+pytestmark = pytest.mark.gpu
+
+PROMPT = [259, 272, 44, 32, 259, 261, 103, 97, 264]
+ABS_TOL = 2e-2
+
+CONFIGS = {
+    "default (block 64)": dict(),
+    "identity signs": dict(explicit_signs=0),
+    "no hadamard": dict(hadamard=0),
+    "gdn v tiled": dict(gdn_v_grouped=0),
+    "f32 alpha/beta": dict(small_mat_type=0),
+    "real head geometry": dict(n_layer=4, n_embd=1024, n_ff=2048, n_head=4, n_head_kv=1, head_dim=256, n_rot=64,
+                               d_state=128, n_group=2, dt_rank=8, hadamard_block=1024),
+}
+
+
+@pytest.mark.parametrize("label", list(CONFIGS))
+def test_decoder_matches_emulator(cuda, btf, ref, tmp_path, label):
+    cfg = dict(CONFIGS[label])
+    n_layer = cfg.pop("n_layer", 8)
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=n_layer, seed=1, **cfg)
+    emu = oracle.Emulator(ref, path, n_ctx=64)
+    gpu = btf.Decoder(path, n_ctx=64)
+    eager = btf.Decoder(path, n_ctx=64, cuda_graph=False)
+    info = gpu.info()
+    assert info["n_vocab"] == emu.hp["n_vocab"] and info["n_layer"] == n_layer
+    worst, steps, same = 0.0, 0, 0
+    last_prompt = None
+
+    def run(t):
+        nonlocal worst, steps
+        ne, le = emu.step(t)
+        ng, lg = gpu.step(t, logits=True)
+        nx, lx = eager.step(t, logits=True)
+        assert np.all(np.isfinite(lg))
+        worst = max(worst, rel_rms(lg, le))
+        assert np.array_equal(lg, lx), "graph replay != eager launches"
+        assert ng == nx == int(np.argmax(lg))
+        steps += 1
+        return ne, ng, lg
+
+    for t in PROMPT:
+        ne, ng, last_prompt = run(t)
+    t = ne
+    for _ in range(24):
+        ne, ng, _ = run(t)
+        same += ne == ng
+        t = ne
+    assert worst <= ABS_TOL, (label, worst)
+    assert same >= 23, (label, same)
+    assert gpu.info()["pos"] == steps
+    gpu.reset()
+    assert gpu.info()["pos"] == 0
+    for t in PROMPT:
+        nxt, _ = gpu.step(t)
+    assert nxt == int(np.argmax(last_prompt))
+    assert btf.device_error() == 0
+    gpu.close()
+    eager.close()
+    emu.close()
+
+
+def test_decoder_rejects_bad_tokens_and_full_context(cuda, btf, ref, tmp_path):
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=4, seed=2)
+    with btf.Decoder(path, n_ctx=3) as dec:
+        with pytest.raises(RuntimeError):
+            dec.step(dec.info()["n_vocab"])
+        for _ in range(3):
+            dec.step(1)
+        with pytest.raises(RuntimeError):
+            dec.step(1)  # context full
+        dec.reset()
+        dec.step(1)
+
+
+def test_synthetic_decoder_graph_equals_eager(cuda, btf):
+    dims = dict(n_layer=4, n_embd=512, n_ff=1024, n_vocab=1000, n_head=4, n_head_kv=2, head_dim=128, n_rot=64,
+                d_state=64, n_group=2, dt_rank=4, conv_kernel=4, hadamard_block=128, rope_base=1e7, rms_eps=1e-6)
+    a = btf.Decoder(dims=dims, seed=5, n_ctx=32)
+    b = btf.Decoder(dims=dims, seed=5, n_ctx=32, cuda_graph=False)
+    t = 7
+    for _ in range(6):
+        na, la = a.step(t, logits=True)
+        nb, lb = b.step(t, logits=True)
+        assert np.all(np.isfinite(la)) and np.array_equal(la, lb) and na == nb
+        t = na
+    # device-side loop: the greedy token feeds the next step without the host
+    a.reset()
+    a.run(5)
+    import torch
+
+    torch.cuda.synchronize()
+    assert a.info()["pos"] == 5 and btf.device_error() == 0
+    a.close()
+    b.close()
