@@ -430,6 +430,7 @@ def gpu_arm(args):
         }
         if world == 1:
             line["prefill_gemm_config2"] = prefill_gemm(btf, torch, dev)
+            line["decode_config3"] = decode_config3(btf, torch, dev)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(host_threads())
         print(json.dumps(line), flush=True)
@@ -443,6 +444,65 @@ def gpu_arm(args):
 
 
 PREFILL_SHAPES = ((64, 5120, 17408), (512, 5120, 17408), (64, 17408, 5120), (512, 17408, 5120))
+
+# Benchmark configuration 3: the 64-layer hybrid decoder (hidden 5120, FFN 17408,
+# vocab 248320; 3 of 4 layers gated delta net, every 4th full GQA attention over
+# a 4096-token fp16 KV cache), with the real model's per-head geometry (24 q / 4
+# kv heads of 256, RoPE on 64 dims; delta net 16 k-heads / 48 v-heads of 128,
+# inner 6144, conv 4) and Hadamard block 1024. Seeded random weights.
+CONFIG3 = dict(n_layer=64, n_embd=5120, n_ff=17408, n_vocab=248320, n_head=24, n_head_kv=4, head_dim=256, n_rot=64,
+               d_state=128, n_group=16, dt_rank=48, d_inner=6144, conv_kernel=4, hadamard_block=1024,
+               rope_base=1e7, rms_eps=1e-6)
+
+
+def decode_config3(btf, torch, dev, steps=64, warmup=8, n_ctx=4096):
+    """Benchmark configuration 3: batch-1 decode steps of the synthetic 64-layer
+    decoder as one CUDA graph per token (btf_decoder_*). `value`: tokens/s of a
+    device-side greedy loop (each step feeds its argmax to the next), CUDA events
+    on the decoder's stream; `e2e`: the synchronous step API (token from the host,
+    next token back). Roofline: bytes one token reads (resident weights, one
+    embedding row, recurrent state read + written, K/V of the cached tokens)."""
+    dec = btf.Decoder(dims=CONFIG3, seed=3, n_ctx=n_ctx)
+    info = dec.info()
+    st = torch.cuda.ExternalStream(info["stream"], device=dev)
+    nxt, _ = dec.step(1)  # captures the graph
+    dec.run(warmup)
+    torch.cuda.synchronize()
+    p0 = dec.info()["pos"]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    dec.run(steps)
+    b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    ne2e = 16
+    nxt = 1
+    a.record(st)
+    for _ in range(ne2e):
+        nxt, _ = dec.step(nxt)
+    b.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = a.elapsed_time(b) / ne2e
+    err = btf.device_error()
+    ctx_mean = p0 + (steps + 1) / 2.0  # cached tokens the timed steps read on average
+    per_tok = info["weight_bytes"] + info["state_bytes"] + info["kv_bytes_per_token"] * ctx_mean
+    gbs = per_tok / (ms * 1e-3) / 1e9
+    peak, peak_src = measured_peaks()
+    n_gdn = sum(1 for il in range(CONFIG3["n_layer"]) if (il + 1) % 4)
+    out = {"metric": "decode tokens/s, batch 1 (config 3)", "value": 1e3 / ms, "unit": "tok/s", "ms_per_token": ms,
+           "steps": steps, "warmup": warmup + 1, "context_start": p0, "n_ctx": n_ctx,
+           "config": dict(CONFIG3), "data": "synthetic (seeded ternary panels, uniform vectors)",
+           "bytes_per_token": per_tok, "weight_bytes": info["weight_bytes"], "state_bytes": info["state_bytes"],
+           "kv_bytes_per_cached_token": info["kv_bytes_per_token"],
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                        "peak_source": peak_src},
+           "e2e": {"value": 1e3 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+           # per token: 11 launches per layer (prep + GEMV x 4, and the mixer's 3), embed, final prep,
+           # lm_head, 2 argmax stages
+           "gpu_launches_per_token": 11 * CONFIG3["n_layer"] + 5, "n_gdn_layers": n_gdn,
+           "device_error_word": err, "path": "btf_decoder_run: one graph replay per token"}
+    dec.close()
+    return out
 
 
 def prefill_gemm(btf, torch, dev, reps=10):

@@ -5,16 +5,17 @@
 // decode step (src/emu_decoder.cpp of bonsai-ternary-fast), which is the
 // oracle the decoder is tested against:
 //   embed_kernel      packed token_embd row -> inverse transform   (:175-183)
-//   ab_gates_kernel   alpha / beta dots, softplus, sigmoid          (:235-249)
-//   conv_silu_kernel  causal conv (K taps) + SiLU, state shift      (:251-264)
-//   gdn_kernel        gated delta rule + gated RMSNorm per v-head   (:266-298)
+//   gdn_mix_kernel    per v-head: alpha / beta dots, causal conv +
+//                     SiLU, gated delta rule, gated RMSNorm         (:235-298)
 //   attn_prep_kernel  q/k RMSNorm, partial RoPE, fp16 KV write      (:307-338)
 //   attn_split_kernel / attn_combine_kernel
 //                     softmax attention over the fp16 KV cache in
 //                     key splits, then the sigmoid gate             (:339-372)
 //   argmax kernels    greedy token, lowest index on ties            (:214-217)
 // The decode position lives in device memory, so one captured graph serves
-// every token.
+// every token. Every kernel is launched with programmatic dependent launch:
+// it may start while the previous kernel drains and reads that kernel's
+// outputs only after griddepcontrol.wait.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -65,6 +66,8 @@ __device__ __forceinline__ float rms_scale(double sumsq, int n, float eps) {
 __global__ void embed_kernel(const uint8_t* __restrict__ pan, int V, int E, int S, const int32_t* __restrict__ tok,
                              int blk, const float* __restrict__ signs, float* __restrict__ x) {
   extern __shared__ float sh[];
+  pdl_launch_dependents();
+  pdl_wait();  // the token is written by the previous step's argmax
   const int n = blk ? blk : blockDim.x;
   const int e = blockIdx.x * n + threadIdx.x;
   const int r = min(max(*tok, 0), V - 1);  // the host validates tokens; the clamp keeps reads in bounds
@@ -107,84 +110,107 @@ __global__ void embed_kernel(const uint8_t* __restrict__ pan, int V, int E, int 
   }
 }
 
-// ------------------------------------------------------------------ alpha / beta
-// CTA per v-head h: beta[h] = sigmoid(bw[h] . x), g[h] = softplus(aw[h] . x + dt[h]) * a[h],
-// x = xn rounded to bf16 when the alpha/beta weights are bf16.
-__global__ void ab_gates_kernel(const float* __restrict__ xn, int E, const float* __restrict__ aw,
-                                const float* __restrict__ bw, const float* __restrict__ dt,
-                                const float* __restrict__ a, int bf16_in, float* __restrict__ beta,
-                                float* __restrict__ g) {
+// ------------------------------------------------------------------ delta-net mixer
+// One CTA per v-head h (kTpc threads per state column): the whole recurrent
+// mixer of one head after the qkv / z GEMV.
+//   alpha / beta (emulator :235-249): beta = sigmoid(bw[h] . x),
+//     g = softplus(aw[h] . x + dt[h]) * a[h], x = xn rounded to bf16 when the
+//     weights are bf16;
+//   causal conv + SiLU (:251-264) of the head's channels: q and k rows of
+//     k-head kh = h % NK and the head's v row. The conv state is a ring of K
+//     input rows indexed by position: tap i reads the input of position
+//     pos - (K-1) + i; the step writes only slot pos % K, which no tap of this
+//     step reads, so heads sharing a k-head read and write it without a race
+//     (they write the same values);
+//   gated delta rule (:266-290) on the l2-normalised q, k, then RMSNorm with
+//     ssm_norm and * silu(z) (:291-298).
+constexpr int kTpc = 4;
+struct GdnParams {
+  const float *xn, *aw, *bw, *dt, *a;
+  int E, bf16_in;
+  const float* qkv;   // [C] GEMV output (conv input)
+  float* ring;        // [K][C]
+  const float* conv_w;  // [C][K]
+  int K, C;
+  const float* z;     // [DI]
+  float* state;       // [NV][DV][DK]
+  const float* norm_w;
+  int NK, DK, DV, QK;
+  float eps;
+  const int32_t* pos;
+  float* o;           // [DI]
+};
+__global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
+  extern __shared__ float sm[];  // q[DK], k[DK], v[DV], out[DV]
   __shared__ double red[32];
-  const int h = blockIdx.x;
+  float* q = sm;
+  float* k = sm + p.DK;
+  float* vv = sm + 2 * p.DK;
+  float* ov = sm + 2 * p.DK + p.DV;
+  const int h = blockIdx.x, kh = h % p.NK, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // xn, qkv, z and the ring come from earlier kernels
+  // alpha / beta dots
   double sa = 0.0, sb = 0.0;
-  for (int i = threadIdx.x; i < E; i += blockDim.x) {
-    const float xv = bf16_in ? round_bf16(xn[i]) : xn[i];
-    sa += (double)__fmul_rn(aw[(int64_t)h * E + i], xv);
-    sb += (double)__fmul_rn(bw[(int64_t)h * E + i], xv);
+  {  // 16-byte loads, unrolled: the rows are read with a few latencies (E % 4 == 0, rows 16-byte aligned)
+    const float4* x4 = reinterpret_cast<const float4*>(p.xn);
+    const float4* a4 = reinterpret_cast<const float4*>(p.aw + (int64_t)h * p.E);
+    const float4* b4 = reinterpret_cast<const float4*>(p.bw + (int64_t)h * p.E);
+#pragma unroll 4
+    for (int i = tid; i < (p.E >> 2); i += blockDim.x) {
+      float4 xv = x4[i];
+      if (p.bf16_in) xv = make_float4(round_bf16(xv.x), round_bf16(xv.y), round_bf16(xv.z), round_bf16(xv.w));
+      const float4 av = a4[i], bv = b4[i];
+      sa += (double)__fmul_rn(av.x, xv.x) + (double)__fmul_rn(av.y, xv.y) + (double)__fmul_rn(av.z, xv.z) +
+            (double)__fmul_rn(av.w, xv.w);
+      sb += (double)__fmul_rn(bv.x, xv.x) + (double)__fmul_rn(bv.y, xv.y) + (double)__fmul_rn(bv.z, xv.z) +
+            (double)__fmul_rn(bv.w, xv.w);
+    }
   }
   sa = block_sum(sa, red);
   sb = block_sum(sb, red);
-  if (threadIdx.x == 0) {
-    beta[h] = sigmoidf_((float)sb);
-    g[h] = __fmul_rn(softplus(__fadd_rn((float)sa, dt[h])), a[h]);
+  const float bt = sigmoidf_((float)sb);
+  const float decay = expf(__fmul_rn(softplus(__fadd_rn((float)sa, p.dt[h])), p.a[h]));
+  // conv + silu of the head's channels
+  const int pos = *p.pos, nch = 2 * p.DK + p.DV;
+  for (int idx = tid; idx < nch; idx += blockDim.x) {
+    const int c = idx < p.DK ? kh * p.DK + idx
+                             : idx < 2 * p.DK ? p.QK + kh * p.DK + (idx - p.DK) : 2 * p.QK + h * p.DV + (idx - 2 * p.DK);
+    float sum = 0.f;
+    for (int i = 0; i < p.K - 1; ++i) {
+      const int slot = ((pos - (p.K - 1) + i) % p.K + p.K) % p.K;
+      sum = __fadd_rn(sum, __fmul_rn(p.ring[(int64_t)slot * p.C + c], p.conv_w[(int64_t)c * p.K + i]));
+    }
+    const float xin = p.qkv[c];
+    sum = __fadd_rn(sum, __fmul_rn(xin, p.conv_w[(int64_t)c * p.K + p.K - 1]));
+    p.ring[(int64_t)(pos % p.K) * p.C + c] = xin;
+    sm[idx] = silu(sum);  // q | k | v
   }
-}
-
-// ------------------------------------------------------------------ conv + silu
-// Channel c: s = sum_{i<K-1} state[i][c] w[c][i] + x[c] w[c][K-1] (that order),
-// out = silu(s); the state shifts by one and takes x[c].
-__global__ void conv_silu_kernel(const float* __restrict__ x, float* __restrict__ state, const float* __restrict__ w,
-                                 int C, int K, float* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
-  float s = 0.f;
-  for (int i = 0; i < K - 1; ++i) s = __fadd_rn(s, __fmul_rn(state[(int64_t)i * C + c], w[(int64_t)c * K + i]));
-  const float xin = x[c];
-  s = __fadd_rn(s, __fmul_rn(xin, w[(int64_t)c * K + K - 1]));
-  for (int i = 0; i + 1 < K - 1; ++i) state[(int64_t)i * C + c] = state[(int64_t)(i + 1) * C + c];
-  state[(int64_t)(K - 2) * C + c] = xin;
-  out[c] = silu(s);
-}
-
-// ------------------------------------------------------------------ gated delta rule
-// CTA per v-head h, kTpc threads per state column j (DV columns of DK floats;
-// state[h][j][i], DK a multiple of 16 up to 128). q, k: l2-normalised rows kh = h % NK of the conv output.
-constexpr int kTpc = 4;
-__global__ void gdn_kernel(const float* __restrict__ cv, const float* __restrict__ z, const float* __restrict__ beta,
-                           const float* __restrict__ gg, float* __restrict__ state, const float* __restrict__ nw,
-                           int NK, int DK, int DV, int QK, float eps, float* __restrict__ o) {
-  extern __shared__ float sm[];  // q[DK], k[DK], out[DV]
-  __shared__ double red[32];
-  float* q = sm;
-  float* k = sm + DK;
-  float* ov = sm + 2 * DK;
-  const int h = blockIdx.x, kh = h % NK, tid = threadIdx.x;
-  // bd::l2norm (cpu_ops.cpp:124-129): x / max(sqrt(sum x^2), eps), sum in double
-  const float* qs = cv + (int64_t)kh * DK;
-  const float* ks = cv + QK + (int64_t)kh * DK;
+  __syncthreads();
+  // bd::l2norm (cpu_ops.cpp:124-129) of q and k: x / max(sqrt(sum x^2), eps), sum in double
   double sq = 0.0, sk = 0.0;
-  for (int i = tid; i < DK; i += blockDim.x) {
-    sq += (double)qs[i] * qs[i];
-    sk += (double)ks[i] * ks[i];
+  for (int i = tid; i < p.DK; i += blockDim.x) {
+    sq += (double)q[i] * q[i];
+    sk += (double)k[i] * k[i];
   }
   sq = block_sum(sq, red);
   sk = block_sum(sk, red);
-  const float iq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), eps));
-  const float ik = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), eps));
-  for (int i = tid; i < DK; i += blockDim.x) {
-    q[i] = __fmul_rn(qs[i], iq);
-    k[i] = __fmul_rn(ks[i], ik);
+  const float iq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), p.eps));
+  const float ik = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), p.eps));
+  __syncthreads();
+  for (int i = tid; i < p.DK; i += blockDim.x) {
+    q[i] = __fmul_rn(q[i], iq);
+    k[i] = __fmul_rn(k[i], ik);
   }
   __syncthreads();
-  const float decay = expf(gg[h]), bt = beta[h];
-  const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)DK));
+  const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)p.DK));
   // thread (j, part) holds floats i = 16 t + 4 part + {0..3} of column j (DK <= 128)
   const int j = tid / kTpc, part = tid % kTpc;
-  const int nt = DK / (4 * kTpc);
-  float4* col = reinterpret_cast<float4*>(state + ((int64_t)h * DV + j) * DK) + part;
+  const int nt = p.DK / (4 * kTpc);
+  float4* col = reinterpret_cast<float4*>(p.state + ((int64_t)h * p.DV + j) * p.DK) + part;
   const float4* k4 = reinterpret_cast<const float4*>(k) + part;
   const float4* q4 = reinterpret_cast<const float4*>(q) + part;
-  const float vj = cv[2 * QK + (int64_t)h * DV + j];
+  const float vj = vv[j];
   float4 st[8];
   float kv = 0.f;
 #pragma unroll
@@ -220,17 +246,16 @@ __global__ void gdn_kernel(const float* __restrict__ cv, const float* __restrict
   }
 #pragma unroll
   for (int off = 1; off < kTpc; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  const float oj = __fmul_rn(acc, qscale);
-  if (part == 0) ov[j] = oj;
+  if (part == 0) ov[j] = __fmul_rn(acc, qscale);
   __syncthreads();
   // bd::rmsnorm over the head's DV outputs with ssm_norm, then * silu(z)
   double ss = 0.0;
-  for (int i = tid; i < DV; i += blockDim.x) ss += (double)ov[i] * ov[i];
+  for (int i = tid; i < p.DV; i += blockDim.x) ss += (double)ov[i] * ov[i];
   ss = block_sum(ss, red);
-  const float sc = rms_scale(ss, DV, eps);
-  for (int i = tid; i < DV; i += blockDim.x) {
-    const float y = __fmul_rn(__fmul_rn(ov[i], sc), nw[i]);
-    o[(int64_t)h * DV + i] = __fmul_rn(y, silu(z[(int64_t)h * DV + i]));
+  const float sc = rms_scale(ss, p.DV, p.eps);
+  for (int i = tid; i < p.DV; i += blockDim.x) {
+    const float y = __fmul_rn(__fmul_rn(ov[i], sc), p.norm_w[i]);
+    p.o[(int64_t)h * p.DV + i] = __fmul_rn(y, silu(p.z[(int64_t)h * p.DV + i]));
   }
 }
 
@@ -247,6 +272,8 @@ __global__ void attn_prep_kernel(const float* __restrict__ qf, const float* __re
                                  __half* __restrict__ kc, __half* __restrict__ vc) {
   extern __shared__ float hv[];
   __shared__ double red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x, i = threadIdx.x;
   const bool isq = b < H;
   const int hh = isq ? b : b - H;
@@ -287,6 +314,8 @@ __global__ void attn_split_kernel(const float* __restrict__ q, const __half* __r
                                   const __half* __restrict__ vc, int H, int HK, int D, int chunk, float scale,
                                   const int32_t* __restrict__ pos_p, float* __restrict__ part) {
   extern __shared__ float sm[];  // q[D], then per warp: m, l, acc[D]
+  pdl_launch_dependents();
+  pdl_wait();
   const int h = blockIdx.x, sp = blockIdx.y, lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int g = h / (H / HK), T = *pos_p + 1;
   const int t0 = sp * chunk, t1 = min(t0 + chunk, T);
@@ -345,6 +374,8 @@ __global__ void attn_split_kernel(const float* __restrict__ q, const __half* __r
 // CTA per head: o = (sum_s acc_s e^{m_s - M}) / (sum_s l_s e^{m_s - M}) * sigmoid(gate).
 __global__ void attn_combine_kernel(const float* __restrict__ part, int splits, int D, const float* __restrict__ qf,
                                     float* __restrict__ o) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int h = blockIdx.x;
   const float* ph = part + (int64_t)h * splits * (D + 2);
   float M = -INFINITY;
@@ -380,6 +411,8 @@ __device__ __forceinline__ void better(float& v, int& i, float v2, int i2) {
 __global__ void argmax1_kernel(const float* __restrict__ x, int n, float* __restrict__ pv, int* __restrict__ pi) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int per = (n + gridDim.x - 1) / gridDim.x, b0 = blockIdx.x * per, b1 = min(n, b0 + per);
   float v = -INFINITY;
   int idx = -1;
@@ -401,6 +434,8 @@ __global__ void argmax1_kernel(const float* __restrict__ x, int n, float* __rest
 // position (pos += 1) when those pointers are given.
 __global__ void argmax2_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int parts,
                                int32_t* __restrict__ out, int32_t* __restrict__ tok_next, int32_t* __restrict__ pos) {
+  pdl_launch_dependents();
+  pdl_wait();
   float v = -INFINITY;
   int idx = -1;
   for (int i = threadIdx.x; i < parts; i += 32) better(v, idx, pv[i], pi[i]);
@@ -479,51 +514,37 @@ __global__ void fill_uniform_kernel(float* __restrict__ x, int64_t n, uint64_t s
 cudaError_t launch_embed(const uint8_t* pan, int V, int E, const int32_t* tok, int blk, const float* signs, float* x,
                          cudaStream_t st) {
   const int n = blk ? blk : 256;
-  embed_kernel<<<(E + n - 1) / n, n, blk ? blk * sizeof(float) : 0, st>>>(pan, V, E, (int)slices_of(E), tok, blk,
-                                                                          signs, x);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3((E + n - 1) / n), dim3(n), blk ? blk * sizeof(float) : 0, st, pan, V, E,
+                    (int)slices_of(E), tok, blk, signs, x);
 }
-cudaError_t launch_ab_gates(const float* xn, int E, const float* aw, const float* bw, const float* dt, const float* a,
-                            int bf16_in, int NV, float* beta, float* g, cudaStream_t st) {
-  ab_gates_kernel<<<NV, 256, 0, st>>>(xn, E, aw, bw, dt, a, bf16_in, beta, g);
-  return cudaGetLastError();
-}
-cudaError_t launch_conv_silu(const float* x, float* state, const float* w, int C, int K, float* out, cudaStream_t st) {
-  conv_silu_kernel<<<(C + 255) / 256, 256, 0, st>>>(x, state, w, C, K, out);
-  return cudaGetLastError();
-}
-cudaError_t launch_gdn(const float* cv, const float* z, const float* beta, const float* g, float* state,
-                       const float* norm_w, int NV, int NK, int DK, int DV, int QK, float eps, float* o,
-                       cudaStream_t st) {
-  gdn_kernel<<<NV, DV * kTpc, (2 * DK + DV) * sizeof(float), st>>>(cv, z, beta, g, state, norm_w, NK, DK, DV, QK, eps,
-                                                                    o);
-  return cudaGetLastError();
+cudaError_t launch_gdn_mix(const GdnArgs& g, cudaStream_t st) {
+  const GdnParams p{g.xn, g.aw, g.bw, g.dt, g.a, g.E, g.bf16_in, g.qkv, g.ring, g.conv_w, g.K, g.C, g.z, g.state,
+                    g.norm_w, g.NK, g.DK, g.DV, g.QK, g.eps, g.pos, g.o};
+  return launch_pdl(gdn_mix_kernel, dim3(g.NV), dim3(g.DV * kTpc), (size_t)(2 * g.DK + 2 * g.DV) * sizeof(float), st,
+                    p);
 }
 cudaError_t launch_attn_prep(const float* qf, const float* k, const float* v, const float* qn, const float* kn, int H,
                              int HK, int D, int R, float theta_scale, float eps, const int32_t* pos, int round_q,
                              float* qout, void* kc, void* vc, cudaStream_t st) {
   const int threads = (D + 31) / 32 * 32;
-  attn_prep_kernel<<<H + HK, threads, D * sizeof(float), st>>>(qf, k, v, qn, kn, H, HK, D, R, theta_scale, eps, pos,
-                                                                round_q, qout, static_cast<__half*>(kc),
-                                                                static_cast<__half*>(vc));
-  return cudaGetLastError();
+  return launch_pdl(attn_prep_kernel, dim3(H + HK), dim3(threads), D * sizeof(float), st, qf, k, v, qn, kn, H, HK, D,
+                    R, theta_scale, eps, pos, round_q, qout, static_cast<__half*>(kc), static_cast<__half*>(vc));
 }
 cudaError_t launch_attention(const float* q, const void* kc, const void* vc, const float* qf, int H, int HK, int D,
                              int n_ctx, int splits, const int32_t* pos, float* part, float* o, cudaStream_t st) {
   const int chunk = (n_ctx + splits - 1) / splits;
   const float scale = 1.0f / sqrtf((float)D);
-  attn_split_kernel<<<dim3(H, splits), kAttnWarps * 32, (D + kAttnWarps * (D + 2)) * sizeof(float), st>>>(
-      q, static_cast<const __half*>(kc), static_cast<const __half*>(vc), H, HK, D, chunk, scale, pos, part);
-  if (cudaError_t e = cudaGetLastError()) return e;
-  attn_combine_kernel<<<H, 128, 0, st>>>(part, splits, D, qf, o);
-  return cudaGetLastError();
+  if (cudaError_t e = launch_pdl(attn_split_kernel, dim3(H, splits), dim3(kAttnWarps * 32),
+                                 (D + kAttnWarps * (D + 2)) * sizeof(float), st, q, static_cast<const __half*>(kc),
+                                 static_cast<const __half*>(vc), H, HK, D, chunk, scale, pos, part))
+    return e;
+  return launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, static_cast<const float*>(part), splits, D, qf, o);
 }
 cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, int32_t* out, int32_t* tok_next,
                           int32_t* pos, cudaStream_t st) {
-  argmax1_kernel<<<parts, 256, 0, st>>>(x, n, pv, pi);
-  if (cudaError_t e = cudaGetLastError()) return e;
-  argmax2_kernel<<<1, 32, 0, st>>>(pv, pi, parts, out, tok_next, pos);
-  return cudaGetLastError();
+  if (cudaError_t e = launch_pdl(argmax1_kernel, dim3(parts), dim3(256), 0, st, x, n, pv, pi)) return e;
+  return launch_pdl(argmax2_kernel, dim3(1), dim3(32), 0, st, static_cast<const float*>(pv),
+                    static_cast<const int*>(pi), parts, out, tok_next, pos);
 }
 cudaError_t launch_fill_panels(uint8_t* pan, int N, int K, uint64_t seed, float scale_mul, cudaStream_t st) {
   const int64_t np = groups_of(N) * slices_of(K);

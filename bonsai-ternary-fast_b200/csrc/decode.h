@@ -10,16 +10,26 @@ namespace btf {
 // x[E] = inverse transform of row *tok of a panel matrix [V][E] (blk = 0: none).
 cudaError_t launch_embed(const uint8_t* panels, int V, int E, const int32_t* tok, int blk, const float* signs,
                          float* x, cudaStream_t st);
-// beta[h] = sigmoid(bw[h] . x), g[h] = softplus(aw[h] . x + dt[h]) * a[h] for h < NV.
-cudaError_t launch_ab_gates(const float* xn, int E, const float* aw, const float* bw, const float* dt, const float* a,
-                            int bf16_in, int NV, float* beta, float* g, cudaStream_t st);
-// out[C] = silu(causal conv of x with the K-tap state); state [(K-1)][C] advances.
-cudaError_t launch_conv_silu(const float* x, float* state, const float* w, int C, int K, float* out, cudaStream_t st);
-// Gated delta rule of NV v-heads on the conv output cv, state [NV][DV][DK], then
-// RMSNorm(norm_w) * silu(z) -> o[NV * DV].
-cudaError_t launch_gdn(const float* cv, const float* z, const float* beta, const float* g, float* state,
-                       const float* norm_w, int NV, int NK, int DK, int DV, int QK, float eps, float* o,
-                       cudaStream_t st);
+// The recurrent mixer of NV v-heads (one kernel): alpha/beta gates from xn, the
+// causal conv (ring [K][C] indexed by *pos) + SiLU of qkv, the gated delta rule
+// on state [NV][DV][DK], RMSNorm(norm_w) * silu(z) -> o[NV * DV].
+struct GdnArgs {
+  const float *xn, *aw, *bw, *dt, *a;
+  int E, bf16_in;
+  const float* qkv;
+  float* ring;
+  const float* conv_w;
+  int K, C;
+  const float* z;
+  float* state;
+  const float* norm_w;
+  int NK, DK, DV, QK;
+  float eps;
+  const int32_t* pos;
+  float* o;
+  int NV;
+};
+cudaError_t launch_gdn_mix(const GdnArgs& args, cudaStream_t st);
 // q/k RMSNorm + RoPE at *pos; q -> qout[H*D] (fp16-rounded when round_q), k and v
 // -> fp16 caches [n_ctx][HK*D] row *pos.
 cudaError_t launch_attn_prep(const float* qf, const float* k, const float* v, const float* qn, const float* kn, int H,

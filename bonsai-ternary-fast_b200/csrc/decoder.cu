@@ -139,7 +139,7 @@ int make_buffers(Decoder& D) {
   D.d_next = D.d_tok + 2;
   for (Layer& l : D.L) {
     if (l.rec) {
-      l.conv_state = D.alloc<float>((size_t)(d.conv_kernel - 1) * D.C, &rc);
+      l.conv_state = D.alloc<float>((size_t)d.conv_kernel * D.C, &rc);  // ring of K input rows
       l.ssm_state = D.alloc<float>((size_t)D.NV * D.DV * D.DK, &rc);
       D.state_bytes += 2 * ((uint64_t)(d.conv_kernel - 1) * D.C + (uint64_t)D.NV * D.DV * D.DK) * 4;
     } else {
@@ -158,7 +158,7 @@ int reset_state(Decoder& D) {
   for (Layer& l : D.L) {
     if (l.rec) {
       if (e == cudaSuccess)
-        e = cudaMemsetAsync(l.conv_state, 0, (size_t)(D.d.conv_kernel - 1) * D.C * sizeof(float), D.st);
+        e = cudaMemsetAsync(l.conv_state, 0, (size_t)D.d.conv_kernel * D.C * sizeof(float), D.st);
       if (e == cudaSuccess) e = cudaMemsetAsync(l.ssm_state, 0, (size_t)D.NV * D.DV * D.DK * sizeof(float), D.st);
     }
   }
@@ -199,10 +199,10 @@ int enqueue_step(Decoder& D) {
       BTF_TRY(prep(D, D.x, E, l.attn_norm, l.qkv.hx, D.xn));
       BTF_TRY(gemv(D, {{l.qkv.pan, l.qkv.N, D.bA, l.qkv.N}, {l.zg.pan, l.zg.N, D.bB, l.zg.N}}, E,
                    BTF_STORE));
-      BTF_TRYC(launch_ab_gates(D.xn, E, l.alpha_w, l.beta_w, l.ssm_dt, l.ssm_a, l.ab_bf16, D.NV, D.beta, D.gg, D.st));
-      BTF_TRYC(launch_conv_silu(D.bA, l.conv_state, l.conv_w, D.C, d.conv_kernel, D.bC, D.st));
-      BTF_TRYC(launch_gdn(D.bC, D.bB, D.beta, D.gg, l.ssm_state, l.ssm_norm, D.NV, D.NK, D.DK, D.DV, D.QK, d.rms_eps,
-                          D.bO, D.st));
+      const GdnArgs ga{D.xn, l.alpha_w, l.beta_w, l.ssm_dt, l.ssm_a, E, l.ab_bf16, D.bA, l.conv_state, l.conv_w,
+                       d.conv_kernel, D.C, D.bB, l.ssm_state, l.ssm_norm, D.NK, D.DK, D.DV, D.QK, d.rms_eps, D.d_pos,
+                       D.bO, D.NV};
+      BTF_TRYC(launch_gdn_mix(ga, D.st));
       BTF_TRY(prep(D, D.bO, D.DI, nullptr, l.out.hx, nullptr));
       BTF_TRY(gemv(D, {{l.out.pan, E, D.x, E}}, D.DI, BTF_ADD));
     } else {

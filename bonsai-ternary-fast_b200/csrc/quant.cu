@@ -78,7 +78,19 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constan
   float scale = 1.0f;
   if constexpr (NORM) {
     double acc = 0.0;
-    for (int i = threadIdx.x; i < a.n; i += kPrepThreads) acc += (double)xr[i] * (double)xr[i];
+    if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0 && (a.n & 3) == 0) {
+      // 16-byte loads, several in flight per thread (the row is read with one latency, not n/256)
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
+#pragma unroll 4
+      for (int i = threadIdx.x; i < (a.n >> 2); i += kPrepThreads) {
+        const float4 v = x4[i];
+        acc += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
+               (double)v.w * (double)v.w;
+      }
+    } else {
+#pragma unroll 4
+      for (int i = threadIdx.x; i < a.n; i += kPrepThreads) acc += (double)xr[i] * (double)xr[i];
+    }
     acc = warp_sum_d(acc);
     if (lane == 0) red[warp] = acc;
     __syncthreads();
@@ -88,6 +100,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constan
     const float mean = (float)(tot / (double)a.n);
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
   }
+#pragma unroll 4
   for (int o = threadIdx.x; o < a.S; o += kPrepThreads) {
     const int og = base + o;
     int src = og;
