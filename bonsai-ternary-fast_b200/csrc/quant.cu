@@ -4,6 +4,8 @@
 //   id = amax != 0 ? 127 / amax : 0, q = round_half_even(x * id), s = sum(q).
 // IEEE division and multiplication only (no fast-math), as in the quantising
 // tail of the reference's prep_kernel (src/cuda/kernels.cu:185-201).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace btf {
@@ -44,7 +46,8 @@ __global__ void __launch_bounds__(kQThreads)
 // CTAs. Every butterfly computes (a + b, a - b) in the host's stage order, and
 // the norm scale and the products are correctly rounded, so only the order of
 // the double sum of squares differs from the host.
-constexpr int kPrepThreads = 256;
+constexpr int kPrepThreads = 256;      // fewest threads a CTA is launched with
+constexpr int kPrepMaxThreads = 1024;  // one thread per column of a 1024-wide span
 
 struct PrepParams {
   const float* x;
@@ -67,9 +70,10 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 }
 
 template <bool NORM>
-__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constant__ PrepParams a) {
+__global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_constant__ PrepParams a) {
   extern __shared__ float buf[];  // [S]
-  __shared__ double red[kPrepThreads / 32];
+  __shared__ double red[kPrepMaxThreads / 32];
+  const int nthr = blockDim.x, nwarp = nthr >> 5;
   const int m = blockIdx.y, base = blockIdx.x * a.S;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = a.x + (size_t)m * a.ldx;
@@ -82,26 +86,26 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constan
       // 16-byte loads, several in flight per thread (the row is read with one latency, not n/256)
       const float4* x4 = reinterpret_cast<const float4*>(xr);
 #pragma unroll 4
-      for (int i = threadIdx.x; i < (a.n >> 2); i += kPrepThreads) {
+      for (int i = threadIdx.x; i < (a.n >> 2); i += nthr) {
         const float4 v = x4[i];
         acc += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
                (double)v.w * (double)v.w;
       }
     } else {
 #pragma unroll 4
-      for (int i = threadIdx.x; i < a.n; i += kPrepThreads) acc += (double)xr[i] * (double)xr[i];
+      for (int i = threadIdx.x; i < a.n; i += nthr) acc += (double)xr[i] * (double)xr[i];
     }
     acc = warp_sum_d(acc);
     if (lane == 0) red[warp] = acc;
     __syncthreads();
     double tot = 0.0;
 #pragma unroll
-    for (int w = 0; w < kPrepThreads / 32; ++w) tot += red[w];
+    for (int w = 0; w < nwarp; ++w) tot += red[w];
     const float mean = (float)(tot / (double)a.n);
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
   }
 #pragma unroll 4
-  for (int o = threadIdx.x; o < a.S; o += kPrepThreads) {
+  for (int o = threadIdx.x; o < a.S; o += nthr) {
     const int og = base + o;
     int src = og;
     if (a.perm_rep > 1) {  // tiled [hd, nk, rep] -> grouped [hd, rep, nk]
@@ -124,7 +128,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constan
   if (a.block > 1) {
     // stages len = 1 .. 16 inside each warp's 32 consecutive values (shuffles)
     const int lim = min(a.block, 32);
-    for (int c = warp; c < a.S / 32; c += kPrepThreads / 32) {
+    for (int c = warp; c < a.S / 32; c += nwarp) {
       float v = buf[c * 32 + lane];
       for (int len = 1; len < lim; len <<= 1) {
         const float p = __shfl_xor_sync(0xffffffffu, v, len);
@@ -135,7 +139,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constan
     __syncthreads();
     // stages len = 32 .. block/2 in shared memory
     for (int len = 32; len < a.block; len <<= 1) {
-      for (int pidx = threadIdx.x; pidx < (a.S >> 1); pidx += kPrepThreads) {
+      for (int pidx = threadIdx.x; pidx < (a.S >> 1); pidx += nthr) {
         const int j = (pidx / len) * (len << 1) + (pidx % len);
         const float x0 = buf[j], x1 = buf[j + len];
         buf[j] = __fadd_rn(x0, x1);
@@ -145,7 +149,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __grid_constan
     }
     hs = __fdiv_rn(1.0f, __fsqrt_rn((float)a.block));
   }
-  for (int g = warp; g < a.S / 32; g += kPrepThreads / 32) {
+  for (int g = warp; g < a.S / 32; g += nwarp) {
     float v = buf[g * 32 + lane];
     if (a.block > 1) v = __fmul_rn(v, hs);
     float dq;
@@ -189,8 +193,9 @@ extern "C" int btf_prep(const float* x, int ldx, int M, int n, const float* norm
                act.q, act.d, act.s};
   const dim3 grid(n / S, M);
   const size_t smem = (size_t)S * sizeof(float);
-  const cudaError_t e = normw ? launch_pdl(prep_kernel<true>, grid, dim3(kPrepThreads), smem, (cudaStream_t)stream, p)
-                              : launch_pdl(prep_kernel<false>, grid, dim3(kPrepThreads), smem, (cudaStream_t)stream, p);
+  const int threads = std::max(kPrepThreads, S);  // S <= 1024: one thread per column of the span
+  const cudaError_t e = normw ? launch_pdl(prep_kernel<true>, grid, dim3(threads), smem, (cudaStream_t)stream, p)
+                              : launch_pdl(prep_kernel<false>, grid, dim3(threads), smem, (cudaStream_t)stream, p);
   return e == cudaSuccess ? launch_status("prep_kernel") : cuda_fail(e, "prep_kernel launch");
 }
 
