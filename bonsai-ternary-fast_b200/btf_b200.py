@@ -36,7 +36,8 @@ EXPORTS = (
     "btf_gather_epoch_advance", "btf_gather_wait", "btf_gather_barrier", "btf_prep",
     "btf_gguf_open", "btf_gguf_close", "btf_gguf_tensor_count", "btf_gguf_find", "btf_gguf_tensor",
     "btf_gguf_load_panels", "btf_decoder_open", "btf_decoder_synthetic", "btf_decoder_step", "btf_decoder_run",
-    "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info",
+    "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
+    "btf_decoder_arena", "btf_decoder_connect",
 )
 
 
@@ -159,6 +160,10 @@ def lib() -> ctypes.CDLL:
         "btf_decoder_reset": (i32, [vp]),
         "btf_decoder_close": (i32, [vp]),
         "btf_decoder_get_info": (i32, [vp, ctypes.POINTER(DecoderInfoC)]),
+        "btf_decoder_synthetic_tp": (i32, [ctypes.POINTER(DecoderDimsC), ctypes.c_uint64, ctypes.POINTER(DecoderOptsC),
+                                           i32, i32, ctypes.POINTER(vp)]),
+        "btf_decoder_arena": (i32, [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]),
+        "btf_decoder_connect": (i32, [vp, ctypes.POINTER(vp)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -473,7 +478,8 @@ class Decoder:
     rope_base / rms_eps)."""
 
     def __init__(self, path: Optional[str] = None, dims: Optional[dict] = None, seed: int = 1, n_ctx: int = 4096,
-                 round_q_f16: bool = True, attn_splits: int = 16, cuda_graph: bool = True, device: int = 0):
+                 round_q_f16: bool = True, attn_splits: int = 16, cuda_graph: bool = True, device: int = 0,
+                 world: int = 1, rank: int = 0):
         torch = _torch()
         torch.cuda.set_device(device)
         ensure_init(device)
@@ -484,20 +490,41 @@ class Decoder:
         else:
             d = DecoderDimsC(*[int(dims.get(f, 0)) for f in DIM_FIELDS], float(dims.get("rope_base", 1e4)),
                              float(dims.get("rms_eps", 1e-6)))
-            check(lib().btf_decoder_synthetic(ctypes.byref(d), seed, ctypes.byref(o), ctypes.byref(h)),
+            check(lib().btf_decoder_synthetic_tp(ctypes.byref(d), seed, ctypes.byref(o), world, rank, ctypes.byref(h)),
                   "btf_decoder_synthetic")
         self.h = h.value
+        self.world, self.rank, self._peers = world, rank, []
 
     def close(self) -> None:
+        """Frees the decoder. Under tensor parallelism call it on every rank only
+        after all ranks have synchronised (no rank still stores into another's arena)."""
         if self.h:
             lib().btf_decoder_close(self.h)
             self.h = None
+        for p in self._peers:
+            ipc_close(p)
+        self._peers = []
 
     def __enter__(self):
         return self
 
     def __exit__(self, *a):
         self.close()
+
+    def connect_tp(self) -> None:
+        """Tensor parallelism: exchanges the activation arenas' IPC handles over the
+        default process group and connects the ranks (collective)."""
+        import torch.distributed as dist
+
+        base, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+        check(lib().btf_decoder_arena(self.h, ctypes.byref(base), ctypes.byref(nbytes)), "btf_decoder_arena")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, ipc_handle(base.value))
+        arenas = [base.value if r == self.rank else ipc_open(handles[r]) for r in range(self.world)]
+        self._peers = [a for r, a in enumerate(arenas) if r != self.rank]
+        arr = (ctypes.c_void_p * self.world)(*arenas)
+        check(lib().btf_decoder_connect(self.h, arr), "btf_decoder_connect")
+        dist.barrier()
 
     def info(self) -> dict:
         i = DecoderInfoC()

@@ -459,10 +459,13 @@ __device__ __forceinline__ uint32_t mix32(uint64_t x) {
   x ^= x >> 33;
   return (uint32_t)x;
 }
-__global__ void fill_panels_kernel(uint8_t* __restrict__ pan, int64_t npanels, int N, int K, int S, uint64_t seed,
-                                   float scale_mul) {
+// Row groups g0 .. of the full matrix: every value depends on its global
+// position only, so a row shard holds exactly the rows of the full matrix.
+__global__ void fill_panels_kernel(uint8_t* __restrict__ pan, int64_t npanels, int g0, int N, int K, int S,
+                                   uint64_t seed, float scale_mul) {
   const int64_t nb = npanels * kPanelBytes;
-  for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t bl = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; bl < nb; bl += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = bl + (int64_t)g0 * S * kPanelBytes;  // global byte index
     const int64_t pidx = b / kPanelBytes;
     const int off = (int)(b % kPanelBytes);
     const int g = (int)(pidx / S), j = (int)(pidx % S);
@@ -482,7 +485,7 @@ __global__ void fill_panels_kernel(uint8_t* __restrict__ pan, int64_t npanels, i
         }
         byte |= (uint8_t)(code << (2 * k));
       }
-      pan[b] = byte;
+      pan[bl] = byte;
     } else {
       const int so = off - kCodeBytes, bb = so >> 4, rr = (so >> 1) & 7;
       const int row = g * 8 + rr, col = j * 1024 + bb * 128;
@@ -494,8 +497,8 @@ __global__ void fill_panels_kernel(uint8_t* __restrict__ pan, int64_t npanels, i
         v = fabsf(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2)) * scale_mul;
       }
       const uint16_t hb = __half_as_ushort(__float2half_rn(v));
-      pan[b] = (uint8_t)(hb & 0xff);
-      pan[b + 1] = (uint8_t)(hb >> 8);
+      pan[bl] = (uint8_t)(hb & 0xff);
+      pan[bl + 1] = (uint8_t)(hb >> 8);
     }
   }
 }
@@ -546,9 +549,10 @@ cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, 
   return launch_pdl(argmax2_kernel, dim3(1), dim3(32), 0, st, static_cast<const float*>(pv),
                     static_cast<const int*>(pi), parts, out, tok_next, pos);
 }
-cudaError_t launch_fill_panels(uint8_t* pan, int N, int K, uint64_t seed, float scale_mul, cudaStream_t st) {
-  const int64_t np = groups_of(N) * slices_of(K);
-  fill_panels_kernel<<<1184, 256, 0, st>>>(pan, np, N, K, (int)slices_of(K), seed, scale_mul);
+cudaError_t launch_fill_panels(uint8_t* pan, int row0, int rows, int N, int K, uint64_t seed, float scale_mul,
+                               cudaStream_t st) {
+  const int64_t np = groups_of(rows) * slices_of(K);
+  fill_panels_kernel<<<1184, 256, 0, st>>>(pan, np, row0 / kRows, N, K, (int)slices_of(K), seed, scale_mul);
   return cudaGetLastError();
 }
 cudaError_t launch_fill_uniform(float* x, int64_t n, uint64_t seed, float base, float spread, cudaStream_t st) {

@@ -43,9 +43,12 @@ cudaError_t launch_attention(const float* q, const void* kc, const void* vc, con
 // *pos += 1 when those are non-null. pv/pi: `parts` partials.
 cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, int32_t* out, int32_t* tok_next,
                           int32_t* pos, cudaStream_t st);
-// Seeded synthetic weights: a panel matrix [N][K] of codes 0..2 with fp16
-// scales |N(0,1)| * scale_mul, and uniform floats base +- spread.
-cudaError_t launch_fill_panels(uint8_t* panels, int N, int K, uint64_t seed, float scale_mul, cudaStream_t st);
+// Seeded synthetic weights: rows [row0, row0 + rows) (row0 a multiple of 8) of
+// a panel matrix [N][K] of codes 0..2 with fp16 scales |N(0,1)| * scale_mul
+// (each value a function of its position in the full matrix), and uniform
+// floats base +- spread.
+cudaError_t launch_fill_panels(uint8_t* panels, int row0, int rows, int N, int K, uint64_t seed, float scale_mul,
+                               cudaStream_t st);
 cudaError_t launch_fill_uniform(float* x, int64_t n, uint64_t seed, float base, float spread, cudaStream_t st);
 
 }  // namespace btf

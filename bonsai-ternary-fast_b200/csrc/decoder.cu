@@ -36,7 +36,17 @@ struct Mat {
   uint8_t* pan = nullptr;
   int N = 0, K = 0;
   btf_hx hx{0, 0, 0, 0, nullptr};
+  int row0 = 0, n = 0;  // this rank's rows [row0, row0 + n) (n = N on one GPU)
 };
+
+// Row shard of `rank` among `world`: whole 8-row groups, ceil(groups / world)
+// groups per rank, the last ranks clipped (shard.shard_rows in Python).
+void shard_rows(int N, int world, int rank, int* r0, int* n) {
+  const int groups = (N + kRows - 1) / kRows;
+  const int per = (groups + world - 1) / world * kRows;
+  *r0 = std::min(N, rank * per);
+  *n = std::max(0, std::min(N, *r0 + per) - *r0);
+}
 
 struct Layer {
   bool rec = false;
@@ -81,6 +91,17 @@ struct Decoder {
   cudaGraphExec_t exec = nullptr;
   uint64_t weight_bytes = 0, state_bytes = 0, kv_bytes_per_token = 0;
   static constexpr int kArgmaxParts = 148;
+  // tensor parallelism: every matmul N-sharded over `world` ranks, its outputs
+  // stored into every rank's arena (btf_gemv_gather, counted completion). The
+  // arena holds the activation buffers after a 256-byte control block (arrival
+  // counter +0, consumed arrivals +4, CTA completion +8), laid out the same on
+  // every rank; peers[r] is rank r's arena as mapped in this process.
+  int world = 1, rank = 0;
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  uint8_t* peers[BTF_MAX_RANKS] = {};
+  bool connected = false;
+  static constexpr size_t kCtl = 256;
 
   ~Decoder() {
     if (exec) cudaGraphExecDestroy(exec);
@@ -116,17 +137,22 @@ int make_buffers(Decoder& D) {
   const int wc = std::max(n_gdn ? D.C : 0, n_attn ? HK * HD : 0);
   const int wo = std::max(n_gdn ? D.DI : 0, n_attn ? H * HD : 0);
   D.Kmax = std::max({E, F, wo});
-  D.x = D.alloc<float>(E, &rc);
-  D.xn = D.alloc<float>(E, &rc);
-  D.bA = D.alloc<float>(wa, &rc);
-  D.bB = D.alloc<float>(wb, &rc);
-  D.bC = D.alloc<float>(wc, &rc);
-  D.bO = D.alloc<float>(wo, &rc);
-  D.bQ = D.alloc<float>(std::max(1, H * HD), &rc);
-  D.bG = D.alloc<float>(F, &rc);
+  // activation buffers in one arena (shared with the other ranks under tensor parallelism)
+  const int sizes[9] = {E, E, wa, wb, wc, wo, std::max(1, H * HD), F, d.n_vocab};
+  size_t off[9], total = Decoder::kCtl;
+  for (int i = 0; i < 9; ++i) {
+    off[i] = total;
+    total += ((size_t)sizes[i] * 4 + 255) / 256 * 256;
+  }
+  D.arena = D.alloc<uint8_t>(total, &rc);
+  if (rc) return rc;
+  D.arena_bytes = total;
+  if (cudaMemset(D.arena, 0, total) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder: arena clear");
+  float** dst[9] = {&D.x, &D.xn, &D.bA, &D.bB, &D.bC, &D.bO, &D.bQ, &D.bG, &D.logits};
+  for (int i = 0; i < 9; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
+  D.peers[D.rank] = D.arena;
   D.beta = D.alloc<float>(std::max(1, D.NV), &rc);
   D.gg = D.alloc<float>(std::max(1, D.NV), &rc);
-  D.logits = D.alloc<float>(d.n_vocab, &rc);
   D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
   D.amax_v = D.alloc<float>(Decoder::kArgmaxParts, &rc);
   D.amax_i = D.alloc<int>(Decoder::kArgmaxParts, &rc);
@@ -169,9 +195,31 @@ int reset_state(Decoder& D) {
 }
 
 // ---------------------------------------------------------------- one step
-int gemv(Decoder& D, std::initializer_list<btf_gemv_seg> segs, int K, int mode) {
+// One output of a GEMV launch: matrix m into y (the full output row of the
+// local buffer; null for the up half of SwiGLU).
+struct Out {
+  const Mat* m;
+  float* y;
+};
+int gemv(Decoder& D, std::initializer_list<Out> outs, int K, int mode) {
   const btf_q8act act{D.aq, D.ad, D.as};
-  return btf_gemv(segs.begin(), (int)segs.size(), K, 1, act, mode, D.st);
+  btf_gemv_seg segs[3];
+  int ns = 0;
+  const bool tp = D.world > 1;
+  for (const Out& o : outs)
+    segs[ns++] = {o.m->pan, tp ? o.m->n : o.m->N, o.y ? o.y + (tp ? o.m->row0 : 0) : nullptr, o.y ? o.m->N : 0};
+  if (!tp) return btf_gemv(segs, ns, K, 1, act, mode, D.st);
+  btf_gather g{};
+  g.world = D.world;
+  g.rank = D.rank;
+  const int nout = mode == BTF_SWIGLU ? 1 : ns;
+  for (int s = 0; s < nout; ++s)
+    for (int r = 0; r < D.world; ++r)
+      g.peer_y[s][r] = reinterpret_cast<float*>(D.peers[r] + (reinterpret_cast<uint8_t*>(segs[s].y) - D.arena));
+  for (int r = 0; r < D.world; ++r) g.flags[r] = reinterpret_cast<unsigned*>(D.peers[r]);
+  g.expect = reinterpret_cast<unsigned*>(D.arena + 4);
+  g.done = reinterpret_cast<unsigned*>(D.arena + 8);
+  return btf_gemv_gather(segs, ns, K, 1, act, mode, &g, D.st);
 }
 int prep(Decoder& D, const float* x, int n, const float* normw, const btf_hx& hx, float* xn) {
   const btf_q8act act{D.aq, D.ad, D.as};
@@ -197,35 +245,30 @@ int enqueue_step(Decoder& D) {
   for (Layer& l : D.L) {
     if (l.rec) {
       BTF_TRY(prep(D, D.x, E, l.attn_norm, l.qkv.hx, D.xn));
-      BTF_TRY(gemv(D, {{l.qkv.pan, l.qkv.N, D.bA, l.qkv.N}, {l.zg.pan, l.zg.N, D.bB, l.zg.N}}, E,
-                   BTF_STORE));
+      BTF_TRY(gemv(D, {{&l.qkv, D.bA}, {&l.zg, D.bB}}, E, BTF_STORE));
       const GdnArgs ga{D.xn, l.alpha_w, l.beta_w, l.ssm_dt, l.ssm_a, E, l.ab_bf16, D.bA, l.conv_state, l.conv_w,
                        d.conv_kernel, D.C, D.bB, l.ssm_state, l.ssm_norm, D.NK, D.DK, D.DV, D.QK, d.rms_eps, D.d_pos,
                        D.bO, D.NV};
       BTF_TRYC(launch_gdn_mix(ga, D.st));
       BTF_TRY(prep(D, D.bO, D.DI, nullptr, l.out.hx, nullptr));
-      BTF_TRY(gemv(D, {{l.out.pan, E, D.x, E}}, D.DI, BTF_ADD));
+      BTF_TRY(gemv(D, {{&l.out, D.x}}, D.DI, BTF_ADD));
     } else {
       BTF_TRY(prep(D, D.x, E, l.attn_norm, l.wq.hx, nullptr));
-      BTF_TRY(gemv(D,
-                   {{l.wq.pan, l.wq.N, D.bA, l.wq.N},
-                    {l.wk.pan, l.wk.N, D.bB, l.wk.N},
-                    {l.wv.pan, l.wv.N, D.bC, l.wv.N}},
-                   E, BTF_STORE));
+      BTF_TRY(gemv(D, {{&l.wq, D.bA}, {&l.wk, D.bB}, {&l.wv, D.bC}}, E, BTF_STORE));
       BTF_TRYC(launch_attn_prep(D.bA, D.bB, D.bC, l.q_norm, l.k_norm, H, HK, HD, d.n_rot, D.theta_scale, d.rms_eps,
                                 D.d_pos, D.o.round_q_f16, D.bQ, l.kc, l.vc, D.st));
       BTF_TRYC(launch_attention(D.bQ, l.kc, l.vc, D.bA, H, HK, HD, D.o.n_ctx, D.o.attn_splits, D.d_pos, D.part, D.bO,
                                 D.st));
       BTF_TRY(prep(D, D.bO, H * HD, nullptr, l.wo.hx, nullptr));
-      BTF_TRY(gemv(D, {{l.wo.pan, E, D.x, E}}, H * HD, BTF_ADD));
+      BTF_TRY(gemv(D, {{&l.wo, D.x}}, H * HD, BTF_ADD));
     }
     BTF_TRY(prep(D, D.x, E, l.post_norm, l.gate.hx, nullptr));
-    BTF_TRY(gemv(D, {{l.gate.pan, F, D.bG, F}, {l.up.pan, F, nullptr, 0}}, E, BTF_SWIGLU));
+    BTF_TRY(gemv(D, {{&l.gate, D.bG}, {&l.up, nullptr}}, E, BTF_SWIGLU));
     BTF_TRY(prep(D, D.bG, F, nullptr, l.down.hx, nullptr));
-    BTF_TRY(gemv(D, {{l.down.pan, E, D.x, E}}, F, BTF_ADD));
+    BTF_TRY(gemv(D, {{&l.down, D.x}}, F, BTF_ADD));
   }
   BTF_TRY(prep(D, D.x, E, D.out_norm, D.output.hx, nullptr));
-  BTF_TRY(gemv(D, {{D.output.pan, d.n_vocab, D.logits, d.n_vocab}}, E, BTF_STORE));
+  BTF_TRY(gemv(D, {{&D.output, D.logits}}, E, BTF_STORE));
   BTF_TRYC(launch_argmax(D.logits, d.n_vocab, D.amax_v, D.amax_i, Decoder::kArgmaxParts, D.d_next, D.d_tok, D.d_pos,
                          D.st));
   return BTF_OK;
@@ -250,6 +293,7 @@ int capture(Decoder& D) {
 // Runs one step (graph replay or eager) on D.st, no host synchronisation.
 int run_step(Decoder& D) {
   if (D.pos >= D.o.n_ctx) return fail(BTF_ERR_ARG, "btf_decoder: context full (n_ctx %d)", D.o.n_ctx);
+  if (D.world > 1 && !D.connected) return fail(BTF_ERR_STATE, "btf_decoder: tensor-parallel decoder not connected");
   if (D.o.cuda_graph) {
     if (!D.exec) BTF_TRY(capture(D));
     const cudaError_t e = cudaGraphLaunch(D.exec, D.st);
@@ -564,17 +608,23 @@ int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void**
   btf_gguf_close(g);
   if (rc) return rc;
   BTF_TRY(finish_open(*D));
+  D->connected = true;
   *handle = D.release();
   return BTF_OK;
 }
 
-int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, void** handle) {
+int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, int world,
+                             int rank, void** handle) {
   if (!dims || !handle) return fail(BTF_ERR_ARG, "btf_decoder_synthetic: null argument");
+  if (world < 1 || world > BTF_MAX_RANKS || rank < 0 || rank >= world)
+    return fail(BTF_ERR_ARG, "btf_decoder_synthetic: need 1 <= world <= %d and 0 <= rank < world", BTF_MAX_RANKS);
   *handle = nullptr;
   auto D = std::make_unique<Decoder>();
   Decoder& R = *D;
   R.o = defaults(opts);
   R.d = *dims;
+  R.world = world;
+  R.rank = rank;
   const btf_decoder_dims& d = R.d;
   if (d.n_layer <= 0 || d.n_head_kv <= 0 || d.n_head % d.n_head_kv || d.n_group <= 0 || d.dt_rank % d.n_group ||
       d.n_rot > d.head_dim || d.n_rot % 2 || d.n_vocab <= 0)
@@ -601,12 +651,22 @@ int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf
   int rc = BTF_OK;
   uint64_t s = seed * 1000003ull;
   const int blk = d.hadamard_block;
-  auto mat = [&](Mat* m, int N, int K, bool ssm_out) -> int {
+  // sharded: this rank's rows of the full matrix (the embedding table is never sharded)
+  auto mat = [&](Mat* m, int N, int K, bool ssm_out, bool shard = true) -> int {
     m->N = N;
     m->K = K;
-    m->pan = R.alloc<uint8_t>(btf_panel_bytes(N, K), &rc);
+    m->row0 = 0;
+    m->n = N;
+    if (shard && world > 1) {
+      shard_rows(N, world, rank, &m->row0, &m->n);
+      int lr0 = 0, ln = 0;
+      shard_rows(N, world, world - 1, &lr0, &ln);
+      if (ln <= 0)
+        return fail(BTF_ERR_ARG, "btf_decoder_synthetic: %d output rows leave a rank of %d without rows", N, world);
+    }
+    m->pan = R.alloc<uint8_t>(btf_panel_bytes(m->n, K), &rc);
     if (rc) return rc;
-    R.weight_bytes += btf_panel_bytes(N, K);
+    R.weight_bytes += btf_panel_bytes(m->n, K);
     if (blk) {
       m->hx.block = blk;
       if (ssm_out) {
@@ -615,7 +675,7 @@ int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf
         m->hx.perm_rep = R.NV / R.NK;
       }
     }
-    const cudaError_t e = launch_fill_panels(m->pan, N, K, ++s, 1.0f / std::sqrt((float)K), R.st);
+    const cudaError_t e = launch_fill_panels(m->pan, m->row0, m->n, N, K, ++s, 1.0f / std::sqrt((float)K), R.st);
     return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_synthetic: fill");
   };
   auto vec = [&](float** p, int64_t n, float base, float spread) -> int {
@@ -626,7 +686,7 @@ int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf
     return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_synthetic: fill");
   };
   const int E = d.n_embd, F = d.n_ff, H = d.n_head, HK = d.n_head_kv, HD = d.head_dim;
-  BTF_TRY(mat(&R.embd, d.n_vocab, E, false));
+  BTF_TRY(mat(&R.embd, d.n_vocab, E, false, false));
   R.embd.hx = btf_hx{0, 0, 0, 0, nullptr};
   R.weight_bytes -= btf_panel_bytes(d.n_vocab, E);
   R.weight_bytes += (uint64_t)E / 4 + (uint64_t)E / 64;
@@ -663,7 +723,33 @@ int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf
   }
   if (cudaStreamSynchronize(R.st) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: fill");
   BTF_TRY(finish_open(R));
+  R.connected = world == 1;
   *handle = D.release();
+  return BTF_OK;
+}
+
+int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, void** handle) {
+  return btf_decoder_synthetic_tp(dims, seed, opts, 1, 0, handle);
+}
+
+int btf_decoder_arena(void* handle, void** base, uint64_t* bytes) {
+  if (!handle || !base || !bytes) return fail(BTF_ERR_ARG, "btf_decoder_arena: null argument");
+  const Decoder& D = *static_cast<const Decoder*>(handle);
+  *base = D.arena;
+  *bytes = D.arena_bytes;
+  return BTF_OK;
+}
+
+int btf_decoder_connect(void* handle, void* const* peer_arenas) {
+  if (!handle || !peer_arenas) return fail(BTF_ERR_ARG, "btf_decoder_connect: null argument");
+  Decoder& D = *static_cast<Decoder*>(handle);
+  if (D.world < 2) return fail(BTF_ERR_STATE, "btf_decoder_connect: not a tensor-parallel decoder");
+  if (D.exec) return fail(BTF_ERR_STATE, "btf_decoder_connect: already captured");
+  for (int r = 0; r < D.world; ++r) {
+    if (r != D.rank && !peer_arenas[r]) return fail(BTF_ERR_ARG, "btf_decoder_connect: arena of rank %d is null", r);
+    D.peers[r] = r == D.rank ? D.arena : static_cast<uint8_t*>(peer_arenas[r]);
+  }
+  D.connected = true;
   return BTF_OK;
 }
 

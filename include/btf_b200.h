@@ -294,6 +294,20 @@ int btf_decoder_reset(void* handle);
 int btf_decoder_close(void* handle);
 int btf_decoder_get_info(void* handle, btf_decoder_info* out);
 
+/* Tensor-parallel decode (row f4): every ternary matmul of the step is N-sharded
+ * over `world` GPUs (one process each; rank r holds rows shard r of every matrix,
+ * whole 8-row groups) and its outputs are stored into every rank's activation
+ * arena by btf_gemv_gather (counted completion); the rest of the step runs
+ * replicated. Set-up: btf_decoder_synthetic_tp on every rank, export the arena
+ * of btf_decoder_arena with btf_ipc_handle, open the peers' with btf_ipc_open,
+ * then btf_decoder_connect(h, arenas[world]) before the first step. All ranks
+ * then make the same sequence of step / run calls. Tear down only after every
+ * rank has synchronised (no rank still stores into another's arena). */
+int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, int world,
+                             int rank, void** handle);
+int btf_decoder_arena(void* handle, void** base, uint64_t* bytes);
+int btf_decoder_connect(void* handle, void* const* peer_arenas);
+
 #ifdef __cplusplus
 }
 #endif
