@@ -397,6 +397,9 @@ def gpu_arm(args):
     kernels = {k: {"us": kern_ms[k] * 1e3, "GB/s": (kernel_bytes[k] / world) / (kern_ms[k] * 1e-3) / 1e9}
                for k in kinds}
 
+    dec3 = None
+    if world > 1:  # collective: the tensor-parallel decode step on every rank
+        dec3 = decode_config3(btf, torch, dev, world=world, rank=rank)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -431,6 +434,8 @@ def gpu_arm(args):
         if world == 1:
             line["prefill_gemm_config2"] = prefill_gemm(btf, torch, dev)
             line["decode_config3"] = decode_config3(btf, torch, dev)
+        else:
+            line["decode_config3"] = dec3
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference(host_threads())
         print(json.dumps(line), flush=True)
@@ -455,34 +460,50 @@ CONFIG3 = dict(n_layer=64, n_embd=5120, n_ff=17408, n_vocab=248320, n_head=24, n
                rope_base=1e7, rms_eps=1e-6)
 
 
-def decode_config3(btf, torch, dev, steps=64, warmup=8, n_ctx=4096):
+def decode_config3(btf, torch, dev, steps=64, warmup=8, n_ctx=4096, world=1, rank=0):
     """Benchmark configuration 3: batch-1 decode steps of the synthetic 64-layer
     decoder as one CUDA graph per token (btf_decoder_*). `value`: tokens/s of a
     device-side greedy loop (each step feeds its argmax to the next), CUDA events
     on the decoder's stream; `e2e`: the synchronous step API (token from the host,
     next token back). Roofline: bytes one token reads (resident weights, one
-    embedding row, recurrent state read + written, K/V of the cached tokens)."""
-    dec = btf.Decoder(dims=CONFIG3, seed=3, n_ctx=n_ctx)
+    embedding row, recurrent state read + written, K/V of the cached tokens).
+    With world > 1 (collective) every matmul is N-sharded over the ranks
+    (btf_decoder_synthetic_tp) and times are the max over ranks; the roofline
+    is per GPU (this rank's bytes)."""
+    if world > 1:
+        import torch.distributed as dist
+    dec = btf.Decoder(dims=CONFIG3, seed=3, n_ctx=n_ctx, device=dev.index, world=world, rank=rank)
+    if world > 1:
+        dec.connect_tp()
     info = dec.info()
     st = torch.cuda.ExternalStream(info["stream"], device=dev)
-    nxt, _ = dec.step(1)  # captures the graph
+
+    def timed(fn, n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    dec.step(1)  # captures the graph
     dec.run(warmup)
     torch.cuda.synchronize()
     p0 = dec.info()["pos"]
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(st)
-    dec.run(steps)
-    b.record(st)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / steps
+    ms = timed(lambda: dec.run(steps), steps)
     ne2e = 16
-    nxt = 1
-    a.record(st)
-    for _ in range(ne2e):
-        nxt, _ = dec.step(nxt)
-    b.record(st)
-    torch.cuda.synchronize()
-    ms_e2e = a.elapsed_time(b) / ne2e
+
+    def e2e_steps():
+        nxt = 1
+        for _ in range(ne2e):
+            nxt, _ = dec.step(nxt)
+
+    ms_e2e = timed(e2e_steps, ne2e)
     err = btf.device_error()
     ctx_mean = p0 + (steps + 1) / 2.0  # cached tokens the timed steps read on average
     per_tok = info["weight_bytes"] + info["state_bytes"] + info["kv_bytes_per_token"] * ctx_mean
@@ -490,18 +511,26 @@ def decode_config3(btf, torch, dev, steps=64, warmup=8, n_ctx=4096):
     peak, peak_src = measured_peaks()
     n_gdn = sum(1 for il in range(CONFIG3["n_layer"]) if (il + 1) % 4)
     out = {"metric": "decode tokens/s, batch 1 (config 3)", "value": 1e3 / ms, "unit": "tok/s", "ms_per_token": ms,
-           "steps": steps, "warmup": warmup + 1, "context_start": p0, "n_ctx": n_ctx,
+           "n_gpus": world, "steps": steps, "warmup": warmup + 1, "context_start": p0, "n_ctx": n_ctx,
            "config": dict(CONFIG3), "data": "synthetic (seeded ternary panels, uniform vectors)",
-           "bytes_per_token": per_tok, "weight_bytes": info["weight_bytes"], "state_bytes": info["state_bytes"],
-           "kv_bytes_per_cached_token": info["kv_bytes_per_token"],
+           "parallelism": "one GPU" if world == 1 else
+           f"tensor parallel x{world}: every matmul N-sharded, outputs all-gathered in the GEMV epilogue "
+           "(NVLink stores, counted completion); the rest replicated",
+           "bytes_per_token_per_gpu": per_tok, "weight_bytes_per_gpu": info["weight_bytes"],
+           "state_bytes": info["state_bytes"], "kv_bytes_per_cached_token": info["kv_bytes_per_token"],
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                        "peak_source": peak_src},
+                        "peak_source": peak_src, "per": "GPU"},
            "e2e": {"value": 1e3 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-           # per token: 11 launches per layer (prep + GEMV x 4, and the mixer's 3), embed, final prep,
-           # lm_head, 2 argmax stages
-           "gpu_launches_per_token": 11 * CONFIG3["n_layer"] + 5, "n_gdn_layers": n_gdn,
+           # per token: 9 launches per delta-net layer (prep + GEMV x 4, the mixer), 11 per
+           # attention layer (3 attention kernels), embed, final prep, lm_head, 2 argmax stages
+           "gpu_launches_per_token": 9 * n_gdn + 11 * (CONFIG3["n_layer"] - n_gdn) + 5, "n_gdn_layers": n_gdn,
            "device_error_word": err, "path": "btf_decoder_run: one graph replay per token"}
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # no rank still stores into another's arena
     dec.close()
+    if world > 1:
+        dist.barrier()
     return out
 
 
