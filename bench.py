@@ -580,6 +580,14 @@ def only_kernel(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     btf.kernels_init(0)
+    if args.only == "decode":  # eager config-3 decode steps (one launch per kernel, no graph)
+        with btf.Decoder(dims=CONFIG3, seed=3, n_ctx=4096, cuda_graph=False) as dec:
+            t = 1
+            for _ in range(args.iters):
+                t, _ = dec.step(t)
+            torch.cuda.synchronize()
+            print(f"decode: {args.iters} eager steps, last token {t}, device error {btf.device_error()}")
+        return
     if args.only == "gemm":  # one prefill GEMM: M=512, K=5120 -> N=17408
         M, K, N = 512, 5120, 17408
         src = torch.from_numpy(synth.ternary_ptq(N, K, seed=0)).to(dev)
@@ -626,7 +634,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm"], help="profile mode: one kernel kind")
+    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm", "decode"],
+                    help="profile mode: one kernel kind, or (decode) eager config-3 decode steps")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--fused", type=int, default=0, help="--only: 1 = btf_gemv_f32 (quantise inside the GEMV)")
     args = ap.parse_args()
