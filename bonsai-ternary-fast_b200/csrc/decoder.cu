@@ -79,7 +79,7 @@ struct Decoder {
   std::vector<void*> allocs;
   // step buffers
   float *x = nullptr, *xn = nullptr, *bA = nullptr, *bB = nullptr, *bC = nullptr, *bO = nullptr, *bQ = nullptr,
-        *bG = nullptr, *beta = nullptr, *gg = nullptr, *logits = nullptr, *part = nullptr, *amax_v = nullptr;
+        *bG = nullptr, *logits = nullptr, *part = nullptr, *amax_v = nullptr;
   int* amax_i = nullptr;
   int8_t* aq = nullptr;
   float* ad = nullptr;
@@ -151,8 +151,6 @@ int make_buffers(Decoder& D) {
   float** dst[9] = {&D.x, &D.xn, &D.bA, &D.bB, &D.bC, &D.bO, &D.bQ, &D.bG, &D.logits};
   for (int i = 0; i < 9; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
   D.peers[D.rank] = D.arena;
-  D.beta = D.alloc<float>(std::max(1, D.NV), &rc);
-  D.gg = D.alloc<float>(std::max(1, D.NV), &rc);
   D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
   D.amax_v = D.alloc<float>(Decoder::kArgmaxParts, &rc);
   D.amax_i = D.alloc<int>(Decoder::kArgmaxParts, &rc);
