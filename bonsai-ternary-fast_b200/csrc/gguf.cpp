@@ -284,8 +284,10 @@ int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_
     return btf::fail(BTF_ERR_UNSUPPORTED, "btf_gguf_load_panels: %s is not a 2-D PTQ1_0 tensor", t.name.c_str());
   const int64_t K = t.ne[0], N = t.ne[1];
   const int64_t row_bytes = K / 128 * 28, S = (K + 1023) / 1024;
-  // whole 8-row groups per chunk, so every chunk starts a panel row group
-  const int64_t rows_per = std::max<int64_t>(8, staging_bytes / row_bytes / 8 * 8);
+  // whole 8-row groups per chunk, so every chunk starts a panel row group; no
+  // chunk larger than the tensor (a small tensor gets small staging buffers)
+  const int64_t rows_per =
+      std::min<int64_t>((N + 7) / 8 * 8, std::max<int64_t>(8, staging_bytes / row_bytes / 8 * 8));
   const size_t stage = (size_t)(rows_per * row_bytes);
   const uint8_t* src = f->map + f->data_start + t.offset;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
