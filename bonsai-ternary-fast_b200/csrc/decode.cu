@@ -148,24 +148,40 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   float* vv = sm + 2 * p.DK;
   float* ov = sm + 2 * p.DK + p.DV;
   const int h = blockIdx.x, kh = h % p.NK, tid = threadIdx.x;
+  // the head's alpha / beta weight rows (16-byte loads; E % 4 == 0, rows 16-byte
+  // aligned) are constants: the first kPre float4 of each per thread are fetched
+  // before the wait, while the previous kernel drains
+  constexpr int kPre = 4;
+  const float4* a4 = reinterpret_cast<const float4*>(p.aw + (int64_t)h * p.E);
+  const float4* b4 = reinterpret_cast<const float4*>(p.bw + (int64_t)h * p.E);
+  const int n4 = p.E >> 2;
+  float4 ap[kPre], bp[kPre];
+#pragma unroll
+  for (int u = 0; u < kPre; ++u) {
+    const int i = tid + u * blockDim.x;
+    ap[u] = i < n4 ? a4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    bp[u] = i < n4 ? b4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   pdl_launch_dependents();
   pdl_wait();  // xn, qkv, z and the ring come from earlier kernels
   // alpha / beta dots
   double sa = 0.0, sb = 0.0;
-  {  // 16-byte loads, unrolled: the rows are read with a few latencies (E % 4 == 0, rows 16-byte aligned)
+  {
     const float4* x4 = reinterpret_cast<const float4*>(p.xn);
-    const float4* a4 = reinterpret_cast<const float4*>(p.aw + (int64_t)h * p.E);
-    const float4* b4 = reinterpret_cast<const float4*>(p.bw + (int64_t)h * p.E);
-#pragma unroll 4
-    for (int i = tid; i < (p.E >> 2); i += blockDim.x) {
-      float4 xv = x4[i];
+    auto dot = [&](const float4& av, const float4& bv, float4 xv) {
       if (p.bf16_in) xv = make_float4(round_bf16(xv.x), round_bf16(xv.y), round_bf16(xv.z), round_bf16(xv.w));
-      const float4 av = a4[i], bv = b4[i];
       sa += (double)__fmul_rn(av.x, xv.x) + (double)__fmul_rn(av.y, xv.y) + (double)__fmul_rn(av.z, xv.z) +
             (double)__fmul_rn(av.w, xv.w);
       sb += (double)__fmul_rn(bv.x, xv.x) + (double)__fmul_rn(bv.y, xv.y) + (double)__fmul_rn(bv.z, xv.z) +
             (double)__fmul_rn(bv.w, xv.w);
+    };
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int i = tid + u * blockDim.x;
+      if (i < n4) dot(ap[u], bp[u], x4[i]);
     }
+#pragma unroll 4
+    for (int i = tid + kPre * blockDim.x; i < n4; i += blockDim.x) dot(a4[i], b4[i], x4[i]);
   }
   sa = block_sum(sa, red);
   sb = block_sum(sb, red);

@@ -77,6 +77,25 @@ __global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_cons
   const int m = blockIdx.y, base = blockIdx.x * a.S;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* xr = a.x + (size_t)m * a.ldx;
+  // column map of this thread's first span column (the launch gives every
+  // column its own thread), and its norm weight and sign: constants, fetched
+  // before the wait while the previous kernel drains
+  auto src_of = [&](int og) {
+    if (a.perm_rep <= 1) return og;
+    const int dd = og % a.perm_hd, t = og / a.perm_hd;  // tiled [hd, nk, rep] -> grouped [hd, rep, nk]
+    const int r = t % a.perm_rep, k = t / a.perm_rep;
+    return dd + a.perm_hd * (k + a.perm_nk * r);
+  };
+  const int og0 = base + threadIdx.x, src0 = src_of(og0);
+  const bool own = threadIdx.x < a.S;
+  float w0 = 1.0f, wo0 = 1.0f, sg0 = 1.0f;
+  if (own) {
+    if constexpr (NORM) {
+      w0 = a.normw[src0];
+      wo0 = a.normw[og0];
+    }
+    if (a.signs) sg0 = a.signs[og0];
+  }
   pdl_launch_dependents();
   pdl_wait();  // x is written by the previous kernel
   float scale = 1.0f;
@@ -104,22 +123,16 @@ __global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_cons
     const float mean = (float)(tot / (double)a.n);
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
   }
-#pragma unroll 4
   for (int o = threadIdx.x; o < a.S; o += nthr) {
-    const int og = base + o;
-    int src = og;
-    if (a.perm_rep > 1) {  // tiled [hd, nk, rep] -> grouped [hd, rep, nk]
-      const int dd = og % a.perm_hd, t = og / a.perm_hd;
-      const int r = t % a.perm_rep, k = t / a.perm_rep;
-      src = dd + a.perm_hd * (k + a.perm_nk * r);
-    }
+    const bool first = o == (int)threadIdx.x;  // the prefetched column
+    const int og = base + o, src = first ? src0 : src_of(og);
     float v = xr[src];
-    if constexpr (NORM) v = __fmul_rn(__fmul_rn(v, scale), a.normw[src]);
-    if (a.signs) v = __fmul_rn(v, a.signs[og]);
+    if constexpr (NORM) v = __fmul_rn(__fmul_rn(v, scale), first ? w0 : a.normw[src]);
+    if (a.signs) v = __fmul_rn(v, first ? sg0 : a.signs[og]);
     buf[o] = v;
     if (a.xn_out) {
       float u = xr[og];
-      if constexpr (NORM) u = __fmul_rn(__fmul_rn(u, scale), a.normw[og]);
+      if constexpr (NORM) u = __fmul_rn(__fmul_rn(u, scale), first ? wo0 : a.normw[og]);
       a.xn_out[(size_t)m * a.ldxn + og] = u;
     }
   }
