@@ -8,7 +8,8 @@
 //     and GemvSeg::scales must be nullptr: the scales live inside the panels;
 //   - launch_repack keeps the reference's T2 output; launch_repack_panels is the
 //     loader for the B200 layout and needs N and K;
-//   - launch_prep runs the whole prep (RMSNorm, permutation, signs, Hadamard, Q8).
+//   - launch_prep runs the whole prep (RMSNorm, permutation, signs, Hadamard, Q8);
+//   - Decoder is the batch-1 decode step over a qwen35 GGUF (btf_decoder_*).
 #pragma once
 #include <cuda_runtime_api.h>
 
@@ -83,6 +84,48 @@ inline void launch_gemv(const GemvSeg* segs, int nseg, int K, int M, const Q8Act
   }
   throw_if(btf_gemv(s, nseg, K, M, btf_q8act{a.q, a.d, a.s}, (int)mode, st), "launch_gemv");
 }
+
+// The batch-1 decode step (btf_decoder_*). Mirrors FastDecoder
+// (include/btf/fast.hpp:71-101): step() returns the greedy next token and fills
+// the logits when given; prefill() feeds the prompt one token per step.
+struct DecoderOptions {  // the FastOptions fields the decoder uses (fast.hpp:13-27)
+  int n_ctx = 4096;
+  bool round_q_f16 = true;
+  int attn_splits = 16;
+  bool cuda_graph = true;
+};
+
+class Decoder {
+ public:
+  explicit Decoder(const std::string& gguf_path, const DecoderOptions& o = DecoderOptions()) {
+    const btf_decoder_opts c{o.n_ctx, o.round_q_f16 ? 1 : 0, o.attn_splits, o.cuda_graph ? 1 : 0};
+    throw_if(btf_decoder_open(gguf_path.c_str(), &c, &h_), "btf_decoder_open");
+  }
+  Decoder(const Decoder&) = delete;
+  Decoder& operator=(const Decoder&) = delete;
+  ~Decoder() { btf_decoder_close(h_); }
+  int step(int32_t token, float* logits) {
+    int32_t next = -1;
+    throw_if(btf_decoder_step(h_, token, logits, &next), "btf_decoder_step");
+    return next;
+  }
+  int prefill(const int32_t* tokens, int n, float* logits) {
+    int next = -1;
+    for (int i = 0; i < n; ++i) next = step(tokens[i], i + 1 == n ? logits : nullptr);
+    return next;
+  }
+  void reset() { throw_if(btf_decoder_reset(h_), "btf_decoder_reset"); }
+  int pos() const { return info().pos; }
+  int n_vocab() const { return info().dims.n_vocab; }
+  btf_decoder_info info() const {
+    btf_decoder_info i{};
+    throw_if(btf_decoder_get_info(h_, &i), "btf_decoder_get_info");
+    return i;
+  }
+
+ private:
+  void* h_ = nullptr;
+};
 
 }  // namespace cuda
 }  // namespace btf

@@ -112,3 +112,26 @@ def test_gather_entry_points_reject_bad_arguments(btf):
     assert L.btf_gather_barrier(ctypes.byref(btf.GatherC()), None) == 1
     assert L.btf_alloc(0, ctypes.byref(ctypes.c_void_p())) == 1
     assert L.btf_ipc_handle(None, ctypes.create_string_buffer(64)) == 1
+
+
+def test_decoder_entry_points_reject_bad_arguments(btf):
+    # argument checks run before any device access, so they are testable without a GPU
+    import ctypes
+
+    L = btf.lib()
+    h = ctypes.c_void_p()
+    assert L.btf_decoder_open(None, None, ctypes.byref(h)) == 1
+    dims = btf.DecoderDimsC(*([4, 256, 512, 300, 3, 2, 128, 32, 32, 2, 4, 0, 4, 128]), 1e7, 1e-6)  # 3 % 2 heads
+    assert L.btf_decoder_synthetic(ctypes.byref(dims), 1, None, ctypes.byref(h)) == 1
+    assert "dims" in L.btf_last_error().decode()
+    dims.n_head = 4
+    assert L.btf_decoder_synthetic_tp(ctypes.byref(dims), 1, None, 9, 0, ctypes.byref(h)) == 1  # world > 8
+    assert L.btf_decoder_synthetic_tp(ctypes.byref(dims), 1, None, 2, 2, ctypes.byref(h)) == 1  # rank >= world
+    dims.hadamard_block = 96  # not a power of two
+    assert L.btf_decoder_synthetic(ctypes.byref(dims), 1, None, ctypes.byref(h)) == 1
+    nxt = ctypes.c_int32()
+    assert L.btf_decoder_step(None, 1, None, ctypes.byref(nxt)) == 1
+    assert L.btf_decoder_run(None, 1) == 1
+    assert L.btf_decoder_connect(None, None) == 1
+    info = btf.DecoderInfoC()
+    assert L.btf_decoder_get_info(None, ctypes.byref(info)) == 1
