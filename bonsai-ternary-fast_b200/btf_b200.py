@@ -37,7 +37,7 @@ EXPORTS = (
     "btf_gguf_open", "btf_gguf_close", "btf_gguf_tensor_count", "btf_gguf_find", "btf_gguf_tensor",
     "btf_gguf_load_panels", "btf_decoder_open", "btf_decoder_synthetic", "btf_decoder_step", "btf_decoder_run",
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
-    "btf_decoder_arena", "btf_decoder_connect",
+    "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows",
 )
 
 
@@ -164,6 +164,7 @@ def lib() -> ctypes.CDLL:
                                            i32, i32, ctypes.POINTER(vp)]),
         "btf_decoder_arena": (i32, [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]),
         "btf_decoder_connect": (i32, [vp, ctypes.POINTER(vp)]),
+        "btf_shard_rows": (i32, [i32, i32, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

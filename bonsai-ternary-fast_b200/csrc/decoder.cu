@@ -730,6 +730,13 @@ int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf
   return btf_decoder_synthetic_tp(dims, seed, opts, 1, 0, handle);
 }
 
+int btf_shard_rows(int N, int world, int rank, int* row0, int* rows) {
+  if (N <= 0 || world < 1 || rank < 0 || rank >= world || !row0 || !rows)
+    return fail(BTF_ERR_ARG, "btf_shard_rows: need N > 0, 0 <= rank < world and output pointers");
+  shard_rows(N, world, rank, row0, rows);
+  return BTF_OK;
+}
+
 int btf_decoder_arena(void* handle, void** base, uint64_t* bytes) {
   if (!handle || !base || !bytes) return fail(BTF_ERR_ARG, "btf_decoder_arena: null argument");
   const Decoder& D = *static_cast<const Decoder*>(handle);

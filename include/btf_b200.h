@@ -305,6 +305,10 @@ int btf_decoder_get_info(void* handle, btf_decoder_info* out);
  * rank has synchronised (no rank still stores into another's arena). */
 int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, int world,
                              int rank, void** handle);
+/* The row shard of `rank` among `world` that the tensor-parallel decoder uses for
+ * an N-row matrix: whole 8-row groups, ceil(groups / world) groups per rank, the
+ * last ranks clipped (rows may be 0 for small N). Host-only. */
+int btf_shard_rows(int N, int world, int rank, int* row0, int* rows);
 int btf_decoder_arena(void* handle, void** base, uint64_t* bytes);
 int btf_decoder_connect(void* handle, void* const* peer_arenas);
 

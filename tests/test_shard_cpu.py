@@ -81,3 +81,18 @@ def test_gloo_world2_sharded_gemv_bit_exact(orc, tmp_path, N, K, M):
     for r in range(world):
         got = np.load(tmp_path / f"y{r}.npy")
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), r
+
+
+def test_decoder_shard_rule_equals_shard_rows(btf):
+    # the tensor-parallel decoder (C++) splits every matrix exactly as shard.shard_rows
+    import ctypes
+
+    L = btf.lib()
+    r0, n = ctypes.c_int(), ctypes.c_int()
+    for N in (8, 37, 256, 1000, 1024, 5120, 6144, 10240, 17408, 248320):
+        for world in (1, 2, 3, 4, 8):
+            for rank in range(world):
+                assert L.btf_shard_rows(N, world, rank, ctypes.byref(r0), ctypes.byref(n)) == 0
+                want = shard.shard_rows(N, world, rank)
+                assert (r0.value, n.value) == (want.r0, want.n), (N, world, rank)
+    assert L.btf_shard_rows(0, 2, 0, ctypes.byref(r0), ctypes.byref(n)) == 1
