@@ -37,7 +37,7 @@ EXPORTS = (
     "btf_gguf_open", "btf_gguf_close", "btf_gguf_tensor_count", "btf_gguf_find", "btf_gguf_tensor",
     "btf_gguf_load_panels", "btf_decoder_open", "btf_decoder_synthetic", "btf_decoder_step", "btf_decoder_run",
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
-    "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows",
+    "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
 )
 
 
@@ -165,6 +165,8 @@ def lib() -> ctypes.CDLL:
         "btf_decoder_arena": (i32, [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]),
         "btf_decoder_connect": (i32, [vp, ctypes.POINTER(vp)]),
         "btf_shard_rows": (i32, [i32, i32, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
+        "btf_decoder_open_tp": (i32, [ctypes.c_char_p, ctypes.POINTER(DecoderOptsC), i32, i32, ctypes.POINTER(vp)]),
+        "btf_gguf_load_panels_rows": (i32, [vp, i64, i64, i64, vp, i64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -460,17 +462,19 @@ class GgufFile:
         buf = (ctypes.c_uint8 * t["bytes"]).from_address(t["data"])
         return np.frombuffer(buf, dtype=np.uint8)
 
-    def load_panels(self, index: int, staging_bytes: int = 8 << 20, stream=None) -> PanelMatrix:
-        """A 2-D PTQ1_0 tensor -> resident panels on the current device."""
+    def load_panels(self, index: int, staging_bytes: int = 8 << 20, stream=None, rows=None) -> PanelMatrix:
+        """A 2-D PTQ1_0 tensor -> resident panels on the current device; rows = (row0, n)
+        loads only those rows (row0 a multiple of 8), as one rank's shard."""
         torch = _torch()
         t = self.tensor(index)
         K, N = t["ne"][0], t["ne"][1]
+        row0, n = (0, N) if rows is None else rows
         dev = torch.device("cuda", torch.cuda.current_device())
         ensure_init(dev.index)
-        out = torch.empty(panel_bytes(N, K), dtype=torch.uint8, device=dev)
-        check(lib().btf_gguf_load_panels(self.h, index, _ptr(out), staging_bytes, _stream(stream)),
+        out = torch.empty(panel_bytes(n, K), dtype=torch.uint8, device=dev)
+        check(lib().btf_gguf_load_panels_rows(self.h, index, row0, n, _ptr(out), staging_bytes, _stream(stream)),
               "btf_gguf_load_panels")
-        return PanelMatrix(out, N, K)
+        return PanelMatrix(out, n, K)
 
 
 class Decoder:
@@ -487,7 +491,8 @@ class Decoder:
         o = DecoderOptsC(n_ctx, int(round_q_f16), attn_splits, int(cuda_graph))
         h = ctypes.c_void_p()
         if path is not None:
-            check(lib().btf_decoder_open(path.encode(), ctypes.byref(o), ctypes.byref(h)), "btf_decoder_open")
+            check(lib().btf_decoder_open_tp(path.encode(), ctypes.byref(o), world, rank, ctypes.byref(h)),
+                  "btf_decoder_open")
         else:
             d = DecoderDimsC(*[int(dims.get(f, 0)) for f in DIM_FIELDS], float(dims.get("rope_base", 1e4)),
                              float(dims.get("rms_eps", 1e-6)))

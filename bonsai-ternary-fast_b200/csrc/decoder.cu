@@ -360,18 +360,28 @@ struct Binder {
     return btf_gguf_tensor(g, i, t) == BTF_OK;
   }
   // A PTQ1_0 matrix [out][in] -> panels, with its input transform (model.cpp:29-58).
-  int mat(const std::string& name, Mat* m) {
+  // Under tensor parallelism only this rank's rows are loaded (shard = false:
+  // the embedding table, which every rank reads whole).
+  int mat(const std::string& name, Mat* m, bool shard = true) {
     btf_gguf_tensor_info t;
     int64_t idx = -1;
     if (!tensor(name, &t, &idx)) return fail(BTF_ERR_ARG, "btf_decoder: missing tensor %s", name.c_str());
     if (t.type != kPTQ || t.n_dims != 2) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: %s is not a 2-D PTQ1_0 matrix", name.c_str());
     m->K = (int)t.ne[0];
     m->N = (int)t.ne[1];
+    m->row0 = 0;
+    m->n = m->N;
+    if (shard && D.world > 1) {
+      shard_rows(m->N, D.world, D.rank, &m->row0, &m->n);
+      int lr0 = 0, ln = 0;
+      shard_rows(m->N, D.world, D.world - 1, &lr0, &ln);
+      if (ln <= 0) return fail(BTF_ERR_ARG, "btf_decoder: %s has too few rows for %d ranks", name.c_str(), D.world);
+    }
     int rc = BTF_OK;
-    m->pan = D.alloc<uint8_t>(btf_panel_bytes(m->N, m->K), &rc);
+    m->pan = D.alloc<uint8_t>(btf_panel_bytes(m->n, m->K), &rc);
     if (rc) return rc;
-    BTF_TRY(btf_gguf_load_panels(g, idx, m->pan, 64 << 20, D.st));
-    D.weight_bytes += btf_panel_bytes(m->N, m->K);
+    BTF_TRY(btf_gguf_load_panels_rows(g, idx, m->row0, m->n, m->pan, 64 << 20, D.st));
+    D.weight_bytes += btf_panel_bytes(m->n, m->K);
     if (folded.count(name)) {
       if (m->K % block) return fail(BTF_ERR_ARG, "btf_decoder: %s width not a multiple of the hadamard block", name.c_str());
       m->hx.block = block;
@@ -495,7 +505,7 @@ struct Binder {
     // embedding (never transformed on lookup), output norm, lm_head
     const bool embd_folded = folded.count("token_embd.weight") != 0;
     folded.erase("token_embd.weight");
-    BTF_TRY(mat("token_embd.weight", &D.embd));
+    BTF_TRY(mat("token_embd.weight", &D.embd, false));
     D.weight_bytes -= btf_panel_bytes(D.embd.N, D.embd.K);  // one row per step is read, counted below
     D.weight_bytes += (uint64_t)D.embd.K / 4 + (uint64_t)D.embd.K / 64;
     d.n_vocab = D.embd.N;
@@ -590,11 +600,15 @@ using namespace btf;
 
 extern "C" {
 
-int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void** handle) {
+int btf_decoder_open_tp(const char* gguf_path, const btf_decoder_opts* opts, int world, int rank, void** handle) {
   if (!gguf_path || !handle) return fail(BTF_ERR_ARG, "btf_decoder_open: null argument");
+  if (world < 1 || world > BTF_MAX_RANKS || rank < 0 || rank >= world)
+    return fail(BTF_ERR_ARG, "btf_decoder_open: need 1 <= world <= %d and 0 <= rank < world", BTF_MAX_RANKS);
   *handle = nullptr;
   auto D = std::make_unique<Decoder>();
   D->o = defaults(opts);
+  D->world = world;
+  D->rank = rank;
   if (cudaGetDevice(&D->device) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_open: no device");
   if (int rc = btf_init(D->device)) return rc;
   if (cudaStreamCreateWithFlags(&D->st, cudaStreamNonBlocking) != cudaSuccess)
@@ -606,9 +620,13 @@ int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void**
   btf_gguf_close(g);
   if (rc) return rc;
   BTF_TRY(finish_open(*D));
-  D->connected = true;
+  D->connected = world == 1;
   *handle = D.release();
   return BTF_OK;
+}
+
+int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void** handle) {
+  return btf_decoder_open_tp(gguf_path, opts, 1, 0, handle);
 }
 
 int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, int world,

@@ -277,19 +277,31 @@ int btf_gguf_tensor(const void* handle, int64_t index, btf_gguf_tensor_info* out
 
 int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_t staging_bytes, void* stream) {
   const File* f = static_cast<const File*>(handle);
+  if (!f || index < 0 || index >= (int64_t)f->tensors.size())
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_load_panels: bad handle or index");
+  return btf_gguf_load_panels_rows(handle, index, 0, f->tensors[(size_t)index].ne[1], panels, staging_bytes, stream);
+}
+
+int btf_gguf_load_panels_rows(const void* handle, int64_t index, int64_t row0, int64_t rows, void* panels,
+                              int64_t staging_bytes, void* stream) {
+  const File* f = static_cast<const File*>(handle);
   if (!f || !panels || index < 0 || index >= (int64_t)f->tensors.size())
     return btf::fail(BTF_ERR_ARG, "btf_gguf_load_panels: bad handle, index or panel buffer");
   const Tensor& t = f->tensors[(size_t)index];
   if (t.type != kTypePtq1_0 || t.n_dims != 2)
     return btf::fail(BTF_ERR_UNSUPPORTED, "btf_gguf_load_panels: %s is not a 2-D PTQ1_0 tensor", t.name.c_str());
-  const int64_t K = t.ne[0], N = t.ne[1];
+  const int64_t K = t.ne[0], NT = t.ne[1];
+  if (row0 < 0 || row0 % 8 || rows <= 0 || row0 + rows > NT)
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_load_panels: rows [%lld, %lld) of %lld (row0 a multiple of 8)",
+                     (long long)row0, (long long)(row0 + rows), (long long)NT);
+  const int64_t N = rows;  // the rows loaded, written from panel row group 0
   const int64_t row_bytes = K / 128 * 28, S = (K + 1023) / 1024;
   // whole 8-row groups per chunk, so every chunk starts a panel row group; no
   // chunk larger than the tensor (a small tensor gets small staging buffers)
   const int64_t rows_per =
       std::min<int64_t>((N + 7) / 8 * 8, std::max<int64_t>(8, staging_bytes / row_bytes / 8 * 8));
   const size_t stage = (size_t)(rows_per * row_bytes);
-  const uint8_t* src = f->map + f->data_start + t.offset;
+  const uint8_t* src = f->map + f->data_start + t.offset + row0 * row_bytes;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // two pinned staging buffers, read by the repack kernel over the bus (mapped)
   void* buf[2] = {nullptr, nullptr};
@@ -303,14 +315,14 @@ int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_
   if (e != cudaSuccess) rc = btf::cuda_fail(e, "btf_gguf_load_panels: staging");
   int slot = 0;
   for (int64_t r0 = 0; r0 < N && rc == BTF_OK; r0 += rows_per, slot ^= 1) {
-    const int64_t rows = std::min(rows_per, N - r0);
+    const int64_t nr = std::min(rows_per, N - r0);
     if ((e = cudaEventSynchronize(ev[slot])) != cudaSuccess) {  // this buffer's previous repack is done
       rc = btf::cuda_fail(e, "btf_gguf_load_panels: staging wait");
       break;
     }
-    std::memcpy(buf[slot], src + r0 * row_bytes, (size_t)(rows * row_bytes));
+    std::memcpy(buf[slot], src + r0 * row_bytes, (size_t)(nr * row_bytes));
     uint8_t* dst = static_cast<uint8_t*>(panels) + (r0 / 8) * S * BTF_PANEL_BYTES;
-    if ((rc = btf_repack_panels(buf[slot], rows, K, dst, stream)) != BTF_OK) break;
+    if ((rc = btf_repack_panels(buf[slot], nr, K, dst, stream)) != BTF_OK) break;
     if ((e = cudaEventRecord(ev[slot], st)) != cudaSuccess) rc = btf::cuda_fail(e, "btf_gguf_load_panels: record");
   }
   if ((e = cudaStreamSynchronize(st)) != cudaSuccess && rc == BTF_OK) rc = btf::cuda_fail(e, "btf_gguf_load_panels");

@@ -252,6 +252,10 @@ int btf_gguf_tensor(const void* handle, int64_t index, btf_gguf_tensor_info* out
  * buffers of about staging_bytes and repacked on the GPU as they arrive.
  * Returns after the panels are complete. */
 int btf_gguf_load_panels(const void* handle, int64_t index, void* panels, int64_t staging_bytes, void* stream);
+/* Rows [row0, row0 + rows) of the tensor (row0 a multiple of 8) into panels of a
+ * rows x K matrix (btf_panel_bytes(rows, K)): one rank's shard of an N-sharded matrix. */
+int btf_gguf_load_panels_rows(const void* handle, int64_t index, int64_t row0, int64_t rows, void* panels,
+                              int64_t staging_bytes, void* stream);
 
 /* ---- batch-1 decode step of the qwen35 hybrid decoder (gated delta net + gated
  * full attention) as one CUDA graph: the decode path the ternary GEMV serves.
@@ -305,6 +309,9 @@ int btf_decoder_get_info(void* handle, btf_decoder_info* out);
  * rank has synchronised (no rank still stores into another's arena). */
 int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, int world,
                              int rank, void** handle);
+/* The same from a qwen35 GGUF: rank `rank` loads its rows of every matrix
+ * (btf_gguf_load_panels_rows) and the whole embedding table. */
+int btf_decoder_open_tp(const char* gguf_path, const btf_decoder_opts* opts, int world, int rank, void** handle);
 /* The row shard of `rank` among `world` that the tensor-parallel decoder uses for
  * an N-row matrix: whole 8-row groups, ceil(groups / world) groups per rank, the
  * last ranks clipped (rows may be 0 for small N). Host-only. */

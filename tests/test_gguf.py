@@ -71,3 +71,29 @@ def test_load_panels_on_device_equals_host_twin(cuda, btf, staging):
             pm = g.load_panels(i, staging_bytes=staging)
             host = btf.repack_panels_host(g.data(i).reshape(t["ne1"], -1), t["ne1"], t["ne0"])
             assert np.array_equal(pm.panels.cpu().numpy(), host)
+
+
+def test_load_rows_rejects_bad_ranges(btf):
+    # the row-range checks run before any device access
+    L = btf.lib()
+    with btf.GgufFile(PATH) as g:
+        i = g.find("blk.0.ffn_up.weight")  # 37 rows
+        for row0, rows in ((4, 8), (0, 0), (32, 8), (-8, 8), (40, 1)):  # row0 % 8, empty, past the end, negative
+            assert L.btf_gguf_load_panels_rows(g.h, i, row0, rows, 256, 1 << 20, None) == 1, (row0, rows)
+        j = g.find("output_norm.weight")  # not PTQ1_0
+        assert L.btf_gguf_load_panels_rows(g.h, j, 0, 1, 256, 1 << 20, None) == 3
+
+
+@pytest.mark.gpu
+def test_load_rows_equals_the_full_load(cuda, btf):
+    # one rank's shard: rows [8, 8 + n) of a 37-row tensor land in panel row
+    # groups 0.. exactly as groups 1.. of the full load; a ragged tail (n = 29)
+    # ends like the full matrix's last group
+    with btf.GgufFile(PATH) as g:
+        i = g.find("blk.0.ffn_up.weight")
+        full = g.load_panels(i).panels.cpu().numpy()
+        gbytes = btf.panel_bytes(8, 1152)  # one row group of all slices
+        for row0, n in ((8, 16), (16, 8), (8, 29)):
+            part = g.load_panels(i, rows=(row0, n)).panels.cpu().numpy()
+            assert part.size == btf.panel_bytes(n, 1152)
+            assert np.array_equal(part, full[row0 // 8 * gbytes:row0 // 8 * gbytes + part.size]), (row0, n)
