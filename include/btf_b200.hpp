@@ -3,7 +3,7 @@
 // written against btf::cuda (e.g. src/cuda/gpu_decoder.cu:396-450) compile
 // unchanged; errors throw std::runtime_error like the reference's launchers.
 //
-// Differences a maintainer must know (see INTEGRATION.md):
+// Differences a maintainer must know:
 //   - GemvSeg::codes points at the PANEL buffer of the matrix (include/btf_b200.h)
 //     and GemvSeg::scales must be nullptr: the scales live inside the panels;
 //   - launch_repack keeps the reference's T2 output; launch_repack_panels is the
