@@ -298,7 +298,7 @@ int btf_decoder_reset(void* handle);
 int btf_decoder_close(void* handle);
 int btf_decoder_get_info(void* handle, btf_decoder_info* out);
 
-/* Tensor-parallel decode (row f4): every ternary matmul of the step is N-sharded
+/* Tensor-parallel decode: every ternary matmul of the step is N-sharded
  * over `world` GPUs (one process each; rank r holds rows shard r of every matrix,
  * whole 8-row groups) and its outputs are stored into every rank's activation
  * arena by btf_gemv_gather (counted completion); the rest of the step runs
