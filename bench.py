@@ -1,6 +1,6 @@
 """Benchmark of the ternary GEMV hot path (one JSON line on rank 0).
 
-Workload (per-layer shape set at batch 1): a step is
+Workload (benchmark configuration 1, per-layer shape set at batch 1): a step is
 one pass over a 64-layer model's ternary matmuls at batch 1. Every layer holds
 its own resident weights of the seven config-1 shapes (q 5120->6144, k/v
 5120->1024, o 6144->5120, gate/up 5120->17408, down 17408->5120; 5.8 GB in

@@ -198,7 +198,7 @@ def test_gemv_rejects_bad_arguments(cuda, btf):
 
 @pytest.mark.parametrize("M", [1, 16])
 def test_lm_head_shape_row_subsets(cuda, btf, orc, M):
-    # BASELINE configuration 4's lm_head, 5120 -> 248320 (31040 row groups; M=16 runs as
+    # benchmark configuration 4's lm_head, 5120 -> 248320 (31040 row groups; M=16 runs as
     # four 4-row passes), checked on rows from the first, a middle and the last row groups
     import torch
 
