@@ -18,6 +18,22 @@ for p in (ROOT, PKG, os.path.join(ROOT, "oracle")):
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
+# the reference's decoder-test prompt (tests/test_common.hpp:67-70)
+DECODER_PROMPT = [259, 272, 44, 32, 259, 261, 103, 97, 264]
+
+# synthetic qwen35 models (bd::make_synth_qwen35 options over the defaults):
+# the Hadamard variants the binding distinguishes, f32 alpha/beta, and the real
+# model's head geometry (head_dim 256, d_state 128, block 1024)
+DECODER_CONFIGS = {
+    "default (block 64)": dict(),
+    "identity signs": dict(explicit_signs=0),
+    "no hadamard": dict(hadamard=0),
+    "gdn v tiled": dict(gdn_v_grouped=0),
+    "f32 alpha/beta": dict(small_mat_type=0),
+    "real head geometry": dict(n_layer=4, n_embd=1024, n_ff=2048, n_head=4, n_head_kv=1, head_dim=256, n_rot=64,
+                               d_state=128, n_group=2, dt_rank=8, hadamard_block=1024),
+}
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")

@@ -12,22 +12,13 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import rel_rms
+from conftest import DECODER_CONFIGS as CONFIGS, DECODER_PROMPT, rel_rms
 
 pytestmark = pytest.mark.gpu
 
-PROMPT = [259, 272, 44, 32, 259, 261, 103, 97, 264]
+PROMPT = DECODER_PROMPT
 ABS_TOL = 2e-2
 
-CONFIGS = {
-    "default (block 64)": dict(),
-    "identity signs": dict(explicit_signs=0),
-    "no hadamard": dict(hadamard=0),
-    "gdn v tiled": dict(gdn_v_grouped=0),
-    "f32 alpha/beta": dict(small_mat_type=0),
-    "real head geometry": dict(n_layer=4, n_embd=1024, n_ff=2048, n_head=4, n_head_kv=1, head_dim=256, n_rot=64,
-                               d_state=128, n_group=2, dt_rank=8, hadamard_block=1024),
-}
 
 
 @pytest.mark.parametrize("label", list(CONFIGS))

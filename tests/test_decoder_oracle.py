@@ -1,19 +1,22 @@
-"""CPU checks of the whole-decoder oracle and of the GGUF metadata the decoder binds.
+"""CPU checks of the whole-decoder oracles and of the GGUF metadata the decoder binds.
 
-The decoder's oracle is the reference's CPU emulator of its CUDA decode step
-(src/emu_decoder.cpp, btf::make_emu_decoder) on the reference's synthetic
-qwen35 model (ref/bonsai-decoder/src/synth.cpp), both compiled from the
-reference's sources into oracle/_ref/libbtf_ref.so.
+Two oracles for the decode step:
+- the reference's CPU emulator of its CUDA decode step (src/emu_decoder.cpp,
+  btf::make_emu_decoder), compiled from the reference's sources into
+  oracle/_ref/libbtf_ref.so with its synthetic qwen35 writer
+  (ref/bonsai-decoder/src/synth.cpp);
+- oracle/decode.py, a restatement of that step over the plain-C oracle and
+  numpy, pinned here to the emulator's logits on every synthetic model the GPU
+  decoder is tested on.
 """
-import os
-
 import numpy as np
 import pytest
 
+import decode
 import oracle
+from conftest import DECODER_CONFIGS, DECODER_PROMPT, rel_rms
 
-# the reference's decoder-test prompt (tests/test_common.hpp:67-70)
-PROMPT = [259, 272, 44, 32, 259, 261, 103, 97, 264]
+PROMPT = DECODER_PROMPT
 
 
 def test_emulator_runs_and_is_deterministic(ref, tmp_path):
@@ -45,3 +48,72 @@ def test_gguf_metadata_of_the_synthetic_model(ref, btf, tmp_path):
         assert t["type"] == 30 and t["ne"] == [128, 4]  # BF16 [dt_rank][n_embd]
         t = g.tensor(g.find("blk.0.ffn_gate.weight"))
         assert t["type"] == btf.PTQ1_0 and t["ne"] == [128, 256]
+
+
+@pytest.mark.parametrize("label", list(DECODER_CONFIGS))
+def test_restated_decode_step_matches_the_emulator(orc, ref, tmp_path, label):
+    # prompt, then 15 greedy steps fed back: the restatement reproduces the
+    # emulator's logits bit for bit (same C library transcendentals, same
+    # float32 summation order, the pinned C oracle for prep, Q8 and GEMV)
+    cfg = dict(DECODER_CONFIGS[label])
+    n_layer = cfg.pop("n_layer", 8)
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=n_layer, seed=1, **cfg)
+    emu = oracle.Emulator(ref, path, n_ctx=32, threads=1)
+    dec = decode.DecodeOracle(orc, path, n_ctx=32)
+    assert dec.V == emu.hp["n_vocab"] and dec.L == n_layer and dec.DI == emu.hp["d_inner"]
+    tok, first = None, None
+    for i in range(len(PROMPT) + 15):
+        t = PROMPT[i] if i < len(PROMPT) else tok
+        ne, le = emu.step(t)
+        nd, ld = dec.step(t)
+        first = ld if first is None else first
+        assert np.array_equal(ld, le), f"step {i}: logits differ, rel-rms {rel_rms(ld, le):.3e}"
+        assert nd == ne
+        tok = ne
+    emu.close()
+    # reset clears the conv, delta-rule and KV state: the first step repeats
+    dec.reset()
+    assert np.array_equal(dec.step(PROMPT[0])[1], first)
+
+
+@pytest.mark.parametrize("plant", ["no q rounding", "no bf16 alpha/beta", "no v regrouping"])
+def test_pin_detects_a_planted_mistake(orc, ref, tmp_path, plant):
+    # the bit-exact pin is sensitive: one planted deviation in the restatement
+    # (never in the product) shows up in the logits within the prompt
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=8, seed=1)
+    emu = oracle.Emulator(ref, path, n_ctx=16, threads=1)
+    dec = decode.DecodeOracle(orc, path, n_ctx=16, round_q_f16=plant != "no q rounding")
+    for lay in dec.layers:
+        if plant == "no bf16 alpha/beta" and lay["rec"]:
+            lay["ab_bf16"] = False
+        if plant == "no v regrouping" and lay["rec"]:
+            block, perm, signs = lay["out"].hx
+            lay["out"].hx = (block, (0, 0, 0), signs)
+    differs = [not np.array_equal(dec.step(t)[1], emu.step(t)[1]) for t in PROMPT]
+    emu.close()
+    assert any(differs)
+
+
+def test_restated_decode_step_rejects_like_the_emulator(orc, ref, tmp_path):
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=4, seed=2)
+    dec = decode.DecodeOracle(orc, path, n_ctx=2)
+    with pytest.raises(ValueError):
+        dec.step(dec.V)
+    dec.step(1)
+    dec.step(2)
+    with pytest.raises(RuntimeError):
+        dec.step(3)  # context full
+
+
+def test_restated_gguf_reader_agrees_with_the_library(btf, ref, tmp_path):
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=4, seed=3)
+    kv, ts = decode.read_gguf(path)
+    assert kv["general.architecture"] == "qwen35" and kv["qwen35.block_count"] == 4
+    with btf.GgufFile(path) as g:
+        for name, (t, ne, raw) in ts.items():
+            info = g.tensor(g.find(name))
+            assert info["type"] == t and info["ne"] == ne, name
