@@ -38,6 +38,7 @@ EXPORTS = (
     "btf_gguf_load_panels", "btf_decoder_open", "btf_decoder_synthetic", "btf_decoder_step", "btf_decoder_run",
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
+    "btf_plan_memory", "btf_plan_memory_synthetic",
 )
 
 
@@ -104,7 +105,16 @@ class DecoderDimsC(ctypes.Structure):
 class DecoderInfoC(ctypes.Structure):
     _fields_ = [("dims", DecoderDimsC), ("pos", ctypes.c_int), ("stream", ctypes.c_void_p),
                 ("weight_bytes", ctypes.c_uint64), ("state_bytes", ctypes.c_uint64),
-                ("kv_bytes_per_token", ctypes.c_uint64), ("logits", ctypes.c_void_p)]
+                ("kv_bytes_per_token", ctypes.c_uint64), ("logits", ctypes.c_void_p), ("device_bytes", ctypes.c_uint64)]
+
+
+PLAN_FIELDS = ("panel_bytes", "vector_bytes", "kv_cache_bytes", "state_bytes", "work_bytes", "device_bytes",
+               "pinned_bytes", "staging_bytes", "decode_bytes_fixed", "decode_bytes_per_ctx")
+
+
+class MemoryPlanC(ctypes.Structure):
+    """btf_memory_plan (btf::MemoryPlan, include/btf/fast.hpp:50-69, for the panel layout)."""
+    _fields_ = [(f, ctypes.c_uint64) for f in PLAN_FIELDS] + [("n_matrices", ctypes.c_int), ("dims", DecoderDimsC)]
 
 
 def lib() -> ctypes.CDLL:
@@ -167,6 +177,9 @@ def lib() -> ctypes.CDLL:
         "btf_shard_rows": (i32, [i32, i32, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
         "btf_decoder_open_tp": (i32, [ctypes.c_char_p, ctypes.POINTER(DecoderOptsC), i32, i32, ctypes.POINTER(vp)]),
         "btf_gguf_load_panels_rows": (i32, [vp, i64, i64, i64, vp, i64, vp]),
+        "btf_plan_memory": (i32, [ctypes.c_char_p, ctypes.POINTER(DecoderOptsC), i32, i32, ctypes.POINTER(MemoryPlanC)]),
+        "btf_plan_memory_synthetic": (i32, [ctypes.POINTER(DecoderDimsC), ctypes.POINTER(DecoderOptsC), i32, i32,
+                                            ctypes.POINTER(MemoryPlanC)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -477,6 +490,44 @@ class GgufFile:
         return PanelMatrix(out, n, K)
 
 
+def _dims_c(dims: dict) -> DecoderDimsC:
+    return DecoderDimsC(*[int(dims.get(f, 0)) for f in DIM_FIELDS], float(dims.get("rope_base", 1e4)),
+                        float(dims.get("rms_eps", 1e-6)))
+
+
+def plan_memory(path: Optional[str] = None, dims: Optional[dict] = None, n_ctx: int = 4096, attn_splits: int = 16,
+                world: int = 1, rank: int = 0) -> dict:
+    """btf_plan_memory: the device and pinned memory a Decoder with these
+    arguments would allocate on `rank`, and the bytes one decode step reads
+    (btf::plan_memory, src/repack.cpp:142-204). Host only: needs no GPU."""
+    o = DecoderOptsC(n_ctx, 1, attn_splits, 1)
+    p = MemoryPlanC()
+    if path is not None:
+        check(lib().btf_plan_memory(path.encode(), ctypes.byref(o), world, rank, ctypes.byref(p)), "btf_plan_memory")
+    else:
+        check(lib().btf_plan_memory_synthetic(ctypes.byref(_dims_c(dims)), ctypes.byref(o), world, rank,
+                                              ctypes.byref(p)), "btf_plan_memory_synthetic")
+    r = {f: int(getattr(p, f)) for f in PLAN_FIELDS}
+    r["n_matrices"] = p.n_matrices
+    r["dims"] = {f: getattr(p.dims, f) for f in DIM_FIELDS}
+    return r
+
+
+def plan_table(plan: dict) -> str:
+    """Human-readable plan, one line per item (MemoryPlan::table, src/repack.cpp:125-140)."""
+    rows = [(f"ternary matrices in panels ({plan['n_matrices']})", plan["panel_bytes"], "device"),
+            ("f32 vectors (norms, ssm, conv1d, signs)", plan["vector_bytes"], "device"),
+            ("KV cache fp16", plan["kv_cache_bytes"], "device"),
+            ("delta-net + conv state", plan["state_bytes"], "device"),
+            ("activations, partials, Q8, argmax", plan["work_bytes"], "device"),
+            ("token in/out", plan["pinned_bytes"], "host"),
+            ("load staging (peak, freed after load)", plan["staging_bytes"], "host")]
+    out = [f"  {w:<44s} {k:<6s} {b:>14d} B  {b / 1048576.0:9.2f} MiB" for w, b, k in rows]
+    dev = plan["device_bytes"]
+    out.append(f"  {'total resident':<44s} {'device':<6s} {dev:>14d} B  {dev / 1048576.0:9.2f} MiB ({dev / 1e9:.3f} GB)")
+    return "\n".join(out) + "\n"
+
+
 class Decoder:
     """The batch-1 qwen35 decode step (btf_decoder_*): from a GGUF file or from
     seeded synthetic weights of a given geometry (a dict of DIM_FIELDS plus
@@ -494,8 +545,7 @@ class Decoder:
             check(lib().btf_decoder_open_tp(path.encode(), ctypes.byref(o), world, rank, ctypes.byref(h)),
                   "btf_decoder_open")
         else:
-            d = DecoderDimsC(*[int(dims.get(f, 0)) for f in DIM_FIELDS], float(dims.get("rope_base", 1e4)),
-                             float(dims.get("rms_eps", 1e-6)))
+            d = _dims_c(dims)
             check(lib().btf_decoder_synthetic_tp(ctypes.byref(d), seed, ctypes.byref(o), world, rank, ctypes.byref(h)),
                   "btf_decoder_synthetic")
         self.h = h.value
@@ -538,7 +588,7 @@ class Decoder:
         r = {f: getattr(i.dims, f) for f in DIM_FIELDS}
         r.update(rope_base=i.dims.rope_base, rms_eps=i.dims.rms_eps, pos=i.pos, stream=i.stream,
                  weight_bytes=int(i.weight_bytes), state_bytes=int(i.state_bytes),
-                 kv_bytes_per_token=int(i.kv_bytes_per_token), logits=i.logits)
+                 kv_bytes_per_token=int(i.kv_bytes_per_token), logits=i.logits, device_bytes=int(i.device_bytes))
         return r
 
     def step(self, token: int, logits: bool = False):

@@ -31,6 +31,7 @@ namespace btf {
 namespace {
 
 constexpr uint32_t kF32 = 0, kF16 = 1, kBF16 = 30, kPTQ = 143;
+constexpr int64_t kStaging = 64 << 20;  // source bytes per chunk of a matrix load
 
 struct Mat {
   uint8_t* pan = nullptr;
@@ -90,6 +91,14 @@ struct Decoder {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   uint64_t weight_bytes = 0, state_bytes = 0, kv_bytes_per_token = 0;
+  // Memory plan (btf_plan_memory): every device allocation by kind. A dry
+  // decoder runs the same binding and buffer set-up, sizes every allocation
+  // and touches no device: no allocation, copy, fill or launch.
+  enum Kind { kPanels, kVectors, kKv, kState, kWork, kKinds };
+  bool dry = false;
+  uint64_t dev_bytes[kKinds] = {};
+  uint64_t sign_bytes = 0, staging_peak = 0;
+  int n_mats = 0;
   static constexpr int kArgmaxParts = 148;
   // tensor parallelism: every matmul N-sharded over `world` ranks, its outputs
   // stored into every rank's arena (btf_gemv_gather, counted completion). The
@@ -112,16 +121,24 @@ struct Decoder {
     if (st) cudaStreamDestroy(st);
   }
   template <class T>
-  T* alloc(size_t n, int* rc) {
+  T* alloc(size_t n, int* rc, Kind kind = kWork) {
     void* p = nullptr;
     if (*rc) return nullptr;
-    const cudaError_t e = cudaMalloc(&p, n * sizeof(T) > 0 ? n * sizeof(T) : 16);
+    const size_t bytes = n * sizeof(T) > 0 ? n * sizeof(T) : 16;
+    dev_bytes[kind] += bytes;
+    if (dry) return nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
     if (e != cudaSuccess) {
       *rc = cuda_fail(e, "btf_decoder: cudaMalloc");
       return nullptr;
     }
     allocs.push_back(p);
     return static_cast<T*>(p);
+  }
+  uint64_t device_total() const {
+    uint64_t t = 0;
+    for (uint64_t b : dev_bytes) t += b;
+    return t;
   }
 };
 
@@ -147,9 +164,10 @@ int make_buffers(Decoder& D) {
   D.arena = D.alloc<uint8_t>(total, &rc);
   if (rc) return rc;
   D.arena_bytes = total;
-  if (cudaMemset(D.arena, 0, total) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder: arena clear");
+  if (!D.dry && cudaMemset(D.arena, 0, total) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder: arena clear");
   float** dst[9] = {&D.x, &D.xn, &D.bA, &D.bB, &D.bC, &D.bO, &D.bQ, &D.bG, &D.logits};
-  for (int i = 0; i < 9; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
+  if (!D.dry)
+    for (int i = 0; i < 9; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
   D.peers[D.rank] = D.arena;
   D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
   D.amax_v = D.alloc<float>(Decoder::kArgmaxParts, &rc);
@@ -159,20 +177,22 @@ int make_buffers(Decoder& D) {
   D.as = D.alloc<int32_t>(D.Kmax / 32, &rc);
   D.d_tok = D.alloc<int32_t>(4, &rc);
   if (rc) return rc;
-  D.d_pos = D.d_tok + 1;
-  D.d_next = D.d_tok + 2;
+  if (!D.dry) {
+    D.d_pos = D.d_tok + 1;
+    D.d_next = D.d_tok + 2;
+  }
   for (Layer& l : D.L) {
     if (l.rec) {
-      l.conv_state = D.alloc<float>((size_t)d.conv_kernel * D.C, &rc);  // ring of K input rows
-      l.ssm_state = D.alloc<float>((size_t)D.NV * D.DV * D.DK, &rc);
+      l.conv_state = D.alloc<float>((size_t)d.conv_kernel * D.C, &rc, Decoder::kState);  // ring of K input rows
+      l.ssm_state = D.alloc<float>((size_t)D.NV * D.DV * D.DK, &rc, Decoder::kState);
       D.state_bytes += 2 * ((uint64_t)(d.conv_kernel - 1) * D.C + (uint64_t)D.NV * D.DV * D.DK) * 4;
     } else {
-      l.kc = D.alloc<__half>((size_t)D.o.n_ctx * HK * HD, &rc);
-      l.vc = D.alloc<__half>((size_t)D.o.n_ctx * HK * HD, &rc);
+      l.kc = D.alloc<__half>((size_t)D.o.n_ctx * HK * HD, &rc, Decoder::kKv);
+      l.vc = D.alloc<__half>((size_t)D.o.n_ctx * HK * HD, &rc, Decoder::kKv);
       D.kv_bytes_per_token += 2ull * HK * HD * 2;
     }
   }
-  if (rc) return rc;
+  if (rc || D.dry) return rc;
   const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&D.h_io), 4 * sizeof(int32_t), cudaHostAllocDefault);
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder: pinned io");
 }
@@ -305,9 +325,11 @@ int run_step(Decoder& D) {
 
 // ---------------------------------------------------------------- weights
 int upload_f32(Decoder& D, const void* src, uint32_t type, int64_t n, float** out) {
+  if (type != kF32 && type != kBF16 && type != kF16)
+    return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: vector tensor of type %u", type);
   int rc = BTF_OK;
-  float* p = D.alloc<float>(n, &rc);
-  if (rc) return rc;
+  float* p = D.alloc<float>(n, &rc, Decoder::kVectors);
+  if (rc || D.dry) return rc;
   std::vector<float> h(n);
   const uint16_t* s16 = static_cast<const uint16_t*>(src);
   if (type == kF32) {
@@ -369,6 +391,7 @@ struct Binder {
     if (t.type != kPTQ || t.n_dims != 2) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: %s is not a 2-D PTQ1_0 matrix", name.c_str());
     m->K = (int)t.ne[0];
     m->N = (int)t.ne[1];
+    if (m->K % 128) return fail(BTF_ERR_ARG, "btf_decoder: %s width %d is not a multiple of 128", name.c_str(), m->K);
     m->row0 = 0;
     m->n = m->N;
     if (shard && D.world > 1) {
@@ -378,9 +401,15 @@ struct Binder {
       if (ln <= 0) return fail(BTF_ERR_ARG, "btf_decoder: %s has too few rows for %d ranks", name.c_str(), D.world);
     }
     int rc = BTF_OK;
-    m->pan = D.alloc<uint8_t>(btf_panel_bytes(m->n, m->K), &rc);
+    m->pan = D.alloc<uint8_t>(btf_panel_bytes(m->n, m->K), &rc, Decoder::kPanels);
     if (rc) return rc;
-    BTF_TRY(btf_gguf_load_panels_rows(g, idx, m->row0, m->n, m->pan, 64 << 20, D.st));
+    D.n_mats += 1;
+    if (D.dry) {
+      // the loader's two pinned staging buffers, freed after each matrix
+      D.staging_peak = std::max<uint64_t>(D.staging_peak, 2 * gguf::staging_buffer_bytes(m->K, m->n, kStaging));
+    } else {
+      BTF_TRY(btf_gguf_load_panels_rows(g, idx, m->row0, m->n, m->pan, kStaging, D.st));
+    }
     D.weight_bytes += btf_panel_bytes(m->n, m->K);
     if (folded.count(name)) {
       if (m->K % block) return fail(BTF_ERR_ARG, "btf_decoder: %s width not a multiple of the hadamard block", name.c_str());
@@ -484,9 +513,10 @@ struct Binder {
             h[i] = (float)v;
           }
           int rc = BTF_OK;
-          float* dv = D.alloc<float>(width, &rc);
+          float* dv = D.alloc<float>(width, &rc, Decoder::kVectors);
           if (rc) return rc;
-          if (cudaMemcpy(dv, h.data(), width * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+          D.sign_bytes += (uint64_t)width * 4;
+          if (!D.dry && cudaMemcpy(dv, h.data(), width * 4, cudaMemcpyHostToDevice) != cudaSuccess)
             return fail(BTF_ERR_CUDA, "btf_decoder: sign upload");
           signs[(int)width] = dv;
           off += width;
@@ -584,13 +614,44 @@ int finish_open(Decoder& D) {
   BTF_TRY(check_dims(D));
   D.theta_scale = std::pow(D.d.rope_base, -2.0f / (float)D.d.n_rot);
   BTF_TRY(make_buffers(D));
-  return reset_state(D);
+  return D.dry ? BTF_OK : reset_state(D);
 }
 
 btf_decoder_opts defaults(const btf_decoder_opts* o) {
   btf_decoder_opts r{4096, 1, 16, 1};
   if (o) r = *o;
   return r;
+}
+
+// The decoder's device, library state and stream (nothing for a dry decoder).
+int device_setup(Decoder& D, const char* who) {
+  if (D.dry) return BTF_OK;
+  if (cudaGetDevice(&D.device) != cudaSuccess) return fail(BTF_ERR_CUDA, "%s: no device", who);
+  if (int rc = btf_init(D.device)) return rc;
+  if (cudaStreamCreateWithFlags(&D.st, cudaStreamNonBlocking) != cudaSuccess) return fail(BTF_ERR_CUDA, "%s: stream", who);
+  return BTF_OK;
+}
+
+// Binds a qwen35 GGUF: loads this rank's weights and allocates the step buffers
+// (a dry decoder only sizes them).
+int open_gguf(Decoder& D, const char* path) {
+  BTF_TRY(device_setup(D, "btf_decoder_open"));
+  void* g = nullptr;
+  BTF_TRY(btf_gguf_open(path, &g));
+  Binder b{D, g};
+  const int rc = b.bind();
+  btf_gguf_close(g);
+  if (rc) return rc;
+  return finish_open(D);
+}
+
+// Seeded synthetic weights of geometry R.d on this rank (a dry decoder only sizes them).
+int build_synthetic(Decoder& R, uint64_t seed);
+
+int check_tp(int world, int rank, const char* who) {
+  if (world < 1 || world > BTF_MAX_RANKS || rank < 0 || rank >= world)
+    return fail(BTF_ERR_ARG, "%s: need 1 <= world <= %d and 0 <= rank < world", who, BTF_MAX_RANKS);
+  return BTF_OK;
 }
 
 }  // namespace
@@ -602,24 +663,13 @@ extern "C" {
 
 int btf_decoder_open_tp(const char* gguf_path, const btf_decoder_opts* opts, int world, int rank, void** handle) {
   if (!gguf_path || !handle) return fail(BTF_ERR_ARG, "btf_decoder_open: null argument");
-  if (world < 1 || world > BTF_MAX_RANKS || rank < 0 || rank >= world)
-    return fail(BTF_ERR_ARG, "btf_decoder_open: need 1 <= world <= %d and 0 <= rank < world", BTF_MAX_RANKS);
+  BTF_TRY(check_tp(world, rank, "btf_decoder_open"));
   *handle = nullptr;
   auto D = std::make_unique<Decoder>();
   D->o = defaults(opts);
   D->world = world;
   D->rank = rank;
-  if (cudaGetDevice(&D->device) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_open: no device");
-  if (int rc = btf_init(D->device)) return rc;
-  if (cudaStreamCreateWithFlags(&D->st, cudaStreamNonBlocking) != cudaSuccess)
-    return fail(BTF_ERR_CUDA, "btf_decoder_open: stream");
-  void* g = nullptr;
-  BTF_TRY(btf_gguf_open(gguf_path, &g));
-  Binder b{*D, g};
-  const int rc = b.bind();
-  btf_gguf_close(g);
-  if (rc) return rc;
-  BTF_TRY(finish_open(*D));
+  BTF_TRY(open_gguf(*D, gguf_path));
   D->connected = world == 1;
   *handle = D.release();
   return BTF_OK;
@@ -632,25 +682,33 @@ int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void**
 int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, int world,
                              int rank, void** handle) {
   if (!dims || !handle) return fail(BTF_ERR_ARG, "btf_decoder_synthetic: null argument");
-  if (world < 1 || world > BTF_MAX_RANKS || rank < 0 || rank >= world)
-    return fail(BTF_ERR_ARG, "btf_decoder_synthetic: need 1 <= world <= %d and 0 <= rank < world", BTF_MAX_RANKS);
+  BTF_TRY(check_tp(world, rank, "btf_decoder_synthetic"));
   *handle = nullptr;
   auto D = std::make_unique<Decoder>();
-  Decoder& R = *D;
-  R.o = defaults(opts);
-  R.d = *dims;
-  R.world = world;
-  R.rank = rank;
+  D->o = defaults(opts);
+  D->d = *dims;
+  D->world = world;
+  D->rank = rank;
+  BTF_TRY(build_synthetic(*D, seed));
+  D->connected = world == 1;
+  *handle = D.release();
+  return BTF_OK;
+}
+
+}  // extern "C"
+
+namespace btf {
+namespace {
+
+int build_synthetic(Decoder& R, uint64_t seed) {
+  const int world = R.world, rank = R.rank;
   const btf_decoder_dims& d = R.d;
   if (d.n_layer <= 0 || d.n_head_kv <= 0 || d.n_head % d.n_head_kv || d.n_group <= 0 || d.dt_rank % d.n_group ||
       d.n_rot > d.head_dim || d.n_rot % 2 || d.n_vocab <= 0)
     return fail(BTF_ERR_ARG, "btf_decoder_synthetic: inconsistent dims");
   if (d.hadamard_block < 0 || (d.hadamard_block & (d.hadamard_block - 1)) || d.hadamard_block > 1024)
     return fail(BTF_ERR_ARG, "btf_decoder_synthetic: hadamard_block 0 or a power of two <= 1024");
-  if (cudaGetDevice(&R.device) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: no device");
-  if (int rc = btf_init(R.device)) return rc;
-  if (cudaStreamCreateWithFlags(&R.st, cudaStreamNonBlocking) != cudaSuccess)
-    return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: stream");
+  BTF_TRY(device_setup(R, "btf_decoder_synthetic"));
   if (R.d.d_inner == 0) R.d.d_inner = d.dt_rank * d.d_state;
   if (d.d_inner % d.dt_rank) return fail(BTF_ERR_ARG, "btf_decoder_synthetic: d_inner %% dt_rank");
   R.DK = d.d_state;
@@ -680,8 +738,9 @@ int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const 
       if (ln <= 0)
         return fail(BTF_ERR_ARG, "btf_decoder_synthetic: %d output rows leave a rank of %d without rows", N, world);
     }
-    m->pan = R.alloc<uint8_t>(btf_panel_bytes(m->n, K), &rc);
+    m->pan = R.alloc<uint8_t>(btf_panel_bytes(m->n, K), &rc, Decoder::kPanels);
     if (rc) return rc;
+    R.n_mats += 1;
     R.weight_bytes += btf_panel_bytes(m->n, K);
     if (blk) {
       m->hx.block = blk;
@@ -691,14 +750,18 @@ int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const 
         m->hx.perm_rep = R.NV / R.NK;
       }
     }
-    const cudaError_t e = launch_fill_panels(m->pan, m->row0, m->n, N, K, ++s, 1.0f / std::sqrt((float)K), R.st);
+    ++s;
+    if (R.dry) return BTF_OK;
+    const cudaError_t e = launch_fill_panels(m->pan, m->row0, m->n, N, K, s, 1.0f / std::sqrt((float)K), R.st);
     return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_synthetic: fill");
   };
   auto vec = [&](float** p, int64_t n, float base, float spread) -> int {
-    *p = R.alloc<float>(n, &rc);
+    *p = R.alloc<float>(n, &rc, Decoder::kVectors);
     if (rc) return rc;
     R.weight_bytes += n * 4;
-    const cudaError_t e = launch_fill_uniform(*p, n, ++s, base, spread, R.st);
+    ++s;
+    if (R.dry) return BTF_OK;
+    const cudaError_t e = launch_fill_uniform(*p, n, s, base, spread, R.st);
     return e == cudaSuccess ? BTF_OK : cuda_fail(e, "btf_decoder_synthetic: fill");
   };
   const int E = d.n_embd, F = d.n_ff, H = d.n_head, HK = d.n_head_kv, HD = d.head_dim;
@@ -737,12 +800,14 @@ int btf_decoder_synthetic_tp(const btf_decoder_dims* dims, uint64_t seed, const 
       BTF_TRY(vec(&l.k_norm, HD, 1.2f, 0.3f));
     }
   }
-  if (cudaStreamSynchronize(R.st) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: fill");
-  BTF_TRY(finish_open(R));
-  R.connected = world == 1;
-  *handle = D.release();
-  return BTF_OK;
+  if (!R.dry && cudaStreamSynchronize(R.st) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder_synthetic: fill");
+  return finish_open(R);
 }
+
+}  // namespace
+}  // namespace btf
+
+extern "C" {
 
 int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, void** handle) {
   return btf_decoder_synthetic_tp(dims, seed, opts, 1, 0, handle);
@@ -820,6 +885,64 @@ int btf_decoder_get_info(void* handle, btf_decoder_info* out) {
   out->state_bytes = D.state_bytes;
   out->kv_bytes_per_token = D.kv_bytes_per_token;
   out->logits = D.logits;
+  out->device_bytes = D.device_total();
+  return BTF_OK;
+}
+
+}  // extern "C"
+
+namespace btf {
+namespace {
+
+void fill_plan(const Decoder& D, btf_memory_plan* p) {
+  std::memset(p, 0, sizeof *p);
+  p->panel_bytes = D.dev_bytes[Decoder::kPanels];
+  p->vector_bytes = D.dev_bytes[Decoder::kVectors];
+  p->kv_cache_bytes = D.dev_bytes[Decoder::kKv];
+  p->state_bytes = D.dev_bytes[Decoder::kState];
+  p->work_bytes = D.dev_bytes[Decoder::kWork];
+  p->device_bytes = D.device_total();
+  p->pinned_bytes = 4 * sizeof(int32_t);
+  p->staging_bytes = D.staging_peak;
+  // every resident byte one step reads once (one embedding row, the weights,
+  // the sign vectors), the recurrent state read and written, the logits
+  // written and read by the argmax; plus the K and V rows per cached token
+  p->decode_bytes_fixed = D.weight_bytes + D.sign_bytes + D.state_bytes + 2ull * D.d.n_vocab * 4;
+  p->decode_bytes_per_ctx = D.kv_bytes_per_token;
+  p->n_matrices = D.n_mats;
+  p->dims = D.d;
+}
+
+}  // namespace
+}  // namespace btf
+
+extern "C" {
+
+int btf_plan_memory(const char* gguf_path, const btf_decoder_opts* opts, int world, int rank, btf_memory_plan* out) {
+  if (!gguf_path || !out) return fail(BTF_ERR_ARG, "btf_plan_memory: null argument");
+  BTF_TRY(check_tp(world, rank, "btf_plan_memory"));
+  Decoder D;
+  D.dry = true;
+  D.o = defaults(opts);
+  D.world = world;
+  D.rank = rank;
+  BTF_TRY(open_gguf(D, gguf_path));
+  fill_plan(D, out);
+  return BTF_OK;
+}
+
+int btf_plan_memory_synthetic(const btf_decoder_dims* dims, const btf_decoder_opts* opts, int world, int rank,
+                              btf_memory_plan* out) {
+  if (!dims || !out) return fail(BTF_ERR_ARG, "btf_plan_memory_synthetic: null argument");
+  BTF_TRY(check_tp(world, rank, "btf_plan_memory_synthetic"));
+  Decoder D;
+  D.dry = true;
+  D.o = defaults(opts);
+  D.d = *dims;
+  D.world = world;
+  D.rank = rank;
+  BTF_TRY(build_synthetic(D, 0));
+  fill_plan(D, out);
   return BTF_OK;
 }
 

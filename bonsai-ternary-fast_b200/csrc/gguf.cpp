@@ -291,15 +291,13 @@ int btf_gguf_load_panels_rows(const void* handle, int64_t index, int64_t row0, i
   if (t.type != kTypePtq1_0 || t.n_dims != 2)
     return btf::fail(BTF_ERR_UNSUPPORTED, "btf_gguf_load_panels: %s is not a 2-D PTQ1_0 tensor", t.name.c_str());
   const int64_t K = t.ne[0], NT = t.ne[1];
+  if (K % 128) return btf::fail(BTF_ERR_ARG, "btf_gguf_load_panels: %s width %lld is not a multiple of 128", t.name.c_str(), (long long)K);
   if (row0 < 0 || row0 % 8 || rows <= 0 || row0 + rows > NT)
     return btf::fail(BTF_ERR_ARG, "btf_gguf_load_panels: rows [%lld, %lld) of %lld (row0 a multiple of 8)",
                      (long long)row0, (long long)(row0 + rows), (long long)NT);
   const int64_t N = rows;  // the rows loaded, written from panel row group 0
   const int64_t row_bytes = K / 128 * 28, S = (K + 1023) / 1024;
-  // whole 8-row groups per chunk, so every chunk starts a panel row group; no
-  // chunk larger than the tensor (a small tensor gets small staging buffers)
-  const int64_t rows_per =
-      std::min<int64_t>((N + 7) / 8 * 8, std::max<int64_t>(8, staging_bytes / row_bytes / 8 * 8));
+  const int64_t rows_per = btf::gguf::staging_rows(K, N, staging_bytes);
   const size_t stage = (size_t)(rows_per * row_bytes);
   const uint8_t* src = f->map + f->data_start + t.offset + row0 * row_bytes;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -1,6 +1,8 @@
 // GGUF metadata as read by csrc/gguf.cpp, for the library's own model binding
-// (csrc/qwen35.cpp). Internal: not part of the C ABI.
+// (csrc/decoder.cu), and the load path's staging rule. Internal: not part of
+// the C ABI.
 #pragma once
+#include <algorithm>
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -23,6 +25,20 @@ struct Value {
 
 // Metadata entry `key` of a handle from btf_gguf_open, or nullptr.
 const Value* meta(const void* handle, const std::string& key);
+
+// Rows per chunk of btf_gguf_load_panels_rows for `rows` rows of a PTQ1_0
+// matrix of width K (a multiple of 128): whole 8-row groups, so every chunk
+// starts a panel row group; at most `chunk_bytes` of source per chunk but at
+// least one group; no chunk larger than the rows loaded.
+inline int64_t staging_rows(int64_t K, int64_t rows, int64_t chunk_bytes) {
+  const int64_t row_bytes = K / 128 * 28;
+  return std::min<int64_t>((rows + 7) / 8 * 8, std::max<int64_t>(8, chunk_bytes / row_bytes / 8 * 8));
+}
+
+// Bytes of each of the loader's two pinned staging buffers.
+inline uint64_t staging_buffer_bytes(int64_t K, int64_t rows, int64_t chunk_bytes) {
+  return (uint64_t)(staging_rows(K, rows, chunk_bytes) * (K / 128 * 28));
+}
 
 }  // namespace gguf
 }  // namespace btf

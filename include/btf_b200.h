@@ -285,6 +285,7 @@ typedef struct btf_decoder_info {
   uint64_t state_bytes;        /* recurrent state read + written per step */
   uint64_t kv_bytes_per_token; /* KV cache bytes read per step per cached token */
   const float* logits;         /* device [n_vocab] of the last step */
+  uint64_t device_bytes;       /* every device allocation the decoder holds (btf_plan_memory's device_bytes) */
 } btf_decoder_info;
 
 int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void** handle);
@@ -318,6 +319,33 @@ int btf_decoder_open_tp(const char* gguf_path, const btf_decoder_opts* opts, int
 int btf_shard_rows(int N, int world, int rank, int* row0, int* rows);
 int btf_decoder_arena(void* handle, void** base, uint64_t* bytes);
 int btf_decoder_connect(void* handle, void* const* peer_arenas);
+
+/* Memory plan of a decoder before it is opened: the exact device allocations
+ * btf_decoder_open_tp / btf_decoder_synthetic_tp would make for these options
+ * on this rank, and the minimum traffic of one decode step. Replaces
+ * btf::plan_memory + MemoryPlan (src/repack.cpp:142-204, include/btf/fast.hpp:50-69)
+ * for the panel layout. It runs the decoder's own binding and buffer set-up
+ * without touching a device, so it needs no GPU and agrees with the opened
+ * decoder's btf_decoder_info.device_bytes by construction. */
+typedef struct btf_memory_plan {
+  uint64_t panel_bytes;          /* ternary matrices in panels: this rank's rows; the whole embedding table */
+  uint64_t vector_bytes;         /* f32 vectors: norms, ssm_alpha/beta, ssm_a, dt bias, conv1d, Hadamard signs */
+  uint64_t kv_cache_bytes;       /* fp16 K and V of every attention layer, n_ctx tokens */
+  uint64_t state_bytes;          /* conv ring + delta-rule state of every recurrent layer */
+  uint64_t work_bytes;           /* activation arena, attention partials, Q8 activation, argmax partials, token/pos */
+  uint64_t device_bytes;         /* sum of the five above */
+  uint64_t pinned_bytes;         /* resident pinned host memory (the step's token in/out) */
+  uint64_t staging_bytes;        /* peak pinned staging while loading a GGUF, freed after each matrix */
+  uint64_t decode_bytes_fixed;   /* one step reads every weight byte once (one embedding row), reads and writes
+                                    the recurrent state, writes and reads the logits (MemoryPlan::decode_bytes_fixed) */
+  uint64_t decode_bytes_per_ctx; /* plus this per token already in the KV cache (K and V rows) */
+  int n_matrices;                /* ternary matrices resident (lm_head counted, tied or not) */
+  btf_decoder_dims dims;         /* the geometry bound */
+} btf_memory_plan;
+
+int btf_plan_memory(const char* gguf_path, const btf_decoder_opts* opts, int world, int rank, btf_memory_plan* out);
+int btf_plan_memory_synthetic(const btf_decoder_dims* dims, const btf_decoder_opts* opts, int world, int rank,
+                              btf_memory_plan* out);
 
 #ifdef __cplusplus
 }

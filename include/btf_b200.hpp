@@ -9,13 +9,16 @@
 //   - launch_repack keeps the reference's T2 output; launch_repack_panels is the
 //     loader for the B200 layout and needs N and K;
 //   - launch_prep runs the whole prep (RMSNorm, permutation, signs, Hadamard, Q8);
-//   - Decoder is the batch-1 decode step over a qwen35 GGUF (btf_decoder_*).
+//   - Decoder is the batch-1 decode step over a qwen35 GGUF (btf_decoder_*);
+//     plan_memory sizes it before it is opened (btf_plan_memory).
 #pragma once
 #include <cuda_runtime_api.h>
 
 #include <cstdint>
+#include <cstdio>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "btf_b200.h"
 
@@ -126,6 +129,61 @@ class Decoder {
  private:
   void* h_ = nullptr;
 };
+
+// The decoder's memory before it is opened. Mirrors PlanItem / MemoryPlan /
+// plan_memory (include/btf/fast.hpp:50-69, src/repack.cpp:114-204) for the
+// panel layout: items, device_bytes(), host_bytes(), table(), and the
+// bytes-per-step figures. Host only; needs no GPU.
+struct PlanItem {
+  std::string what;
+  uint64_t bytes = 0;
+  bool host = false;
+};
+struct MemoryPlan {
+  std::vector<PlanItem> items;
+  uint64_t decode_bytes_fixed = 0;
+  uint64_t decode_bytes_per_ctx = 0;
+  uint64_t device_bytes() const {
+    uint64_t s = 0;
+    for (const auto& i : items) s += i.host ? 0 : i.bytes;
+    return s;
+  }
+  uint64_t host_bytes() const {
+    uint64_t s = 0;
+    for (const auto& i : items) s += i.host ? i.bytes : 0;
+    return s;
+  }
+  std::string table() const {
+    std::string out;
+    char buf[256];
+    for (const auto& i : items) {
+      std::snprintf(buf, sizeof buf, "  %-44s %-6s %14llu B  %9.2f MiB\n", i.what.c_str(), i.host ? "host" : "device",
+                    (unsigned long long)i.bytes, i.bytes / 1048576.0);
+      out += buf;
+    }
+    std::snprintf(buf, sizeof buf, "  %-44s %-6s %14llu B  %9.2f MiB (%.3f GB)\n", "total resident", "device",
+                  (unsigned long long)device_bytes(), device_bytes() / 1048576.0, device_bytes() / 1e9);
+    return out + buf;
+  }
+};
+
+inline MemoryPlan plan_memory(const std::string& gguf_path, const DecoderOptions& o = DecoderOptions(),
+                              int world = 1, int rank = 0) {
+  const btf_decoder_opts c{o.n_ctx, o.round_q_f16 ? 1 : 0, o.attn_splits, o.cuda_graph ? 1 : 0};
+  btf_memory_plan p{};
+  throw_if(btf_plan_memory(gguf_path.c_str(), &c, world, rank, &p), "btf_plan_memory");
+  MemoryPlan m;
+  m.items = {{"ternary matrices in panels (" + std::to_string(p.n_matrices) + ")", p.panel_bytes, false},
+             {"f32 vectors (norms, ssm, conv1d, signs)", p.vector_bytes, false},
+             {"KV cache fp16", p.kv_cache_bytes, false},
+             {"delta-net + conv state", p.state_bytes, false},
+             {"activations, partials, Q8, argmax", p.work_bytes, false},
+             {"token in/out", p.pinned_bytes, true},
+             {"load staging (peak, freed after load)", p.staging_bytes, true}};
+  m.decode_bytes_fixed = p.decode_bytes_fixed;
+  m.decode_bytes_per_ctx = p.decode_bytes_per_ctx;
+  return m;
+}
 
 }  // namespace cuda
 }  // namespace btf

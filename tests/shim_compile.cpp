@@ -19,6 +19,8 @@ void ffn_call_site(const uint8_t* gate, const uint8_t* up, const uint8_t* down, 
 int decode_call_site(const std::string& path, const std::vector<int32_t>& prompt, std::vector<float>& logits) {
   btf::cuda::DecoderOptions o;
   o.n_ctx = 64;
+  const btf::cuda::MemoryPlan plan = btf::cuda::plan_memory(path, o);
+  if (plan.device_bytes() == 0 || plan.table().empty()) return -1;
   btf::cuda::Decoder dec(path, o);
   logits.resize(dec.n_vocab());
   int t = dec.prefill(prompt.data(), (int)prompt.size(), logits.data());

@@ -32,6 +32,10 @@ def test_decoder_matches_emulator(cuda, btf, ref, tmp_path, label):
     eager = btf.Decoder(path, n_ctx=64, cuda_graph=False)
     info = gpu.info()
     assert info["n_vocab"] == emu.hp["n_vocab"] and info["n_layer"] == n_layer
+    # the memory plan, computed without a device, is what the decoder allocated
+    plan = btf.plan_memory(path, n_ctx=64)
+    assert info["device_bytes"] == plan["device_bytes"] > 0
+    assert plan["decode_bytes_per_ctx"] == info["kv_bytes_per_token"]
     worst, steps, same = 0.0, 0, 0
     last_prompt = None
 
@@ -87,6 +91,7 @@ def test_synthetic_decoder_graph_equals_eager(cuda, btf):
                 d_state=64, n_group=2, dt_rank=4, conv_kernel=4, hadamard_block=128, rope_base=1e7, rms_eps=1e-6)
     a = btf.Decoder(dims=dims, seed=5, n_ctx=32)
     b = btf.Decoder(dims=dims, seed=5, n_ctx=32, cuda_graph=False)
+    assert a.info()["device_bytes"] == btf.plan_memory(dims=dims, n_ctx=32)["device_bytes"]
     t = 7
     for _ in range(6):
         na, la = a.step(t, logits=True)

@@ -42,6 +42,8 @@ def _worker(rank, world, port, out_dir):
     try:
         btf.kernels_init(rank)
         dec = btf.Decoder(dims=DIMS, seed=11, n_ctx=32, device=rank, world=world, rank=rank)
+        plan = btf.plan_memory(dims=DIMS, n_ctx=32, world=world, rank=rank)
+        np.save(os.path.join(out_dir, f"mem_r{rank}.npy"), np.array([dec.info()["device_bytes"], plan["device_bytes"]]))
         dec.connect_tp()
         logits, toks = [], []
         for t in TOKENS:
@@ -80,3 +82,6 @@ def test_tp_decode_matches_one_gpu(tmp_path):
     for s in range(len(TOKENS)):
         assert np.all(np.isfinite(tp[0][s]))
         assert rel_rms(tp[0][s], one[s]) <= 1e-3, (s, rel_rms(tp[0][s], one[s]))
+    for r in range(world):  # each rank allocated exactly its memory plan
+        held, planned = np.load(tmp_path / f"mem_r{r}.npy")
+        assert held == planned > 0, (r, held, planned)

@@ -84,6 +84,26 @@ def test_load_rows_rejects_bad_ranges(btf):
         assert L.btf_gguf_load_panels_rows(g.h, j, 0, 1, 256, 1 << 20, None) == 3
 
 
+def test_load_rejects_a_ptq_width_not_a_multiple_of_128(btf, tmp_path):
+    # a header that gives a PTQ1_0 tensor 64 columns (its data size becomes 0,
+    # so the file opens): the loader refuses it before any device access
+    import struct
+
+    data = bytearray(open(PATH, "rb").read())
+    name = b"blk.0.ffn_up.weight"
+    at = data.index(struct.pack("<Q", len(name)) + name) + 8 + len(name)
+    assert struct.unpack_from("<I", data, at)[0] == 2
+    struct.pack_into("<Q", data, at + 4, 64)
+    p = tmp_path / "narrow.gguf"
+    p.write_bytes(bytes(data))
+    L = btf.lib()
+    with btf.GgufFile(str(p)) as g:
+        i = g.find(name.decode())
+        assert g.tensor(i)["ne"][0] == 64
+        assert L.btf_gguf_load_panels_rows(g.h, i, 0, 8, 256, 1 << 20, None) == 1
+        assert "multiple of 128" in L.btf_last_error().decode()
+
+
 @pytest.mark.gpu
 def test_load_rows_equals_the_full_load(cuda, btf):
     # one rank's shard: rows [8, 8 + n) of a 37-row tensor land in panel row
