@@ -570,6 +570,62 @@ def prefill_gemm(btf, torch, dev, reps=10):
     return out
 
 
+def load_config3(args):
+    """Load path of benchmark configuration 3 (GGUF -> resident panels).
+
+    Writes the 64-layer qwen35 GGUF with seeded weights (synth.write_qwen35_gguf),
+    then times the memory plan (host only) and opening the decoder from the
+    file: mmap, pinned staging, the GPU repack of every matrix into panels, and
+    the step buffers. The file was just written, so it is read from the page
+    cache. One decode step checks the loaded model, and the decoder's
+    allocation total is checked against the plan."""
+    import shutil
+
+    import torch
+
+    import btf_b200 as btf
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    btf.kernels_init(0)
+    dims = dict(CONFIG3, n_layer=args.layers)
+    tensors = synth.qwen35_tensors(dims)
+    ptq = sum(ne[0] // 128 * 28 * ne[1] for _, ne, t in tensors if t == 143)
+    need = ptq + sum(4 * int(np.prod(ne)) for _, ne, t in tensors if t != 143)
+    dirs = [d for d in (os.environ.get("TMPDIR"), "/dev/shm", "/tmp", ROOT) if d and os.path.isdir(d)]
+    room = [d for d in dirs if shutil.disk_usage(d).free > need * 1.25]
+    if not room:
+        raise SystemExit(f"no directory with {need * 1.25 / 1e9:.1f} GB free among {dirs}")
+    path = os.path.join(room[0], f"btf_config3_{os.getpid()}.gguf")
+    try:
+        t0 = time.perf_counter()
+        size = synth.write_qwen35_gguf(path, dims, seed=3)
+        t_write = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        plan = btf.plan_memory(path, n_ctx=4096)
+        t_plan = time.perf_counter() - t0
+        opens, first, held = [], None, None
+        for i in range(2):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            dec = btf.Decoder(path, n_ctx=4096)
+            torch.cuda.synchronize()
+            opens.append(time.perf_counter() - t0)
+            if i == 0:
+                nxt, lg = dec.step(1, logits=True)
+                first = (int(nxt), bool(np.all(np.isfinite(lg))))
+                held = dec.info()["device_bytes"]
+            dec.close()
+    finally:
+        os.remove(path)
+    print(json.dumps({"load": "config3", "n_layer": dims["n_layer"], "dir": room[0], "gguf_bytes": size,
+                      "ptq1_0_bytes": ptq, "panel_bytes": plan["panel_bytes"], "write_s": round(t_write, 3),
+                      "plan_s": round(t_plan, 4), "open_s": [round(t, 3) for t in opens],
+                      "GB/s_ptq1_0": round(ptq / min(opens) / 1e9, 2), "device_bytes": held,
+                      "device_bytes_planned": plan["device_bytes"], "staging_bytes": plan["staging_bytes"],
+                      "first_step": {"token": first[0], "finite": first[1]}}))
+
+
 def only_kernel(args):
     """Runs ONE config-1 GEMV kind (no graph) `--iters` times over 4 rotating weight
     copies (> L2), for profiler captures of a single kernel; prints per-launch us."""
@@ -634,14 +690,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm", "decode"],
-                    help="profile mode: one kernel kind, or (decode) eager config-3 decode steps")
+    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm", "decode", "load"],
+                    help="profile mode: one kernel kind, (decode) eager config-3 decode steps, or (load) "
+                         "config 3 from a GGUF file into panels")
+    ap.add_argument("--layers", type=int, default=64, help="--only load: layers of the config-3 model")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--fused", type=int, default=0, help="--only: 1 = btf_gemv_f32 (quantise inside the GEMV)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.only:
+    if args.only == "load":
+        load_config3(args)
+    elif args.only:
         only_kernel(args)
     elif args.impl == "reference":
         run_reference_arm(args)

@@ -80,3 +80,116 @@ def gemv_bytes(N: int, K: int, M: int = 1, add: bool = False) -> int:
     (q + d + s) + fp32 output (read too in add mode)."""
     b = N * K // 4 + N * (K // 128) * 2 + M * (K + (K // 32) * 8) + M * N * 4
     return b + (M * N * 4 if add else 0)
+
+
+# ---------------------------------------------------------------- synthetic qwen35 GGUF
+_GGUF_U32, _GGUF_F32, _GGUF_STR = 4, 6, 8
+_T_F32, _T_PTQ1_0 = 0, 143
+
+
+def qwen35_tensors(dims: dict):
+    """(name, ne, type) of every tensor a qwen35 GGUF of this geometry holds, in
+    the order bd::Model::bind reads them (ref/bonsai-decoder/src/model.cpp:157-205);
+    ne[0] is the input width. Every layer il with (il + 1) % 4 != 0 is a gated
+    delta-net layer, the others full attention."""
+    E, F, V = dims["n_embd"], dims["n_ff"], dims["n_vocab"]
+    H, HK, HD = dims["n_head"], dims["n_head_kv"], dims["head_dim"]
+    NV, DK, NK, KC = dims["dt_rank"], dims["d_state"], dims["n_group"], dims["conv_kernel"]
+    DI = dims.get("d_inner") or NV * DK
+    C = 2 * DK * NK + DI
+    out = [("token_embd.weight", (E, V), _T_PTQ1_0), ("output_norm.weight", (E,), _T_F32),
+           ("output.weight", (E, V), _T_PTQ1_0)]
+    for il in range(dims["n_layer"]):
+        b = f"blk.{il}."
+        out += [(b + "attn_norm.weight", (E,), _T_F32), (b + "post_attention_norm.weight", (E,), _T_F32),
+                (b + "ffn_gate.weight", (E, F), _T_PTQ1_0), (b + "ffn_up.weight", (E, F), _T_PTQ1_0),
+                (b + "ffn_down.weight", (F, E), _T_PTQ1_0)]
+        if (il + 1) % 4:
+            out += [(b + "attn_qkv.weight", (E, C), _T_PTQ1_0), (b + "attn_gate.weight", (E, DI), _T_PTQ1_0),
+                    (b + "ssm_alpha.weight", (E, NV), _T_F32), (b + "ssm_beta.weight", (E, NV), _T_F32),
+                    (b + "ssm_a", (NV,), _T_F32), (b + "ssm_dt.bias", (NV,), _T_F32),
+                    (b + "ssm_conv1d.weight", (KC, C), _T_F32), (b + "ssm_norm.weight", (DI // NV,), _T_F32),
+                    (b + "ssm_out.weight", (DI, E), _T_PTQ1_0)]
+        else:
+            out += [(b + "attn_q.weight", (E, 2 * H * HD), _T_PTQ1_0), (b + "attn_k.weight", (E, HK * HD), _T_PTQ1_0),
+                    (b + "attn_v.weight", (E, HK * HD), _T_PTQ1_0), (b + "attn_output.weight", (H * HD, E), _T_PTQ1_0),
+                    (b + "attn_q_norm.weight", (HD,), _T_F32), (b + "attn_k_norm.weight", (HD,), _T_F32)]
+    return out
+
+
+def _vector(name: str, n: int, fan_in: int, rng) -> np.ndarray:
+    if name.endswith("ssm_a"):
+        return -rng.uniform(0.05, 1.0, n).astype(np.float32)
+    if name.endswith("ssm_dt.bias") or name.endswith("ssm_conv1d.weight"):
+        return (rng.standard_normal(n) * (1.0 if "dt" in name else 0.3)).astype(np.float32)
+    if name.endswith("ssm_alpha.weight") or name.endswith("ssm_beta.weight"):
+        return (rng.standard_normal(n) / np.sqrt(fan_in)).astype(np.float32)
+    return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # norms
+
+
+def write_qwen35_gguf(path: str, dims: dict, seed: int = 0, pool_rows: int = 1024) -> int:
+    """Writes a qwen35 GGUF (v3) of geometry `dims` (the btf_decoder_dims fields)
+    with seeded weights: every ternary matrix in PTQ1_0, every vector in F32, no
+    Hadamard metadata. It stands in for bd::make_synth_qwen35
+    (ref/bonsai-decoder/src/synth.cpp), which has a fixed vocabulary.
+
+    Matrix rows come from `pool_rows` encoded rows of the widest input. A prefix
+    of whole 128-blocks of a PTQ1_0 row is a valid narrower row. Row r of
+    matrix i is pool row (r + 7919 i) mod pool_rows, so a model of billions of
+    weights writes at file speed. Returns the file size in bytes."""
+    import struct
+
+    rng = np.random.default_rng(seed)
+    tensors = qwen35_tensors(dims)
+    kmax = max(ne[0] for _, ne, t in tensors if t == _T_PTQ1_0)
+    pool = ternary_ptq(pool_rows, kmax, seed=seed + 1)
+    p = "qwen35."
+    kv = [("general.architecture", _GGUF_STR, "qwen35"), ("general.alignment", _GGUF_U32, 32)]
+    for key, field in (("block_count", "n_layer"), ("embedding_length", "n_embd"), ("feed_forward_length", "n_ff"),
+                       ("attention.head_count", "n_head"), ("attention.head_count_kv", "n_head_kv"),
+                       ("attention.key_length", "head_dim"), ("attention.value_length", "head_dim"),
+                       ("rope.dimension_count", "n_rot"), ("ssm.conv_kernel", "conv_kernel"),
+                       ("ssm.state_size", "d_state"), ("ssm.group_count", "n_group"),
+                       ("ssm.time_step_rank", "dt_rank")):
+        kv.append((p + key, _GGUF_U32, int(dims[field])))
+    kv += [(p + "ssm.inner_size", _GGUF_U32, int(dims.get("d_inner") or dims["dt_rank"] * dims["d_state"])),
+           (p + "full_attention_interval", _GGUF_U32, 4),
+           (p + "rope.freq_base", _GGUF_F32, float(dims.get("rope_base", 1e7))),
+           (p + "attention.layer_norm_rms_epsilon", _GGUF_F32, float(dims.get("rms_eps", 1e-6)))]
+
+    def s(x: str) -> bytes:
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    head = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kv)))
+    for key, t, v in kv:
+        head += s(key) + struct.pack("<I", t)
+        head += s(v) if t == _GGUF_STR else struct.pack("<I" if t == _GGUF_U32 else "<f", v)
+    sizes, off = [], 0
+    for name, ne, t in tensors:
+        n = int(np.prod(ne))
+        nbytes = n * 4 if t == _T_F32 else n // 128 * 28
+        head += s(name) + struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", d) for d in ne)
+        head += struct.pack("<IQ", t, off)
+        sizes.append(nbytes)
+        off += (nbytes + 31) // 32 * 32
+    head += b"\0" * ((-len(head)) % 32)
+    by_width = {}
+    with open(path, "wb") as f:
+        f.write(head)
+        for i, ((name, ne, t), nbytes) in enumerate(zip(tensors, sizes)):
+            if t == _T_F32:
+                blob = _vector(name, int(np.prod(ne)), ne[0], rng).tobytes()
+                f.write(blob)
+            else:
+                K, N = ne
+                if K not in by_width:
+                    by_width[K] = np.ascontiguousarray(pool[:, :K // 128 * 28])
+                w = by_width[K]
+                r, start = 0, (i * 7919) % pool_rows
+                while r < N:  # contiguous runs of pool rows
+                    n = min(N - r, pool_rows - start)
+                    f.write(memoryview(w[start:start + n]))
+                    r, start = r + n, 0
+            f.write(b"\0" * ((-nbytes) % 32))
+        return f.tell()

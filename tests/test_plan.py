@@ -175,3 +175,44 @@ def test_cpp_shim_plan_runs_without_a_gpu(btf, ref, tmp_path):
     assert "total resident" in r.stdout
     r = subprocess.run([exe, str(tmp_path / "missing.gguf")], capture_output=True, text=True, timeout=60)
     assert r.returncode == 1 and "btf_plan_memory" in r.stderr
+
+
+SMALL = dict(n_layer=8, n_embd=256, n_ff=512, n_vocab=300, n_head=2, n_head_kv=1, head_dim=128, n_rot=32, d_state=32,
+             n_group=2, dt_rank=4, d_inner=128, conv_kernel=4, hadamard_block=0, rope_base=1e7, rms_eps=1e-6)
+
+
+def test_written_gguf_plans_like_the_synthetic_decoder(btf, tmp_path):
+    # synth.write_qwen35_gguf (the load benchmark's model file) binds to the same
+    # allocations as the synthetic decoder of that geometry; only the load's
+    # staging differs (synthetic weights are generated on the device)
+    import synth
+
+    path = str(tmp_path / "w.gguf")
+    size = synth.write_qwen35_gguf(path, SMALL, seed=3)
+    assert size == __import__("os").path.getsize(path)
+    a = btf.plan_memory(path, n_ctx=64)
+    b = btf.plan_memory(dims=SMALL, n_ctx=64)
+    assert a["staging_bytes"] > 0 == b["staging_bytes"]
+    for k in a:
+        if k not in ("staging_bytes", "dims"):
+            assert a[k] == b[k], (k, a[k], b[k])
+    want = expected_from_gguf(path, 64)
+    for k, v in want.items():
+        assert a[k] == v, (k, a[k], v)
+
+
+def test_written_gguf_decodes_like_the_reference_emulator(orc, ref, tmp_path):
+    # the reference's own binding accepts the file, and the restated decode
+    # step reproduces its emulator bit for bit on it
+    import synth
+
+    path = str(tmp_path / "w.gguf")
+    synth.write_qwen35_gguf(path, SMALL, seed=5)
+    emu = oracle.Emulator(ref, path, n_ctx=16, threads=1)
+    assert emu.hp["n_layer"] == 8 and emu.hp["n_vocab"] == 300 and emu.hp["d_inner"] == 128
+    dec = decode.DecodeOracle(orc, path, n_ctx=16)
+    for t in (1, 5, 9, 200, 33, 7):
+        ne, le = emu.step(t)
+        nd, ld = dec.step(t)
+        assert np.array_equal(ld, le) and nd == ne and np.all(np.isfinite(le))
+    emu.close()
