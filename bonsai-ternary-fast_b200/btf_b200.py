@@ -38,7 +38,7 @@ EXPORTS = (
     "btf_gguf_load_panels", "btf_decoder_open", "btf_decoder_synthetic", "btf_decoder_step", "btf_decoder_run",
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
-    "btf_plan_memory", "btf_plan_memory_synthetic",
+    "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
 )
 
 
@@ -106,6 +106,13 @@ class DecoderInfoC(ctypes.Structure):
     _fields_ = [("dims", DecoderDimsC), ("pos", ctypes.c_int), ("stream", ctypes.c_void_p),
                 ("weight_bytes", ctypes.c_uint64), ("state_bytes", ctypes.c_uint64),
                 ("kv_bytes_per_token", ctypes.c_uint64), ("logits", ctypes.c_void_p), ("device_bytes", ctypes.c_uint64)]
+
+
+class StepStatsC(ctypes.Structure):
+    """btf_step_stats (StepStats, include/btf/fast.hpp:72-80)."""
+    _fields_ = [("steps", ctypes.c_uint64), ("wall_s", ctypes.c_double), ("gpu_s", ctypes.c_double),
+                ("weight_xfer_bytes", ctypes.c_uint64), ("weight_xfer_s", ctypes.c_double),
+                ("mapped_read_bytes", ctypes.c_uint64)]
 
 
 PLAN_FIELDS = ("panel_bytes", "vector_bytes", "kv_cache_bytes", "state_bytes", "work_bytes", "device_bytes",
@@ -177,6 +184,8 @@ def lib() -> ctypes.CDLL:
         "btf_shard_rows": (i32, [i32, i32, i32, ctypes.POINTER(i32), ctypes.POINTER(i32)]),
         "btf_decoder_open_tp": (i32, [ctypes.c_char_p, ctypes.POINTER(DecoderOptsC), i32, i32, ctypes.POINTER(vp)]),
         "btf_gguf_load_panels_rows": (i32, [vp, i64, i64, i64, vp, i64, vp]),
+        "btf_decoder_stats": (i32, [vp, ctypes.POINTER(StepStatsC)]),
+        "btf_decoder_reset_stats": (i32, [vp]),
         "btf_plan_memory": (i32, [ctypes.c_char_p, ctypes.POINTER(DecoderOptsC), i32, i32, ctypes.POINTER(MemoryPlanC)]),
         "btf_plan_memory_synthetic": (i32, [ctypes.POINTER(DecoderDimsC), ctypes.POINTER(DecoderOptsC), i32, i32,
                                             ctypes.POINTER(MemoryPlanC)]),
@@ -607,3 +616,13 @@ class Decoder:
 
     def reset(self) -> None:
         check(lib().btf_decoder_reset(self.h), "btf_decoder_reset")
+
+    def stats(self) -> dict:
+        """Steps since reset_stats with their host wall time and device time
+        (FastDecoder::stats); waits for a pending run()."""
+        s = StepStatsC()
+        check(lib().btf_decoder_stats(self.h, ctypes.byref(s)), "btf_decoder_stats")
+        return {f: getattr(s, f) for f, _ in StepStatsC._fields_}
+
+    def reset_stats(self) -> None:
+        check(lib().btf_decoder_reset_stats(self.h), "btf_decoder_reset_stats")

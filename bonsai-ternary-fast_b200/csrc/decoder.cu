@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -99,6 +100,13 @@ struct Decoder {
   uint64_t dev_bytes[kKinds] = {};
   uint64_t sign_bytes = 0, staging_peak = 0;
   int n_mats = 0;
+  // Step accounting (FastDecoder::stats): steps, host wall time inside
+  // step/run, device time between CUDA events around them. The events of an
+  // asynchronous run are read when the stats are next touched.
+  uint64_t n_steps = 0;
+  double wall_s = 0, gpu_s = 0;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  bool ev_pending = false;
   static constexpr int kArgmaxParts = 148;
   // tensor parallelism: every matmul N-sharded over `world` ranks, its outputs
   // stored into every rank's arena (btf_gemv_gather, counted completion). The
@@ -113,6 +121,8 @@ struct Decoder {
   static constexpr size_t kCtl = 256;
 
   ~Decoder() {
+    for (cudaEvent_t e : ev)
+      if (e) cudaEventDestroy(e);
     if (exec) cudaGraphExecDestroy(exec);
     if (graph) cudaGraphDestroy(graph);
     if (st) cudaStreamSynchronize(st);
@@ -614,7 +624,26 @@ int finish_open(Decoder& D) {
   BTF_TRY(check_dims(D));
   D.theta_scale = std::pow(D.d.rope_base, -2.0f / (float)D.d.n_rot);
   BTF_TRY(make_buffers(D));
-  return D.dry ? BTF_OK : reset_state(D);
+  if (D.dry) return BTF_OK;
+  for (cudaEvent_t& e : D.ev)
+    if (cudaEventCreate(&e) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder: events");
+  return reset_state(D);
+}
+
+// Adds the device time of the last bracketed step or run once its end event is reached.
+int settle(Decoder& D) {
+  if (!D.ev_pending) return BTF_OK;
+  D.ev_pending = false;
+  float ms = 0.f;
+  cudaError_t e = cudaEventSynchronize(D.ev[1]);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, D.ev[0], D.ev[1]);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder: step timing");
+  D.gpu_s += ms * 1e-3;
+  return BTF_OK;
+}
+
+double seconds_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
 
 btf_decoder_opts defaults(const btf_decoder_opts* o) {
@@ -845,15 +874,23 @@ int btf_decoder_step(void* handle, int32_t token, float* logits, int32_t* next) 
   if (!handle) return fail(BTF_ERR_ARG, "btf_decoder_step: null handle");
   Decoder& D = *static_cast<Decoder*>(handle);
   if (token < 0 || token >= D.d.n_vocab) return fail(BTF_ERR_ARG, "btf_decoder_step: token %d out of range", token);
+  const auto t0 = std::chrono::steady_clock::now();
+  BTF_TRY(settle(D));
   D.h_io[0] = token;
   cudaError_t e = cudaMemcpyAsync(D.d_tok, D.h_io, sizeof(int32_t), cudaMemcpyHostToDevice, D.st);
+  if (e == cudaSuccess) e = cudaEventRecord(D.ev[0], D.st);
   if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_step: token");
   BTF_TRY(run_step(D));
-  e = cudaMemcpyAsync(D.h_io + 1, D.d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, D.st);
+  e = cudaEventRecord(D.ev[1], D.st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(D.h_io + 1, D.d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, D.st);
   if (e == cudaSuccess && logits)
     e = cudaMemcpyAsync(logits, D.logits, (size_t)D.d.n_vocab * sizeof(float), cudaMemcpyDeviceToHost, D.st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(D.st);
   if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_step");
+  D.ev_pending = true;
+  BTF_TRY(settle(D));
+  D.n_steps += 1;
+  D.wall_s += seconds_since(t0);
   if (next) *next = D.h_io[1];
   return BTF_OK;
 }
@@ -861,7 +898,42 @@ int btf_decoder_step(void* handle, int32_t token, float* logits, int32_t* next) 
 int btf_decoder_run(void* handle, int steps) {
   if (!handle || steps < 0) return fail(BTF_ERR_ARG, "btf_decoder_run: bad argument");
   Decoder& D = *static_cast<Decoder*>(handle);
-  for (int i = 0; i < steps; ++i) BTF_TRY(run_step(D));
+  const auto t0 = std::chrono::steady_clock::now();
+  BTF_TRY(settle(D));
+  cudaError_t e = cudaEventRecord(D.ev[0], D.st);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_run: event");
+  int done = 0, rc = BTF_OK;
+  for (; done < steps && rc == BTF_OK; ++done) rc = run_step(D);
+  if (rc) --done;
+  D.n_steps += done;
+  if ((e = cudaEventRecord(D.ev[1], D.st)) != cudaSuccess && rc == BTF_OK) rc = cuda_fail(e, "btf_decoder_run: event");
+  D.ev_pending = e == cudaSuccess;
+  D.wall_s += seconds_since(t0);
+  return rc;
+}
+
+int btf_decoder_stats(void* handle, btf_step_stats* out) {
+  if (!handle || !out) return fail(BTF_ERR_ARG, "btf_decoder_stats: null argument");
+  Decoder& D = *static_cast<Decoder*>(handle);
+  BTF_TRY(settle(D));
+  std::memset(out, 0, sizeof *out);
+  out->steps = D.n_steps;
+  out->wall_s = D.wall_s;
+  out->gpu_s = D.gpu_s;
+  // weights and the embedding table are device-resident: a step copies none
+  // and reads nothing from mapped host memory
+  out->weight_xfer_bytes = 0;
+  out->weight_xfer_s = 0;
+  out->mapped_read_bytes = 0;
+  return BTF_OK;
+}
+
+int btf_decoder_reset_stats(void* handle) {
+  if (!handle) return fail(BTF_ERR_ARG, "btf_decoder_reset_stats: null handle");
+  Decoder& D = *static_cast<Decoder*>(handle);
+  BTF_TRY(settle(D));
+  D.n_steps = 0;
+  D.wall_s = D.gpu_s = 0;
   return BTF_OK;
 }
 

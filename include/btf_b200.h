@@ -299,6 +299,20 @@ int btf_decoder_reset(void* handle);
 int btf_decoder_close(void* handle);
 int btf_decoder_get_info(void* handle, btf_decoder_info* out);
 
+/* Per-step accounting since the last reset_stats (FastDecoder::stats /
+ * reset_stats and StepStats, include/btf/fast.hpp:72-96). Kept across
+ * btf_decoder_reset. Reading the stats waits for a pending btf_decoder_run. */
+typedef struct btf_step_stats {
+  uint64_t steps;             /* steps made by btf_decoder_step and btf_decoder_run */
+  double wall_s;              /* host wall time inside those calls */
+  double gpu_s;               /* device time between CUDA events around each step / run */
+  uint64_t weight_xfer_bytes; /* host-to-device weight copies during those steps: 0 (weights are resident) */
+  double weight_xfer_s;       /* wall time of those copies: 0 */
+  uint64_t mapped_read_bytes; /* bytes read zero-copy from mapped host memory: 0 (the embedding is resident) */
+} btf_step_stats;
+int btf_decoder_stats(void* handle, btf_step_stats* out);
+int btf_decoder_reset_stats(void* handle);
+
 /* Tensor-parallel decode: every ternary matmul of the step is N-sharded
  * over `world` GPUs (one process each; rank r holds rows shard r of every matrix,
  * whole 8-row groups) and its outputs are stored into every rank's activation

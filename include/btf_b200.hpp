@@ -118,6 +118,14 @@ class Decoder {
     return next;
   }
   void reset() { throw_if(btf_decoder_reset(h_), "btf_decoder_reset"); }
+  // FastDecoder::stats / reset_stats / device_bytes (fast.hpp:90-95)
+  btf_step_stats stats() const {
+    btf_step_stats s{};
+    throw_if(btf_decoder_stats(h_, &s), "btf_decoder_stats");
+    return s;
+  }
+  void reset_stats() { throw_if(btf_decoder_reset_stats(h_), "btf_decoder_reset_stats"); }
+  uint64_t device_bytes() const { return info().device_bytes; }
   int pos() const { return info().pos; }
   int n_vocab() const { return info().dims.n_vocab; }
   btf_decoder_info info() const {

@@ -26,5 +26,7 @@ int decode_call_site(const std::string& path, const std::vector<int32_t>& prompt
   int t = dec.prefill(prompt.data(), (int)prompt.size(), logits.data());
   for (int i = 0; i < 4; ++i) t = dec.step(t, nullptr);
   dec.reset();
-  return t + dec.pos();
+  const btf_step_stats st = dec.stats();
+  dec.reset_stats();
+  return t + dec.pos() + (int)st.steps + (dec.device_bytes() == plan.device_bytes() ? 0 : 1);
 }

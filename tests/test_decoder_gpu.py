@@ -105,5 +105,14 @@ def test_synthetic_decoder_graph_equals_eager(cuda, btf):
 
     torch.cuda.synchronize()
     assert a.info()["pos"] == 5 and btf.device_error() == 0
+    # step accounting (FastDecoder::stats): 6 steps + a run of 5, device time
+    # measured, no weight copies (test_gpu_decoder.cpp:92-99 of the reference)
+    st = a.stats()
+    assert st["steps"] == 11 and st["gpu_s"] > 0 and st["wall_s"] > 0
+    assert st["weight_xfer_bytes"] == 0 and st["mapped_read_bytes"] == 0
+    a.reset_stats()
+    a.step(3)
+    st = a.stats()
+    assert st["steps"] == 1 and 0 < st["gpu_s"] < 1.0
     a.close()
     b.close()

@@ -135,3 +135,12 @@ def test_decoder_entry_points_reject_bad_arguments(btf):
     assert L.btf_decoder_connect(None, None) == 1
     info = btf.DecoderInfoC()
     assert L.btf_decoder_get_info(None, ctypes.byref(info)) == 1
+
+
+def test_decoder_stats_reject_null_handles(btf):
+    import ctypes
+
+    L = btf.lib()
+    s = btf.StepStatsC()
+    assert L.btf_decoder_stats(None, ctypes.byref(s)) == 1
+    assert L.btf_decoder_reset_stats(None) == 1
