@@ -574,10 +574,12 @@ def load_config3(args):
     """Load path of benchmark configuration 3 (GGUF -> resident panels).
 
     Writes the 64-layer qwen35 GGUF with seeded weights (synth.write_qwen35_gguf),
-    then times the memory plan (host only) and opening the decoder from the
-    file: mmap, pinned staging, the GPU repack of every matrix into panels, and
-    the step buffers. The file was just written, so it is read from the page
-    cache. One decode step checks the loaded model, and the decoder's
+    then times the memory plan (host only) and opening the decoder twice from
+    the file: mmap, pinned staging, the GPU repack of every matrix into panels,
+    and the step buffers. The first open reads the just-written file from the
+    page cache. Each open then drops the file's pages (drop_page_cache), so on
+    a disk-backed directory the second open reads the disk; on tmpfs both
+    read memory. One decode step checks the loaded model, and the decoder's
     allocation total is checked against the plan."""
     import shutil
 
@@ -618,7 +620,12 @@ def load_config3(args):
             dec.close()
     finally:
         os.remove(path)
-    print(json.dumps({"load": "config3", "n_layer": dims["n_layer"], "dir": room[0], "gguf_bytes": size,
+    fs = ""
+    try:
+        fs = next((ln.split()[2] for ln in open("/proc/mounts") if ln.split()[1] == room[0]), "")
+    except OSError:
+        pass
+    print(json.dumps({"load": "config3", "n_layer": dims["n_layer"], "dir": room[0], "fs": fs, "gguf_bytes": size,
                       "ptq1_0_bytes": ptq, "panel_bytes": plan["panel_bytes"], "write_s": round(t_write, 3),
                       "plan_s": round(t_plan, 4), "open_s": [round(t, 3) for t in opens],
                       "GB/s_ptq1_0": round(ptq / min(opens) / 1e9, 2), "device_bytes": held,

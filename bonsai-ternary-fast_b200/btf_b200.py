@@ -91,7 +91,7 @@ class TaggedBufC(ctypes.Structure):
 
 class DecoderOptsC(ctypes.Structure):
     _fields_ = [("n_ctx", ctypes.c_int), ("round_q_f16", ctypes.c_int), ("attn_splits", ctypes.c_int),
-                ("cuda_graph", ctypes.c_int)]
+                ("cuda_graph", ctypes.c_int), ("staging_mb", ctypes.c_int), ("keep_page_cache", ctypes.c_int)]
 
 
 DIM_FIELDS = ("n_layer", "n_embd", "n_ff", "n_vocab", "n_head", "n_head_kv", "head_dim", "n_rot", "d_state",
@@ -505,11 +505,11 @@ def _dims_c(dims: dict) -> DecoderDimsC:
 
 
 def plan_memory(path: Optional[str] = None, dims: Optional[dict] = None, n_ctx: int = 4096, attn_splits: int = 16,
-                world: int = 1, rank: int = 0) -> dict:
+                world: int = 1, rank: int = 0, staging_mb: int = 64) -> dict:
     """btf_plan_memory: the device and pinned memory a Decoder with these
     arguments would allocate on `rank`, and the bytes one decode step reads
     (btf::plan_memory, src/repack.cpp:142-204). Host only: needs no GPU."""
-    o = DecoderOptsC(n_ctx, 1, attn_splits, 1)
+    o = DecoderOptsC(n_ctx, 1, attn_splits, 1, staging_mb, 0)
     p = MemoryPlanC()
     if path is not None:
         check(lib().btf_plan_memory(path.encode(), ctypes.byref(o), world, rank, ctypes.byref(p)), "btf_plan_memory")
@@ -544,11 +544,11 @@ class Decoder:
 
     def __init__(self, path: Optional[str] = None, dims: Optional[dict] = None, seed: int = 1, n_ctx: int = 4096,
                  round_q_f16: bool = True, attn_splits: int = 16, cuda_graph: bool = True, device: int = 0,
-                 world: int = 1, rank: int = 0):
+                 world: int = 1, rank: int = 0, staging_mb: int = 64, drop_page_cache: bool = True):
         torch = _torch()
         torch.cuda.set_device(device)
         ensure_init(device)
-        o = DecoderOptsC(n_ctx, int(round_q_f16), attn_splits, int(cuda_graph))
+        o = DecoderOptsC(n_ctx, int(round_q_f16), attn_splits, int(cuda_graph), staging_mb, int(not drop_page_cache))
         h = ctypes.c_void_p()
         if path is not None:
             check(lib().btf_decoder_open_tp(path.encode(), ctypes.byref(o), world, rank, ctypes.byref(h)),

@@ -12,6 +12,8 @@
 // input token live in device memory, so the captured graph replays for every
 // token. Batch 1 only: a prompt is fed one token per step.
 #include <cuda_fp16.h>
+#include <fcntl.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <chrono>
@@ -32,7 +34,6 @@ namespace btf {
 namespace {
 
 constexpr uint32_t kF32 = 0, kF16 = 1, kBF16 = 30, kPTQ = 143;
-constexpr int64_t kStaging = 64 << 20;  // source bytes per chunk of a matrix load
 
 struct Mat {
   uint8_t* pan = nullptr;
@@ -414,11 +415,12 @@ struct Binder {
     m->pan = D.alloc<uint8_t>(btf_panel_bytes(m->n, m->K), &rc, Decoder::kPanels);
     if (rc) return rc;
     D.n_mats += 1;
+    const int64_t chunk = (int64_t)D.o.staging_mb << 20;  // source bytes per chunk of the load
     if (D.dry) {
       // the loader's two pinned staging buffers, freed after each matrix
-      D.staging_peak = std::max<uint64_t>(D.staging_peak, 2 * gguf::staging_buffer_bytes(m->K, m->n, kStaging));
+      D.staging_peak = std::max<uint64_t>(D.staging_peak, 2 * gguf::staging_buffer_bytes(m->K, m->n, chunk));
     } else {
-      BTF_TRY(btf_gguf_load_panels_rows(g, idx, m->row0, m->n, m->pan, kStaging, D.st));
+      BTF_TRY(btf_gguf_load_panels_rows(g, idx, m->row0, m->n, m->pan, chunk, D.st));
     }
     D.weight_bytes += btf_panel_bytes(m->n, m->K);
     if (folded.count(name)) {
@@ -617,6 +619,7 @@ int check_dims(const Decoder& D) {
   if (d.conv_kernel < 2) return fail(BTF_ERR_UNSUPPORTED, "btf_decoder: conv_kernel < 2");
   if (D.o.n_ctx < 1 || D.o.attn_splits < 1 || D.o.attn_splits > 256)
     return fail(BTF_ERR_ARG, "btf_decoder: n_ctx >= 1 and 1 <= attn_splits <= 256");
+  if (D.o.staging_mb < 1 || D.o.staging_mb > 4096) return fail(BTF_ERR_ARG, "btf_decoder: staging_mb 1..4096");
   return BTF_OK;
 }
 
@@ -647,8 +650,9 @@ double seconds_since(std::chrono::steady_clock::time_point t0) {
 }
 
 btf_decoder_opts defaults(const btf_decoder_opts* o) {
-  btf_decoder_opts r{4096, 1, 16, 1};
+  btf_decoder_opts r{4096, 1, 16, 1, 64, 0};
   if (o) r = *o;
+  if (r.staging_mb == 0) r.staging_mb = 64;
   return r;
 }
 
@@ -671,7 +675,16 @@ int open_gguf(Decoder& D, const char* path) {
   const int rc = b.bind();
   btf_gguf_close(g);
   if (rc) return rc;
-  return finish_open(D);
+  BTF_TRY(finish_open(D));
+  if (!D.dry && !D.o.keep_page_cache) {
+    // the weights are resident: the file's pages need not stay cached (gpu_decoder.cu:385-391)
+    const int fd = ::open(path, O_RDONLY);
+    if (fd >= 0) {
+      posix_fadvise(fd, 0, 0, POSIX_FADV_DONTNEED);
+      ::close(fd);
+    }
+  }
+  return BTF_OK;
 }
 
 // Seeded synthetic weights of geometry R.d on this rank (a dry decoder only sizes them).

@@ -268,7 +268,10 @@ typedef struct btf_decoder_opts {
   int round_q_f16; /* round q to fp16 before q.k (FastOptions::round_q_f16) */
   int attn_splits; /* key ranges of the attention (FastOptions::attn_splits), 1..256 */
   int cuda_graph;  /* capture one step as a graph and replay it (FastOptions::cuda_graph) */
-} btf_decoder_opts;  /* NULL options: {4096, 1, 16, 1} */
+  int staging_mb;  /* GGUF load: pinned staging per slot in MiB, 2 slots (FastOptions::staging_mb); 0: 64 */
+  int keep_page_cache; /* GGUF load: 0 drops the file's pages from the host page cache once the weights
+                          are resident (FastOptions::drop_page_cache, on by default there) */
+} btf_decoder_opts;  /* NULL options: {4096, 1, 16, 1, 64, 0} */
 
 typedef struct btf_decoder_dims { /* bd::HParams (ref/bonsai-decoder/include/bd/model.hpp:18-35) */
   int n_layer, n_embd, n_ff, n_vocab, n_head, n_head_kv, head_dim, n_rot;

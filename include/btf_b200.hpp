@@ -96,12 +96,19 @@ struct DecoderOptions {  // the FastOptions fields the decoder uses (fast.hpp:13
   bool round_q_f16 = true;
   int attn_splits = 16;
   bool cuda_graph = true;
+  int staging_mb = 64;
+  bool drop_page_cache = true;
 };
+
+inline btf_decoder_opts to_c(const DecoderOptions& o) {
+  return btf_decoder_opts{o.n_ctx,      o.round_q_f16 ? 1 : 0, o.attn_splits,
+                          o.cuda_graph ? 1 : 0, o.staging_mb, o.drop_page_cache ? 0 : 1};
+}
 
 class Decoder {
  public:
   explicit Decoder(const std::string& gguf_path, const DecoderOptions& o = DecoderOptions()) {
-    const btf_decoder_opts c{o.n_ctx, o.round_q_f16 ? 1 : 0, o.attn_splits, o.cuda_graph ? 1 : 0};
+    const btf_decoder_opts c = to_c(o);
     throw_if(btf_decoder_open(gguf_path.c_str(), &c, &h_), "btf_decoder_open");
   }
   Decoder(const Decoder&) = delete;
@@ -177,7 +184,7 @@ struct MemoryPlan {
 
 inline MemoryPlan plan_memory(const std::string& gguf_path, const DecoderOptions& o = DecoderOptions(),
                               int world = 1, int rank = 0) {
-  const btf_decoder_opts c{o.n_ctx, o.round_q_f16 ? 1 : 0, o.attn_splits, o.cuda_graph ? 1 : 0};
+  const btf_decoder_opts c = to_c(o);
   btf_memory_plan p{};
   throw_if(btf_plan_memory(gguf_path.c_str(), &c, world, rank, &p), "btf_plan_memory");
   MemoryPlan m;

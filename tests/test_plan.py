@@ -137,6 +137,18 @@ def test_plan_of_the_synthetic_config3_decoder(btf):
     assert plan["device_bytes"] < 8e9
 
 
+def test_plan_follows_the_staging_size(btf, ref, tmp_path):
+    # FastOptions::staging_mb: smaller chunks, smaller pinned staging; the device plan is unchanged
+    path = str(tmp_path / "synth.gguf")
+    oracle.synth_model(ref, path, n_layer=4, seed=1)
+    a = btf.plan_memory(path, n_ctx=64, staging_mb=64)
+    b = btf.plan_memory(path, n_ctx=64, staging_mb=1)
+    assert b["staging_bytes"] == expected_from_gguf(path, 64, chunk=1 << 20)["staging_bytes"]
+    assert a["device_bytes"] == b["device_bytes"]
+    with pytest.raises(RuntimeError):
+        btf.plan_memory(path, staging_mb=5000)
+
+
 def test_plan_rejects_bad_arguments(btf, ref, tmp_path):
     with pytest.raises(RuntimeError):
         btf.plan_memory(str(tmp_path / "missing.gguf"))
