@@ -39,6 +39,7 @@ EXPORTS = (
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
     "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
+    "btf_gemm_f32_noalloc",
 )
 
 
@@ -153,6 +154,7 @@ def lib() -> ctypes.CDLL:
         "btf_device_error": (i32, [i32]),
         "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
         "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
+        "btf_gemm_f32_noalloc": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
         "btf_gemv_gather": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, ctypes.POINTER(GatherC), vp]),
         "btf_alloc": (i32, [ctypes.c_size_t, ctypes.POINTER(vp)]),
         "btf_free": (i32, [vp]),
@@ -361,6 +363,16 @@ def launch_gemv_f32(segs: Sequence[tuple], K: int, M: int, x, mode: int = STORE,
 def launch_gemm(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int = STORE, stream=None) -> None:
     """Prefill GEMM on the tcgen05 int8 tensor cores (btf_gemm), M >= 64; store / add modes."""
     check(lib().btf_gemm(_segs(segs), len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemm")
+
+
+GEMM_NOALLOC_MAX_MK = 512 * 17408  # BTF_GEMM_NOALLOC_MAX_MK
+
+
+def launch_gemm_f32_noalloc(segs: Sequence[tuple], K: int, M: int, x, mode: int = STORE, stream=None) -> None:
+    """Prefill GEMM from fp32 activations x [M][>=K] with no allocation (btf_gemm_f32_noalloc): the Q8
+    intermediate lives in the library's fixed device array, M * K <= GEMM_NOALLOC_MAX_MK."""
+    check(lib().btf_gemm_f32_noalloc(_segs(segs), len(segs), K, M, _ptr(x), x.stride(0), mode, _stream(stream)),
+          "btf_gemm_f32_noalloc")
 
 
 def device_error(clear: bool = False) -> int:

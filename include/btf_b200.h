@@ -157,6 +157,27 @@ int btf_device_error(int clear);
  * for large M. q and d must be 16-byte aligned. */
 int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
+/* The prefill GEMM from fp32 activations x [M][ldx], allocating nothing. No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory, such as a plugin whose host engine has reserved the whole
+ * device and passes it only operand tensors, or a serving loop that may not
+ * call cudaMalloc (which can synchronise the device) between steps. It
+ * quantises x exactly as btf_quant_q8 does and runs btf_gemm, with the Q8
+ * intermediate in a fixed device array inside the library instead of a caller
+ * buffer, so its outputs equal those of btf_quant_q8 + btf_gemm.
+ *   - Limit: M * K <= BTF_GEMM_NOALLOC_MAX_MK (512 x 17408); larger calls return
+ *     BTF_ERR_ARG. Every GPU that loads the library holds the array
+ *     (BTF_GEMM_NOALLOC_MAX_MK * 1.25 bytes, about 11 MB) until the process exits.
+ *   - The first call on a device looks up the array's device address; make that
+ *     first call outside any stream capture.
+ *   - All calls on a device share the one array: calls that can overlap on the
+ *     GPU (different streams without ordering between them) race. Calls in one
+ *     stream are ordered and safe.
+ *   - segs, K, mode and the output contract are btf_gemm's; x needs ldx >= K. */
+#define BTF_GEMM_NOALLOC_MAX_MK 8912896
+int btf_gemm_f32_noalloc(const btf_gemv_seg* segs, int nseg, int K, int M, const float* x, int ldx, int mode,
+                         void* stream);
+
 /* Debug/parity entry point: the exact int32 trit dot of every (m, row,
  * sub-block), idot[M][N][K/32] = code_dot - sum(q) — the integers the GEMV
  * scales (src/emu_decoder.cpp:154-157). Same decode path as btf_gemv. */
