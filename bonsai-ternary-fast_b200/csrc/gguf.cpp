@@ -117,7 +117,7 @@ void read_scalar(Reader& r, uint32_t t, int64_t& i, double& f) {
     default: r.ok = false;
   }
   if (t != 6 && t != 12) f = (double)i;
-  else i = (int64_t)f;
+  else i = (f > -9.2e18 && f < 9.2e18) ? (int64_t)f : 0;  // NaN or out of range: no integer view
 }
 
 // Reads one metadata value (scalars, strings and one level of arrays).
@@ -167,7 +167,11 @@ int parse(File& f) {
   f.version = r.get<uint32_t>();
   if (f.version < 2 || f.version > 3) return btf::fail(BTF_ERR_UNSUPPORTED, "btf_gguf_open: GGUF version %u", f.version);
   const uint64_t n_tensors = r.get<uint64_t>(), n_kv = r.get<uint64_t>();
-  if (!r.ok || n_tensors > (1u << 24) || n_kv > (1u << 24)) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: bad header");
+  // every key/value takes at least 12 bytes (empty key, type), every tensor entry at least 32
+  // (empty name, n_dims, one ne, type, offset): counts beyond what the file holds are malformed
+  if (!r.ok || n_tensors > (1u << 24) || n_kv > (1u << 24) || n_kv > (r.n - r.pos) / 12 ||
+      n_tensors > (r.n - r.pos) / 32)
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_open: bad header");
   for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
     const std::string key = r.str();
     const uint32_t type = r.get<uint32_t>();
@@ -196,7 +200,8 @@ int parse(File& f) {
     t.bytes = tensor_bytes(t.type, n_elem, t.ne[0]);
   }
   if (!r.ok) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: truncated or malformed header");
-  if (f.alignment == 0 || (f.alignment & (f.alignment - 1))) return btf::fail(BTF_ERR_ARG, "btf_gguf_open: bad alignment");
+  if (f.alignment == 0 || (f.alignment & (f.alignment - 1)) || f.alignment > (uint64_t(1) << 30))
+    return btf::fail(BTF_ERR_ARG, "btf_gguf_open: bad alignment");
   f.data_start = (r.pos + f.alignment - 1) / f.alignment * f.alignment;
   for (const Tensor& t : f.tensors)
     if (f.data_start > f.size || t.offset > f.size - f.data_start || t.bytes > f.size - f.data_start - t.offset)

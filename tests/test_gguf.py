@@ -60,6 +60,35 @@ def test_reader_rejects_malformed_files(btf, tmp_path):
             btf.GgufFile(str(p))
 
 
+def _gguf_bytes(n_tensors, kvs):
+    """A GGUF v3 header with the given tensor count and (key, type, value bytes) pairs, no tensor entries."""
+    import struct
+
+    out = b"GGUF" + struct.pack("<IQQ", 3, n_tensors, len(kvs))
+    for key, typ, val in kvs:
+        out += struct.pack("<Q", len(key)) + key.encode() + struct.pack("<I", typ) + val
+    return out + bytes(64)
+
+
+def test_reader_bounds_counts_alignment_and_float_metadata(btf, tmp_path):
+    import struct
+
+    bad = {"tensor_count": _gguf_bytes(1 << 23, []),
+           "kv_count": b"GGUF" + struct.pack("<IQQ", 3, 0, 1 << 20) + bytes(64),
+           "alignment": _gguf_bytes(0, [("general.alignment", 10, struct.pack("<Q", 1 << 40))])}
+    for name, blob in bad.items():
+        p = tmp_path / f"{name}.gguf"
+        p.write_bytes(blob)
+        with pytest.raises(RuntimeError, match="bad header|bad alignment"):
+            btf.GgufFile(str(p))
+    # float metadata that has no integer value (NaN, 1e30) is kept, not converted with undefined behaviour
+    ok = tmp_path / "floats.gguf"
+    ok.write_bytes(_gguf_bytes(0, [("a.nan", 6, struct.pack("<f", float("nan"))),
+                                   ("a.big", 12, struct.pack("<d", 1e30))]))
+    with btf.GgufFile(str(ok)) as g:
+        assert len(g) == 0
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("staging", [1 << 20, 8 * 288])  # one chunk; one 8-row group per chunk
 def test_load_panels_on_device_equals_host_twin(cuda, btf, staging):
