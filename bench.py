@@ -16,8 +16,16 @@ e2e    = same metric through the same C-ABI calls with the step's activation
          inputs copied from pinned host memory and its outputs copied back,
          inside the timed region.
 With --gpus N > 1 (torchrun), every matrix is N-sharded by rows across the
-ranks (whole 8-row groups, shard.shard_rows) and each GEMV's output is all-gathered over NCCL;
-the total work is fixed, so scaling is "strong".
+ranks (whole 8-row groups, shard.shard_rows) and each GEMV's output is
+all-gathered in its epilogue over NVLink (tagged 64-bit stores into every
+rank's buffer, btf_gemv_gather; no NCCL in the step); the total work is fixed,
+so scaling is "strong".
+
+The line also carries benchmark configuration 2 (the tcgen05 prefill GEMM, one
+GPU) and configuration 3 (the 64-layer decode step as one CUDA graph; tensor
+parallel at N > 1). On one GPU, `cpu_baseline` times the reference's CPU GEMV
+and `decode_config3.cpu_baseline` its CPU emulator's decode step, both built
+from the reference's sources into oracle/_ref, on bounded samples.
 
 --impl reference times the reference's own CPU GEMV (oracle/_ref, built from
 the reference sources; its emulator loop on all host threads) on a bounded
@@ -172,6 +180,60 @@ def cpu_baseline_line(threads: int) -> dict:
         one = cpu_reference(1, reps=1)
         cb["single_thread"] = {"value": one["value"], "unit": one["unit"], "sample": one["sample"]}
     return cb
+
+
+def cpu_decode_reference(threads: int, steps: int = 3, geometry: dict | None = None) -> dict:
+    """The reference's CPU emulator of its CUDA decode step (btf::make_emu_decoder,
+    src/emu_decoder.cpp, compiled from the reference sources into oracle/_ref) on
+    benchmark configuration 3's geometry, as a bounded sample: models with config
+    3's widths and 4 and 8 layers (one and two periods of 3 delta-net layers + 1
+    attention layer, plus the embedding and the 248320-row lm_head) are written
+    with seeded weights, and each is timed over `steps` greedy steps after one
+    warm-up step. The per-token time is linear in the layer count, so the 64-layer
+    time is t4 + (t8 - t4) * 15. The context holds at most 5 tokens (the GPU
+    bench's attention reads about 40; attention is a negligible share on the CPU).
+    `geometry` replaces config 3's widths (tests use a small model)."""
+    import shutil
+
+    if os.path.join(ROOT, "oracle") not in sys.path:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    kind = "reference" if oracle.Reference.available() else None
+    if kind is None:
+        return {"unavailable": "oracle/_ref/libbtf_ref.so is not built"}
+    R = oracle.Reference()
+    base = geometry or CONFIG3
+    per_tok = {}
+    for n_layer in (4, 8):
+        dims = dict(base, n_layer=n_layer)
+        tensors = synth.qwen35_tensors(dims)
+        need = sum(ne[0] // 128 * 28 * ne[1] if t == 143 else 4 * int(np.prod(ne)) for _, ne, t in tensors)
+        dirs = [d for d in (os.environ.get("TMPDIR"), "/dev/shm", "/tmp", ROOT) if d and os.path.isdir(d)]
+        room = [d for d in dirs if shutil.disk_usage(d).free > need * 1.25]
+        if not room:
+            return {"unavailable": f"no directory with {need * 1.25 / 1e9:.1f} GB free for the sample model"}
+        path = os.path.join(room[0], f"btf_cpu_decode_{os.getpid()}_{n_layer}.gguf")
+        try:
+            synth.write_qwen35_gguf(path, dims, seed=3)
+            em = oracle.Emulator(R, path, n_ctx=16, threads=threads)
+            try:
+                nxt, _ = em.step(1)
+                t0 = time.perf_counter()
+                for _ in range(steps):
+                    nxt, _ = em.step(int(nxt))
+                per_tok[n_layer] = (time.perf_counter() - t0) / steps
+            finally:
+                em.close()
+        finally:
+            if os.path.exists(path):
+                os.remove(path)
+    t64 = per_tok[4] + (per_tok[8] - per_tok[4]) * (base["n_layer"] - 4) / 4
+    return {"value": 1.0 / t64, "unit": "tok/s", "s_per_token": t64, "cores": threads, "kind": kind,
+            "sample": f"reference CPU emulator decode step at config-3 widths with 4 and 8 layers, {steps} timed "
+                      f"steps each ({per_tok[4]:.3f} and {per_tok[8]:.3f} s per token), extrapolated linearly "
+                      f"to {base['n_layer']} layers",
+            "cpu_model": cpu_model()}
 
 
 def run_reference_arm(args):
@@ -464,6 +526,10 @@ def gpu_arm(args):
             line["decode_config3"] = dec3
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_line(host_threads())
+            try:
+                line["decode_config3"]["cpu_baseline"] = cpu_decode_reference(host_threads())
+            except Exception as ex:  # the GPU line must still print
+                line["decode_config3"]["cpu_baseline"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
         print(json.dumps(line), flush=True)
     if world > 1:
         del g_dev, g_e2e, g_unf
