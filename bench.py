@@ -522,6 +522,10 @@ def gpu_arm(args):
         if world == 1:
             line["prefill_gemm_config2"] = prefill_gemm(btf, torch, dev)
             line["decode_config3"] = decode_config3(btf, torch, dev)
+            try:  # last of the GPU legs, so that a failure here costs only this entry
+                line["lm_head_config4"] = lm_head_config4(btf, torch, dev)
+            except Exception as ex:
+                line["lm_head_config4"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
         else:
             line["decode_config3"] = dec3
         if world == 1 and not args.no_cpu_baseline:
@@ -659,6 +663,55 @@ def prefill_gemm(btf, torch, dev, reps=10):
                                   "frac_of_int8_spec_4500": ops / us / 1e6 / 4500.0,
                                   "weight_GBps": btf.panel_bytes(N, K) / us / 1e3}
         del g, mats, src
+    return out
+
+
+def lm_head_config4(btf, torch, dev, reps=20):
+    """Benchmark configuration 4's lm_head on one GPU: the ternary GEMV K=5120 ->
+    N=248320 (338 MB of panels, 2.7x L2) at batch 1 and batch 16 (btf_gemv; batch
+    16 runs as four 4-row passes over the weights), each launch over one of 2
+    weight copies, timed with CUDA events around a CUDA graph of `reps` launches.
+    GB/s counts the algorithmic bytes (weights once, the Q8 activation, the fp32
+    output); `weight_passes` is how often one launch streams the weights. The
+    weights are 16 copies of one seeded 15520-row PTQ1_0 block with config 0's
+    distributions (the number of bytes, not their values, sets the time)."""
+    _, K, N = synth.LM_HEAD
+    base = torch.from_numpy(synth.ternary_ptq(N // 16, K, seed=7)).to(dev)
+    src = base.repeat(16, 1).contiguous()
+    mats = [btf.repack_panels(src, N, K) for _ in range(2)]
+    torch.cuda.synchronize()
+    del src, base
+    peak, peak_src = measured_peaks()
+    nb = btf.gemv_max_nb(K)
+    out = {"shape": f"K{K}_N{N}", "panel_bytes": btf.panel_bytes(N, K), "peak": peak, "peak_source": peak_src}
+    st = torch.cuda.Stream(device=dev)
+    for M in (1, 16):
+        act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=8)).to(dev))
+        y = torch.empty((M, N), device=dev)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(st):
+            for i in range(4):
+                btf.launch_gemv([(mats[i % 2], y, N)], K, M, act, btf.STORE, st)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(reps):
+                btf.launch_gemv([(mats[i % 2], y, N)], K, M, act, btf.STORE, st)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        with torch.cuda.stream(st):
+            g.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        gbs = synth.gemv_bytes(N, K, M) / us / 1e3
+        out[f"M{M}"] = {"us": us, "GB/s": gbs, "frac_of_hbm": gbs / peak, "weight_passes": -(-M // nb),
+                        "bytes_per_launch": synth.gemv_bytes(N, K, M)}
+        del g
+    out["device_error_word"] = btf.device_error()
+    del mats
     return out
 
 
