@@ -29,7 +29,8 @@ from the reference's sources into oracle/_ref, on bounded samples.
 
 --impl reference times the reference's own CPU GEMV (oracle/_ref, built from
 the reference sources; its emulator loop on all host threads) on a bounded
-sample of the same workload.
+sample of the same workload, and adds its CPU emulator's decode step on
+configuration 3's geometry (`decode_config3`, a bounded sample).
 """
 from __future__ import annotations
 
@@ -247,6 +248,10 @@ def run_reference_arm(args):
             "data": "synthetic", "config": {"workload": "config1 layer set, batch 1, CPU emulator GEMV"},
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}, "vs_baseline": None}
+    try:  # benchmark configuration 3 on the reference's CPU emulator (bounded sample)
+        line["decode_config3"] = cpu_decode_reference(threads)
+    except Exception as ex:
+        line["decode_config3"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
     print(json.dumps(line), flush=True)
 
 
