@@ -79,6 +79,10 @@ extern "C" int btf_gemm_f32_noalloc(const btf_gemv_seg* segs, int nseg, int K, i
   if (!segs || nseg < 1 || nseg > 3) return fail(BTF_ERR_ARG, "btf_gemm_f32_noalloc: 1..3 segments (got %d)", nseg);
   if (mode != BTF_STORE && mode != BTF_ADD)
     return fail(BTF_ERR_ARG, "btf_gemm_f32_noalloc: mode must be BTF_STORE or BTF_ADD");
+  for (int i = 0; i < nseg; ++i)  // btf_gemm's segment rules, checked before anything is launched
+    if (!segs[i].panels || (reinterpret_cast<uintptr_t>(segs[i].panels) & 15) || segs[i].N <= 0 || !segs[i].y ||
+        segs[i].ldy < segs[i].N)
+      return fail(BTF_ERR_ARG, "btf_gemm_f32_noalloc: segment %d has a bad panel buffer, N, y or ldy", i);
   if (!current_device()) return BTF_ERR_STATE;
   uint8_t* base = nullptr;
   if (int rc = scratch_base(&base)) return rc;

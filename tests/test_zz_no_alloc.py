@@ -78,3 +78,6 @@ def test_gemm_noalloc_rejects_sizes_beyond_its_array(btf):
     assert rc == 1  # BTF_ERR_ARG
     assert "exceeds the static scratch" in L.btf_last_error().decode()
     assert L.btf_gemm_f32_noalloc(seg, 1, 1000, 64, ctypes.c_void_p(16), 1000, btf.STORE, None) == 1  # K % 128
+    # a segment without panels is refused before anything is launched
+    assert L.btf_gemm_f32_noalloc(seg, 1, 1024, 64, ctypes.c_void_p(16), 1024, btf.STORE, None) == 1
+    assert "segment 0" in L.btf_last_error().decode()
