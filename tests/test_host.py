@@ -36,13 +36,17 @@ def test_layout_sizes(btf):
     assert btf.gemv_max_nb(5120) == 4 and btf.gemv_max_nb(100) == 0
 
 
-@pytest.mark.parametrize("N,K", [(37, 1024), (41, 1152), (16, 128), (1, 5120), (33, 3072)])
-def test_host_repack_matches_reference_t2(btf, orc, N, K):
+@pytest.mark.parametrize("N,K,random_bytes,threads", [(37, 1024, 0, 3), (41, 1152, 0, 3), (16, 128, 0, 3),
+                                                      (1, 5120, 0, 3), (33, 3072, 0, 3), (41, 1152, 1, 1),
+                                                      (300, 1280, 1, 4)])
+def test_host_repack_matches_reference_t2(btf, orc, N, K, random_bytes, threads):
     import oracle
     import synth
 
     src = synth.ternary_ptq(N, K, seed=N + K)
-    pan = btf.repack_panels_host(src, N, K, threads=3)
+    if random_bytes:  # every byte value decodes to five digits, 243..255 included
+        src = np.random.default_rng(N * K).integers(0, 256, size=src.shape, dtype=np.uint8)
+    pan = btf.repack_panels_host(src, N, K, threads=threads)
     assert pan.size == btf.panel_bytes(N, K)
     codes, scales = oracle.panel_decode(pan, N, K)
     c_ref, s_ref = orc.repack_t2(src, N, K)
