@@ -10,7 +10,9 @@
 //     loader for the B200 layout and needs N and K;
 //   - launch_prep runs the whole prep (RMSNorm, permutation, signs, Hadamard, Q8);
 //   - Decoder is the batch-1 decode step over a qwen35 GGUF (btf_decoder_*);
-//     plan_memory sizes it before it is opened (btf_plan_memory).
+//     plan_memory sizes it before it is opened (btf_plan_memory);
+//   - repack_panels_host / PanelMatrix are the host repack (repack / PackedMatrix)
+//     for the panel layout.
 #pragma once
 #include <cuda_runtime_api.h>
 
@@ -144,6 +146,28 @@ class Decoder {
  private:
   void* h_ = nullptr;
 };
+
+// One ternary matrix in the panel layout on the host. Mirrors PackedMatrix /
+// repack / packed_codes_bytes (include/btf/fast.hpp:33-46, src/repack.cpp:16-45)
+// for the panel layout: one buffer of panel_bytes(N, K) holds the codes and the
+// scales. Host only; needs no GPU.
+struct PanelMatrix {
+  int64_t N = 0, K = 0;
+  std::vector<uint8_t> panels;
+};
+inline uint64_t panel_bytes(int64_t N, int64_t K) { return (uint64_t)btf_panel_bytes(N, K); }
+// Repacks a PTQ1_0 tensor of N rows x K columns (src points to row 0) on the
+// host with `threads` threads (0 = all, as FastOptions::threads).
+inline PanelMatrix repack_panels_host(const uint8_t* src, int64_t N, int64_t K, int threads = 0) {
+  if (!src || N <= 0 || K <= 0 || K % 128)
+    throw std::runtime_error("repack_panels_host: null source or bad shape (K a positive multiple of 128)");
+  PanelMatrix m;
+  m.N = N;
+  m.K = K;
+  m.panels.resize(panel_bytes(N, K));
+  throw_if(btf_repack_panels_host(src, N, K, m.panels.data(), threads), "repack_panels_host");
+  return m;
+}
 
 // The decoder's memory before it is opened. Mirrors PlanItem / MemoryPlan /
 // plan_memory (include/btf/fast.hpp:50-69, src/repack.cpp:114-204) for the

@@ -148,3 +148,22 @@ def test_decoder_stats_reject_null_handles(btf):
     s = btf.StepStatsC()
     assert L.btf_decoder_stats(None, ctypes.byref(s)) == 1
     assert L.btf_decoder_reset_stats(None) == 1
+
+
+def test_cpp_shim_host_repack_equals_the_c_abi(btf, tmp_path):
+    # btf::cuda::repack_panels_host (include/btf_b200.hpp) linked against the library, no GPU
+    import synth
+
+    exe = str(tmp_path / "shim_repack")
+    r = subprocess.run(["g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include",
+                        os.path.join(ROOT, "tests", "shim_repack.cpp"), "-o", exe, "-L", PKG, "-lbtf_b200",
+                        f"-Wl,-rpath,{PKG}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    N, K = 41, 1152
+    src = synth.ternary_ptq(N, K, seed=5)
+    (tmp_path / "src.bin").write_bytes(src.tobytes())
+    r = subprocess.run([exe, str(N), str(K), str(tmp_path / "src.bin"), str(tmp_path / "pan.bin")],
+                       capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    got = np.frombuffer((tmp_path / "pan.bin").read_bytes(), dtype=np.uint8)
+    assert np.array_equal(got, btf.repack_panels_host(src, N, K, threads=1))
