@@ -512,7 +512,7 @@ def gpu_arm(args):
                          "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,SWIGLU> gate+up",
                          "bytes_per_launch": dom_bytes, "launch_us": kern_ms["gateup"] * 1e3,
                          "timing": "CUDA events around the GEMV launch of the last layer of each timed step",
-                         "peak_source": peak_kind},
+                         "peak_source": peak_kind, "frac_of_spec_8000": dom_ach / 8000.0},
             "kernels": kernels,
             "fused_quantise_path": {"value": fused_v, "unit": UNIT, "note": "btf_gemv_f32: quantisation inside "
                                     "each GEMV (4-CTA clusters), 4 launches per layer (same bytes counted)"}
