@@ -39,7 +39,7 @@ EXPORTS = (
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
     "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
-    "btf_gemm_f32_noalloc",
+    "btf_gemm_f32_noalloc", "btf_chain_program_bytes", "btf_chain_encode", "btf_chain_run",
 )
 
 
@@ -53,6 +53,20 @@ class Q8ActC(ctypes.Structure):
     """btf_q8act: Q8_0 activations (Q8Act, kernels.cuh:27-31)."""
 
     _fields_ = [("q", ctypes.c_void_p), ("d", ctypes.c_void_p), ("s", ctypes.c_void_p)]
+
+
+class ChainOpC(ctypes.Structure):
+    """btf_chain_op: one matmul call site of a persistent GEMV chain."""
+
+    _fields_ = [("segs", GemvSeg * 3), ("nseg", ctypes.c_int), ("K", ctypes.c_int), ("mode", ctypes.c_int),
+                ("x", ctypes.c_void_p), ("ldx", ctypes.c_int), ("normw", ctypes.c_void_p), ("eps", ctypes.c_float)]
+
+
+class ChainC(ctypes.Structure):
+    """btf_chain: an encoded chain (program buffer + launch shape)."""
+
+    _fields_ = [("program", ctypes.c_void_p), ("n_ops", ctypes.c_int), ("M", ctypes.c_int), ("max_K", ctypes.c_int),
+                ("grid", ctypes.c_int), ("depth", ctypes.c_int), ("smem", ctypes.c_int)]
 
 
 _lib: Optional[ctypes.CDLL] = None
@@ -155,6 +169,9 @@ def lib() -> ctypes.CDLL:
         "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
         "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
         "btf_gemm_f32_noalloc": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
+        "btf_chain_program_bytes": (i64, [i32]),
+        "btf_chain_encode": (i32, [ctypes.POINTER(ChainOpC), i32, i32, vp, ctypes.POINTER(ChainC)]),
+        "btf_chain_run": (i32, [ctypes.POINTER(ChainC), vp]),
         "btf_gemv_gather": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, ctypes.POINTER(GatherC), vp]),
         "btf_alloc": (i32, [ctypes.c_size_t, ctypes.POINTER(vp)]),
         "btf_free": (i32, [vp]),
@@ -373,6 +390,53 @@ def launch_gemm_f32_noalloc(segs: Sequence[tuple], K: int, M: int, x, mode: int 
     intermediate lives in the library's fixed device array, M * K <= GEMM_NOALLOC_MAX_MK."""
     check(lib().btf_gemm_f32_noalloc(_segs(segs), len(segs), K, M, _ptr(x), x.stride(0), mode, _stream(stream)),
           "btf_gemm_f32_noalloc")
+
+
+@dataclass
+class ChainOp:
+    """One matmul call site of a GEMV chain: btf_gemv(segs, K, Q8(prep(x)), mode) with
+    prep = RMSNorm with `normw` (None: no norm). segs: (PanelMatrix, y or None, ldy)."""
+
+    segs: Sequence[tuple]
+    K: int
+    mode: int
+    x: object
+    normw: object = None
+    eps: float = 1e-6
+
+
+class Chain:
+    """A persistent GEMV chain (btf_chain_encode / btf_chain_run): the ops run in
+    order in one launch, each reading what the ops before it wrote. The program
+    buffer is a device tensor held by this object; the tensors the ops name must
+    stay alive (they are kept here)."""
+
+    def __init__(self, ops: Sequence[ChainOp], M: int = 1):
+        torch = _torch()
+        n = len(ops)
+        arr = (ChainOpC * n)()
+        for i, op in enumerate(ops):
+            c = ChainOpC()
+            for k, (pm, y, ldy) in enumerate(op.segs):
+                c.segs[k] = GemvSeg(_ptr(pm.panels), pm.N, _ptr(y), ldy)
+            c.nseg, c.K, c.mode = len(op.segs), op.K, op.mode
+            c.x, c.ldx = _ptr(op.x), op.x.stride(0)
+            c.normw, c.eps = _ptr(op.normw), op.eps
+            arr[i] = c
+        dev = ops[0].x.device
+        ensure_init(dev.index)
+        nbytes = lib().btf_chain_program_bytes(n)
+        self.program = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self.c = ChainC()
+        check(lib().btf_chain_encode(arr, n, M, _ptr(self.program), ctypes.byref(self.c)), "btf_chain_encode")
+        self.ops = list(ops)
+
+    @property
+    def grid(self) -> int:
+        return self.c.grid
+
+    def run(self, stream=None) -> None:
+        check(lib().btf_chain_run(ctypes.byref(self.c), _stream(stream)), "btf_chain_run")
 
 
 def device_error(clear: bool = False) -> int:

@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 
 namespace btf {
 namespace {
@@ -113,57 +114,7 @@ struct GemvParams {
   btf_gather gather;   // world == 0: plain launch; else the epilogue all-gathers over NVLink
 };
 
-// Per-row code dots of one row quad over one 32-column sub-block. cw0/cw1:
-// the quad words of columns 0..15 / 16..31; qa/qb: the activation words of the
-// same columns. c[k] = 4^k * code_dot(row k) accumulated onto c[k].
-__device__ __forceinline__ void quad_dots(const uint4& cw0, const uint4& cw1, const uint4& qa, const uint4& qb,
-                                          int c[4]) {
-  const uint32_t w[8] = {cw0.x, cw0.y, cw0.z, cw0.w, cw1.x, cw1.y, cw1.z, cw1.w};
-  const uint32_t a[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    c[0] = dp4a_us(w[i] & 0x03030303u, a[i], c[0]);
-    c[1] = dp4a_us(w[i] & 0x0c0c0c0cu, a[i], c[1]);
-    c[2] = dp4a_us(w[i] & 0x30303030u, a[i], c[2]);
-    c[3] = dp4a_us(w[i] & 0xc0c0c0c0u, a[i], c[3]);
-  }
-}
-
-// kMagicInt + idot of row k from its quad accumulator (exact shift) and
-// magic_s = kMagicInt - sum(q).
-template <int k>
-__device__ __forceinline__ int biased_idot(int c, int magic_s) { return (c >> (2 * k)) + magic_s; }
-
-__device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 & 0xffffu))); }
-__device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((unsigned short)(h2 >> 16))); }
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
-
-// Sums v[0..7] over the 32 lanes by recursive halving: after 9 shuffles lane l
-// holds in v[0] the total of row r(l) = 4*bit4(l) + 2*bit3(l) + bit2(l) (the 4
-// lanes of a group of four hold the same row). Returns r(l).
-__device__ __forceinline__ int reduce_rows8(float (&v)[8], int lane) {
-  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {  // keep rows 0..3 (b4 = 0) or 4..7 (b4 = 1)
-    const float send = b4 ? v[i] : v[i + 4];
-    const float keep = b4 ? v[i + 4] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float send = b3 ? v[i] : v[i + 2];
-    const float keep = b3 ? v[i + 2] : v[i];
-    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  {
-    const float send = b2 ? v[0] : v[1];
-    const float keep = b2 ? v[1] : v[0];
-    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  }
-  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
-  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
-  return 4 * (int)b4 + 2 * (int)b3 + (int)b2;
-}
+using namespace core;
 
 // Shared-memory layout (bytes), identical on host and device.
 struct SmemPlan {

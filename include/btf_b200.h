@@ -178,6 +178,55 @@ int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
 int btf_gemm_f32_noalloc(const btf_gemv_seg* segs, int nseg, int K, int M, const float* x, int ldx, int mode,
                          void* stream);
 
+/* ---- persistent GEMV chain: a decoder's sequence of matmul call sites in ONE launch
+ * Replaces the per-matmul launch_prep + launch_gemv pairs that the reference
+ * decoder issues into its captured stream for one token (GpuDecoder::forward_chunk /
+ * gdn_layer / attn_layer, src/cuda/gpu_decoder.cu:401-450; launchers
+ * src/cuda/kernels.cu:745-822) when each matmul's input is written by the matmul
+ * before it. Op i is btf_gemv(segs, nseg, K, M, Q8(prep(x)), mode) with prep =
+ * RMSNorm with normw (when normw != NULL; bd::rmsnorm's formula,
+ * ref/bonsai-decoder/src/cpu_ops.cpp:113-127, its double sum of squares taken in a
+ * fixed parallel order) and Q8 = btf_quant_q8's rule. Ops run in order: op i+1
+ * reads its x only after every output of ops 0..i is stored, exactly as if each op
+ * were its own launch in one stream, so any op may read what earlier ops wrote
+ * (including in-place BTF_ADD outputs). One persistent grid runs all ops; the
+ * weight panels of later ops stream into shared memory while earlier ops finish. */
+typedef struct btf_chain_op {
+  btf_gemv_seg segs[3]; /* btf_gemv's segments; nseg used */
+  int nseg;
+  int K;               /* K % 128 == 0 */
+  int mode;            /* BTF_STORE / BTF_ADD / BTF_SWIGLU */
+  const float* x;      /* fp32 input [M][ldx], 4-byte aligned */
+  int ldx;             /* >= K */
+  const float* normw;  /* RMSNorm weight [K] applied before Q8, or NULL */
+  float eps;           /* RMSNorm epsilon */
+} btf_chain_op;
+
+/* An encoded chain (filled by btf_chain_encode; pass it to btf_chain_run). */
+typedef struct btf_chain {
+  void* program; /* the caller's device buffer holding the encoded ops and counters */
+  int n_ops;
+  int M;         /* activation rows, 1..2 */
+  int max_K;     /* widest op input, in columns padded to 1024 */
+  int grid;      /* CTAs of one run (persistent, all co-resident) */
+  int depth;     /* weight-ring slots per warp */
+  int smem;      /* dynamic shared memory per CTA */
+} btf_chain;
+
+/* Device bytes of the program buffer of an n_ops chain. */
+int64_t btf_chain_program_bytes(int n_ops);
+/* Validates and encodes ops[0..n_ops) for M activation rows into `program` (a
+ * caller-owned, 256-byte-aligned device buffer of btf_chain_program_bytes(n_ops)
+ * bytes) on the current device. Set-up call: it copies synchronously, so make it
+ * outside stream capture. The pointers in ops are used by every later run. */
+int btf_chain_encode(const btf_chain_op* ops, int n_ops, int M, void* program, btf_chain* chain);
+/* One run of the whole chain: one launch, asynchronous, allocates nothing, legal
+ * inside CUDA graph capture. The grid waits on itself, so do not run other
+ * kernels concurrently on this device that could keep its CTAs from being resident
+ * (a CTA that waits 1 s gives up: BTF error word set, outputs incomplete). Runs of
+ * one program must be ordered (one stream). */
+int btf_chain_run(const btf_chain* chain, void* stream);
+
 /* Debug/parity entry point: the exact int32 trit dot of every (m, row,
  * sub-block), idot[M][N][K/32] = code_dot - sum(q) — the integers the GEMV
  * scales (src/emu_decoder.cpp:154-157). Same decode path as btf_gemv. */
