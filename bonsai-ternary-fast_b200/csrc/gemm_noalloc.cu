@@ -15,8 +15,6 @@
 // The array belongs to the module: every GPU that loads the library holds its
 // own copy of it until the process exits. Its size fixes the largest call,
 // M*K <= BTF_GEMM_NOALLOC_MAX_MK.
-#include <mutex>
-
 #include "common.cuh"
 
 namespace btf {
@@ -29,10 +27,6 @@ constexpr int64_t kSBytes = kMaxMK / 32 * 4;        // int32 s [M][K/32]
 static_assert(kMaxMK % (32 * 64) == 0, "every region starts on a 256-byte boundary");
 static_assert(kQBytes % 256 == 0 && kDBytes % 256 == 0, "q, d and s start 256-byte aligned");
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};  // device address of the array, per device (set on first use)
-
 }  // namespace
 
 // The Q8 activation of the most recent call on this device: q, then d, then s.
@@ -42,22 +36,15 @@ static __device__ __align__(256) uint8_t g_q8_scratch[kQBytes + kDBytes + kSByte
 
 namespace {
 
-// Device address of g_q8_scratch on the current device. The first call on a
-// device looks it up (which also loads this module on that device) and keeps it.
+// Device address of g_q8_scratch on the current device, looked up on every
+// call (a cheap host-side lookup once the module is loaded on the device). No
+// address is cached, so a cudaDeviceReset followed by btf_init, which loads the
+// module again and may place the array elsewhere, is handled.
 int scratch_base(uint8_t** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "btf_gemm_f32_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices)
-    return fail(BTF_ERR_UNSUPPORTED, "btf_gemm_f32_noalloc: device %d beyond %d", dev, kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_q8_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "btf_gemm_f32_noalloc: cudaGetSymbolAddress");
-    g_scratch_addr[dev] = p;
-  }
-  *out = static_cast<uint8_t*>(g_scratch_addr[dev]);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_q8_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_gemm_f32_noalloc: cudaGetSymbolAddress");
+  *out = static_cast<uint8_t*>(p);
   return BTF_OK;
 }
 

@@ -120,9 +120,18 @@ extern "C" int btf_repack_panels_host(const void* ptq_src_host, int64_t N, int64
     btf::repack_groups(src, N, K, dst, 0, G);
     return BTF_OK;
   }
+  // Threads that cannot be created (std::system_error) or a failed allocation
+  // must not unwind across the C ABI: the groups the pool did not start are
+  // repacked on this thread instead, after joining the threads that did start.
   std::vector<std::thread> pool;
-  for (int i = 0; i < t; ++i)
-    pool.emplace_back(btf::repack_groups, src, N, K, dst, G * i / t, G * (i + 1) / t);
+  int started = 0;
+  try {
+    pool.reserve((size_t)t);
+    for (; started < t; ++started)
+      pool.emplace_back(btf::repack_groups, src, N, K, dst, G * started / t, G * (started + 1) / t);
+  } catch (...) {
+  }
   for (auto& th : pool) th.join();
+  if (started < t) btf::repack_groups(src, N, K, dst, G * started / t, G);
   return BTF_OK;
 }

@@ -168,8 +168,9 @@ int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
  *   - Limit: M * K <= BTF_GEMM_NOALLOC_MAX_MK (512 x 17408); larger calls return
  *     BTF_ERR_ARG. Every GPU that loads the library holds the array
  *     (BTF_GEMM_NOALLOC_MAX_MK * 1.25 bytes, about 11 MB) until the process exits.
- *   - The first call on a device looks up the array's device address; make that
- *     first call outside any stream capture.
+ *   - Every call looks up the array's device address (cudaGetSymbolAddress); the
+ *     first call on a device may also load the library's module there, so make
+ *     that first call outside any stream capture.
  *   - All calls on a device share the one array: calls that can overlap on the
  *     GPU (different streams without ordering between them) race. Calls in one
  *     stream are ordered and safe.

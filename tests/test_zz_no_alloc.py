@@ -68,6 +68,37 @@ def test_gemm_noalloc_matches_two_call_route(cuda, btf, orc):
     assert rel_rms(y_one, want) <= TOL, rel_rms(y_one, want)
 
 
+@pytest.mark.gpu
+def test_gemm_noalloc_strided_and_unaligned_x(cuda, btf):
+    """x as a strided view (ldx = K + 4) and x at a base pointer 4 bytes past a
+    16-byte boundary: both take the quantiser's scalar-load path. Each call is
+    compared with the two-call route on the same view, two calls in a row."""
+    import torch
+
+    M, K, N = 80, 1024, 96
+    src = synth.ternary_ptq(N, K, seed=61)
+    pm = btf.repack_panels(torch.from_numpy(src).to(cuda), N, K)
+    wide = torch.from_numpy(synth.activations(M, K + 4, seed=62)).to(cuda)
+    flat = torch.from_numpy(synth.activations(1, M * K + 4, seed=63).reshape(-1)).to(cuda)
+    views = {"strided": wide[:, :K], "offset": flat[1:1 + M * K].view(M, K)}
+    assert views["strided"].stride(0) == K + 4 and views["offset"].data_ptr() % 16 == 4
+    for name, x in views.items():
+        act = btf.Q8Act.empty(M, K, cuda)
+        L = btf.lib()
+        import ctypes as C
+
+        st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = L.btf_quant_q8(C.c_void_p(x.data_ptr()), x.stride(0), M, K, act.c(), st)
+        assert rc == 0, L.btf_last_error().decode()
+        y_two = torch.full((M, N), 5.0, device=cuda)
+        y_one = torch.full((M, N), -5.0, device=cuda)
+        btf.launch_gemm([(pm, y_two, N)], K, M, act, btf.STORE)
+        _noalloc(btf, [(pm, y_one, N)], K, M, x, btf.STORE)
+        torch.cuda.synchronize()
+        assert btf.device_error() == 0
+        assert rel_rms(y_one.cpu().numpy(), y_two.cpu().numpy()) <= TOL, name
+
+
 def test_gemm_noalloc_rejects_sizes_beyond_its_array(btf):
     """M * K above the array's size is refused before any CUDA call (runs without a GPU)."""
     L = btf.lib()
