@@ -334,36 +334,36 @@ def gpu_arm(args):
 
     stream = torch.cuda.Stream(device=dev)
 
-    # per-kernel timing events around the launches of the last layer of a step
+    # kernel end stamps (btf_stamp_next) in the timed graph: slot 8 * layer + k for
+    # k = quantiser / GEMV of q,k,v | o | gate,up | down; they cost no event nodes,
+    # so the programmatic-dependent-launch chain stays intact
     kinds = ("qkv", "o", "gateup", "down")
-    evs = {k: (torch.cuda.Event(enable_timing=True, external=True),
-               torch.cuda.Event(enable_timing=True, external=True)) for k in kinds}
+    stamps = torch.zeros(N_LAYERS * 8, dtype=torch.int64, device=dev)
+    fstamps = torch.zeros(N_LAYERS * 4, dtype=torch.int64, device=dev)  # the fused path: one launch per GEMV
 
-    def layer(L, li, timed=False, fused=True):
+    def layer(L, li, stamped=False, fused=True):
         # fused: quantisation inside each GEMV (btf_gemv_f32, 4 launches per layer);
         # otherwise the drop-in pair launch_prep -> launch_gemv (8 launches per layer)
-        def t0(k):
-            if timed:
-                evs[k][0].record(stream)
-
-        def t1(k):
-            if timed:
-                evs[k][1].record(stream)
+        def st_(k):
+            if stamped:
+                btf.stamp_next(stamps.data_ptr() + 8 * (8 * li + k))
 
         def gemv(segs, K, xk, mode, kind):
-            # timed layer: the events bracket the GEMV launch alone (after its quantiser)
+            ki = kinds.index(kind)
             if world > 1:  # drop-in pair with the all-gather in the GEMV epilogue
+                st_(2 * ki)
                 btf.quant_q8(x_in[xk], acts[xk], stream=stream)
-                t0(kind)
+                st_(2 * ki + 1)
                 btf.launch_gemv_gather(segs, K, 1, acts[xk], mode, gdesc[li][kind], stream)
             elif fused:
-                t0(kind)
+                if stamped:
+                    btf.stamp_next(fstamps.data_ptr() + 8 * (4 * li + ki))
                 btf.launch_gemv_f32(segs, K, 1, x_in[xk], mode, stream)
             else:
+                st_(2 * ki)
                 btf.quant_q8(x_in[xk], acts[xk], stream=stream)
-                t0(kind)
+                st_(2 * ki + 1)
                 btf.launch_gemv(segs, K, 1, acts[xk], mode, stream)
-            t1(kind)
 
         def seg(n):
             r = model.rows[n]
@@ -376,11 +376,11 @@ def gpu_arm(args):
         if world > 1:  # every rank's rows of this layer's outputs have arrived
             btf.gather_wait(gwait[li], arena.epoch_ptr, stream)
 
-    def step(fused=False):
+    def step(fused=False, stamped=False):
         if world > 1:
             btf.gather_epoch_advance(arena.epoch_ptr, stream)
         for i, L in enumerate(model.layers):
-            layer(L, i, timed=(i == len(model.layers) - 1) and not fused, fused=fused)
+            layer(L, i, stamped=stamped, fused=fused)
         if world > 1:
             btf.gather_barrier(gbar, stream)
 
@@ -407,12 +407,12 @@ def gpu_arm(args):
     torch.cuda.synchronize()
     g_dev, g_e2e, g_unf = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_dev, stream=stream):
-        step()
+        step(stamped=True)
     with torch.cuda.graph(g_e2e, stream=stream):
         step_e2e()
     if world == 1:  # with N > 1 the step always runs the gathering pairs
         with torch.cuda.graph(g_unf, stream=stream):
-            step(fused=True)
+            step(fused=True, stamped=True)
     torch.cuda.synchronize()
 
     def timed(graph, K, W):
@@ -445,7 +445,14 @@ def gpu_arm(args):
     clocks.start()
     ms_dev = timed(g_dev, args.steps, args.warmup)
     clocks.stop()
-    kern_ms = {k: evs[k][0].elapsed_time(evs[k][1]) for k in kinds}
+    # exclusive time of each launch in the last timed replay: its end minus the end
+    # of the launch before it (layers 1..63; layer 0's first launch follows the
+    # previous replay); the eight per-layer means add up to the layer time
+    ends = stamps.cpu().numpy().astype(np.float64).reshape(N_LAYERS, 8)
+    excl = np.diff(ends.reshape(-1))[7:].reshape(N_LAYERS - 1, 8) / 1e3  # us
+    excl_us = excl.mean(axis=0)
+    kern_ms = {k: excl_us[2 * i + 1] / 1e3 for i, k in enumerate(kinds)}  # the GEMV launches alone
+    quant_ms = {k: excl_us[2 * i] / 1e3 for i, k in enumerate(kinds)}
     ms_e2e = timed(g_e2e, args.steps, args.warmup)
     ms_unf = timed(g_unf, args.steps, args.warmup) if world == 1 else None
     dev_err = btf.device_error()
@@ -477,6 +484,13 @@ def gpu_arm(args):
         "gateup": 2 * synth.gemv_bytes(sh["gate"][1], 5120) - 5120 * 5 // 4 - sh["gate"][1] * 4,
         "down": synth.gemv_bytes(sh["down"][1], sh["down"][0], add=True),
     }
+    fused_kernels = None
+    if ms_unf:
+        fe = fstamps.cpu().numpy().astype(np.float64).reshape(-1)
+        fx = (np.diff(fe)[3:].reshape(N_LAYERS - 1, 4) / 1e3).mean(axis=0)
+        fused_kernels = {k: {"us": float(fx[i]), "GB/s": kernel_bytes[k] / (fx[i] * 1e-6) / 1e9}
+                         for i, k in enumerate(kinds)}
+        fused_kernels["sum_us_per_layer"] = float(fx.sum())
     peak, peak_kind = measured_peaks()
     # dominant kernel: the gate/up swiglu GEMV (52 % of the step's bytes); on this rank's shard
     dom_bytes = kernel_bytes["gateup"] / world
@@ -487,8 +501,15 @@ def gpu_arm(args):
         for line in open(tpath):
             if line.startswith("dram_bytes_per_launch:"):
                 traffic = int(line.split(":")[1].strip()) // world
-    kernels = {k: {"us": kern_ms[k] * 1e3, "GB/s": (kernel_bytes[k] / world) / (kern_ms[k] * 1e-3) / 1e9}
+    kernels = {k: {"us": kern_ms[k] * 1e3, "GB/s": (kernel_bytes[k] / world) / (kern_ms[k] * 1e-3) / 1e9,
+                   "quantiser_us": quant_ms[k] * 1e3,
+                   "pair_GB/s": (kernel_bytes[k] / world) / ((kern_ms[k] + quant_ms[k]) * 1e-3) / 1e9}
                for k in kinds}
+    kernels["sum_us_per_layer"] = float(excl_us.sum())
+    kernels["layer_us_from_ms_per_step"] = ms_dev / args.steps * 1e3 / N_LAYERS
+    kernels["timing"] = ("exclusive time per launch in the timed graph: its end stamp (btf_stamp_next: the last "
+                         "CTA's global timer) minus the previous launch's, mean over layers 1..63 of the last "
+                         "timed replay; no events between launches")
 
     dec3 = None
     if world > 1:  # collective: the tensor-parallel decode step on every rank
@@ -511,10 +532,13 @@ def gpu_arm(args):
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
                          "frac": dom_ach / peak, "traffic": traffic, "kernel": "gemv_kernel<1,SWIGLU> gate+up",
                          "bytes_per_launch": dom_bytes, "launch_us": kern_ms["gateup"] * 1e3,
-                         "timing": "CUDA events around the GEMV launch of the last layer of each timed step",
+                         "timing": "exclusive time of the gate+up GEMV launch inside the timed graph (its end "
+                                   "stamp minus its quantiser's end stamp), mean over 63 layers; the eight "
+                                   "launches of a layer add up to the layer time",
                          "peak_source": peak_kind, "frac_of_spec_8000": dom_ach / 8000.0},
             "kernels": kernels,
-            "fused_quantise_path": {"value": fused_v, "unit": UNIT, "note": "btf_gemv_f32: quantisation inside "
+            "fused_quantise_path": {"value": fused_v, "unit": UNIT, "kernels": fused_kernels,
+                                    "note": "btf_gemv_f32: quantisation inside "
                                     "each GEMV (4-CTA clusters), 4 launches per layer (same bytes counted)"}
             if world == 1 else None,
             "device_error_word": dev_err,
@@ -525,6 +549,13 @@ def gpu_arm(args):
             "clocks": clocks.report(),
         }
         if world == 1:
+            try:
+                line["reference_gpu_baseline"] = reference_gpu_baseline(torch, dev, step_bytes, args.steps,
+                                                                         args.warmup)
+                line["reference_gpu_baseline"]["product_over_reference"] = (
+                    value / line["reference_gpu_baseline"]["value"])
+            except Exception as ex:  # a baseline leg must not cost the product line
+                line["reference_gpu_baseline"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
             line["prefill_gemm_config2"] = prefill_gemm(btf, torch, dev)
             line["decode_config3"] = decode_config3(btf, torch, dev)
             try:  # last of the GPU legs, so that a failure here costs only this entry
@@ -547,6 +578,88 @@ def gpu_arm(args):
         arena.close()
         dist.barrier()
         dist.destroy_process_group()
+
+
+def reference_gpu_baseline(torch, dev, step_bytes, steps, warmup):
+    """The reference's OWN GPU matmul path on the same workload, as the GPU number to
+    beat: its launch_prep (Q8 only) + launch_gemv (src/cuda/kernels.cu, built
+    unmodified for sm_100a into oracle/_ref/libbtf_ref_gpu.so) over the same 64
+    layers of config-1 weights, repacked to its T2 layout by its own launch_repack,
+    in the same call order and captured as one CUDA graph per step (as its decoder
+    captures its step). Same algorithmic bytes per step as the product's line."""
+    if os.path.join(ROOT, "oracle") not in sys.path:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    if not oracle.ReferenceGPU.available():
+        return {"unavailable": "oracle/_ref/libbtf_ref_gpu.so is not built (reference tree absent at build time)"}
+    R = oracle.ReferenceGPU()
+    R.init(dev.index)
+    st = torch.cuda.Stream(device=dev)
+    sh = {name: (K, N) for name, K, N in synth.LAYER_SHAPES}
+    layer0 = {}
+    for name, (K, N) in sh.items():
+        src = torch.from_numpy(synth.ternary_ptq(N, K, seed=0)).to(dev)
+        codes = torch.empty(N * K // 4, dtype=torch.uint8, device=dev)
+        scales = torch.empty(N * K // 128, dtype=torch.int16, device=dev)
+        R.repack(src.data_ptr(), N * K // 128, codes.data_ptr(), scales.data_ptr(), st.cuda_stream)
+        layer0[name] = (codes, scales)
+    torch.cuda.synchronize()
+    layers = [layer0] + [{n: (c.clone(), s.clone()) for n, (c, s) in layer0.items()} for _ in range(N_LAYERS - 1)]
+    xs = {k: torch.from_numpy(synth.activations(1, k, seed=2 + i)).to(dev) for i, k in enumerate((5120, 6144, 17408))}
+    x_in = {"attn": xs[5120], "o": xs[6144], "ffn": xs[5120].clone(), "down": xs[17408]}
+    acts = {k: (torch.empty(v.shape[1], dtype=torch.int8, device=dev),
+                torch.empty(v.shape[1] // 32, dtype=torch.float32, device=dev),
+                torch.empty(v.shape[1] // 32, dtype=torch.int32, device=dev)) for k, v in x_in.items()}
+    ys = {n: torch.zeros((1, sh[n][1]), device=dev) for n in sh if n != "up"}
+
+    def gemv(names, xk, mode):
+        K = sh[names[0]][0]
+        x = x_in[xk]
+        q, d, s = acts[xk]
+        R.quant(x.data_ptr(), K, 1, K, q.data_ptr(), d.data_ptr(), s.data_ptr(), st.cuda_stream)
+        segs = []
+        for n in names:
+            c, sc = L[n]
+            y = ys.get(n)
+            segs.append((c.data_ptr(), sc.data_ptr(), sh[n][1], y.data_ptr() if y is not None else 0,
+                         sh[n][1] if y is not None else 0))
+        R.gemv(segs, K, 1, q.data_ptr(), d.data_ptr(), s.data_ptr(), mode, st.cuda_stream)
+
+    def step():
+        nonlocal L
+        for L in layers:
+            gemv(("q", "k", "v"), "attn", 0)
+            gemv(("o",), "o", 1)
+            gemv(("gate", "up"), "ffn", 2)
+            gemv(("down",), "down", 1)
+
+    L = None
+    with torch.cuda.stream(st):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        step()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    with torch.cuda.stream(st):
+        for _ in range(steps):
+            g.replay()
+    b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    out = {"value": step_bytes / (ms * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": ms, "steps": steps,
+           "kind": "reference", "path": "reference launch_prep (Q8) + launch_gemv, src/cuda/kernels.cu built "
+                                          "unmodified for sm_100a, T2 weights from its launch_repack, one CUDA graph "
+                                          "per step, same call order and bytes as the product line",
+           "gpu_launches": steps * N_LAYERS * 8}
+    del g, layers, layer0
+    torch.cuda.empty_cache()
+    return out
 
 
 PREFILL_SHAPES = ((64, 5120, 17408), (512, 5120, 17408), (64, 17408, 5120), (512, 17408, 5120))

@@ -39,7 +39,7 @@ EXPORTS = (
     "btf_decoder_reset", "btf_decoder_close", "btf_decoder_get_info", "btf_decoder_synthetic_tp",
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
     "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
-    "btf_gemm_f32_noalloc", "btf_chain_program_bytes", "btf_chain_encode", "btf_chain_run",
+    "btf_gemm_f32_noalloc", "btf_chain_program_bytes", "btf_chain_encode", "btf_chain_run", "btf_stamp_next",
 )
 
 
@@ -170,6 +170,7 @@ def lib() -> ctypes.CDLL:
         "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
         "btf_gemm_f32_noalloc": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
         "btf_chain_program_bytes": (i64, [i32]),
+        "btf_stamp_next": (i32, [vp]),
         "btf_chain_encode": (i32, [ctypes.POINTER(ChainOpC), i32, i32, vp, ctypes.POINTER(ChainC)]),
         "btf_chain_run": (i32, [ctypes.POINTER(ChainC), vp]),
         "btf_gemv_gather": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, ctypes.POINTER(GatherC), vp]),
@@ -437,6 +438,12 @@ class Chain:
 
     def run(self, stream=None) -> None:
         check(lib().btf_chain_run(ctypes.byref(self.c), _stream(stream)), "btf_chain_run")
+
+
+def stamp_next(slot_ptr: Optional[int]) -> None:
+    """The next quantiser / GEMV launch from this thread records its end time
+    (global timer, ns; atomic max over its CTAs) at device address slot_ptr."""
+    check(lib().btf_stamp_next(slot_ptr), "btf_stamp_next")
 
 
 def device_error(clear: bool = False) -> int:

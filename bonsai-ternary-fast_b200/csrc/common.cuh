@@ -287,6 +287,18 @@ __device__ __forceinline__ void st_cluster_b32(uint32_t addr, uint32_t v) {
 // Device-side error word (time-outs of bounded waits); read by btf_device_error().
 constexpr int kErrWaitTimeout = 1;
 
+// Kernel end stamps (btf_stamp_next): the slot requested for the next launch made
+// by this host thread, or nullptr; taking it clears the request.
+unsigned long long* take_stamp();
+// Called by every thread of a CTA at its very end (CTA-uniform `slot`): once
+// the CTA's work is done, thread 0 raises *slot to the global timer (ns), so
+// after the launch *slot is the end time of its last CTA.
+__device__ __forceinline__ void stamp_end(unsigned long long* slot) {
+  if (slot == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) atomicMax(slot, (unsigned long long)globaltimer_ns());
+}
+
 // Launches kern<<<grid, block, smem, st>>> with programmatic stream
 // serialisation enabled, so it may overlap the tail of the previous kernel.
 template <typename... KArgs, typename... Args>

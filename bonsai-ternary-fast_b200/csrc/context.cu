@@ -9,6 +9,7 @@ namespace btf {
 
 namespace {
 thread_local std::string g_last_error;
+thread_local unsigned long long* g_stamp_next = nullptr;
 constexpr int kMaxDevices = 64;
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -26,6 +27,12 @@ int fail(int status, const char* fmt, ...) {
 
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(BTF_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+unsigned long long* take_stamp() {
+  unsigned long long* s = g_stamp_next;
+  g_stamp_next = nullptr;
+  return s;
 }
 
 const DeviceInfo* current_device() {
@@ -67,7 +74,14 @@ const char* btf_status_string(int status) {
 
 const char* btf_last_error(void) { return g_last_error.c_str(); }
 
-const char* btf_version(void) { return "btf_b200 0.1 (sm_100a)"; }
+const char* btf_version(void) { return "btf_b200 0.2 (sm_100a)"; }
+
+int btf_stamp_next(unsigned long long* slot) {
+  if (slot && (reinterpret_cast<uintptr_t>(slot) & 7))
+    return fail(BTF_ERR_ARG, "btf_stamp_next: the slot must be 8-byte aligned");
+  g_stamp_next = slot;
+  return BTF_OK;
+}
 
 int btf_init(int device) {
   if (device < 0 || device >= kMaxDevices) return fail(BTF_ERR_ARG, "btf_init: device %d out of range", device);

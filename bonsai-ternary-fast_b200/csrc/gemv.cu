@@ -112,6 +112,7 @@ struct GemvParams {
   int slots;           // ring slots of a CTA, shared by the warps that have work
   int* err;
   btf_gather gather;   // world == 0: plain launch; else the epilogue all-gathers over NVLink
+  unsigned long long* stamp;  // end stamp slot (btf_stamp_next) or null
 };
 
 using namespace core;
@@ -547,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
     }
   }
   if constexpr (GATHER == 1) gather_arrive(p.gather, p.err);
+  stamp_end(p.stamp);
 }
 
 // Cross-rank barrier (one thread): the release-adds / bounded acquire wait of
@@ -749,6 +751,7 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
   p.ldx = ldx;
   p.err = dev->err_word;
   if (gather) p.gather = *gather;
+  p.stamp = take_stamp();  // every pass raises it: the slot ends as the last pass's end
   for (int m0 = 0; m0 < M; m0 += kMaxNb) {
     const int nb = std::min(kMaxNb, M - m0);
     const int NB = nb <= 1 ? 1 : nb <= 2 ? 2 : 4;

@@ -150,6 +150,18 @@ int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* 
  * not for use inside stream capture. clear != 0 resets it. Returns -1 on failure. */
 int btf_device_error(int clear);
 
+/* Measurement hook, no counterpart in the reference: the next btf_quant_q8 or
+ * btf_gemv / btf_gemv_f32 / btf_gemv_gather call made by this host thread makes
+ * its kernel raise *slot (device memory, 8-byte aligned) to the device's global
+ * timer in ns as each CTA finishes, so after the launch *slot holds the end time
+ * of its last CTA (atomic max: a slot that starts at 0, or keeps an earlier
+ * replay's stamp, ends with this launch's end). The request applies to one call
+ * and is then cleared; slot = NULL clears it. Legal during stream capture: a
+ * captured launch stamps the same slot at every replay. Exclusive kernel times
+ * (end minus the previous kernel's end) then add up to the step time without
+ * events between the launches, which would break programmatic dependent launch. */
+int btf_stamp_next(unsigned long long* slot);
+
 /* ---- ternary GEMM for prefill batches (M >= 64): tcgen05 int8 tensor cores
  * (kind::i8, one exact 32-deep MMA step per activation block, fp32 epilogue on
  * the CUDA cores). Same result contract as btf_gemv for BTF_STORE / BTF_ADD; it

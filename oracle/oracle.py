@@ -5,7 +5,10 @@ Two libraries, built by oracle/Makefile:
     reference path (always present once built; travels to GPU hosts);
   * ``_ref/libbtf_ref.so`` — the reference's own sources compiled in place,
     plus ref_shim.cpp (present where the reference tree was available at build
-    time; the built file also travels).
+    time; the built file also travels);
+  * ``_ref/libbtf_ref_gpu.so`` — the reference's own CUDA kernels
+    (src/cuda/kernels.cu) for sm_100a with ref_gpu_shim.cu: its GPU GEMV, timed
+    by bench.py as the GPU baseline.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline /
 ``--impl reference`` legs may import this module, and only as the checker or
@@ -23,6 +26,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libbtf_ref.so")
+REF_GPU_SO = os.path.join(HERE, "_ref", "libbtf_ref_gpu.so")
 
 _vp, _i32, _i64, _u16, _u32, _f32 = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_uint16,
                                      ctypes.c_uint32, ctypes.c_float)
@@ -293,6 +297,54 @@ class Reference:
         self.L.ref_matvec_raw(None, _p(np.ascontiguousarray(src)), N, K, _p(np.ascontiguousarray(x, np.float32)),
                               _p(y))
         return y
+
+
+class ReferenceGPU:
+    """libbtf_ref_gpu.so: the reference's own CUDA launchers (src/cuda/kernels.cuh:17-56)
+    over device pointers (ints) and a stream handle (int or None)."""
+
+    def __init__(self, path: str = REF_GPU_SO):
+        L = ctypes.CDLL(path)
+        vpp, ip = ctypes.POINTER(_vp), ctypes.POINTER(_i32)
+        sig = {
+            "ref_gpu_last_error": (ctypes.c_char_p, []),
+            "ref_gpu_init": (_i32, [_i32]),
+            "ref_gpu_max_nb": (_i32, [_i32]),
+            "ref_gpu_repack": (_i32, [_vp, ctypes.c_longlong, _vp, _vp, _vp]),
+            "ref_gpu_quant": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
+            "ref_gpu_gemv": (_i32, [vpp, vpp, ip, vpp, ip, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _vp]),
+        }
+        for n, (r, a) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = r, a
+        self.L = L
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_GPU_SO)
+
+    def _check(self, rc: int, what: str) -> None:
+        if rc != 0:
+            raise RuntimeError(f"{what}: {self.L.ref_gpu_last_error().decode()}")
+
+    def init(self, device: int) -> None:
+        self._check(self.L.ref_gpu_init(device), "kernels_init")
+
+    def repack(self, src: int, nblocks: int, codes: int, scales: int, stream=None) -> None:
+        self._check(self.L.ref_gpu_repack(src, nblocks, codes, scales, stream), "launch_repack")
+
+    def quant(self, x: int, ldx: int, M: int, n: int, q: int, d: int, s: int, stream=None) -> None:
+        self._check(self.L.ref_gpu_quant(x, ldx, M, n, q, d, s, stream), "launch_prep")
+
+    def gemv(self, segs, K: int, M: int, q: int, d: int, s: int, mode: int, stream=None) -> None:
+        """segs: [(codes, scales, N, y, ldy)] device pointers."""
+        n = len(segs)
+        codes = (_vp * 3)(*[sg[0] for sg in segs])
+        scales = (_vp * 3)(*[sg[1] for sg in segs])
+        Ns = (_i32 * 3)(*[sg[2] for sg in segs])
+        ys = (_vp * 3)(*[sg[3] for sg in segs])
+        lds = (_i32 * 3)(*[sg[4] for sg in segs])
+        self._check(self.L.ref_gpu_gemv(codes, scales, Ns, ys, lds, n, K, M, q, d, s, mode, stream), "launch_gemv")
 
 
 def panel_decode(panels: np.ndarray, N: int, K: int):
