@@ -312,10 +312,15 @@ def gpu_arm(args):
     if world > 1:
         # tagged (value, tag) outputs: no counters or waits in the GEMV; one bounded
         # tag check per layer (btf_gather_wait) over the layer's six outputs
-        # Per-layer output buffers (nothing is stored twice within a step) and one
-        # cross-rank barrier per step (no rank stores into the next step's
-        # buffers before every rank has checked this step's).
-        arena = shard.GatherArena(btf, N_LAYERS * sum(8 * sh[n][1] + 256 for n in outs), world, rank, dev)
+        # Per-layer output buffers, each stored exactly once per step, so the tag
+        # only has to name the step (epoch; site 0 for every launch). The buffers
+        # are 8*N bytes, multiples of 256, hence contiguous: one bounded tag check
+        # over the whole range at the end of the step proves that every rank's
+        # rows of every output have arrived (the inputs of this workload do not
+        # depend on earlier outputs, so no launch waits for them sooner), and one
+        # cross-rank barrier per step keeps every rank from storing into the next
+        # step's buffers before all have checked this step's.
+        arena = shard.GatherArena(btf, N_LAYERS * sum(8 * sh[n][1] for n in outs), world, rank, dev)
         offs = [{} for _ in range(N_LAYERS)]
         lay_out = [{} for _ in range(N_LAYERS)]
         for li in range(N_LAYERS):
@@ -323,11 +328,11 @@ def gpu_arm(args):
                 offs[li][n], lay_out[li][n] = arena.buffer((1, sh[n][1]), tagged=True)
         full_out = lay_out[N_LAYERS - 1]
         kind_names = (("qkv", ("q", "k", "v")), ("o", ("o",)), ("gateup", ("gate",)), ("down", ("down",)))
-        gdesc = [{kind: arena.gather_desc([offs[li][n] + 8 * model.rows[n].r0 for n in names], tagged=True,
-                                          site=4 * li + ki)
-                  for ki, (kind, names) in enumerate(kind_names)} for li in range(N_LAYERS)]
-        gwait = [[(arena.word_ptr(offs[li][n]), sh[n][1], 4 * li + ki) for ki, (kind, names) in enumerate(kind_names)
-                  for n in names] for li in range(N_LAYERS)]
+        gdesc = [{kind: arena.gather_desc([offs[li][n] + 8 * model.rows[n].r0 for n in names], tagged=True, site=0)
+                  for kind, names in kind_names} for li in range(N_LAYERS)]
+        total_words = N_LAYERS * sum(sh[n][1] for n in outs)
+        assert offs[N_LAYERS - 1]["down"] + 8 * sh["down"][1] == 8 * total_words, "output buffers not contiguous"
+        gwait_all = [(arena.word_ptr(0), total_words, 0)]
         gbar = arena.gather_desc([])
     else:
         full_out = {n: torch.zeros((1, sh[n][1]), device=dev) for n in outs}
@@ -373,15 +378,14 @@ def gpu_arm(args):
         gemv([seg("o")], 6144, "o", btf.ADD, "o")
         gemv([seg("gate"), (L["up"], None, 0)], 5120, "ffn", btf.SWIGLU, "gateup")
         gemv([seg("down")], 17408, "down", btf.ADD, "down")
-        if world > 1:  # every rank's rows of this layer's outputs have arrived
-            btf.gather_wait(gwait[li], arena.epoch_ptr, stream)
 
     def step(fused=False, stamped=False):
         if world > 1:
             btf.gather_epoch_advance(arena.epoch_ptr, stream)
         for i, L in enumerate(model.layers):
             layer(L, i, stamped=stamped, fused=fused)
-        if world > 1:
+        if world > 1:  # every rank's rows of every output of the step have arrived
+            btf.gather_wait(gwait_all, arena.epoch_ptr, stream)
             btf.gather_barrier(gbar, stream)
 
     # e2e variant: inputs from pinned host memory in, outputs back, every step
@@ -511,9 +515,13 @@ def gpu_arm(args):
                          "CTA's global timer) minus the previous launch's, mean over layers 1..63 of the last "
                          "timed replay; no events between launches")
 
-    dec3 = None
-    if world > 1:  # collective: the tensor-parallel decode step on every rank
+    dec3 = lmh = None
+    if world > 1:  # collective: the tensor-parallel decode step and the sharded lm_head on every rank
         dec3 = decode_config3(btf, torch, dev, world=world, rank=rank)
+        try:
+            lmh = lm_head_sharded(btf, torch, dev, world, rank)
+        except Exception as ex:
+            lmh = {"unavailable": f"{type(ex).__name__}: {ex}"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -525,8 +533,9 @@ def gpu_arm(args):
                        "layers": N_LAYERS, "bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2: 5.8 GB of distinct resident weights per step",
                        "parallelism": f"N-shard x{world}" + (", all-gather fused into the GEMV epilogue (NVLink "
-                                                             "64-bit (value, tag) stores; one tag check per "
-                                                             "layer; no NCCL in the step)" if world > 1 else ""),
+                                                             "64-bit (value, tag) stores; one tag check of all "
+                                                             "outputs per step; no NCCL in the step)"
+                                                             if world > 1 else ""),
                        "graph": "one CUDA graph per step, programmatic dependent launch between kernels",
                        "path": "drop-in pairs: btf_quant_q8 (launch_prep) + btf_gemv (launch_gemv), PDL-chained"},
             "roofline": {"bound": "hbm", "achieved": dom_ach, "peak": peak, "unit": "GB/s",
@@ -543,9 +552,9 @@ def gpu_arm(args):
             if world == 1 else None,
             "device_error_word": dev_err,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            # per step: 4 x (quantiser + GEMV) per layer; with N > 1 also one tag check per
-            # layer, the epoch advance and the cross-rank barrier
-            "gpu_launches": args.steps * (N_LAYERS * 8 + (N_LAYERS + 2 if world > 1 else 0)),
+            # per step: 4 x (quantiser + GEMV) per layer; with N > 1 also the epoch
+            # advance, one tag check of the step's outputs and the cross-rank barrier
+            "gpu_launches": args.steps * (N_LAYERS * 8 + (3 if world > 1 else 0)),
             "clocks": clocks.report(),
         }
         if world == 1:
@@ -564,6 +573,7 @@ def gpu_arm(args):
                 line["lm_head_config4"] = {"unavailable": f"{type(ex).__name__}: {ex}"}
         else:
             line["decode_config3"] = dec3
+            line["lm_head_config4"] = lmh
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_line(host_threads())
             try:
@@ -659,6 +669,84 @@ def reference_gpu_baseline(torch, dev, step_bytes, steps, warmup):
            "gpu_launches": steps * N_LAYERS * 8}
     del g, layers, layer0
     torch.cuda.empty_cache()
+    return out
+
+
+def lm_head_sharded(btf, torch, dev, world, rank, reps=10, replays=3):
+    """Benchmark configuration 4's lm_head N-sharded over `world` GPUs (collective):
+    K=5120 -> N=248320, rank r holding its rows (shard.shard_rows, whole 8-row
+    groups; 338/world MB of panels), at batch 1 and 16, with the all-gather fused
+    into the GEMV epilogue (btf_gemv_gather, tagged 64-bit stores into every rank's
+    full-width output over NVLink). One run: epoch advance, `reps` launches (each
+    into its own output buffer), one bounded tag check of all the run's outputs,
+    one cross-rank barrier; captured as a CUDA graph, CUDA events, max over ranks.
+    GB/s = algorithmic bytes of the whole lm_head per launch (weights once, the Q8
+    activation, the fp32 output) / time per launch: the aggregate over the ranks.
+    The weights are the same 16-fold seeded block as lm_head_config4."""
+    import torch.distributed as dist
+
+    import shard
+
+    _, K, N = synth.LM_HEAD
+    r = shard.shard_rows(N, world, rank)
+    full = torch.from_numpy(synth.ternary_ptq(N // 16, K, seed=7)).to(dev).repeat(16, 1)
+    src = full[r.r0:r.r0 + r.n].contiguous()
+    del full
+    pm = btf.repack_panels(src, r.n, K)
+    torch.cuda.synchronize()
+    del src
+    peak, peak_src = measured_peaks()
+    st = torch.cuda.Stream(device=dev)
+    out = {"shape": f"K{K}_N{N}", "n_gpus": world, "rows_per_gpu": r.per,
+           "panel_bytes_per_gpu": btf.panel_bytes(r.n, K), "peak_per_gpu": peak, "peak_source": peak_src,
+           "launches_per_run": reps}
+    for M in (1, 16):
+        arena = shard.GatherArena(btf, reps * M * N * 8, world, rank, dev)
+        bufs = [arena.buffer((M, N), tagged=True) for _ in range(reps)]
+        descs = [arena.gather_desc([off + 8 * r.r0], tagged=True, site=0) for off, _ in bufs]
+        gwait_all = [(arena.word_ptr(bufs[0][0]), reps * M * N, 0)]
+        gbar = arena.gather_desc([])
+        act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=8)).to(dev))
+        torch.cuda.synchronize()
+
+        def run():
+            btf.gather_epoch_advance(arena.epoch_ptr, st)
+            for k in range(reps):
+                btf.launch_gemv_gather([(pm, bufs[k][1][:, r.r0:], N)], K, M, act, btf.STORE, descs[k], st)
+            btf.gather_wait(gwait_all, arena.epoch_ptr, st)
+            btf.gather_barrier(gbar, st)
+
+        with torch.cuda.stream(st):
+            run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            run()
+        g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        with torch.cuda.stream(st):
+            for _ in range(replays):
+                g.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item()) * 1e3 / (replays * reps)
+        nbytes = btf.panel_bytes(N, K) + M * (K + K // 32 * 8) + M * N * 4
+        err = btf.device_error()
+        out[f"M{M}"] = {"us": us, "GB/s": nbytes / (us * 1e-6) / 1e9,
+                        "GB/s_per_gpu": nbytes / world / (us * 1e-6) / 1e9,
+                        "frac_of_hbm_per_gpu": nbytes / world / (us * 1e-6) / 1e9 / peak,
+                        "bytes_per_launch": nbytes, "weight_passes": -(-M // btf.gemv_max_nb(K)),
+                        "device_error_word": err}
+        del g
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still stores into another's arena
+        arena.close()
+        dist.barrier()
     return out
 
 

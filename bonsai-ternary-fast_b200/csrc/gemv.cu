@@ -858,8 +858,8 @@ int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act 
   for (int s = 0; s < nout; ++s)
     if (g->peer_y[s][g->rank] != segs[s].y)
       return fail(BTF_ERR_ARG, "btf_gemv_gather: peer_y[%d][rank] must be segs[%d].y", s, s);
-  if (M > kMaxNb)
-    return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_gather: M <= %d (one pass; one arrival per launch)", kMaxNb);
+  if (!g->tagged && M > kMaxNb)  // counted completion: one arrival per launch, so one pass
+    return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_gather: counted completion needs M <= %d (one pass)", kMaxNb);
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream, g);
 }
 

@@ -278,6 +278,9 @@ typedef struct btf_gather {
   int site;
   const unsigned int* epoch; /* this rank's epoch counter (device) */
 } btf_gather;
+/* Counted completion serves M <= btf_gemv_max_nb(K) (one pass, one arrival per
+ * launch); the tagged form serves any M (every pass stores its rows' words with
+ * the launch's tag). */
 int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, const btf_gather* g,
                     void* stream);
 
