@@ -566,7 +566,8 @@ int gemm_setup(DeviceInfo& d) {
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemm_kernel)");
 }
 
-// One matrix: y[M][ldy] (=|+=) W q. Called by btf_gemm / btf_gemv (M >= 64).
+// One matrix: y[M][ldy] (=|+=) W q. Called by btf_gemm, which btf_gemv calls
+// for M >= 64 in store / add mode.
 int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st) {
   const DeviceInfo* dev = current_device();
   if (!dev) return BTF_ERR_STATE;

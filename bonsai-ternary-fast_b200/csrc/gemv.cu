@@ -61,6 +61,7 @@ constexpr int kWarps = BTF_GEMV_WARPS;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSeg = 3;
 constexpr int kMaxNb = 4;                                  // activation rows per pass
+constexpr int kGemmMinM = 64;                              // btf_gemv hands M >= this to btf_gemm
 constexpr uint64_t kWaitLimitNs = 1000000000ull;           // 1 s per bounded wait
 constexpr uint64_t kGatherWaitNs = 2000000000ull;          // 2 s for the other ranks' arrivals
 
@@ -832,6 +833,11 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
   if (int rc = check_segs("btf_gemv", segs, nseg, K, mode)) return rc;
   if (!act.q || !act.d || !act.s || !aligned(act.q, 16) || !aligned(act.d, 4) || !aligned(act.s, 4))
     return fail(BTF_ERR_ARG, "btf_gemv: activation pointers null or misaligned (q needs 16 B)");
+  // A prefill batch is a dense contraction: M >= 64 rows go to the tcgen05 GEMM
+  // (store / add; its tensor maps need d 16-byte aligned) instead of the
+  // reference's repeated small-batch passes over the weights (kernels.cu:805-821).
+  if (M >= kGemmMinM && mode != BTF_SWIGLU && aligned(act.d, 16))
+    return btf_gemm(segs, nseg, K, M, act, mode, stream);
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream);
 }
 

@@ -137,7 +137,9 @@ int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float ep
 /* ---- ternary GEMV (batch M, CUDA cores: dp4a on the 2-bit codes)
  * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
- * segments (gate, up) with the same N. K % 128 == 0. */
+ * segments (gate, up) with the same N. K % 128 == 0. M >= 64 in store / add mode
+ * (with d 16-byte aligned) runs as btf_gemm on the tensor cores; smaller M and
+ * swiglu run in passes of btf_gemv_max_nb(K) rows. */
 int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
 /* Fused form: the activation is given as fp32 x [M][ldx] and quantised to Q8_0

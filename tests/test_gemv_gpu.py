@@ -221,3 +221,30 @@ def test_lm_head_shape_row_subsets(cuda, btf, orc, M):
     q, d, s = orc.q8_rows(x)
     want = orc.gemv(codes, scales, K, q, d, s, threads=8)
     assert rel_rms(y.cpu().numpy()[:, rows], want) <= TOL
+
+
+@pytest.mark.parametrize("M,mode", [(64, 0), (96, 1)])
+def test_gemv_prefill_batch_runs_on_the_gemm(cuda, btf, orc, M, mode):
+    # launch_gemv with a prefill batch (M >= 64, store / add) is the tcgen05 GEMM:
+    # bit for bit btf_gemm's output, and within the GEMV bar of the oracle
+    import torch
+
+    K = 2048
+    rng = np.random.default_rng(M + mode)
+    q, d, s = _random_act(M, K, rng)
+    act = _act_dev(btf, q, d, s, cuda)
+    mats = [Mat(btf, orc, n, K, seed=500 + n, device=cuda) for n in (72, 40)]
+    y0 = [rng.standard_normal((M, m.N)).astype(np.float32) for m in mats]
+    yv = [_dev(y, cuda) for y in y0]
+    yg = [_dev(y, cuda) for y in y0]
+    btf.launch_gemv([(m.pm, y, m.N) for m, y in zip(mats, yv)], K, M, act, mode)
+    btf.launch_gemm([(m.pm, y, m.N) for m, y in zip(mats, yg)], K, M, act, mode)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    for m, a, b, y_init in zip(mats, yv, yg, y0):
+        a, b = a.cpu().numpy(), b.cpu().numpy()
+        assert np.array_equal(a, b)
+        add = mode == btf.ADD
+        y_orc = orc.gemv(m.codes, m.scales, K, q, d, s, y=y_init.copy() if add else None, add=add)
+        y64 = orc.gemv_f64(m.codes, m.scales, K, q, d) + (y_init if add else 0)
+        _check(a, y_orc, y64, _abs_terms(orc, m, q, d, s) + (np.abs(y_init) if add else 0), f"M={M}")
