@@ -40,6 +40,7 @@ EXPORTS = (
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
     "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
     "btf_gemm_f32_noalloc", "btf_chain_program_bytes", "btf_chain_encode", "btf_chain_run", "btf_stamp_next",
+    "btf_gemm_idot",
 )
 
 
@@ -167,6 +168,7 @@ def lib() -> ctypes.CDLL:
         "btf_gemv_f32": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
         "btf_device_error": (i32, [i32]),
         "btf_gemv_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
+        "btf_gemm_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
         "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
         "btf_gemm_f32_noalloc": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
         "btf_chain_program_bytes": (i64, [i32]),
@@ -456,6 +458,14 @@ def gemv_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):
     torch = _torch()
     out = torch.empty((M, pm.N, pm.K // 32), dtype=torch.int32, device=pm.panels.device)
     check(lib().btf_gemv_idot(_ptr(pm.panels), pm.N, pm.K, M, act.c(), _ptr(out), _stream(stream)), "btf_gemv_idot")
+    return out
+
+
+def gemm_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):
+    """Exact int32 accumulators idot[M][N][K/32] from the tcgen05 GEMM's tensor memory."""
+    torch = _torch()
+    out = torch.empty((M, pm.N, pm.K // 32), dtype=torch.int32, device=pm.panels.device)
+    check(lib().btf_gemm_idot(_ptr(pm.panels), pm.N, pm.K, M, act.c(), _ptr(out), _stream(stream)), "btf_gemm_idot")
     return out
 
 

@@ -117,6 +117,7 @@ struct GemmParams {
   int ldy;
   int mode;            // BTF_STORE / BTF_ADD
   int* err;
+  int32_t* idot;       // DUMP kernel: [M][N][K/32] integer accumulators (no y is stored)
 };
 
 // ---- tcgen05 / descriptor helpers (PTX ISA, sm_100a)
@@ -218,6 +219,9 @@ __device__ __forceinline__ uint32_t codes_to_trits(uint32_t c) {
 // Tensor maps: tmA the int8 activation [M][K]; tmC the panel codes as a 5-D
 // tensor {512 B of a quad half, half v, quad h, slice, group}; tmR the panel
 // scales {16 B of a block, slice, group}; tmD the activation scales [M][K/32].
+// DUMP (parity/debug): the same kernel writes every 32-column region's integer
+// accumulator P - kBias (= idot) to p.idot instead of storing y.
+template <bool DUMP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmC,
                 const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
@@ -482,6 +486,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+          if constexpr (DUMP) {
+            if (m0 + m < p.M) {
+              const int nsub = p.K >> 5, nb = n0 + cg * kEpiCols;
+              int32_t* out = p.idot + ((int64_t)(m0 + m) * p.N + nb) * nsub + c * kStepsPerChunk + ks;
+#pragma unroll
+              for (int i = 0; i < kEpiCols; ++i)
+                if (nb + i < p.N) out[(int64_t)i * nsub] = (int)buf[ks & 1][i] - kBias;
+            }
+          }
           step_math(buf[ks & 1], dk[ks], ks == 0);
         }
         // weight scales of the chunk's 128-column block; then the stage is free
@@ -512,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // every epilogue warp reaches this barrier once (its chunk loop always ends)
     asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-    if (!*abort_flag) {
+    if (!DUMP && !*abort_flag) {
       const int we = warp - kEpiWarp0;
 #pragma unroll 1
       for (int rr = 0; rr < kTileM / kEpiWarps; ++rr) {
@@ -562,13 +575,16 @@ EncodeFn encode_fn() {
 
 int gemm_setup(DeviceInfo& d) {
   if (d.optin_smem < kSmemBytes) return fail(BTF_ERR_UNSUPPORTED, "btf_gemm needs %d B of shared memory", kSmemBytes);
-  const cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemm_kernel)");
 }
 
 // One matrix: y[M][ldy] (=|+=) W q. Called by btf_gemm, which btf_gemv calls
 // for M >= 64 in store / add mode.
-int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st) {
+int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
+             int32_t* idot = nullptr) {
   const DeviceInfo* dev = current_device();
   if (!dev) return BTF_ERR_STATE;
   const EncodeFn enc = encode_fn();
@@ -627,12 +643,16 @@ int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mo
   p.ldy = seg.ldy;
   p.mode = mode;
   p.err = dev->err_word;
+  p.idot = idot;
 #if BTF_GEMM_RASTER_M
   const dim3 grid((M + kTileM - 1) / kTileM, (seg.N + kTileN - 1) / kTileN);
 #else
   const dim3 grid((seg.N + kTileN - 1) / kTileN, (M + kTileM - 1) / kTileM);
 #endif
-  const cudaError_t e = launch_pdl(gemm_kernel, grid, dim3(kThreads), (size_t)kSmemBytes, st, mA, mC, mR, mD, p);
+  const cudaError_t e = idot ? launch_pdl(gemm_kernel<true>, grid, dim3(kThreads), (size_t)kSmemBytes, st, mA, mC,
+                                          mR, mD, p)
+                             : launch_pdl(gemm_kernel<false>, grid, dim3(kThreads), (size_t)kSmemBytes, st, mA, mC,
+                                          mR, mD, p);
   return e == cudaSuccess ? launch_status("gemm_kernel") : cuda_fail(e, "gemm_kernel launch");
 }
 
@@ -655,4 +675,13 @@ extern "C" int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8
   for (int i = 0; i < nseg; ++i)
     if (int rc = run_gemm(segs[i], K, M, act, mode, (cudaStream_t)stream)) return rc;
   return BTF_OK;
+}
+
+extern "C" int btf_gemm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (!panels || (reinterpret_cast<uintptr_t>(panels) & 15) || N <= 0 || K <= 0 || K % 128 || !idot || !act.q ||
+      !act.d || (reinterpret_cast<uintptr_t>(act.q) & 15) || (reinterpret_cast<uintptr_t>(act.d) & 15))
+    return fail(BTF_ERR_ARG, "btf_gemm_idot: bad arguments (K % 128, q and d 16-byte aligned)");
+  const btf_gemv_seg seg{panels, N, nullptr, N};
+  return run_gemm(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot);
 }

@@ -114,6 +114,7 @@ struct GemvParams {
   int* err;
   btf_gather gather;   // world == 0: plain launch; else the epilogue all-gathers over NVLink
   unsigned long long* stamp;  // end stamp slot (btf_stamp_next) or null
+  int32_t* idot;              // DUMP kernels: [M][n0][K/32] integer dots of segment 0 (no y is stored)
 };
 
 using namespace core;
@@ -166,7 +167,10 @@ __device__ __noinline__ void gather_arrive(const btf_gather& g, int* err) {
 
 // GATHER: 0 = plain launch; 1 = N-sharded, counted completion; 2 = N-sharded,
 // tagged (value, tag) words. Compile-time, so plain launches carry none of it.
-template <int NB, int MODE, bool FUSE, int GATHER>
+// DUMP (parity/debug, store mode, one segment): the same kernel writes, for
+// every (m, row, sub-block), the fp32 operand its epilogue multiplies
+// ((float)idot from the biased integer) as int32 to p.idot, instead of y.
+template <int NB, int MODE, bool FUSE, int GATHER, bool DUMP = false>
 __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __grid_constant__ GemvParams p) {
   constexpr bool kSwi = MODE == BTF_SWIGLU;
   constexpr bool kCluster = FUSE && kFuseCluster > 1;
@@ -216,7 +220,9 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
   // (single-copy atomic), so a reader that sees the tag also sees the value.
   unsigned tag = 0;  // set after griddepcontrol.wait (the epoch is advanced in stream order)
   auto put = [&](int seg, float* y, int64_t idx, float val) {
-    if constexpr (GATHER == 0) {
+    if constexpr (DUMP) {
+      return;
+    } else if constexpr (GATHER == 0) {
       y[idx] = val;
     } else if constexpr (GATHER == 2) {
       const unsigned long long w = (unsigned long long)__float_as_uint(val) | ((unsigned long long)tag << 32);
@@ -460,6 +466,19 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
           const float2 f23 = __fadd2_rn(make_float2(__int_as_float(biased_idot<2>(c[2], ms)),
                                                     __int_as_float(biased_idot<3>(c[3], ms))), nmagic);
           const int r = 4 * h;
+          if constexpr (DUMP) {
+            int seg_d, g_d;
+            locate(first + ui * stride, seg_d, g_d);
+            const int sb = j * kSubPerSlice + lane;
+            if (m < p.nb && sb < p.nsub) {
+              const float fv[4] = {f01.x, f01.y, f23.x, f23.y};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int row = g_d * kRows + r + k;
+                if (row < p.n0) p.idot[((int64_t)(p.m0 + m) * p.n0 + row) * p.nsub + sb] = __float2int_rz(fv[k]);
+              }
+            }
+          }
           const float2 s01 = __fmul2_rn(make_float2(sc[pp][r], sc[pp][r + 1]), d2);
           const float2 s23 = __fmul2_rn(make_float2(sc[pp][r + 2], sc[pp][r + 3]), d2);
           acc[pp][h][0][m] = __ffma2_rn(s01, f01, acc[pp][h][0][m]);
@@ -603,30 +622,6 @@ __global__ void __launch_bounds__(1024) gather_wait_kernel(const __grid_constant
   }
 }
 
-// Exact idot dump (parity/debug): one thread per (m, row, sub-block), same
-// quad decode as the GEMV.
-__global__ void __launch_bounds__(256)
-    idot_kernel(const uint8_t* __restrict__ pan, int N, int K, int M, const int8_t* __restrict__ q,
-                const int32_t* __restrict__ s, int32_t* __restrict__ idot) {
-  const int nsub = K / 32;
-  const int64_t S = slices_of(K);
-  const int64_t total = (int64_t)M * N * nsub;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int sbk = (int)(i % nsub);
-    const int64_t mr = i / nsub;
-    const int r = (int)(mr % N), m = (int)(mr / N);
-    const int rg = r % kRows, h = rg / 4, kk = rg % 4, l = sbk % kSubPerSlice;
-    const uint8_t* pp = pan + panel_offset(r / kRows, sbk / kSubPerSlice, S) + h * 1024 + l * 16;
-    const uint4 cw0 = *reinterpret_cast<const uint4*>(pp), cw1 = *reinterpret_cast<const uint4*>(pp + 512);
-    const int8_t* qp = q + (int64_t)m * K + (int64_t)sbk * 32;
-    const uint4 qa = *reinterpret_cast<const uint4*>(qp), qb = *reinterpret_cast<const uint4*>(qp + 16);
-    int c[4] = {0, 0, 0, 0};
-    quad_dots(cw0, cw1, qa, qb, c);
-    const int cd = kk == 0 ? c[0] : kk == 1 ? (c[1] >> 2) : kk == 2 ? (c[2] >> 4) : (c[3] >> 6);
-    idot[i] = cd - s[(int64_t)m * nsub + sbk];
-  }
-}
-
 using KernelFn = void (*)(const GemvParams);
 
 template <int MODE, bool FUSE, int GATHER>
@@ -642,6 +637,14 @@ KernelFn pick_mode(int NB, int mode) {
   return mode == BTF_STORE ? pick<BTF_STORE, FUSE, GATHER>(NB)
          : mode == BTF_ADD ? pick<BTF_ADD, FUSE, GATHER>(NB)
                            : pick<BTF_SWIGLU, FUSE, GATHER>(NB);
+}
+// the integer-dump form of the store kernel (btf_gemv_idot)
+KernelFn pick_dump(int NB) {
+  switch (NB) {
+    case 1: return gemv_kernel<1, BTF_STORE, false, 0, true>;
+    case 2: return gemv_kernel<2, BTF_STORE, false, 0, true>;
+    default: return gemv_kernel<4, BTF_STORE, false, 0, true>;
+  }
 }
 // fused-quantise launches are never N-sharded
 KernelFn pick(int NB, int mode, bool fuse, int gather) {
@@ -718,7 +721,7 @@ int resident_cluster_ctas(KernelFn fn, int smem, int cluster, cudaStream_t st) {
 
 // Launches the GEMV over M rows in passes of at most kMaxNb activation rows.
 int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* act, const float* x, int ldx,
-             int mode, cudaStream_t st, const btf_gather* gather = nullptr) {
+             int mode, cudaStream_t st, const btf_gather* gather = nullptr, int32_t* idot = nullptr) {
   const DeviceInfo* dev = current_device();
   if (!dev) return BTF_ERR_STATE;
   GemvParams p{};
@@ -753,6 +756,7 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
   p.err = dev->err_word;
   if (gather) p.gather = *gather;
   p.stamp = take_stamp();  // every pass raises it: the slot ends as the last pass's end
+  p.idot = idot;
   for (int m0 = 0; m0 < M; m0 += kMaxNb) {
     const int nb = std::min(kMaxNb, M - m0);
     const int NB = nb <= 1 ? 1 : nb <= 2 ? 2 : 4;
@@ -767,7 +771,7 @@ int run_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, const btf_q8act* 
     p.slots = slots;
     p.m0 = m0;
     p.nb = nb;
-    const KernelFn fn = pick(NB, mode, x != nullptr, !gather ? 0 : gather->tagged ? 2 : 1);
+    const KernelFn fn = idot ? pick_dump(NB) : pick(NB, mode, x != nullptr, !gather ? 0 : gather->tagged ? 2 : 1);
     const int cluster = x != nullptr ? kFuseCluster : 1;
     const int resident = cluster > 1 ? resident_cluster_ctas(fn, plan.total, cluster, st)
                                      : dev->sm_count * resident_ctas(fn, plan.total);
@@ -817,6 +821,9 @@ int gemv_setup(DeviceInfo& d) {
   if ((e = set_attrs_all<false, 0>(dyn)) || (e = set_attrs_all<false, 1>(dyn)) || (e = set_attrs_all<false, 2>(dyn)) ||
       (e = set_attrs_all<true, 0>(dyn)))
     return cuda_fail(e, "cudaFuncSetAttribute(gemv_kernel)");
+  for (int nb : {1, 2, 4})
+    if ((e = cudaFuncSetAttribute(pick_dump(nb), cudaFuncAttributeMaxDynamicSharedMemorySize, dyn)))
+      return cuda_fail(e, "cudaFuncSetAttribute(gemv_kernel, dump)");
   return BTF_OK;
 }
 
@@ -929,15 +936,11 @@ int btf_device_error(int clear) {
 
 int btf_gemv_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream) {
   if (M <= 0) return BTF_OK;
-  if (!panels || !idot || !act.q || !act.s || N <= 0 || K <= 0 || K % 128 || !aligned(act.q, 16) ||
-      !aligned(panels, 16))
+  if (!panels || !idot || !act.q || !act.d || !act.s || N <= 0 || K <= 0 || K % 128 || !aligned(act.q, 16) ||
+      !aligned(panels, 16) || !aligned(act.d, 4) || !aligned(act.s, 4))
     return fail(BTF_ERR_ARG, "btf_gemv_idot: bad arguments");
-  const DeviceInfo* dev = current_device();
-  if (!dev) return BTF_ERR_STATE;
-  const int64_t total = (int64_t)M * N * (K / 32);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)dev->sm_count * 32));
-  idot_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint8_t*>(panels), N, K, M, act.q, act.s, idot);
-  return launch_status("idot_kernel");
+  btf_gemv_seg seg{panels, N, nullptr, N};
+  return run_gemv(&seg, 1, K, M, &act, nullptr, 0, BTF_STORE, (cudaStream_t)stream, nullptr, idot);
 }
 
 }  // extern "C"

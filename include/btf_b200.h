@@ -243,9 +243,15 @@ int btf_chain_encode(const btf_chain_op* ops, int n_ops, int M, void* program, b
 int btf_chain_run(const btf_chain* chain, void* stream);
 
 /* Debug/parity entry point: the exact int32 trit dot of every (m, row,
- * sub-block), idot[M][N][K/32] = code_dot - sum(q) — the integers the GEMV
- * scales (src/emu_decoder.cpp:154-157). Same decode path as btf_gemv. */
+ * sub-block), idot[M][N][K/32] = code_dot - sum(q) -- the integers the GEMV
+ * scales (src/emu_decoder.cpp:154-157). It runs the shipped GEMV kernel itself in
+ * its dump form: each value is the fp32 operand that kernel's epilogue multiplies
+ * (the biased integer of its dp4a dots converted exactly), written as int32. */
 int btf_gemv_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
+/* The same dump from the tcgen05 GEMM (btf_gemm): each 32-column step's integer
+ * accumulator read from tensor memory (P - 4096 of its biased region), the
+ * integers the GEMM's epilogue scales; idot[M][N][K/32]. q and d 16-byte aligned. */
+int btf_gemm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
 
 /* ---- N-sharded GEMV with the all-gather fused into the epilogue
  * The reference is single-GPU (src/cuda/gpu_decoder.cu); this is the B200

@@ -142,3 +142,19 @@ def test_gemm_extreme_activation_scales(cuda, btf, orc):
     for r in range(M):
         if r != 7:
             assert rel_rms(got[r], want[r]) <= TOL, (r, rel_rms(got[r], want[r]))
+
+
+@pytest.mark.parametrize("M,K,N,rows", [(64, 5120, 17408, 2048), (64, 17408, 5120, 640), (77, 1152, 200, 200)])
+def test_gemm_integer_accumulators_bit_exact(cuda, btf, orc, M, K, N, rows):
+    # the GEMM kernel itself (its dump form, btf_gemm_idot) writes each 32-column
+    # region's int32 accumulator from tensor memory; every one must equal the
+    # oracle's idot (the integer of src/emu_decoder.cpp:154-157). Configuration
+    # 2's shapes on their first `rows` weight rows (the oracle stays quick).
+    src = synth.ternary_ptq(N, K, seed=0)[:rows]
+    pm = btf.repack_panels(_dev(src, cuda), rows, K)
+    x = synth.activations(M, K, seed=2)
+    act = btf.quant_q8(_dev(x, cuda))
+    got = btf.gemm_idot(pm, M, act).cpu().numpy()
+    codes, _ = orc.repack_t2(src, rows, K)
+    q, d, s = orc.q8_rows(x)
+    assert np.array_equal(got, orc.idot(codes, K, q, s))

@@ -248,3 +248,19 @@ def test_gemv_prefill_batch_runs_on_the_gemm(cuda, btf, orc, M, mode):
         y_orc = orc.gemv(m.codes, m.scales, K, q, d, s, y=y_init.copy() if add else None, add=add)
         y64 = orc.gemv_f64(m.codes, m.scales, K, q, d) + (y_init if add else 0)
         _check(a, y_orc, y64, _abs_terms(orc, m, q, d, s) + (np.abs(y_init) if add else 0), f"M={M}")
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 5120, 17408), (4, 17408, 5120), (3, 1152, 44)])
+def test_gemv_kernel_integer_dots_bit_exact(cuda, btf, orc, M, K, N):
+    # btf_gemv_idot runs the shipped GEMV kernel in its dump form: every
+    # (m, row, sub-block) value is the fp32 operand its epilogue multiplies
+    # ((float) of the biased dp4a integer), written as int32. Configuration 0's
+    # full 5120 -> 17408 matrix, a 4-row pass at K = 17408 and a ragged case.
+    src = synth.ternary_ptq(N, K, seed=0)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    x = synth.activations(M, K, seed=2)
+    act = btf.quant_q8(_dev(x, cuda))
+    got = btf.gemv_idot(pm, M, act).cpu().numpy()
+    codes, _ = orc.repack_t2(src, N, K)
+    q, d, s = orc.q8_rows(x)
+    assert np.array_equal(got, orc.idot(codes, K, q, s))
