@@ -40,7 +40,7 @@ EXPORTS = (
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
     "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
     "btf_gemm_f32_noalloc", "btf_chain_program_bytes", "btf_chain_encode", "btf_chain_run", "btf_stamp_next",
-    "btf_gemm_idot",
+    "btf_gemm_idot", "btf_decoder_prefill",
 )
 
 
@@ -196,6 +196,7 @@ def lib() -> ctypes.CDLL:
                                         ctypes.POINTER(vp)]),
         "btf_decoder_step": (i32, [vp, ctypes.c_int32, vp, ctypes.POINTER(ctypes.c_int32)]),
         "btf_decoder_run": (i32, [vp, i32]),
+        "btf_decoder_prefill": (i32, [vp, vp, i32, i32, vp, ctypes.POINTER(ctypes.c_int32)]),
         "btf_decoder_reset": (i32, [vp]),
         "btf_decoder_close": (i32, [vp]),
         "btf_decoder_get_info": (i32, [vp, ctypes.POINTER(DecoderInfoC)]),
@@ -701,6 +702,18 @@ class Decoder:
         nxt = ctypes.c_int32()
         check(lib().btf_decoder_step(self.h, token, out.ctypes.data if logits else None, ctypes.byref(nxt)),
               "btf_decoder_step")
+        return nxt.value, out
+
+    def prefill(self, tokens, max_chunk: int = 0, logits: bool = False):
+        """The prompt in chunks of up to max_chunk (0: 8) tokens -> (greedy next token,
+        logits of the last prompt token or None) (btf_decoder_prefill)."""
+        import numpy as np
+
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.empty(self.info()["n_vocab"], dtype=np.float32) if logits else None
+        nxt = ctypes.c_int32()
+        check(lib().btf_decoder_prefill(self.h, toks.ctypes.data, len(toks), max_chunk,
+                                        out.ctypes.data if logits else None, ctypes.byref(nxt)), "btf_decoder_prefill")
         return nxt.value, out
 
     def run(self, steps: int) -> None:

@@ -88,6 +88,9 @@ struct Decoder {
   float* ad = nullptr;
   int32_t* as = nullptr;
   int32_t *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr;
+  // prompt chunks (btf_decoder_prefill): up to kMaxChunk tokens and their positions
+  static constexpr int kMaxChunk = 8;
+  int32_t *d_ptok = nullptr, *d_ppos = nullptr;
   int32_t* h_io = nullptr;  // pinned: [0] token in, [1] token out
   int pos = 0;
   cudaGraph_t graph = nullptr;
@@ -166,7 +169,10 @@ int make_buffers(Decoder& D) {
   const int wo = std::max(n_gdn ? D.DI : 0, n_attn ? H * HD : 0);
   D.Kmax = std::max({E, F, wo});
   // activation buffers in one arena (shared with the other ranks under tensor parallelism)
-  const int sizes[9] = {E, E, wa, wb, wc, wo, std::max(1, H * HD), F, d.n_vocab};
+  // the row buffers hold a prompt chunk of kMaxChunk rows (decode steps use row 0);
+  // bQ (one token's rotated q) and the logits (the last token's) hold one row
+  const int R = Decoder::kMaxChunk;
+  const int sizes[9] = {R * E, R * E, R * wa, R * wb, R * wc, R * wo, std::max(1, H * HD), R * F, d.n_vocab};
   size_t off[9], total = Decoder::kCtl;
   for (int i = 0; i < 9; ++i) {
     off[i] = total;
@@ -183,14 +189,16 @@ int make_buffers(Decoder& D) {
   D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
   D.amax_v = D.alloc<float>(Decoder::kArgmaxParts, &rc);
   D.amax_i = D.alloc<int>(Decoder::kArgmaxParts, &rc);
-  D.aq = D.alloc<int8_t>(D.Kmax, &rc);
-  D.ad = D.alloc<float>(D.Kmax / 32, &rc);
-  D.as = D.alloc<int32_t>(D.Kmax / 32, &rc);
-  D.d_tok = D.alloc<int32_t>(4, &rc);
+  D.aq = D.alloc<int8_t>((size_t)R * D.Kmax, &rc);
+  D.ad = D.alloc<float>((size_t)R * D.Kmax / 32, &rc);
+  D.as = D.alloc<int32_t>((size_t)R * D.Kmax / 32, &rc);
+  D.d_tok = D.alloc<int32_t>(4 + 2 * R, &rc);
   if (rc) return rc;
   if (!D.dry) {
     D.d_pos = D.d_tok + 1;
     D.d_next = D.d_tok + 2;
+    D.d_ptok = D.d_tok + 4;
+    D.d_ppos = D.d_tok + 4 + R;
   }
   for (Layer& l : D.L) {
     if (l.rec) {
@@ -230,14 +238,14 @@ struct Out {
   const Mat* m;
   float* y;
 };
-int gemv(Decoder& D, std::initializer_list<Out> outs, int K, int mode) {
+int gemv(Decoder& D, std::initializer_list<Out> outs, int K, int mode, int M = 1) {
   const btf_q8act act{D.aq, D.ad, D.as};
   btf_gemv_seg segs[3];
   int ns = 0;
   const bool tp = D.world > 1;
   for (const Out& o : outs)
     segs[ns++] = {o.m->pan, tp ? o.m->n : o.m->N, o.y ? o.y + (tp ? o.m->row0 : 0) : nullptr, o.y ? o.m->N : 0};
-  if (!tp) return btf_gemv(segs, ns, K, 1, act, mode, D.st);
+  if (!tp) return btf_gemv(segs, ns, K, M, act, mode, D.st);
   btf_gather g{};
   g.world = D.world;
   g.rank = D.rank;
@@ -248,11 +256,12 @@ int gemv(Decoder& D, std::initializer_list<Out> outs, int K, int mode) {
   for (int r = 0; r < D.world; ++r) g.flags[r] = reinterpret_cast<unsigned*>(D.peers[r]);
   g.expect = reinterpret_cast<unsigned*>(D.arena + 4);
   g.done = reinterpret_cast<unsigned*>(D.arena + 8);
-  return btf_gemv_gather(segs, ns, K, 1, act, mode, &g, D.st);
+  return btf_gemv_gather(segs, ns, K, M, act, mode, &g, D.st);
 }
-int prep(Decoder& D, const float* x, int n, const float* normw, const btf_hx& hx, float* xn) {
+// M rows of width n (row stride n) -> the Q8 activation (and xn rows when non-null)
+int prep(Decoder& D, const float* x, int n, const float* normw, const btf_hx& hx, float* xn, int M = 1) {
   const btf_q8act act{D.aq, D.ad, D.as};
-  return btf_prep(x, n, 1, n, normw, D.d.rms_eps, hx, xn, n, act, D.st);
+  return btf_prep(x, n, M, n, normw, D.d.rms_eps, hx, xn, n, act, D.st);
 }
 #define BTF_TRY(call)                   \
   do {                                  \
@@ -299,6 +308,60 @@ int enqueue_step(Decoder& D) {
   BTF_TRY(prep(D, D.x, E, D.out_norm, D.output.hx, nullptr));
   BTF_TRY(gemv(D, {{&D.output, D.logits}}, E, BTF_STORE));
   BTF_TRYC(launch_argmax(D.logits, d.n_vocab, D.amax_v, D.amax_i, Decoder::kArgmaxParts, D.d_next, D.d_tok, D.d_pos,
+                         D.st));
+  return BTF_OK;
+}
+
+// Enqueues one prompt chunk of M tokens (d_ptok[0..M), positions d_ppos[0..M)),
+// as the reference's forward_chunk (src/cuda/gpu_decoder.cu:401-450): every
+// prep and ternary matmul runs once over the M rows (the weights stream once per
+// chunk); the recurrent mixer and the attention run token by token in order, at
+// each token's own position, so the state and the KV cache advance exactly as in
+// M decode steps. The logits, the greedy token (into d_next and d_tok) come
+// from the chunk's last token.
+int enqueue_chunk(Decoder& D, int M) {
+  const btf_decoder_dims& d = D.d;
+  const int E = d.n_embd, F = d.n_ff, H = d.n_head, HK = d.n_head_kv, HD = d.head_dim;
+  for (int m = 0; m < M; ++m)
+    BTF_TRYC(launch_embed(D.embd.pan, d.n_vocab, E, D.d_ptok + m, D.inv_block, D.inv_signs, D.x + (size_t)m * E,
+                          D.st));
+  for (Layer& l : D.L) {
+    if (l.rec) {
+      const int C = l.qkv.N, Z = l.zg.N;
+      BTF_TRY(prep(D, D.x, E, l.attn_norm, l.qkv.hx, D.xn, M));
+      BTF_TRY(gemv(D, {{&l.qkv, D.bA}, {&l.zg, D.bB}}, E, BTF_STORE, M));
+      for (int m = 0; m < M; ++m) {
+        const GdnArgs ga{D.xn + (size_t)m * E, l.alpha_w, l.beta_w, l.ssm_dt, l.ssm_a, E, l.ab_bf16,
+                         D.bA + (size_t)m * C, l.conv_state, l.conv_w, d.conv_kernel, D.C, D.bB + (size_t)m * Z,
+                         l.ssm_state, l.ssm_norm, D.NK, D.DK, D.DV, D.QK, d.rms_eps, D.d_ppos + m,
+                         D.bO + (size_t)m * D.DI, D.NV};
+        BTF_TRYC(launch_gdn_mix(ga, D.st));
+      }
+      BTF_TRY(prep(D, D.bO, D.DI, nullptr, l.out.hx, nullptr, M));
+      BTF_TRY(gemv(D, {{&l.out, D.x}}, D.DI, BTF_ADD, M));
+    } else {
+      const int NQ = l.wq.N, NK = l.wk.N, NV = l.wv.N, HO = H * HD;
+      BTF_TRY(prep(D, D.x, E, l.attn_norm, l.wq.hx, nullptr, M));
+      BTF_TRY(gemv(D, {{&l.wq, D.bA}, {&l.wk, D.bB}, {&l.wv, D.bC}}, E, BTF_STORE, M));
+      for (int m = 0; m < M; ++m) {
+        const float* qf = D.bA + (size_t)m * NQ;
+        BTF_TRYC(launch_attn_prep(qf, D.bB + (size_t)m * NK, D.bC + (size_t)m * NV, l.q_norm, l.k_norm, H, HK, HD,
+                                  d.n_rot, D.theta_scale, d.rms_eps, D.d_ppos + m, D.o.round_q_f16, D.bQ, l.kc, l.vc,
+                                  D.st));
+        BTF_TRYC(launch_attention(D.bQ, l.kc, l.vc, qf, H, HK, HD, D.o.n_ctx, D.o.attn_splits, D.d_ppos + m, D.part,
+                                  D.bO + (size_t)m * HO, D.st));
+      }
+      BTF_TRY(prep(D, D.bO, HO, nullptr, l.wo.hx, nullptr, M));
+      BTF_TRY(gemv(D, {{&l.wo, D.x}}, HO, BTF_ADD, M));
+    }
+    BTF_TRY(prep(D, D.x, E, l.post_norm, l.gate.hx, nullptr, M));
+    BTF_TRY(gemv(D, {{&l.gate, D.bG}, {&l.up, nullptr}}, E, BTF_SWIGLU, M));
+    BTF_TRY(prep(D, D.bG, F, nullptr, l.down.hx, nullptr, M));
+    BTF_TRY(gemv(D, {{&l.down, D.x}}, F, BTF_ADD, M));
+  }
+  BTF_TRY(prep(D, D.x + (size_t)(M - 1) * E, E, D.out_norm, D.output.hx, nullptr));
+  BTF_TRY(gemv(D, {{&D.output, D.logits}}, E, BTF_STORE));
+  BTF_TRYC(launch_argmax(D.logits, d.n_vocab, D.amax_v, D.amax_i, Decoder::kArgmaxParts, D.d_next, D.d_tok, nullptr,
                          D.st));
   return BTF_OK;
 }
@@ -904,6 +967,46 @@ int btf_decoder_step(void* handle, int32_t token, float* logits, int32_t* next) 
   BTF_TRY(settle(D));
   D.n_steps += 1;
   D.wall_s += seconds_since(t0);
+  if (next) *next = D.h_io[1];
+  return BTF_OK;
+}
+
+int btf_decoder_prefill(void* handle, const int32_t* tokens_host, int n, int max_chunk, float* logits,
+                        int32_t* next) {
+  if (!handle || !tokens_host || n < 1) return fail(BTF_ERR_ARG, "btf_decoder_prefill: null handle/tokens or n < 1");
+  Decoder& D = *static_cast<Decoder*>(handle);
+  if (max_chunk == 0) max_chunk = Decoder::kMaxChunk;
+  if (max_chunk < 1 || max_chunk > Decoder::kMaxChunk)
+    return fail(BTF_ERR_ARG, "btf_decoder_prefill: max_chunk must be 1..%d (got %d)", Decoder::kMaxChunk, max_chunk);
+  if (D.world > 1)
+    return fail(BTF_ERR_UNSUPPORTED, "btf_decoder_prefill: tensor-parallel decoders take the prompt by btf_decoder_step");
+  if (D.pos + n > D.o.n_ctx) return fail(BTF_ERR_ARG, "btf_decoder_prefill: context full (n_ctx %d)", D.o.n_ctx);
+  for (int i = 0; i < n; ++i)
+    if (tokens_host[i] < 0 || tokens_host[i] >= D.d.n_vocab)
+      return fail(BTF_ERR_ARG, "btf_decoder_prefill: token %d out of range", tokens_host[i]);
+  BTF_TRY(settle(D));
+  for (int i = 0; i < n; i += max_chunk) {
+    const int M = std::min(max_chunk, n - i);
+    int32_t tp[2 * Decoder::kMaxChunk] = {};
+    for (int m = 0; m < M; ++m) {
+      tp[m] = tokens_host[i + m];
+      tp[Decoder::kMaxChunk + m] = D.pos + m;
+    }
+    // the previous chunk's kernels are done with the chunk arrays (the stream is idle here)
+    cudaError_t e = cudaStreamSynchronize(D.st);
+    if (e == cudaSuccess) e = cudaMemcpy(D.d_ptok, tp, 2 * Decoder::kMaxChunk * sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_prefill: tokens");
+    BTF_TRY(enqueue_chunk(D, M));
+    D.pos += M;
+    const int32_t pos = D.pos;  // the device position the next step reads
+    if ((e = cudaStreamSynchronize(D.st)) == cudaSuccess)
+      e = cudaMemcpy(D.d_pos, &pos, sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_prefill");
+  }
+  cudaError_t e = cudaMemcpy(D.h_io + 1, D.d_next, sizeof(int32_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpy(logits, D.logits, (size_t)D.d.n_vocab * sizeof(float), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "btf_decoder_prefill: results");
   if (next) *next = D.h_io[1];
   return BTF_OK;
 }

@@ -390,6 +390,14 @@ int btf_decoder_open(const char* gguf_path, const btf_decoder_opts* opts, void**
 int btf_decoder_synthetic(const btf_decoder_dims* dims, uint64_t seed, const btf_decoder_opts* opts, void** handle);
 /* One step for `token`: the greedy next token into *next; logits (host, n_vocab) when non-NULL. Synchronous. */
 int btf_decoder_step(void* handle, int32_t token, float* logits, int32_t* next);
+/* The prompt in chunks of up to max_chunk tokens (0: 8; 1..8), as GpuDecoder::prefill /
+ * forward_chunk (src/cuda/gpu_decoder.cu:154-171, :401-450): each chunk runs every
+ * prep and ternary matmul once over its rows, the mixers and the attention token by
+ * token at each token's position. After it, pos += n; the greedy token after the last
+ * prompt token goes to *next (and to the device token a btf_decoder_run would read);
+ * logits (host, n_vocab) of the last prompt token when non-NULL. Synchronous, eager
+ * (no graph). One GPU only: a tensor-parallel decoder returns BTF_ERR_UNSUPPORTED. */
+int btf_decoder_prefill(void* handle, const int32_t* tokens_host, int n, int max_chunk, float* logits, int32_t* next);
 /* `steps` steps, each fed the previous step's greedy token on the device; asynchronous on the decoder's stream. */
 int btf_decoder_run(void* handle, int steps);
 int btf_decoder_reset(void* handle);

@@ -121,9 +121,10 @@ class Decoder {
     throw_if(btf_decoder_step(h_, token, logits, &next), "btf_decoder_step");
     return next;
   }
-  int prefill(const int32_t* tokens, int n, float* logits) {
-    int next = -1;
-    for (int i = 0; i < n; ++i) next = step(tokens[i], i + 1 == n ? logits : nullptr);
+  // FastDecoder::prefill (gpu_decoder.cu:154-171): chunks of up to max_batch tokens
+  int prefill(const int32_t* tokens, int n, float* logits, int max_batch = 0) {
+    int32_t next = -1;
+    throw_if(btf_decoder_prefill(h_, tokens, n, max_batch, logits, &next), "btf_decoder_prefill");
     return next;
   }
   void reset() { throw_if(btf_decoder_reset(h_), "btf_decoder_reset"); }

@@ -66,6 +66,22 @@ def test_decoder_matches_emulator(cuda, btf, ref, tmp_path, label):
     for t in PROMPT:
         nxt, _ = gpu.step(t)
     assert nxt == int(np.argmax(last_prompt))
+    # batched prompt == one token at a time (test_gpu_decoder.cpp:102-121): chunks of
+    # 8 and of 3 tokens; next == argmax, pos == prompt length, logits within rel-RMS
+    # 1e-5 of the per-token ones, a reset and a repeat bit-exact, then a step works
+    for mb in (8, 3):
+        with btf.Decoder(path, n_ctx=64) as pb:
+            outs = []
+            for rep in range(2):
+                if rep:
+                    pb.reset()
+                nxt, lb = pb.prefill(PROMPT, max_chunk=mb, logits=True)
+                assert nxt == int(np.argmax(lb)) and pb.info()["pos"] == len(PROMPT)
+                outs.append(lb)
+            assert rel_rms(outs[0], last_prompt) <= 1e-5, (label, mb, rel_rms(outs[0], last_prompt))
+            assert np.array_equal(outs[0], outs[1])
+            pb.step(nxt)
+            assert pb.info()["pos"] == len(PROMPT) + 1
     assert btf.device_error() == 0
     gpu.close()
     eager.close()
