@@ -52,6 +52,7 @@ const DeviceInfo* current_device() {
 // Kernel attribute set-up lives beside each kernel; btf_init calls these.
 int gemv_setup(DeviceInfo& d);
 int gemm_setup(DeviceInfo& d);
+int gemm_wm_setup(DeviceInfo& d);
 int chain_setup(DeviceInfo& d);
 
 }  // namespace btf
@@ -106,7 +107,7 @@ int btf_init(int device) {
     st = fail(BTF_ERR_UNSUPPORTED, "btf_b200 is built for sm_100a (B200); device %d is sm_%d%d", device, major, minor);
   } else if (g_dev[device].ready) {
     st = BTF_OK;  // already initialised
-  } else if ((st = gemv_setup(d)) == BTF_OK && (st = gemm_setup(d)) == BTF_OK &&
+  } else if ((st = gemv_setup(d)) == BTF_OK && (st = gemm_setup(d)) == BTF_OK && (st = gemm_wm_setup(d)) == BTF_OK &&
              (st = chain_setup(d)) == BTF_OK) {
     d.ready = true;
     g_dev[device] = d;

@@ -1,0 +1,713 @@
+// Weight-major ternary GEMM on the tcgen05 tensor cores, for small batches
+// (1 <= M <= 64 rows per tile): the 128-row MMA operand is the WEIGHTS and the
+// activation rows are the MMA's N side.
+//
+// Same contract as gemm_kernel (gemm.cu), which replaces the reference's
+// repeated small-batch passes of launch_gemv (src/cuda/kernels.cu:805-821)
+// with the math of src/emu_decoder.cpp:143-165: per (activation row m, weight
+// row n, 32-column step) one exact int32 idot, scaled by fp16 scale[n] * d[m]
+// and summed in fp32. gemm_kernel puts 128 activation rows on the MMA's M side,
+// so a batch of 16 fills an eighth of every instruction; here a CTA covers 128
+// weight rows x up to 64 activation rows, and every weight byte is read once
+// for the whole batch.
+//
+// The kernel is persistent: CTA b takes the 128-row weight tiles b, b + grid,
+// ... and its pipelines run on across tile boundaries, so the epilogue writes
+// one tile's rows while the next tile's copies and MMAs are in flight. NA (16,
+// 32 or 64) is the activation rows padded to the MMA's N; a TMEM slot of 256
+// columns holds 256 / (4 NA) whole 128-column blocks (4 steps of NA columns).
+//   warp 0      producer (one thread): per block, TMA of the int8 activation
+//               tile (NA rows, 128B swizzle) into the B ring;
+//   warp 1      MMA issuer (one thread) + TMEM owner: per slot one bias MMA
+//               (N = 256), per block 4 data MMAs (A = weight codes, B =
+//               activations); 2 slots in flight;
+//   warps 2-3   expanders: per 1024-column slice, expander thread 0 copies the
+//               tile's 16 whole panels and the slice's d and s (activation
+//               block scales and sums); per block, the 2-bit codes become int8
+//               codes (trit + 1: 0, 1, 2) of the K-major SW128 A tile, the fp16
+//               weight scales fp32 (x 2^39), and each activation row gets its
+//               d per step and the code-sum correction below;
+//   warps 4-19  epilogue: TMEM lane = weight row; each warp reads 16 activation
+//               rows x the 4 steps of one block of every slot.
+// Arithmetic: the codes are trit + 1, so a step's MMA result is sum (t+1) q =
+// idot + s, with s = sum q of the step (the Q8 block sum); a bias MMA of two
+// constant tiles first sets every region to 8192, so P = idot + s + 8192 lies
+// in [64, 16320]. P's bits read as fp32 are the denormal P * 2^-149, and
+//   x = fma(P * 2^-149, 2^110, -2^-26) = (idot + s) * 2^-39
+// exactly (an exact product, and an integer below 2^14 times 2^-39 for the
+// sum). Per step T = fma(d, x, T); per block T -= sum_steps d * s * 2^-39 (the
+// expanders' correction) and acc += scale * 2^39 * T. No integer-to-float
+// conversion runs, and every finite d takes the same path. The warps of one
+// column group that read different blocks of a slot add their sums in a fixed
+// order at the end of the tile, and rows go to y with coalesced stores (lanes
+// are consecutive weight rows).
+// Every wait is bounded; on a time-out the kernel records the error word, stops
+// issuing work, waits (bounded) for its copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace btf {
+namespace {
+
+using namespace tc;
+
+constexpr int kTileW = 128;         // weight rows per tile (MMA M)
+constexpr int kNAMax = 64;          // activation rows per tile at most (MMA N)
+constexpr int kWmMaxM = kNAMax;     // btf_gemm_wm takes 1 <= M <= this
+constexpr int kChunk = 128;         // K columns per block (one weight-scale block)
+constexpr int kSteps = 4;           // 32-column MMA steps per block
+constexpr int kBlocksPerSliceW = kCols / kChunk;  // 8 blocks per 1024-column panel slice
+constexpr int kGroups = kTileW / kRows;  // 16 panel row groups per tile
+constexpr int kStagesS = 8;         // scale stages (a power of two)
+constexpr int kSlots = 2;           // TMEM slots in flight
+constexpr int kSlotCols = 256;      // TMEM columns per slot
+constexpr int kTmemCols = kSlots * kSlotCols;  // 512: all of TMEM
+constexpr int kEpiWarps = 16;       // 4 lane quarters x 4
+constexpr int kExpWarps = 2;        // expanders (64 threads)
+constexpr int kExpWarp0 = 2, kEpiWarp0 = kExpWarp0 + kExpWarps;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 640: 5 warps per SMSP, 96 registers a thread
+constexpr int kBiasA = 4, kBiasB = 64, kBias = 32 * kBiasA * kBiasB;  // every region starts at 8192
+static_assert(kBias == 8192, "the bias is a power of two above 32 * 2 * 127");
+static_assert(kTileW % (kExpWarps * 32) == 0 && kGroups % (kExpWarps * 2) == 0, "expander work divides evenly");
+constexpr uint64_t kWaitNs = 1000000000ull;
+
+// Shared memory, per padded batch width NA:
+//   code ring   (kCodeStages) one 1024-column slice of the tile: the 16 row
+//               groups' whole panels (16 x 2176 B, 1-D bulk copies: codes and
+//               fp16 scales), the activation scales d of the slice [NA][32]
+//               fp32 and the activation block sums s [NA][32] int32 (one tiled
+//               copy of NA 128-byte rows each);
+//   A ring      (kAStages) [128][128] int8 codes (trit + 1) of one block
+//               (SW128), written by the expanders;
+//   B ring      (kBStages) [NA][128] int8 activations of one block (SW128, TMA);
+//   scale ring  (8) per block: W fp32 weight scales x 2^39 [128], d [4 steps]
+//               [64] fp32, the code-sum correction -sum_steps d * s * 2^-39 [64]
+//               fp32, and (dump form) s [4 steps][64] int32;
+//   Stg         [16 activation rows][128 weight rows] fp32, the end-of-tile combine.
+// Whole panels keep the number of copy requests per block low: a tiled copy of
+// a block's codes alone was 64 rows of 64 bytes, and the copy unit's request
+// rate, not HBM, then set the pace.
+constexpr int kABytes = kTileW * kChunk;          // 16 KB
+constexpr int kPanelsBytes = kGroups * kPanelBytes;  // 34816 B
+constexpr int kWBytes = kTileW * 4;               // 512 B
+constexpr int kDTBytes = kSteps * kNAMax * 4;     // 1 KB: d [step][row]
+constexpr int kCorrBytes = kNAMax * 4;            // 256 B
+constexpr int kSTBytes = kSteps * kNAMax * 4;     // 1 KB: s [step][row]
+constexpr int kSOffD = kWBytes, kSOffCorr = kSOffD + kDTBytes, kSOffS = kSOffCorr + kCorrBytes;
+constexpr int kScaleStageBytes = kSOffS + kSTBytes;
+constexpr int kStgBytes = 16 * kTileW * 4;        // 8 KB
+// bias operands: K-major, no swizzle, 8-row x 16-byte core matrices; every
+// byte equal, so any core-matrix order reads the same values
+constexpr int kBiasN = kSlotCols;                 // one bias MMA covers a slot
+constexpr int kBiasABytes = kTileW * 32, kBiasBBytes = kBiasN * 32;
+constexpr uint32_t kIdescBias = idesc_i8(kTileW, kBiasN);
+static_assert(kBiasN <= 256 && kBiasN % 16 == 0, "M=128 MMA: N a multiple of 16 up to 256");
+constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+
+template <int NA>
+struct Shape {
+  static_assert(NA == 16 || NA == 32 || NA == 64, "NA is 16, 32 or 64");
+  static constexpr int kNcg = NA / 16;             // 16-row column groups per step
+  static constexpr int kBlkPerSlot = 4 / kNcg;     // blocks per TMEM slot
+  static constexpr uint32_t kIdesc = idesc_i8(kTileW, NA);
+  static_assert(kBlkPerSlot * kSteps * NA == kSlotCols, "a slot is whole blocks");
+  // ring depths: what fits 227 KB for this width
+  static constexpr int kCodeStages = NA == 16 ? 3 : 2;
+  static constexpr int kAStages = NA == 32 ? 4 : 3;
+  static constexpr int kBStages = NA == 64 ? 4 : 6;
+  static constexpr int kBBytes = NA * kChunk;
+  static constexpr int kDSliceBytes = NA * 32 * 4;  // d (and s) of one slice: [NA][32]
+  static constexpr int kCodeStageBytes = kPanelsBytes + 2 * kDSliceBytes;
+  static constexpr int kOffCode = 0;
+  static constexpr int kOffA = align1k(kOffCode + kCodeStages * kCodeStageBytes);
+  static constexpr int kOffB = kOffA + kAStages * kABytes;
+  static constexpr int kOffS = kOffB + kBStages * kBBytes;
+  static constexpr int kOffStg = kOffS + kStagesS * kScaleStageBytes;
+  static constexpr int kOffBiasA = align1k(kOffStg + kStgBytes);
+  static constexpr int kOffBiasB = kOffBiasA + kBiasABytes;
+  static constexpr int kOffBar = kOffBiasB + kBiasBBytes;
+  // c_full; a_full, a_empty; b_full, b_empty; s_full, s_empty; mma_done, d_free; final; x_done
+  static constexpr int kNumBars = 2 * kCodeStages + 2 * kAStages + 2 * kBStages + 2 * kStagesS + 2 * kSlots + 1;
+  static constexpr int kOffFlags = kOffBar + kNumBars * 8;  // TMEM base (4 B), abort flag (4 B)
+  static constexpr int kSmemBytes = kOffFlags + 16 + 1024;   // + slack for 1024-B alignment
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kCodeStageBytes % 1024 == 0 && kBBytes % 1024 == 0 && kOffB % 1024 == 0, "SW128 / copy alignment");
+  static_assert(kOffS % 16 == 0 && kOffStg % 16 == 0, "vector accesses aligned");
+};
+
+struct WmParams {
+  int N, M, K;
+  int ntiles;           // ceil(N / 128)
+  int nslices;          // panel slices per row group: ceil(K / 1024)
+  int ngroups;          // row groups of the matrix: ceil(N / 8)
+  const uint8_t* panels;
+  float* y;
+  int ldy;
+  int mode;             // BTF_STORE / BTF_ADD
+  int* err;
+  int32_t* idot;        // DUMP kernel: [M][N][K/32] integer accumulators (no y is stored)
+};
+
+// Tensor maps: tmB the int8 activation [M][K] (box 128 x NA, SW128); tmD the
+// activation scales [M][K/32] and tmS the activation block sums [M][K/32]
+// (box 32 x NA: one slice). The panels arrive by 1-D bulk copies from p.panels.
+// DUMP (parity/debug): the kernel writes every step's integer accumulator
+// P - kBias (= idot) to p.idot and stores no y.
+template <int NA, bool DUMP>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_wm_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
+                   const __grid_constant__ CUtensorMap tmS, const WmParams p) {
+  using S = Shape<NA>;
+  constexpr int CS = S::kCodeStages, AS = S::kAStages, BS = S::kBStages;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned base (SW128 atoms and TMA destinations)
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.K / kChunk;                                   // blocks per tile
+  const int nsl = (nb + kBlocksPerSliceW - 1) / kBlocksPerSliceW;  // slices per tile
+  // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ... (the grid is at most ntiles)
+  const int my_tiles = ((int)blockIdx.x < p.ntiles) ? (p.ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+  const uint32_t bar0 = sbase + S::kOffBar;
+  auto c_full = [&](int q) { return bar0 + q * 8; };                          // copies: slice stage q landed
+  auto a_full = [&](int s) { return bar0 + (CS + s) * 8; };                   // expanders: A[s] written
+  auto a_empty = [&](int s) { return bar0 + (CS + AS + s) * 8; };             // MMA commit: A[s] read
+  auto b_full = [&](int s) { return bar0 + (CS + 2 * AS + s) * 8; };          // TMA: B[s] landed
+  auto b_empty = [&](int s) { return bar0 + (CS + 2 * AS + BS + s) * 8; };    // MMA commit: B[s] read
+  constexpr int kB1 = CS + 2 * AS + 2 * BS;
+  auto s_full = [&](int s) { return bar0 + (kB1 + s) * 8; };                  // expanders: scale stage ready
+  auto s_empty = [&](int s) { return bar0 + (kB1 + kStagesS + s) * 8; };      // epilogue: stage read
+  auto mma_done = [&](int cs) { return bar0 + (kB1 + 2 * kStagesS + cs) * 8; };
+  auto d_free = [&](int cs) { return bar0 + (kB1 + 2 * kStagesS + kSlots + cs) * 8; };
+  const uint32_t final_bar = bar0 + (kB1 + 2 * kStagesS + 2 * kSlots) * 8;
+  auto x_done = [&](int q) { return bar0 + (kB1 + 2 * kStagesS + 2 * kSlots + 1 + q) * 8; };  // expanders: slice q read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffFlags);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kOffFlags + 8);
+  // scale stage ss: Dblk, W, P, F
+  auto sstage = [&](int ss) { return smem + S::kOffS + ss * kScaleStageBytes; };
+
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < CS; ++q) {
+      mbar_init(c_full(q), 1);
+      mbar_init(x_done(q), kExpWarps);
+    }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(a_full(s), kExpWarps);
+      mbar_init(a_empty(s), 1);
+    }
+    for (int s = 0; s < BS; ++s) {
+      mbar_init(b_full(s), 1);
+      mbar_init(b_empty(s), 1);
+    }
+    for (int s = 0; s < kStagesS; ++s) {
+      mbar_init(s_full(s), kExpWarps);
+      mbar_init(s_empty(s), 4 * S::kNcg);  // the warps that read one block: 4 lane quarters x column groups
+    }
+    for (int r = 0; r < kSlots; ++r) {
+      mbar_init(mma_done(r), 1);
+      mbar_init(d_free(r), kEpiWarps);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  {  // the bias MMA's constant operand tiles
+    const uint32_t va = 0x01010101u * kBiasA, vb = 0x01010101u * kBiasB;
+    for (int i = threadIdx.x; i < (kBiasABytes + kBiasBBytes) / 16; i += kThreads) {
+      const uint32_t v = i < kBiasABytes / 16 ? va : vb;
+      reinterpret_cast<uint4*>(smem + S::kOffBiasA)[i] = make_uint4(v, v, v, v);
+    }
+    fence_proxy_async_smem();  // generic writes -> visible to the tensor core (async proxy)
+  }
+  if (warp == 1) {  // TMEM: all 512 columns (2 slots x 256) for this CTA
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // bounded wait; false (and the abort flag set) on a time-out or after another role's time-out
+  auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (mbar_wait_bounded(bar, parity, kWaitNs)) return true;
+    atomicCAS(p.err, 0, kErrWaitTimeout);
+    *abort_flag = 1;
+    return false;
+  };
+  // the same wait made warp-uniform: every lane waits, the warp goes on only if all of them saw the phase
+  auto wwait = [&](uint32_t bar, uint32_t parity) -> bool { return __all_sync(0xffffffffu, wait(bar, parity)); };
+
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer: activation tiles
+    if (lane == 0) {
+      int issued = 0;  // blocks whose activation copy was issued
+      pdl_wait();      // the activation is written by the previous kernel
+      int s = 0, it = 0;
+      uint32_t ph = 0;
+      bool stop = false;
+      for (int ti = 0; ti < my_tiles && !stop; ++ti) {
+        for (int kb = 0; kb < nb; ++kb, ++it) {
+          if (it >= BS && !wait(b_empty(s), ph ^ 1u)) {
+            stop = true;
+            break;
+          }
+          mbar_expect_tx(b_full(s), S::kBBytes);
+          tma_load_2d(sbase + S::kOffB + s * S::kBBytes, &tmB, kb * kChunk, 0, b_full(s));
+          issued = it + 1;
+          if (++s == BS) s = 0, ph ^= 1u;
+        }
+      }
+      if (*abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
+        for (int c = max(0, issued - BS); c < issued; ++c)
+          mbar_wait_bounded(b_full(c % BS), (uint32_t)((c / BS) & 1), kWaitNs / 10);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint64_t bias_ad = smem_desc_noswz(sbase + S::kOffBiasA), bias_bd = smem_desc_noswz(sbase + S::kOffBiasB);
+      const uint64_t a_desc0 = smem_desc_sw128(sbase + S::kOffA), b_desc0 = smem_desc_sw128(sbase + S::kOffB);
+      int sa = 0, sb = 0, u = 0;  // A stage, B stage; TMEM slot uses so far
+      uint32_t pha = 0, phb = 0;
+      bool stop = false;
+      for (int ti = 0; ti < my_tiles && !stop; ++ti) {
+        for (int kb = 0; kb < nb; ++kb) {
+          if (!wait(a_full(sa), pha) || !wait(b_full(sb), phb)) {
+            stop = true;
+            break;
+          }
+          const int pos = kb % S::kBlkPerSlot, cs = u & 1;
+          const uint32_t dt = tmem_base + cs * kSlotCols;
+          if (pos == 0) {
+            if (u >= kSlots && !wait(d_free(cs), (uint32_t)(((u >> 1) - 1) & 1))) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            mma_i8<kIdescBias>(dt, bias_ad, bias_bd, 0u);  // the slot's regions = kBias
+          } else {
+            tc_fence_after();
+          }
+          const uint64_t ad = a_desc0 + (uint64_t)((sa * kABytes) >> 4);
+          const uint64_t bd = b_desc0 + (uint64_t)((sb * S::kBBytes) >> 4);
+#pragma unroll
+          for (int ks = 0; ks < kSteps; ++ks)
+            mma_i8<S::kIdesc>(dt + (pos * kSteps + ks) * NA, ad + (ks * 32 >> 4), bd + (ks * 32 >> 4), 1u);
+          mma_commit(a_empty(sa));  // A and B of this block are free once its MMAs finish
+          mma_commit(b_empty(sb));
+          if (pos == S::kBlkPerSlot - 1 || kb == nb - 1) {
+            mma_commit(mma_done(cs));  // the slot's MMAs (commits track all prior MMAs)
+            ++u;
+          }
+          if (++sa == AS) sa = 0, pha ^= 1u;
+          if (++sb == BS) sb = 0, phb ^= 1u;
+        }
+      }
+      mma_commit(final_bar);  // completes when every MMA issued above has finished
+      mbar_wait_bounded(final_bar, 0, kWaitNs);
+    }
+  } else if (warp < kEpiWarp0) {
+    // ------------------------------------------------------------ code expanders
+    // Thread e expands quad h of row groups gi, gi + GS, ... (GS = expander
+    // threads / 16) x 16 columns (sub-block t/2, half t&1) of every block: the
+    // 16-byte quad words at panel(group) + h*1024 + (t&1)*512 + block*64 +
+    // (t/2)*16 of the slice stage, into the int8 codes (trit + 1: 0, 1, 2) of
+    // the K-major SW128 A tile. It converts the fp16 scales of tile rows e,
+    // e + E, ... (E = expander threads), and thread e < NA writes activation
+    // row e's d per step and its code-sum correction. Expander thread 0 also
+    // issues the slice copies, kCodeStages slices ahead of the slice being
+    // expanded.
+    constexpr int E = kExpWarps * 32, GS = E / 16;
+    static_assert(NA <= E, "one expander thread per activation row");
+    const int e = threadIdx.x - kExpWarp0 * 32;
+    const int t = e & 7, h = (e >> 3) & 1, gi = e >> 4;
+    const int coff = h * 1024 + (t & 1) * 512 + (t >> 1) * 16;
+    const int total_sl = my_tiles * nsl;  // slices this CTA walks, over all its tiles
+    // one slice into stage gsl % CS: the tile's whole panels of the slice and its activation scales
+    auto issue_slice = [&](int gsl) {
+      const int ti = gsl / nsl, sl = gsl % nsl, q = gsl % CS;
+      const int g0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kGroups;
+      const int ng = min(kGroups, p.ngroups - g0);  // row groups of a partial last tile are left unloaded
+      uint8_t* dst = smem + S::kOffCode + q * S::kCodeStageBytes;
+      mbar_expect_tx(c_full(q), (uint32_t)(ng * kPanelBytes + 2 * S::kDSliceBytes));
+      for (int g = 0; g < ng; ++g)
+        bulk_g2s(smem_u32(dst + g * kPanelBytes), p.panels + ((int64_t)(g0 + g) * p.nslices + sl) * kPanelBytes,
+                 kPanelBytes, c_full(q));
+      tma_load_2d(smem_u32(dst + kPanelsBytes), &tmD, sl * 32, 0, c_full(q));
+      tma_load_2d(smem_u32(dst + kPanelsBytes + S::kDSliceBytes), &tmS, sl * 32, 0, c_full(q));
+    };
+    int nissued = 0;
+    if (e == 0) {
+      pdl_wait();  // the activation scales are written by the previous kernel
+      for (; nissued < min(CS, total_sl); ++nissued) issue_slice(nissued);
+    }
+    int sa = 0, ss = 0, it = 0, q = 0;
+    uint32_t pha = 0, phs = 0, phc = 0;
+    bool stop = false;
+    for (int ti = 0; ti < my_tiles && !stop; ++ti) {
+      for (int kb = 0; kb < nb; ++kb, ++it) {
+        const int b = kb & (kBlocksPerSliceW - 1);
+        if (b == 0 && !wwait(c_full(q), phc)) {
+          stop = true;
+          break;
+        }
+        // A[sa] is free once the MMAs of block it - AS have read it
+        if (it >= AS && !wwait(a_empty(sa), pha ^ 1u)) {
+          stop = true;
+          break;
+        }
+        const uint8_t* cst = smem + S::kOffCode + q * S::kCodeStageBytes;
+        uint8_t* as = smem + S::kOffA + sa * kABytes;
+#pragma unroll
+        for (int r = 0; r < kGroups / GS; ++r) {
+          const int g = gi + GS * r;
+          const uint4 w = *reinterpret_cast<const uint4*>(cst + g * kPanelBytes + coff + b * 64);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int n = g * 8 + h * 4 + k;  // row of the tile
+            const uint4 o = make_uint4((w.x >> (2 * k)) & 0x03030303u, (w.y >> (2 * k)) & 0x03030303u,
+                                       (w.z >> (2 * k)) & 0x03030303u, (w.w >> (2 * k)) & 0x03030303u);
+            const int off = (n >> 3) * 1024 + (n & 7) * 128 + ((t ^ (n & 7)) << 4);
+            *reinterpret_cast<uint4*>(as + off) = o;
+          }
+        }
+        fence_proxy_async_smem();  // generic writes of A -> visible to the tensor core (async proxy)
+        uint16_t hb[kTileW / E];
+#pragma unroll
+        for (int r = 0; r < kTileW / E; ++r) {
+          const int row = e + r * E;  // fp16 scale of tile row `row` for this block: [block][row in group]
+          hb[r] = *reinterpret_cast<const uint16_t*>(cst + (row >> 3) * kPanelBytes + kCodeBytes + b * 16 + (row & 7) * 2);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full(sa));
+        // scale stage: after the epilogue has released it
+        if (it >= kStagesS && !wwait(s_empty(ss), phs ^ 1u)) {
+          stop = true;
+          break;
+        }
+        uint8_t* sst = sstage(ss);
+#pragma unroll
+        for (int r = 0; r < kTileW / E; ++r)
+          reinterpret_cast<float*>(sst)[e + r * E] = __half2float(__ushort_as_half(hb[r])) * 0x1p39f;
+        if (e < NA) {
+          // row e's d and s of this block: 16-byte chunk b of its 128-byte slice
+          // row, which the 128B-swizzled copy placed at chunk b ^ (e & 7)
+          const int off = e * 128 + ((b ^ (e & 7)) << 4);
+          const float4 d4 = *reinterpret_cast<const float4*>(cst + kPanelsBytes + off);
+          const int4 s4 = *reinterpret_cast<const int4*>(cst + kPanelsBytes + S::kDSliceBytes + off);
+          float* dT = reinterpret_cast<float*>(sst + kSOffD);  // [step][row]
+          dT[0 * NA + e] = d4.x;
+          dT[1 * NA + e] = d4.y;
+          dT[2 * NA + e] = d4.z;
+          dT[3 * NA + e] = d4.w;
+          // the codes are trit + 1, so the MMA adds s = sum q of each step:
+          // correction -sum_steps d * s * 2^-39 for the epilogue's block sum
+          float c = fmaf(d4.x * -0x1p-39f, (float)s4.x, 0.f);
+          c = fmaf(d4.y * -0x1p-39f, (float)s4.y, c);
+          c = fmaf(d4.z * -0x1p-39f, (float)s4.z, c);
+          c = fmaf(d4.w * -0x1p-39f, (float)s4.w, c);
+          reinterpret_cast<float*>(sst + kSOffCorr)[e] = c;
+          if constexpr (DUMP) {
+            int* sT = reinterpret_cast<int*>(sst + kSOffS);
+            sT[0 * NA + e] = s4.x;
+            sT[1 * NA + e] = s4.y;
+            sT[2 * NA + e] = s4.z;
+            sT[3 * NA + e] = s4.w;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_full(ss));
+        if (++sa == AS) sa = 0, pha ^= 1u;
+        if (++ss == kStagesS) ss = 0, phs ^= 1u;
+        if (b == kBlocksPerSliceW - 1 || kb == nb - 1) {
+          // the slice is expanded: once both expander warps are past it, its
+          // stage takes the slice CS ahead
+          __syncwarp();
+          if (lane == 0) mbar_arrive(x_done(q));
+          if (e == 0 && nissued < total_sl) {
+            if (wait(x_done(q), phc)) {
+              issue_slice(nissued);
+              ++nissued;
+            }
+          }
+          if (++q == CS) q = 0, phc ^= 1u;
+        }
+      }
+    }
+    if (e == 0 && *abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
+      for (int c = max(0, nissued - CS); c < nissued; ++c)
+        mbar_wait_bounded(c_full(c % CS), (uint32_t)((c / CS) & 1), kWaitNs / 10);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Warp (q, j): TMEM lanes q*32.. (weight rows), column group cg of every
+    // step (16 activation rows), block blk of every slot.
+    const int we = warp - kEpiWarp0;
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int cg = (we >> 2) % S::kNcg, blk = (we >> 2) / S::kNcg;
+    const int n = q * 32 + lane;        // weight row of the tile
+    const bool live = cg * 16 < p.M;    // some of this warp's activation rows exist
+    const int nslots = (nb + S::kBlkPerSlot - 1) / S::kBlkPerSlot;
+    float* stg = reinterpret_cast<float*>(smem + S::kOffStg);
+    // x = fma(P * 2^-149, 2^110, -2^-26) = (P - 8192) * 2^-39 exactly: P's bits
+    // read as fp32 are the denormal P * 2^-149, the product is exact and so is
+    // the sum, an integer below 2^14 times 2^-39
+    const float2 k110 = make_float2(0x1p110f, 0x1p110f), nbias = make_float2(-0x1p-26f, -0x1p-26f);
+    pdl_wait();  // y is read (BTF_ADD) and written below
+    int u = 0, git = 0;  // TMEM slot uses; this tile's first block in the CTA's block sequence
+    bool ok = true;
+    for (int ti = 0; ti < my_tiles; ++ti, git += nb) {
+      const int n0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kTileW;
+      float2 acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
+      for (int su = 0; su < nslots; ++su, ++u) {
+        const int cs = u & 1, kb = su * S::kBlkPerSlot + blk;
+        const bool has = kb < nb;  // the last slot of a tile may hold fewer blocks
+        const int gb = git + kb, ss = gb & (kStagesS - 1);
+        if (ok) ok = wwait(mma_done(cs), (uint32_t)(u >> 1) & 1u);
+        if (ok && has) ok = wwait(s_full(ss), (uint32_t)(gb / kStagesS) & 1u);
+        if (!ok) continue;
+        if (has && live) {
+          tc_fence_after();
+          const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + cs * kSlotCols + blk * kSteps * NA + cg * 16;
+          const float4* dp = reinterpret_cast<const float4*>(sstage(ss) + kSOffD) + cg * 4;  // d [step][row]
+          uint32_t buf[2][16];
+          float2 tsum[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) tsum[i] = make_float2(0.f, 0.f);
+          tmem_ld16_async(tl, buf[0]);
+#pragma unroll
+          for (int ks = 0; ks < kSteps; ++ks) {
+            tmem_wait16(buf[ks & 1]);
+            if (ks + 1 < kSteps) {
+              tmem_ld16_async(tl + (ks + 1) * NA, buf[(ks + 1) & 1]);  // in flight during this step's math
+            } else {  // the block is in registers: this warp's reads of the slot are done
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(d_free(cs));
+            }
+            const uint32_t* P = buf[ks & 1];
+            if constexpr (DUMP) {  // integer accumulators only: idot = P - kBias - s, no y
+              if (n0 + n < p.N) {
+                const int* sT = reinterpret_cast<const int*>(sstage(ss) + kSOffS) + ks * NA + cg * 16;
+                const int64_t mstride = (int64_t)p.N * (p.K >> 5);
+                int32_t* out = p.idot + (int64_t)(n0 + n) * (p.K >> 5) + kb * kSteps + ks + cg * 16 * mstride;
+#pragma unroll
+                for (int i = 0; i < 16; ++i, out += mstride)
+                  if (cg * 16 + i < p.M) *out = (int)P[i] - kBias - sT[i];
+              }
+            } else {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {  // activation rows 4v .. 4v+3 of the column group
+                const float4 d4 = dp[ks * (NA / 4) + v];
+                const float2 x0 = __ffma2_rn(make_float2(__uint_as_float(P[4 * v]), __uint_as_float(P[4 * v + 1])),
+                                             k110, nbias);
+                const float2 x1 = __ffma2_rn(
+                    make_float2(__uint_as_float(P[4 * v + 2]), __uint_as_float(P[4 * v + 3])), k110, nbias);
+                tsum[2 * v] = __ffma2_rn(make_float2(d4.x, d4.y), x0, tsum[2 * v]);
+                tsum[2 * v + 1] = __ffma2_rn(make_float2(d4.z, d4.w), x1, tsum[2 * v + 1]);
+              }
+            }
+          }
+          if constexpr (!DUMP) {
+            // the block sum less the code-sum correction, times the weight scale
+            const float4* cp = reinterpret_cast<const float4*>(sstage(ss) + kSOffCorr) + cg * 4;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const float4 c4 = cp[v];
+              tsum[2 * v] = __fadd2_rn(tsum[2 * v], make_float2(c4.x, c4.y));
+              tsum[2 * v + 1] = __fadd2_rn(tsum[2 * v + 1], make_float2(c4.z, c4.w));
+            }
+            const float w = reinterpret_cast<const float*>(sstage(ss))[n];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __ffma2_rn(make_float2(w, w), tsum[i], acc[i]);
+          }
+        } else {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(d_free(cs));
+        }
+        if (has) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_empty(ss));
+        }
+      }
+      // End of tile: the column group's per-block sums are added in block order
+      // through shared memory; every epilogue warp reaches each barrier.
+#pragma unroll 1
+      for (int r = 1; r < S::kBlkPerSlot; ++r) {
+#pragma unroll 1
+        for (int c = 0; c < S::kNcg; ++c) {
+          if (blk == r && cg == c) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              stg[(2 * i) * kTileW + n] = acc[i].x;
+              stg[(2 * i + 1) * kTileW + n] = acc[i].y;
+            }
+          }
+          asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+          if (blk == 0 && cg == c) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              acc[i].x += stg[(2 * i) * kTileW + n];
+              acc[i].y += stg[(2 * i + 1) * kTileW + n];
+            }
+          }
+          asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+        }
+      }
+      if (!DUMP && blk == 0 && live && ok && !*abort_flag && n0 + n < p.N) {
+        // a warp's 32 lanes store 32 consecutive floats of one row
+        float* dst = p.y + (int64_t)(cg * 16) * p.ldy + n0 + n;
+        const int mrows = min(16, p.M - cg * 16);
+        const bool add = p.mode == BTF_ADD;
+#pragma unroll
+        for (int i = 0; i < 16; ++i, dst += p.ldy) {
+          const float v = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
+          if (i < mrows) *dst = add ? *dst + v : v;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)kTmemCols)
+                 : "memory");
+  }
+}
+
+template <int NA>
+cudaError_t launch_wm(dim3 grid, cudaStream_t st, const CUtensorMap& mB, const CUtensorMap& mD,
+                      const CUtensorMap& mS, const WmParams& p) {
+  constexpr size_t smem = (size_t)Shape<NA>::kSmemBytes;
+  return p.idot ? launch_pdl(gemm_wm_kernel<NA, true>, grid, dim3(kThreads), smem, st, mB, mD, mS, p)
+                : launch_pdl(gemm_wm_kernel<NA, false>, grid, dim3(kThreads), smem, st, mB, mD, mS, p);
+}
+
+template <int NA>
+cudaError_t set_smem() {
+  cudaError_t e = cudaFuncSetAttribute(gemm_wm_kernel<NA, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Shape<NA>::kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_wm_kernel<NA, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Shape<NA>::kSmemBytes);
+  return e;
+}
+
+}  // namespace
+
+int gemm_wm_setup(DeviceInfo& d) {
+  constexpr int need = std::max(Shape<16>::kSmemBytes, std::max(Shape<32>::kSmemBytes, Shape<64>::kSmemBytes));
+  if (d.optin_smem < need) return fail(BTF_ERR_UNSUPPORTED, "btf_gemm_wm needs %d B of shared memory", need);
+  cudaError_t e = set_smem<16>();
+  if (e == cudaSuccess) e = set_smem<32>();
+  if (e == cudaSuccess) e = set_smem<64>();
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemm_wm_kernel)");
+}
+
+// One matrix, 1 <= M <= kWmMaxM: y[M][ldy] (=|+=) W q with the weight rows on
+// the MMA's 128-row side. idot != nullptr runs the dump form instead.
+int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
+                int32_t* idot) {
+  const DeviceInfo* dev = current_device();
+  if (!dev) return BTF_ERR_STATE;
+  const EncodeFn enc = encode_fn();
+  if (!enc) return fail(BTF_ERR_CUDA, "btf_gemm_wm: cuTensorMapEncodeTiled unavailable");
+  auto encode = [&](CUtensorMap* map, CUtensorMapDataType type, const void* base, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+                    const char* what) -> int {
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, type, 2u, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? BTF_OK : fail(BTF_ERR_ARG, "btf_gemm_wm: %s tensor map encoding failed (%d)", what, (int)r);
+  };
+  const int NA = M <= 16 ? 16 : M <= 32 ? 32 : 64;
+  CUtensorMap mB, mD, mS;
+  {  // activation: int8 [M][K], box 128 columns x NA rows, 128B swizzle; rows beyond M read as zero
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunk, (cuuint32_t)NA};
+    if (int rc = encode(&mB, CU_TENSOR_MAP_DATA_TYPE_UINT8, act.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                        "activation"))
+      return rc;
+  }
+  {  // activation block scales d (fp32) and sums s (int32), [M][K/32] each: box 32 blocks (one slice) x NA
+     // rows, 128B swizzle (a block's 4 values are one 16-byte chunk, spread over the banks by the row);
+     // columns past K and rows past M read as zero
+    const cuuint64_t dims[2] = {(cuuint64_t)(K / 32), (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)(K / 32) * 4};
+    const cuuint32_t box[2] = {32u, (cuuint32_t)NA};
+    if (int rc = encode(&mD, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act.d, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                        "activation scale"))
+      return rc;
+    if (int rc = encode(&mS, CU_TENSOR_MAP_DATA_TYPE_INT32, act.s, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                        "activation sum"))
+      return rc;
+  }
+  WmParams p{};
+  p.N = seg.N;
+  p.M = M;
+  p.K = K;
+  p.ntiles = (seg.N + kTileW - 1) / kTileW;
+  p.nslices = (int)slices_of(K);
+  p.ngroups = (int)groups_of(seg.N);
+  p.panels = static_cast<const uint8_t*>(seg.panels);
+  p.y = seg.y;
+  p.ldy = seg.ldy;
+  p.mode = mode;
+  p.err = dev->err_word;
+  p.idot = idot;
+  const dim3 grid(std::min(p.ntiles, dev->sm_count));
+  const cudaError_t e = NA == 16   ? launch_wm<16>(grid, st, mB, mD, mS, p)
+                        : NA == 32 ? launch_wm<32>(grid, st, mB, mD, mS, p)
+                                   : launch_wm<64>(grid, st, mB, mD, mS, p);
+  return e == cudaSuccess ? launch_status("gemm_wm_kernel") : cuda_fail(e, "gemm_wm_kernel launch");
+}
+
+}  // namespace btf
+
+using namespace btf;
+
+extern "C" int btf_gemm_wm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (M > kWmMaxM) return fail(BTF_ERR_ARG, "btf_gemm_wm: M must be at most %d (M=%d); use btf_gemm", kWmMaxM, M);
+  if (!segs || nseg < 1 || nseg > 3) return fail(BTF_ERR_ARG, "btf_gemm_wm: 1..3 segments (got %d)", nseg);
+  if (mode != BTF_STORE && mode != BTF_ADD) return fail(BTF_ERR_ARG, "btf_gemm_wm: mode must be BTF_STORE or BTF_ADD");
+  if (K <= 0 || K % 128) return fail(BTF_ERR_ARG, "btf_gemm_wm: K must be a positive multiple of 128 (K=%d)", K);
+  if (!act.q || !act.d || !act.s || (reinterpret_cast<uintptr_t>(act.q) & 15) ||
+      (reinterpret_cast<uintptr_t>(act.d) & 15) || (reinterpret_cast<uintptr_t>(act.s) & 15))
+    return fail(BTF_ERR_ARG, "btf_gemm_wm: q, d and s must be 16-byte aligned");
+  for (int i = 0; i < nseg; ++i) {
+    if (!segs[i].panels || (reinterpret_cast<uintptr_t>(segs[i].panels) & 15) || segs[i].N <= 0 || !segs[i].y ||
+        segs[i].ldy < segs[i].N)
+      return fail(BTF_ERR_ARG, "btf_gemm_wm: segment %d has a bad panel buffer, N, y or ldy", i);
+  }
+  for (int i = 0; i < nseg; ++i)
+    if (int rc = run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)) return rc;
+  return BTF_OK;
+}
+
+extern "C" int btf_gemm_wm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot,
+                                void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (M > kWmMaxM || !panels || (reinterpret_cast<uintptr_t>(panels) & 15) || N <= 0 || K <= 0 || K % 128 || !idot ||
+      !act.q || !act.d || !act.s || (reinterpret_cast<uintptr_t>(act.q) & 15) ||
+      (reinterpret_cast<uintptr_t>(act.d) & 15) || (reinterpret_cast<uintptr_t>(act.s) & 15))
+    return fail(BTF_ERR_ARG, "btf_gemm_wm_idot: bad arguments (M <= %d, K %% 128, q, d, s 16-byte aligned)", kWmMaxM);
+  const btf_gemv_seg seg{panels, N, nullptr, N};
+  return run_gemm_wm(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot);
+}

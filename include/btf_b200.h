@@ -171,6 +171,16 @@ int btf_stamp_next(unsigned long long* slot);
  * for large M. q and d must be 16-byte aligned. */
 int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
+/* The GEMM for small batches (1 <= M <= 64), weight-major: the weights are the
+ * tensor core's 128-row operand and the M activation rows (padded to 16, 32 or
+ * 64) its N side, so every weight byte is read once for the whole batch. A
+ * persistent kernel: one CTA per SM walks 128-row weight tiles. Same result
+ * contract and arguments as btf_gemm (store / add modes, 1..3 segments, K a
+ * multiple of 128, q and d 16-byte aligned); M > 64 returns BTF_ERR_ARG. It
+ * replaces the batch-M passes of launch_gemv (src/cuda/kernels.cu:805-821).
+ * btf_gemv and btf_gemm route their small-batch calls here. */
+int btf_gemm_wm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
+
 /* The prefill GEMM from fp32 activations x [M][ldx], allocating nothing. No
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory, such as a plugin whose host engine has reserved the whole
@@ -252,6 +262,9 @@ int btf_gemv_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_
  * accumulator read from tensor memory (P - 4096 of its biased region), the
  * integers the GEMM's epilogue scales; idot[M][N][K/32]. q and d 16-byte aligned. */
 int btf_gemm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
+
+/* The same dump from the weight-major GEMM (btf_gemm_wm), 1 <= M <= 64. */
+int btf_gemm_wm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
 
 /* ---- N-sharded GEMV with the all-gather fused into the epilogue
  * The reference is single-GPU (src/cuda/gpu_decoder.cu); this is the B200
