@@ -62,50 +62,40 @@ constexpr int kChunk = 128;         // K columns per block (one weight-scale blo
 constexpr int kSteps = 4;           // 32-column MMA steps per block
 constexpr int kBlocksPerSliceW = kCols / kChunk;  // 8 blocks per 1024-column panel slice
 constexpr int kGroups = kTileW / kRows;  // 16 panel row groups per tile
-constexpr int kStagesS = 8;         // scale stages (a power of two)
 constexpr int kSlots = 2;           // TMEM slots in flight
 constexpr int kSlotCols = 256;      // TMEM columns per slot
 constexpr int kTmemCols = kSlots * kSlotCols;  // 512: all of TMEM
-constexpr int kEpiWarps = 16;       // 4 lane quarters x 4
-constexpr int kExpWarps = 2;        // expanders (64 threads)
-constexpr int kExpWarp0 = 2, kEpiWarp0 = kExpWarp0 + kExpWarps;
-constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 640: 5 warps per SMSP, 96 registers a thread
+constexpr int kWorkers = 4;         // worker warps (one per SMSP): expand a block, issue its MMAs
+constexpr int kEpiWarp0 = kWorkers;
 constexpr int kBiasA = 4, kBiasB = 64, kBias = 32 * kBiasA * kBiasB;  // every region starts at 8192
 static_assert(kBias == 8192, "the bias is a power of two above 32 * 2 * 127");
-static_assert(kTileW % (kExpWarps * 32) == 0 && kGroups % (kExpWarps * 2) == 0, "expander work divides evenly");
 constexpr uint64_t kWaitNs = 1000000000ull;
 
 // Shared memory, per padded batch width NA:
-//   code ring   (kCodeStages) one 1024-column slice of the tile: the 16 row
+//   code ring   (2 stages) one 1024-column slice of the tile: the 16 row
 //               groups' whole panels (16 x 2176 B, 1-D bulk copies: codes and
 //               fp16 scales), the activation scales d of the slice [NA][32]
-//               fp32 and the activation block sums s [NA][32] int32 (one tiled
-//               copy of NA 128-byte rows each);
+//               fp32 and the activation block sums s [NA][32] int32 (128B
+//               swizzled tiled copies of NA rows each);
 //   A ring      (kAStages) [128][128] int8 codes (trit + 1) of one block
-//               (SW128), written by the expanders;
-//   B ring      (kBStages) [NA][128] int8 activations of one block (SW128, TMA);
-//   scale ring  (8) per block: W fp32 weight scales x 2^39 [128], d [4 steps]
-//               [64] fp32, the code-sum correction -sum_steps d * s * 2^-39 [64]
-//               fp32, and (dump form) s [4 steps][64] int32;
-//   Stg         [16 activation rows][128 weight rows] fp32, the end-of-tile combine.
-// Whole panels keep the number of copy requests per block low: a tiled copy of
-// a block's codes alone was 64 rows of 64 bytes, and the copy unit's request
-// rate, not HBM, then set the pace.
+//               (SW128), block i in stage i % kAStages;
+//   B ring      (kBStages) [NA][128] int8 activations of one block (SW128,
+//               TMA), block i in stage i % kBStages, loaded by the worker of
+//               block i - 4;
+//   scale ring  (kScaleStages) per block: W fp32 weight scales x 2^39 [128],
+//               d [4 steps][NA] fp32, the code-sum correction
+//               -sum_steps d * s * 2^-39 [NA] fp32, and (dump form) s [4][NA];
+//   Stg         [16 activation rows][128 weight rows] fp32, the end-of-tile
+//               combine (NA < 64).
+// Whole panels keep the number of copy requests per block low (a tiled copy of
+// a block's codes alone is 64 rows of 64 bytes).
 constexpr int kABytes = kTileW * kChunk;          // 16 KB
 constexpr int kPanelsBytes = kGroups * kPanelBytes;  // 34816 B
-constexpr int kWBytes = kTileW * 4;               // 512 B
-constexpr int kDTBytes = kSteps * kNAMax * 4;     // 1 KB: d [step][row]
-constexpr int kCorrBytes = kNAMax * 4;            // 256 B
-constexpr int kSTBytes = kSteps * kNAMax * 4;     // 1 KB: s [step][row]
-constexpr int kSOffD = kWBytes, kSOffCorr = kSOffD + kDTBytes, kSOffS = kSOffCorr + kCorrBytes;
-constexpr int kScaleStageBytes = kSOffS + kSTBytes;
+constexpr int kCodeStages = 2;
 constexpr int kStgBytes = 16 * kTileW * 4;        // 8 KB
 // bias operands: K-major, no swizzle, 8-row x 16-byte core matrices; every
 // byte equal, so any core-matrix order reads the same values
-constexpr int kBiasN = kSlotCols;                 // one bias MMA covers a slot
-constexpr int kBiasABytes = kTileW * 32, kBiasBBytes = kBiasN * 32;
-constexpr uint32_t kIdescBias = idesc_i8(kTileW, kBiasN);
-static_assert(kBiasN <= 256 && kBiasN % 16 == 0, "M=128 MMA: N a multiple of 16 up to 256");
+constexpr int kBiasABytes = kTileW * 32, kBiasBBytes = kSlotCols * 32;
 constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
 
 template <int NA>
@@ -113,30 +103,39 @@ struct Shape {
   static_assert(NA == 16 || NA == 32 || NA == 64, "NA is 16, 32 or 64");
   static constexpr int kNcg = NA / 16;             // 16-row column groups per step
   static constexpr int kBlkPerSlot = 4 / kNcg;     // blocks per TMEM slot
+  // epilogue warps: 4 lane quarters x 4 at NA = 64; x 2 below, each warp then
+  // reading 2 blocks (NA = 16) or both column groups' blocks (NA = 32) of a slot
+  static constexpr int kEpiWarps = NA == 64 ? 16 : 8;
+  static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 640 (96 registers) or 384 (168)
   static constexpr uint32_t kIdesc = idesc_i8(kTileW, NA);
+  static constexpr uint32_t kIdescBias = idesc_i8(kTileW, kSteps * NA);  // a block's 4 regions
   static_assert(kBlkPerSlot * kSteps * NA == kSlotCols, "a slot is whole blocks");
   // ring depths: what fits 227 KB for this width
-  static constexpr int kCodeStages = NA == 16 ? 3 : 2;
-  static constexpr int kAStages = NA == 32 ? 4 : 3;
-  static constexpr int kBStages = NA == 64 ? 4 : 6;
+  static constexpr int kAStages = NA == 16 ? 6 : NA == 32 ? 4 : 3;
+  static constexpr int kBStages = NA == 64 ? 6 : 8;
+  static constexpr int kScaleStages = NA == 64 ? 4 : 8;  // a power of two
   static constexpr int kBBytes = NA * kChunk;
   static constexpr int kDSliceBytes = NA * 32 * 4;  // d (and s) of one slice: [NA][32]
   static constexpr int kCodeStageBytes = kPanelsBytes + 2 * kDSliceBytes;
+  // scale stage
+  static constexpr int kSOffD = kTileW * 4, kSOffCorr = kSOffD + kSteps * NA * 4, kSOffS = kSOffCorr + NA * 4;
+  static constexpr int kScaleStageBytes = kSOffS + kSteps * NA * 4;
   static constexpr int kOffCode = 0;
   static constexpr int kOffA = align1k(kOffCode + kCodeStages * kCodeStageBytes);
   static constexpr int kOffB = kOffA + kAStages * kABytes;
   static constexpr int kOffS = kOffB + kBStages * kBBytes;
-  static constexpr int kOffStg = kOffS + kStagesS * kScaleStageBytes;
-  static constexpr int kOffBiasA = align1k(kOffStg + kStgBytes);
+  static constexpr int kOffStg = kOffS + kScaleStages * kScaleStageBytes;
+  static constexpr int kOffBiasA = align1k(kOffStg + (NA < 64 ? kStgBytes : 0));
   static constexpr int kOffBiasB = kOffBiasA + kBiasABytes;
   static constexpr int kOffBar = kOffBiasB + kBiasBBytes;
-  // c_full; a_full, a_empty; b_full, b_empty; s_full, s_empty; mma_done, d_free; final; x_done
-  static constexpr int kNumBars = 2 * kCodeStages + 2 * kAStages + 2 * kBStages + 2 * kStagesS + 2 * kSlots + 1;
-  static constexpr int kOffFlags = kOffBar + kNumBars * 8;  // TMEM base (4 B), abort flag (4 B)
-  static constexpr int kSmemBytes = kOffFlags + 16 + 1024;   // + slack for 1024-B alignment
+  // c_full; a_empty; b_full, b_empty; s_full, s_empty; mma_done, d_free; final
+  static constexpr int kNumBars = kCodeStages + kAStages + 2 * kBStages + 2 * kScaleStages + 2 * kSlots + 1;
+  // TMEM base (4 B), abort flag (4 B), slice counters (4 B each)
+  static constexpr int kOffFlags = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffFlags + 16 + 4 * (kCodeStages + 1) + 1024;  // + slack for 1024-B alignment
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(kCodeStageBytes % 1024 == 0 && kBBytes % 1024 == 0 && kOffB % 1024 == 0, "SW128 / copy alignment");
-  static_assert(kOffS % 16 == 0 && kOffStg % 16 == 0, "vector accesses aligned");
+  static_assert(kOffS % 16 == 0 && kOffStg % 16 == 0 && kScaleStageBytes % 16 == 0, "vector accesses aligned");
 };
 
 struct WmParams {
@@ -158,73 +157,71 @@ struct WmParams {
 // DUMP (parity/debug): the kernel writes every step's integer accumulator
 // P - kBias (= idot) to p.idot and stores no y.
 template <int NA, bool DUMP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
     gemm_wm_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
                    const __grid_constant__ CUtensorMap tmS, const WmParams p) {
   using S = Shape<NA>;
-  constexpr int CS = S::kCodeStages, AS = S::kAStages, BS = S::kBStages;
+  constexpr int CS = kCodeStages, AS = S::kAStages, BS = S::kBStages, SS = S::kScaleStages;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base (SW128 atoms and TMA destinations)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nb = p.K / kChunk;                                   // blocks per tile
+  const int nb = p.K / kChunk;                                     // blocks per tile
   const int nsl = (nb + kBlocksPerSliceW - 1) / kBlocksPerSliceW;  // slices per tile
+  const int nslots = (nb + S::kBlkPerSlot - 1) / S::kBlkPerSlot;   // TMEM slot uses per tile
   // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ... (the grid is at most ntiles)
   const int my_tiles = ((int)blockIdx.x < p.ntiles) ? (p.ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
   const uint32_t bar0 = sbase + S::kOffBar;
   auto c_full = [&](int q) { return bar0 + q * 8; };                          // copies: slice stage q landed
-  auto a_full = [&](int s) { return bar0 + (CS + s) * 8; };                   // expanders: A[s] written
-  auto a_empty = [&](int s) { return bar0 + (CS + AS + s) * 8; };             // MMA commit: A[s] read
-  auto b_full = [&](int s) { return bar0 + (CS + 2 * AS + s) * 8; };          // TMA: B[s] landed
-  auto b_empty = [&](int s) { return bar0 + (CS + 2 * AS + BS + s) * 8; };    // MMA commit: B[s] read
-  constexpr int kB1 = CS + 2 * AS + 2 * BS;
-  auto s_full = [&](int s) { return bar0 + (kB1 + s) * 8; };                  // expanders: scale stage ready
-  auto s_empty = [&](int s) { return bar0 + (kB1 + kStagesS + s) * 8; };      // epilogue: stage read
-  auto mma_done = [&](int cs) { return bar0 + (kB1 + 2 * kStagesS + cs) * 8; };
-  auto d_free = [&](int cs) { return bar0 + (kB1 + 2 * kStagesS + kSlots + cs) * 8; };
-  const uint32_t final_bar = bar0 + (kB1 + 2 * kStagesS + 2 * kSlots) * 8;
-  auto x_done = [&](int q) { return bar0 + (kB1 + 2 * kStagesS + 2 * kSlots + 1 + q) * 8; };  // expanders: slice q read
+  auto a_empty = [&](int s) { return bar0 + (CS + s) * 8; };                  // MMA commit: A[s] read
+  auto b_full = [&](int s) { return bar0 + (CS + AS + s) * 8; };              // TMA: B[s] landed
+  auto b_empty = [&](int s) { return bar0 + (CS + AS + BS + s) * 8; };        // MMA commit: B[s] read
+  constexpr int kB1 = CS + AS + 2 * BS;
+  auto s_full = [&](int s) { return bar0 + (kB1 + s) * 8; };                  // worker: scale stage ready
+  auto s_empty = [&](int s) { return bar0 + (kB1 + SS + s) * 8; };            // epilogue: stage read
+  auto mma_done = [&](int cs) { return bar0 + (kB1 + 2 * SS + cs) * 8; };     // MMA commits: slot written
+  auto d_free = [&](int cs) { return bar0 + (kB1 + 2 * SS + kSlots + cs) * 8; };  // epilogue: slot read
+  const uint32_t final_bar = bar0 + (kB1 + 2 * SS + 2 * kSlots) * 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffFlags);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kOffFlags + 8);
-  // scale stage ss: Dblk, W, P, F
-  auto sstage = [&](int ss) { return smem + S::kOffS + ss * kScaleStageBytes; };
+  int* slice_cnt = reinterpret_cast<int*>(smem + S::kOffFlags + 16);  // blocks of slice stage q expanded
+  // scale stage ss: W, d [step][row], correction, s [step][row]
+  auto sstage = [&](int ss) { return smem + S::kOffS + ss * S::kScaleStageBytes; };
 
   if (threadIdx.x == 0) {
     for (int q = 0; q < CS; ++q) {
       mbar_init(c_full(q), 1);
-      mbar_init(x_done(q), kExpWarps);
+      slice_cnt[q] = 0;
     }
-    for (int s = 0; s < AS; ++s) {
-      mbar_init(a_full(s), kExpWarps);
-      mbar_init(a_empty(s), 1);
-    }
+    slice_cnt[CS] = 0;  // slices issued
+    for (int s = 0; s < AS; ++s) mbar_init(a_empty(s), 1);
     for (int s = 0; s < BS; ++s) {
       mbar_init(b_full(s), 1);
       mbar_init(b_empty(s), 1);
     }
-    for (int s = 0; s < kStagesS; ++s) {
-      mbar_init(s_full(s), kExpWarps);
+    for (int s = 0; s < SS; ++s) {
+      mbar_init(s_full(s), 1);
       mbar_init(s_empty(s), 4 * S::kNcg);  // the warps that read one block: 4 lane quarters x column groups
     }
     for (int r = 0; r < kSlots; ++r) {
-      mbar_init(mma_done(r), 1);
-      mbar_init(d_free(r), kEpiWarps);
+      mbar_init(mma_done(r), S::kBlkPerSlot);  // one commit per block of the slot
+      mbar_init(d_free(r), S::kEpiWarps);
     }
-    mbar_init(final_bar, 1);
+    mbar_init(final_bar, kWorkers);
     *abort_flag = 0;
     fence_mbar_init();
   }
   {  // the bias MMA's constant operand tiles
     const uint32_t va = 0x01010101u * kBiasA, vb = 0x01010101u * kBiasB;
-    for (int i = threadIdx.x; i < (kBiasABytes + kBiasBBytes) / 16; i += kThreads) {
+    for (int i = threadIdx.x; i < (kBiasABytes + kBiasBBytes) / 16; i += S::kThreads) {
       const uint32_t v = i < kBiasABytes / 16 ? va : vb;
       reinterpret_cast<uint4*>(smem + S::kOffBiasA)[i] = make_uint4(v, v, v, v);
     }
     fence_proxy_async_smem();  // generic writes -> visible to the tensor core (async proxy)
   }
-  if (warp == 1) {  // TMEM: all 512 columns (2 slots x 256) for this CTA
+  if (warp == 0) {  // TMEM: all 512 columns (2 slots x 256) for this CTA
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"((uint32_t)kTmemCols)
                  : "memory");
@@ -246,95 +243,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   // the same wait made warp-uniform: every lane waits, the warp goes on only if all of them saw the phase
   auto wwait = [&](uint32_t bar, uint32_t parity) -> bool { return __all_sync(0xffffffffu, wait(bar, parity)); };
+  // a warp-uniform wait that sleeps between tries (about 100 ns), for the
+  // epilogue's long waits: a spinning warp would take issue slots from the
+  // worker warp on its SM sub-partition
+  auto wwait_sleep = [&](uint32_t bar, uint32_t parity) -> bool {
+    bool done = mbar_try_wait(bar, parity);
+    if (!__all_sync(0xffffffffu, done)) {
+      const uint64_t t0 = globaltimer_ns();
+      for (;;) {
+        __nanosleep(100);
+        done = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, done)) break;
+        if (*abort_flag || globaltimer_ns() - t0 > kWaitNs) {
+          atomicCAS(p.err, 0, kErrWaitTimeout);
+          *abort_flag = 1;
+          return false;
+        }
+      }
+    }
+    return true;
+  };
 
   pdl_launch_dependents();
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer: activation tiles
-    if (lane == 0) {
-      int issued = 0;  // blocks whose activation copy was issued
-      pdl_wait();      // the activation is written by the previous kernel
-      int s = 0, it = 0;
-      uint32_t ph = 0;
-      bool stop = false;
-      for (int ti = 0; ti < my_tiles && !stop; ++ti) {
-        for (int kb = 0; kb < nb; ++kb, ++it) {
-          if (it >= BS && !wait(b_empty(s), ph ^ 1u)) {
-            stop = true;
-            break;
-          }
-          mbar_expect_tx(b_full(s), S::kBBytes);
-          tma_load_2d(sbase + S::kOffB + s * S::kBBytes, &tmB, kb * kChunk, 0, b_full(s));
-          issued = it + 1;
-          if (++s == BS) s = 0, ph ^= 1u;
-        }
-      }
-      if (*abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
-        for (int c = max(0, issued - BS); c < issued; ++c)
-          mbar_wait_bounded(b_full(c % BS), (uint32_t)((c / BS) & 1), kWaitNs / 10);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint64_t bias_ad = smem_desc_noswz(sbase + S::kOffBiasA), bias_bd = smem_desc_noswz(sbase + S::kOffBiasB);
-      const uint64_t a_desc0 = smem_desc_sw128(sbase + S::kOffA), b_desc0 = smem_desc_sw128(sbase + S::kOffB);
-      int sa = 0, sb = 0, u = 0;  // A stage, B stage; TMEM slot uses so far
-      uint32_t pha = 0, phb = 0;
-      bool stop = false;
-      for (int ti = 0; ti < my_tiles && !stop; ++ti) {
-        for (int kb = 0; kb < nb; ++kb) {
-          if (!wait(a_full(sa), pha) || !wait(b_full(sb), phb)) {
-            stop = true;
-            break;
-          }
-          const int pos = kb % S::kBlkPerSlot, cs = u & 1;
-          const uint32_t dt = tmem_base + cs * kSlotCols;
-          if (pos == 0) {
-            if (u >= kSlots && !wait(d_free(cs), (uint32_t)(((u >> 1) - 1) & 1))) {
-              stop = true;
-              break;
-            }
-            tc_fence_after();
-            mma_i8<kIdescBias>(dt, bias_ad, bias_bd, 0u);  // the slot's regions = kBias
-          } else {
-            tc_fence_after();
-          }
-          const uint64_t ad = a_desc0 + (uint64_t)((sa * kABytes) >> 4);
-          const uint64_t bd = b_desc0 + (uint64_t)((sb * S::kBBytes) >> 4);
-#pragma unroll
-          for (int ks = 0; ks < kSteps; ++ks)
-            mma_i8<S::kIdesc>(dt + (pos * kSteps + ks) * NA, ad + (ks * 32 >> 4), bd + (ks * 32 >> 4), 1u);
-          mma_commit(a_empty(sa));  // A and B of this block are free once its MMAs finish
-          mma_commit(b_empty(sb));
-          if (pos == S::kBlkPerSlot - 1 || kb == nb - 1) {
-            mma_commit(mma_done(cs));  // the slot's MMAs (commits track all prior MMAs)
-            ++u;
-          }
-          if (++sa == AS) sa = 0, pha ^= 1u;
-          if (++sb == BS) sb = 0, phb ^= 1u;
-        }
-      }
-      mma_commit(final_bar);  // completes when every MMA issued above has finished
-      mbar_wait_bounded(final_bar, 0, kWaitNs);
-    }
-  } else if (warp < kEpiWarp0) {
-    // ------------------------------------------------------------ code expanders
-    // Thread e expands quad h of row groups gi, gi + GS, ... (GS = expander
-    // threads / 16) x 16 columns (sub-block t/2, half t&1) of every block: the
-    // 16-byte quad words at panel(group) + h*1024 + (t&1)*512 + block*64 +
-    // (t/2)*16 of the slice stage, into the int8 codes (trit + 1: 0, 1, 2) of
-    // the K-major SW128 A tile. It converts the fp16 scales of tile rows e,
-    // e + E, ... (E = expander threads), and thread e < NA writes activation
-    // row e's d per step and its code-sum correction. Expander thread 0 also
-    // issues the slice copies, kCodeStages slices ahead of the slice being
-    // expanded.
-    constexpr int E = kExpWarps * 32, GS = E / 16;
-    static_assert(NA <= E, "one expander thread per activation row");
-    const int e = threadIdx.x - kExpWarp0 * 32;
-    const int t = e & 7, h = (e >> 3) & 1, gi = e >> 4;
+  if (warp < kWorkers) {
+    // ------------------------------------------------------------ workers
+    // Worker w takes the CTA's blocks w, w + 4, ... (over all its tiles). For
+    // each: the 2-bit codes of the block become int8 codes (trit + 1) of the
+    // K-major SW128 A tile (lane: quad h of row groups gi, gi + 2, ... x 16
+    // columns, sub-block t/2, half t&1 of the panel), the scale stage gets the
+    // fp32 weight scales, d per step and the code-sum correction, and lane 0
+    // issues the block's MMAs: a bias MMA over its 4 regions, then 4 steps.
+    // Lane 0 also loads the activation tile of the warp's next block (once the
+    // stage's previous block, kBStages back, has been read by its MMAs), and
+    // the worker that expands the last block of a slice reloads its stage with
+    // the slice kCodeStages ahead.
+    const int w = warp;
+    const int t = lane & 7, h = (lane >> 3) & 1, gi = lane >> 4;
     const int coff = h * 1024 + (t & 1) * 512 + (t >> 1) * 16;
-    const int total_sl = my_tiles * nsl;  // slices this CTA walks, over all its tiles
-    // one slice into stage gsl % CS: the tile's whole panels of the slice and its activation scales
+    const int total_sl = my_tiles * nsl, total_blk = my_tiles * nb;
+    int* slices_issued = slice_cnt + CS;  // slices whose copies were issued (for the abort drain)
+    // one slice into stage gsl % CS: the tile's whole panels of the slice and its d and s
     auto issue_slice = [&](int gsl) {
       const int ti = gsl / nsl, sl = gsl % nsl, q = gsl % CS;
       const int g0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kGroups;
@@ -346,118 +295,158 @@ __global__ void __launch_bounds__(kThreads, 1)
                  kPanelBytes, c_full(q));
       tma_load_2d(smem_u32(dst + kPanelsBytes), &tmD, sl * 32, 0, c_full(q));
       tma_load_2d(smem_u32(dst + kPanelsBytes + S::kDSliceBytes), &tmS, sl * 32, 0, c_full(q));
+      *slices_issued = gsl + 1;
     };
-    int nissued = 0;
-    if (e == 0) {
-      pdl_wait();  // the activation scales are written by the previous kernel
-      for (; nissued < min(CS, total_sl); ++nissued) issue_slice(nissued);
+    // the activation tile of CTA block j into B stage j % BS
+    auto issue_b = [&](int j) {
+      const int bs = j % BS;
+      mbar_expect_tx(b_full(bs), S::kBBytes);
+      tma_load_2d(sbase + S::kOffB + bs * S::kBBytes, &tmB, (j % nb) * kChunk, 0, b_full(bs));
+    };
+    const int my_blocks = total_blk > w ? (total_blk - 1 - w) / kWorkers + 1 : 0;
+    int b_issued = 0;  // this warp's blocks whose activation copy was issued (lane 0)
+    if (lane == 0) {
+      pdl_wait();  // the activation, its scales and sums are written by the previous kernel
+      if (w == 0)
+        for (int g = 0; g < min(CS, total_sl); ++g) issue_slice(g);
+      if (my_blocks > 0) issue_b(w), b_issued = 1;
     }
-    int sa = 0, ss = 0, it = 0, q = 0;
-    uint32_t pha = 0, phs = 0, phc = 0;
-    bool stop = false;
-    for (int ti = 0; ti < my_tiles && !stop; ++ti) {
-      for (int kb = 0; kb < nb; ++kb, ++it) {
-        const int b = kb & (kBlocksPerSliceW - 1);
-        if (b == 0 && !wwait(c_full(q), phc)) {
-          stop = true;
-          break;
-        }
-        // A[sa] is free once the MMAs of block it - AS have read it
-        if (it >= AS && !wwait(a_empty(sa), pha ^ 1u)) {
-          stop = true;
-          break;
-        }
-        const uint8_t* cst = smem + S::kOffCode + q * S::kCodeStageBytes;
-        uint8_t* as = smem + S::kOffA + sa * kABytes;
+    int last_gsl = -1;
+    bool ok = true;
+    for (int k = 0; k < my_blocks && ok; ++k) {
+      const int j = w + k * kWorkers, ti = j / nb, kb = j % nb;
+      const int gsl = ti * nsl + (kb >> 3), q = gsl % CS, b = kb & (kBlocksPerSliceW - 1);
+      if (gsl != last_gsl) {
+        if (!wwait(c_full(q), (uint32_t)((gsl / CS) & 1))) break;
+        last_gsl = gsl;
+      }
+      const int sa = j % AS;
+      if (j >= AS && !wwait(a_empty(sa), (uint32_t)(((j / AS) - 1) & 1))) break;
+      const uint8_t* cst = smem + S::kOffCode + q * S::kCodeStageBytes;
+      uint8_t* as = smem + S::kOffA + sa * kABytes;
 #pragma unroll
-        for (int r = 0; r < kGroups / GS; ++r) {
-          const int g = gi + GS * r;
-          const uint4 w = *reinterpret_cast<const uint4*>(cst + g * kPanelBytes + coff + b * 64);
+      for (int r = 0; r < kGroups / 2; ++r) {
+        const int g = gi + 2 * r;
+        const uint4 c4 = *reinterpret_cast<const uint4*>(cst + g * kPanelBytes + coff + b * 64);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int n = g * 8 + h * 4 + k;  // row of the tile
-            const uint4 o = make_uint4((w.x >> (2 * k)) & 0x03030303u, (w.y >> (2 * k)) & 0x03030303u,
-                                       (w.z >> (2 * k)) & 0x03030303u, (w.w >> (2 * k)) & 0x03030303u);
-            const int off = (n >> 3) * 1024 + (n & 7) * 128 + ((t ^ (n & 7)) << 4);
-            *reinterpret_cast<uint4*>(as + off) = o;
-          }
-        }
-        fence_proxy_async_smem();  // generic writes of A -> visible to the tensor core (async proxy)
-        uint16_t hb[kTileW / E];
-#pragma unroll
-        for (int r = 0; r < kTileW / E; ++r) {
-          const int row = e + r * E;  // fp16 scale of tile row `row` for this block: [block][row in group]
-          hb[r] = *reinterpret_cast<const uint16_t*>(cst + (row >> 3) * kPanelBytes + kCodeBytes + b * 16 + (row & 7) * 2);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(a_full(sa));
-        // scale stage: after the epilogue has released it
-        if (it >= kStagesS && !wwait(s_empty(ss), phs ^ 1u)) {
-          stop = true;
-          break;
-        }
-        uint8_t* sst = sstage(ss);
-#pragma unroll
-        for (int r = 0; r < kTileW / E; ++r)
-          reinterpret_cast<float*>(sst)[e + r * E] = __half2float(__ushort_as_half(hb[r])) * 0x1p39f;
-        if (e < NA) {
-          // row e's d and s of this block: 16-byte chunk b of its 128-byte slice
-          // row, which the 128B-swizzled copy placed at chunk b ^ (e & 7)
-          const int off = e * 128 + ((b ^ (e & 7)) << 4);
-          const float4 d4 = *reinterpret_cast<const float4*>(cst + kPanelsBytes + off);
-          const int4 s4 = *reinterpret_cast<const int4*>(cst + kPanelsBytes + S::kDSliceBytes + off);
-          float* dT = reinterpret_cast<float*>(sst + kSOffD);  // [step][row]
-          dT[0 * NA + e] = d4.x;
-          dT[1 * NA + e] = d4.y;
-          dT[2 * NA + e] = d4.z;
-          dT[3 * NA + e] = d4.w;
-          // the codes are trit + 1, so the MMA adds s = sum q of each step:
-          // correction -sum_steps d * s * 2^-39 for the epilogue's block sum
-          float c = fmaf(d4.x * -0x1p-39f, (float)s4.x, 0.f);
-          c = fmaf(d4.y * -0x1p-39f, (float)s4.y, c);
-          c = fmaf(d4.z * -0x1p-39f, (float)s4.z, c);
-          c = fmaf(d4.w * -0x1p-39f, (float)s4.w, c);
-          reinterpret_cast<float*>(sst + kSOffCorr)[e] = c;
-          if constexpr (DUMP) {
-            int* sT = reinterpret_cast<int*>(sst + kSOffS);
-            sT[0 * NA + e] = s4.x;
-            sT[1 * NA + e] = s4.y;
-            sT[2 * NA + e] = s4.z;
-            sT[3 * NA + e] = s4.w;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(s_full(ss));
-        if (++sa == AS) sa = 0, pha ^= 1u;
-        if (++ss == kStagesS) ss = 0, phs ^= 1u;
-        if (b == kBlocksPerSliceW - 1 || kb == nb - 1) {
-          // the slice is expanded: once both expander warps are past it, its
-          // stage takes the slice CS ahead
-          __syncwarp();
-          if (lane == 0) mbar_arrive(x_done(q));
-          if (e == 0 && nissued < total_sl) {
-            if (wait(x_done(q), phc)) {
-              issue_slice(nissued);
-              ++nissued;
-            }
-          }
-          if (++q == CS) q = 0, phc ^= 1u;
+        for (int kk = 0; kk < 4; ++kk) {
+          const int n = g * 8 + h * 4 + kk;  // row of the tile
+          const uint4 o = make_uint4((c4.x >> (2 * kk)) & 0x03030303u, (c4.y >> (2 * kk)) & 0x03030303u,
+                                     (c4.z >> (2 * kk)) & 0x03030303u, (c4.w >> (2 * kk)) & 0x03030303u);
+          *reinterpret_cast<uint4*>(as + (n >> 3) * 1024 + (n & 7) * 128 + ((t ^ (n & 7)) << 4)) = o;
         }
       }
+      fence_proxy_async_smem();  // generic writes of A -> visible to the tensor core (async proxy)
+      // scale stage of block j: after the epilogue has released block j - SS's
+      const int ss = j & (SS - 1);
+      if (j >= SS && !wwait(s_empty(ss), (uint32_t)(((j / SS) - 1) & 1))) break;
+      uint8_t* sst = sstage(ss);
+#pragma unroll
+      for (int r = 0; r < kTileW / 32; ++r) {
+        const int row = lane + 32 * r;  // fp16 scale of tile row `row` for this block: [block][row in group]
+        const uint16_t hb =
+            *reinterpret_cast<const uint16_t*>(cst + (row >> 3) * kPanelBytes + kCodeBytes + b * 16 + (row & 7) * 2);
+        reinterpret_cast<float*>(sst)[row] = __half2float(__ushort_as_half(hb)) * 0x1p39f;
+      }
+#pragma unroll
+      for (int m = lane; m < NA; m += 32) {
+        // row m's d and s of this block: 16-byte chunk b of its 128-byte slice
+        // row, which the 128B-swizzled copy placed at chunk b ^ (m & 7)
+        const int off = m * 128 + ((b ^ (m & 7)) << 4);
+        const float4 d4 = *reinterpret_cast<const float4*>(cst + kPanelsBytes + off);
+        const int4 s4 = *reinterpret_cast<const int4*>(cst + kPanelsBytes + S::kDSliceBytes + off);
+        float* dT = reinterpret_cast<float*>(sst + S::kSOffD);  // [step][row]
+        dT[0 * NA + m] = d4.x;
+        dT[1 * NA + m] = d4.y;
+        dT[2 * NA + m] = d4.z;
+        dT[3 * NA + m] = d4.w;
+        // the codes are trit + 1, so each step's MMA adds s = sum q of the
+        // step: correction -sum_steps d * s * 2^-39 for the epilogue's block sum
+        float c = fmaf(d4.x * -0x1p-39f, (float)s4.x, 0.f);
+        c = fmaf(d4.y * -0x1p-39f, (float)s4.y, c);
+        c = fmaf(d4.z * -0x1p-39f, (float)s4.z, c);
+        c = fmaf(d4.w * -0x1p-39f, (float)s4.w, c);
+        reinterpret_cast<float*>(sst + S::kSOffCorr)[m] = c;
+        if constexpr (DUMP) {
+          int* sT = reinterpret_cast<int*>(sst + S::kSOffS);
+          sT[0 * NA + m] = s4.x;
+          sT[1 * NA + m] = s4.y;
+          sT[2 * NA + m] = s4.z;
+          sT[3 * NA + m] = s4.w;
+        }
+      }
+      __syncwarp();
+      int lok = 1;
+      if (lane == 0) {
+        mbar_arrive(s_full(ss));
+        // this warp is done with the slice stage for block j; the last of the
+        // slice's blocks reloads the stage
+        const int in_slice = min(kBlocksPerSliceW, nb - (kb & ~(kBlocksPerSliceW - 1)));
+        __threadfence_block();  // this warp's reads of the stage come before its count
+        if (atomicAdd(&slice_cnt[q], 1) + 1 == in_slice) {
+          slice_cnt[q] = 0;
+          if (gsl + CS < total_sl) {
+            fence_proxy_async_smem();  // the generic reads of the stage before the copies that overwrite it
+            issue_slice(gsl + CS);
+          }
+        }
+        // the activation of this warp's next block j + 4: its stage's previous
+        // block j + 4 - BS was issued well before this block's MMAs
+        if (b_issued == k + 1 && b_issued < my_blocks) {
+          const int jn = j + kWorkers;
+          if (jn < BS || wait(b_empty(jn % BS), (uint32_t)((jn / BS - 1) & 1))) {
+            issue_b(jn);
+            ++b_issued;
+          }
+        }
+        // the block's MMAs, once its activation has landed and its slot is free
+        const int bs = j % BS;
+        const int pos = kb % S::kBlkPerSlot, u = ti * nslots + kb / S::kBlkPerSlot, cs = u & 1;
+        lok = wait(b_full(bs), (uint32_t)((j / BS) & 1));
+        if (lok && u >= kSlots) lok = wait(d_free(cs), (uint32_t)(((u >> 1) - 1) & 1));
+        if (lok) {
+          tc_fence_after();
+          const uint32_t dt = tmem_base + cs * kSlotCols + pos * kSteps * NA;
+          // the block's 4 regions = kBias
+          mma_i8<S::kIdescBias>(dt, smem_desc_noswz(sbase + S::kOffBiasA), smem_desc_noswz(sbase + S::kOffBiasB), 0u);
+          const uint64_t ad = smem_desc_sw128(sbase + S::kOffA + sa * kABytes);
+          const uint64_t bd = smem_desc_sw128(sbase + S::kOffB + bs * S::kBBytes);
+#pragma unroll
+          for (int ks = 0; ks < kSteps; ++ks)
+            mma_i8<S::kIdesc>(dt + ks * NA, ad + (ks * 32 >> 4), bd + (ks * 32 >> 4), 1u);
+          mma_commit(a_empty(sa));  // A and B of this block are free once its MMAs finish
+          mma_commit(b_empty(bs));
+          // one commit per block of the slot; the last block of a partial slot also commits for the missing ones
+          const int reps = kb == nb - 1 ? S::kBlkPerSlot - pos : 1;
+          for (int r = 0; r < reps; ++r) mma_commit(mma_done(cs));
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, lok, 0) != 0;
     }
-    if (e == 0 && *abort_flag)  // leave no copy in flight into this CTA's shared memory (bounded)
-      for (int c = max(0, nissued - CS); c < nissued; ++c)
-        mbar_wait_bounded(c_full(c % CS), (uint32_t)((c / CS) & 1), kWaitNs / 10);
+    if (lane == 0) {
+      mma_commit(final_bar);  // completes (with the other workers') when every MMA issued above has finished
+      mbar_wait_bounded(final_bar, 0, kWaitNs);
+      if (*abort_flag) {  // leave no copy in flight into this CTA's shared memory (bounded)
+        for (int c = max(0, b_issued - 2); c < b_issued; ++c) {
+          const int jc = w + c * kWorkers;
+          mbar_wait_bounded(b_full(jc % BS), (uint32_t)((jc / BS) & 1), kWaitNs / 10);
+        }
+        if (w == 0)
+          for (int c = max(0, *slices_issued - CS); c < *slices_issued; ++c)
+            mbar_wait_bounded(c_full(c % CS), (uint32_t)((c / CS) & 1), kWaitNs / 10);
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     // Warp (q, j): TMEM lanes q*32.. (weight rows), column group cg of every
-    // step (16 activation rows), block blk of every slot.
+    // step (16 activation rows), blocks blk0, blk0 + kBlkStep, ... of every
+    // slot (their sums collect in the same accumulators).
+    constexpr int kBlkStep = (S::kEpiWarps / 4) / S::kNcg;  // warps of one (quarter, column group)
     const int we = warp - kEpiWarp0;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int cg = (we >> 2) % S::kNcg, blk = (we >> 2) / S::kNcg;
-    const int n = q * 32 + lane;        // weight row of the tile
-    const bool live = cg * 16 < p.M;    // some of this warp's activation rows exist
-    const int nslots = (nb + S::kBlkPerSlot - 1) / S::kBlkPerSlot;
+    const int cg = (we >> 2) % S::kNcg, blk0 = (we >> 2) / S::kNcg;
+    const int n = q * 32 + lane;      // weight row of the tile
+    const bool live = cg * 16 < p.M;  // some of this warp's activation rows exist
     float* stg = reinterpret_cast<float*>(smem + S::kOffStg);
     // x = fma(P * 2^-149, 2^110, -2^-26) = (P - 8192) * 2^-39 exactly: P's bits
     // read as fp32 are the denormal P * 2^-149, the product is exact and so is
@@ -472,101 +461,101 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
       for (int su = 0; su < nslots; ++su, ++u) {
-        const int cs = u & 1, kb = su * S::kBlkPerSlot + blk;
-        const bool has = kb < nb;  // the last slot of a tile may hold fewer blocks
-        const int gb = git + kb, ss = gb & (kStagesS - 1);
-        if (ok) ok = wwait(mma_done(cs), (uint32_t)(u >> 1) & 1u);
-        if (ok && has) ok = wwait(s_full(ss), (uint32_t)(gb / kStagesS) & 1u);
-        if (!ok) continue;
-        if (has && live) {
-          tc_fence_after();
-          const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + cs * kSlotCols + blk * kSteps * NA + cg * 16;
-          const float4* dp = reinterpret_cast<const float4*>(sstage(ss) + kSOffD) + cg * 4;  // d [step][row]
-          uint32_t buf[2][16];
-          float2 tsum[8];
+        const int cs = u & 1;
+        if (ok) ok = wwait_sleep(mma_done(cs), (uint32_t)(u >> 1) & 1u);
+        tc_fence_after();
+#pragma unroll 1
+        for (int blk = blk0; blk < S::kBlkPerSlot && ok; blk += kBlkStep) {
+          const int kb = su * S::kBlkPerSlot + blk;
+          if (kb >= nb) break;  // the last slot of a tile may hold fewer blocks
+          const int gb = git + kb, ss = gb & (SS - 1);
+          if (!wwait(s_full(ss), (uint32_t)(gb / SS) & 1u)) {
+            ok = false;
+            break;
+          }
+          if (live) {
+            const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16) + cs * kSlotCols + blk * kSteps * NA + cg * 16;
+            const float4* dp = reinterpret_cast<const float4*>(sstage(ss) + S::kSOffD) + cg * 4;  // d [step][row]
+            uint32_t buf[2][16];
+            float2 tsum[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) tsum[i] = make_float2(0.f, 0.f);
-          tmem_ld16_async(tl, buf[0]);
+            for (int i = 0; i < 8; ++i) tsum[i] = make_float2(0.f, 0.f);
+            tmem_ld16_async(tl, buf[0]);
 #pragma unroll
-          for (int ks = 0; ks < kSteps; ++ks) {
-            tmem_wait16(buf[ks & 1]);
-            if (ks + 1 < kSteps) {
-              tmem_ld16_async(tl + (ks + 1) * NA, buf[(ks + 1) & 1]);  // in flight during this step's math
-            } else {  // the block is in registers: this warp's reads of the slot are done
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(d_free(cs));
+            for (int ks = 0; ks < kSteps; ++ks) {
+              tmem_wait16(buf[ks & 1]);
+              if (ks + 1 < kSteps) tmem_ld16_async(tl + (ks + 1) * NA, buf[(ks + 1) & 1]);  // in flight during the math
+              const uint32_t* P = buf[ks & 1];
+              if constexpr (DUMP) {  // integer accumulators only: idot = P - kBias - s, no y
+                if (n0 + n < p.N) {
+                  const int* sT = reinterpret_cast<const int*>(sstage(ss) + S::kSOffS) + ks * NA + cg * 16;
+                  const int64_t mstride = (int64_t)p.N * (p.K >> 5);
+                  int32_t* out = p.idot + (int64_t)(n0 + n) * (p.K >> 5) + kb * kSteps + ks + cg * 16 * mstride;
+#pragma unroll
+                  for (int i = 0; i < 16; ++i, out += mstride)
+                    if (cg * 16 + i < p.M) *out = (int)P[i] - kBias - sT[i];
+                }
+              } else {
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {  // activation rows 4v .. 4v+3 of the column group
+                  const float4 d4 = dp[ks * (NA / 4) + v];
+                  const float2 x0 = __ffma2_rn(
+                      make_float2(__uint_as_float(P[4 * v]), __uint_as_float(P[4 * v + 1])), k110, nbias);
+                  const float2 x1 = __ffma2_rn(
+                      make_float2(__uint_as_float(P[4 * v + 2]), __uint_as_float(P[4 * v + 3])), k110, nbias);
+                  tsum[2 * v] = __ffma2_rn(make_float2(d4.x, d4.y), x0, tsum[2 * v]);
+                  tsum[2 * v + 1] = __ffma2_rn(make_float2(d4.z, d4.w), x1, tsum[2 * v + 1]);
+                }
+              }
             }
-            const uint32_t* P = buf[ks & 1];
-            if constexpr (DUMP) {  // integer accumulators only: idot = P - kBias - s, no y
-              if (n0 + n < p.N) {
-                const int* sT = reinterpret_cast<const int*>(sstage(ss) + kSOffS) + ks * NA + cg * 16;
-                const int64_t mstride = (int64_t)p.N * (p.K >> 5);
-                int32_t* out = p.idot + (int64_t)(n0 + n) * (p.K >> 5) + kb * kSteps + ks + cg * 16 * mstride;
+            if constexpr (!DUMP) {
+              // the block sum less the code-sum correction, times the weight scale
+              const float4* cp = reinterpret_cast<const float4*>(sstage(ss) + S::kSOffCorr) + cg * 4;
 #pragma unroll
-                for (int i = 0; i < 16; ++i, out += mstride)
-                  if (cg * 16 + i < p.M) *out = (int)P[i] - kBias - sT[i];
+              for (int v = 0; v < 4; ++v) {
+                const float4 c4 = cp[v];
+                tsum[2 * v] = __fadd2_rn(tsum[2 * v], make_float2(c4.x, c4.y));
+                tsum[2 * v + 1] = __fadd2_rn(tsum[2 * v + 1], make_float2(c4.z, c4.w));
               }
-            } else {
+              const float w = reinterpret_cast<const float*>(sstage(ss))[n];
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {  // activation rows 4v .. 4v+3 of the column group
-                const float4 d4 = dp[ks * (NA / 4) + v];
-                const float2 x0 = __ffma2_rn(make_float2(__uint_as_float(P[4 * v]), __uint_as_float(P[4 * v + 1])),
-                                             k110, nbias);
-                const float2 x1 = __ffma2_rn(
-                    make_float2(__uint_as_float(P[4 * v + 2]), __uint_as_float(P[4 * v + 3])), k110, nbias);
-                tsum[2 * v] = __ffma2_rn(make_float2(d4.x, d4.y), x0, tsum[2 * v]);
-                tsum[2 * v + 1] = __ffma2_rn(make_float2(d4.z, d4.w), x1, tsum[2 * v + 1]);
-              }
+              for (int i = 0; i < 8; ++i) acc[i] = __ffma2_rn(make_float2(w, w), tsum[i], acc[i]);
             }
           }
-          if constexpr (!DUMP) {
-            // the block sum less the code-sum correction, times the weight scale
-            const float4* cp = reinterpret_cast<const float4*>(sstage(ss) + kSOffCorr) + cg * 4;
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const float4 c4 = cp[v];
-              tsum[2 * v] = __fadd2_rn(tsum[2 * v], make_float2(c4.x, c4.y));
-              tsum[2 * v + 1] = __fadd2_rn(tsum[2 * v + 1], make_float2(c4.z, c4.w));
-            }
-            const float w = reinterpret_cast<const float*>(sstage(ss))[n];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = __ffma2_rn(make_float2(w, w), tsum[i], acc[i]);
-          }
-        } else {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(d_free(cs));
-        }
-        if (has) {
           __syncwarp();
           if (lane == 0) mbar_arrive(s_empty(ss));
         }
+        if (!ok) continue;
+        // this warp's reads of the slot are done
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_free(cs));
       }
-      // End of tile: the column group's per-block sums are added in block order
-      // through shared memory; every epilogue warp reaches each barrier.
+      // End of tile: the per-warp sums of a column group are added in blk0
+      // order through shared memory; every epilogue warp reaches each barrier.
 #pragma unroll 1
-      for (int r = 1; r < S::kBlkPerSlot; ++r) {
+      for (int r = 1; r < kBlkStep; ++r) {
 #pragma unroll 1
         for (int c = 0; c < S::kNcg; ++c) {
-          if (blk == r && cg == c) {
+          if (blk0 == r && cg == c) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               stg[(2 * i) * kTileW + n] = acc[i].x;
               stg[(2 * i + 1) * kTileW + n] = acc[i].y;
             }
           }
-          asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-          if (blk == 0 && cg == c) {
+          asm volatile("bar.sync 1, %0;" ::"r"(S::kEpiWarps * 32) : "memory");
+          if (blk0 == 0 && cg == c) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               acc[i].x += stg[(2 * i) * kTileW + n];
               acc[i].y += stg[(2 * i + 1) * kTileW + n];
             }
           }
-          asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+          asm volatile("bar.sync 1, %0;" ::"r"(S::kEpiWarps * 32) : "memory");
         }
       }
-      if (!DUMP && blk == 0 && live && ok && !*abort_flag && n0 + n < p.N) {
+      if (!DUMP && blk0 == 0 && live && ok && !*abort_flag && n0 + n < p.N) {
         // a warp's 32 lanes store 32 consecutive floats of one row
         float* dst = p.y + (int64_t)(cg * 16) * p.ldy + n0 + n;
         const int mrows = min(16, p.M - cg * 16);
@@ -575,6 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i, dst += p.ldy) {
           const float v = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
           if (i < mrows) *dst = add ? *dst + v : v;
+          if ((i & 3) == 3) asm volatile("" ::: "memory");  // at most 4 reads of y in flight: the register budget
         }
       }
     }
@@ -582,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)kTmemCols)
                  : "memory");
@@ -593,8 +583,9 @@ template <int NA>
 cudaError_t launch_wm(dim3 grid, cudaStream_t st, const CUtensorMap& mB, const CUtensorMap& mD,
                       const CUtensorMap& mS, const WmParams& p) {
   constexpr size_t smem = (size_t)Shape<NA>::kSmemBytes;
-  return p.idot ? launch_pdl(gemm_wm_kernel<NA, true>, grid, dim3(kThreads), smem, st, mB, mD, mS, p)
-                : launch_pdl(gemm_wm_kernel<NA, false>, grid, dim3(kThreads), smem, st, mB, mD, mS, p);
+  constexpr int threads = Shape<NA>::kThreads;
+  return p.idot ? launch_pdl(gemm_wm_kernel<NA, true>, grid, dim3(threads), smem, st, mB, mD, mS, p)
+                : launch_pdl(gemm_wm_kernel<NA, false>, grid, dim3(threads), smem, st, mB, mD, mS, p);
 }
 
 template <int NA>
