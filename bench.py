@@ -839,7 +839,9 @@ def decode_config3(btf, torch, dev, steps=64, warmup=8, n_ctx=4096, world=1, ran
 def prefill_gemm(btf, torch, dev, reps=10):
     """Benchmark configuration 2: the tcgen05 prefill GEMM (btf_gemm) at M = 64 and 512
     on both weight shapes, each launch over one of 4 rotating weight copies (> L2),
-    timed with CUDA events around a CUDA graph of `reps` launches."""
+    timed with CUDA events around a CUDA graph of `reps` launches. btf_gemm runs
+    M = 64 over the 136 tiles of 5120 -> 17408 on the weight-major kernel and the
+    other cases on the 128-row GEMM (`kernel` names which)."""
     out = {}
     for M, K, N in PREFILL_SHAPES:
         src = torch.from_numpy(synth.ternary_ptq(N, K, seed=0)).to(dev)
@@ -865,20 +867,24 @@ def prefill_gemm(btf, torch, dev, reps=10):
         torch.cuda.synchronize()
         us = a.elapsed_time(b) * 1e3 / reps
         ops = 2.0 * M * N * K
+        tiles = -(-N // 128)
         out[f"M{M}_K{K}_N{N}"] = {"us": us, "TOPS": ops / us / 1e6,
                                   "frac_of_int8_spec_4500": ops / us / 1e6 / 4500.0,
-                                  "weight_GBps": btf.panel_bytes(N, K) / us / 1e3}
+                                  "weight_GBps": btf.panel_bytes(N, K) / us / 1e3,
+                                  "kernel": "gemm_wm_kernel" if M <= 64 and tiles >= 148 * 2 // 3 else "gemm_kernel"}
         del g, mats, src
     return out
 
 
 def lm_head_config4(btf, torch, dev, reps=20):
     """Benchmark configuration 4's lm_head on one GPU: the ternary GEMV K=5120 ->
-    N=248320 (338 MB of panels, 2.7x L2) at batch 1 and batch 16 (btf_gemv; batch
-    16 runs as four 4-row passes over the weights), each launch over one of 2
-    weight copies, timed with CUDA events around a CUDA graph of `reps` launches.
+    N=248320 (338 MB of panels, 2.7x L2) at batch 1 and batch 16 through btf_gemv
+    (batch 16 runs on the weight-major tcgen05 GEMM, one pass over the weights;
+    the four 4-row GEMV passes it replaced are timed beside it), each launch over
+    one of 2 weight copies, timed with CUDA events around a CUDA graph of `reps`
+    launches.
     GB/s counts the algorithmic bytes (weights once, the Q8 activation, the fp32
-    output); `weight_passes` is how often one launch streams the weights. The
+    output); `weight_passes` is how often a launch streams the weights. The
     weights are 16 copies of one seeded 15520-row PTQ1_0 block with config 0's
     distributions (the number of bytes, not their values, sets the time)."""
     _, K, N = synth.LM_HEAD
@@ -891,18 +897,16 @@ def lm_head_config4(btf, torch, dev, reps=20):
     nb = btf.gemv_max_nb(K)
     out = {"shape": f"K{K}_N{N}", "panel_bytes": btf.panel_bytes(N, K), "peak": peak, "peak_source": peak_src}
     st = torch.cuda.Stream(device=dev)
-    for M in (1, 16):
-        act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=8)).to(dev))
-        y = torch.empty((M, N), device=dev)
-        torch.cuda.synchronize()
+
+    def timed(launch):  # mean us per launch of a graph of `reps` launches (alternating weight copies)
         with torch.cuda.stream(st):
             for i in range(4):
-                btf.launch_gemv([(mats[i % 2], y, N)], K, M, act, btf.STORE, st)
+                launch(mats[i % 2])
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
             for i in range(reps):
-                btf.launch_gemv([(mats[i % 2], y, N)], K, M, act, btf.STORE, st)
+                launch(mats[i % 2])
         g.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -911,11 +915,26 @@ def lm_head_config4(btf, torch, dev, reps=20):
             g.replay()
         b.record(st)
         torch.cuda.synchronize()
-        us = a.elapsed_time(b) * 1e3 / reps
-        gbs = synth.gemv_bytes(N, K, M) / us / 1e3
-        out[f"M{M}"] = {"us": us, "GB/s": gbs, "frac_of_hbm": gbs / peak, "weight_passes": -(-M // nb),
-                        "bytes_per_launch": synth.gemv_bytes(N, K, M)}
         del g
+        return a.elapsed_time(b) * 1e3 / reps
+
+    for M in (1, 16):
+        act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=8)).to(dev))
+        y = torch.empty((M, N), device=dev)
+        torch.cuda.synchronize()
+        us = timed(lambda pm: btf.launch_gemv([(pm, y, N)], K, M, act, btf.STORE, st))
+        gbs = synth.gemv_bytes(N, K, M) / us / 1e3
+        out[f"M{M}"] = {"us": us, "GB/s": gbs, "frac_of_hbm": gbs / peak, "weight_passes": 1,
+                        "bytes_per_launch": synth.gemv_bytes(N, K, M),
+                        "path": "btf_gemv -> " + ("gemv_kernel" if M < 9 else "gemm_wm_kernel (weight-major tcgen05)")}
+        if M > nb:  # the GEMV passes the weight-major kernel replaced, on row views of the same activation
+            def passes(pm):
+                for m0 in range(0, M, nb):
+                    sub = btf.Q8Act(act.q[m0:m0 + nb], act.d[m0:m0 + nb], act.s[m0:m0 + nb])
+                    btf.launch_gemv([(pm, y[m0:m0 + nb], N)], K, min(nb, M - m0), sub, btf.STORE, st)
+            us_p = timed(passes)
+            out[f"M{M}"]["gemv_passes"] = {"us": us_p, "weight_passes": -(-M // nb),
+                                           "GB/s": synth.gemv_bytes(N, K, M) / us_p / 1e3}
     out["device_error_word"] = btf.device_error()
     del mats
     return out

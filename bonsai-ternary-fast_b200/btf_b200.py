@@ -384,7 +384,8 @@ def launch_gemv_f32(segs: Sequence[tuple], K: int, M: int, x, mode: int = STORE,
 
 
 def launch_gemm(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int = STORE, stream=None) -> None:
-    """Prefill GEMM on the tcgen05 int8 tensor cores (btf_gemm), M >= 64; store / add modes."""
+    """Prefill GEMM on the tcgen05 int8 tensor cores (btf_gemm), store / add modes; M <= 64 over
+    large matrices runs on the weight-major kernel (btf_gemm_wm)."""
     check(lib().btf_gemm(_segs(segs), len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemm")
 
 

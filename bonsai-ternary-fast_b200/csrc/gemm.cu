@@ -478,6 +478,10 @@ int gemm_setup(DeviceInfo& d) {
 
 // One matrix: y[M][ldy] (=|+=) W q. Called by btf_gemm, which btf_gemv calls
 // for M >= 64 in store / add mode.
+bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
+int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
+                int32_t* idot);
+
 int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
              int32_t* idot = nullptr) {
   const DeviceInfo* dev = current_device();
@@ -567,8 +571,12 @@ extern "C" int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8
         segs[i].ldy < segs[i].N)
       return fail(BTF_ERR_ARG, "btf_gemm: segment %d has a bad panel buffer, N, y or ldy", i);
   }
-  for (int i = 0; i < nseg; ++i)
-    if (int rc = run_gemm(segs[i], K, M, act, mode, (cudaStream_t)stream)) return rc;
+  // per segment: a small batch over many weight tiles goes to the weight-major kernel
+  for (int i = 0; i < nseg; ++i) {
+    const int rc = wm_serves(segs[i], M, act) ? run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)
+                                              : run_gemm(segs[i], K, M, act, mode, (cudaStream_t)stream);
+    if (rc) return rc;
+  }
   return BTF_OK;
 }
 

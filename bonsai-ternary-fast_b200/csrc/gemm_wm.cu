@@ -58,6 +58,7 @@ using namespace tc;
 constexpr int kTileW = 128;         // weight rows per tile (MMA M)
 constexpr int kNAMax = 64;          // activation rows per tile at most (MMA N)
 constexpr int kWmMaxM = kNAMax;     // btf_gemm_wm takes 1 <= M <= this
+constexpr int kWmMinM = 9;          // btf_gemv / btf_gemm route 9 <= M <= 64 here (wm_serves)
 constexpr int kChunk = 128;         // K columns per block (one weight-scale block)
 constexpr int kSteps = 4;           // 32-column MMA steps per block
 constexpr int kBlocksPerSliceW = kCols / kChunk;  // 8 blocks per 1024-column panel slice
@@ -607,6 +608,16 @@ int gemm_wm_setup(DeviceInfo& d) {
   if (e == cudaSuccess) e = set_smem<32>();
   if (e == cudaSuccess) e = set_smem<64>();
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemm_wm_kernel)");
+}
+
+// Dispatch rule of btf_gemv / btf_gemm: the weight-major kernel serves
+// 9 <= M <= 64 (below that the GEMV passes read the weights once or twice and
+// are faster) when a segment has enough 128-row tiles to fill most SMs; it also
+// needs the block sums s 16-byte aligned (tensor-map base).
+bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act) {
+  const DeviceInfo* dev = current_device();
+  return dev && M >= kWmMinM && M <= kWmMaxM && act.s && (reinterpret_cast<uintptr_t>(act.s) & 15) == 0 &&
+         (seg.N + kTileW - 1) / kTileW >= dev->sm_count * 2 / 3;
 }
 
 // One matrix, 1 <= M <= kWmMaxM: y[M][ldy] (=|+=) W q with the weight rows on

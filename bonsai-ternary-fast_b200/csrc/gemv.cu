@@ -827,6 +827,9 @@ int gemv_setup(DeviceInfo& d) {
   return BTF_OK;
 }
 
+// the weight-major GEMM's dispatch rule (gemm_wm.cu)
+bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
+
 }  // namespace btf
 
 using namespace btf;
@@ -840,11 +843,17 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
   if (int rc = check_segs("btf_gemv", segs, nseg, K, mode)) return rc;
   if (!act.q || !act.d || !act.s || !aligned(act.q, 16) || !aligned(act.d, 4) || !aligned(act.s, 4))
     return fail(BTF_ERR_ARG, "btf_gemv: activation pointers null or misaligned (q needs 16 B)");
-  // A prefill batch is a dense contraction: M >= 64 rows go to the tcgen05 GEMM
-  // (store / add; its tensor maps need d 16-byte aligned) instead of the
-  // reference's repeated small-batch passes over the weights (kernels.cu:805-821).
-  if (M >= kGemmMinM && mode != BTF_SWIGLU && aligned(act.d, 16))
-    return btf_gemm(segs, nseg, K, M, act, mode, stream);
+  // A batch of rows is a dense contraction: instead of the reference's repeated
+  // small-batch passes over the weights (kernels.cu:805-821), store / add calls
+  // go to the tcgen05 GEMMs (their tensor maps need d 16-byte aligned): 9..64
+  // rows over large matrices to the weight-major kernel (one weight pass), 64
+  // rows and more to the 128-row GEMM.
+  if (mode != BTF_SWIGLU && aligned(act.d, 16)) {
+    bool wm = true;
+    for (int i = 0; i < nseg; ++i) wm = wm && wm_serves(segs[i], M, act);
+    if (wm) return btf_gemm_wm(segs, nseg, K, M, act, mode, stream);
+    if (M >= kGemmMinM) return btf_gemm(segs, nseg, K, M, act, mode, stream);
+  }
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream);
 }
 

@@ -137,8 +137,10 @@ int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float ep
 /* ---- ternary GEMV (batch M, CUDA cores: dp4a on the 2-bit codes)
  * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
- * segments (gate, up) with the same N. K % 128 == 0. M >= 64 in store / add mode
- * (with d 16-byte aligned) runs as btf_gemm on the tensor cores; smaller M and
+ * segments (gate, up) with the same N. K % 128 == 0. Store / add calls with d
+ * 16-byte aligned run on the tensor cores: 9 <= M <= 64 as btf_gemm_wm when
+ * every segment has at least 2/3 as many 128-row tiles as the device has SMs
+ * (and s is 16-byte aligned), M >= 64 otherwise as btf_gemm. Other calls and
  * swiglu run in passes of btf_gemv_max_nb(K) rows. */
 int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
@@ -168,7 +170,9 @@ int btf_stamp_next(unsigned long long* slot);
  * (kind::i8, one exact 32-deep MMA step per activation block, fp32 epilogue on
  * the CUDA cores). Same result contract as btf_gemv for BTF_STORE / BTF_ADD; it
  * replaces the repeated 8-row passes of launch_gemv (src/cuda/kernels.cu:805-821)
- * for large M. q and d must be 16-byte aligned. */
+ * for large M. q and d must be 16-byte aligned. A segment with M <= 64 and at
+ * least 2/3 as many 128-row tiles as SMs (s 16-byte aligned) runs on the
+ * weight-major kernel of btf_gemm_wm instead. */
 int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
 /* The GEMM for small batches (1 <= M <= 64), weight-major: the weights are the
@@ -176,9 +180,10 @@ int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
  * 64) its N side, so every weight byte is read once for the whole batch. A
  * persistent kernel: one CTA per SM walks 128-row weight tiles. Same result
  * contract and arguments as btf_gemm (store / add modes, 1..3 segments, K a
- * multiple of 128, q and d 16-byte aligned); M > 64 returns BTF_ERR_ARG. It
- * replaces the batch-M passes of launch_gemv (src/cuda/kernels.cu:805-821).
- * btf_gemv and btf_gemm route their small-batch calls here. */
+ * multiple of 128); q, d and s must be 16-byte aligned; M > 64 returns
+ * BTF_ERR_ARG. It replaces the batch-M passes of launch_gemv
+ * (src/cuda/kernels.cu:805-821). btf_gemv and btf_gemm route their small-batch
+ * calls over large matrices here. */
 int btf_gemm_wm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
 /* The prefill GEMM from fp32 activations x [M][ldx], allocating nothing. No

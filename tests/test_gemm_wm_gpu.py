@@ -169,3 +169,30 @@ def test_gemm_wm_rejects_bad_arguments(btf):
     assert "segment 0" in L.btf_last_error().decode()
     assert L.btf_gemm_wm(seg, 1, 1024, 0, act, btf.STORE, None) == 0  # nothing to do
     assert L.btf_gemm_wm_idot(None, 64, 1024, 16, act, ctypes.c_void_p(16), None) == 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [9, 16, 40, 64])
+def test_gemv_and_gemm_route_small_batches_here(cuda, btf, orc, M):
+    # btf_gemv and btf_gemm hand 9 <= M <= 64 rows over a matrix with an SM's
+    # worth of 128-row tiles to the weight-major kernel: bit for bit its output,
+    # and within the bar of the oracle on a subset of rows
+    import torch
+
+    K, N = 1024, 148 * 128
+    src = synth.ternary_ptq(N, K, seed=90 + M)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    x = synth.activations(M, K, seed=91 + M)
+    act = btf.quant_q8(_dev(x, cuda))
+    ys = [torch.full((M, N), 3.0, device=cuda) for _ in range(3)]
+    btf.launch_gemm_wm([(pm, ys[0], N)], K, M, act, btf.STORE)
+    btf.launch_gemv([(pm, ys[1], N)], K, M, act, btf.STORE)
+    btf.launch_gemm([(pm, ys[2], N)], K, M, act, btf.STORE)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    a, b, c = (y.cpu().numpy() for y in ys)
+    assert np.array_equal(a, b) and np.array_equal(a, c)
+    rows = np.r_[0:200, N - 200:N]
+    codes, scales = orc.repack_t2(src[rows], len(rows), K)
+    q, d, s = orc.q8_rows(x)
+    assert rel_rms(a[:, rows], orc.gemv(codes, scales, K, q, d, s, threads=8)) <= TOL
