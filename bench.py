@@ -677,7 +677,8 @@ def lm_head_sharded(btf, torch, dev, world, rank, reps=10, replays=3):
     K=5120 -> N=248320, rank r holding its rows (shard.shard_rows, whole 8-row
     groups; 338/world MB of panels), at batch 1 and 16, with the all-gather fused
     into the GEMV epilogue (btf_gemv_gather, tagged 64-bit stores into every rank's
-    full-width output over NVLink). One run: epoch advance, `reps` launches (each
+    full-width output over NVLink; batch 16 runs on the weight-major tcgen05 GEMM
+    with the same stores). One run: epoch advance, `reps` launches (each
     into its own output buffer), one bounded tag check of all the run's outputs,
     one cross-rank barrier; captured as a CUDA graph, CUDA events, max over ranks.
     GB/s = algorithmic bytes of the whole lm_head per launch (weights once, the Q8
@@ -736,11 +737,14 @@ def lm_head_sharded(btf, torch, dev, world, rank, reps=10, replays=3):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us = float(t.item()) * 1e3 / (replays * reps)
         nbytes = btf.panel_bytes(N, K) + M * (K + K // 32 * 8) + M * N * 4
+        wm = M >= 9 and -(-r.n // 128) >= torch.cuda.get_device_properties(dev).multi_processor_count * 2 // 3
         err = btf.device_error()
         out[f"M{M}"] = {"us": us, "GB/s": nbytes / (us * 1e-6) / 1e9,
                         "GB/s_per_gpu": nbytes / world / (us * 1e-6) / 1e9,
                         "frac_of_hbm_per_gpu": nbytes / world / (us * 1e-6) / 1e9 / peak,
-                        "bytes_per_launch": nbytes, "weight_passes": -(-M // btf.gemv_max_nb(K)),
+                        "bytes_per_launch": nbytes, "weight_passes": 1 if wm else -(-M // btf.gemv_max_nb(K)),
+                        "path": "btf_gemv_gather -> " + ("gemm_wm_kernel (weight-major tcgen05, tagged stores)"
+                                                         if wm else "gemv_kernel (tagged stores)"),
                         "device_error_word": err}
         del g
         torch.cuda.synchronize()

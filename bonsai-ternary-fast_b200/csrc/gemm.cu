@@ -480,7 +480,7 @@ int gemm_setup(DeviceInfo& d) {
 // for M >= 64 in store / add mode.
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
-                int32_t* idot);
+                int32_t* idot, const btf_gather* g, int gseg);
 
 int run_gemm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
              int32_t* idot = nullptr) {
@@ -573,8 +573,9 @@ extern "C" int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8
   }
   // per segment: a small batch over many weight tiles goes to the weight-major kernel
   for (int i = 0; i < nseg; ++i) {
-    const int rc = wm_serves(segs[i], M, act) ? run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)
-                                              : run_gemm(segs[i], K, M, act, mode, (cudaStream_t)stream);
+    const int rc = wm_serves(segs[i], M, act)
+                       ? run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, nullptr, 0)
+                       : run_gemm(segs[i], K, M, act, mode, (cudaStream_t)stream);
     if (rc) return rc;
   }
   return BTF_OK;

@@ -150,14 +150,23 @@ struct WmParams {
   int mode;             // BTF_STORE / BTF_ADD
   int* err;
   int32_t* idot;        // DUMP kernel: [M][N][K/32] integer accumulators (no y is stored)
+  // GATHER kernel (tagged N-sharded store): every output goes to all `world`
+  // ranks' full-width buffers as one 64-bit word (value bits | tag << 32), at
+  // the same index as y; tag = *epoch * 1024 + site
+  int world;
+  unsigned long long* peer[BTF_MAX_RANKS];
+  const unsigned* epoch;
+  int site;
+  unsigned long long* stamp;  // end stamp slot (btf_stamp_next) or null
 };
 
 // Tensor maps: tmB the int8 activation [M][K] (box 128 x NA, SW128); tmD the
 // activation scales [M][K/32] and tmS the activation block sums [M][K/32]
 // (box 32 x NA: one slice). The panels arrive by 1-D bulk copies from p.panels.
 // DUMP (parity/debug): the kernel writes every step's integer accumulator
-// P - kBias (= idot) to p.idot and stores no y.
-template <int NA, bool DUMP>
+// P - kBias (= idot) to p.idot and stores no y. GATHER: the tagged N-sharded
+// store of btf_gemv_gather (store mode).
+template <int NA, bool DUMP, bool GATHER = false>
 __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
     gemm_wm_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmD,
                    const __grid_constant__ CUtensorMap tmS, const WmParams p) {
@@ -556,7 +565,21 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
           asm volatile("bar.sync 1, %0;" ::"r"(S::kEpiWarps * 32) : "memory");
         }
       }
-      if (!DUMP && blk0 == 0 && live && ok && !*abort_flag && n0 + n < p.N) {
+      if (GATHER && blk0 == 0 && live && ok && !*abort_flag && n0 + n < p.N) {
+        // every rank's copy: one single-copy-atomic 64-bit word per output
+        const unsigned long long tag = (unsigned long long)(*p.epoch * 1024u + (unsigned)p.site) << 32;
+        const int64_t idx0 = (int64_t)(cg * 16) * p.ldy + n0 + n;
+        const int mrows = min(16, p.M - cg * 16);
+#pragma unroll 1
+        for (int r = 0; r < p.world; ++r) {
+          unsigned long long* dst = p.peer[r] + idx0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i, dst += p.ldy) {
+            const float v = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
+            if (i < mrows) *dst = (unsigned long long)__float_as_uint(v) | tag;
+          }
+        }
+      } else if (!DUMP && !GATHER && blk0 == 0 && live && ok && !*abort_flag && n0 + n < p.N) {
         // a warp's 32 lanes store 32 consecutive floats of one row
         float* dst = p.y + (int64_t)(cg * 16) * p.ldy + n0 + n;
         const int mrows = min(16, p.M - cg * 16);
@@ -578,6 +601,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)kTmemCols)
                  : "memory");
   }
+  stamp_end(p.stamp);
 }
 
 template <int NA>
@@ -585,6 +609,7 @@ cudaError_t launch_wm(dim3 grid, cudaStream_t st, const CUtensorMap& mB, const C
                       const CUtensorMap& mS, const WmParams& p) {
   constexpr size_t smem = (size_t)Shape<NA>::kSmemBytes;
   constexpr int threads = Shape<NA>::kThreads;
+  if (p.world > 0) return launch_pdl(gemm_wm_kernel<NA, false, true>, grid, dim3(threads), smem, st, mB, mD, mS, p);
   return p.idot ? launch_pdl(gemm_wm_kernel<NA, true>, grid, dim3(threads), smem, st, mB, mD, mS, p)
                 : launch_pdl(gemm_wm_kernel<NA, false>, grid, dim3(threads), smem, st, mB, mD, mS, p);
 }
@@ -595,6 +620,9 @@ cudaError_t set_smem() {
                                        Shape<NA>::kSmemBytes);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gemm_wm_kernel<NA, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Shape<NA>::kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_wm_kernel<NA, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Shape<NA>::kSmemBytes);
   return e;
 }
@@ -621,9 +649,10 @@ bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act) {
 }
 
 // One matrix, 1 <= M <= kWmMaxM: y[M][ldy] (=|+=) W q with the weight rows on
-// the MMA's 128-row side. idot != nullptr runs the dump form instead.
+// the MMA's 128-row side. idot != nullptr runs the dump form instead; g != null
+// (tagged, store mode) stores segment `gseg` into every rank's buffer.
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
-                int32_t* idot) {
+                int32_t* idot, const btf_gather* g, int gseg) {
   const DeviceInfo* dev = current_device();
   if (!dev) return BTF_ERR_STATE;
   const EncodeFn enc = encode_fn();
@@ -673,6 +702,13 @@ int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int
   p.mode = mode;
   p.err = dev->err_word;
   p.idot = idot;
+  p.stamp = take_stamp();
+  if (g) {
+    p.world = g->world;
+    for (int r = 0; r < g->world; ++r) p.peer[r] = reinterpret_cast<unsigned long long*>(g->peer_y[gseg][r]);
+    p.epoch = g->epoch;
+    p.site = g->site;
+  }
   const dim3 grid(std::min(p.ntiles, dev->sm_count));
   const cudaError_t e = NA == 16   ? launch_wm<16>(grid, st, mB, mD, mS, p)
                         : NA == 32 ? launch_wm<32>(grid, st, mB, mD, mS, p)
@@ -699,7 +735,7 @@ extern "C" int btf_gemm_wm(const btf_gemv_seg* segs, int nseg, int K, int M, btf
       return fail(BTF_ERR_ARG, "btf_gemm_wm: segment %d has a bad panel buffer, N, y or ldy", i);
   }
   for (int i = 0; i < nseg; ++i)
-    if (int rc = run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)) return rc;
+    if (int rc = run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, nullptr, 0)) return rc;
   return BTF_OK;
 }
 
@@ -711,5 +747,5 @@ extern "C" int btf_gemm_wm_idot(const void* panels, int N, int K, int M, btf_q8a
       (reinterpret_cast<uintptr_t>(act.d) & 15) || (reinterpret_cast<uintptr_t>(act.s) & 15))
     return fail(BTF_ERR_ARG, "btf_gemm_wm_idot: bad arguments (M <= %d, K %% 128, q, d, s 16-byte aligned)", kWmMaxM);
   const btf_gemv_seg seg{panels, N, nullptr, N};
-  return run_gemm_wm(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot);
+  return run_gemm_wm(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot, nullptr, 0);
 }

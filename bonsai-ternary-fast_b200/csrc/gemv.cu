@@ -827,8 +827,10 @@ int gemv_setup(DeviceInfo& d) {
   return BTF_OK;
 }
 
-// the weight-major GEMM's dispatch rule (gemm_wm.cu)
+// the weight-major GEMM's dispatch rule and launch (gemm_wm.cu)
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
+int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
+                int32_t* idot, const btf_gather* g, int gseg);
 
 }  // namespace btf
 
@@ -852,7 +854,10 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
     bool wm = true;
     for (int i = 0; i < nseg; ++i) wm = wm && wm_serves(segs[i], M, act);
     if (wm) return btf_gemm_wm(segs, nseg, K, M, act, mode, stream);
-    if (M >= kGemmMinM) return btf_gemm(segs, nseg, K, M, act, mode, stream);
+    if (M >= kGemmMinM) {
+      take_stamp();  // the 128-row GEMM writes no end stamp: drop a pending request
+      return btf_gemm(segs, nseg, K, M, act, mode, stream);
+    }
   }
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream);
 }
@@ -880,6 +885,16 @@ int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act 
   for (int s = 0; s < nout; ++s)
     if (g->peer_y[s][g->rank] != segs[s].y)
       return fail(BTF_ERR_ARG, "btf_gemv_gather: peer_y[%d][rank] must be segs[%d].y", s, s);
+  // tagged store calls over large shards: the weight-major tcgen05 GEMM, one weight pass
+  if (g->tagged && mode == BTF_STORE && aligned(act.d, 16)) {
+    bool wm = true;
+    for (int i = 0; i < nseg; ++i) wm = wm && wm_serves(segs[i], M, act);
+    if (wm) {
+      for (int i = 0; i < nseg; ++i)
+        if (int rc = run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, g, i)) return rc;
+      return BTF_OK;
+    }
+  }
   if (!g->tagged && M > kMaxNb)  // counted completion: one arrival per launch, so one pass
     return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_gather: counted completion needs M <= %d (one pass)", kMaxNb);
   return run_gemv(segs, nseg, K, M, &act, nullptr, 0, mode, (cudaStream_t)stream, g);

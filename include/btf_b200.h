@@ -154,9 +154,9 @@ int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* 
  * not for use inside stream capture. clear != 0 resets it. Returns -1 on failure. */
 int btf_device_error(int clear);
 
-/* Measurement hook, no counterpart in the reference: the next btf_quant_q8 or
- * btf_gemv / btf_gemv_f32 / btf_gemv_gather call made by this host thread makes
- * its kernel raise *slot (device memory, 8-byte aligned) to the device's global
+/* Measurement hook, no counterpart in the reference: the next btf_quant_q8,
+ * btf_gemv / btf_gemv_f32 / btf_gemv_gather or btf_gemm_wm call made by this host
+ * thread makes its kernel raise *slot (device memory, 8-byte aligned) to the device's global
  * timer in ns as each CTA finishes, so after the launch *slot holds the end time
  * of its last CTA (atomic max: a slot that starts at 0, or keeps an earlier
  * replay's stamp, ends with this launch's end). The request applies to one call
@@ -306,7 +306,10 @@ typedef struct btf_gather {
 } btf_gather;
 /* Counted completion serves M <= btf_gemv_max_nb(K) (one pass, one arrival per
  * launch); the tagged form serves any M (every pass stores its rows' words with
- * the launch's tag). */
+ * the launch's tag). Tagged store calls with 9 <= M <= 64 whose every shard has
+ * at least 2/3 as many 128-row tiles as SMs (d and s 16-byte aligned) run on the
+ * weight-major tcgen05 GEMM (btf_gemm_wm), one pass over the shard's weights,
+ * with the same tagged stores. */
 int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, const btf_gather* g,
                     void* stream);
 

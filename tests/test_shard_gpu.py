@@ -5,8 +5,9 @@ every rank's gathered output must match the unsharded oracle within rel-RMS
 unsharded launch's, so the fp32 summation order of a row may differ). Run
 three times: all-gather by NCCL after the GEMV; fused into the GEMV epilogue
 (btf_gemv_gather: NVLink stores into every rank's buffer + arrival counters);
-and the tagged form (64-bit (value, tag) words checked by btf_gather_wait).
-Skipped with fewer than 2 GPUs."""
+and the tagged form (64-bit (value, tag) words checked by btf_gather_wait),
+which also runs a batch of 16 over large shards on the weight-major tcgen05
+GEMM. Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -20,6 +21,9 @@ from conftest import rel_rms
 pytestmark = pytest.mark.gpu
 
 CASES = [(17408, 5120, 1, 0), (5120, 17408, 1, 1), (1000, 1024, 3, 1), (37, 256, 2, 2)]  # N, K, M, mode
+# tagged form only: a batch of 16 over shards of 148 128-row tiles, which
+# btf_gemv_gather runs on the weight-major tcgen05 GEMM (one weight pass)
+TAGGED_EXTRA = [(2 * 148 * 128, 1024, 16, 0)]
 
 
 def _free_port():
@@ -66,7 +70,8 @@ def _worker(rank, world, port, out_dir):
             np.save(os.path.join(out_dir, f"c{ci}_r{rank}.npy"), shard.unpad(y_full, N).cpu().numpy())
         dist.barrier()
         # the same cases with the all-gather fused into the GEMV epilogue (NVLink stores)
-        arena = shard.GatherArena(btf, sum(M * N * 12 + 512 for N, K, M, _ in CASES), world, rank, dev)
+        arena = shard.GatherArena(btf, sum(M * N * 12 + 512 for N, K, M, _ in CASES + TAGGED_EXTRA), world, rank,
+                                  dev)
         for ci, (N, K, M, mode) in enumerate(CASES):
             src = synth.ternary_ptq(N, K, seed=10 + ci)
             act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=20 + ci)).to(dev))
@@ -89,7 +94,7 @@ def _worker(rank, world, port, out_dir):
         dist.barrier()
         # tagged form: (value, tag) words, no counters; a bounded device wait checks the tags
         btf.gather_epoch_advance(arena.epoch_ptr)
-        for ci, (N, K, M, mode) in enumerate(CASES):
+        for ci, (N, K, M, mode) in enumerate(CASES + TAGGED_EXTRA):
             src = synth.ternary_ptq(N, K, seed=10 + ci)
             act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=20 + ci)).to(dev))
             gate = shard.ShardedMatrix(btf, src, N, K, world, rank, dev)
@@ -143,3 +148,10 @@ def test_sharded_gemv_nccl_matches_oracle(orc, tmp_path):
             assert rel_rms(got, want) <= 1e-5, ("gather", ci, r, rel_rms(got, want))
             got = np.load(tmp_path / f"t{ci}_r{r}.npy")  # tagged (value, tag) words
             assert rel_rms(got, want) <= 1e-5, ("tagged", ci, r, rel_rms(got, want))
+    for ci, (N, K, M, mode) in enumerate(TAGGED_EXTRA, start=len(CASES)):
+        codes, scales = orc.repack_t2(synth.ternary_ptq(N, K, seed=10 + ci), N, K)
+        q, d, s = orc.q8_rows(synth.activations(M, K, seed=20 + ci))
+        want = orc.gemv(codes, scales, K, q, d, s, threads=8)
+        for r in range(world):
+            got = np.load(tmp_path / f"t{ci}_r{r}.npy")
+            assert rel_rms(got, want) <= 1e-5, ("tagged, weight-major", ci, r, rel_rms(got, want))
