@@ -66,8 +66,7 @@ constexpr int kGroups = kTileW / kRows;  // 16 panel row groups per tile
 constexpr int kSlots = 2;           // TMEM slots in flight
 constexpr int kSlotCols = 256;      // TMEM columns per slot
 constexpr int kTmemCols = kSlots * kSlotCols;  // 512: all of TMEM
-constexpr int kWorkers = 4;         // worker warps (one per SMSP): expand a block, issue its MMAs
-constexpr int kEpiWarp0 = kWorkers;
+constexpr int kBlockWorkers = 4;    // blocks in flight: one worker warp, or a pair, per block
 constexpr int kBiasA = 4, kBiasB = 64, kBias = 32 * kBiasA * kBiasB;  // every region starts at 8192
 static_assert(kBias == 8192, "the bias is a power of two above 32 * 2 * 127");
 constexpr uint64_t kWaitNs = 1000000000ull;
@@ -107,7 +106,12 @@ struct Shape {
   // epilogue warps: 4 lane quarters x 4 at NA = 64; x 2 below, each warp then
   // reading 2 blocks (NA = 16) or both column groups' blocks (NA = 32) of a slot
   static constexpr int kEpiWarps = NA == 64 ? 16 : 8;
-  static constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 640 (96 registers) or 384 (168)
+  // warps per block's expansion: a pair below NA = 64 (16 warps, 128 registers);
+  // one at NA = 64, whose 16 epilogue warps leave no register room for more
+  static constexpr int kP = NA == 64 ? 1 : 2;
+  static constexpr int kWorkers = kBlockWorkers * kP;
+  static constexpr int kEpiWarp0 = kWorkers;
+  static constexpr int kThreads = (kWorkers + kEpiWarps) * 32;  // 512 or 640
   static constexpr uint32_t kIdesc = idesc_i8(kTileW, NA);
   static constexpr uint32_t kIdescBias = idesc_i8(kTileW, kSteps * NA);  // a block's 4 regions
   static_assert(kBlkPerSlot * kSteps * NA == kSlotCols, "a slot is whole blocks");
@@ -129,8 +133,9 @@ struct Shape {
   static constexpr int kOffBiasA = align1k(kOffStg + (NA < 64 ? kStgBytes : 0));
   static constexpr int kOffBiasB = kOffBiasA + kBiasABytes;
   static constexpr int kOffBar = kOffBiasB + kBiasBBytes;
-  // c_full; a_empty; b_full, b_empty; s_full, s_empty; mma_done, d_free; final
-  static constexpr int kNumBars = kCodeStages + kAStages + 2 * kBStages + 2 * kScaleStages + 2 * kSlots + 1;
+  // c_full; a_empty; b_full, b_empty; s_full, s_empty; mma_done, d_free; final; pair
+  static constexpr int kNumBars =
+      kCodeStages + kAStages + 2 * kBStages + 2 * kScaleStages + 2 * kSlots + 1 + kBlockWorkers;
   // TMEM base (4 B), abort flag (4 B), slice counters (4 B each)
   static constexpr int kOffFlags = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffFlags + 16 + 4 * (kCodeStages + 1) + 1024;  // + slack for 1024-B alignment
@@ -194,6 +199,9 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
   auto mma_done = [&](int cs) { return bar0 + (kB1 + 2 * SS + cs) * 8; };     // MMA commits: slot written
   auto d_free = [&](int cs) { return bar0 + (kB1 + 2 * SS + kSlots + cs) * 8; };  // epilogue: slot read
   const uint32_t final_bar = bar0 + (kB1 + 2 * SS + 2 * kSlots) * 8;
+  // both warps of a block's pair have written their halves of the A tile (a
+  // two-arrival barrier both wait on, so neither can run a phase ahead)
+  auto pair_done = [&](int pw) { return bar0 + (kB1 + 2 * SS + 2 * kSlots + 1 + pw) * 8; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::kOffFlags);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kOffFlags + 8);
   int* slice_cnt = reinterpret_cast<int*>(smem + S::kOffFlags + 16);  // blocks of slice stage q expanded
@@ -212,14 +220,15 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       mbar_init(b_empty(s), 1);
     }
     for (int s = 0; s < SS; ++s) {
-      mbar_init(s_full(s), 1);
+      mbar_init(s_full(s), S::kP);  // each warp of the block's pair
       mbar_init(s_empty(s), 4 * S::kNcg);  // the warps that read one block: 4 lane quarters x column groups
     }
     for (int r = 0; r < kSlots; ++r) {
       mbar_init(mma_done(r), S::kBlkPerSlot);  // one commit per block of the slot
       mbar_init(d_free(r), S::kEpiWarps);
     }
-    mbar_init(final_bar, kWorkers);
+    mbar_init(final_bar, S::kWorkers);
+    for (int i = 0; i < kBlockWorkers; ++i) mbar_init(pair_done(i), 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -276,19 +285,24 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
 
   pdl_launch_dependents();
 
-  if (warp < kWorkers) {
+  if (warp < S::kWorkers) {
     // ------------------------------------------------------------ workers
-    // Worker w takes the CTA's blocks w, w + 4, ... (over all its tiles). For
-    // each: the 2-bit codes of the block become int8 codes (trit + 1) of the
+    // Worker pair (or single warp at NA = 64) w takes the CTA's blocks w, w + 4,
+    // ... (over all its tiles). For each, half `half` of the pair: the 2-bit
+    // codes of its 8 (or 16) row groups become int8 codes (trit + 1) of the
     // K-major SW128 A tile (lane: quad h of row groups gi, gi + 2, ... x 16
-    // columns, sub-block t/2, half t&1 of the panel), the scale stage gets the
-    // fp32 weight scales, d per step and the code-sum correction, and lane 0
-    // issues the block's MMAs: a bias MMA over its 4 regions, then 4 steps.
-    // Lane 0 also loads the activation tile of the warp's next block (once the
-    // stage's previous block, kBStages back, has been read by its MMAs), and
-    // the worker that expands the last block of a slice reloads its stage with
-    // the slice kCodeStages ahead.
-    const int w = warp;
+    // columns, sub-block t/2, half t&1 of the panel), and the scale stage gets
+    // its rows' fp32 weight scales. The leader's lane 0, once its partner's
+    // half is written, issues the block's MMAs: a bias MMA over its 4 regions,
+    // then 4 steps. The other warp (the single warp at NA = 64) writes d per
+    // step and the code-sum correction, and its lane 0 loads the activation
+    // tile of the pair's next block (once the stage's previous block, kBStages
+    // back, has been read by its MMAs). The warp that expands the last of a
+    // slice's blocks reloads its stage with the slice kCodeStages ahead.
+    constexpr int P = S::kP;
+    const int w = warp / P, half = warp % P;
+    const bool leader = half == 0;
+    const bool helper = P == 1 || !leader;  // d, s, the correction and the activation loads
     const int t = lane & 7, h = (lane >> 3) & 1, gi = lane >> 4;
     const int coff = h * 1024 + (t & 1) * 512 + (t >> 1) * 16;
     const int total_sl = my_tiles * nsl, total_blk = my_tiles * nb;
@@ -313,18 +327,18 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       mbar_expect_tx(b_full(bs), S::kBBytes);
       tma_load_2d(sbase + S::kOffB + bs * S::kBBytes, &tmB, (j % nb) * kChunk, 0, b_full(bs));
     };
-    const int my_blocks = total_blk > w ? (total_blk - 1 - w) / kWorkers + 1 : 0;
+    const int my_blocks = total_blk > w ? (total_blk - 1 - w) / kBlockWorkers + 1 : 0;
     int b_issued = 0;  // this warp's blocks whose activation copy was issued (lane 0)
     if (lane == 0) {
       pdl_wait();  // the activation, its scales and sums are written by the previous kernel
-      if (w == 0)
+      if (warp == 0)
         for (int g = 0; g < min(CS, total_sl); ++g) issue_slice(g);
-      if (my_blocks > 0) issue_b(w), b_issued = 1;
+      if (helper && my_blocks > 0) issue_b(w), b_issued = 1;
     }
     int last_gsl = -1;
     bool ok = true;
     for (int k = 0; k < my_blocks && ok; ++k) {
-      const int j = w + k * kWorkers, ti = j / nb, kb = j % nb;
+      const int j = w + k * kBlockWorkers, ti = j / nb, kb = j % nb;
       const int gsl = ti * nsl + (kb >> 3), q = gsl % CS, b = kb & (kBlocksPerSliceW - 1);
       if (gsl != last_gsl) {
         if (!wwait(c_full(q), (uint32_t)((gsl / CS) & 1))) break;
@@ -335,8 +349,8 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       const uint8_t* cst = smem + S::kOffCode + q * S::kCodeStageBytes;
       uint8_t* as = smem + S::kOffA + sa * kABytes;
 #pragma unroll
-      for (int r = 0; r < kGroups / 2; ++r) {
-        const int g = gi + 2 * r;
+      for (int r = 0; r < kGroups / 2 / P; ++r) {
+        const int g = half * (kGroups / P) + gi + 2 * r;
         const uint4 c4 = *reinterpret_cast<const uint4*>(cst + g * kPanelBytes + coff + b * 64);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -352,14 +366,15 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       if (j >= SS && !wwait(s_empty(ss), (uint32_t)(((j / SS) - 1) & 1))) break;
       uint8_t* sst = sstage(ss);
 #pragma unroll
-      for (int r = 0; r < kTileW / 32; ++r) {
-        const int row = lane + 32 * r;  // fp16 scale of tile row `row` for this block: [block][row in group]
+      for (int r = 0; r < kTileW / 32 / P; ++r) {
+        // fp16 scale of tile row `row` for this block: [block][row in group]
+        const int row = half * (kTileW / P) + lane + 32 * r;
         const uint16_t hb =
             *reinterpret_cast<const uint16_t*>(cst + (row >> 3) * kPanelBytes + kCodeBytes + b * 16 + (row & 7) * 2);
         reinterpret_cast<float*>(sst)[row] = __half2float(__ushort_as_half(hb)) * 0x1p39f;
       }
 #pragma unroll
-      for (int m = lane; m < NA; m += 32) {
+      for (int m = lane; helper && m < NA; m += 32) {
         // row m's d and s of this block: 16-byte chunk b of its 128-byte slice
         // row, which the 128B-swizzled copy placed at chunk b ^ (m & 7)
         const int off = m * 128 + ((b ^ (m & 7)) << 4);
@@ -391,7 +406,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
         mbar_arrive(s_full(ss));
         // this warp is done with the slice stage for block j; the last of the
         // slice's blocks reloads the stage
-        const int in_slice = min(kBlocksPerSliceW, nb - (kb & ~(kBlocksPerSliceW - 1)));
+        const int in_slice = P * min(kBlocksPerSliceW, nb - (kb & ~(kBlocksPerSliceW - 1)));
         __threadfence_block();  // this warp's reads of the stage come before its count
         if (atomicAdd(&slice_cnt[q], 1) + 1 == in_slice) {
           slice_cnt[q] = 0;
@@ -400,19 +415,25 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
             issue_slice(gsl + CS);
           }
         }
-        // the activation of this warp's next block j + 4: its stage's previous
+      }
+      if (helper && lane == 0) {
+        // the activation of this pair's next block j + 4: its stage's previous
         // block j + 4 - BS was issued well before this block's MMAs
         if (b_issued == k + 1 && b_issued < my_blocks) {
-          const int jn = j + kWorkers;
+          const int jn = j + kBlockWorkers;
           if (jn < BS || wait(b_empty(jn % BS), (uint32_t)((jn / BS - 1) & 1))) {
             issue_b(jn);
             ++b_issued;
           }
         }
+      }
+      if (leader && lane == 0) {
         // the block's MMAs, once its activation has landed and its slot is free
         const int bs = j % BS;
         const int pos = kb % S::kBlkPerSlot, u = ti * nslots + kb / S::kBlkPerSlot, cs = u & 1;
+        if (P > 1) mbar_arrive(pair_done(w));  // after this warp's A writes and proxy fences
         lok = wait(b_full(bs), (uint32_t)((j / BS) & 1));
+        if (lok && P > 1) lok = wait(pair_done(w), (uint32_t)(k & 1));  // the partner's half of A
         if (lok && u >= kSlots) lok = wait(d_free(cs), (uint32_t)(((u >> 1) - 1) & 1));
         if (lok) {
           tc_fence_after();
@@ -431,17 +452,21 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
           for (int r = 0; r < reps; ++r) mma_commit(mma_done(cs));
         }
       }
+      if (!leader && lane == 0) {  // after this warp's A writes and proxy fences; then the leader's
+        mbar_arrive(pair_done(w));
+        lok = wait(pair_done(w), (uint32_t)(k & 1));
+      }
       ok = __shfl_sync(0xffffffffu, lok, 0) != 0;
     }
     if (lane == 0) {
       mma_commit(final_bar);  // completes (with the other workers') when every MMA issued above has finished
       mbar_wait_bounded(final_bar, 0, kWaitNs);
       if (*abort_flag) {  // leave no copy in flight into this CTA's shared memory (bounded)
-        for (int c = max(0, b_issued - 2); c < b_issued; ++c) {
-          const int jc = w + c * kWorkers;
+        for (int c = max(0, b_issued - 2); helper && c < b_issued; ++c) {
+          const int jc = w + c * kBlockWorkers;
           mbar_wait_bounded(b_full(jc % BS), (uint32_t)((jc / BS) & 1), kWaitNs / 10);
         }
-        if (w == 0)
+        if (warp == 0)
           for (int c = max(0, *slices_issued - CS); c < *slices_issued; ++c)
             mbar_wait_bounded(c_full(c % CS), (uint32_t)((c / CS) & 1), kWaitNs / 10);
       }
@@ -452,7 +477,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
     // step (16 activation rows), blocks blk0, blk0 + kBlkStep, ... of every
     // slot (their sums collect in the same accumulators).
     constexpr int kBlkStep = (S::kEpiWarps / 4) / S::kNcg;  // warps of one (quarter, column group)
-    const int we = warp - kEpiWarp0;
+    const int we = warp - S::kEpiWarp0;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int cg = (we >> 2) % S::kNcg, blk0 = (we >> 2) / S::kNcg;
     const int n = q * 32 + lane;      // weight row of the tile
