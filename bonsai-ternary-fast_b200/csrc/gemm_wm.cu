@@ -66,7 +66,6 @@ constexpr int kGroups = kTileW / kRows;  // 16 panel row groups per tile
 constexpr int kSlots = 2;           // TMEM slots in flight
 constexpr int kSlotCols = 256;      // TMEM columns per slot
 constexpr int kTmemCols = kSlots * kSlotCols;  // 512: all of TMEM
-constexpr int kBlockWorkers = 4;    // blocks in flight: one worker warp, or a pair, per block
 constexpr int kBiasA = 4, kBiasB = 64, kBias = 32 * kBiasA * kBiasB;  // every region starts at 8192
 static_assert(kBias == 8192, "the bias is a power of two above 32 * 2 * 127");
 constexpr uint64_t kWaitNs = 1000000000ull;
@@ -109,6 +108,10 @@ struct Shape {
   // warps per block's expansion: a pair below NA = 64 (16 warps, 128 registers);
   // one at NA = 64, whose 16 epilogue warps leave no register room for more
   static constexpr int kP = NA == 64 ? 1 : 2;
+  // blocks in flight (one pair, or warp, each): 5 at NA = 16, whose 6 A stages
+  // keep a pair's next block out of its own previous block's stage (6 pairs,
+  // 20 warps at 96 registers, measured slower); 4 otherwise
+  static constexpr int kBlockWorkers = NA == 16 ? 5 : 4;
   static constexpr int kWorkers = kBlockWorkers * kP;
   static constexpr int kEpiWarp0 = kWorkers;
   static constexpr int kThreads = (kWorkers + kEpiWarps) * 32;  // 512 or 640
@@ -136,6 +139,8 @@ struct Shape {
   // c_full; a_empty; b_full, b_empty; s_full, s_empty; mma_done, d_free; final; pair
   static constexpr int kNumBars =
       kCodeStages + kAStages + 2 * kBStages + 2 * kScaleStages + 2 * kSlots + 1 + kBlockWorkers;
+  // the activation of block j + kBlockWorkers goes into the stage of an older block than j
+  static_assert(kBStages > kBlockWorkers, "activation ring deeper than the blocks in flight");
   // TMEM base (4 B), abort flag (4 B), slice counters (4 B each)
   static constexpr int kOffFlags = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffFlags + 16 + 4 * (kCodeStages + 1) + 1024;  // + slack for 1024-B alignment
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       mbar_init(d_free(r), S::kEpiWarps);
     }
     mbar_init(final_bar, S::kWorkers);
-    for (int i = 0; i < kBlockWorkers; ++i) mbar_init(pair_done(i), 2);
+    for (int i = 0; i < S::kBlockWorkers; ++i) mbar_init(pair_done(i), 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -287,8 +292,8 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
 
   if (warp < S::kWorkers) {
     // ------------------------------------------------------------ workers
-    // Worker pair (or single warp at NA = 64) w takes the CTA's blocks w, w + 4,
-    // ... (over all its tiles). For each, half `half` of the pair: the 2-bit
+    // Worker pair (or single warp at NA = 64) w takes the CTA's blocks w, w + B,
+    // ... (B = kBlockWorkers pairs; over all its tiles). For each, half `half` of the pair: the 2-bit
     // codes of its 8 (or 16) row groups become int8 codes (trit + 1) of the
     // K-major SW128 A tile (lane: quad h of row groups gi, gi + 2, ... x 16
     // columns, sub-block t/2, half t&1 of the panel), and the scale stage gets
@@ -327,7 +332,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       mbar_expect_tx(b_full(bs), S::kBBytes);
       tma_load_2d(sbase + S::kOffB + bs * S::kBBytes, &tmB, (j % nb) * kChunk, 0, b_full(bs));
     };
-    const int my_blocks = total_blk > w ? (total_blk - 1 - w) / kBlockWorkers + 1 : 0;
+    const int my_blocks = total_blk > w ? (total_blk - 1 - w) / S::kBlockWorkers + 1 : 0;
     int b_issued = 0;  // this warp's blocks whose activation copy was issued (lane 0)
     if (lane == 0) {
       pdl_wait();  // the activation, its scales and sums are written by the previous kernel
@@ -338,7 +343,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
     int last_gsl = -1;
     bool ok = true;
     for (int k = 0; k < my_blocks && ok; ++k) {
-      const int j = w + k * kBlockWorkers, ti = j / nb, kb = j % nb;
+      const int j = w + k * S::kBlockWorkers, ti = j / nb, kb = j % nb;
       const int gsl = ti * nsl + (kb >> 3), q = gsl % CS, b = kb & (kBlocksPerSliceW - 1);
       if (gsl != last_gsl) {
         if (!wwait(c_full(q), (uint32_t)((gsl / CS) & 1))) break;
@@ -417,10 +422,10 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
         }
       }
       if (helper && lane == 0) {
-        // the activation of this pair's next block j + 4: its stage's previous
-        // block j + 4 - BS was issued well before this block's MMAs
+        // the activation of this pair's next block j + B: its stage's previous
+        // block j + B - BS was issued well before this block's MMAs
         if (b_issued == k + 1 && b_issued < my_blocks) {
-          const int jn = j + kBlockWorkers;
+          const int jn = j + S::kBlockWorkers;
           if (jn < BS || wait(b_empty(jn % BS), (uint32_t)((jn / BS - 1) & 1))) {
             issue_b(jn);
             ++b_issued;
@@ -463,7 +468,7 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
       mbar_wait_bounded(final_bar, 0, kWaitNs);
       if (*abort_flag) {  // leave no copy in flight into this CTA's shared memory (bounded)
         for (int c = max(0, b_issued - 2); helper && c < b_issued; ++c) {
-          const int jc = w + c * kBlockWorkers;
+          const int jc = w + c * S::kBlockWorkers;
           mbar_wait_bounded(b_full(jc % BS), (uint32_t)((jc / BS) & 1), kWaitNs / 10);
         }
         if (warp == 0)
