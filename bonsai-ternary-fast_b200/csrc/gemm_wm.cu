@@ -16,19 +16,21 @@
 // one tile's rows while the next tile's copies and MMAs are in flight. NA (16,
 // 32 or 64) is the activation rows padded to the MMA's N; a TMEM slot of 256
 // columns holds 256 / (4 NA) whole 128-column blocks (4 steps of NA columns).
-//   warp 0      producer (one thread): per block, TMA of the int8 activation
-//               tile (NA rows, 128B swizzle) into the B ring;
-//   warp 1      MMA issuer (one thread) + TMEM owner: per slot one bias MMA
-//               (N = 256), per block 4 data MMAs (A = weight codes, B =
-//               activations); 2 slots in flight;
-//   warps 2-3   expanders: per 1024-column slice, expander thread 0 copies the
-//               tile's 16 whole panels and the slice's d and s (activation
-//               block scales and sums); per block, the 2-bit codes become int8
-//               codes (trit + 1: 0, 1, 2) of the K-major SW128 A tile, the fp16
-//               weight scales fp32 (x 2^39), and each activation row gets its
-//               d per step and the code-sum correction below;
-//   warps 4-19  epilogue: TMEM lane = weight row; each warp reads 16 activation
-//               rows x the 4 steps of one block of every slot.
+//   workers     kBlockWorkers blocks in flight, each owned by a pair of warps
+//               (a single warp at NA = 64). Per 1024-column slice, the tile's 16
+//               whole panels and the slice's d and s (activation block scales
+//               and sums) are copied into a slice stage (the worker that
+//               finishes a slice's last block reloads it). Per block, the pair
+//               turns the 2-bit codes into int8 codes (trit + 1: 0, 1, 2) of the
+//               K-major SW128 A tile and the fp16 weight scales into fp32
+//               (x 2^39); the helper warp writes each activation row's d per
+//               step and the code-sum correction below, and loads the pair's
+//               next activation tile; the leader's lane 0 issues the block's
+//               MMAs (a bias MMA over the block's 4 regions, 4 data MMAs: A =
+//               weight codes, B = activations) and their commits. Blocks own
+//               disjoint TMEM regions: 2 slots of 256 columns in flight;
+//   epilogue    TMEM lane = weight row; each warp reads 16 activation rows x
+//               the 4 steps of its blocks of every slot. Warp 0 owns TMEM.
 // Arithmetic: the codes are trit + 1, so a step's MMA result is sum (t+1) q =
 // idot + s, with s = sum q of the step (the Q8 block sum); a bias MMA of two
 // constant tiles first sets every region to 8192, so P = idot + s + 8192 lies
@@ -79,8 +81,8 @@ constexpr uint64_t kWaitNs = 1000000000ull;
 //   A ring      (kAStages) [128][128] int8 codes (trit + 1) of one block
 //               (SW128), block i in stage i % kAStages;
 //   B ring      (kBStages) [NA][128] int8 activations of one block (SW128,
-//               TMA), block i in stage i % kBStages, loaded by the worker of
-//               block i - 4;
+//               TMA), block i in stage i % kBStages, loaded by the helper of
+//               block i - kBlockWorkers;
 //   scale ring  (kScaleStages) per block: W fp32 weight scales x 2^39 [128],
 //               d [4 steps][NA] fp32, the code-sum correction
 //               -sum_steps d * s * 2^-39 [NA] fp32, and (dump form) s [4][NA];
@@ -105,8 +107,8 @@ struct Shape {
   // epilogue warps: 4 lane quarters x 4 at NA = 64; x 2 below, each warp then
   // reading 2 blocks (NA = 16) or both column groups' blocks (NA = 32) of a slot
   static constexpr int kEpiWarps = NA == 64 ? 16 : 8;
-  // warps per block's expansion: a pair below NA = 64 (16 warps, 128 registers);
-  // one at NA = 64, whose 16 epilogue warps leave no register room for more
+  // warps per block: a pair below NA = 64; one at NA = 64, whose 16 epilogue
+  // warps leave no register room for more
   static constexpr int kP = NA == 64 ? 1 : 2;
   // blocks in flight (one pair, or warp, each): 5 at NA = 16, whose 6 A stages
   // keep a pair's next block out of its own previous block's stage (6 pairs,
@@ -114,7 +116,7 @@ struct Shape {
   static constexpr int kBlockWorkers = NA == 16 ? 5 : 4;
   static constexpr int kWorkers = kBlockWorkers * kP;
   static constexpr int kEpiWarp0 = kWorkers;
-  static constexpr int kThreads = (kWorkers + kEpiWarps) * 32;  // 512 or 640
+  static constexpr int kThreads = (kWorkers + kEpiWarps) * 32;  // 576 (NA 16), 512 (32), 640 (64)
   static constexpr uint32_t kIdesc = idesc_i8(kTileW, NA);
   static constexpr uint32_t kIdescBias = idesc_i8(kTileW, kSteps * NA);  // a block's 4 regions
   static_assert(kBlkPerSlot * kSteps * NA == kSlotCols, "a slot is whole blocks");
@@ -293,8 +295,8 @@ __global__ void __launch_bounds__(Shape<NA>::kThreads, 1)
   if (warp < S::kWorkers) {
     // ------------------------------------------------------------ workers
     // Worker pair (or single warp at NA = 64) w takes the CTA's blocks w, w + B,
-    // ... (B = kBlockWorkers pairs; over all its tiles). For each, half `half` of the pair: the 2-bit
-    // codes of its 8 (or 16) row groups become int8 codes (trit + 1) of the
+    // ... (B = kBlockWorkers; over all its tiles). For each, half `half` of the
+    // pair: the 2-bit codes of its 8 (or 16) row groups become int8 codes (trit + 1) of the
     // K-major SW128 A tile (lane: quad h of row groups gi, gi + 2, ... x 16
     // columns, sub-block t/2, half t&1 of the panel), and the scale stage gets
     // its rows' fp32 weight scales. The leader's lane 0, once its partner's
