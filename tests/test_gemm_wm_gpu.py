@@ -196,3 +196,35 @@ def test_gemv_and_gemm_route_small_batches_here(cuda, btf, orc, M):
     codes, scales = orc.repack_t2(src[rows], len(rows), K)
     q, d, s = orc.q8_rows(x)
     assert rel_rms(a[:, rows], orc.gemv(codes, scales, K, q, d, s, threads=8)) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", [0, 1])
+def test_gemm_wm_segments_and_strided_output(cuda, btf, orc, mode):
+    # three segments sharing K and the activation (one launch each), outputs with
+    # ldy > N, in store and add mode
+    import torch
+
+    M, K = 24, 1024
+    Ns = (300, 128, 77)
+    x = synth.activations(M, K, seed=121 + mode)
+    act = btf.quant_q8(_dev(x, cuda))
+    q, d, s = orc.q8_rows(x)
+    segs, srcs, ys, y0s = [], [], [], []
+    for i, N in enumerate(Ns):
+        src = synth.ternary_ptq(N, K, seed=122 + i)
+        y0 = np.random.default_rng(i).standard_normal((M, N + 5)).astype(np.float32)
+        y = _dev(y0, cuda)
+        segs.append((btf.repack_panels(_dev(src, cuda), N, K), y, N + 5))
+        srcs.append(src)
+        ys.append(y)
+        y0s.append(y0)
+    btf.launch_gemm_wm(segs, K, M, act, mode)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    for src, y, y0, N in zip(srcs, ys, y0s, Ns):
+        got = y.cpu().numpy()
+        codes, scales = orc.repack_t2(src, N, K)
+        want = orc.gemv(codes, scales, K, q, d, s, threads=8) + (y0[:, :N] if mode == btf.ADD else 0)
+        assert rel_rms(got[:, :N], want) <= TOL, rel_rms(got[:, :N], want)
+        assert np.array_equal(got[:, N:], y0[:, N:])  # the columns past N are untouched
