@@ -882,11 +882,11 @@ def prefill_gemm(btf, torch, dev, reps=10):
 
 def lm_head_config4(btf, torch, dev, reps=20):
     """Benchmark configuration 4's lm_head on one GPU: the ternary GEMV K=5120 ->
-    N=248320 (338 MB of panels, 2.7x L2) at batch 1 and batch 16 through btf_gemv
-    (batch 16 runs on the weight-major tcgen05 GEMM, one pass over the weights;
-    the four 4-row GEMV passes it replaced are timed beside it), each launch over
-    one of 2 weight copies, timed with CUDA events around a CUDA graph of `reps`
-    launches.
+    N=248320 (338 MB of panels, 2.7x L2) at batches 1, 8 and 16 through btf_gemv
+    (batches 8 and 16 run on the warp-MMA GEMM, one pass over the weights; the
+    4-row GEMV passes it replaced and, at batch 16, the tcgen05 weight-major GEMM
+    are timed beside it), each launch over one of 2 weight copies, timed with
+    CUDA events around a CUDA graph of `reps` launches.
     GB/s counts the algorithmic bytes (weights once, the Q8 activation, the fp32
     output); `weight_passes` is how often a launch streams the weights. The
     weights are 16 copies of one seeded 15520-row PTQ1_0 block with config 0's
@@ -922,7 +922,7 @@ def lm_head_config4(btf, torch, dev, reps=20):
         del g
         return a.elapsed_time(b) * 1e3 / reps
 
-    for M in (1, 16):
+    for M in (1, 8, 16):
         act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=8)).to(dev))
         y = torch.empty((M, N), device=dev)
         torch.cuda.synchronize()
@@ -930,8 +930,12 @@ def lm_head_config4(btf, torch, dev, reps=20):
         gbs = synth.gemv_bytes(N, K, M) / us / 1e3
         out[f"M{M}"] = {"us": us, "GB/s": gbs, "frac_of_hbm": gbs / peak, "weight_passes": 1,
                         "bytes_per_launch": synth.gemv_bytes(N, K, M),
-                        "path": "btf_gemv -> " + ("gemv_kernel" if M < 9 else "gemm_wm_kernel (weight-major tcgen05)")}
-        if M > nb:  # the GEMV passes the weight-major kernel replaced, on row views of the same activation
+                        "path": "btf_gemv -> " + ("gemv_kernel" if M <= nb else "gemv_mma_kernel (warp int8 MMA)")}
+        if M >= 9:  # the tcgen05 weight-major kernel on the same call, for comparison
+            us_w = timed(lambda pm: btf.launch_gemm_wm([(pm, y, N)], K, M, act, btf.STORE, st))
+            out[f"M{M}"]["weight_major"] = {"us": us_w, "GB/s": synth.gemv_bytes(N, K, M) / us_w / 1e3,
+                                            "path": "btf_gemm_wm -> gemm_wm_kernel (tcgen05)"}
+        if M > nb:  # the GEMV passes the MMA kernels replaced, on row views of the same activation
             def passes(pm):
                 for m0 in range(0, M, nb):
                     sub = btf.Q8Act(act.q[m0:m0 + nb], act.d[m0:m0 + nb], act.s[m0:m0 + nb])

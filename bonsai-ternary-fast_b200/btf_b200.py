@@ -40,7 +40,7 @@ EXPORTS = (
     "btf_decoder_arena", "btf_decoder_connect", "btf_shard_rows", "btf_decoder_open_tp", "btf_gguf_load_panels_rows",
     "btf_plan_memory", "btf_plan_memory_synthetic", "btf_decoder_stats", "btf_decoder_reset_stats",
     "btf_gemm_f32_noalloc", "btf_chain_program_bytes", "btf_chain_encode", "btf_chain_run", "btf_stamp_next",
-    "btf_gemm_idot", "btf_decoder_prefill", "btf_gemm_wm", "btf_gemm_wm_idot",
+    "btf_gemm_idot", "btf_decoder_prefill", "btf_gemm_wm", "btf_gemm_wm_idot", "btf_gemv_mma", "btf_gemv_mma_idot",
 )
 
 
@@ -172,6 +172,8 @@ def lib() -> ctypes.CDLL:
         "btf_gemm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
         "btf_gemm_wm": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
         "btf_gemm_wm_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
+        "btf_gemv_mma": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, Q8ActC, i32, vp]),
+        "btf_gemv_mma_idot": (i32, [vp, i32, i32, i32, Q8ActC, vp, vp]),
         "btf_gemm_f32_noalloc": (i32, [ctypes.POINTER(GemvSeg), i32, i32, i32, vp, i32, i32, vp]),
         "btf_chain_program_bytes": (i64, [i32]),
         "btf_stamp_next": (i32, [vp]),
@@ -397,6 +399,15 @@ def launch_gemm_wm(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int 
     check(lib().btf_gemm_wm(_segs(segs), len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemm_wm")
 
 
+GEMV_MMA_MAX_M = 16  # btf_gemv_mma takes 1 <= M <= this and K <= GEMV_MMA_MAX_K
+GEMV_MMA_MAX_K = 8192
+
+
+def launch_gemv_mma(segs: Sequence[tuple], K: int, M: int, act: Q8Act, mode: int = STORE, stream=None) -> None:
+    """Small-batch GEMM on warp-level int8 MMA (btf_gemv_mma), 1 <= M <= 16, K <= 8192, store / add modes."""
+    check(lib().btf_gemv_mma(_segs(segs), len(segs), K, M, act.c(), mode, _stream(stream)), "btf_gemv_mma")
+
+
 GEMM_NOALLOC_MAX_MK = 512 * 17408  # BTF_GEMM_NOALLOC_MAX_MK
 
 
@@ -487,6 +498,15 @@ def gemm_wm_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):
     out = torch.empty((M, pm.N, pm.K // 32), dtype=torch.int32, device=pm.panels.device)
     check(lib().btf_gemm_wm_idot(_ptr(pm.panels), pm.N, pm.K, M, act.c(), _ptr(out), _stream(stream)),
           "btf_gemm_wm_idot")
+    return out
+
+
+def gemv_mma_idot(pm: PanelMatrix, M: int, act: Q8Act, stream=None):
+    """Exact int32 accumulators idot[M][N][K/32] from the warp-MMA small-batch GEMM's registers (M <= 16)."""
+    torch = _torch()
+    out = torch.empty((M, pm.N, pm.K // 32), dtype=torch.int32, device=pm.panels.device)
+    check(lib().btf_gemv_mma_idot(_ptr(pm.panels), pm.N, pm.K, M, act.c(), _ptr(out), _stream(stream)),
+          "btf_gemv_mma_idot")
     return out
 
 

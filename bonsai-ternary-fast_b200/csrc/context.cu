@@ -53,6 +53,7 @@ const DeviceInfo* current_device() {
 int gemv_setup(DeviceInfo& d);
 int gemm_setup(DeviceInfo& d);
 int gemm_wm_setup(DeviceInfo& d);
+int gemv_mma_setup(DeviceInfo& d);
 int chain_setup(DeviceInfo& d);
 
 }  // namespace btf
@@ -108,7 +109,7 @@ int btf_init(int device) {
   } else if (g_dev[device].ready) {
     st = BTF_OK;  // already initialised
   } else if ((st = gemv_setup(d)) == BTF_OK && (st = gemm_setup(d)) == BTF_OK && (st = gemm_wm_setup(d)) == BTF_OK &&
-             (st = chain_setup(d)) == BTF_OK) {
+             (st = gemv_mma_setup(d)) == BTF_OK && (st = chain_setup(d)) == BTF_OK) {
     d.ready = true;
     g_dev[device] = d;
   }

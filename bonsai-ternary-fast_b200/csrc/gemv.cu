@@ -827,8 +827,10 @@ int gemv_setup(DeviceInfo& d) {
   return BTF_OK;
 }
 
-// the weight-major GEMM's dispatch rule and launch (gemm_wm.cu)
+// the weight-major GEMM's dispatch rule and launch (gemm_wm.cu), and the
+// warp-MMA small-batch GEMM's rule (gemv_mma.cu)
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
+bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
                 int32_t* idot, const btf_gather* g, int gseg);
 
@@ -847,11 +849,14 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
     return fail(BTF_ERR_ARG, "btf_gemv: activation pointers null or misaligned (q needs 16 B)");
   // A batch of rows is a dense contraction: instead of the reference's repeated
   // small-batch passes over the weights (kernels.cu:805-821), store / add calls
-  // go to the tcgen05 GEMMs (their tensor maps need d 16-byte aligned): 9..64
-  // rows over large matrices to the weight-major kernel (one weight pass), 64
-  // rows and more to the 128-row GEMM.
+  // go to the MMA kernels (d 16-byte aligned): 5..16 rows over very large
+  // matrices (an lm_head) to the warp-MMA kernel, 9..64 rows over large
+  // matrices to the tcgen05 weight-major kernel (one weight pass each), 64
+  // rows and more to the 128-row tcgen05 GEMM.
   if (mode != BTF_SWIGLU && aligned(act.d, 16)) {
-    bool wm = true;
+    bool mma = true, wm = true;
+    for (int i = 0; i < nseg; ++i) mma = mma && mma_serves(segs[i], K, M, act);
+    if (mma) return btf_gemv_mma(segs, nseg, K, M, act, mode, stream);
     for (int i = 0; i < nseg; ++i) wm = wm && wm_serves(segs[i], M, act);
     if (wm) return btf_gemm_wm(segs, nseg, K, M, act, mode, stream);
     if (M >= kGemmMinM) {

@@ -1,0 +1,417 @@
+// Small-batch ternary GEMM on warp-level int8 MMA (mma.sync m16n8k32), for
+// 1 <= M <= 16 activation rows and K <= 8192 against the resident panels.
+//
+// Same contract as the GEMV and the weight-major GEMM (one segment per launch):
+//   y[m][r] {=, +=} sum_b  scale[r][b/4] * d[m][b] * idot[m][r][b],
+// idot the exact int32 dot of the trits of row r and the Q8 values q[m] over
+// 32-column block b (the reference's launch_gemv for NB rows,
+// src/cuda/kernels.cu:211-334, :776-822; exact integer per block as in its
+// emulator, src/emu_decoder.cpp:143-165).
+//
+// Why a warp MMA here: at M <= 16 the per-block work after the integer dot (one
+// fp32 scale per (row, activation row, 32-column block)) is as large as the
+// MMA itself, and the tcgen05 weight-major kernel pays for a shared-memory code
+// expansion and a TMEM read-back per block with one serial chain per worker.
+// The warp MMA takes its A operand from registers, so the 2-bit codes go from
+// the staged panel bytes into the fragment with one AND each, and the integer
+// result lands in registers for the epilogue.
+//
+// Data flow:
+//   - the CTA's prologue copies the M activation rows (zero rows up to 16) into
+//     shared memory with a 32-byte row pad, and builds two small tables: d
+//     transposed to [block][row], and per 128 columns the code-sum correction
+//     -sum d * s * 2^-39 of each row;
+//   - a unit is 32 weight rows (four 8-row panels) x all K; each of the 8 warps
+//     streams its own units in stages of 512 columns: lanes issue 1-D bulk copies
+//     of the stage's 16 code half-regions (256 bytes; row quad h, 16-column half
+//     v of each panel) and 4 scale blocks into the warp's ring, the first stages
+//     before griddepcontrol.wait (the weights do not depend on the previous
+//     kernel). The half-regions land 272 bytes apart and the scale blocks 80, so
+//     the fragment loads below hit distinct banks;
+//   - the MMA's 16 A rows of a thread are two rows of one row quad (quad g =
+//     lane / 4 holds weight rows 4g .. 4g+3): m-tile 0 takes rows 4g (fragment
+//     row g) and 4g+1 (row g+8), m-tile 1 rows 4g+2 and 4g+3. Inside a
+//     32-column block the K positions are permuted, identically for A and B:
+//     positions 4t .. 4t+3 and 16+4t .. 16+4t+3 of thread t = lane % 4 are
+//     columns 8t .. 8t+7, so one 8-byte shared load gives a thread its codes for
+//     all four rows and another its activation bytes of one row;
+//   - the codes of row k sit at bits 2k of each byte, so code word AND
+//     (0x03030303 << 2k) is 4^k c (c = trit + 1 in {0, 1, 2}; at most 128, an
+//     unsigned A byte). With the accumulator input 2^20 the MMA returns
+//     P = 4^k (idot + s) + 2^20 in (2^19, 2^21) (s = the block's sum of q);
+//   - epilogue per value: x = fma(P * 2^-149, 2^(110-2k), -2^(-19-2k))
+//     = (idot + s) * 2^-39 exactly (P's bits read as fp32 are the denormal
+//     P * 2^-149; the product is exact, and so is the sum, an integer below
+//     2^13 times 2^-39); per block T = fma(d, x, T); per 128 columns T plus the
+//     correction, then acc = fma(scale * 2^39, T, acc). Packed f32x2 FMAs, two
+//     activation rows per instruction.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace btf {
+namespace {
+
+#ifndef BTF_MMA_WARPS
+#define BTF_MMA_WARPS 8
+#endif
+constexpr int kMmWarps = BTF_MMA_WARPS;
+constexpr int kMmThreads = kMmWarps * 32;
+constexpr int kMmPanels = 4;                                       // panels (8 rows each) of a unit
+constexpr int kMmRegion = 272;                                     // pitch of a 256-byte code half-region
+constexpr int kMmScalePitch = 80;                                  // pitch of a 64-byte scale block
+constexpr int kMmScaleOff = 16 * kMmRegion;                        // 4352
+constexpr int kMmStage = kMmScaleOff + kMmPanels * kMmScalePitch;  // 4672: 32 rows x 512 columns
+constexpr int kMmMaxDepth = 4;
+constexpr int kMmBarBytes = 512;  // ring barriers (warps x depth) and the spare
+constexpr int kMmRowPad = 32;     // activation row pitch K + 32 bytes
+constexpr int kMmMaxM = 16;
+constexpr int kMmMinM = 5;  // btf_gemv / btf_gemm route 5 <= M <= 16 here (mma_serves)
+constexpr int kMmMaxK = 8192;
+constexpr uint64_t kMmWaitNs = 1000000000ull;
+constexpr int kMmBias = 1 << 20;
+static_assert(kMmRegion % 16 == 0 && kMmScalePitch % 16 == 0 && kMmStage % 16 == 0, "bulk copy alignment");
+static_assert(kMmWarps * kMmMaxDepth * 8 <= kMmBarBytes, "barrier area");
+
+// shared memory of a launch: ring, barriers, activation rows, d table, correction table
+__host__ __device__ constexpr int mm_ring_bytes(int depth) { return kMmWarps * depth * kMmStage; }
+__host__ __device__ constexpr int mm_act_off(int depth) { return mm_ring_bytes(depth) + kMmBarBytes; }
+__host__ __device__ constexpr int mm_dt_off(int depth, int K) { return mm_act_off(depth) + 16 * (K + kMmRowPad); }
+__host__ __device__ constexpr int mm_ct_off(int depth, int K) { return mm_dt_off(depth, K) + 16 * 4 * (K / 32); }
+__host__ __device__ constexpr int mm_smem(int depth, int K) { return mm_ct_off(depth, K) + 16 * 4 * (K / 128); }
+
+struct MmParams {
+  const uint8_t* panels;
+  float* y;
+  int ldy, N, K, M, mode, depth;
+  int ngroups, nhalves, nunits;  // 8-row groups, 512-column stages per unit, 32-row units
+  const int8_t* q;
+  const float* d;
+  const int32_t* s;
+  int32_t* idot;  // dump form: idot[m][n][K/32], no y
+  int* err;
+  unsigned long long* stamp;
+};
+
+// D = A (16 x 32, u8, row) * B (32 x 8, s8, col) + C (every element kMmBias), int32
+__device__ __forceinline__ void mma_u8s8(int (&dd)[4], const uint32_t (&a)[4], uint2 b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=r"(dd[0]), "=r"(dd[1]), "=r"(dd[2]), "=r"(dd[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(kMmBias));
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float2 lds64f(uint32_t addr) {
+  const uint2 v = lds64(addr);
+  return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+}
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 as_f2(int x, int y) { return make_float2(__int_as_float(x), __int_as_float(y)); }
+__device__ __forceinline__ float h2f_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
+
+// x = fma(P * 2^-149, 2^(110-2k), -2^(-19-2k)) for row k of a quad (see the header)
+template <int k>
+__device__ __forceinline__ float2 mm_x(int p0, int p1) {
+  constexpr float kMul = k == 0 ? 0x1p110f : k == 1 ? 0x1p108f : k == 2 ? 0x1p106f : 0x1p104f;
+  constexpr float kSub = k == 0 ? -0x1p-19f : k == 1 ? -0x1p-21f : k == 2 ? -0x1p-23f : -0x1p-25f;
+  return ffma2(as_f2(p0, p1), make_float2(kMul, kMul), make_float2(kSub, kSub));
+}
+
+// DUMP writes the exact idot of every (row, activation row, block) instead of y.
+template <bool DUMP>
+__global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_constant__ MmParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int depth = p.depth, K = p.K;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t ring = sbase + warp * depth * kMmStage;
+  const uint32_t bars = sbase + mm_ring_bytes(depth) + warp * depth * 8;
+  const int H = p.nhalves;
+  const int W = gridDim.x * kMmWarps, wg = blockIdx.x * kMmWarps + warp;
+  const int my_units = wg < p.nunits ? (p.nunits - wg + W - 1) / W : 0;
+  const int items = my_units * H;  // (unit, 512-column stage) items of this warp, unit-major
+  if (lane == 0) {
+    for (int i = 0; i < depth; ++i) mbar_init(bars + 8 * i, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  // Item `it` (unit wg + (it / H) W, columns 512 (it % H) ..) into slot it % depth:
+  // lanes 0 .. 4np-1 copy half-region lane & 3 (h = bit 1, v = bit 0) of panel
+  // lane >> 2, lanes 16 .. 16+np-1 the panels' scale blocks of the 4 blocks.
+  auto issue = [&](int it, int slot) {
+    const int u = wg + (it / H) * W, j = it % H;
+    const int np = min(kMmPanels, p.ngroups - kMmPanels * u);
+    const uint32_t bar = bars + 8 * slot, dst = ring + slot * kMmStage;
+    if (lane == 0) mbar_expect_tx(bar, (uint32_t)np * (16 * 256 / 4 + 64));
+    __syncwarp();
+    const int64_t S = (p.nhalves + 1) >> 1;
+    const uint8_t* pan0 = p.panels + panel_offset((int64_t)kMmPanels * u, j >> 1, S);
+    const int64_t pstride = S * kPanelBytes;  // next 8-row group, same slice
+    const int half = j & 1;
+    if (lane < 4 * np)
+      bulk_g2s(dst + lane * kMmRegion, pan0 + (lane >> 2) * pstride + (lane & 3) * 512 + half * 256, 256, bar);
+    else if (lane >= 16 && lane < 16 + np)
+      bulk_g2s(dst + kMmScaleOff + (lane - 16) * kMmScalePitch,
+               pan0 + (lane - 16) * pstride + kCodeBytes + half * 64, 64, bar);
+  };
+
+  const int pre = min(items, depth);
+  for (int it = 0; it < pre; ++it) issue(it, it);  // the panels do not depend on the previous kernel
+  pdl_launch_dependents();
+  pdl_wait();  // q, d, s (and y in add mode) are written by earlier kernels
+
+  // activation rows (zeros past M), d transposed to [block][row], and the
+  // per-128-column correction -sum_steps d s 2^-39 of each row
+  const int pitch = K + kMmRowPad, kb = K >> 5;
+  uint8_t* qs = smem + mm_act_off(depth);
+  float* dt = reinterpret_cast<float*>(smem + mm_dt_off(depth, K));
+  float* ct = reinterpret_cast<float*>(smem + mm_ct_off(depth, K));
+  for (int i = threadIdx.x; i < 16 * (K >> 4); i += kMmThreads) {
+    const int m = i / (K >> 4), c = i - m * (K >> 4);
+    const uint4 v = m < p.M ? reinterpret_cast<const uint4*>(p.q + (size_t)m * K)[c] : make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(qs + m * pitch + 16 * c) = v;
+  }
+  for (int i = threadIdx.x; i < 16 * kb; i += kMmThreads) {
+    const int b = i >> 4, m = i & 15;
+    dt[i] = m < p.M ? p.d[(size_t)m * kb + b] : 0.f;
+  }
+  for (int i = threadIdx.x; i < 16 * (K >> 7); i += kMmThreads) {
+    const int bb = i >> 4, m = i & 15;
+    float c = 0.f;
+    if (m < p.M) {
+      const float4 d4 = reinterpret_cast<const float4*>(p.d + (size_t)m * kb)[bb];
+      const int4 s4 = reinterpret_cast<const int4*>(p.s + (size_t)m * kb)[bb];
+      c = fmaf(d4.x * -0x1p-39f, (float)s4.x, c);
+      c = fmaf(d4.y * -0x1p-39f, (float)s4.y, c);
+      c = fmaf(d4.z * -0x1p-39f, (float)s4.z, c);
+      c = fmaf(d4.w * -0x1p-39f, (float)s4.w, c);
+    }
+    ct[i] = c;
+  }
+  __syncthreads();
+
+  const uint32_t M3 = 0x03030303u;
+  const bool add = p.mode == BTF_ADD;
+  const bool vec = ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0) && (p.ldy & 3) == 0;
+  const uint32_t qrow0 = sbase + mm_act_off(depth) + g * pitch + tig * 8;  // + 8 pitch for n-tile 1
+  const uint32_t dt0 = sbase + mm_dt_off(depth, K) + 8 * tig;              // + 64 b + 32 nt
+  const uint32_t ct0 = sbase + mm_ct_off(depth, K) + 8 * tig;              // + 64 gb + 32 nt
+  float2 acc[4][2];  // [row 4g + k][n-tile]: (column 2t, column 2t + 1)
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k][0] = acc[k][1] = make_float2(0.f, 0.f);
+  int failed = -1, slot = 0, phase = 0;
+#pragma unroll 1
+  for (int it = 0; it < items; ++it) {
+    const int j = it % H;
+    const int u = wg + (it / H) * W;
+    if (!mbar_wait_bounded(bars + 8 * slot, (uint32_t)phase, kMmWaitNs)) {
+      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+      failed = it;
+      break;
+    }
+    const uint32_t st = ring + slot * kMmStage;
+    const uint32_t code = st + (2 * g + (tig >> 1)) * kMmRegion + (tig & 1) * 8;  // + 16 per 32-column step
+    const uint32_t scl = st + kMmScaleOff + (g >> 1) * kMmScalePitch + (g & 1) * 8;  // + 16 per 128 columns
+    const int nb = min(4, (K >> 7) - 4 * j);
+#pragma unroll 1
+    for (int bb = 0; bb < nb; ++bb) {
+      const int gb = 4 * j + bb;  // 128-column block of the row
+      float2 T[4][2];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) T[k][0] = T[k][1] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint2 cw = lds64(code + (bb * 4 + ks) * 16);
+        // m-tile 0: rows 4g (fragment row g) and 4g+1 (row g+8); m-tile 1: 4g+2, 4g+3
+        const uint32_t a0[4] = {cw.x & M3, cw.x & (M3 << 2), cw.y & M3, cw.y & (M3 << 2)};
+        const uint32_t a1[4] = {cw.x & (M3 << 4), cw.x & (M3 << 6), cw.y & (M3 << 4), cw.y & (M3 << 6)};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint2 qv = lds64(qrow0 + nt * 8 * pitch + gb * 128 + ks * 32);
+          int d0[4], d1[4];
+          mma_u8s8(d0, a0, qv);
+          mma_u8s8(d1, a1, qv);
+          if constexpr (DUMP) {
+            const int r0 = 32 * u + 4 * g, blk = gb * 4 + ks;
+            const int pv[4][2] = {{d0[0], d0[1]}, {d0[2], d0[3]}, {d1[0], d1[1]}, {d1[2], d1[3]}};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int c = 0; c < 2; ++c) {
+                const int m = nt * 8 + 2 * tig + c;
+                if (m < p.M && r0 + k < p.N)
+                  p.idot[((int64_t)m * p.N + r0 + k) * kb + blk] =
+                      ((pv[k][c] - kMmBias) >> (2 * k)) - p.s[(size_t)m * kb + blk];
+              }
+          } else {
+            const float2 dv = lds64f(dt0 + (gb * 4 + ks) * 64 + nt * 32);
+            T[0][nt] = ffma2(dv, mm_x<0>(d0[0], d0[1]), T[0][nt]);
+            T[1][nt] = ffma2(dv, mm_x<1>(d0[2], d0[3]), T[1][nt]);
+            T[2][nt] = ffma2(dv, mm_x<2>(d1[0], d1[1]), T[2][nt]);
+            T[3][nt] = ffma2(dv, mm_x<3>(d1[2], d1[3]), T[3][nt]);
+          }
+        }
+      }
+      if constexpr (!DUMP) {
+        const uint2 sc = lds64(scl + bb * 16);  // fp16 scales of rows 4g .. 4g+3, this block
+        const float w[4] = {h2f_bits(sc.x & 0xffffu) * 0x1p39f, h2f_bits(sc.x >> 16) * 0x1p39f,
+                            h2f_bits(sc.y & 0xffffu) * 0x1p39f, h2f_bits(sc.y >> 16) * 0x1p39f};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float2 cv = lds64f(ct0 + gb * 64 + nt * 32);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            acc[k][nt] = ffma2(make_float2(w[k], w[k]), __fadd2_rn(T[k][nt], cv), acc[k][nt]);
+        }
+      }
+    }
+    __syncwarp();  // every lane's reads of the slot are done
+    if (it + depth < items) issue(it + depth, slot);
+    if (++slot == depth) {
+      slot = 0;
+      phase ^= 1;
+    }
+    if (j == H - 1) {  // the unit's last stage: rows 32u + 4g .. +3
+      if constexpr (!DUMP) {
+        const int r0 = 32 * u + 4 * g;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int m = nt * 8 + 2 * tig + c;
+            if (m >= p.M) continue;
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = c ? acc[k][nt].y : acc[k][nt].x;
+            float* dst = p.y + (int64_t)m * p.ldy + r0;
+            if (vec && r0 + 3 < p.N) {
+              float4 o = make_float4(v[0], v[1], v[2], v[3]);
+              if (add) {
+                const float4 yo = *reinterpret_cast<const float4*>(dst);
+                o = make_float4(yo.x + o.x, yo.y + o.y, yo.z + o.z, yo.w + o.w);
+              }
+              *reinterpret_cast<float4*>(dst) = o;
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                if (r0 + k < p.N) dst[k] = add ? dst[k] + v[k] : v[k];
+            }
+          }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[k][0] = acc[k][1] = make_float2(0.f, 0.f);
+    }
+  }
+  if (failed >= 0) {  // leave no copy of this warp in flight into shared memory (bounded)
+    const int last = min(items, failed + depth);
+    for (int it = failed; it < last; ++it)
+      mbar_wait_bounded(bars + 8 * (it % depth), (uint32_t)((it / depth) & 1), kMmWaitNs / 10);
+  }
+  stamp_end(p.stamp);
+}
+
+}  // namespace
+
+int gemv_mma_setup(DeviceInfo& d) {
+  const int need = mm_smem(2, kMmMaxK);
+  if (d.optin_smem < need) return fail(BTF_ERR_UNSUPPORTED, "btf_gemv_mma needs %d B of shared memory", need);
+  cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemv_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemv_mma_kernel)");
+}
+
+// Dispatch rule of btf_gemv / btf_gemm: 5 <= M <= 16 rows (at most 4 the GEMV
+// reads the weights once and is faster) with K <= 8192, over a matrix with at
+// least two 32-row units per warp of the device (fewer leave SMs idle, where
+// the weight-major kernel or the GEMV passes are as fast); q, d and s 16-byte
+// aligned.
+bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act) {
+  const DeviceInfo* dev = current_device();
+  return dev && M >= kMmMinM && M <= kMmMaxM && K > 0 && K % 128 == 0 && K <= kMmMaxK && act.q && act.d && act.s &&
+         (reinterpret_cast<uintptr_t>(act.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(act.d) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(act.s) & 15) == 0 &&
+         (groups_of(seg.N) + kMmPanels - 1) / kMmPanels >= 2 * dev->sm_count * kMmWarps;
+}
+
+// One segment, 1 <= M <= kMmMaxM, K <= kMmMaxK; idot != nullptr runs the dump form.
+int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
+                 int32_t* idot) {
+  const DeviceInfo* dev = current_device();
+  if (!dev) return BTF_ERR_STATE;
+  MmParams p{};
+  p.panels = static_cast<const uint8_t*>(seg.panels);
+  p.y = seg.y;
+  p.ldy = seg.ldy;
+  p.N = seg.N;
+  p.K = K;
+  p.M = M;
+  p.mode = mode;
+  p.ngroups = (int)groups_of(seg.N);
+  p.nhalves = (K + 511) / 512;
+  p.nunits = (p.ngroups + kMmPanels - 1) / kMmPanels;
+  p.q = act.q;
+  p.d = act.d;
+  p.s = act.s;
+  p.idot = idot;
+  p.err = dev->err_word;
+  p.stamp = take_stamp();
+  // the deepest ring that fits beside this K's activation tables
+  const int limit = mm_smem(2, kMmMaxK);
+  p.depth = 2;
+  while (p.depth < kMmMaxDepth && mm_smem(p.depth + 1, K) <= limit) ++p.depth;
+  const size_t smem = (size_t)mm_smem(p.depth, K);
+  const int grid = std::max(1, std::min(dev->sm_count, (p.nunits + kMmWarps - 1) / kMmWarps));
+  const cudaError_t e = idot ? launch_pdl(gemv_mma_kernel<true>, dim3(grid), dim3(kMmThreads), smem, st, p)
+                             : launch_pdl(gemv_mma_kernel<false>, dim3(grid), dim3(kMmThreads), smem, st, p);
+  return e == cudaSuccess ? launch_status("gemv_mma_kernel") : cuda_fail(e, "gemv_mma_kernel launch");
+}
+
+}  // namespace btf
+
+using namespace btf;
+
+namespace {
+bool mma_args_ok(const btf_q8act& act, int K, int M) {
+  return M <= kMmMaxM && K > 0 && K % 128 == 0 && K <= kMmMaxK && act.q && act.d && act.s &&
+         (reinterpret_cast<uintptr_t>(act.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(act.d) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(act.s) & 15) == 0;
+}
+}  // namespace
+
+extern "C" int btf_gemv_mma(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode,
+                            void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (!mma_args_ok(act, K, M))
+    return fail(BTF_ERR_ARG,
+                "btf_gemv_mma: need M <= %d, K a positive multiple of 128 up to %d, q, d, s 16-byte aligned",
+                kMmMaxM, kMmMaxK);
+  if (!segs || nseg < 1 || nseg > 3) return fail(BTF_ERR_ARG, "btf_gemv_mma: 1..3 segments (got %d)", nseg);
+  if (mode != BTF_STORE && mode != BTF_ADD) return fail(BTF_ERR_ARG, "btf_gemv_mma: mode must be BTF_STORE or BTF_ADD");
+  for (int i = 0; i < nseg; ++i)
+    if (!segs[i].panels || (reinterpret_cast<uintptr_t>(segs[i].panels) & 15) || segs[i].N <= 0 || !segs[i].y ||
+        segs[i].ldy < segs[i].N)
+      return fail(BTF_ERR_ARG, "btf_gemv_mma: segment %d has a bad panel buffer, N, y or ldy", i);
+  for (int i = 0; i < nseg; ++i)
+    if (int rc = run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)) return rc;
+  return BTF_OK;
+}
+
+extern "C" int btf_gemv_mma_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot,
+                                 void* stream) {
+  if (M <= 0) return BTF_OK;
+  if (!mma_args_ok(act, K, M) || !panels || (reinterpret_cast<uintptr_t>(panels) & 15) || N <= 0 || !idot)
+    return fail(BTF_ERR_ARG, "btf_gemv_mma_idot: bad arguments (M <= %d, K %% 128 up to %d, q, d, s 16-byte aligned)",
+                kMmMaxM, kMmMaxK);
+  const btf_gemv_seg seg{panels, N, nullptr, N};
+  return run_gemv_mma(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot);
+}

@@ -138,7 +138,9 @@ int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float ep
  * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
  * segments (gate, up) with the same N. K % 128 == 0. Store / add calls with d
- * 16-byte aligned run on the tensor cores: 9 <= M <= 64 as btf_gemm_wm when
+ * 16-byte aligned run on the tensor cores: 5 <= M <= 16 with K <= 8192 as
+ * btf_gemv_mma when every segment has at least 2 * 8 * (SM count) 32-row units
+ * (an lm_head; q, d, s 16-byte aligned), else 9 <= M <= 64 as btf_gemm_wm when
  * every segment has at least 2/3 as many 128-row tiles as the device has SMs
  * (and s is 16-byte aligned), M >= 64 otherwise as btf_gemm. Other calls and
  * swiglu run in passes of btf_gemv_max_nb(K) rows. */
@@ -155,7 +157,7 @@ int btf_gemv_f32(const btf_gemv_seg* segs, int nseg, int K, int M, const float* 
 int btf_device_error(int clear);
 
 /* Measurement hook, no counterpart in the reference: the next btf_quant_q8,
- * btf_gemv / btf_gemv_f32 / btf_gemv_gather or btf_gemm_wm call made by this host
+ * btf_gemv / btf_gemv_f32 / btf_gemv_gather, btf_gemm_wm or btf_gemv_mma call made by this host
  * thread makes its kernel raise *slot (device memory, 8-byte aligned) to the device's global
  * timer in ns as each CTA finishes, so after the launch *slot holds the end time
  * of its last CTA (atomic max: a slot that starts at 0, or keeps an earlier
@@ -170,9 +172,10 @@ int btf_stamp_next(unsigned long long* slot);
  * (kind::i8, one exact 32-deep MMA step per activation block, fp32 epilogue on
  * the CUDA cores). Same result contract as btf_gemv for BTF_STORE / BTF_ADD; it
  * replaces the repeated 8-row passes of launch_gemv (src/cuda/kernels.cu:805-821)
- * for large M. q and d must be 16-byte aligned. A segment with M <= 64 and at
- * least 2/3 as many 128-row tiles as SMs (s 16-byte aligned) runs on the
- * weight-major kernel of btf_gemm_wm instead. */
+ * for large M. q and d must be 16-byte aligned. A segment that btf_gemv would
+ * give to btf_gemv_mma runs there; one with M <= 64 and at least 2/3 as many
+ * 128-row tiles as SMs (s 16-byte aligned) runs on the weight-major kernel of
+ * btf_gemm_wm instead. */
 int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
 /* The GEMM for small batches (1 <= M <= 64), weight-major: the weights are the
@@ -185,6 +188,17 @@ int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
  * (src/cuda/kernels.cu:805-821). btf_gemv and btf_gemm route their small-batch
  * calls over large matrices here. */
 int btf_gemm_wm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
+
+/* The small-batch GEMM on warp-level int8 MMA (1 <= M <= 16, K <= 8192): 32
+ * weight rows per warp, the 2-bit codes moved from the staged panels straight
+ * into the MMA operand registers, one exact 32-deep integer dot per activation
+ * block and the fp32 block scaling in registers; the activation rows sit in
+ * shared memory. Every weight byte is read once for the batch. Same result
+ * contract and arguments as btf_gemm_wm (store / add, 1..3 segments, K a
+ * multiple of 128, q, d and s 16-byte aligned); M > 16 or K > 8192 returns
+ * BTF_ERR_ARG. Replaces the batch-M passes of launch_gemv
+ * (src/cuda/kernels.cu:805-821). */
+int btf_gemv_mma(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, int mode, void* stream);
 
 /* The prefill GEMM from fp32 activations x [M][ldx], allocating nothing. No
  * counterpart in the reference: it exists for callers that cannot allocate
@@ -270,6 +284,9 @@ int btf_gemm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_
 
 /* The same dump from the weight-major GEMM (btf_gemm_wm), 1 <= M <= 64. */
 int btf_gemm_wm_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
+
+/* The same dump from the warp-MMA small-batch GEMM (btf_gemv_mma), 1 <= M <= 16, K <= 8192. */
+int btf_gemv_mma_idot(const void* panels, int N, int K, int M, btf_q8act act, int32_t* idot, void* stream);
 
 /* ---- N-sharded GEMV with the all-gather fused into the epilogue
  * The reference is single-GPU (src/cuda/gpu_decoder.cu); this is the B200
