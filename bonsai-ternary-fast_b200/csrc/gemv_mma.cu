@@ -22,12 +22,15 @@
 //     transposed to [block][row], and per 128 columns the code-sum correction
 //     -sum d * s * 2^-39 of each row;
 //   - a unit is 32 weight rows (four 8-row panels) x all K; each of the 8 warps
-//     streams its own units in stages of 512 columns: lanes issue 1-D bulk copies
-//     of the stage's 16 code half-regions (256 bytes; row quad h, 16-column half
-//     v of each panel) and 4 scale blocks into the warp's ring, the first stages
-//     before griddepcontrol.wait (the weights do not depend on the previous
-//     kernel). The half-regions land 272 bytes apart and the scale blocks 80, so
-//     the fragment loads below hit distinct banks;
+//     streams its own units in stages of 512 columns: its lanes copy the stage's
+//     16 code half-regions (256 bytes; row quad h, 16-column half v of each
+//     panel) and 4 scale blocks into the warp's ring with 16-byte cp.async
+//     copies, one commit group per stage, the first stages before
+//     griddepcontrol.wait (the weights do not depend on the previous kernel).
+//     The half-regions land 272 bytes apart and the scale blocks 80, so the
+//     fragment loads below hit distinct banks. (One TMA bulk copy per
+//     half-region streamed at only ~3 TB/s: the copy engine's per-copy cost
+//     bounds copies this small.);
 //   - the MMA's 16 A rows of a thread are two rows of one row quad (quad g =
 //     lane / 4 holds weight rows 4g .. 4g+3): m-tile 0 takes rows 4g (fragment
 //     row g) and 4g+1 (row g+8), m-tile 1 rows 4g+2 and 4g+3. Inside a
@@ -39,12 +42,13 @@
 //     (0x03030303 << 2k) is 4^k c (c = trit + 1 in {0, 1, 2}; at most 128, an
 //     unsigned A byte). With the accumulator input 2^20 the MMA returns
 //     P = 4^k (idot + s) + 2^20 in (2^19, 2^21) (s = the block's sum of q);
-//   - epilogue per value: x = fma(P * 2^-149, 2^(110-2k), -2^(-19-2k))
-//     = (idot + s) * 2^-39 exactly (P's bits read as fp32 are the denormal
+//   - epilogue per value: x = fma(P * 2^-149, 2^110, -2^-19)
+//     = 4^k (idot + s) * 2^-39 exactly (P's bits read as fp32 are the denormal
 //     P * 2^-149; the product is exact, and so is the sum, an integer below
-//     2^13 times 2^-39); per block T = fma(d, x, T); per 128 columns T plus the
-//     correction, then acc = fma(scale * 2^39, T, acc). Packed f32x2 FMAs, two
-//     activation rows per instruction.
+//     2^21 times 2^-39); per block T = fma(d, x, T); per 128 columns
+//     acc = fma(scale 2^39 4^-k, T, acc) and acc = fma(scale 2^39, corr, acc)
+//     (the powers of two are exact). Packed f32x2 FMAs, two activation rows per
+//     instruction.
 #include <algorithm>
 
 #include "common.cuh"
@@ -63,7 +67,7 @@ constexpr int kMmScalePitch = 80;                                  // pitch of a
 constexpr int kMmScaleOff = 16 * kMmRegion;                        // 4352
 constexpr int kMmStage = kMmScaleOff + kMmPanels * kMmScalePitch;  // 4672: 32 rows x 512 columns
 constexpr int kMmMaxDepth = 4;
-constexpr int kMmBarBytes = 512;  // ring barriers (warps x depth) and the spare
+constexpr int kMmBarBytes = 512;  // the activation copy's barrier (last 8 bytes)
 constexpr int kMmRowPad = 32;     // activation row pitch K + 32 bytes
 constexpr int kMmMaxM = 16;
 constexpr int kMmMinM = 5;  // btf_gemv / btf_gemm route 5 <= M <= 16 here (mma_serves)
@@ -71,7 +75,6 @@ constexpr int kMmMaxK = 8192;
 constexpr uint64_t kMmWaitNs = 1000000000ull;
 constexpr int kMmBias = 1 << 20;
 static_assert(kMmRegion % 16 == 0 && kMmScalePitch % 16 == 0 && kMmStage % 16 == 0, "bulk copy alignment");
-static_assert(kMmWarps * kMmMaxDepth * 8 <= kMmBarBytes, "barrier area");
 
 // shared memory of a launch: ring, barriers, activation rows, d table, correction table
 __host__ __device__ constexpr int mm_ring_bytes(int depth) { return kMmWarps * depth * kMmStage; }
@@ -102,6 +105,21 @@ __device__ __forceinline__ void mma_u8s8(int (&dd)[4], const uint32_t (&a)[4], u
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y), "r"(kMmBias));
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), and its group fences
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most n (0 .. kMmMaxDepth - 1) of this thread's groups are pending
+__device__ __forceinline__ void cp_async_wait(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+  }
+}
+
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 v;
   asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
@@ -116,12 +134,10 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return _
 __device__ __forceinline__ float2 as_f2(int x, int y) { return make_float2(__int_as_float(x), __int_as_float(y)); }
 __device__ __forceinline__ float h2f_bits(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
 
-// x = fma(P * 2^-149, 2^(110-2k), -2^(-19-2k)) for row k of a quad (see the header)
-template <int k>
+// x = fma(P * 2^-149, 2^110, -2^-19) = 4^k (idot + s) 2^-39 for row k of a
+// quad; the 4^k is removed with the weight scale (see the header)
 __device__ __forceinline__ float2 mm_x(int p0, int p1) {
-  constexpr float kMul = k == 0 ? 0x1p110f : k == 1 ? 0x1p108f : k == 2 ? 0x1p106f : 0x1p104f;
-  constexpr float kSub = k == 0 ? -0x1p-19f : k == 1 ? -0x1p-21f : k == 2 ? -0x1p-23f : -0x1p-25f;
-  return ffma2(as_f2(p0, p1), make_float2(kMul, kMul), make_float2(kSub, kSub));
+  return ffma2(as_f2(p0, p1), make_float2(0x1p110f, 0x1p110f), make_float2(-0x1p-19f, -0x1p-19f));
 }
 
 // DUMP writes the exact idot of every (row, activation row, block) instead of y.
@@ -133,35 +149,37 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
   const int depth = p.depth, K = p.K;
   const uint32_t sbase = smem_u32(smem);
   const uint32_t ring = sbase + warp * depth * kMmStage;
-  const uint32_t bars = sbase + mm_ring_bytes(depth) + warp * depth * 8;
   const int H = p.nhalves;
   const int W = gridDim.x * kMmWarps, wg = blockIdx.x * kMmWarps + warp;
   const int my_units = wg < p.nunits ? (p.nunits - wg + W - 1) / W : 0;
   const int items = my_units * H;  // (unit, 512-column stage) items of this warp, unit-major
-  if (lane == 0) {
-    for (int i = 0; i < depth; ++i) mbar_init(bars + 8 * i, 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
 
-  // Item `it` (unit wg + (it / H) W, columns 512 (it % H) ..) into slot it % depth:
-  // lanes 0 .. 4np-1 copy half-region lane & 3 (h = bit 1, v = bit 0) of panel
-  // lane >> 2, lanes 16 .. 16+np-1 the panels' scale blocks of the 4 blocks.
+  // Item `it` (unit wg + (it / H) W, columns 512 (it % H) ..) into `slot`, one
+  // commit group per item: 16-byte copies, lane-strided over the stage's 16
+  // code half-regions (row quad h, 16-column half v of each panel; 256 bytes)
+  // and its 4 scale blocks (64 bytes); panels past the matrix are skipped.
   auto issue = [&](int it, int slot) {
     const int u = wg + (it / H) * W, j = it % H;
     const int np = min(kMmPanels, p.ngroups - kMmPanels * u);
-    const uint32_t bar = bars + 8 * slot, dst = ring + slot * kMmStage;
-    if (lane == 0) mbar_expect_tx(bar, (uint32_t)np * (16 * 256 / 4 + 64));
-    __syncwarp();
+    const uint32_t dst = ring + slot * kMmStage;
     const int64_t S = (p.nhalves + 1) >> 1;
     const uint8_t* pan0 = p.panels + panel_offset((int64_t)kMmPanels * u, j >> 1, S);
     const int64_t pstride = S * kPanelBytes;  // next 8-row group, same slice
     const int half = j & 1;
-    if (lane < 4 * np)
-      bulk_g2s(dst + lane * kMmRegion, pan0 + (lane >> 2) * pstride + (lane & 3) * 512 + half * 256, 256, bar);
-    else if (lane >= 16 && lane < 16 + np)
-      bulk_g2s(dst + kMmScaleOff + (lane - 16) * kMmScalePitch,
-               pan0 + (lane - 16) * pstride + kCodeBytes + half * 64, 64, bar);
+#pragma unroll
+    for (int c = lane; c < 16 * 16 + kMmPanels * 4; c += 32) {
+      if (c < 256) {
+        const int r = c >> 4, ch = c & 15;
+        if ((r >> 2) < np)
+          cp_async16(dst + r * kMmRegion + ch * 16, pan0 + (r >> 2) * pstride + (r & 3) * 512 + half * 256 + ch * 16);
+      } else {
+        const int pi = (c - 256) >> 2, ch = c & 3;
+        if (pi < np)
+          cp_async16(dst + kMmScaleOff + pi * kMmScalePitch + ch * 16,
+                     pan0 + pi * pstride + kCodeBytes + half * 64 + ch * 16);
+      }
+    }
+    cp_async_commit();
   };
 
   const int pre = min(items, depth);
@@ -169,35 +187,48 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
   pdl_launch_dependents();
   pdl_wait();  // q, d, s (and y in add mode) are written by earlier kernels
 
-  // activation rows (zeros past M), d transposed to [block][row], and the
-  // per-128-column correction -sum_steps d s 2^-39 of each row
+  // activation rows (bulk copies; zeros past M), d transposed to [block][row],
+  // and the per-128-column correction -sum_steps d s 2^-39 of each row
   const int pitch = K + kMmRowPad, kb = K >> 5;
   uint8_t* qs = smem + mm_act_off(depth);
   float* dt = reinterpret_cast<float*>(smem + mm_dt_off(depth, K));
   float* ct = reinterpret_cast<float*>(smem + mm_ct_off(depth, K));
-  for (int i = threadIdx.x; i < 16 * (K >> 4); i += kMmThreads) {
-    const int m = i / (K >> 4), c = i - m * (K >> 4);
-    const uint4 v = m < p.M ? reinterpret_cast<const uint4*>(p.q + (size_t)m * K)[c] : make_uint4(0u, 0u, 0u, 0u);
-    *reinterpret_cast<uint4*>(qs + m * pitch + 16 * c) = v;
-  }
-  for (int i = threadIdx.x; i < 16 * kb; i += kMmThreads) {
-    const int b = i >> 4, m = i & 15;
-    dt[i] = m < p.M ? p.d[(size_t)m * kb + b] : 0.f;
-  }
-  for (int i = threadIdx.x; i < 16 * (K >> 7); i += kMmThreads) {
-    const int bb = i >> 4, m = i & 15;
-    float c = 0.f;
-    if (m < p.M) {
-      const float4 d4 = reinterpret_cast<const float4*>(p.d + (size_t)m * kb)[bb];
-      const int4 s4 = reinterpret_cast<const int4*>(p.s + (size_t)m * kb)[bb];
-      c = fmaf(d4.x * -0x1p-39f, (float)s4.x, c);
-      c = fmaf(d4.y * -0x1p-39f, (float)s4.y, c);
-      c = fmaf(d4.z * -0x1p-39f, (float)s4.z, c);
-      c = fmaf(d4.w * -0x1p-39f, (float)s4.w, c);
+  const uint32_t act_bar = sbase + mm_ring_bytes(depth) + kMmBarBytes - 8;
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_init(act_bar, 1);
+      fence_mbar_init();
+      mbar_expect_tx(act_bar, (uint32_t)(p.M * K));
     }
-    ct[i] = c;
+    __syncwarp();
+    if (lane < p.M) bulk_g2s(smem_u32(qs + lane * pitch), p.q + (size_t)lane * K, (uint32_t)K, act_bar);
   }
-  __syncthreads();
+  for (int i = threadIdx.x; i < (16 - p.M) * (K >> 4); i += kMmThreads) {
+    const int m = p.M + i / (K >> 4), c = i % (K >> 4);
+    *reinterpret_cast<uint4*>(qs + m * pitch + 16 * c) = make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll 2
+  for (int i = threadIdx.x; i < 16 * (K >> 7); i += kMmThreads) {  // one row's 4 blocks of 32 columns
+    const int m = i / (K >> 7), b4 = i % (K >> 7);
+    float4 d4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    int4 s4 = make_int4(0, 0, 0, 0);
+    if (m < p.M) {
+      d4 = reinterpret_cast<const float4*>(p.d + (size_t)m * kb)[b4];
+      s4 = reinterpret_cast<const int4*>(p.s + (size_t)m * kb)[b4];
+    }
+    dt[(4 * b4 + 0) * 16 + m] = d4.x;
+    dt[(4 * b4 + 1) * 16 + m] = d4.y;
+    dt[(4 * b4 + 2) * 16 + m] = d4.z;
+    dt[(4 * b4 + 3) * 16 + m] = d4.w;
+    float c = fmaf(d4.x * -0x1p-39f, (float)s4.x, 0.f);
+    c = fmaf(d4.y * -0x1p-39f, (float)s4.y, c);
+    c = fmaf(d4.z * -0x1p-39f, (float)s4.z, c);
+    ct[b4 * 16 + m] = fmaf(d4.w * -0x1p-39f, (float)s4.w, c);
+  }
+  __syncthreads();  // the barrier's initialisation is visible to every warp
+  // CTA-uniform: every warp either runs its items or, after a time-out, none
+  const bool failed_act = __syncthreads_or(!mbar_wait_bounded(act_bar, 0u, kMmWaitNs)) != 0;
+  if (failed_act && threadIdx.x == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
 
   const uint32_t M3 = 0x03030303u;
   const bool add = p.mode == BTF_ADD;
@@ -208,16 +239,13 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
   float2 acc[4][2];  // [row 4g + k][n-tile]: (column 2t, column 2t + 1)
 #pragma unroll
   for (int k = 0; k < 4; ++k) acc[k][0] = acc[k][1] = make_float2(0.f, 0.f);
-  int failed = -1, slot = 0, phase = 0;
+  int slot = 0;
 #pragma unroll 1
-  for (int it = 0; it < items; ++it) {
+  for (int it = 0; it < (failed_act ? 0 : items); ++it) {
     const int j = it % H;
     const int u = wg + (it / H) * W;
-    if (!mbar_wait_bounded(bars + 8 * slot, (uint32_t)phase, kMmWaitNs)) {
-      if (lane == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
-      failed = it;
-      break;
-    }
+    cp_async_wait(min(items - 1, it + depth - 1) - it);  // this item's group has landed
+    __syncwarp();  // and every lane's copies of it are visible to the warp
     const uint32_t st = ring + slot * kMmStage;
     const uint32_t code = st + (2 * g + (tig >> 1)) * kMmRegion + (tig & 1) * 8;  // + 16 per 32-column step
     const uint32_t scl = st + kMmScaleOff + (g >> 1) * kMmScalePitch + (g & 1) * 8;  // + 16 per 128 columns
@@ -225,21 +253,36 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
 #pragma unroll 1
     for (int bb = 0; bb < nb; ++bb) {
       const int gb = 4 * j + bb;  // 128-column block of the row
+      // the block's 16 MMAs first (independent), then their epilogue
+      uint2 cw[4], qv[4][2];
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        cw[ks] = lds64(code + (bb * 4 + ks) * 16);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) qv[ks][nt] = lds64(qrow0 + nt * 8 * pitch + gb * 128 + ks * 32);
+      }
+      int P[4][2][2][4];  // [step][n-tile][m-tile][fragment]
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        // m-tile 0: rows 4g (fragment row g) and 4g+1 (row g+8); m-tile 1: 4g+2, 4g+3
+        const uint32_t a0[4] = {cw[ks].x & M3, cw[ks].x & (M3 << 2), cw[ks].y & M3, cw[ks].y & (M3 << 2)};
+        const uint32_t a1[4] = {cw[ks].x & (M3 << 4), cw[ks].x & (M3 << 6), cw[ks].y & (M3 << 4),
+                                cw[ks].y & (M3 << 6)};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          mma_u8s8(P[ks][nt][0], a0, qv[ks][nt]);
+          mma_u8s8(P[ks][nt][1], a1, qv[ks][nt]);
+        }
+      }
       float2 T[4][2];
 #pragma unroll
       for (int k = 0; k < 4; ++k) T[k][0] = T[k][1] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        const uint2 cw = lds64(code + (bb * 4 + ks) * 16);
-        // m-tile 0: rows 4g (fragment row g) and 4g+1 (row g+8); m-tile 1: 4g+2, 4g+3
-        const uint32_t a0[4] = {cw.x & M3, cw.x & (M3 << 2), cw.y & M3, cw.y & (M3 << 2)};
-        const uint32_t a1[4] = {cw.x & (M3 << 4), cw.x & (M3 << 6), cw.y & (M3 << 4), cw.y & (M3 << 6)};
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-          const uint2 qv = lds64(qrow0 + nt * 8 * pitch + gb * 128 + ks * 32);
-          int d0[4], d1[4];
-          mma_u8s8(d0, a0, qv);
-          mma_u8s8(d1, a1, qv);
+          const int(&d0)[4] = P[ks][nt][0];
+          const int(&d1)[4] = P[ks][nt][1];
           if constexpr (DUMP) {
             const int r0 = 32 * u + 4 * g, blk = gb * 4 + ks;
             const int pv[4][2] = {{d0[0], d0[1]}, {d0[2], d0[3]}, {d1[0], d1[1]}, {d1[2], d1[3]}};
@@ -254,32 +297,32 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
               }
           } else {
             const float2 dv = lds64f(dt0 + (gb * 4 + ks) * 64 + nt * 32);
-            T[0][nt] = ffma2(dv, mm_x<0>(d0[0], d0[1]), T[0][nt]);
-            T[1][nt] = ffma2(dv, mm_x<1>(d0[2], d0[3]), T[1][nt]);
-            T[2][nt] = ffma2(dv, mm_x<2>(d1[0], d1[1]), T[2][nt]);
-            T[3][nt] = ffma2(dv, mm_x<3>(d1[2], d1[3]), T[3][nt]);
+            T[0][nt] = ffma2(dv, mm_x(d0[0], d0[1]), T[0][nt]);
+            T[1][nt] = ffma2(dv, mm_x(d0[2], d0[3]), T[1][nt]);
+            T[2][nt] = ffma2(dv, mm_x(d1[0], d1[1]), T[2][nt]);
+            T[3][nt] = ffma2(dv, mm_x(d1[2], d1[3]), T[3][nt]);
           }
         }
       }
       if constexpr (!DUMP) {
         const uint2 sc = lds64(scl + bb * 16);  // fp16 scales of rows 4g .. 4g+3, this block
+        // T of row k holds 4^k times the block sum: acc += scale 2^39 4^-k T + scale 2^39 corr
         const float w[4] = {h2f_bits(sc.x & 0xffffu) * 0x1p39f, h2f_bits(sc.x >> 16) * 0x1p39f,
                             h2f_bits(sc.y & 0xffffu) * 0x1p39f, h2f_bits(sc.y >> 16) * 0x1p39f};
+        const float wk[4] = {w[0], w[1] * 0x1p-2f, w[2] * 0x1p-4f, w[3] * 0x1p-6f};
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const float2 cv = lds64f(ct0 + gb * 64 + nt * 32);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            acc[k][nt] = ffma2(make_float2(w[k], w[k]), __fadd2_rn(T[k][nt], cv), acc[k][nt]);
+            acc[k][nt] = ffma2(make_float2(w[k], w[k]), cv,
+                               ffma2(make_float2(wk[k], wk[k]), T[k][nt], acc[k][nt]));
         }
       }
     }
     __syncwarp();  // every lane's reads of the slot are done
     if (it + depth < items) issue(it + depth, slot);
-    if (++slot == depth) {
-      slot = 0;
-      phase ^= 1;
-    }
+    if (++slot == depth) slot = 0;
     if (j == H - 1) {  // the unit's last stage: rows 32u + 4g .. +3
       if constexpr (!DUMP) {
         const int r0 = 32 * u + 4 * g;
@@ -311,11 +354,10 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
       for (int k = 0; k < 4; ++k) acc[k][0] = acc[k][1] = make_float2(0.f, 0.f);
     }
   }
-  if (failed >= 0) {  // leave no copy of this warp in flight into shared memory (bounded)
-    const int last = min(items, failed + depth);
-    for (int it = failed; it < last; ++it)
-      mbar_wait_bounded(bars + 8 * (it % depth), (uint32_t)((it / depth) & 1), kMmWaitNs / 10);
-  }
+  // leave no copy in flight into shared memory: this warp's skipped items
+  // (after an activation time-out) and, bounded, the activation copy
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  if (failed_act && threadIdx.x == 0) mbar_wait_bounded(act_bar, 0u, kMmWaitNs / 10);
   stamp_end(p.stamp);
 }
 
