@@ -849,7 +849,7 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
     return fail(BTF_ERR_ARG, "btf_gemv: activation pointers null or misaligned (q needs 16 B)");
   // A batch of rows is a dense contraction: instead of the reference's repeated
   // small-batch passes over the weights (kernels.cu:805-821), store / add calls
-  // go to the MMA kernels (d 16-byte aligned): 5..16 rows over very large
+  // go to the MMA kernels (d 16-byte aligned): 3..16 rows over very large
   // matrices (an lm_head) to the warp-MMA kernel, 9..64 rows over large
   // matrices to the tcgen05 weight-major kernel (one weight pass each), 64
   // rows and more to the 128-row tcgen05 GEMM.

@@ -70,7 +70,7 @@ constexpr int kMmMaxDepth = 4;
 constexpr int kMmBarBytes = 512;  // the activation copy's barrier (last 8 bytes)
 constexpr int kMmRowPad = 32;     // activation row pitch K + 32 bytes
 constexpr int kMmMaxM = 16;
-constexpr int kMmMinM = 5;  // btf_gemv / btf_gemm route 5 <= M <= 16 here (mma_serves)
+constexpr int kMmMinM = 3;  // btf_gemv / btf_gemm route 3 <= M <= 16 here (mma_serves)
 constexpr int kMmMaxK = 8192;
 constexpr uint64_t kMmWaitNs = 1000000000ull;
 constexpr int kMmBias = 1 << 20;
@@ -98,7 +98,7 @@ struct MmParams {
 
 // D = A (16 x 32, u8, row) * B (32 x 8, s8, col) + C (every element kMmBias), int32
 __device__ __forceinline__ void mma_u8s8(int (&dd)[4], const uint32_t (&a)[4], uint2 b) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%10, %10, %10, %10};"
       : "=r"(dd[0]), "=r"(dd[1]), "=r"(dd[2]), "=r"(dd[3])
@@ -120,15 +120,8 @@ __device__ __forceinline__ void cp_async_wait(int n) {
   }
 }
 
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ float2 lds64f(uint32_t addr) {
-  const uint2 v = lds64(addr);
-  return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
-}
+__device__ __forceinline__ uint2 ld8(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ float2 ld8f(const float* p) { return *reinterpret_cast<const float2*>(p); }
 
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 as_f2(int x, int y) { return make_float2(__int_as_float(x), __int_as_float(y)); }
@@ -233,9 +226,10 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
   const uint32_t M3 = 0x03030303u;
   const bool add = p.mode == BTF_ADD;
   const bool vec = ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0) && (p.ldy & 3) == 0;
-  const uint32_t qrow0 = sbase + mm_act_off(depth) + g * pitch + tig * 8;  // + 8 pitch for n-tile 1
-  const uint32_t dt0 = sbase + mm_dt_off(depth, K) + 8 * tig;              // + 64 b + 32 nt
-  const uint32_t ct0 = sbase + mm_ct_off(depth, K) + 8 * tig;              // + 64 gb + 32 nt
+  const uint8_t* qrow0 = smem + mm_act_off(depth) + g * pitch + tig * 8;  // + 8 pitch for n-tile 1
+  const float* dt0 = dt + 2 * tig;                                          // + 16 b + 8 nt
+  const float* ct0 = ct + 2 * tig;                                          // + 16 gb + 8 nt
+  const uint8_t* ringp = smem + warp * depth * kMmStage;
   float2 acc[4][2];  // [row 4g + k][n-tile]: (column 2t, column 2t + 1)
 #pragma unroll
   for (int k = 0; k < 4; ++k) acc[k][0] = acc[k][1] = make_float2(0.f, 0.f);
@@ -246,9 +240,9 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
     const int u = wg + (it / H) * W;
     cp_async_wait(min(items - 1, it + depth - 1) - it);  // this item's group has landed
     __syncwarp();  // and every lane's copies of it are visible to the warp
-    const uint32_t st = ring + slot * kMmStage;
-    const uint32_t code = st + (2 * g + (tig >> 1)) * kMmRegion + (tig & 1) * 8;  // + 16 per 32-column step
-    const uint32_t scl = st + kMmScaleOff + (g >> 1) * kMmScalePitch + (g & 1) * 8;  // + 16 per 128 columns
+    const uint8_t* st = ringp + slot * kMmStage;
+    const uint8_t* code = st + (2 * g + (tig >> 1)) * kMmRegion + (tig & 1) * 8;  // + 16 per 32-column step
+    const uint8_t* scl = st + kMmScaleOff + (g >> 1) * kMmScalePitch + (g & 1) * 8;  // + 16 per 128 columns
     const int nb = min(4, (K >> 7) - 4 * j);
 #pragma unroll 1
     for (int bb = 0; bb < nb; ++bb) {
@@ -257,9 +251,9 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
       uint2 cw[4], qv[4][2];
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        cw[ks] = lds64(code + (bb * 4 + ks) * 16);
+        cw[ks] = ld8(code + (bb * 4 + ks) * 16);
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) qv[ks][nt] = lds64(qrow0 + nt * 8 * pitch + gb * 128 + ks * 32);
+        for (int nt = 0; nt < 2; ++nt) qv[ks][nt] = ld8(qrow0 + nt * 8 * pitch + gb * 128 + ks * 32);
       }
       int P[4][2][2][4];  // [step][n-tile][m-tile][fragment]
 #pragma unroll
@@ -296,7 +290,7 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
                       ((pv[k][c] - kMmBias) >> (2 * k)) - p.s[(size_t)m * kb + blk];
               }
           } else {
-            const float2 dv = lds64f(dt0 + (gb * 4 + ks) * 64 + nt * 32);
+            const float2 dv = ld8f(dt0 + (gb * 4 + ks) * 16 + nt * 8);
             T[0][nt] = ffma2(dv, mm_x(d0[0], d0[1]), T[0][nt]);
             T[1][nt] = ffma2(dv, mm_x(d0[2], d0[3]), T[1][nt]);
             T[2][nt] = ffma2(dv, mm_x(d1[0], d1[1]), T[2][nt]);
@@ -305,14 +299,14 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
         }
       }
       if constexpr (!DUMP) {
-        const uint2 sc = lds64(scl + bb * 16);  // fp16 scales of rows 4g .. 4g+3, this block
+        const uint2 sc = ld8(scl + bb * 16);  // fp16 scales of rows 4g .. 4g+3, this block
         // T of row k holds 4^k times the block sum: acc += scale 2^39 4^-k T + scale 2^39 corr
         const float w[4] = {h2f_bits(sc.x & 0xffffu) * 0x1p39f, h2f_bits(sc.x >> 16) * 0x1p39f,
                             h2f_bits(sc.y & 0xffffu) * 0x1p39f, h2f_bits(sc.y >> 16) * 0x1p39f};
         const float wk[4] = {w[0], w[1] * 0x1p-2f, w[2] * 0x1p-4f, w[3] * 0x1p-6f};
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-          const float2 cv = lds64f(ct0 + gb * 64 + nt * 32);
+          const float2 cv = ld8f(ct0 + gb * 16 + nt * 8);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             acc[k][nt] = ffma2(make_float2(w[k], w[k]), cv,
@@ -372,8 +366,9 @@ int gemv_mma_setup(DeviceInfo& d) {
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemv_mma_kernel)");
 }
 
-// Dispatch rule of btf_gemv / btf_gemm: 5 <= M <= 16 rows (at most 4 the GEMV
-// reads the weights once and is faster) with K <= 8192, over a matrix with at
+// Dispatch rule of btf_gemv / btf_gemm: 3 <= M <= 16 rows (for 1 or 2 rows the
+// GEMV's dp4a pass is faster; from 3 rows on its time doubles) with K <= 8192,
+// over a matrix with at
 // least two 32-row units per warp of the device (fewer leave SMs idle, where
 // the weight-major kernel or the GEMV passes are as fast); q, d and s 16-byte
 // aligned.

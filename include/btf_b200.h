@@ -138,7 +138,7 @@ int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float ep
  * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
  * segments (gate, up) with the same N. K % 128 == 0. Store / add calls with d
- * 16-byte aligned run on the tensor cores: 5 <= M <= 16 with K <= 8192 as
+ * 16-byte aligned run on the tensor cores: 3 <= M <= 16 with K <= 8192 as
  * btf_gemv_mma when every segment has at least 2 * 8 * (SM count) 32-row units
  * (an lm_head; q, d, s 16-byte aligned), else 9 <= M <= 64 as btf_gemm_wm when
  * every segment has at least 2/3 as many 128-row tiles as the device has SMs
