@@ -1029,7 +1029,8 @@ def only_kernel(args):
             torch.cuda.synchronize()
             print(f"decode: {args.iters} eager steps, last token {t}, device error {btf.device_error()}")
         return
-    if args.only == "lmhead16":  # config 4's lm_head, batch 16, through btf_gemv (routed to btf_gemm_wm)
+    if args.only in ("lmhead16", "lmhead16wm"):  # config 4's lm_head, batch 16: btf_gemv (routed to
+        # btf_gemv_mma), or the tcgen05 weight-major kernel called directly
         _, K, N = synth.LM_HEAD
         M = 16
         base = torch.from_numpy(synth.ternary_ptq(N // 16, K, seed=7)).to(dev)
@@ -1038,10 +1039,11 @@ def only_kernel(args):
         del src, base
         act = btf.quant_q8(torch.from_numpy(synth.activations(M, K, seed=8)).to(dev))
         y = torch.empty((M, N), device=dev)
+        launch = btf.launch_gemm_wm if args.only == "lmhead16wm" else btf.launch_gemv
         for i in range(args.iters):
-            btf.launch_gemv([(mats[i % 2], y, N)], K, M, act, btf.STORE)
+            launch([(mats[i % 2], y, N)], K, M, act, btf.STORE)
         torch.cuda.synchronize()
-        print(json.dumps({"kernel": "lmhead16", "iters": args.iters, "device_error": btf.device_error()}))
+        print(json.dumps({"kernel": args.only, "iters": args.iters, "device_error": btf.device_error()}))
         return
     if args.only == "gemm":  # one prefill GEMM: M=512, K=5120 -> N=17408
         M, K, N = 512, 5120, 17408
@@ -1089,10 +1091,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm", "lmhead16", "decode", "load"],
+    ap.add_argument("--only", choices=["qkv", "o", "gateup", "down", "gemm", "lmhead16", "lmhead16wm", "decode",
+                                       "load"],
                     help="profile mode: one kernel kind, (lmhead16) config 4's lm_head at batch 16 through "
-                         "btf_gemv (the weight-major GEMM), (decode) eager config-3 decode steps, or (load) "
-                         "config 3 from a GGUF file into panels")
+                         "btf_gemv (the warp-MMA GEMM), (lmhead16wm) the same on the weight-major tcgen05 GEMM, "
+                         "(decode) eager config-3 decode steps, or (load) config 3 from a GGUF file into panels")
     ap.add_argument("--layers", type=int, default=64, help="--only load: layers of the config-3 model")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--fused", type=int, default=0, help="--only: 1 = btf_gemv_f32 (quantise inside the GEMV)")
