@@ -737,13 +737,18 @@ def lm_head_sharded(btf, torch, dev, world, rank, reps=10, replays=3):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         us = float(t.item()) * 1e3 / (replays * reps)
         nbytes = btf.panel_bytes(N, K) + M * (K + K // 32 * 8) + M * N * 4
-        wm = M >= 9 and -(-r.n // 128) >= torch.cuda.get_device_properties(dev).multi_processor_count * 2 // 3
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        # the routing rules of btf_gemv_gather (mma_serves, wm_serves)
+        mma = 3 <= M <= 16 and K <= btf.GEMV_MMA_MAX_K and -(-r.n // 32) >= sms * 8
+        wm = not mma and M >= 9 and -(-r.n // 128) >= sms * 2 // 3
         err = btf.device_error()
         out[f"M{M}"] = {"us": us, "GB/s": nbytes / (us * 1e-6) / 1e9,
                         "GB/s_per_gpu": nbytes / world / (us * 1e-6) / 1e9,
                         "frac_of_hbm_per_gpu": nbytes / world / (us * 1e-6) / 1e9 / peak,
-                        "bytes_per_launch": nbytes, "weight_passes": 1 if wm else -(-M // btf.gemv_max_nb(K)),
-                        "path": "btf_gemv_gather -> " + ("gemm_wm_kernel (weight-major tcgen05, tagged stores)"
+                        "bytes_per_launch": nbytes,
+                        "weight_passes": 1 if mma or wm else -(-M // btf.gemv_max_nb(K)),
+                        "path": "btf_gemv_gather -> " + ("gemv_mma_kernel (warp int8 MMA, tagged stores)" if mma
+                                                         else "gemm_wm_kernel (weight-major tcgen05, tagged stores)"
                                                          if wm else "gemv_kernel (tagged stores)"),
                         "device_error_word": err}
         del g

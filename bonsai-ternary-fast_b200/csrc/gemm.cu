@@ -481,7 +481,7 @@ int gemm_setup(DeviceInfo& d) {
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
 bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
 int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
-                 int32_t* idot);
+                 int32_t* idot, const btf_gather* g, int gseg);
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
                 int32_t* idot, const btf_gather* g, int gseg);
 
@@ -577,7 +577,8 @@ extern "C" int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8
   // per segment: a small batch over a very large matrix goes to the warp-MMA
   // kernel, over many weight tiles to the weight-major kernel
   for (int i = 0; i < nseg; ++i) {
-    const int rc = mma_serves(segs[i], K, M, act) ? run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)
+    const int rc = mma_serves(segs[i], K, M, act)
+                       ? run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, nullptr, 0)
                    : wm_serves(segs[i], M, act)
                        ? run_gemm_wm(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, nullptr, 0)
                        : run_gemm(segs[i], K, M, act, mode, (cudaStream_t)stream);

@@ -831,6 +831,8 @@ int gemv_setup(DeviceInfo& d) {
 // warp-MMA small-batch GEMM's rule (gemv_mma.cu)
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
 bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
+int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
+                 int32_t* idot, const btf_gather* g, int gseg);
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
                 int32_t* idot, const btf_gather* g, int gseg);
 
@@ -890,9 +892,16 @@ int btf_gemv_gather(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act 
   for (int s = 0; s < nout; ++s)
     if (g->peer_y[s][g->rank] != segs[s].y)
       return fail(BTF_ERR_ARG, "btf_gemv_gather: peer_y[%d][rank] must be segs[%d].y", s, s);
-  // tagged store calls over large shards: the weight-major tcgen05 GEMM, one weight pass
+  // tagged store calls over large shards: the warp-MMA GEMM (3..16 rows over
+  // lm_head-size shards) or the weight-major tcgen05 GEMM, one weight pass
   if (g->tagged && mode == BTF_STORE && aligned(act.d, 16)) {
-    bool wm = true;
+    bool mma = true, wm = true;
+    for (int i = 0; i < nseg; ++i) mma = mma && mma_serves(segs[i], K, M, act);
+    if (mma) {
+      for (int i = 0; i < nseg; ++i)
+        if (int rc = run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, g, i)) return rc;
+      return BTF_OK;
+    }
     for (int i = 0; i < nseg; ++i) wm = wm && wm_serves(segs[i], M, act);
     if (wm) {
       for (int i = 0; i < nseg; ++i)

@@ -94,6 +94,13 @@ struct MmParams {
   int32_t* idot;  // dump form: idot[m][n][K/32], no y
   int* err;
   unsigned long long* stamp;
+  // GATHER form (tagged N-sharded store): every output goes to all `world`
+  // ranks' buffers as a 64-bit word (fp32 bits | tag << 32) at the same index
+  // as y; tag = *epoch * 1024 + site
+  int world;
+  unsigned long long* peer[BTF_MAX_RANKS];
+  const unsigned* epoch;
+  int site;
 };
 
 // D = A (16 x 32, u8, row) * B (32 x 8, s8, col) + C (every element kMmBias), int32
@@ -133,8 +140,9 @@ __device__ __forceinline__ float2 mm_x(int p0, int p1) {
   return ffma2(as_f2(p0, p1), make_float2(0x1p110f, 0x1p110f), make_float2(-0x1p-19f, -0x1p-19f));
 }
 
-// DUMP writes the exact idot of every (row, activation row, block) instead of y.
-template <bool DUMP>
+// DUMP writes the exact idot of every (row, activation row, block) instead of
+// y; GATHER stores tagged words into every rank's buffer (store mode).
+template <bool DUMP, bool GATHER = false>
 __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_constant__ MmParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -222,6 +230,8 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
   // CTA-uniform: every warp either runs its items or, after a time-out, none
   const bool failed_act = __syncthreads_or(!mbar_wait_bounded(act_bar, 0u, kMmWaitNs)) != 0;
   if (failed_act && threadIdx.x == 0) atomicCAS(p.err, 0, kErrWaitTimeout);
+  // the epoch is advanced in stream order: read after griddepcontrol.wait
+  const unsigned long long tag = GATHER ? (unsigned long long)(*p.epoch * 1024u + (unsigned)p.site) << 32 : 0ull;
 
   const uint32_t M3 = 0x03030303u;
   const bool add = p.mode == BTF_ADD;
@@ -329,6 +339,14 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
             float v[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) v[k] = c ? acc[k][nt].y : acc[k][nt].x;
+            if constexpr (GATHER) {  // one single-copy-atomic 64-bit word per output and rank
+              const int64_t idx = (int64_t)m * p.ldy + r0;
+              for (int r = 0; r < p.world; ++r)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  if (r0 + k < p.N) p.peer[r][idx + k] = (unsigned long long)__float_as_uint(v[k]) | tag;
+              continue;
+            }
             float* dst = p.y + (int64_t)m * p.ldy + r0;
             if (vec && r0 + 3 < p.N) {
               float4 o = make_float4(v[0], v[1], v[2], v[3]);
@@ -363,26 +381,28 @@ int gemv_mma_setup(DeviceInfo& d) {
   cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gemv_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemv_mma_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemv_mma_kernel)");
 }
 
-// Dispatch rule of btf_gemv / btf_gemm: 3 <= M <= 16 rows (for 1 or 2 rows the
-// GEMV's dp4a pass is faster; from 3 rows on its time doubles) with K <= 8192,
-// over a matrix with at
-// least two 32-row units per warp of the device (fewer leave SMs idle, where
-// the weight-major kernel or the GEMV passes are as fast); q, d and s 16-byte
-// aligned.
+// Dispatch rule of btf_gemv / btf_gemm / btf_gemv_gather: 3 <= M <= 16 rows
+// (for 1 or 2 rows the GEMV's dp4a pass is faster; from 3 rows on its time
+// doubles) with K <= 8192, over a matrix with at least one 32-row unit per warp
+// of the device (fewer leave SMs idle, where the weight-major kernel or the
+// GEMV passes are as fast); q, d and s 16-byte aligned.
 bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act) {
   const DeviceInfo* dev = current_device();
   return dev && M >= kMmMinM && M <= kMmMaxM && K > 0 && K % 128 == 0 && K <= kMmMaxK && act.q && act.d && act.s &&
          (reinterpret_cast<uintptr_t>(act.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(act.d) & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(act.s) & 15) == 0 &&
-         (groups_of(seg.N) + kMmPanels - 1) / kMmPanels >= 2 * dev->sm_count * kMmWarps;
+         (groups_of(seg.N) + kMmPanels - 1) / kMmPanels >= dev->sm_count * kMmWarps;
 }
 
-// One segment, 1 <= M <= kMmMaxM, K <= kMmMaxK; idot != nullptr runs the dump form.
+// One segment, 1 <= M <= kMmMaxM, K <= kMmMaxK; idot != nullptr runs the dump
+// form; g != null (tagged, store mode) stores segment `gseg` into every rank's buffer.
 int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
-                 int32_t* idot) {
+                 int32_t* idot, const btf_gather* g, int gseg) {
   const DeviceInfo* dev = current_device();
   if (!dev) return BTF_ERR_STATE;
   MmParams p{};
@@ -402,6 +422,12 @@ int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, in
   p.idot = idot;
   p.err = dev->err_word;
   p.stamp = take_stamp();
+  if (g) {
+    p.world = g->world;
+    for (int r = 0; r < g->world; ++r) p.peer[r] = reinterpret_cast<unsigned long long*>(g->peer_y[gseg][r]);
+    p.epoch = g->epoch;
+    p.site = g->site;
+  }
   // the deepest ring that fits beside this K's activation tables
   const int limit = mm_smem(2, kMmMaxK);
   p.depth = 2;
@@ -409,7 +435,8 @@ int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, in
   const size_t smem = (size_t)mm_smem(p.depth, K);
   const int grid = std::max(1, std::min(dev->sm_count, (p.nunits + kMmWarps - 1) / kMmWarps));
   const cudaError_t e = idot ? launch_pdl(gemv_mma_kernel<true>, dim3(grid), dim3(kMmThreads), smem, st, p)
-                             : launch_pdl(gemv_mma_kernel<false>, dim3(grid), dim3(kMmThreads), smem, st, p);
+                        : g    ? launch_pdl(gemv_mma_kernel<false, true>, dim3(grid), dim3(kMmThreads), smem, st, p)
+                               : launch_pdl(gemv_mma_kernel<false>, dim3(grid), dim3(kMmThreads), smem, st, p);
   return e == cudaSuccess ? launch_status("gemv_mma_kernel") : cuda_fail(e, "gemv_mma_kernel launch");
 }
 
@@ -439,7 +466,7 @@ extern "C" int btf_gemv_mma(const btf_gemv_seg* segs, int nseg, int K, int M, bt
         segs[i].ldy < segs[i].N)
       return fail(BTF_ERR_ARG, "btf_gemv_mma: segment %d has a bad panel buffer, N, y or ldy", i);
   for (int i = 0; i < nseg; ++i)
-    if (int rc = run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr)) return rc;
+    if (int rc = run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, nullptr, 0)) return rc;
   return BTF_OK;
 }
 
@@ -450,5 +477,5 @@ extern "C" int btf_gemv_mma_idot(const void* panels, int N, int K, int M, btf_q8
     return fail(BTF_ERR_ARG, "btf_gemv_mma_idot: bad arguments (M <= %d, K %% 128 up to %d, q, d, s 16-byte aligned)",
                 kMmMaxM, kMmMaxK);
   const btf_gemv_seg seg{panels, N, nullptr, N};
-  return run_gemv_mma(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot);
+  return run_gemv_mma(seg, K, M, act, BTF_STORE, (cudaStream_t)stream, idot, nullptr, 0);
 }

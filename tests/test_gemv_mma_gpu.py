@@ -181,8 +181,8 @@ def test_gemv_mma_segments(cuda, btf, orc):
 @pytest.mark.gpu
 @pytest.mark.parametrize("M", [3, 8, 16])
 def test_gemv_and_gemm_route_lm_head_batches_here(cuda, btf, orc, M):
-    # btf_gemv and btf_gemm hand 3 <= M <= 16 rows over a matrix with two 32-row
-    # units per warp of the device to the warp-MMA kernel: bit for bit its output,
+    # btf_gemv and btf_gemm hand 3 <= M <= 16 rows over a matrix with at least one
+    # 32-row unit per warp of the device to the warp-MMA kernel: bit for bit its output,
     # and within the bar of the oracle on a subset of rows
     import torch
 
