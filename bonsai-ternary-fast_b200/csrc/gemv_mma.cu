@@ -341,10 +341,22 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
             for (int k = 0; k < 4; ++k) v[k] = c ? acc[k][nt].y : acc[k][nt].x;
             if constexpr (GATHER) {  // one single-copy-atomic 64-bit word per output and rank
               const int64_t idx = (int64_t)m * p.ldy + r0;
-              for (int r = 0; r < p.world; ++r)
+              unsigned long long wv[4];
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  if (r0 + k < p.N) p.peer[r][idx + k] = (unsigned long long)__float_as_uint(v[k]) | tag;
+              for (int k = 0; k < 4; ++k) wv[k] = (unsigned long long)__float_as_uint(v[k]) | tag;
+              for (int r = 0; r < p.world; ++r) {
+                unsigned long long* dst = p.peer[r] + idx;
+                if ((p.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(p.peer[r]) & 15) == 0 && r0 + 3 < p.N) {
+                  // two 16-byte stores of two words each (each word single-copy atomic): the 8
+                  // lanes of a row quad column write 256 contiguous bytes per activation row
+                  asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(wv[0]), "l"(wv[1]) : "memory");
+                  asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(wv[2]), "l"(wv[3]) : "memory");
+                } else {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    if (r0 + k < p.N) dst[k] = wv[k];
+                }
+              }
               continue;
             }
             float* dst = p.y + (int64_t)m * p.ldy + r0;
