@@ -100,6 +100,10 @@ __global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_cons
   }
   pdl_launch_dependents();
   pdl_wait();  // x is written by the previous kernel
+  // this thread's first span column (and its own-order column for xn), loaded
+  // before the norm pass so that both reads of x are in flight together
+  const float x0 = own ? xr[src0] : 0.f;
+  const float xo0 = own && a.xn_out ? xr[og0] : 0.f;
   float scale = 1.0f;
   if constexpr (NORM) {
     double acc = 0.0;
@@ -128,12 +132,12 @@ __global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_cons
   for (int o = threadIdx.x; o < a.S; o += nthr) {
     const bool first = o == (int)threadIdx.x;  // the prefetched column
     const int og = base + o, src = first ? src0 : src_of(og);
-    float v = xr[src];
+    float v = first ? x0 : xr[src];
     if constexpr (NORM) v = __fmul_rn(__fmul_rn(v, scale), first ? w0 : a.normw[src]);
     if (a.signs) v = __fmul_rn(v, first ? sg0 : a.signs[og]);
     buf[o] = v;
     if (a.xn_out) {
-      float u = xr[og];
+      float u = first ? xo0 : xr[og];
       if constexpr (NORM) u = __fmul_rn(__fmul_rn(u, scale), first ? wo0 : a.normw[og]);
       a.xn_out[(size_t)m * a.ldxn + og] = u;
     }
