@@ -72,8 +72,8 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 }
 
 template <bool NORM>
-__global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_constant__ PrepParams a) {
-  extern __shared__ float buf[];  // [S]
+__global__ void __launch_bounds__(kPrepMaxThreads, 1) prep_kernel(const __grid_constant__ PrepParams a) {
+  extern __shared__ float buf[];  // [S + S / 32]
   __shared__ double red[kPrepMaxThreads / 32];
   const int nthr = blockDim.x, nwarp = nthr >> 5;
   const int m = blockIdx.y, base = blockIdx.x * a.S;
@@ -128,6 +128,53 @@ __global__ void __launch_bounds__(kPrepMaxThreads) prep_kernel(const __grid_cons
     for (int w = 0; w < nwarp; ++w) tot += red[w];
     const float mean = (float)(tot / (double)a.n);
     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+  }
+  if (a.S == 1024 && nthr == 1024) {
+    // One column per thread (column e = threadIdx.x of the span, warp c holds
+    // 32c .. 32c+31): the butterflies of length 1 .. 16 run on registers
+    // (shuffles), then one padded transpose through shared memory gives thread
+    // (c, l) column 32 l + c, so the lengths 32 .. 512 are shuffles too; the
+    // transpose back leaves each warp its own 32-column Q8 block. Same stage
+    // order and (a + b, a - b) pairs as below, 2 barriers instead of 7.
+    float v = x0;
+    if constexpr (NORM) v = __fmul_rn(__fmul_rn(v, scale), w0);
+    if (a.signs) v = __fmul_rn(v, sg0);
+    const int og = base + (int)threadIdx.x;
+    if (a.xn_out) {
+      float u = xo0;
+      if constexpr (NORM) u = __fmul_rn(__fmul_rn(u, scale), wo0);
+      a.xn_out[(size_t)m * a.ldxn + og] = u;
+    }
+    if (a.block > 1) {
+      const int lim = min(a.block, 32);
+      for (int len = 1; len < lim; len <<= 1) {
+        const float p = __shfl_xor_sync(0xffffffffu, v, len);
+        v = (lane & len) ? __fsub_rn(p, v) : __fadd_rn(v, p);
+      }
+      if (a.block > 32) {
+        buf[threadIdx.x + warp] = v;  // column e at e + e / 32: conflict-free both ways
+        __syncthreads();
+        float t = buf[33 * lane + warp];  // column 32 lane + warp
+        for (int k = 1; 32 * k < a.block; k <<= 1) {  // length 32 k
+          const float p = __shfl_xor_sync(0xffffffffu, t, k);
+          t = (lane & k) ? __fsub_rn(p, t) : __fadd_rn(t, p);
+        }
+        buf[33 * lane + warp] = t;
+        __syncthreads();
+        v = buf[threadIdx.x + warp];
+      }
+      v = __fmul_rn(v, __fdiv_rn(1.0f, __fsqrt_rn((float)a.block)));
+    }
+    float dq;
+    int sum;
+    const int qv = q8_warp(v, dq, sum);
+    a.q[(size_t)m * a.n + og] = (int8_t)qv;
+    if (lane == 0) {
+      const size_t bi = (size_t)m * (a.n / 32) + (base / 32 + warp);
+      a.d[bi] = dq;
+      a.s[bi] = sum;
+    }
+    return;
   }
   for (int o = threadIdx.x; o < a.S; o += nthr) {
     const bool first = o == (int)threadIdx.x;  // the prefetched column
@@ -211,7 +258,7 @@ extern "C" int btf_prep(const float* x, int ldx, int M, int n, const float* norm
   PrepParams p{x, ldx, n, S, normw, eps, hx.block, hx.perm_hd, hx.perm_nk, hx.perm_rep, hx.signs, xn_out, ldxn,
                act.q, act.d, act.s};
   const dim3 grid(n / S, M);
-  const size_t smem = (size_t)S * sizeof(float);
+  const size_t smem = (size_t)(S + S / 32) * sizeof(float);  // padded for the one-column-per-thread transpose
   const int threads = std::max(kPrepThreads, S);  // S <= 1024: one thread per column of the span
   const cudaError_t e = normw ? launch_pdl(prep_kernel<true>, grid, dim3(threads), smem, (cudaStream_t)stream, p)
                               : launch_pdl(prep_kernel<false>, grid, dim3(threads), smem, (cudaStream_t)stream, p);
