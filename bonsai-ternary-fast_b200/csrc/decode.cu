@@ -52,6 +52,30 @@ __device__ double block_sum(double v, double* red) {
   return s;
 }
 
+// Two block sums at once, in block_sum's order, with one barrier: red must hold
+// 2 x 32 doubles and must not be read by an unfinished earlier reduction (the
+// caller alternates buffers, or a barrier lies between).
+__device__ void block_sum2(double& a, double& b, double* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    red[w] = a;
+    red[32 + w] = b;
+  }
+  __syncthreads();
+  double sa = 0.0, sb = 0.0;
+  for (int i = 0; i < nw; ++i) {
+    sa += red[i];
+    sb += red[32 + i];
+  }
+  a = sa;
+  b = sb;
+}
+
 // bd::rmsnorm (cpu_ops.cpp:116-122): double sum of squares, float mean,
 // 1/sqrt(mean + eps) in float.
 __device__ __forceinline__ float rms_scale(double sumsq, int n, float eps) {
@@ -142,7 +166,9 @@ struct GdnParams {
 };
 __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   extern __shared__ float sm[];  // q[DK], k[DK], v[DV], out[DV]
-  __shared__ double red[32];
+  // reduction buffers, used in turn: each is rewritten only after a barrier
+  // that follows every read of its previous use
+  __shared__ double red[2][64];
   float* q = sm;
   float* k = sm + p.DK;
   float* vv = sm + 2 * p.DK;
@@ -183,8 +209,7 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
 #pragma unroll 4
     for (int i = tid + kPre * blockDim.x; i < n4; i += blockDim.x) dot(a4[i], b4[i], x4[i]);
   }
-  sa = block_sum(sa, red);
-  sb = block_sum(sb, red);
+  block_sum2(sa, sb, red[0]);
   const float bt = sigmoidf_((float)sb);
   const float decay = expf(__fmul_rn(softplus(__fadd_rn((float)sa, p.dt[h])), p.a[h]));
   // conv + silu of the head's channels
@@ -209,16 +234,11 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
     sq += (double)q[i] * q[i];
     sk += (double)k[i] * k[i];
   }
-  sq = block_sum(sq, red);
-  sk = block_sum(sk, red);
+  block_sum2(sq, sk, red[1]);
+  // the l2-normalised q and k (x * (1 / max(norm, eps)), rounded as the
+  // emulator's stored values) are formed where they are read below
   const float iq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), p.eps));
   const float ik = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), p.eps));
-  __syncthreads();
-  for (int i = tid; i < p.DK; i += blockDim.x) {
-    q[i] = __fmul_rn(q[i], iq);
-    k[i] = __fmul_rn(k[i], ik);
-  }
-  __syncthreads();
   const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)p.DK));
   // thread (j, part) holds floats i = 16 t + 4 part + {0..3} of column j (DK <= 128)
   const int j = tid / kTpc, part = tid % kTpc;
@@ -229,10 +249,13 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   const float vj = vv[j];
   float4 st[8];
   float kv = 0.f;
+  auto nrm = [](float4 x, float s) {
+    return make_float4(__fmul_rn(x.x, s), __fmul_rn(x.y, s), __fmul_rn(x.z, s), __fmul_rn(x.w, s));
+  };
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     if (t < nt) {
-      const float4 c = col[t * kTpc], kk = k4[t * kTpc];
+      const float4 c = col[t * kTpc], kk = nrm(k4[t * kTpc], ik);
       st[t] = make_float4(__fmul_rn(c.x, decay), __fmul_rn(c.y, decay), __fmul_rn(c.z, decay), __fmul_rn(c.w, decay));
       kv = __fadd_rn(kv, __fmul_rn(st[t].x, kk.x));
       kv = __fadd_rn(kv, __fmul_rn(st[t].y, kk.y));
@@ -247,7 +270,7 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     if (t < nt) {
-      const float4 kk = k4[t * kTpc], qq = q4[t * kTpc];
+      const float4 kk = nrm(k4[t * kTpc], ik), qq = nrm(q4[t * kTpc], iq);
       float4 c = st[t];
       c.x = __fadd_rn(c.x, __fmul_rn(kk.x, dl));
       c.y = __fadd_rn(c.y, __fmul_rn(kk.y, dl));
@@ -265,9 +288,9 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   if (part == 0) ov[j] = __fmul_rn(acc, qscale);
   __syncthreads();
   // bd::rmsnorm over the head's DV outputs with ssm_norm, then * silu(z)
-  double ss = 0.0;
+  double ss = 0.0, unused = 0.0;
   for (int i = tid; i < p.DV; i += blockDim.x) ss += (double)ov[i] * ov[i];
-  ss = block_sum(ss, red);
+  block_sum2(ss, unused, red[0]);
   const float sc = rms_scale(ss, p.DV, p.eps);
   for (int i = tid; i < p.DV; i += blockDim.x) {
     const float y = __fmul_rn(__fmul_rn(ov[i], sc), p.norm_w[i]);
