@@ -190,6 +190,15 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   }
   pdl_launch_dependents();
   pdl_wait();  // xn, qkv, z and the ring come from earlier kernels
+  // thread (j, part) holds floats i = 16 t + 4 part + {0..3} of state column j
+  // (DK <= 128); its part of the state is loaded now, so that the read is in
+  // flight during the dots, the conv and the norms below
+  const int j = tid / kTpc, part = tid % kTpc;
+  const int nt = p.DK / (4 * kTpc);
+  float4* col = reinterpret_cast<float4*>(p.state + ((int64_t)h * p.DV + j) * p.DK) + part;
+  float4 st[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) st[t] = t < nt ? col[t * kTpc] : make_float4(0.f, 0.f, 0.f, 0.f);
   // alpha / beta dots
   double sa = 0.0, sb = 0.0;
   {
@@ -240,14 +249,9 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   const float iq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), p.eps));
   const float ik = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), p.eps));
   const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)p.DK));
-  // thread (j, part) holds floats i = 16 t + 4 part + {0..3} of column j (DK <= 128)
-  const int j = tid / kTpc, part = tid % kTpc;
-  const int nt = p.DK / (4 * kTpc);
-  float4* col = reinterpret_cast<float4*>(p.state + ((int64_t)h * p.DV + j) * p.DK) + part;
   const float4* k4 = reinterpret_cast<const float4*>(k) + part;
   const float4* q4 = reinterpret_cast<const float4*>(q) + part;
   const float vj = vv[j];
-  float4 st[8];
   float kv = 0.f;
   auto nrm = [](float4 x, float s) {
     return make_float4(__fmul_rn(x.x, s), __fmul_rn(x.y, s), __fmul_rn(x.z, s), __fmul_rn(x.w, s));
@@ -255,7 +259,7 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
     if (t < nt) {
-      const float4 c = col[t * kTpc], kk = nrm(k4[t * kTpc], ik);
+      const float4 c = st[t], kk = nrm(k4[t * kTpc], ik);
       st[t] = make_float4(__fmul_rn(c.x, decay), __fmul_rn(c.y, decay), __fmul_rn(c.z, decay), __fmul_rn(c.w, decay));
       kv = __fadd_rn(kv, __fmul_rn(st[t].x, kk.x));
       kv = __fadd_rn(kv, __fmul_rn(st[t].y, kk.y));
