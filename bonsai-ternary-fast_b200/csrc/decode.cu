@@ -110,6 +110,31 @@ __global__ void embed_kernel(const uint8_t* __restrict__ pan, int V, int E, int 
     return;
   }
   // bd::hadamard_inverse (cpu_ops.cpp:109-114): fwht of the block, * 1/sqrt(blk), then signs
+  if (n == 1024) {
+    // the same butterflies in the same order with 2 barriers: lengths 1 .. 16 in
+    // shuffles (warp c holds columns 32c .. 32c+31), a padded transpose (column
+    // 32 l + c to thread (c, l)) for lengths 32 .. 512, and back
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int len = 1; len < 32; len <<= 1) {
+      const float q = __shfl_xor_sync(0xffffffffu, v, len);
+      v = (lane & len) ? __fsub_rn(q, v) : __fadd_rn(v, q);
+    }
+    sh[threadIdx.x + w] = v;
+    __syncthreads();
+    float t = sh[33 * lane + w];
+    for (int k2 = 1; k2 < 32; k2 <<= 1) {
+      const float q = __shfl_xor_sync(0xffffffffu, t, k2);
+      t = (lane & k2) ? __fsub_rn(q, t) : __fadd_rn(t, q);
+    }
+    sh[33 * lane + w] = t;
+    __syncthreads();
+    if (e < E) {
+      float o = __fmul_rn(sh[threadIdx.x + w], __fdiv_rn(1.0f, __fsqrt_rn((float)n)));
+      if (signs) o = __fmul_rn(o, signs[e]);
+      x[e] = o;
+    }
+    return;
+  }
   sh[threadIdx.x] = v;
   __syncthreads();
   for (int len = 1; len < n; len <<= 1) {
@@ -560,7 +585,8 @@ __global__ void fill_uniform_kernel(float* __restrict__ x, int64_t n, uint64_t s
 cudaError_t launch_embed(const uint8_t* pan, int V, int E, const int32_t* tok, int blk, const float* signs, float* x,
                          cudaStream_t st) {
   const int n = blk ? blk : 256;
-  return launch_pdl(embed_kernel, dim3((E + n - 1) / n), dim3(n), blk ? blk * sizeof(float) : 0, st, pan, V, E,
+  return launch_pdl(embed_kernel, dim3((E + n - 1) / n), dim3(n), blk ? (blk + blk / 32) * sizeof(float) : 0, st,
+                    pan, V, E,
                     (int)slices_of(E), tok, blk, signs, x);
 }
 cudaError_t launch_gdn_mix(const GdnArgs& g, cudaStream_t st) {
