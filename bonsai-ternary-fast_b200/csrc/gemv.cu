@@ -281,6 +281,40 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
   }
   pdl_wait();
   if constexpr (GATHER == 2) tag = *p.gather.epoch * 1024u + (unsigned)p.gather.site;
+  // Add mode: the current y of the rows a lane will write is loaded when their
+  // unit starts, so the read-modify-write at the unit's end does not wait on
+  // it (only the unit's owner writes those rows). G = 1: lanes 4r hold row r of
+  // the warp's current unit (the reduce_rows8 map); G > 1: the combining lane
+  // (row lane & 7, activation row lane >> 3) of the warp's unit.
+  constexpr bool kPreY = MODE == BTF_ADD && !DUMP;
+  float ypre[NB];
+#pragma unroll
+  for (int m = 0; m < NB; ++m) ypre[m] = 0.0f;
+  auto prefetch_y = [&](int uix) {  // G = 1: unit first + uix * stride
+    if (uix >= n_units || (lane & 3) != 0) return;
+    int seg, g;
+    locate(first + uix * stride, seg, g);
+    const int n = seg == 0 ? p.n0 : seg == 1 ? p.n1 : p.n2;
+    const int ldy = seg == 0 ? p.ld0 : seg == 1 ? p.ld1 : p.ld2;
+    const float* y = seg == 0 ? p.y0 : seg == 1 ? p.y1 : p.y2;
+    const int row = g * kRows + (lane >> 2);
+#pragma unroll
+    for (int m = 0; m < NB; ++m)
+      if (row < n && m < p.nb) ypre[m] = get(y, (int64_t)(p.m0 + m) * ldy + row);
+  };
+  if constexpr (kPreY) {
+    if (G == 1) {
+      prefetch_y(0);
+    } else if (has_work && part == 0) {
+      int seg, g;
+      locate(first, seg, g);
+      const int n = seg == 0 ? p.n0 : seg == 1 ? p.n1 : p.n2;
+      const int ldy = seg == 0 ? p.ld0 : seg == 1 ? p.ld1 : p.ld2;
+      const float* y = seg == 0 ? p.y0 : seg == 1 ? p.y1 : p.y2;
+      const int r = lane & 7, m = lane >> 3, row = g * kRows + r;
+      if (m < NB && row < n && m < p.nb) ypre[0] = get(y, (int64_t)(p.m0 + m) * ldy + row);
+    }
+  }
   // The activation is read next (few KB, L2-resident); the rest of the ring is
   // started once those loads are in flight.
   auto start_ring = [&]() {
@@ -533,11 +567,14 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
             if (row < n && m < p.nb) {
               const int64_t idx = (int64_t)(p.m0 + m) * ldy + row;
               if constexpr (MODE == BTF_STORE) put(seg, y, idx, v[0]);
-              else if constexpr (MODE == BTF_ADD) put(seg, y, idx, get(y, idx) + v[0]);
+              else if constexpr (MODE == BTF_ADD) put(seg, y, idx, (kPreY ? ypre[m] : get(y, idx)) + v[0]);
               else put(seg, y, idx, silu(v[0]) * up);
             }
           }
         }
+      }
+      if constexpr (kPreY) {
+        if (G == 1) prefetch_y(ui);  // the next unit's rows
       }
     }
   }
@@ -561,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, BTF_GEMV_MINB) gemv_kernel(const __g
         if (row < n && m < p.nb) {
           const int64_t idx = (int64_t)(p.m0 + m) * ldy + row;
           if constexpr (MODE == BTF_STORE) put(seg, y, idx, sg);
-          else if constexpr (MODE == BTF_ADD) put(seg, y, idx, get(y, idx) + sg);
+          else if constexpr (MODE == BTF_ADD) put(seg, y, idx, (kPreY ? ypre[0] : get(y, idx)) + sg);
           else put(seg, y, idx, silu(sg) * su);
         }
       }
