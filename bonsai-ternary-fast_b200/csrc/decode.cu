@@ -213,8 +213,10 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
     ap[u] = i < n4 ? a4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     bp[u] = i < n4 ? b4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  const float nw0 = tid < p.DV ? p.norm_w[tid] : 0.f;  // the output norm weight (a constant)
   pdl_launch_dependents();
   pdl_wait();  // xn, qkv, z and the ring come from earlier kernels
+  const float z0 = tid < p.DV ? p.z[(int64_t)h * p.DV + tid] : 0.f;  // read early, used last
   // thread (j, part) holds floats i = 16 t + 4 part + {0..3} of state column j
   // (DK <= 128); its part of the state is loaded now, so that the read is in
   // flight during the dots, the conv and the norms below
@@ -322,8 +324,9 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   block_sum2(ss, unused, red[0]);
   const float sc = rms_scale(ss, p.DV, p.eps);
   for (int i = tid; i < p.DV; i += blockDim.x) {
-    const float y = __fmul_rn(__fmul_rn(ov[i], sc), p.norm_w[i]);
-    p.o[(int64_t)h * p.DV + i] = __fmul_rn(y, silu(p.z[(int64_t)h * p.DV + i]));
+    const bool first = i == tid;
+    const float y = __fmul_rn(__fmul_rn(ov[i], sc), first ? nw0 : p.norm_w[i]);
+    p.o[(int64_t)h * p.DV + i] = __fmul_rn(y, silu(first ? z0 : p.z[(int64_t)h * p.DV + i]));
   }
 }
 
