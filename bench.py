@@ -840,9 +840,9 @@ def decode_config3(btf, torch, dev, steps=64, warmup=8, n_ctx=4096, world=1, ran
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                         "peak_source": peak_src, "per": "GPU"},
            "e2e": {"value": 1e3 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-           # per token: 9 launches per delta-net layer (prep + GEMV x 4, the mixer), 11 per
-           # attention layer (3 attention kernels), embed, final prep, lm_head, 2 argmax stages
-           "gpu_launches_per_token": 9 * n_gdn + 11 * (CONFIG3["n_layer"] - n_gdn) + 5, "n_gdn_layers": n_gdn,
+           # per token: 9 launches per layer (prep + GEMV x 4, the mixer or the one attention
+           # kernel), embed, final prep, lm_head, 2 argmax stages
+           "gpu_launches_per_token": 9 * CONFIG3["n_layer"] + 5, "n_gdn_layers": n_gdn,
            "device_error_word": err, "path": "btf_decoder_run: one graph replay per token"}
     torch.cuda.synchronize()
     if world > 1:

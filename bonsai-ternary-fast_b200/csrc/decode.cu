@@ -7,10 +7,9 @@
 //   embed_kernel      packed token_embd row -> inverse transform   (:175-183)
 //   gdn_mix_kernel    per v-head: alpha / beta dots, causal conv +
 //                     SiLU, gated delta rule, gated RMSNorm         (:235-298)
-//   attn_prep_kernel  q/k RMSNorm, partial RoPE, fp16 KV write      (:307-338)
-//   attn_split_kernel / attn_combine_kernel
-//                     softmax attention over the fp16 KV cache in
-//                     key splits, then the sigmoid gate             (:339-372)
+//   attn_fused_kernel q/k RMSNorm, partial RoPE, fp16 KV write      (:307-338)
+//                     and softmax attention over the fp16 KV cache
+//                     in key splits, then the sigmoid gate          (:339-372)
 //   argmax kernels    greedy token, lowest index on ties            (:214-217)
 // The decode position lives in device memory, so one captured graph serves
 // every token. Every kernel is launched with programmatic dependent launch:
@@ -330,92 +329,118 @@ __global__ void gdn_mix_kernel(const __grid_constant__ GdnParams p) {
   }
 }
 
-// ------------------------------------------------------------------ attention prep
-// CTA per head: blockIdx.x < H are q heads (rows h*2D .. of qf), the rest k
-// heads. D threads. RMSNorm with q_norm / k_norm, then RoPE on the first R
-// dims at position *pos: theta_0 = pos, theta_{i+1} = theta_i * base^(-2/R)
-// (in float, as the emulator), pairs (i, i + R/2). q is rounded to fp16 when
-// round_q; k and v go to the fp16 cache row pos.
-__global__ void attn_prep_kernel(const float* __restrict__ qf, const float* __restrict__ kin,
-                                 const float* __restrict__ vin, const float* __restrict__ qn,
-                                 const float* __restrict__ kn, int H, int HK, int D, int R, float theta_scale,
-                                 float eps, const int32_t* __restrict__ pos_p, int round_q, float* __restrict__ qout,
-                                 __half* __restrict__ kc, __half* __restrict__ vc) {
-  extern __shared__ float hv[];
-  __shared__ double red[32];
-  pdl_launch_dependents();
-  pdl_wait();
-  const int b = blockIdx.x, i = threadIdx.x;
-  const bool isq = b < H;
-  const int hh = isq ? b : b - H;
-  const float* src = isq ? qf + (int64_t)hh * 2 * D : kin + (int64_t)hh * D;
-  const float* w = isq ? qn : kn;
-  const float xv = i < D ? src[i] : 0.f;
-  double ss = block_sum(i < D ? (double)xv * xv : 0.0, red);
+constexpr int kAttnWarps = 4;  // fewest warps of an attention CTA
+
+// ------------------------------------------------------------------ attention, one launch
+// The step's attention of one layer in one launch. Grid (H, splits), T
+// threads (T >= D, a multiple of 32). CTA (h, sp):
+//   - q of head h: RMSNorm with q_norm, then RoPE on the first R dims at
+//     position *pos (theta_0 = pos, theta_{i+1} = theta_i * base^(-2/R) in
+//     float, as the emulator; pairs (i, i + R/2)), rounded to fp16 when
+//     round_q, into shared memory;
+//   - the CTA whose key range holds *pos also forms k (the same with k_norm)
+//     and v of kv-head g, rounded to fp16, writes them to cache row *pos and
+//     takes key *pos from shared memory (the CTAs of the kv-head's other q-heads
+//     write the same values; no CTA reads that cache row from global memory);
+//   - split sp covers keys [sp * chunk, min((sp + 1) * chunk, pos + 1)); warp w
+//     walks every (T/32)-th key: a lane-sliced dot q.k (D/32 dims per lane),
+//     then an online softmax with its running max / sum and V accumulator; the
+//     warps are merged into part[h][sp] = (max, sum, acc[D]);
+//   - the last CTA of head h to finish (a per-head counter; the writers fence
+//     before they count) combines the splits,
+//     o = (sum_s acc_s e^{m_s - M}) / (sum_s l_s e^{m_s - M}) * sigmoid(gate),
+//     and resets the counter for the next launch.
+struct AttnParams {
+  const float *qf, *kin, *vin, *qn, *kn;
+  int H, HK, D, R;
+  float theta_scale, eps, scale;
+  const int32_t* pos;
+  int round_q, chunk;
+  __half *kc, *vc;
+  float* part;
+  int* cnt;
+  float* o;
+};
+
+// out[i] = rope(rmsnorm(x) * w)[i] for i < D (RoPE on the first R dims at
+// position pos, pairs (i, i + R/2)); hv: D floats of scratch. Ends with a barrier.
+__device__ void attn_norm_rope(const float* __restrict__ x, const float* __restrict__ w, int D, int R, float eps,
+                               float theta_scale, int pos, float* hv, float* out, double* red) {
+  const int i = threadIdx.x;
+  const float xv = i < D ? x[i] : 0.f;
+  const double ss = block_sum(i < D ? (double)xv * xv : 0.0, red);
   const float sc = rms_scale(ss, D, eps);
   if (i < D) hv[i] = __fmul_rn(__fmul_rn(xv, sc), w[i]);
   __syncthreads();
-  const int p = *pos_p;
-  float outv = i < D ? hv[i] : 0.f;
-  if (i < R) {
-    const int ic = i < R / 2 ? i : i - R / 2;
-    float theta = (float)p;
-    for (int t = 0; t < ic; ++t) theta = __fmul_rn(theta, theta_scale);
-    const float c = cosf(theta), s = sinf(theta);
-    const float x0 = hv[ic], x1 = hv[ic + R / 2];
-    outv = i < R / 2 ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)) : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  if (i < D) {
+    float outv = hv[i];
+    if (i < R) {
+      const int ic = i < R / 2 ? i : i - R / 2;
+      float theta = (float)pos;
+      for (int t = 0; t < ic; ++t) theta = __fmul_rn(theta, theta_scale);
+      const float c = cosf(theta), s = sinf(theta);
+      const float x0 = hv[ic], x1 = hv[ic + R / 2];
+      outv = i < R / 2 ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)) : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
+    out[i] = outv;
   }
-  if (i >= D) return;
-  const int64_t kvw = (int64_t)HK * D;
-  if (isq) {
-    qout[(int64_t)hh * D + i] = round_q ? __half2float(__float2half_rn(outv)) : outv;
-  } else {
-    kc[(int64_t)p * kvw + (int64_t)hh * D + i] = __float2half_rn(outv);
-    vc[(int64_t)p * kvw + (int64_t)hh * D + i] = __float2half_rn(vin[(int64_t)hh * D + i]);
-  }
+  __syncthreads();
 }
 
-// ------------------------------------------------------------------ attention
-// Grid (H, splits): split s covers keys [s*chunk, min((s+1)*chunk, pos+1)).
-// Each of the 4 warps walks every 4th key: lane-sliced dot q.k (D/32 dims per
-// lane), then an online softmax with its running max / sum and V accumulator.
-// The CTA merges its warps and writes (max, sum, acc[D]) for the split.
-constexpr int kAttnWarps = 4;
-__global__ void attn_split_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                                  const __half* __restrict__ vc, int H, int HK, int D, int chunk, float scale,
-                                  const int32_t* __restrict__ pos_p, float* __restrict__ part) {
-  extern __shared__ float sm[];  // q[D], then per warp: m, l, acc[D]
+__global__ void attn_fused_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ float sm[];  // q[D], k[D], v[D], scratch[D], per warp: m, l, acc[D]
+  __shared__ double red[32];
+  __shared__ int is_last;
   pdl_launch_dependents();
   pdl_wait();
-  const int h = blockIdx.x, sp = blockIdx.y, lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
-  const int g = h / (H / HK), T = *pos_p + 1;
-  const int t0 = sp * chunk, t1 = min(t0 + chunk, T);
+  const int D = p.D, h = blockIdx.x, sp = blockIdx.y, tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  const int nw = blockDim.x >> 5;
+  const int g = h / (p.H / p.HK), pos = *p.pos, T = pos + 1;
+  const int t0 = sp * p.chunk, t1 = min(t0 + p.chunk, T);
+  const bool mine = t0 <= pos && pos < t1;  // this split holds the new key (CTA-uniform)
   float* qs = sm;
-  float* wm = sm + D + wp * (D + 2);
-  for (int i = threadIdx.x; i < D; i += blockDim.x) qs[i] = q[(int64_t)h * D + i];
+  float* ks = sm + D;
+  float* vs = sm + 2 * D;
+  float* hv = sm + 3 * D;
+  attn_norm_rope(p.qf + (int64_t)h * 2 * D, p.qn, D, p.R, p.eps, p.theta_scale, pos, hv, qs, red);
+  if (p.round_q && tid < D) qs[tid] = __half2float(__float2half_rn(qs[tid]));
+  const int64_t kvw = (int64_t)p.HK * D;
+  if (mine) {
+    attn_norm_rope(p.kin + (int64_t)g * D, p.kn, D, p.R, p.eps, p.theta_scale, pos, hv, ks, red);
+    if (tid < D) {
+      const __half kh = __float2half_rn(ks[tid]), vh = __float2half_rn(p.vin[(int64_t)g * D + tid]);
+      ks[tid] = __half2float(kh);
+      vs[tid] = __half2float(vh);
+      p.kc[(int64_t)pos * kvw + (int64_t)g * D + tid] = kh;
+      p.vc[(int64_t)pos * kvw + (int64_t)g * D + tid] = vh;
+    }
+  }
   __syncthreads();
+  // the key range: online softmax per warp
+  float* wm = sm + 4 * D + wp * (D + 2);
   const int per = D / 32;
   float m = -INFINITY, l = 0.f;
   float acc[8];  // D <= 256
 #pragma unroll
   for (int r = 0; r < 8; ++r) acc[r] = 0.f;
-  const int64_t kvw = (int64_t)HK * D;
-  for (int t = t0 + wp; t < t1; t += kAttnWarps) {
-    const __half* kt = kc + (int64_t)t * kvw + (int64_t)g * D;
+  for (int t = t0 + wp; t < t1; t += nw) {
+    const bool fresh = t == pos;  // the new key, from shared memory
+    const __half* kt = p.kc + (int64_t)t * kvw + (int64_t)g * D;
     float dd = 0.f;
 #pragma unroll
     for (int r = 0; r < 8; ++r)
-      if (r < per) dd = fmaf(qs[lane * per + r], __half2float(kt[lane * per + r]), dd);
+      if (r < per)
+        dd = fmaf(qs[lane * per + r], fresh ? ks[lane * per + r] : __half2float(kt[lane * per + r]), dd);
 #pragma unroll
     for (int o = 16; o; o >>= 1) dd += __shfl_xor_sync(0xffffffffu, dd, o);
-    const float s = dd * scale;
-    const float mn = fmaxf(m, s);
-    const float cf = expf(m - mn), pf = expf(s - mn);
+    const float sc = dd * p.scale;
+    const float mn = fmaxf(m, sc);
+    const float cf = expf(m - mn), pf = expf(sc - mn);
     l = l * cf + pf;
-    const __half* vt = vc + (int64_t)t * kvw + (int64_t)g * D;
+    const __half* vt = p.vc + (int64_t)t * kvw + (int64_t)g * D;
 #pragma unroll
     for (int r = 0; r < 8; ++r)
-      if (r < per) acc[r] = fmaf(pf, __half2float(vt[lane * per + r]), acc[r] * cf);
+      if (r < per) acc[r] = fmaf(pf, fresh ? vs[lane * per + r] : __half2float(vt[lane * per + r]), acc[r] * cf);
     m = mn;
   }
   if (lane == 0) {
@@ -426,45 +451,48 @@ __global__ void attn_split_kernel(const float* __restrict__ q, const __half* __r
   for (int r = 0; r < 8; ++r)
     if (r < per) wm[2 + lane * per + r] = acc[r];
   __syncthreads();
-  // merge the warps
-  float* out = part + ((int64_t)h * gridDim.y + sp) * (D + 2);
-  float M = -INFINITY;
-  for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm[D + w * (D + 2)]);
-  for (int i = threadIdx.x; i < D + 2; i += blockDim.x) {
-    float v = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float* ww = sm + D + w * (D + 2);
-      const float f = ww[0] == -INFINITY ? 0.f : expf(ww[0] - M);
-      if (i == 1) v += ww[1] * f;
-      else if (i >= 2) v += ww[i] * f;
+  // merge the warps into this split's partial
+  float* out = p.part + ((int64_t)h * gridDim.y + sp) * (D + 2);
+  {
+    float M = -INFINITY;
+    for (int w = 0; w < nw; ++w) M = fmaxf(M, sm[4 * D + w * (D + 2)]);
+    for (int i = tid; i < D + 2; i += blockDim.x) {
+      float v = 0.f;
+      for (int w = 0; w < nw; ++w) {
+        const float* ww = sm + 4 * D + w * (D + 2);
+        const float f = ww[0] == -INFINITY ? 0.f : expf(ww[0] - M);
+        if (i == 1) v += ww[1] * f;
+        else if (i >= 2) v += ww[i] * f;
+      }
+      out[i] = i == 0 ? M : v;
     }
-    out[i] = i == 0 ? M : v;
   }
-}
-
-// CTA per head: o = (sum_s acc_s e^{m_s - M}) / (sum_s l_s e^{m_s - M}) * sigmoid(gate).
-__global__ void attn_combine_kernel(const float* __restrict__ part, int splits, int D, const float* __restrict__ qf,
-                                    float* __restrict__ o) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int h = blockIdx.x;
-  const float* ph = part + (int64_t)h * splits * (D + 2);
+  // the last CTA of head h combines the splits
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(p.cnt + h, 1) == (int)gridDim.y - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const int splits = gridDim.y;
+  const float* ph = p.part + (int64_t)h * splits * (D + 2);  // other CTAs' writes: read past L1 (__ldcg)
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, ph[(int64_t)s * (D + 2)]);
+  for (int s2 = 0; s2 < splits; ++s2) M = fmaxf(M, __ldcg(ph + (int64_t)s2 * (D + 2)));
   float L = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float ms = ph[(int64_t)s * (D + 2)];
-    if (ms != -INFINITY) L += ph[(int64_t)s * (D + 2) + 1] * expf(ms - M);
+  for (int s2 = 0; s2 < splits; ++s2) {
+    const float ms = __ldcg(ph + (int64_t)s2 * (D + 2));
+    if (ms != -INFINITY) L += __ldcg(ph + (int64_t)s2 * (D + 2) + 1) * expf(ms - M);
   }
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+  for (int i = tid; i < D; i += blockDim.x) {
     float a = 0.f;
-    for (int s = 0; s < splits; ++s) {
-      const float ms = ph[(int64_t)s * (D + 2)];
-      if (ms != -INFINITY) a += ph[(int64_t)s * (D + 2) + 2 + i] * expf(ms - M);
+    for (int s2 = 0; s2 < splits; ++s2) {
+      const float ms = __ldcg(ph + (int64_t)s2 * (D + 2));
+      if (ms != -INFINITY) a += __ldcg(ph + (int64_t)s2 * (D + 2) + 2 + i) * expf(ms - M);
     }
-    const float gate = qf[(int64_t)h * 2 * D + D + i];
-    o[(int64_t)h * D + i] = a / L * sigmoidf_(gate);
+    const float gate = p.qf[(int64_t)h * 2 * D + D + i];
+    p.o[(int64_t)h * D + i] = a / L * sigmoidf_(gate);
   }
+  if (tid == 0) p.cnt[h] = 0;
 }
 
 // ------------------------------------------------------------------ argmax
@@ -598,22 +626,15 @@ cudaError_t launch_gdn_mix(const GdnArgs& g, cudaStream_t st) {
   return launch_pdl(gdn_mix_kernel, dim3(g.NV), dim3(g.DV * kTpc), (size_t)(2 * g.DK + 2 * g.DV) * sizeof(float), st,
                     p);
 }
-cudaError_t launch_attn_prep(const float* qf, const float* k, const float* v, const float* qn, const float* kn, int H,
-                             int HK, int D, int R, float theta_scale, float eps, const int32_t* pos, int round_q,
-                             float* qout, void* kc, void* vc, cudaStream_t st) {
-  const int threads = (D + 31) / 32 * 32;
-  return launch_pdl(attn_prep_kernel, dim3(H + HK), dim3(threads), D * sizeof(float), st, qf, k, v, qn, kn, H, HK, D,
-                    R, theta_scale, eps, pos, round_q, qout, static_cast<__half*>(kc), static_cast<__half*>(vc));
-}
-cudaError_t launch_attention(const float* q, const void* kc, const void* vc, const float* qf, int H, int HK, int D,
-                             int n_ctx, int splits, const int32_t* pos, float* part, float* o, cudaStream_t st) {
-  const int chunk = (n_ctx + splits - 1) / splits;
-  const float scale = 1.0f / sqrtf((float)D);
-  if (cudaError_t e = launch_pdl(attn_split_kernel, dim3(H, splits), dim3(kAttnWarps * 32),
-                                 (D + kAttnWarps * (D + 2)) * sizeof(float), st, q, static_cast<const __half*>(kc),
-                                 static_cast<const __half*>(vc), H, HK, D, chunk, scale, pos, part))
-    return e;
-  return launch_pdl(attn_combine_kernel, dim3(H), dim3(128), 0, st, static_cast<const float*>(part), splits, D, qf, o);
+cudaError_t launch_attention_fused(const float* qf, const float* k, const float* v, const float* qn, const float* kn,
+                                   int H, int HK, int D, int R, float theta_scale, float eps, const int32_t* pos,
+                                   int round_q, void* kc, void* vc, int n_ctx, int splits, float* part, int* cnt,
+                                   float* o, cudaStream_t st) {
+  const int threads = (D + 31) / 32 * 32 > kAttnWarps * 32 ? (D + 31) / 32 * 32 : kAttnWarps * 32;
+  AttnParams p{qf, k, v, qn, kn, H, HK, D, R, theta_scale, eps, 1.0f / sqrtf((float)D), pos, round_q,
+               (n_ctx + splits - 1) / splits, static_cast<__half*>(kc), static_cast<__half*>(vc), part, cnt, o};
+  const size_t smem = (size_t)(4 * D + (threads / 32) * (D + 2)) * sizeof(float);
+  return launch_pdl(attn_fused_kernel, dim3(H, splits), dim3(threads), smem, st, p);
 }
 cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, int32_t* out, int32_t* tok_next,
                           int32_t* pos, cudaStream_t st) {

@@ -30,15 +30,16 @@ struct GdnArgs {
   int NV;
 };
 cudaError_t launch_gdn_mix(const GdnArgs& args, cudaStream_t st);
-// q/k RMSNorm + RoPE at *pos; q -> qout[H*D] (fp16-rounded when round_q), k and v
-// -> fp16 caches [n_ctx][HK*D] row *pos.
-cudaError_t launch_attn_prep(const float* qf, const float* k, const float* v, const float* qn, const float* kn, int H,
-                             int HK, int D, int R, float theta_scale, float eps, const int32_t* pos, int round_q,
-                             float* qout, void* kc, void* vc, cudaStream_t st);
-// Softmax attention of H q-heads over keys 0..*pos of the fp16 caches, in
-// `splits` key ranges (part: [H][splits][D + 2] floats), times sigmoid(gate) -> o[H*D].
-cudaError_t launch_attention(const float* q, const void* kc, const void* vc, const float* qf, int H, int HK, int D,
-                             int n_ctx, int splits, const int32_t* pos, float* part, float* o, cudaStream_t st);
+// The attention of one layer at position *pos, one launch: q/k RMSNorm + RoPE
+// (q fp16-rounded when round_q), k and v into row *pos of the fp16 caches
+// [n_ctx][HK*D], softmax attention of the H q-heads over keys 0..*pos in
+// `splits` key ranges (part: [H][splits][D + 2] floats), combined by each
+// head's last CTA, times sigmoid(gate) -> o[H*D]. cnt: H ints, zero before the
+// first launch (each launch leaves them zero).
+cudaError_t launch_attention_fused(const float* qf, const float* k, const float* v, const float* qn, const float* kn,
+                                   int H, int HK, int D, int R, float theta_scale, float eps, const int32_t* pos,
+                                   int round_q, void* kc, void* vc, int n_ctx, int splits, float* part, int* cnt,
+                                   float* o, cudaStream_t st);
 // Greedy argmax of x[n] (lowest index on ties) -> *out; also *tok_next = token and
 // *pos += 1 when those are non-null. pv/pi: `parts` partials.
 cudaError_t launch_argmax(const float* x, int n, float* pv, int* pi, int parts, int32_t* out, int32_t* tok_next,

@@ -83,6 +83,7 @@ struct Decoder {
   // step buffers
   float *x = nullptr, *xn = nullptr, *bA = nullptr, *bB = nullptr, *bC = nullptr, *bO = nullptr, *bQ = nullptr,
         *bG = nullptr, *logits = nullptr, *part = nullptr, *amax_v = nullptr;
+  int* attn_cnt = nullptr;  // per-head split counters of the attention launch (zero between launches)
   int* amax_i = nullptr;
   int8_t* aq = nullptr;
   float* ad = nullptr;
@@ -187,6 +188,9 @@ int make_buffers(Decoder& D) {
     for (int i = 0; i < 9; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
   D.peers[D.rank] = D.arena;
   D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
+  D.attn_cnt = D.alloc<int>((size_t)std::max(1, H), &rc);
+  if (!rc && !D.dry && cudaMemset(D.attn_cnt, 0, sizeof(int) * std::max(1, H)) != cudaSuccess)
+    return fail(BTF_ERR_CUDA, "btf_decoder: counter clear");
   D.amax_v = D.alloc<float>(Decoder::kArgmaxParts, &rc);
   D.amax_i = D.alloc<int>(Decoder::kArgmaxParts, &rc);
   D.aq = D.alloc<int8_t>((size_t)R * D.Kmax, &rc);
@@ -293,10 +297,9 @@ int enqueue_step(Decoder& D) {
     } else {
       BTF_TRY(prep(D, D.x, E, l.attn_norm, l.wq.hx, nullptr));
       BTF_TRY(gemv(D, {{&l.wq, D.bA}, {&l.wk, D.bB}, {&l.wv, D.bC}}, E, BTF_STORE));
-      BTF_TRYC(launch_attn_prep(D.bA, D.bB, D.bC, l.q_norm, l.k_norm, H, HK, HD, d.n_rot, D.theta_scale, d.rms_eps,
-                                D.d_pos, D.o.round_q_f16, D.bQ, l.kc, l.vc, D.st));
-      BTF_TRYC(launch_attention(D.bQ, l.kc, l.vc, D.bA, H, HK, HD, D.o.n_ctx, D.o.attn_splits, D.d_pos, D.part, D.bO,
-                                D.st));
+      BTF_TRYC(launch_attention_fused(D.bA, D.bB, D.bC, l.q_norm, l.k_norm, H, HK, HD, d.n_rot, D.theta_scale,
+                                      d.rms_eps, D.d_pos, D.o.round_q_f16, l.kc, l.vc, D.o.n_ctx, D.o.attn_splits,
+                                      D.part, D.attn_cnt, D.bO, D.st));
       BTF_TRY(prep(D, D.bO, H * HD, nullptr, l.wo.hx, nullptr));
       BTF_TRY(gemv(D, {{&l.wo, D.x}}, H * HD, BTF_ADD));
     }
@@ -345,11 +348,10 @@ int enqueue_chunk(Decoder& D, int M) {
       BTF_TRY(gemv(D, {{&l.wq, D.bA}, {&l.wk, D.bB}, {&l.wv, D.bC}}, E, BTF_STORE, M));
       for (int m = 0; m < M; ++m) {
         const float* qf = D.bA + (size_t)m * NQ;
-        BTF_TRYC(launch_attn_prep(qf, D.bB + (size_t)m * NK, D.bC + (size_t)m * NV, l.q_norm, l.k_norm, H, HK, HD,
-                                  d.n_rot, D.theta_scale, d.rms_eps, D.d_ppos + m, D.o.round_q_f16, D.bQ, l.kc, l.vc,
-                                  D.st));
-        BTF_TRYC(launch_attention(D.bQ, l.kc, l.vc, qf, H, HK, HD, D.o.n_ctx, D.o.attn_splits, D.d_ppos + m, D.part,
-                                  D.bO + (size_t)m * HO, D.st));
+        BTF_TRYC(launch_attention_fused(qf, D.bB + (size_t)m * NK, D.bC + (size_t)m * NV, l.q_norm, l.k_norm, H, HK,
+                                        HD, d.n_rot, D.theta_scale, d.rms_eps, D.d_ppos + m, D.o.round_q_f16, l.kc,
+                                        l.vc, D.o.n_ctx, D.o.attn_splits, D.part, D.attn_cnt,
+                                        D.bO + (size_t)m * HO, D.st));
       }
       BTF_TRY(prep(D, D.bO, HO, nullptr, l.wo.hx, nullptr, M));
       BTF_TRY(gemv(D, {{&l.wo, D.x}}, HO, BTF_ADD, M));

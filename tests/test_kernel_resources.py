@@ -40,5 +40,5 @@ def test_every_kernel_has_no_stack_and_no_spills():
 def test_hot_path_kernels_are_in_the_build():
     text = "".join(_logs().values())
     for kernel in ("gemv_kernel", "gemm_kernel", "quant_q8_kernel", "prep_kernel", "repack_panels_kernel",
-                   "gdn_mix_kernel", "attn_split_kernel"):
+                   "gdn_mix_kernel", "attn_fused_kernel"):
         assert re.search(rf"Compiling entry function '\S*{kernel}\S*' for 'sm_100a'", text), kernel
