@@ -747,7 +747,9 @@ def lm_head_sharded(btf, torch, dev, world, rank, reps=10, replays=3):
         nbytes = btf.panel_bytes(N, K) + M * (K + K // 32 * 8) + M * N * 4
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
         # the routing rules of btf_gemv_gather (mma_serves, wm_serves)
-        mma = 3 <= M <= 16 and K <= btf.GEMV_MMA_MAX_K and -(-r.n // 32) >= sms * 8
+        units = -(-r.n // 32)
+        mma = K <= btf.GEMV_MMA_MAX_K and ((9 <= M <= 16 and units >= sms) or (5 <= M <= 8 and units >= 2 * sms)
+                                           or (3 <= M <= 4 and units >= 8 * sms))
         wm = not mma and M >= 9 and -(-r.n // 128) >= sms * 2 // 3
         err = btf.device_error()
         out[f"M{M}"] = {"us": us, "GB/s": nbytes / (us * 1e-6) / 1e9,

@@ -70,7 +70,7 @@ constexpr int kMmMaxDepth = 4;
 constexpr int kMmBarBytes = 512;  // the activation copy's barrier (last 8 bytes)
 constexpr int kMmRowPad = 32;     // activation row pitch K + 32 bytes
 constexpr int kMmMaxM = 16;
-constexpr int kMmMinM = 3;  // btf_gemv / btf_gemm route 3 <= M <= 16 here (mma_serves)
+constexpr int kMmMinM = 3;  // btf_gemv / btf_gemm route calls of 3 <= M <= 16 here (mma_serves)
 constexpr int kMmMaxK = 8192;
 constexpr uint64_t kMmWaitNs = 1000000000ull;
 constexpr int kMmBias = 1 << 20;
@@ -398,17 +398,27 @@ int gemv_mma_setup(DeviceInfo& d) {
   return e == cudaSuccess ? BTF_OK : cuda_fail(e, "cudaFuncSetAttribute(gemv_mma_kernel)");
 }
 
-// Dispatch rule of btf_gemv / btf_gemm / btf_gemv_gather: 3 <= M <= 16 rows
-// (for 1 or 2 rows the GEMV's dp4a pass is faster; from 3 rows on its time
-// doubles) with K <= 8192, over a matrix with at least one 32-row unit per warp
-// of the device (fewer leave SMs idle, where the weight-major kernel or the
-// GEMV passes are as fast); q, d and s 16-byte aligned.
+// Dispatch rule of btf_gemv / btf_gemm / btf_gemv_gather (K <= 8192; q, d
+// and s 16-byte aligned), from B200 timings at K = 5120 against the other
+// kernels on the same call:
+//   - 9 <= M <= 16: from (SM count) 32-row units on (the weight-major tcgen05
+//     kernel was slower at every N measured, 5120 to 248320 rows, e.g. 23
+//     against 26 us at 17408; on fewer units the GEMV passes are faster);
+//   - 5 <= M <= 8: from 2 x (SM count) 32-row units on (two 4-row GEMV passes
+//     are faster on smaller matrices: 17 against 23 us at 6144 rows);
+//   - 3 <= M <= 4: from 8 x (SM count) units on (one GEMV pass is faster on
+//     smaller matrices). M = 1 and 2 stay on the GEMV.
+// A warp's one unit takes ~21 us at K = 5120, which bounds small matrices.
 bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act) {
   const DeviceInfo* dev = current_device();
-  return dev && M >= kMmMinM && M <= kMmMaxM && K > 0 && K % 128 == 0 && K <= kMmMaxK && act.q && act.d && act.s &&
-         (reinterpret_cast<uintptr_t>(act.q) & 15) == 0 && (reinterpret_cast<uintptr_t>(act.d) & 15) == 0 &&
-         (reinterpret_cast<uintptr_t>(act.s) & 15) == 0 &&
-         (groups_of(seg.N) + kMmPanels - 1) / kMmPanels >= dev->sm_count * kMmWarps;
+  if (!dev || M < kMmMinM || M > kMmMaxM || K <= 0 || K % 128 != 0 || K > kMmMaxK || !act.q || !act.d || !act.s ||
+      (reinterpret_cast<uintptr_t>(act.q) & 15) || (reinterpret_cast<uintptr_t>(act.d) & 15) ||
+      (reinterpret_cast<uintptr_t>(act.s) & 15))
+    return false;
+  const int64_t units = (groups_of(seg.N) + kMmPanels - 1) / kMmPanels;
+  if (M >= 9) return units >= dev->sm_count;
+  if (M >= 5) return units >= 2 * dev->sm_count;
+  return units >= (int64_t)dev->sm_count * kMmWarps;
 }
 
 // One segment, 1 <= M <= kMmMaxM, K <= kMmMaxK; idot != nullptr runs the dump

@@ -138,9 +138,10 @@ int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float ep
  * Replaces launch_gemv (src/cuda/kernels.cuh:56, kernels.cu:776-822).
  * 1..3 segments sharing K and the activation; BTF_SWIGLU needs exactly two
  * segments (gate, up) with the same N. K % 128 == 0. Store / add calls with d
- * 16-byte aligned run on the tensor cores: 3 <= M <= 16 with K <= 8192 as
- * btf_gemv_mma when every segment has at least 8 * (SM count) 32-row units
- * (an lm_head; q, d, s 16-byte aligned), else 9 <= M <= 64 as btf_gemm_wm when
+ * 16-byte aligned run on the tensor cores: K <= 8192 and, with u the 32-row
+ * units of every segment and S the SM count, 9 <= M <= 16 and u >= S,
+ * 5 <= M <= 8 and u >= 2 S, or 3 <= M <= 4 and u >= 8 S as btf_gemv_mma (q, d,
+ * s 16-byte aligned), else 9 <= M <= 64 as btf_gemm_wm when
  * every segment has at least 2/3 as many 128-row tiles as the device has SMs
  * (and s is 16-byte aligned), M >= 64 otherwise as btf_gemm. Other calls and
  * swiglu run in passes of btf_gemv_max_nb(K) rows. */
@@ -323,9 +324,9 @@ typedef struct btf_gather {
 } btf_gather;
 /* Counted completion serves M <= btf_gemv_max_nb(K) (one pass, one arrival per
  * launch); the tagged form serves any M (every pass stores its rows' words with
- * the launch's tag). Tagged store calls with 3 <= M <= 16 and K <= 8192 whose
- * every shard has at least 8 x (SM count) 32-row units run on the warp-MMA GEMM
- * (btf_gemv_mma); otherwise those with 9 <= M <= 64 whose every shard has at
+ * the launch's tag). Tagged store calls that btf_gemv would give to
+ * btf_gemv_mma (the rule above, per shard) run on the warp-MMA GEMM;
+ * otherwise those with 9 <= M <= 64 whose every shard has at
  * least 2/3 as many 128-row tiles as SMs run on the weight-major tcgen05 GEMM
  * (btf_gemm_wm); both make one pass over the shard's weights, with the same
  * tagged stores (d and s 16-byte aligned). */
