@@ -6,7 +6,7 @@ unsharded launch's, so the fp32 summation order of a row may differ). Run
 three times: all-gather by NCCL after the GEMV; fused into the GEMV epilogue
 (btf_gemv_gather: NVLink stores into every rank's buffer + arrival counters);
 and the tagged form (64-bit (value, tag) words checked by btf_gather_wait),
-which also runs a batch of 16 over large shards on the weight-major tcgen05
+which also runs a batch of 24 over large shards on the weight-major tcgen05
 GEMM and a batch of 8 over lm_head-size shards on the warp-MMA GEMM. Skipped
 with fewer than 2 GPUs."""
 import os
@@ -22,11 +22,11 @@ from conftest import rel_rms
 pytestmark = pytest.mark.gpu
 
 CASES = [(17408, 5120, 1, 0), (5120, 17408, 1, 1), (1000, 1024, 3, 1), (37, 256, 2, 2)]  # N, K, M, mode
-# tagged form only: a batch of 16 over shards of 148 128-row tiles, which
+# tagged form only: a batch of 24 over shards of 148 128-row tiles, which
 # btf_gemv_gather runs on the weight-major tcgen05 GEMM, and a batch of 8 over
 # shards of 148 x 8 32-row units, which it runs on the warp-MMA GEMM (one weight
 # pass each)
-TAGGED_EXTRA = [(2 * 148 * 128, 1024, 16, 0), (2 * 148 * 8 * 32, 1024, 8, 0)]
+TAGGED_EXTRA = [(2 * 148 * 128, 1024, 24, 0), (2 * 148 * 8 * 32, 1024, 8, 0)]
 
 
 def _free_port():
