@@ -346,7 +346,13 @@ __global__ void __launch_bounds__(kMmThreads, 1) gemv_mma_kernel(const __grid_co
               for (int k = 0; k < 4; ++k) wv[k] = (unsigned long long)__float_as_uint(v[k]) | tag;
               for (int r = 0; r < p.world; ++r) {
                 unsigned long long* dst = p.peer[r] + idx;
-                if ((p.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(p.peer[r]) & 15) == 0 && r0 + 3 < p.N) {
+                if ((p.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(p.peer[r]) & 31) == 0 && r0 + 3 < p.N) {
+                  // one 32-byte store of four words (each word single-copy atomic): the 8
+                  // lanes of a row quad column write 256 contiguous bytes, whole sectors
+                  asm volatile("st.global.v4.u64 [%0], {%1, %2, %3, %4};" ::"l"(dst), "l"(wv[0]), "l"(wv[1]),
+                               "l"(wv[2]), "l"(wv[3])
+                               : "memory");
+                } else if ((p.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(p.peer[r]) & 15) == 0 && r0 + 3 < p.N) {
                   // two 16-byte stores of two words each (each word single-copy atomic): the 8
                   // lanes of a row quad column write 256 contiguous bytes per activation row
                   asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(wv[0]), "l"(wv[1]) : "memory");
