@@ -480,6 +480,9 @@ int gemm_setup(DeviceInfo& d) {
 // for M >= 64 in store / add mode.
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
 bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
+bool mma_two_pass_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
+int run_gemv_mma_rows(const btf_gemv_seg* segs, int nseg, int K, int m0, int M, const btf_q8act& act, int mode,
+                      cudaStream_t st);
 int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
                  int32_t* idot, const btf_gather* g, int gseg);
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
@@ -577,6 +580,11 @@ extern "C" int btf_gemm(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8
   // per segment: a small batch over a very large matrix goes to the warp-MMA
   // kernel, over many weight tiles to the weight-major kernel
   for (int i = 0; i < nseg; ++i) {
+    if (mma_two_pass_serves(segs[i], K, M, act)) {  // two warp-MMA passes of 16 rows
+      if (int rc = run_gemv_mma_rows(segs + i, 1, K, 0, 16, act, mode, (cudaStream_t)stream)) return rc;
+      if (int rc = run_gemv_mma_rows(segs + i, 1, K, 16, M - 16, act, mode, (cudaStream_t)stream)) return rc;
+      continue;
+    }
     const int rc = mma_serves(segs[i], K, M, act)
                        ? run_gemv_mma(segs[i], K, M, act, mode, (cudaStream_t)stream, nullptr, nullptr, 0)
                    : wm_serves(segs[i], M, act)

@@ -868,6 +868,9 @@ int gemv_setup(DeviceInfo& d) {
 // warp-MMA small-batch GEMM's rule (gemv_mma.cu)
 bool wm_serves(const btf_gemv_seg& seg, int M, const btf_q8act& act);
 bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
+bool mma_two_pass_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act);
+int run_gemv_mma_rows(const btf_gemv_seg* segs, int nseg, int K, int m0, int M, const btf_q8act& act, int mode,
+                      cudaStream_t st);
 int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
                  int32_t* idot, const btf_gather* g, int gseg);
 int run_gemm_wm(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
@@ -893,9 +896,15 @@ int btf_gemv(const btf_gemv_seg* segs, int nseg, int K, int M, btf_q8act act, in
   // matrices to the tcgen05 weight-major kernel (one weight pass each), 64
   // rows and more to the 128-row tcgen05 GEMM.
   if (mode != BTF_SWIGLU && aligned(act.d, 16)) {
-    bool mma = true, wm = true;
+    bool mma = true, mma2 = true, wm = true;
     for (int i = 0; i < nseg; ++i) mma = mma && mma_serves(segs[i], K, M, act);
     if (mma) return btf_gemv_mma(segs, nseg, K, M, act, mode, stream);
+    for (int i = 0; i < nseg; ++i) mma2 = mma2 && mma_two_pass_serves(segs[i], K, M, act);
+    if (mma2) {  // 17..32 rows over lm_head-size matrices: two warp-MMA passes of 16 rows
+      take_stamp();  // a stamp request would land on the first pass only: drop it
+      if (int rc = run_gemv_mma_rows(segs, nseg, K, 0, 16, act, mode, (cudaStream_t)stream)) return rc;
+      return run_gemv_mma_rows(segs, nseg, K, 16, M - 16, act, mode, (cudaStream_t)stream);
+    }
     for (int i = 0; i < nseg; ++i) wm = wm && wm_serves(segs[i], M, act);
     if (wm) return btf_gemm_wm(segs, nseg, K, M, act, mode, stream);
     if (M >= kGemmMinM) {

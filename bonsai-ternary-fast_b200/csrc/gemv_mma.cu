@@ -427,6 +427,16 @@ bool mma_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act) {
   return units >= (int64_t)dev->sm_count * kMmWarps;
 }
 
+// Two passes of 16 rows for 17 <= M <= 32 over lm_head-size matrices (at least
+// 8 x (SM count) 32-row units per segment): each pass streams the weights once
+// more, and the two still beat the weight-major kernel's one pass (lm_head,
+// K = 5120, M = 32: 275 against 375 us; 37888 rows: 47 against 60 us).
+bool mma_two_pass_serves(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act) {
+  const DeviceInfo* dev = current_device();
+  return dev && M > kMmMaxM && M <= 2 * kMmMaxM && mma_serves(seg, K, kMmMaxM, act) &&
+         (groups_of(seg.N) + kMmPanels - 1) / kMmPanels >= (int64_t)dev->sm_count * kMmWarps;
+}
+
 // One segment, 1 <= M <= kMmMaxM, K <= kMmMaxK; idot != nullptr runs the dump
 // form; g != null (tagged, store mode) stores segment `gseg` into every rank's buffer.
 int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, int mode, cudaStream_t st,
@@ -466,6 +476,19 @@ int run_gemv_mma(const btf_gemv_seg& seg, int K, int M, const btf_q8act& act, in
                         : g    ? launch_pdl(gemv_mma_kernel<false, true>, dim3(grid), dim3(kMmThreads), smem, st, p)
                                : launch_pdl(gemv_mma_kernel<false>, dim3(grid), dim3(kMmThreads), smem, st, p);
   return e == cudaSuccess ? launch_status("gemv_mma_kernel") : cuda_fail(e, "gemv_mma_kernel launch");
+}
+
+// Rows m0 .. m0 + M of the activation through run_gemv_mma (row views of the
+// Q8 activation and of each segment's output; K % 128 == 0 keeps them 16-byte aligned).
+int run_gemv_mma_rows(const btf_gemv_seg* segs, int nseg, int K, int m0, int M, const btf_q8act& act, int mode,
+                      cudaStream_t st) {
+  const btf_q8act sub{act.q + (size_t)m0 * K, act.d + (size_t)m0 * (K / 32), act.s + (size_t)m0 * (K / 32)};
+  for (int i = 0; i < nseg; ++i) {
+    btf_gemv_seg sg = segs[i];
+    sg.y = segs[i].y + (size_t)m0 * segs[i].ldy;
+    if (int rc = run_gemv_mma(sg, K, M, sub, mode, st, nullptr, nullptr, 0)) return rc;
+  }
+  return BTF_OK;
 }
 
 }  // namespace btf

@@ -141,7 +141,8 @@ int btf_prep(const float* x, int ldx, int M, int n, const float* normw, float ep
  * 16-byte aligned run on the tensor cores: K <= 8192 and, with u the 32-row
  * units of every segment and S the SM count, 9 <= M <= 16 and u >= S,
  * 5 <= M <= 8 and u >= 2 S, or 3 <= M <= 4 and u >= 8 S as btf_gemv_mma (q, d,
- * s 16-byte aligned), else 9 <= M <= 64 as btf_gemm_wm when
+ * s 16-byte aligned); 17 <= M <= 32 with u >= 8 S (and K <= 8192) as two
+ * btf_gemv_mma passes of 16 rows; else 9 <= M <= 64 as btf_gemm_wm when
  * every segment has at least 2/3 as many 128-row tiles as the device has SMs
  * (and s is 16-byte aligned), M >= 64 otherwise as btf_gemm. Other calls and
  * swiglu run in passes of btf_gemv_max_nb(K) rows. */

@@ -207,6 +207,38 @@ def test_gemv_and_gemm_route_to_warp_mma(cuda, btf, orc, M, N):
     assert rel_rms(a[:, rows], orc.gemv(codes, scales, K, q, d, s, threads=8)) <= TOL
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,mode", [(24, 0), (32, 1)])
+def test_gemv_and_gemm_run_two_passes_of_16_rows(cuda, btf, orc, M, mode):
+    # 17 <= M <= 32 rows over a matrix of 8 x (SM count) 32-row units or more:
+    # btf_gemv and btf_gemm run two warp-MMA passes (rows 0..15, then the rest),
+    # bit for bit those two direct calls, and within the bar of the oracle
+    import torch
+
+    K, N = 1024, 148 * 8 * 32
+    src = synth.ternary_ptq(N, K, seed=300 + M)
+    pm = btf.repack_panels(_dev(src, cuda), N, K)
+    x = synth.activations(M, K, seed=301 + M)
+    act = btf.quant_q8(_dev(x, cuda))
+    y0 = np.random.default_rng(M).standard_normal((M, N)).astype(np.float32)
+    ys = [_dev(y0, cuda) for _ in range(3)]
+    for m0 in (0, 16):
+        mm = min(16, M - m0)
+        sub = btf.Q8Act(act.q[m0:m0 + mm], act.d[m0:m0 + mm], act.s[m0:m0 + mm])
+        btf.launch_gemv_mma([(pm, ys[0][m0:m0 + mm], N)], K, mm, sub, mode)
+    btf.launch_gemv([(pm, ys[1], N)], K, M, act, mode)
+    btf.launch_gemm([(pm, ys[2], N)], K, M, act, mode)
+    torch.cuda.synchronize()
+    assert btf.device_error() == 0
+    a, b, c = (y.cpu().numpy() for y in ys)
+    assert np.array_equal(a, b) and np.array_equal(a, c)
+    rows = np.r_[0:200, N - 200:N]
+    codes, scales = orc.repack_t2(src[rows], len(rows), K)
+    q, d, s = orc.q8_rows(x)
+    want = orc.gemv(codes, scales, K, q, d, s, threads=8) + (y0[:, rows] if mode == btf.ADD else 0)
+    assert rel_rms(a[:, rows], want) <= TOL
+
+
 def test_gemv_mma_rejects_bad_arguments(btf):
     """Refused before any CUDA call (runs without a GPU)."""
     import ctypes
