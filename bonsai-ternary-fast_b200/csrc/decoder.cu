@@ -81,7 +81,7 @@ struct Decoder {
   float* inv_signs = nullptr;
   std::vector<void*> allocs;
   // step buffers
-  float *x = nullptr, *xn = nullptr, *bA = nullptr, *bB = nullptr, *bC = nullptr, *bO = nullptr, *bQ = nullptr,
+  float *x = nullptr, *xn = nullptr, *bA = nullptr, *bB = nullptr, *bC = nullptr, *bO = nullptr,
         *bG = nullptr, *logits = nullptr, *part = nullptr, *amax_v = nullptr;
   int* attn_cnt = nullptr;  // per-head split counters of the attention launch (zero between launches)
   int* amax_i = nullptr;
@@ -171,11 +171,11 @@ int make_buffers(Decoder& D) {
   D.Kmax = std::max({E, F, wo});
   // activation buffers in one arena (shared with the other ranks under tensor parallelism)
   // the row buffers hold a prompt chunk of kMaxChunk rows (decode steps use row 0);
-  // bQ (one token's rotated q) and the logits (the last token's) hold one row
+  // the logits (the last token's) hold one row
   const int R = Decoder::kMaxChunk;
-  const int sizes[9] = {R * E, R * E, R * wa, R * wb, R * wc, R * wo, std::max(1, H * HD), R * F, d.n_vocab};
-  size_t off[9], total = Decoder::kCtl;
-  for (int i = 0; i < 9; ++i) {
+  const int sizes[8] = {R * E, R * E, R * wa, R * wb, R * wc, R * wo, R * F, d.n_vocab};
+  size_t off[8], total = Decoder::kCtl;
+  for (int i = 0; i < 8; ++i) {
     off[i] = total;
     total += ((size_t)sizes[i] * 4 + 255) / 256 * 256;
   }
@@ -183,9 +183,9 @@ int make_buffers(Decoder& D) {
   if (rc) return rc;
   D.arena_bytes = total;
   if (!D.dry && cudaMemset(D.arena, 0, total) != cudaSuccess) return fail(BTF_ERR_CUDA, "btf_decoder: arena clear");
-  float** dst[9] = {&D.x, &D.xn, &D.bA, &D.bB, &D.bC, &D.bO, &D.bQ, &D.bG, &D.logits};
+  float** dst[8] = {&D.x, &D.xn, &D.bA, &D.bB, &D.bC, &D.bO, &D.bG, &D.logits};
   if (!D.dry)
-    for (int i = 0; i < 9; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
+    for (int i = 0; i < 8; ++i) *dst[i] = reinterpret_cast<float*>(D.arena + off[i]);
   D.peers[D.rank] = D.arena;
   D.part = D.alloc<float>((size_t)std::max(1, H) * D.o.attn_splits * (HD + 2), &rc);
   D.attn_cnt = D.alloc<int>((size_t)std::max(1, H), &rc);
